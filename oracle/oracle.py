@@ -1,0 +1,218 @@
+"""ctypes access to the checkers — TEST INFRASTRUCTURE ONLY.
+
+Only tests/, ``__graft_entry__.smoke()`` and bench.py's CPU-baseline leg import
+this module. It loads
+
+* ``oracle/_build/libkore_oracle.so`` — the C restatement of kore's attention
+  (kore_attn_oracle.c), and
+* ``oracle/_ref/libkore_ref.so`` — the reference engine itself (kore.cpp,
+  compiled in place by oracle/Makefile) driven through ref_harness.cpp.
+
+Both are built by ``make -C oracle``; the reference library is optional (it
+needs the reference sources at build time) and ``ref_available()`` says
+whether it is present.
+"""
+from __future__ import annotations
+
+import ctypes
+import os
+import subprocess
+
+import numpy as np
+
+HERE = os.path.dirname(os.path.abspath(__file__))
+ORACLE_SO = os.path.join(HERE, "_build", "libkore_oracle.so")
+REF_SO = os.path.join(HERE, "_ref", "libkore_ref.so")
+
+_f32p = ctypes.POINTER(ctypes.c_float)
+_oracle = None
+_ref = None
+
+
+def build(ref_dir: str | None = None) -> None:
+    """Compile the restatement and, when the reference sources exist, the
+    reference harness."""
+    subprocess.run(["make", "-s", "-C", HERE, "oracle"], check=True)
+    ref_dir = ref_dir or os.environ.get("KORE_REF_DIR", "/root/reference")
+    if os.path.exists(os.path.join(ref_dir, "kore.cpp")):
+        subprocess.run(["make", "-s", "-C", HERE, "ref", f"KORE_REF_DIR={ref_dir}"], check=True)
+
+
+def _fp(a: np.ndarray):
+    assert a.dtype == np.float32 and a.flags.c_contiguous
+    return a.ctypes.data_as(_f32p)
+
+
+def lib():
+    global _oracle
+    if _oracle is None:
+        if not os.path.exists(ORACLE_SO):
+            build()
+        L = ctypes.CDLL(ORACLE_SO)
+        L.korc_inv_freq.argtypes = [ctypes.c_float, ctypes.c_int, _f32p]
+        L.korc_rope_angles.argtypes = [_f32p, ctypes.c_int, ctypes.c_int, _f32p, _f32p]
+        L.korc_rope_key.argtypes = [ctypes.c_int, ctypes.c_int, _f32p, ctypes.c_int, _f32p, _f32p]
+        L.korc_cpu_has_avx2.restype = ctypes.c_int
+        L.korc_hd_dot.argtypes = [_f32p, _f32p, ctypes.c_int, ctypes.c_int]
+        L.korc_hd_dot.restype = ctypes.c_float
+        L.korc_attn_decode.argtypes = [ctypes.c_int] * 3 + [_f32p, ctypes.c_int] + [_f32p] * 7
+        L.korc_attn_prefill.argtypes = ([ctypes.c_int] * 3 + [_f32p, ctypes.c_int, ctypes.c_int]
+                                        + [_f32p] * 7 + [ctypes.c_int])
+        L.korc_argmax.argtypes = [_f32p, ctypes.c_int]
+        _oracle = L
+    return _oracle
+
+
+def ref_available() -> bool:
+    return os.path.exists(REF_SO)
+
+
+def ref_lib():
+    global _ref
+    if _ref is None:
+        L = ctypes.CDLL(REF_SO)
+        L.kref_create.argtypes = [ctypes.c_int] * 4 + [ctypes.c_float, ctypes.c_int]
+        L.kref_create.restype = ctypes.c_void_p
+        L.kref_destroy.argtypes = [ctypes.c_void_p]
+        L.kref_avx2.argtypes = [ctypes.c_void_p]
+        L.kref_ctx.argtypes = [ctypes.c_void_p]
+        L.kref_inv_freq.argtypes = [ctypes.c_void_p]
+        L.kref_inv_freq.restype = _f32p
+        L.kref_kcache.argtypes = [ctypes.c_void_p]
+        L.kref_kcache.restype = _f32p
+        L.kref_vcache.argtypes = [ctypes.c_void_p]
+        L.kref_vcache.restype = _f32p
+        L.kref_fill.argtypes = [ctypes.c_void_p, ctypes.c_int, ctypes.c_int, _f32p, _f32p]
+        L.kref_decode.argtypes = [ctypes.c_void_p, ctypes.c_int, _f32p, _f32p, _f32p, _f32p]
+        L.kref_prefill.argtypes = [ctypes.c_void_p, ctypes.c_int, ctypes.c_int, _f32p, _f32p, _f32p, _f32p]
+        L.kref_argmax.argtypes = [_f32p, ctypes.c_int]
+        L.kref_now_ms.restype = ctypes.c_double
+        _ref = L
+    return _ref
+
+
+# ----------------------------------------------------------------- restatement
+
+def inv_freq(rope_base: float, head_dim: int) -> np.ndarray:
+    out = np.empty(head_dim // 2, np.float32)
+    lib().korc_inv_freq(rope_base, head_dim, _fp(out))
+    return out
+
+
+def rope_angles(inv: np.ndarray, pos: int):
+    half = inv.shape[0]
+    c = np.empty(half, np.float32)
+    s = np.empty(half, np.float32)
+    lib().korc_rope_angles(_fp(inv), half, pos, _fp(c), _fp(s))
+    return c, s
+
+
+def rope_keys(G: int, d: int, inv: np.ndarray, pos0: int, k_pre: np.ndarray) -> np.ndarray:
+    """Post-RoPE key rows as kore stores them, for positions pos0.. ."""
+    k_pre = np.ascontiguousarray(k_pre, np.float32).reshape(-1, G * d)
+    out = np.empty_like(k_pre)
+    for z in range(k_pre.shape[0]):
+        lib().korc_rope_key(G, d, _fp(inv), pos0 + z, _fp(k_pre[z]), _fp(out[z]))
+    return out
+
+
+def cpu_has_avx2() -> bool:
+    return bool(lib().korc_cpu_has_avx2())
+
+
+class OracleLayer:
+    """One layer's fp32 KV cache, [ctx][G*d] rows, in kore's layout
+    (kore.cpp:1260, :1344-1345), driven by the restated decode/prefill."""
+
+    def __init__(self, H: int, G: int, d: int, ctx: int, rope_base: float = 1e6):
+        self.H, self.G, self.d, self.ctx = H, G, d, ctx
+        self.inv = inv_freq(rope_base, d)
+        self.kc = np.zeros((ctx, G * d), np.float32)
+        self.vc = np.zeros((ctx, G * d), np.float32)
+
+    def fill(self, pos0: int, k_pre: np.ndarray, v: np.ndarray) -> None:
+        n = k_pre.shape[0]
+        self.kc[pos0:pos0 + n] = rope_keys(self.G, self.d, self.inv, pos0, k_pre)
+        self.vc[pos0:pos0 + n] = v.reshape(n, -1)
+
+    def decode(self, pos: int, q, k, v) -> np.ndarray:
+        q = np.ascontiguousarray(q, np.float32).reshape(-1)
+        k = np.ascontiguousarray(k, np.float32).reshape(-1)
+        v = np.ascontiguousarray(v, np.float32).reshape(-1)
+        out = np.empty(self.H * self.d, np.float32)
+        scores = np.empty(pos + 1, np.float32)
+        rc = lib().korc_attn_decode(self.H, self.G, self.d, _fp(self.inv), pos, _fp(q), _fp(k), _fp(v),
+                                    _fp(self.kc), _fp(self.vc), _fp(out), _fp(scores))
+        if rc:
+            raise ValueError("korc_attn_decode: bad arguments")
+        return out.reshape(self.H, self.d)
+
+    def prefill(self, pos0: int, q, k, v, avx2: bool | None = None) -> np.ndarray:
+        n = q.shape[0]
+        q = np.ascontiguousarray(q, np.float32).reshape(n, -1)
+        k = np.ascontiguousarray(k, np.float32).reshape(n, -1)
+        v = np.ascontiguousarray(v, np.float32).reshape(n, -1)
+        out = np.empty((n, self.H * self.d), np.float32)
+        scratch = np.empty(pos0 + n + n * self.H * self.d, np.float32)
+        if avx2 is None:
+            avx2 = cpu_has_avx2()
+        rc = lib().korc_attn_prefill(self.H, self.G, self.d, _fp(self.inv), pos0, n, _fp(q), _fp(k), _fp(v),
+                                     _fp(self.kc), _fp(self.vc), _fp(out), _fp(scratch), int(avx2))
+        if rc:
+            raise ValueError("korc_attn_prefill: bad arguments")
+        return out.reshape(n, self.H, self.d)
+
+
+class RefLayer:
+    """The same, but running the reference engine's own forward()/forward_batch()
+    (oracle/_ref/libkore_ref.so)."""
+
+    def __init__(self, H: int, G: int, d: int, ctx: int, rope_base: float = 1e6, threads: int = 1):
+        self.H, self.G, self.d, self.ctx = H, G, d, ctx
+        self.h = ref_lib().kref_create(H, G, d, ctx, rope_base, threads)
+        if not self.h:
+            raise RuntimeError("kore engine_init refused the shape")
+        kvd = G * d
+        self.kc = np.ctypeslib.as_array(ref_lib().kref_kcache(self.h), shape=(ctx, kvd))
+        self.vc = np.ctypeslib.as_array(ref_lib().kref_vcache(self.h), shape=(ctx, kvd))
+
+    def __del__(self):
+        h = getattr(self, "h", None)
+        if h:
+            ref_lib().kref_destroy(h)
+            self.h = None
+
+    @property
+    def avx2(self) -> bool:
+        return bool(ref_lib().kref_avx2(self.h))
+
+    def fill(self, pos0: int, k_pre: np.ndarray, v: np.ndarray) -> None:
+        k_pre = np.ascontiguousarray(k_pre, np.float32)
+        v = np.ascontiguousarray(v, np.float32)
+        if ref_lib().kref_fill(self.h, pos0, k_pre.shape[0], _fp(k_pre), _fp(v)):
+            raise ValueError("kref_fill: out of range")
+
+    def decode(self, pos: int, q, k, v) -> np.ndarray:
+        q = np.ascontiguousarray(q, np.float32).reshape(-1)
+        k = np.ascontiguousarray(k, np.float32).reshape(-1)
+        v = np.ascontiguousarray(v, np.float32).reshape(-1)
+        out = np.empty(self.H * self.d, np.float32)
+        if ref_lib().kref_decode(self.h, pos, _fp(q), _fp(k), _fp(v), _fp(out)):
+            raise ValueError("kore forward() returned false")
+        return out.reshape(self.H, self.d)
+
+    def prefill(self, pos0: int, q, k, v) -> np.ndarray:
+        n = q.shape[0]
+        q = np.ascontiguousarray(q, np.float32).reshape(n, -1)
+        k = np.ascontiguousarray(k, np.float32).reshape(n, -1)
+        v = np.ascontiguousarray(v, np.float32).reshape(n, -1)
+        out = np.empty((n, self.H * self.d), np.float32)
+        if ref_lib().kref_prefill(self.h, pos0, n, _fp(q), _fp(k), _fp(v), _fp(out)):
+            raise ValueError("kore forward_batch() returned false")
+        return out.reshape(n, self.H, self.d)
+
+
+def seeded_inputs(seed: int, *shapes):
+    """N(0,1) fp32 arrays from one numpy Generator (PCG64) seeded with `seed`."""
+    g = np.random.default_rng(seed)
+    return [g.standard_normal(s, dtype=np.float32) for s in shapes]
