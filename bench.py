@@ -1,0 +1,410 @@
+"""bench.py — decode attention throughput of the B200 kore path.
+
+Workload (the metric's "@7B ctx 32k"): Qwen2.5-7B-shaped
+attention, 28 layers, 28 query / 4 KV heads, head_dim 128, one sequence,
+fp32 KV cache of 32768 seeded N(0,1) rows per layer (3.5 GiB, far larger than
+the 126 MB L2, so no L2 flush is needed between steps). One step = one decode
+token through all 28 layers: RoPE of q/k at position 32768, append of k/v,
+attention over positions 0..32768.
+
+  value  device-resident: q/k/v already in HBM, CUDA events on the context's
+         stream around K steps; GB/s of algorithmic bytes
+         (per layer: 2*(pos+1)*512*4 K/V + 2*28*128*4 q/out + 2*512*4 append).
+  e2e    the same steps through the host-buffer C entry point
+         kore_cuda_attn_decode (kore's call: host q/k/v in, host out back),
+         wall clock, copies included.
+At N > 1 the KV positions are split over the GPUs by page (round robin); each
+layer's partial outputs and log-sum-exps are all-gathered over NCCL and
+merged. The cache is fixed (strong scaling).
+
+``--impl reference`` times kore's own CPU attention (the reference compiled
+in place, oracle/_ref) on this host: kore.cpp forward() per layer on its
+fp32 cache, layers fanned over the host's cores.
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import statistics
+import subprocess
+import sys
+import threading
+import time
+
+import numpy as np
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, ROOT)
+
+H, G, D, L = 28, 4, 128, 28
+POS = 32768
+CTX = POS + 1
+KVD = G * D
+
+
+def layer_bytes(pos: int) -> int:
+    return 2 * (pos + 1) * KVD * 4 + 2 * H * D * 4 + 2 * KVD * 4
+
+
+def parse():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=1000)
+    ap.add_argument("--warmup", type=int, default=20)
+    ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--e2e-steps", type=int, default=100)
+    return ap.parse_args()
+
+
+# ---------------------------------------------------------------- clocks
+
+class ClockSampler:
+    """nvidia-smi samples of SM clock and throttle reasons during the timed region."""
+
+    Q = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+         "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+         "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, index: int):
+        self.index = index
+        self.proc = None
+        self.lines: list[tuple[float, str]] = []
+
+    def start(self):
+        try:
+            self.proc = subprocess.Popen(["nvidia-smi", f"--id={self.index}", f"--query-gpu={self.Q}",
+                                          "--format=csv,noheader,nounits", "-lms", "100"],
+                                         stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+        except OSError:
+            self.proc = None
+            return
+        self.t = threading.Thread(target=self._read, daemon=True)
+        self.t.start()
+        t0 = time.time()
+        while not self.lines and time.time() - t0 < 3:
+            time.sleep(0.02)
+
+    def _read(self):
+        for line in self.proc.stdout:
+            self.lines.append((time.time(), line.strip()))
+
+    def stop(self, t_begin: float, t_end: float) -> dict:
+        if not self.proc:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvidia-smi unavailable"]}
+        time.sleep(0.15)
+        self.proc.terminate()
+        self.proc.wait()
+        rows = [l for (t, l) in self.lines if t_begin - 0.1 <= t <= t_end + 0.15] or [l for _, l in self.lines[-2:]]
+        mhz, mx, reasons = [], None, set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for r in rows:
+            f = [x.strip() for x in r.split(",")]
+            try:
+                mhz.append(float(f[1]))
+                mx = float(f[2])
+            except (ValueError, IndexError):
+                continue
+            for n, v in zip(names, f[5:9]):
+                if v.lower().startswith("active"):
+                    reasons.add(n)
+        return {"sm_mhz": statistics.median(mhz) if mhz else None, "sm_max_mhz": mx,
+                "reasons": sorted(reasons), "samples": len(mhz)}
+
+
+# ---------------------------------------------------------------- our arm
+
+def run_ours(args, rank: int, world: int, dist) -> dict | None:
+    import torch
+    import kore_b200 as K
+
+    dev = torch.device("cuda", int(os.environ.get("LOCAL_RANK", 0)))
+    torch.cuda.set_device(dev)
+    ctx = K.KoreCuda(L, H, G, D, CTX, device=dev.index, shard_rank=rank, shard_count=world)
+    stream = torch.cuda.ExternalStream(ctx.stream, device=dev)
+
+    # seeded N(0,1) cache: all rows generated on the device per layer; each
+    # shard stores the rows of the pages it holds
+    gen = torch.Generator(device=dev)
+    with torch.cuda.stream(stream):
+        for layer in range(L):
+            gen.manual_seed(1000 + layer)
+            k = torch.randn(POS, KVD, device=dev, generator=gen)
+            v = torch.randn(POS, KVD, device=dev, generator=gen)
+            ctx.append_dev(0, layer, 0, POS, k, v)
+            del k, v
+        gen.manual_seed(7)
+        q = torch.randn(L, H * D, device=dev, generator=gen)
+        kn = torch.randn(L, KVD, device=dev, generator=gen)
+        vn = torch.randn(L, KVD, device=dev, generator=gen)
+        out = torch.empty(L, H * D, device=dev)
+        part = torch.empty(L, ctx.part_floats, device=dev)
+        parts = torch.empty(L, world, ctx.part_floats, device=dev)
+    ctx.sync()
+
+    def step():
+        for layer in range(L):
+            if world == 1:
+                ctx.decode_dev(0, layer, POS, q[layer], kn[layer], vn[layer], out[layer])
+            else:
+                ctx.decode_partial_dev(0, layer, POS, q[layer], kn[layer], vn[layer], part[layer])
+                dist.all_gather_into_tensor(parts[layer], part[layer])
+                ctx.lse_merge_dev(world, parts[layer], out[layer])
+
+    def barrier():
+        if world > 1:
+            dist.barrier()
+        torch.cuda.synchronize(dev)
+
+    with torch.cuda.stream(stream):
+        for _ in range(args.warmup):
+            step()
+    ctx.sync()
+    barrier()
+
+    clocks = ClockSampler(dev.index)
+    clocks.start()
+    e0 = torch.cuda.Event(enable_timing=True)
+    e1 = torch.cuda.Event(enable_timing=True)
+    barrier()
+    t_begin = time.time()
+    with torch.cuda.stream(stream):
+        e0.record(stream)
+        for _ in range(args.steps):
+            step()
+        e1.record(stream)
+    e1.synchronize()
+    t_end = time.time()
+    ctx.sync()
+    barrier()
+    clk = clocks.stop(t_begin, t_end)
+    ms = e0.elapsed_time(e1)
+
+    # per-launch durations of the decode kernel (second pass, same work)
+    n_ev = min(args.steps, 100)
+    evs = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(n_ev * L)]
+    with torch.cuda.stream(stream):
+        for s in range(n_ev):
+            for layer in range(L):
+                a, b = evs[s * L + layer]
+                a.record(stream)
+                if world == 1:
+                    ctx.decode_dev(0, layer, POS, q[layer], kn[layer], vn[layer], out[layer])
+                else:
+                    ctx.decode_partial_dev(0, layer, POS, q[layer], kn[layer], vn[layer], part[layer])
+                b.record(stream)
+    torch.cuda.synchronize(dev)
+    kern_ms = sum(a.elapsed_time(b) for a, b in evs) / len(evs)
+
+    # end to end through the host-buffer entry point (kore's own call shape)
+    e2e_ms = None
+    if world == 1:
+        hq, hk, hv = q.cpu().numpy(), kn.cpu().numpy(), vn.cpu().numpy()
+        ho = np.empty((L, H * D), np.float32)
+        for layer in range(L):
+            ho[layer] = ctx.decode(0, layer, POS, hq[layer], hk[layer], hv[layer]).reshape(-1)
+        t0 = time.perf_counter()
+        for _ in range(args.e2e_steps):
+            for layer in range(L):
+                ho[layer] = ctx.decode(0, layer, POS, hq[layer], hk[layer], hv[layer]).reshape(-1)
+        e2e_ms = (time.perf_counter() - t0) * 1e3 / args.e2e_steps
+    else:
+        # host buffers per layer: pinned copies in, merged output back
+        hq = q.cpu().pin_memory()
+        hk, hv = kn.cpu().pin_memory(), vn.cpu().pin_memory()
+        ho = torch.empty(L, H * D).pin_memory()
+        barrier()
+        t0 = time.perf_counter()
+        with torch.cuda.stream(stream):
+            for _ in range(args.e2e_steps):
+                for layer in range(L):
+                    q[layer].copy_(hq[layer], non_blocking=True)
+                    kn[layer].copy_(hk[layer], non_blocking=True)
+                    vn[layer].copy_(hv[layer], non_blocking=True)
+                    ctx.decode_partial_dev(0, layer, POS, q[layer], kn[layer], vn[layer], part[layer])
+                    dist.all_gather_into_tensor(parts[layer], part[layer])
+                    ctx.lse_merge_dev(world, parts[layer], out[layer])
+                    ho[layer].copy_(out[layer], non_blocking=True)
+                    stream.synchronize()
+        e2e_ms = (time.perf_counter() - t0) * 1e3 / args.e2e_steps
+
+    t = torch.tensor([ms, kern_ms, e2e_ms], device=dev, dtype=torch.float64)
+    if world > 1:
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    ms, kern_ms, e2e_ms = t.tolist()
+    ctx.close()
+    if rank != 0:
+        return None
+
+    step_bytes = L * layer_bytes(POS)
+    ms_step = ms / args.steps
+    gbs = step_bytes / (ms_step * 1e-3) / 1e9
+    e2e_gbs = step_bytes / (e2e_ms * 1e-3) / 1e9
+    peaks = load_peaks()
+    launch_bytes = layer_bytes(POS) / world
+    achieved = launch_bytes / (kern_ms * 1e-3) / 1e9
+    line = {
+        "metric": "decode attn HBM GB/s @7B ctx 32k (28 layers, 28Q/4KV, d128, fp32 KV)",
+        "value": round(gbs, 1), "unit": "GB/s", "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
+        "ms_per_step": round(ms_step, 5), "higher_is_better": True,
+        "scaling": "strong" if world > 1 else "weak",
+        "vs_baseline": None, "dtype": "f32", "data": "synthetic (seeded N(0,1) q/k/v and KV cache)",
+        "config": {"workload": "cfg4: Qwen2.5-7B-shaped decode at position 32768, 28 layers, batch 1",
+                   "kv_bytes_per_step": step_bytes, "l2": "inputs 3.5 GiB > L2, no flush needed",
+                   "kv_split": f"pages round-robin over {world} GPU(s)" if world > 1 else "none"},
+        "e2e": {"value": round(e2e_gbs, 1), "unit": "GB/s", "ms_per_step": round(e2e_ms, 4),
+                "h2d_bytes_per_step": L * (H * D + 2 * KVD) * 4, "d2h_bytes_per_step": L * H * D * 4},
+        "roofline": {"bound": "hbm", "kernel": "attn_decode_kernel<128,7,...>", "achieved": round(achieved, 1),
+                     "peak": peaks["hbm_gbs"], "peak_source": peaks["source"], "unit": "GB/s",
+                     "frac": round(achieved / peaks["hbm_gbs"], 4), "traffic": load_traffic(),
+                     "launch_ms": round(kern_ms, 5), "algorithmic_bytes_per_launch": int(launch_bytes)},
+        "gpu_launches": args.steps * L * (2 if world > 1 else 1),
+        "clocks": clk,
+    }
+    if not args.no_cpu_baseline and world == 1:
+        line["cpu_baseline"] = cpu_baseline_sample()
+    return line
+
+
+def load_peaks() -> dict:
+    p = os.path.join(ROOT, "MEASURED_PEAKS.json")
+    try:
+        with open(p) as f:
+            j = json.load(f)
+        return {"hbm_gbs": float(j["hbm_gbs"]), "bf16_tflops": float(j["bf16_tflops"]), "source": "measured"}
+    except (OSError, KeyError, ValueError):
+        return {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "source": "fallback"}
+
+
+def load_traffic():
+    """DRAM bytes per decode launch from the committed ncu summary, if any."""
+    p = os.path.join(ROOT, "profiles", "traffic.json")
+    try:
+        with open(p) as f:
+            return json.load(f).get("attn_decode_cfg4_bytes_per_launch")
+    except (OSError, ValueError):
+        return None
+
+
+# ---------------------------------------------------------------- reference arm (CPU)
+
+def _ref_layer_engines(n: int, threads: int = 1):
+    from oracle import oracle as O
+    engines = []
+    for i in range(n):
+        e = O.RefLayer(H, G, D, CTX, threads=threads)
+        g = np.random.default_rng(100 + i)
+        for p0 in range(0, POS, 4096):
+            k = g.standard_normal((4096, KVD), dtype=np.float32)
+            v = g.standard_normal((4096, KVD), dtype=np.float32)
+            e.fill(p0, k, v)
+        engines.append(e)
+    return engines
+
+
+def _ref_decode_ms(e, pos: int, reps: int = 1) -> float:
+    from oracle import oracle as O
+    q, k, v = O.seeded_inputs(5, (H * D,), (KVD,), (KVD,))
+    t0 = time.perf_counter()
+    for _ in range(reps):
+        e.decode(pos, q, k, v)
+    return (time.perf_counter() - t0) * 1e3 / reps
+
+
+def cpu_baseline_sample() -> dict:
+    """kore's own decode attention (forward() of the compiled reference) on 1
+    core, one layer at position 32768, minus the same forward() at position 0
+    (embedding, norms and zero-weight projections, i.e. everything that is
+    not attention)."""
+    from oracle import oracle as O
+    if not O.ref_available():
+        return {"value": None, "unavailable": "oracle/_ref not built"}
+    e = _ref_layer_engines(1)[0]
+    base = _ref_decode_ms(e, 0, reps=3)
+    t = min(_ref_decode_ms(e, POS) for _ in range(3))
+    att = max(t - base, 1e-6)
+    return {"value": round(layer_bytes(POS) / (att * 1e-3) / 1e9, 3), "unit": "GB/s", "cores": 1,
+            "kind": "reference",
+            "sample": f"1 of 28 layers, decode at pos {POS}, kore forward() best of 3 = {t:.1f} ms "
+                      f"minus forward() at pos 0 = {base:.1f} ms; attention {att:.1f} ms"}
+
+
+def run_reference(args, rank: int, world: int) -> dict | None:
+    if rank != 0:
+        return None
+    from oracle import oracle as O
+    if not O.ref_available():
+        return {"impl": "reference", "unavailable": "oracle/_ref/libkore_ref.so not built (needs the reference sources)"}
+    cores = len(os.sched_getaffinity(0))
+    T = max(1, min(cores, L))
+    engines = _ref_layer_engines(T)
+    base = _ref_decode_ms(engines[0], 0, reps=3)
+    from oracle import oracle as O2
+    q, k, v = O2.seeded_inputs(5, (H * D,), (KVD,), (KVD,))
+
+    def one_step():
+        # T layers at once, one per core: kore's attention is single-threaded
+        ths = [threading.Thread(target=e.decode, args=(POS, q, k, v)) for e in engines]
+        t0 = time.perf_counter()
+        for th in ths:
+            th.start()
+        for th in ths:
+            th.join()
+        return (time.perf_counter() - t0) * 1e3
+
+    budget_s = 150.0
+    first = one_step()
+    n_total = args.warmup + args.steps
+    steps = max(1, min(args.steps, int(budget_s * 1e3 / max(first, 1.0)) - min(args.warmup, 2)))
+    warm = min(args.warmup, 2)
+    for _ in range(max(0, warm - 1)):
+        one_step()
+    times = [one_step() for _ in range(steps)]
+    ms = sum(times) / len(times)
+    att_ms = max(ms - base, 1e-6)   # non-attention part of forward() runs in parallel too
+    v_gbs = T * layer_bytes(POS) / (att_ms * 1e-3) / 1e9
+    return {
+        "impl": "reference", "metric": "decode attn HBM GB/s @7B ctx 32k (28 layers, 28Q/4KV, d128, fp32 KV)",
+        "value": round(v_gbs, 3), "unit": "GB/s", "n_gpus": world, "steps": steps, "warmup": warm,
+        "steps_requested": args.steps, "ms_per_step": round(att_ms, 3), "higher_is_better": True,
+        "scaling": "weak", "vs_baseline": None, "dtype": "f32", "data": "synthetic (seeded N(0,1))",
+        "config": {"workload": "cfg4: Qwen2.5-7B-shaped decode at position 32768, 28 layers, batch 1"},
+        "cpu_baseline": {"value": round(v_gbs, 3), "unit": "GB/s", "cores": T, "kind": "reference",
+                         "sample": f"each step: {T} of the 28 layers decoded concurrently, one kore forward() "
+                                   f"per core (kore's attention is single-threaded), minus forward() at pos 0 "
+                                   f"({base:.1f} ms); {steps} of {n_total} requested steps within {budget_s:.0f} s"},
+        "e2e": {"value": round(v_gbs, 3), "unit": "GB/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+    }
+
+
+# ---------------------------------------------------------------- main
+
+def main():
+    args = parse()
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    dist = None
+    if args.impl == "reference":
+        line = run_reference(args, rank, world)
+        if line is not None:
+            print(json.dumps(line), flush=True)
+        return
+    if world > 1:
+        import datetime
+        import torch
+        import torch.distributed as dist
+        torch.cuda.set_device(int(os.environ.get("LOCAL_RANK", 0)))
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120),
+                                device_id=torch.device("cuda", int(os.environ.get("LOCAL_RANK", 0))))
+    try:
+        line = run_ours(args, rank, world, dist)
+        if line is not None:
+            print(json.dumps(line), flush=True)
+    finally:
+        if dist is not None:
+            dist.destroy_process_group()
+
+
+if __name__ == "__main__":
+    main()

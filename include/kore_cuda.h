@@ -1,0 +1,183 @@
+/*
+ * kore_cuda.h — C ABI of the B200 attention path for kore (BJZR/kore).
+ *
+ * kore has no attention function: its attention is inlined in forward()
+ * (decode, kore.cpp:1424-1455) and forward_batch() (prefill,
+ * kore.cpp:1535-1563), reading and writing the fp32 KV cache
+ * Engine::kcache/vcache (kore.cpp:1260, allocated at :1344-1345). The entry
+ * points below replace exactly those regions. Their inputs are what kore holds
+ * at the start of each region: the bias-added, PRE-RoPE q, k and v
+ * (e.q/e.k/e.v, or the e.bq/e.bk/e.bv rows); their output is what the region
+ * leaves in e.att / e.batt ([tokens][n_head*head_dim], head-major within a
+ * token), which kore then feeds to the Wo projection (kore.cpp:1456, :1566).
+ *
+ * The KV cache moves into the context: it is device-resident, fp32 as in the
+ * reference, paged (page_tokens positions per page, one page table per
+ * sequence shared by all layers) so that several sequences share one pool.
+ *
+ * Conventions
+ *  - Every function returns KORE_CUDA_OK (0) or a negative KORE_CUDA_E* code
+ *    and leaves a message for kore_cuda_last_error(); none aborts or exits.
+ *    kore maps a non-zero return to `return false` from forward() /
+ *    forward_batch(), as it does for a bad token or position
+ *    (kore.cpp:1400, :1490).
+ *  - Host-pointer entry points copy their inputs to the device, run on the
+ *    context's stream, copy the output back and return once it is valid.
+ *  - *_dev entry points take device pointers, are ordered on the context's
+ *    stream and return without synchronising; kore_cuda_sync() waits and
+ *    reports any error raised on the device since the last check.
+ *  - A context is not re-entrant: one host thread at a time (kore calls
+ *    attention from its main thread, or from the HTTP handler under the
+ *    session mutex, kore.cpp:2600).
+ */
+#ifndef KORE_CUDA_H
+#define KORE_CUDA_H
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define KORE_CUDA_ABI_VERSION 1
+
+enum kore_cuda_status {
+    KORE_CUDA_OK = 0,
+    KORE_CUDA_EINVAL = -1,   /* bad argument: shape, null pointer, unsupported head_dim */
+    KORE_CUDA_ERANGE = -2,   /* seq / layer / position outside the limits (kore.cpp:1400, :1490) */
+    KORE_CUDA_ENOMEM = -3,   /* device memory or KV pages exhausted */
+    KORE_CUDA_ECUDA = -4,    /* a CUDA runtime call failed */
+    KORE_CUDA_ESTATE = -5,   /* out-of-order call, e.g. attending at pos with rows missing below it */
+    KORE_CUDA_EDEVICE = -6,  /* a kernel reported an error (bounded wait expired, bad page) */
+    KORE_CUDA_ENCCL = -7     /* a cross-GPU exchange failed */
+};
+
+typedef struct kore_cuda_ctx kore_cuda_ctx;
+
+typedef struct kore_cuda_cfg {
+    int n_layer;            /* hp.n_layer */
+    int n_head;             /* hp.n_head, H */
+    int n_head_kv;          /* hp.n_head_kv, G; H % G == 0, H/G <= 8 */
+    int head_dim;           /* e.head_dim, d: 64 or 128 */
+    int ctx_max;            /* e.ctx: positions per sequence (kore.cpp:1291) */
+    int max_seqs;           /* sequences sharing the page pool; kore's single session uses 1 */
+    int page_tokens;        /* positions per KV page, a multiple of 64; 0 selects 256 */
+    int n_pages;            /* pages per layer in the pool; 0 selects max_seqs*ceil(ctx_max/page_tokens) */
+    float rope_base;        /* hp.rope_base (kore.cpp:230) */
+    const float *inv_freq;  /* optional host [head_dim/2], e.inv_freq; NULL builds it as kore.cpp:1339 */
+    int device;             /* CUDA device ordinal */
+    int shard_rank;         /* KV-sequence split over GPUs: this context holds the positions of */
+    int shard_count;        /*   every page j with j % shard_count == shard_rank; 0/1 = unsplit */
+} kore_cuda_cfg;
+
+/* Fills *cfg with defaults for the given geometry (page_tokens 256, one
+ * sequence, rope_base 1e6, device 0, unsplit). */
+void kore_cuda_cfg_default(kore_cuda_cfg *cfg, int n_layer, int n_head, int n_head_kv,
+                           int head_dim, int ctx_max);
+
+/* Creates a context: KV page pool for all layers, RoPE angle tables for
+ * positions [0, ctx_max) built on the host exactly as kore.cpp:1405-1410
+ * builds them, a stream and staging buffers. Replaces the KV allocation of
+ * engine_init (kore.cpp:1344-1345). */
+int kore_cuda_create(kore_cuda_ctx **out, const kore_cuda_cfg *cfg);
+void kore_cuda_destroy(kore_cuda_ctx *ctx);
+
+/* Message for the last failed call on ctx (or on a failed create when ctx is
+ * NULL). Never NULL. */
+const char *kore_cuda_last_error(const kore_cuda_ctx *ctx);
+
+/* Drops a sequence's pages: kore starting a new conversation, or about to
+ * re-prefill from position 0 (condense, kore.cpp:1790-1796). */
+int kore_cuda_seq_reset(kore_cuda_ctx *ctx, int seq);
+
+/* Number of positions of (seq, layer) currently held, i.e. the next position
+ * that may be appended. */
+int kore_cuda_seq_len(const kore_cuda_ctx *ctx, int seq, int layer);
+
+/*
+ * RoPE + append of n tokens at positions pos0..pos0+n-1 of (seq, layer):
+ * k is rotated with the tables of its position and stored, v is stored as
+ * is (kore.cpp:1425, :1429-1430 for one token; :1534-1538 per batch row).
+ *   k, v: [n][n_head_kv*head_dim], bias-added, pre-RoPE
+ * pos0 may not exceed the current length (no holes); rows at and past pos0
+ * are overwritten.
+ */
+int kore_cuda_kv_append(kore_cuda_ctx *ctx, int seq, int layer, int pos0, int n,
+                        const float *k, const float *v);
+int kore_cuda_kv_append_dev(kore_cuda_ctx *ctx, int seq, int layer, int pos0, int n,
+                            const float *k, const float *v);
+
+/*
+ * Prefill chunk, replacing kore.cpp:1527-1563: appends k/v for positions
+ * pos0..pos0+n-1 (as kore_cuda_kv_append), then causal grouped-query
+ * attention of the n queries (RoPE'd at their positions) over positions
+ * 0..pos0+z for query row z.
+ *   q: [n][n_head*head_dim], k, v: [n][n_head_kv*head_dim]   (pre-RoPE)
+ *   out: [n][n_head*head_dim]                                 (e.batt rows)
+ * n is not limited to kore's 64-token batch (KORE_BMAX, kore.cpp:690).
+ */
+int kore_cuda_attn_prefill(kore_cuda_ctx *ctx, int seq, int layer, int pos0, int n,
+                           const float *q, const float *k, const float *v, float *out);
+int kore_cuda_attn_prefill_dev(kore_cuda_ctx *ctx, int seq, int layer, int pos0, int n,
+                               const float *q, const float *k, const float *v, float *out);
+
+/*
+ * Decode step, replacing kore.cpp:1424-1455 for one layer: RoPE of q and k
+ * at `pos`, append of k/v at `pos`, attention of the n_head queries over
+ * positions 0..pos.
+ *   q: [n_head*head_dim], k, v: [n_head_kv*head_dim]   (pre-RoPE)
+ *   out: [n_head*head_dim]                             (e.att)
+ */
+int kore_cuda_attn_decode(kore_cuda_ctx *ctx, int seq, int layer, int pos,
+                          const float *q, const float *k, const float *v, float *out);
+int kore_cuda_attn_decode_dev(kore_cuda_ctx *ctx, int seq, int layer, int pos,
+                              const float *q, const float *k, const float *v, float *out);
+
+/*
+ * Decode step for n_seq sequences at once (one token each, own positions):
+ * the batched form of kore_cuda_attn_decode over the shared page pool.
+ *   seq_ids, pos: host arrays [n_seq]
+ *   q: [n_seq][n_head*head_dim], k, v: [n_seq][n_head_kv*head_dim], out like q
+ */
+int kore_cuda_attn_decode_batch(kore_cuda_ctx *ctx, int layer, int n_seq, const int *seq_ids,
+                                const int *pos, const float *q, const float *k, const float *v,
+                                float *out);
+int kore_cuda_attn_decode_batch_dev(kore_cuda_ctx *ctx, int layer, int n_seq, const int *seq_ids,
+                                    const int *pos, const float *q, const float *k, const float *v,
+                                    float *out);
+
+/*
+ * KV-sequence split over GPUs (cfg.shard_count > 1). Each context holds the
+ * positions of every page j with j % shard_count == shard_rank; a decode step
+ * then runs in two parts:
+ *   kore_cuda_attn_decode_partial_dev: this shard's share of the decode at
+ *     pos (the owner of pos also appends k/v there). `part` receives the
+ *     packed partial [n_head*head_dim outputs normalised by this shard's own
+ *     softmax sum][n_head log2-domain log-sum-exp values], -inf where the
+ *     shard holds none of positions 0..pos.
+ *   kore_cuda_lse_merge_dev: merges n_parts packed partials (laid out one
+ *     after another, as an all-gather leaves them) into out [n_head*head_dim].
+ * The merge is kore's single softmax (kore.cpp:1437-1454) regrouped by shard.
+ * Device pointers; stream-ordered.
+ */
+int kore_cuda_attn_decode_partial_dev(kore_cuda_ctx *ctx, int seq, int layer, int pos,
+                                      const float *q, const float *k, const float *v, float *part);
+int kore_cuda_lse_merge_dev(kore_cuda_ctx *ctx, int n_parts, const float *parts, float *out);
+
+/* Copies positions pos0..pos0+n-1 of (seq, layer) back to the host in kore's
+ * row layout, k_out/v_out [n][n_head_kv*head_dim] (post-RoPE keys), so that a
+ * caller can compare with or restore Engine::kcache/vcache. */
+int kore_cuda_kv_read(kore_cuda_ctx *ctx, int seq, int layer, int pos0, int n,
+                      float *k_out, float *v_out);
+
+/* Waits for the context's stream; returns KORE_CUDA_EDEVICE if a kernel
+ * raised its error flag since the last check. */
+int kore_cuda_sync(kore_cuda_ctx *ctx);
+
+/* The context's stream (a cudaStream_t) and a way to replace it with the
+ * caller's (for interop with an engine that already owns a stream). */
+void *kore_cuda_stream(kore_cuda_ctx *ctx);
+int kore_cuda_set_stream(kore_cuda_ctx *ctx, void *stream);
+
+#ifdef __cplusplus
+}
+#endif
+#endif /* KORE_CUDA_H */

@@ -1,0 +1,255 @@
+"""kore_b200 — B200 attention path for kore (BJZR/kore), behind a C ABI.
+
+The product is ``kore_b200/libkore_cuda.so`` (sources in ``kore_b200/csrc``,
+ABI in ``include/kore_cuda.h``). This module binds it with ctypes and mirrors
+kore's per-layer attention call: ``decode`` replaces kore.cpp:1424-1455 and
+``prefill`` kore.cpp:1527-1563, with kore's host buffers (numpy arrays here);
+the ``*_dev`` forms take device tensors and stay on the context's stream.
+
+There is no fallback: if the library is missing, importing this module works
+but creating a context raises, naming the build command.
+"""
+from __future__ import annotations
+
+import ctypes
+import os
+import re
+
+import numpy as np
+
+from .build import LIB, INCLUDE
+
+__all__ = ["KoreCuda", "KoreCudaError", "load_library", "declared_symbols", "STATUS"]
+
+STATUS = {
+    0: "KORE_CUDA_OK", -1: "KORE_CUDA_EINVAL", -2: "KORE_CUDA_ERANGE", -3: "KORE_CUDA_ENOMEM",
+    -4: "KORE_CUDA_ECUDA", -5: "KORE_CUDA_ESTATE", -6: "KORE_CUDA_EDEVICE", -7: "KORE_CUDA_ENCCL",
+}
+
+
+class KoreCudaError(RuntimeError):
+    def __init__(self, code: int, msg: str):
+        super().__init__(f"{STATUS.get(code, code)}: {msg}")
+        self.code = code
+
+
+class _Cfg(ctypes.Structure):
+    _fields_ = [
+        ("n_layer", ctypes.c_int), ("n_head", ctypes.c_int), ("n_head_kv", ctypes.c_int),
+        ("head_dim", ctypes.c_int), ("ctx_max", ctypes.c_int), ("max_seqs", ctypes.c_int),
+        ("page_tokens", ctypes.c_int), ("n_pages", ctypes.c_int), ("rope_base", ctypes.c_float),
+        ("inv_freq", ctypes.POINTER(ctypes.c_float)), ("device", ctypes.c_int),
+        ("shard_rank", ctypes.c_int), ("shard_count", ctypes.c_int),
+    ]
+
+
+_lib = None
+_vp = ctypes.c_void_p
+_ip = ctypes.POINTER(ctypes.c_int)
+_i = ctypes.c_int
+
+
+def declared_symbols() -> list[str]:
+    """Entry points declared in include/*.h (the ABI the library must export)."""
+    names: list[str] = []
+    for fn in sorted(os.listdir(INCLUDE)):
+        if fn.endswith(".h"):
+            src = open(os.path.join(INCLUDE, fn)).read()
+            src = re.sub(r"/\*.*?\*/", "", src, flags=re.S)
+            names += re.findall(r"\b(kore_cuda_\w+)\s*\(", src)
+    return sorted(set(names))
+
+
+def load_library(path: str = LIB):
+    global _lib
+    if _lib is not None:
+        return _lib
+    if not os.path.exists(path):
+        raise ImportError(f"{path} is missing: build it with `python -m kore_b200.build`")
+    L = ctypes.CDLL(path)
+    L.kore_cuda_cfg_default.argtypes = [ctypes.POINTER(_Cfg)] + [_i] * 5
+    L.kore_cuda_cfg_default.restype = None
+    L.kore_cuda_create.argtypes = [ctypes.POINTER(_vp), ctypes.POINTER(_Cfg)]
+    L.kore_cuda_destroy.argtypes = [_vp]
+    L.kore_cuda_destroy.restype = None
+    L.kore_cuda_last_error.argtypes = [_vp]
+    L.kore_cuda_last_error.restype = ctypes.c_char_p
+    L.kore_cuda_seq_reset.argtypes = [_vp, _i]
+    L.kore_cuda_seq_len.argtypes = [_vp, _i, _i]
+    for n in ("kore_cuda_kv_append", "kore_cuda_kv_append_dev"):
+        getattr(L, n).argtypes = [_vp, _i, _i, _i, _i, _vp, _vp]
+    for n in ("kore_cuda_attn_prefill", "kore_cuda_attn_prefill_dev"):
+        getattr(L, n).argtypes = [_vp, _i, _i, _i, _i, _vp, _vp, _vp, _vp]
+    for n in ("kore_cuda_attn_decode", "kore_cuda_attn_decode_dev"):
+        getattr(L, n).argtypes = [_vp, _i, _i, _i, _vp, _vp, _vp, _vp]
+    for n in ("kore_cuda_attn_decode_batch", "kore_cuda_attn_decode_batch_dev"):
+        getattr(L, n).argtypes = [_vp, _i, _i, _ip, _ip, _vp, _vp, _vp, _vp]
+    L.kore_cuda_attn_decode_partial_dev.argtypes = [_vp, _i, _i, _i, _vp, _vp, _vp, _vp]
+    L.kore_cuda_lse_merge_dev.argtypes = [_vp, _i, _vp, _vp]
+    L.kore_cuda_kv_read.argtypes = [_vp, _i, _i, _i, _i, _vp, _vp]
+    L.kore_cuda_sync.argtypes = [_vp]
+    L.kore_cuda_stream.argtypes = [_vp]
+    L.kore_cuda_stream.restype = _vp
+    L.kore_cuda_set_stream.argtypes = [_vp, _vp]
+    _lib = L
+    return L
+
+
+def _host(a, n: int) -> np.ndarray:
+    a = np.ascontiguousarray(a, dtype=np.float32).reshape(-1)
+    if a.size != n:
+        raise ValueError(f"expected {n} floats, got {a.size}")
+    return a
+
+
+def _dptr(t) -> int:
+    """Device address of a contiguous fp32 CUDA tensor."""
+    if not (t.is_cuda and t.dtype.__str__() == "torch.float32" and t.is_contiguous()):
+        raise ValueError("expected a contiguous float32 CUDA tensor")
+    return t.data_ptr()
+
+
+class KoreCuda:
+    """One attention context: the paged KV cache of every layer of a model,
+    for up to ``max_seqs`` sequences, on one GPU (or one shard of the KV
+    positions when ``shard_count`` > 1)."""
+
+    def __init__(self, n_layer: int, n_head: int, n_head_kv: int, head_dim: int, ctx_max: int, *,
+                 max_seqs: int = 1, page_tokens: int = 256, n_pages: int = 0, rope_base: float = 1e6,
+                 inv_freq=None, device: int = 0, shard_rank: int = 0, shard_count: int = 1):
+        L = load_library()
+        cfg = _Cfg()
+        L.kore_cuda_cfg_default(ctypes.byref(cfg), n_layer, n_head, n_head_kv, head_dim, ctx_max)
+        cfg.max_seqs, cfg.page_tokens, cfg.n_pages = max_seqs, page_tokens, n_pages
+        cfg.rope_base, cfg.device = rope_base, device
+        cfg.shard_rank, cfg.shard_count = shard_rank, shard_count
+        self._inv = None
+        if inv_freq is not None:
+            self._inv = np.ascontiguousarray(inv_freq, np.float32)
+            cfg.inv_freq = self._inv.ctypes.data_as(ctypes.POINTER(ctypes.c_float))
+        h = _vp()
+        rc = L.kore_cuda_create(ctypes.byref(h), ctypes.byref(cfg))
+        if rc:
+            raise KoreCudaError(rc, L.kore_cuda_last_error(None).decode())
+        self._h = h
+        self._L = L
+        self.n_layer, self.H, self.G, self.d, self.ctx_max = n_layer, n_head, n_head_kv, head_dim, ctx_max
+        self.kvd = n_head_kv * head_dim
+
+    # ---------------------------------------------------------------- plumbing
+    def close(self) -> None:
+        if getattr(self, "_h", None):
+            self._L.kore_cuda_destroy(self._h)
+            self._h = None
+
+    def __del__(self):
+        self.close()
+
+    def __enter__(self):
+        return self
+
+    def __exit__(self, *a):
+        self.close()
+
+    def _ck(self, rc: int) -> None:
+        if rc:
+            raise KoreCudaError(rc, self._L.kore_cuda_last_error(self._h).decode())
+
+    @property
+    def handle(self) -> int:
+        return self._h.value
+
+    @property
+    def stream(self) -> int:
+        return self._L.kore_cuda_stream(self._h) or 0
+
+    def set_stream(self, stream: int) -> None:
+        self._ck(self._L.kore_cuda_set_stream(self._h, stream))
+
+    def sync(self) -> None:
+        self._ck(self._L.kore_cuda_sync(self._h))
+
+    def seq_reset(self, seq: int) -> None:
+        self._ck(self._L.kore_cuda_seq_reset(self._h, seq))
+
+    def seq_len(self, seq: int, layer: int) -> int:
+        r = self._L.kore_cuda_seq_len(self._h, seq, layer)
+        if r < 0:
+            raise KoreCudaError(r, "seq/layer out of range")
+        return r
+
+    # ---------------------------------------------------------------- host buffers (kore's path)
+    def append(self, seq: int, layer: int, pos0: int, k, v) -> None:
+        k = np.ascontiguousarray(k, np.float32).reshape(-1, self.kvd)
+        n = k.shape[0]
+        v = _host(v, n * self.kvd)
+        self._ck(self._L.kore_cuda_kv_append(self._h, seq, layer, pos0, n, k.ctypes.data, v.ctypes.data))
+
+    def decode(self, seq: int, layer: int, pos: int, q, k, v) -> np.ndarray:
+        q = _host(q, self.H * self.d)
+        k = _host(k, self.kvd)
+        v = _host(v, self.kvd)
+        out = np.empty(self.H * self.d, np.float32)
+        self._ck(self._L.kore_cuda_attn_decode(self._h, seq, layer, pos, q.ctypes.data, k.ctypes.data,
+                                               v.ctypes.data, out.ctypes.data))
+        return out.reshape(self.H, self.d)
+
+    def decode_batch(self, layer: int, seqs, pos, q, k, v) -> np.ndarray:
+        seqs = np.ascontiguousarray(seqs, np.int32)
+        pos = np.ascontiguousarray(pos, np.int32)
+        n = seqs.size
+        q = _host(q, n * self.H * self.d)
+        k = _host(k, n * self.kvd)
+        v = _host(v, n * self.kvd)
+        out = np.empty(n * self.H * self.d, np.float32)
+        self._ck(self._L.kore_cuda_attn_decode_batch(self._h, layer, n, seqs.ctypes.data_as(_ip),
+                                                     pos.ctypes.data_as(_ip), q.ctypes.data, k.ctypes.data,
+                                                     v.ctypes.data, out.ctypes.data))
+        return out.reshape(n, self.H, self.d)
+
+    def prefill(self, seq: int, layer: int, pos0: int, q, k, v) -> np.ndarray:
+        q = np.ascontiguousarray(q, np.float32).reshape(-1, self.H * self.d)
+        n = q.shape[0]
+        k = _host(k, n * self.kvd)
+        v = _host(v, n * self.kvd)
+        out = np.empty((n, self.H * self.d), np.float32)
+        self._ck(self._L.kore_cuda_attn_prefill(self._h, seq, layer, pos0, n, q.ctypes.data, k.ctypes.data,
+                                                v.ctypes.data, out.ctypes.data))
+        return out.reshape(n, self.H, self.d)
+
+    def kv_read(self, seq: int, layer: int, pos0: int, n: int):
+        k = np.zeros((n, self.kvd), np.float32)
+        v = np.zeros((n, self.kvd), np.float32)
+        self._ck(self._L.kore_cuda_kv_read(self._h, seq, layer, pos0, n, k.ctypes.data, v.ctypes.data))
+        return k, v
+
+    # ---------------------------------------------------------------- device tensors (stream-ordered)
+    def append_dev(self, seq: int, layer: int, pos0: int, n: int, k, v) -> None:
+        self._ck(self._L.kore_cuda_kv_append_dev(self._h, seq, layer, pos0, n, _dptr(k), _dptr(v)))
+
+    def decode_dev(self, seq: int, layer: int, pos: int, q, k, v, out) -> None:
+        self._ck(self._L.kore_cuda_attn_decode_dev(self._h, seq, layer, pos, _dptr(q), _dptr(k), _dptr(v),
+                                                   _dptr(out)))
+
+    def decode_batch_dev(self, layer: int, seqs, pos, q, k, v, out) -> None:
+        seqs = np.ascontiguousarray(seqs, np.int32)
+        pos = np.ascontiguousarray(pos, np.int32)
+        self._ck(self._L.kore_cuda_attn_decode_batch_dev(self._h, layer, seqs.size, seqs.ctypes.data_as(_ip),
+                                                         pos.ctypes.data_as(_ip), _dptr(q), _dptr(k), _dptr(v),
+                                                         _dptr(out)))
+
+    def decode_partial_dev(self, seq: int, layer: int, pos: int, q, k, v, part) -> None:
+        """KV-sharded decode: packed partial [H*d outputs][H log2-LSE] of this shard."""
+        self._ck(self._L.kore_cuda_attn_decode_partial_dev(self._h, seq, layer, pos, _dptr(q), _dptr(k), _dptr(v),
+                                                           _dptr(part)))
+
+    def lse_merge_dev(self, n_parts: int, parts, out) -> None:
+        self._ck(self._L.kore_cuda_lse_merge_dev(self._h, n_parts, _dptr(parts), _dptr(out)))
+
+    @property
+    def part_floats(self) -> int:
+        return self.H * self.d + self.H
+
+    def prefill_dev(self, seq: int, layer: int, pos0: int, n: int, q, k, v, out) -> None:
+        self._ck(self._L.kore_cuda_attn_prefill_dev(self._h, seq, layer, pos0, n, _dptr(q), _dptr(k), _dptr(v),
+                                                    _dptr(out)))

@@ -1,0 +1,62 @@
+// attn.cuh — parameter blocks and launchers of the attention kernels.
+#pragma once
+
+#include <cuda_runtime.h>
+
+namespace kore {
+
+constexpr int kMaxBatch = 256;    // queries per decode launch given by (seq, pos) list
+constexpr int kMaxSplits = 256;   // KV splits per (query, kv head)
+
+// One layer's slice of the paged KV pool.
+//   K of (page, head g, token t) at k[((page*G + g)*P + t)*D], V likewise at
+//   k + v_off: every head's run of P tokens in a page is contiguous, so a
+//   tile of consecutive tokens of one head is one linear bulk copy.
+struct PagedKv {
+    float *k;
+    long long v_off;           // floats from the K pool to the V pool
+    const int *page_table;     // [max_seqs][pt_stride] physical page per local page
+    int pt_stride;
+    int P, G, D, n_pages;
+    int shard_rank, shard_count;
+};
+
+struct DecodeParams {
+    PagedKv kv;
+    const float *q;            // [n_q][H*D] pre-RoPE
+    const float *k_new;        // [n_q][G*D] pre-RoPE (append_new only)
+    const float *v_new;        // [n_q][G*D]
+    float *out;                // [n_q][H*D]
+    float *lse;                // optional [n_q][H], log2-domain LSE of a partial result
+    const float2 *rope;        // [ctx_max][D/2] (cos, sin) as kore.cpp:1405-1410
+    float *part_o;             // split scratch [n_q][G][max_splits][R][D]
+    float2 *part_ml;           // split scratch [n_q][G][max_splits][R] (max, sum)
+    unsigned *counters;        // [n_q][G] arrival counters, self-resetting
+    int *err;                  // device error word
+    float scale_log2;          // (1/sqrt(D)) * log2(e)
+    int H, n_q, split_tokens, max_splits;
+    int append_new;            // 1: the token at pos comes from k_new/v_new and is appended
+    int contiguous;            // 1: query i is (seq0, pos0 + i); 0: seq[i], pos[i]
+    int seq0, pos0;
+    int seq[kMaxBatch];
+    int pos[kMaxBatch];
+};
+
+struct AppendParams {
+    PagedKv kv;
+    const float *k;            // [n][G*D] pre-RoPE
+    const float *v;            // [n][G*D]
+    const float2 *rope;
+    int *err;
+    int seq, pos0, n;
+};
+
+// Launch helpers (attn_decode.cu, kv_append.cu). Return cudaGetLastError().
+cudaError_t launch_attn_decode(const DecodeParams &p, int n_rep, int grid_x, cudaStream_t s);
+int decode_ctas_per_sm(int head_dim, int n_rep);
+int decode_tile_tokens();
+size_t decode_smem_bytes(int head_dim);
+cudaError_t launch_kv_append(const AppendParams &p, cudaStream_t s);
+cudaError_t launch_lse_merge(const float *parts, int n_parts, int H, int D, float *out, cudaStream_t s);
+
+}  // namespace kore

@@ -1,0 +1,613 @@
+// capi.cu — the C ABI of include/kore_cuda.h: context, paged KV pool, RoPE
+// tables, staging of host buffers, and the launch decisions (split sizing).
+//
+// Host-side restatements of reference arithmetic in this file:
+//   inv_freq  kore.cpp:1337-1339  (float)pow((double)rope_base, -2.0*i/head_dim)
+//   angles    kore.cpp:1405-1410  (float)cos/sin((double)pos * inv_freq[i])
+// They are computed once per context for every position below ctx_max, so the
+// device rotates with exactly the tables kore would build for that position.
+
+#include "../../include/kore_cuda.h"
+#include "attn.cuh"
+#include "common.cuh"
+
+#include <algorithm>
+#include <cmath>
+#include <cstdarg>
+#include <cstdio>
+#include <cstring>
+#include <string>
+#include <vector>
+
+using namespace kore;
+
+struct kore_cuda_ctx {
+    kore_cuda_cfg cfg{};
+    int H = 0, G = 0, D = 0, R = 0, kvd = 0, P = 0, NS = 1, rank = 0;
+    int pages_per_seq = 0;      // local page-table stride
+    int n_pages = 0;
+    int num_sms = 148;
+    cudaStream_t stream = nullptr;
+    bool own_stream = false;
+    float *kv = nullptr;        // [n_layer][2][n_pages][G][P][D]
+    size_t layer_floats = 0;
+    long long v_off = 0;
+    int *pt_d = nullptr;
+    std::vector<int> pt_h;      // [max_seqs][pages_per_seq]
+    std::vector<int> free_pages;
+    std::vector<int> seq_alloc; // local pages held per sequence
+    std::vector<int> seq_len;   // [max_seqs][n_layer] positions held
+    float2 *rope_d = nullptr;   // [ctx_max][D/2]
+    float *part_o = nullptr;
+    float2 *part_ml = nullptr;
+    size_t part_slots = 0;      // (query, kv head, split) slots of split scratch
+    unsigned *counters = nullptr;
+    int *err_d = nullptr;
+    float *dev_stage = nullptr;
+    size_t dev_stage_floats = 0;
+    float *host_stage = nullptr;
+    size_t host_stage_floats = 0;
+    int *host_err = nullptr;
+    std::string msg;
+};
+
+namespace {
+
+thread_local std::string g_create_msg = "no error";
+
+int fail(kore_cuda_ctx *c, int code, const char *fmt, ...) {
+    char buf[512];
+    va_list ap;
+    va_start(ap, fmt);
+    vsnprintf(buf, sizeof buf, fmt, ap);
+    va_end(ap);
+    if (c) c->msg = buf;
+    else g_create_msg = buf;
+    return code;
+}
+
+#define CK(call)                                                                                   \
+    do {                                                                                           \
+        cudaError_t e_ = (call);                                                                   \
+        if (e_ != cudaSuccess)                                                                     \
+            return fail(c, e_ == cudaErrorMemoryAllocation ? KORE_CUDA_ENOMEM : KORE_CUDA_ECUDA,    \
+                        "%s: %s", #call, cudaGetErrorString(e_));                                  \
+    } while (0)
+
+struct DeviceGuard {
+    int prev = -1;
+    explicit DeviceGuard(int dev) {
+        if (cudaGetDevice(&prev) == cudaSuccess && prev != dev) cudaSetDevice(dev);
+    }
+    ~DeviceGuard() {
+        int cur;
+        if (prev >= 0 && cudaGetDevice(&cur) == cudaSuccess && cur != prev) cudaSetDevice(prev);
+    }
+};
+
+constexpr size_t kPartSlots = 8192;
+
+// Local pages (held by this shard) among global pages [0, gpages).
+int local_pages(const kore_cuda_ctx *c, int gpages) {
+    return gpages > c->rank ? (gpages - c->rank + c->NS - 1) / c->NS : 0;
+}
+
+// Cached positions below `limit` held by this shard (same formula as the kernel).
+int local_count(const kore_cuda_ctx *c, int limit) {
+    const int F = limit / c->P, rem = limit - F * c->P;
+    return local_pages(c, F) * c->P + ((F % c->NS == c->rank) ? rem : 0);
+}
+
+PagedKv layer_kv(const kore_cuda_ctx *c, int layer) {
+    PagedKv kv;
+    kv.k = c->kv + (size_t)layer * c->layer_floats;
+    kv.v_off = c->v_off;
+    kv.page_table = c->pt_d;
+    kv.pt_stride = c->pages_per_seq;
+    kv.P = c->P;
+    kv.G = c->G;
+    kv.D = c->D;
+    kv.n_pages = c->n_pages;
+    kv.shard_rank = c->rank;
+    kv.shard_count = c->NS;
+    return kv;
+}
+
+int check_seq_layer(kore_cuda_ctx *c, int seq, int layer) {
+    if (seq < 0 || seq >= c->cfg.max_seqs) return fail(c, KORE_CUDA_ERANGE, "seq %d outside [0, %d)", seq, c->cfg.max_seqs);
+    if (layer < 0 || layer >= c->cfg.n_layer)
+        return fail(c, KORE_CUDA_ERANGE, "layer %d outside [0, %d)", layer, c->cfg.n_layer);
+    return KORE_CUDA_OK;
+}
+
+// Positions [pos0, pos0+n) may be written when pos0 does not leave a hole
+// below it and the range stays inside the context (kore.cpp:1400, :1490).
+int check_range(kore_cuda_ctx *c, int seq, int layer, int pos0, int n) {
+    if (int rc = check_seq_layer(c, seq, layer)) return rc;
+    if (n <= 0) return fail(c, KORE_CUDA_EINVAL, "n = %d must be positive", n);
+    if (pos0 < 0 || (long long)pos0 + n > c->cfg.ctx_max)
+        return fail(c, KORE_CUDA_ERANGE, "positions [%d, %lld) outside the context of %d", pos0,
+                    (long long)pos0 + n, c->cfg.ctx_max);
+    const int len = c->seq_len[(size_t)seq * c->cfg.n_layer + layer];
+    if (pos0 > len)
+        return fail(c, KORE_CUDA_ESTATE, "seq %d layer %d holds %d positions; cannot write at %d", seq, layer, len, pos0);
+    return KORE_CUDA_OK;
+}
+
+// Makes sure every page holding positions below `end` is allocated.
+int ensure_pages(kore_cuda_ctx *c, int seq, int end) {
+    const int need = local_pages(c, (end + c->P - 1) / c->P);
+    const int have = c->seq_alloc[seq];
+    if (need <= have) return KORE_CUDA_OK;
+    if ((size_t)(need - have) > c->free_pages.size())
+        return fail(c, KORE_CUDA_ENOMEM, "KV page pool exhausted (%d pages per layer)", c->n_pages);
+    int *row = c->pt_h.data() + (size_t)seq * c->pages_per_seq;
+    for (int j = have; j < need; ++j) {
+        row[j] = c->free_pages.back();
+        c->free_pages.pop_back();
+    }
+    c->seq_alloc[seq] = need;
+    CK(cudaMemcpyAsync(c->pt_d + (size_t)seq * c->pages_per_seq + have, row + have, (size_t)(need - have) * sizeof(int),
+                       cudaMemcpyHostToDevice, c->stream));
+    return KORE_CUDA_OK;
+}
+
+void note_len(kore_cuda_ctx *c, int seq, int layer, int end) {
+    int &len = c->seq_len[(size_t)seq * c->cfg.n_layer + layer];
+    len = std::max(len, end);
+}
+
+int grow_stage(kore_cuda_ctx *c, size_t floats) {
+    if (floats > c->dev_stage_floats) {
+        if (c->dev_stage) cudaFree(c->dev_stage);
+        c->dev_stage = nullptr;
+        c->dev_stage_floats = 0;
+        CK(cudaMalloc(&c->dev_stage, floats * sizeof(float)));
+        c->dev_stage_floats = floats;
+    }
+    if (floats > c->host_stage_floats) {
+        if (c->host_stage) cudaFreeHost(c->host_stage);
+        c->host_stage = nullptr;
+        c->host_stage_floats = 0;
+        CK(cudaMallocHost(&c->host_stage, floats * sizeof(float)));
+        c->host_stage_floats = floats;
+    }
+    return KORE_CUDA_OK;
+}
+
+// Reads and clears the device error word (stream-ordered, then synchronises).
+int finish(kore_cuda_ctx *c) {
+    CK(cudaMemcpyAsync(c->host_err, c->err_d, sizeof(int), cudaMemcpyDeviceToHost, c->stream));
+    CK(cudaStreamSynchronize(c->stream));
+    const int e = *c->host_err;
+    if (e != DEV_OK) {
+        CK(cudaMemsetAsync(c->err_d, 0, sizeof(int), c->stream));
+        CK(cudaMemsetAsync(c->counters, 0, sizeof(unsigned) * kMaxBatch * c->G, c->stream));
+        CK(cudaStreamSynchronize(c->stream));
+        return fail(c, KORE_CUDA_EDEVICE, "device error %d (%s)", e,
+                    e == DEV_BAD_PAGE ? "page table entry outside the pool"
+                                      : (e == DEV_WAIT_FULL_TIMEOUT ? "bounded wait for a K/V tile expired"
+                                                                    : "bounded wait for a free stage expired"));
+    }
+    return KORE_CUDA_OK;
+}
+
+int run_append(kore_cuda_ctx *c, int seq, int layer, int pos0, int n, const float *k, const float *v) {
+    AppendParams ap;
+    ap.kv = layer_kv(c, layer);
+    ap.k = k;
+    ap.v = v;
+    ap.rope = c->rope_d;
+    ap.err = c->err_d;
+    ap.seq = seq;
+    ap.pos0 = pos0;
+    ap.n = n;
+    CK(launch_kv_append(ap, c->stream));
+    return KORE_CUDA_OK;
+}
+
+// Launches the decode kernel for n_q queries. `contiguous` queries are
+// (seq0, pos0 + i); otherwise seqs[i], poss[i] (host arrays, n_q <= kMaxBatch).
+int run_decode(kore_cuda_ctx *c, int layer, int n_q, bool contiguous, int seq0, int pos0, const int *seqs,
+               const int *poss, const float *q, const float *k, const float *v, float *out, float *lse,
+               bool append_new) {
+    if (n_q <= 0) return fail(c, KORE_CUDA_EINVAL, "no queries");
+    if (!contiguous && n_q > kMaxBatch)
+        return fail(c, KORE_CUDA_EINVAL, "decode batch of %d exceeds %d sequences per call", n_q, kMaxBatch);
+    if (n_q > 65535) return fail(c, KORE_CUDA_EINVAL, "%d queries exceed one launch", n_q);
+    DecodeParams p;
+    memset(&p, 0, sizeof p);
+    p.kv = layer_kv(c, layer);
+    p.q = q;
+    p.k_new = k;
+    p.v_new = v;
+    p.out = out;
+    p.lse = lse;
+    p.rope = c->rope_d;
+    p.part_o = c->part_o;
+    p.part_ml = c->part_ml;
+    p.counters = c->counters;
+    p.err = c->err_d;
+    p.scale_log2 = (1.0f / std::sqrt((float)c->D)) * 1.4426950408889634f;
+    p.H = c->H;
+    p.n_q = n_q;
+    p.append_new = append_new ? 1 : 0;
+    p.contiguous = contiguous ? 1 : 0;
+    p.seq0 = seq0;
+    p.pos0 = pos0;
+    long long total = 0;
+    int max_count = 0;
+    for (int i = 0; i < n_q; ++i) {
+        const int ps = contiguous ? pos0 + i : poss[i];
+        if (!contiguous) {
+            p.seq[i] = seqs[i];
+            p.pos[i] = ps;
+        }
+        const int cnt = local_count(c, append_new ? ps : ps + 1);
+        total += cnt;
+        max_count = std::max(max_count, cnt);
+    }
+    const int TT = decode_tile_tokens();
+    const long long target = (long long)c->num_sms * decode_ctas_per_sm(c->D, c->R);
+    long long st = (total * c->G + target - 1) / target;
+    st = std::max<long long>(st, 4 * TT);
+    st = std::max<long long>(st, (max_count + kMaxSplits - 1) / kMaxSplits);
+    int grid_x;
+    if (n_q > kMaxBatch) {
+        st = std::max(max_count, TT);   // one split per query: no scratch, no counters
+    }
+    for (;;) {
+        st = (st + TT - 1) / TT * TT;
+        grid_x = std::max(1, (int)((max_count + st - 1) / st));
+        if (grid_x == 1 || (size_t)n_q * c->G * grid_x <= c->part_slots) break;
+        st *= 2;
+    }
+    if (grid_x > kMaxSplits) return fail(c, KORE_CUDA_EINVAL, "too many splits for one decode launch");
+    p.split_tokens = (int)st;
+    p.max_splits = grid_x;
+    CK(launch_attn_decode(p, c->R, grid_x, c->stream));
+    return KORE_CUDA_OK;
+}
+
+}  // namespace
+
+extern "C" {
+
+void kore_cuda_cfg_default(kore_cuda_cfg *cfg, int n_layer, int n_head, int n_head_kv, int head_dim, int ctx_max) {
+    memset(cfg, 0, sizeof *cfg);
+    cfg->n_layer = n_layer;
+    cfg->n_head = n_head;
+    cfg->n_head_kv = n_head_kv;
+    cfg->head_dim = head_dim;
+    cfg->ctx_max = ctx_max;
+    cfg->max_seqs = 1;
+    cfg->page_tokens = 256;
+    cfg->rope_base = 1e6f;
+    cfg->shard_count = 1;
+}
+
+const char *kore_cuda_last_error(const kore_cuda_ctx *c) { return c ? c->msg.c_str() : g_create_msg.c_str(); }
+
+void kore_cuda_destroy(kore_cuda_ctx *c) {
+    if (!c) return;
+    {
+        DeviceGuard dg(c->cfg.device);
+        if (c->stream) cudaStreamSynchronize(c->stream);
+        cudaFree(c->kv);
+        cudaFree(c->pt_d);
+        cudaFree(c->rope_d);
+        cudaFree(c->part_o);
+        cudaFree(c->part_ml);
+        cudaFree(c->counters);
+        cudaFree(c->err_d);
+        cudaFree(c->dev_stage);
+        if (c->host_stage) cudaFreeHost(c->host_stage);
+        if (c->host_err) cudaFreeHost(c->host_err);
+        if (c->own_stream && c->stream) cudaStreamDestroy(c->stream);
+    }
+    delete c;
+}
+
+int kore_cuda_create(kore_cuda_ctx **out, const kore_cuda_cfg *cfg) {
+    kore_cuda_ctx *c = nullptr;
+    if (!out || !cfg) return fail(c, KORE_CUDA_EINVAL, "null argument");
+    *out = nullptr;
+    const kore_cuda_cfg &f = *cfg;
+    if (f.n_layer <= 0 || f.n_head <= 0 || f.n_head_kv <= 0 || f.n_head % f.n_head_kv)
+        return fail(c, KORE_CUDA_EINVAL, "bad head geometry (n_layer %d, n_head %d, n_head_kv %d)", f.n_layer,
+                    f.n_head, f.n_head_kv);
+    if (f.n_head / f.n_head_kv > 8) return fail(c, KORE_CUDA_EINVAL, "n_head/n_head_kv = %d > 8", f.n_head / f.n_head_kv);
+    if (f.head_dim != 64 && f.head_dim != 128) return fail(c, KORE_CUDA_EINVAL, "head_dim %d not 64 or 128", f.head_dim);
+    if (f.ctx_max <= 0 || f.max_seqs <= 0) return fail(c, KORE_CUDA_EINVAL, "ctx_max and max_seqs must be positive");
+    if (!(f.rope_base > 0)) return fail(c, KORE_CUDA_EINVAL, "rope_base must be positive");
+    const int P = f.page_tokens ? f.page_tokens : 256;
+    if (P % 64 || P > 4096) return fail(c, KORE_CUDA_EINVAL, "page_tokens %d not a multiple of 64 up to 4096", P);
+    const int NS = f.shard_count > 1 ? f.shard_count : 1;
+    if (f.shard_rank < 0 || f.shard_rank >= NS) return fail(c, KORE_CUDA_EINVAL, "shard_rank %d outside [0, %d)", f.shard_rank, NS);
+
+    c = new kore_cuda_ctx;
+    c->cfg = f;
+    c->cfg.page_tokens = P;
+    c->cfg.shard_count = NS;
+    c->H = f.n_head;
+    c->G = f.n_head_kv;
+    c->D = f.head_dim;
+    c->R = f.n_head / f.n_head_kv;
+    c->kvd = c->G * c->D;
+    c->P = P;
+    c->NS = NS;
+    c->rank = f.shard_rank;
+    c->pages_per_seq = std::max(1, local_pages(c, (f.ctx_max + P - 1) / P));
+    c->n_pages = f.n_pages > 0 ? f.n_pages : f.max_seqs * c->pages_per_seq;
+    c->pt_h.assign((size_t)f.max_seqs * c->pages_per_seq, -1);
+    c->seq_alloc.assign((size_t)f.max_seqs, 0);
+    c->seq_len.assign((size_t)f.max_seqs * f.n_layer, 0);
+    for (int i = c->n_pages - 1; i >= 0; --i) c->free_pages.push_back(i);
+    c->cfg.inv_freq = nullptr;
+
+    auto bail = [&](int rc) {
+        g_create_msg = c->msg;
+        kore_cuda_destroy(c);
+        return rc;
+    };
+    int ndev = 0;
+    if (cudaGetDeviceCount(&ndev) != cudaSuccess || f.device < 0 || f.device >= ndev)
+        return bail(fail(c, KORE_CUDA_ECUDA, "CUDA device %d not available (%d visible)", f.device, ndev));
+    DeviceGuard dg(f.device);
+#define CKB(call)                                                                                  \
+    do {                                                                                           \
+        int rc_ = [&]() -> int { CK(call); return 0; }();                                          \
+        if (rc_) return bail(rc_);                                                                 \
+    } while (0)
+    CKB(cudaDeviceGetAttribute(&c->num_sms, cudaDevAttrMultiProcessorCount, f.device));
+    CKB(cudaStreamCreateWithFlags(&c->stream, cudaStreamNonBlocking));
+    c->own_stream = true;
+
+    c->layer_floats = (size_t)2 * c->n_pages * c->G * P * c->D;
+    c->v_off = (long long)c->n_pages * c->G * P * c->D;
+    CKB(cudaMalloc(&c->kv, c->layer_floats * f.n_layer * sizeof(float)));
+    CKB(cudaMemsetAsync(c->kv, 0, c->layer_floats * f.n_layer * sizeof(float), c->stream));
+    CKB(cudaMalloc(&c->pt_d, c->pt_h.size() * sizeof(int)));
+    CKB(cudaMemsetAsync(c->pt_d, 0xff, c->pt_h.size() * sizeof(int), c->stream));
+
+    // RoPE tables for every position, as kore builds them per call
+    const int half = c->D / 2;
+    std::vector<float> inv((size_t)half);
+    for (int i = 0; i < half; i++)
+        inv[(size_t)i] = f.inv_freq ? f.inv_freq[i] : (float)std::pow((double)f.rope_base, -2.0 * i / c->D);
+    std::vector<float2> tab((size_t)f.ctx_max * half);
+    for (int pos = 0; pos < f.ctx_max; ++pos)
+        for (int i = 0; i < half; i++) {
+            const double a = (double)pos * inv[(size_t)i];
+            tab[(size_t)pos * half + i] = make_float2((float)std::cos(a), (float)std::sin(a));
+        }
+    CKB(cudaMalloc(&c->rope_d, tab.size() * sizeof(float2)));
+    CKB(cudaMemcpyAsync(c->rope_d, tab.data(), tab.size() * sizeof(float2), cudaMemcpyHostToDevice, c->stream));
+
+    c->part_slots = kPartSlots;
+    CKB(cudaMalloc(&c->part_o, c->part_slots * c->R * c->D * sizeof(float)));
+    CKB(cudaMalloc(&c->part_ml, c->part_slots * c->R * sizeof(float2)));
+    CKB(cudaMalloc(&c->counters, sizeof(unsigned) * kMaxBatch * c->G));
+    CKB(cudaMemsetAsync(c->counters, 0, sizeof(unsigned) * kMaxBatch * c->G, c->stream));
+    CKB(cudaMalloc(&c->err_d, sizeof(int)));
+    CKB(cudaMemsetAsync(c->err_d, 0, sizeof(int), c->stream));
+    CKB(cudaMallocHost(&c->host_err, sizeof(int)));
+    CKB(cudaStreamSynchronize(c->stream));
+#undef CKB
+    c->msg = "no error";
+    *out = c;
+    return KORE_CUDA_OK;
+}
+
+int kore_cuda_seq_reset(kore_cuda_ctx *c, int seq) {
+    if (!c) return KORE_CUDA_EINVAL;
+    if (seq < 0 || seq >= c->cfg.max_seqs) return fail(c, KORE_CUDA_ERANGE, "seq %d outside [0, %d)", seq, c->cfg.max_seqs);
+    int *row = c->pt_h.data() + (size_t)seq * c->pages_per_seq;
+    for (int j = c->seq_alloc[seq] - 1; j >= 0; --j) {
+        c->free_pages.push_back(row[j]);
+        row[j] = -1;
+    }
+    c->seq_alloc[seq] = 0;
+    for (int l = 0; l < c->cfg.n_layer; ++l) c->seq_len[(size_t)seq * c->cfg.n_layer + l] = 0;
+    DeviceGuard dg(c->cfg.device);
+    CK(cudaMemcpyAsync(c->pt_d + (size_t)seq * c->pages_per_seq, row, (size_t)c->pages_per_seq * sizeof(int),
+                       cudaMemcpyHostToDevice, c->stream));
+    return KORE_CUDA_OK;
+}
+
+int kore_cuda_seq_len(const kore_cuda_ctx *c, int seq, int layer) {
+    if (!c || seq < 0 || seq >= c->cfg.max_seqs || layer < 0 || layer >= c->cfg.n_layer) return KORE_CUDA_ERANGE;
+    return c->seq_len[(size_t)seq * c->cfg.n_layer + layer];
+}
+
+int kore_cuda_kv_append_dev(kore_cuda_ctx *c, int seq, int layer, int pos0, int n, const float *k, const float *v) {
+    if (!c) return KORE_CUDA_EINVAL;
+    if (!k || !v) return fail(c, KORE_CUDA_EINVAL, "null k or v");
+    if (int rc = check_range(c, seq, layer, pos0, n)) return rc;
+    DeviceGuard dg(c->cfg.device);
+    if (int rc = ensure_pages(c, seq, pos0 + n)) return rc;
+    if (int rc = run_append(c, seq, layer, pos0, n, k, v)) return rc;
+    note_len(c, seq, layer, pos0 + n);
+    return KORE_CUDA_OK;
+}
+
+int kore_cuda_kv_append(kore_cuda_ctx *c, int seq, int layer, int pos0, int n, const float *k, const float *v) {
+    if (!c) return KORE_CUDA_EINVAL;
+    if (!k || !v) return fail(c, KORE_CUDA_EINVAL, "null k or v");
+    if (int rc = check_range(c, seq, layer, pos0, n)) return rc;
+    DeviceGuard dg(c->cfg.device);
+    const size_t nk = (size_t)n * c->kvd;
+    if (int rc = grow_stage(c, 2 * nk)) return rc;
+    memcpy(c->host_stage, k, nk * sizeof(float));
+    memcpy(c->host_stage + nk, v, nk * sizeof(float));
+    CK(cudaMemcpyAsync(c->dev_stage, c->host_stage, 2 * nk * sizeof(float), cudaMemcpyHostToDevice, c->stream));
+    if (int rc = kore_cuda_kv_append_dev(c, seq, layer, pos0, n, c->dev_stage, c->dev_stage + nk)) return rc;
+    return finish(c);
+}
+
+int kore_cuda_attn_prefill_dev(kore_cuda_ctx *c, int seq, int layer, int pos0, int n, const float *q, const float *k,
+                               const float *v, float *out) {
+    if (!c) return KORE_CUDA_EINVAL;
+    if (!q || !k || !v || !out) return fail(c, KORE_CUDA_EINVAL, "null q, k, v or out");
+    if (c->NS > 1) return fail(c, KORE_CUDA_EINVAL, "prefill on a KV-sharded context is not supported");
+    if (int rc = check_range(c, seq, layer, pos0, n)) return rc;
+    DeviceGuard dg(c->cfg.device);
+    if (int rc = ensure_pages(c, seq, pos0 + n)) return rc;
+    if (int rc = run_append(c, seq, layer, pos0, n, k, v)) return rc;
+    note_len(c, seq, layer, pos0 + n);
+    return run_decode(c, layer, n, true, seq, pos0, nullptr, nullptr, q, nullptr, nullptr, out, nullptr, false);
+}
+
+int kore_cuda_attn_prefill(kore_cuda_ctx *c, int seq, int layer, int pos0, int n, const float *q, const float *k,
+                           const float *v, float *out) {
+    if (!c) return KORE_CUDA_EINVAL;
+    if (!q || !k || !v || !out) return fail(c, KORE_CUDA_EINVAL, "null q, k, v or out");
+    if (int rc = check_range(c, seq, layer, pos0, n)) return rc;
+    DeviceGuard dg(c->cfg.device);
+    const size_t nq = (size_t)n * c->H * c->D, nk = (size_t)n * c->kvd;
+    if (int rc = grow_stage(c, 2 * nq + 2 * nk)) return rc;
+    float *hs = c->host_stage, *ds = c->dev_stage;
+    memcpy(hs, q, nq * sizeof(float));
+    memcpy(hs + nq, k, nk * sizeof(float));
+    memcpy(hs + nq + nk, v, nk * sizeof(float));
+    CK(cudaMemcpyAsync(ds, hs, (nq + 2 * nk) * sizeof(float), cudaMemcpyHostToDevice, c->stream));
+    float *dout = ds + nq + 2 * nk;
+    if (int rc = kore_cuda_attn_prefill_dev(c, seq, layer, pos0, n, ds, ds + nq, ds + nq + nk, dout)) return rc;
+    CK(cudaMemcpyAsync(hs + nq + 2 * nk, dout, nq * sizeof(float), cudaMemcpyDeviceToHost, c->stream));
+    if (int rc = finish(c)) return rc;
+    memcpy(out, hs + nq + 2 * nk, nq * sizeof(float));
+    return KORE_CUDA_OK;
+}
+
+int kore_cuda_attn_decode_batch_dev(kore_cuda_ctx *c, int layer, int n_seq, const int *seq_ids, const int *pos,
+                                    const float *q, const float *k, const float *v, float *out) {
+    if (!c) return KORE_CUDA_EINVAL;
+    if (!seq_ids || !pos || !q || !k || !v || !out) return fail(c, KORE_CUDA_EINVAL, "null argument");
+    if (n_seq <= 0 || n_seq > kMaxBatch) return fail(c, KORE_CUDA_EINVAL, "n_seq %d outside [1, %d]", n_seq, kMaxBatch);
+    for (int i = 0; i < n_seq; ++i) {
+        if (int rc = check_range(c, seq_ids[i], layer, pos[i], 1)) return rc;
+        for (int j = 0; j < i; ++j)
+            if (seq_ids[j] == seq_ids[i]) return fail(c, KORE_CUDA_EINVAL, "sequence %d appears twice", seq_ids[i]);
+    }
+    DeviceGuard dg(c->cfg.device);
+    for (int i = 0; i < n_seq; ++i)
+        if (int rc = ensure_pages(c, seq_ids[i], pos[i] + 1)) return rc;
+    if (int rc = run_decode(c, layer, n_seq, false, 0, 0, seq_ids, pos, q, k, v, out, nullptr, true)) return rc;
+    for (int i = 0; i < n_seq; ++i) note_len(c, seq_ids[i], layer, pos[i] + 1);
+    return KORE_CUDA_OK;
+}
+
+int kore_cuda_attn_decode_dev(kore_cuda_ctx *c, int seq, int layer, int pos, const float *q, const float *k,
+                              const float *v, float *out) {
+    if (!c) return KORE_CUDA_EINVAL;
+    if (!q || !k || !v || !out) return fail(c, KORE_CUDA_EINVAL, "null q, k, v or out");
+    if (int rc = check_range(c, seq, layer, pos, 1)) return rc;
+    DeviceGuard dg(c->cfg.device);
+    if (int rc = ensure_pages(c, seq, pos + 1)) return rc;
+    if (int rc = run_decode(c, layer, 1, true, seq, pos, nullptr, nullptr, q, k, v, out, nullptr, true)) return rc;
+    note_len(c, seq, layer, pos + 1);
+    return KORE_CUDA_OK;
+}
+
+int kore_cuda_attn_decode_partial_dev(kore_cuda_ctx *c, int seq, int layer, int pos, const float *q, const float *k,
+                                      const float *v, float *part) {
+    if (!c) return KORE_CUDA_EINVAL;
+    if (!q || !k || !v || !part) return fail(c, KORE_CUDA_EINVAL, "null q, k, v or part");
+    if (int rc = check_range(c, seq, layer, pos, 1)) return rc;
+    DeviceGuard dg(c->cfg.device);
+    if (int rc = ensure_pages(c, seq, pos + 1)) return rc;
+    float *lse = part + (size_t)c->H * c->D;
+    if (int rc = run_decode(c, layer, 1, true, seq, pos, nullptr, nullptr, q, k, v, part, lse, true)) return rc;
+    note_len(c, seq, layer, pos + 1);
+    return KORE_CUDA_OK;
+}
+
+int kore_cuda_lse_merge_dev(kore_cuda_ctx *c, int n_parts, const float *parts, float *out) {
+    if (!c) return KORE_CUDA_EINVAL;
+    if (!parts || !out || n_parts <= 0) return fail(c, KORE_CUDA_EINVAL, "bad merge arguments");
+    DeviceGuard dg(c->cfg.device);
+    CK(launch_lse_merge(parts, n_parts, c->H, c->D, out, c->stream));
+    return KORE_CUDA_OK;
+}
+
+static int decode_host(kore_cuda_ctx *c, int n_seq, const float *q, const float *k, const float *v, float *out,
+                       const int *seq_ids, const int *pos, int layer, bool batch) {
+    DeviceGuard dg(c->cfg.device);
+    const size_t nq = (size_t)n_seq * c->H * c->D, nk = (size_t)n_seq * c->kvd;
+    if (int rc = grow_stage(c, 2 * nq + 2 * nk)) return rc;
+    float *hs = c->host_stage, *ds = c->dev_stage;
+    memcpy(hs, q, nq * sizeof(float));
+    memcpy(hs + nq, k, nk * sizeof(float));
+    memcpy(hs + nq + nk, v, nk * sizeof(float));
+    CK(cudaMemcpyAsync(ds, hs, (nq + 2 * nk) * sizeof(float), cudaMemcpyHostToDevice, c->stream));
+    float *dout = ds + nq + 2 * nk;
+    int rc = batch ? kore_cuda_attn_decode_batch_dev(c, layer, n_seq, seq_ids, pos, ds, ds + nq, ds + nq + nk, dout)
+                   : kore_cuda_attn_decode_dev(c, seq_ids[0], layer, pos[0], ds, ds + nq, ds + nq + nk, dout);
+    if (rc) return rc;
+    CK(cudaMemcpyAsync(hs + nq + 2 * nk, dout, nq * sizeof(float), cudaMemcpyDeviceToHost, c->stream));
+    if (int rc2 = finish(c)) return rc2;
+    memcpy(out, hs + nq + 2 * nk, nq * sizeof(float));
+    return KORE_CUDA_OK;
+}
+
+int kore_cuda_attn_decode(kore_cuda_ctx *c, int seq, int layer, int pos, const float *q, const float *k,
+                          const float *v, float *out) {
+    if (!c) return KORE_CUDA_EINVAL;
+    if (!q || !k || !v || !out) return fail(c, KORE_CUDA_EINVAL, "null q, k, v or out");
+    if (int rc = check_range(c, seq, layer, pos, 1)) return rc;
+    return decode_host(c, 1, q, k, v, out, &seq, &pos, layer, false);
+}
+
+int kore_cuda_attn_decode_batch(kore_cuda_ctx *c, int layer, int n_seq, const int *seq_ids, const int *pos,
+                                const float *q, const float *k, const float *v, float *out) {
+    if (!c) return KORE_CUDA_EINVAL;
+    if (!seq_ids || !pos || !q || !k || !v || !out) return fail(c, KORE_CUDA_EINVAL, "null argument");
+    if (n_seq <= 0 || n_seq > kMaxBatch) return fail(c, KORE_CUDA_EINVAL, "n_seq %d outside [1, %d]", n_seq, kMaxBatch);
+    return decode_host(c, n_seq, q, k, v, out, seq_ids, pos, layer, true);
+}
+
+int kore_cuda_kv_read(kore_cuda_ctx *c, int seq, int layer, int pos0, int n, float *k_out, float *v_out) {
+    if (!c) return KORE_CUDA_EINVAL;
+    if (!k_out || !v_out) return fail(c, KORE_CUDA_EINVAL, "null output");
+    if (int rc = check_seq_layer(c, seq, layer)) return rc;
+    const int len = c->seq_len[(size_t)seq * c->cfg.n_layer + layer];
+    if (n <= 0 || pos0 < 0 || pos0 + n > len)
+        return fail(c, KORE_CUDA_ERANGE, "positions [%d, %d) outside the %d held", pos0, pos0 + n, len);
+    DeviceGuard dg(c->cfg.device);
+    CK(cudaStreamSynchronize(c->stream));
+    const int *row = c->pt_h.data() + (size_t)seq * c->pages_per_seq;
+    const size_t D = c->D;
+    for (int z = 0; z < n; ++z) {
+        const int pos = pos0 + z, gp = pos / c->P;
+        if (gp % c->NS != c->rank) continue;
+        const int ph = row[gp / c->NS];
+        for (int g = 0; g < c->G; ++g) {
+            const float *src = c->kv + (size_t)layer * c->layer_floats + (((size_t)ph * c->G + g) * c->P + (pos - gp * c->P)) * D;
+            CK(cudaMemcpyAsync(k_out + ((size_t)z * c->G + g) * D, src, D * sizeof(float), cudaMemcpyDeviceToHost, c->stream));
+            CK(cudaMemcpyAsync(v_out + ((size_t)z * c->G + g) * D, src + c->v_off, D * sizeof(float),
+                               cudaMemcpyDeviceToHost, c->stream));
+        }
+    }
+    CK(cudaStreamSynchronize(c->stream));
+    return KORE_CUDA_OK;
+}
+
+int kore_cuda_sync(kore_cuda_ctx *c) {
+    if (!c) return KORE_CUDA_EINVAL;
+    DeviceGuard dg(c->cfg.device);
+    return finish(c);
+}
+
+void *kore_cuda_stream(kore_cuda_ctx *c) { return c ? (void *)c->stream : nullptr; }
+
+int kore_cuda_set_stream(kore_cuda_ctx *c, void *stream) {
+    if (!c) return KORE_CUDA_EINVAL;
+    DeviceGuard dg(c->cfg.device);
+    CK(cudaStreamSynchronize(c->stream));
+    if (c->own_stream) cudaStreamDestroy(c->stream);
+    c->stream = (cudaStream_t)stream;
+    c->own_stream = false;
+    return KORE_CUDA_OK;
+}
+
+}  // extern "C"

@@ -1,0 +1,122 @@
+// common.cuh — device helpers shared by the attention kernels (sm_100a).
+#pragma once
+
+#include <cstdint>
+#include <cuda_runtime.h>
+
+namespace kore {
+
+// Error codes a kernel can leave in the context's device error word. The
+// first failure wins (atomicCAS from 0); the host reads and clears it.
+enum DeviceError : int {
+    DEV_OK = 0,
+    DEV_WAIT_FULL_TIMEOUT = 1,    // consumer waited too long for a tile copy
+    DEV_WAIT_EMPTY_TIMEOUT = 2,   // producer waited too long for a free stage
+    DEV_BAD_PAGE = 3,             // page table entry outside the pool
+};
+
+__device__ __forceinline__ void raise_error(int *err, int code) {
+    if (err) atomicCAS(err, 0, code);
+}
+
+__device__ __forceinline__ uint32_t smem_u32(const void *p) {
+    return static_cast<uint32_t>(__cvta_generic_to_shared(p));
+}
+
+// ---------------------------------------------------------------- mbarrier
+
+__device__ __forceinline__ void mbar_init(uint64_t *bar, uint32_t count) {
+    asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(smem_u32(bar)), "r"(count) : "memory");
+}
+
+// Makes initialised barriers visible to the async (bulk copy) proxy.
+__device__ __forceinline__ void mbar_fence_init() {
+    asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+}
+
+__device__ __forceinline__ void mbar_arrive_expect_tx(uint64_t *bar, uint32_t bytes) {
+    asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(smem_u32(bar)), "r"(bytes)
+                 : "memory");
+}
+
+__device__ __forceinline__ void mbar_arrive(uint64_t *bar) {
+    asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(smem_u32(bar)) : "memory");
+}
+
+__device__ __forceinline__ bool mbar_try_wait(uint64_t *bar, uint32_t parity) {
+    uint32_t ok;
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t"
+        "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
+        "selp.u32 %0, 1, 0, p;\n\t}"
+        : "=r"(ok)
+        : "r"(smem_u32(bar)), "r"(parity)
+        : "memory");
+    return ok != 0;
+}
+
+__device__ __forceinline__ uint64_t global_ns() {
+    uint64_t t;
+    asm volatile("mov.u64 %0, %globaltimer;" : "=l"(t));
+    return t;
+}
+
+// Bounded wait on a phase of an mbarrier: gives up after kWaitNs of wall time
+// (checked every 64 polls) or kWaitPolls polls, whichever comes first, records
+// `code` in the error word and returns false. A healthy pipeline waits
+// microseconds; the bound only turns a lost copy into an error the host sees.
+constexpr uint64_t kWaitNs = 2000000000ull;   // 2 s
+constexpr uint32_t kWaitPolls = 1u << 26;
+
+__device__ __forceinline__ bool mbar_wait(uint64_t *bar, uint32_t parity, int *err, int code) {
+    if (mbar_try_wait(bar, parity)) return true;
+    const uint64_t t0 = global_ns();
+    for (uint32_t it = 1; it < kWaitPolls; ++it) {
+        if (mbar_try_wait(bar, parity)) return true;
+        if ((it & 63) == 0 && global_ns() - t0 > kWaitNs) break;
+    }
+    raise_error(err, code);
+    return false;
+}
+
+// ---------------------------------------------------------------- bulk copy
+
+// Creates an L2 policy that marks lines as first to evict: streamed K/V are
+// read exactly once per launch.
+__device__ __forceinline__ uint64_t l2_evict_first_policy() {
+    uint64_t pol;
+    asm volatile("createpolicy.fractional.L2::evict_first.b64 %0, 1.0;" : "=l"(pol));
+    return pol;
+}
+
+// One-dimensional bulk copy global -> this CTA's shared memory, completing on
+// `bar` with a transaction count of `bytes`. Both addresses 16-byte aligned,
+// bytes a multiple of 16. This is the plain (non-multicast) form.
+__device__ __forceinline__ void bulk_g2s(void *dst, const void *src, uint32_t bytes, uint64_t *bar,
+                                         uint64_t policy) {
+    asm volatile(
+        "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes.L2::cache_hint "
+        "[%0], [%1], %2, [%3], %4;" ::"r"(smem_u32(dst)),
+        "l"(src), "r"(bytes), "r"(smem_u32(bar)), "l"(policy)
+        : "memory");
+}
+
+// ---------------------------------------------------------------- math
+
+__device__ __forceinline__ float fast_exp2(float x) {
+    float y;
+    asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
+    return y;
+}
+
+// NEOX rotation of one element, rounded exactly as kore's rope_neox
+// (kore.cpp:1379-1381): two products and their difference (or sum), each
+// rounded on its own, never fused.
+__device__ __forceinline__ float rope_lo(float x0, float x1, float c, float s) {
+    return __fsub_rn(__fmul_rn(x0, c), __fmul_rn(x1, s));
+}
+__device__ __forceinline__ float rope_hi(float x0, float x1, float c, float s) {
+    return __fadd_rn(__fmul_rn(x0, s), __fmul_rn(x1, c));
+}
+
+}  // namespace kore

@@ -11,6 +11,7 @@
 
 #include <math.h>
 #include <stddef.h>
+#include <stdlib.h>
 #include <string.h>
 
 void korc_inv_freq(float rope_base, int head_dim, float *inv_freq) {
@@ -112,9 +113,9 @@ int korc_attn_decode(int H, int G, int d, const float *inv_freq, int pos,
     /* kore.cpp:1411: the scale is applied after the dot product */
     const float inv_sqrt = 1.0f / sqrtf((float)d);
 
-    float qr[4096];
-    float kr[4096];
-    if ((size_t)H * d > sizeof(qr) / sizeof(qr[0]) || (size_t)kvd > sizeof(kr) / sizeof(kr[0])) return -1;
+    float *qr = (float *)malloc(((size_t)H * d + kvd) * sizeof(float));
+    if (!qr) return -1;
+    float *kr = qr + (size_t)H * d;
     memcpy(qr, q, (size_t)H * d * sizeof(float));
     memcpy(kr, k, (size_t)kvd * sizeof(float));
     korc_rope_neox(qr, H, d, c, s);                              /* kore.cpp:1424 */
@@ -145,6 +146,7 @@ int korc_attn_decode(int H, int G, int d, const float *inv_freq, int pos,
             for (int i = 0; i < d; i++) oh[i] += p * vt[i];
         }
     }
+    free(qr);
     return 0;
 }
 

@@ -1,0 +1,198 @@
+"""GPU parity of the CUDA attention path against the oracle, through the C ABI.
+
+Every case drives kore_b200's C entry points (host buffers, as kore calls
+them; device tensors for the *_dev forms) and compares with the C
+restatement of kore's attention (oracle/), which is pinned bit-exact to the
+reference by tests/test_oracle_pin.py. Tolerance (north star): per head and
+token, max-abs error <= 2e-3 and max-abs error / max |reference| <= 1e-3.
+Rotated key rows and value rows in the cache must be bit-identical to kore's.
+"""
+import numpy as np
+import pytest
+
+import kore_b200 as K
+from oracle import oracle as O
+from tests.attn_check import assert_attn_close, attn_errors, normal
+
+pytestmark = pytest.mark.gpu
+
+
+def make_ctx(H, G, d, ctx, n_layer=1, **kw):
+    return K.KoreCuda(n_layer, H, G, d, ctx, **kw)
+
+
+def fill_both(gpu, ora, seq, layer, n, seed, chunk=4096):
+    """Appends n seeded rows at positions 0..n-1 to the GPU cache and the oracle."""
+    kvd = gpu.kvd
+    k, v = normal(seed, (n, kvd), (n, kvd))
+    for p0 in range(0, n, chunk):
+        gpu.append(seq, layer, p0, k[p0:p0 + chunk], v[p0:p0 + chunk])
+    ora.fill(0, k, v)
+    return k, v
+
+
+# ------------------------------------------------------------------ KV append
+
+@pytest.mark.parametrize("H,G,d", [(14, 2, 64), (28, 4, 128), (16, 2, 128)])
+def test_kv_append_rows_bitexact(H, G, d):
+    n = 700   # crosses pages at 256 and 512
+    g = make_ctx(H, G, d, 1024)
+    o = O.OracleLayer(H, G, d, 1024)
+    fill_both(g, o, 0, 0, n, 11, chunk=300)
+    kr, vr = g.kv_read(0, 0, 0, n)
+    np.testing.assert_array_equal(kr, o.kc[:n])
+    np.testing.assert_array_equal(vr, o.vc[:n])
+
+
+# ------------------------------------------------------------------ decode
+
+@pytest.mark.parametrize("pos", [0, 1, 7, 8, 9, 63, 64, 255, 256, 257, 511, 1000, 2047])
+def test_decode_positions_and_page_edges_3b(pos):
+    H, G, d = 16, 2, 128
+    g = make_ctx(H, G, d, 2048 + 8)
+    o = O.OracleLayer(H, G, d, 2048 + 8)
+    if pos:
+        fill_both(g, o, 0, 0, pos, 100 + pos)
+    q, k, v = normal(pos, (H * d,), (G * d,), (G * d,))
+    out = g.decode(0, 0, pos, q, k, v)
+    ref = o.decode(pos, q, k, v)
+    assert_attn_close(out, ref, f"decode pos {pos}")
+    kr, vr = g.kv_read(0, 0, pos, 1)
+    np.testing.assert_array_equal(kr[0], o.kc[pos])
+    np.testing.assert_array_equal(vr[0], o.vc[pos])
+
+
+def test_cfg1_0p5b_prefill128_then_64_decode_steps():
+    """Config 1: Qwen2.5-0.5B-shaped layer (14Q/2KV, d 64), prefill 128 tokens
+    at positions 0..127, then 64 decode steps at 128..191."""
+    H, G, d = 14, 2, 64
+    g = make_ctx(H, G, d, 192)
+    o = O.OracleLayer(H, G, d, 192)
+    q, k, v = normal(12345, (128, H * d), (128, G * d), (128, G * d))
+    out = g.prefill(0, 0, 0, q, k, v)
+    ref = o.prefill(0, q, k, v)
+    assert_attn_close(out, ref, "cfg1 prefill")
+    for step in range(64):
+        pos = 128 + step
+        q1, k1, v1 = normal(777 + step, (H * d,), (G * d,), (G * d,))
+        assert_attn_close(g.decode(0, 0, pos, q1, k1, v1), o.decode(pos, q1, k1, v1), f"cfg1 decode {pos}")
+    kr, vr = g.kv_read(0, 0, 0, 192)
+    np.testing.assert_array_equal(kr, o.kc)
+    np.testing.assert_array_equal(vr, o.vc)
+
+
+@pytest.mark.parametrize("layer", [0, 27])
+def test_cfg2_7b_decode_at_8192(layer):
+    """Config 2 shape: 28Q/4KV, d 128, 28 layers, decode at position 8192."""
+    H, G, d = 28, 4, 128
+    g = make_ctx(H, G, d, 8193, n_layer=28)
+    o = O.OracleLayer(H, G, d, 8193)
+    fill_both(g, o, 0, layer, 8192, 2000 + layer)
+    q, k, v = normal(3000 + layer, (H * d,), (G * d,), (G * d,))
+    assert_attn_close(g.decode(0, layer, 8192, q, k, v), o.decode(8192, q, k, v), "cfg2 decode")
+
+
+def test_cfg4_7b_decode_at_32768():
+    """Config 4 shape on one GPU: decode at position 32768 (one layer)."""
+    H, G, d = 28, 4, 128
+    g = make_ctx(H, G, d, 32769)
+    o = O.OracleLayer(H, G, d, 32769)
+    fill_both(g, o, 0, 0, 32768, 44)
+    q, k, v = normal(45, (H * d,), (G * d,), (G * d,))
+    assert_attn_close(g.decode(0, 0, 32768, q, k, v), o.decode(32768, q, k, v), "cfg4 decode")
+
+
+def test_decode_dev_matches_host_path():
+    import torch
+    H, G, d = 28, 4, 128
+    g = make_ctx(H, G, d, 4096, n_layer=2)
+    o = O.OracleLayer(H, G, d, 4096)
+    fill_both(g, o, 0, 1, 3000, 5)
+    q, k, v = normal(6, (H * d,), (G * d,), (G * d,))
+    dev = torch.device("cuda", 0)
+    tq, tk, tv = (torch.from_numpy(x).to(dev) for x in (q, k, v))
+    tout = torch.empty(H * d, device=dev)
+    g.decode_dev(0, 1, 3000, tq, tk, tv, tout)
+    g.sync()
+    assert_attn_close(tout.cpu().numpy().reshape(H, d), o.decode(3000, q, k, v), "decode_dev")
+
+
+def test_decode_batch_ragged_3b():
+    """Config 5 shape (16Q/2KV, d 128), 12 sequences with ragged lengths over a
+    shared 256-token page pool, one batched decode call."""
+    H, G, d = 16, 2, 128
+    rng = np.random.default_rng(55)
+    lens = [int(x) for x in rng.integers(1, 3000, size=12)] + [0, 255, 256]
+    n = len(lens)
+    g = make_ctx(H, G, d, 3072, max_seqs=n)
+    oras = []
+    for s, L in enumerate(lens):
+        o = O.OracleLayer(H, G, d, 3072)
+        if L:
+            fill_both(g, o, s, 0, L, 900 + s)
+        oras.append(o)
+    q, k, v = normal(56, (n, H * d), (n, G * d), (n, G * d))
+    seqs = np.arange(n, dtype=np.int32)
+    out = g.decode_batch(0, seqs, np.array(lens, np.int32), q, k, v)
+    for s, L in enumerate(lens):
+        assert_attn_close(out[s], oras[s].decode(L, q[s], k[s], v[s]), f"batch seq {s} len {L}")
+
+
+def test_page_reuse_after_seq_reset():
+    H, G, d = 28, 4, 128
+    g = make_ctx(H, G, d, 1024, max_seqs=2, n_pages=4)
+    o = O.OracleLayer(H, G, d, 1024)
+    fill_both(g, o, 0, 0, 1000, 1)
+    with pytest.raises(K.KoreCudaError) as e:   # pool of 4 pages is full
+        g.append(1, 0, 0, *normal(2, (10, G * d), (10, G * d)))
+    assert e.value.code == -3
+    g.seq_reset(0)
+    o2 = O.OracleLayer(H, G, d, 1024)
+    fill_both(g, o2, 1, 0, 600, 3)
+    q, k, v = normal(4, (H * d,), (G * d,), (G * d,))
+    assert_attn_close(g.decode(1, 0, 600, q, k, v), o2.decode(600, q, k, v), "after reset")
+
+
+# ------------------------------------------------------------------ prefill
+
+def test_prefill_kore_chunk_onto_4096_7b():
+    """A kore-sized 64-token prefill chunk (KORE_BMAX) onto 4096 cached rows."""
+    H, G, d = 28, 4, 128
+    g = make_ctx(H, G, d, 4160)
+    o = O.OracleLayer(H, G, d, 4160)
+    fill_both(g, o, 0, 0, 4096, 31)
+    q, k, v = normal(32, (64, H * d), (64, G * d), (64, G * d))
+    assert_attn_close(g.prefill(0, 0, 4096, q, k, v), o.prefill(4096, q, k, v), "prefill 64 onto 4096")
+
+
+@pytest.mark.parametrize("pos0,n", [(0, 1), (0, 300), (5, 1), (250, 13), (1000, 257)])
+def test_prefill_shapes(pos0, n):
+    H, G, d = 14, 2, 64
+    g = make_ctx(H, G, d, 2048)
+    o = O.OracleLayer(H, G, d, 2048)
+    if pos0:
+        fill_both(g, o, 0, 0, pos0, 70 + pos0)
+    q, k, v = normal(pos0 * 7 + n, (n, H * d), (n, G * d), (n, G * d))
+    assert_attn_close(g.prefill(0, 0, pos0, q, k, v), o.prefill(pos0, q, k, v), f"prefill {pos0}+{n}")
+
+
+# ------------------------------------------------------------------ errors (kore.cpp:1400, :1490)
+
+def test_errors_are_codes_not_crashes():
+    H, G, d = 28, 4, 128
+    g = make_ctx(H, G, d, 64, n_layer=2)
+    q, k, v = normal(1, (H * d,), (G * d,), (G * d,))
+    with pytest.raises(K.KoreCudaError) as e:
+        g.decode(0, 0, 64, q, k, v)             # pos >= ctx
+    assert e.value.code == -2
+    with pytest.raises(K.KoreCudaError) as e:
+        g.decode(0, 0, 5, q, k, v)              # rows 0..4 never written
+    assert e.value.code == -5
+    with pytest.raises(K.KoreCudaError) as e:
+        g.decode(0, 2, 0, q, k, v)              # layer out of range
+    assert e.value.code == -2
+    with pytest.raises(K.KoreCudaError) as e:
+        g.decode(1, 0, 0, q, k, v)              # seq out of range
+    assert e.value.code == -2
+    out = g.decode(0, 0, 0, q, k, v)            # the context is still usable
+    assert np.isfinite(out).all()
