@@ -37,8 +37,9 @@ import numpy as np
 ROOT = os.path.dirname(os.path.abspath(__file__))
 sys.path.insert(0, ROOT)
 
-H, G, D, L = 28, 4, 128, 28
-POS = 32768
+H, G, D = 28, 4, 128
+L = 28          # layers (--layers overrides, for small profiling cases)
+POS = 32768     # decode position (--pos overrides)
 CTX = POS + 1
 KVD = G * D
 
@@ -55,7 +56,12 @@ def parse():
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--e2e-steps", type=int, default=100)
-    return ap.parse_args()
+    ap.add_argument("--layers", type=int, default=28, help="fewer layers: a small case for ncu captures")
+    ap.add_argument("--pos", type=int, default=32768, help="decode position (cached rows per layer)")
+    a = ap.parse_args()
+    global L, POS, CTX
+    L, POS, CTX = a.layers, a.pos, a.pos + 1
+    return a
 
 
 # ---------------------------------------------------------------- clocks
@@ -250,7 +256,7 @@ def run_ours(args, rank: int, world: int, dist) -> dict | None:
         "ms_per_step": round(ms_step, 5), "higher_is_better": True,
         "scaling": "strong" if world > 1 else "weak",
         "vs_baseline": None, "dtype": "f32", "data": "synthetic (seeded N(0,1) q/k/v and KV cache)",
-        "config": {"workload": "cfg4: Qwen2.5-7B-shaped decode at position 32768, 28 layers, batch 1",
+        "config": {"workload": f"cfg4: Qwen2.5-7B-shaped decode at position {POS}, {L} layers, batch 1",
                    "kv_bytes_per_step": step_bytes, "l2": "inputs 3.5 GiB > L2, no flush needed",
                    "kv_split": f"pages round-robin over {world} GPU(s)" if world > 1 else "none"},
         "e2e": {"value": round(e2e_gbs, 1), "unit": "GB/s", "ms_per_step": round(e2e_ms, 4),

@@ -31,12 +31,13 @@ struct DecodeParams {
     const float2 *rope;        // [ctx_max][D/2] (cos, sin) as kore.cpp:1405-1410
     float *part_o;             // split scratch [n_q][G][max_splits][R][D]
     float2 *part_ml;           // split scratch [n_q][G][max_splits][R] (max, sum)
-    unsigned *counters;        // [n_q][G] arrival counters, self-resetting
     int *err;                  // device error word
     float scale_log2;          // (1/sqrt(D)) * log2(e)
     int H, n_q, split_tokens, max_splits;
     int append_new;            // 1: the token at pos comes from k_new/v_new and is appended
     int contiguous;            // 1: query i is (seq0, pos0 + i); 0: seq[i], pos[i]
+    int prefetch_ok;           // 1: the preceding kernel in the stream wrote no KV of this layer,
+                               //    so KV tiles may be fetched before waiting for it
     int seq0, pos0;
     int seq[kMaxBatch];
     int pos[kMaxBatch];
@@ -52,9 +53,11 @@ struct AppendParams {
 };
 
 // Launch helpers (attn_decode.cu, kv_append.cu). Return cudaGetLastError().
+// Decode kernel, followed (when grid_x > 1) by the split-merge kernel.
 cudaError_t launch_attn_decode(const DecodeParams &p, int n_rep, int grid_x, cudaStream_t s);
 int decode_ctas_per_sm(int head_dim, int n_rep);
 int decode_tile_tokens();
+int decode_split_pages_max();
 size_t decode_smem_bytes(int head_dim);
 cudaError_t launch_kv_append(const AppendParams &p, cudaStream_t s);
 cudaError_t launch_lse_merge(const float *parts, int n_parts, int H, int D, float *out, cudaStream_t s);

@@ -4,88 +4,103 @@
 // new k at `pos`, append of k/v at `pos`, then softmax(q k^T / sqrt(d)) v over
 // positions 0..pos for every query head. kore reads each KV head once per
 // query head of its group (n_rep times); here one CTA serves the whole group,
-// so every K/V byte crosses HBM once.
+// so every K/V byte crosses HBM once. The kernel is HBM-bound: per cached
+// position it reads 2*d*4 bytes and does 2*R*d FMAs (R = n_rep).
 //
 // Work decomposition
 //   grid = (splits, n_head_kv, queries). A CTA owns one KV head of one query
-//   and a contiguous range of `split_tokens` cached positions. Warp NW is the
-//   producer: one lane streams TT-token K and V tiles into an S-stage ring of
-//   shared memory with 1-D bulk copies (cp.async.bulk, mbarrier completion,
-//   L2 evict-first). Warps 0..NW-1 consume: tile i goes to stage i % S and to
-//   warp i % NW, and each warp keeps its own online-softmax state (running max
-//   m, running sum l, output o) for the R = n_rep heads of the group.
+//   and a contiguous range of `split_tokens` cached positions, cut into
+//   TT-token tiles; tile i goes to warp i % NW. Every warp streams its own
+//   tiles into a private ring of SPW shared-memory stages with 1-D bulk copies
+//   (cp.async.bulk, mbarrier completion, L2 evict-first), refilling a stage as
+//   soon as it has consumed it, so no warp ever waits for another.
 //
-// Lane layout inside a consumer warp (D = 128: VEC = 4 dims per lane)
+// Lane layout inside a warp (D = 128: VEC = 4 dims per lane)
 //   lane owns dims [VEC*lane, VEC*lane+VEC) of q (R heads, pre-scaled by
-//   log2(e)/sqrt(d)) and of o. A K row is read with one 16-byte LDS per lane.
-//   Scores of 8 tokens x R heads are reduced across the warp by a butterfly
-//   reduce-scatter (xor 16, 8, 4 split tokens; xor 2, 1 split head pairs):
-//   55 shuffles per 8 tokens for R = 7 instead of 35 per token, after which
-//   lane L holds the full scores of token L>>2 for heads 2(L&3), 2(L&3)+1.
-//   Probabilities go through a tiny per-warp shared buffer so that every lane
-//   can accumulate p * v for all R heads over its VEC dims.
+//   log2(e)/sqrt(d)) and of the output accumulator o. A K row is one 16-byte
+//   shared load per lane. The scores of 4 tokens x R heads are reduced across
+//   the warp by a butterfly reduce-scatter (xor 16, 8 split tokens; xor 4, 2,
+//   1 split heads): 28 shuffles per 4 tokens for R = 7, after which lane L
+//   holds the full score of token L>>3 for head L&7. Probabilities go through
+//   a small per-warp buffer so that every lane accumulates p*v for all R
+//   heads over its VEC dims.
 //
-// Merge: the warps of a CTA merge in shared memory; with more than one split
-// each CTA writes (m, l, o) to scratch and the last CTA to arrive for its
-// (query, KV head) — ordered by an atomic counter — merges the splits and
-// writes the normalised output, then resets the counter. In a KV-sharded
-// context (positions split over GPUs) the output is the normalised partial
-// plus its log2-domain LSE, merged across GPUs afterwards.
+// Softmax: online, with a lazily moved reference maximum. Probabilities are
+// exp2(s - m_ref); m_ref and the accumulators are rescaled only when a score
+// exceeds m_ref by more than 8 (log2 domain; checked with one warp vote per
+// tile), so the common tile needs no maximum reduction at all. The final
+// division by the running sum cancels m_ref exactly, as in any online softmax.
+//
+// Merge: warps merge in shared memory; with one split the CTA writes the
+// normalised output, otherwise it writes (max, sum, o) to scratch and exits,
+// and split_merge_kernel — launched next with a programmatic dependency, one
+// CTA per query head with every partial load in flight at once — combines the
+// splits. (A last-arriving-CTA merge, ordered by an atomic, measured ~8 us of
+// serial tail per launch on B200: the release atomic drains the CTA's stores
+// and one SM then pulls every partial of its head.) In a KV-sharded context
+// (positions split over GPUs) the output is the normalised partial plus its
+// log2-domain log-sum-exp.
 
 #include "attn.cuh"
 #include "common.cuh"
-
-#include <cfloat>
 
 namespace kore {
 namespace {
 
 constexpr unsigned FULL = 0xffffffffu;
+constexpr float kRescaleLog2 = 8.0f;   // accumulators may grow by up to 2^8 before a rescale
+constexpr int kSplitPagesMax = 128;    // page ids of one split kept in shared memory
 
-template <int D, int NW, int TT, int S>
+template <int D, int NW, int TT, int SPW>
 struct DecodeSmem {
     static constexpr int TILE_F = TT * D;
-    static constexpr size_t stage_floats = (size_t)S * 2 * TILE_F;
-    static constexpr size_t new_floats = 2 * 8 * D;
+    static constexpr size_t stage_floats = (size_t)NW * SPW * 2 * TILE_F;
+    static constexpr size_t new_floats = 2 * 4 * D;
     static constexpr size_t pbuf_floats = (size_t)NW * TT * 8;
-    static constexpr size_t bytes = (stage_floats + new_floats + pbuf_floats) * 4 + 2 * S * 8;
+    static constexpr size_t bar_off = (stage_floats + new_floats + pbuf_floats) * 4;
+    static constexpr size_t bytes = bar_off + (size_t)NW * SPW * 8 + kSplitPagesMax * 4;
 };
 
-template <int D, int R, int TT>
+template <int D, int R>
 struct WarpState {
     static constexpr int VEC = D / 32;
     float q[R][VEC];
     float o[R][VEC];
-    float m[R];
-    float mA, mB;   // running max of the two heads whose scores this lane owns
-    float lA, lB;   // lane-partial running sums of those heads
+    float m[R];     // reference maximum of every head (same in all lanes)
+    float mo;       // reference maximum of this lane's head (lane & 7)
+    float l;        // lane-partial running sum of this lane's head
 };
 
-// Processes one tile of `nv` (1..TT) tokens whose K rows start at Ks and V rows
-// at Vs (shared memory, row stride D) for one consumer warp.
+template <int VEC>
+__device__ __forceinline__ void load_row(const float *p, float (&x)[VEC]) {
+    if constexpr (VEC == 4) {
+        const float4 v = *reinterpret_cast<const float4 *>(p);
+        x[0] = v.x; x[1] = v.y; x[2] = v.z; x[3] = v.w;
+    } else {
+        const float2 v = *reinterpret_cast<const float2 *>(p);
+        x[0] = v.x; x[1] = v.y;
+    }
+}
+
+// One tile of nv (1..TT) tokens for one warp: K rows at Ks, V rows at Vs
+// (shared memory, row stride D). Rows at and past nv are never accumulated.
 template <int D, int R, int TT>
-__device__ __forceinline__ void process_tile(WarpState<D, R, TT> &st, const float *__restrict__ Ks,
+__device__ __forceinline__ void process_tile(WarpState<D, R> &st, const float *__restrict__ Ks,
                                              const float *__restrict__ Vs, int nv, float *__restrict__ pbuf,
                                              int lane) {
     constexpr int VEC = D / 32;
-    constexpr int ROUNDS = TT / 8;
+    constexpr int ROUNDS = TT / 4;
     const bool b4 = lane & 16, b3 = lane & 8, b2 = lane & 4, b1 = lane & 2, b0 = lane & 1;
+    const int tl = lane >> 3;   // token (within a round) whose score this lane ends up with
 
-    float sc[ROUNDS][2];
+    float sc[ROUNDS];
 #pragma unroll
     for (int r = 0; r < ROUNDS; ++r) {
-        float part[8][R];
+        float part[4][R];
 #pragma unroll
-        for (int t = 0; t < 8; ++t) {
+        for (int t = 0; t < 4; ++t) {
             float kv[VEC];
-            const float *kr = Ks + (r * 8 + t) * D + lane * VEC;
-            if constexpr (VEC == 4) {
-                const float4 x = *reinterpret_cast<const float4 *>(kr);
-                kv[0] = x.x; kv[1] = x.y; kv[2] = x.z; kv[3] = x.w;
-            } else {
-                const float2 x = *reinterpret_cast<const float2 *>(kr);
-                kv[0] = x.x; kv[1] = x.y;
-            }
+            load_row<VEC>(Ks + (r * 4 + t) * D + lane * VEC, kv);
 #pragma unroll
             for (int h = 0; h < R; ++h) {
                 float a = st.q[h][0] * kv[0];
@@ -94,95 +109,72 @@ __device__ __forceinline__ void process_tile(WarpState<D, R, TT> &st, const floa
                 part[t][h] = a;
             }
         }
-        // reduce-scatter over tokens: xor 16 keeps tokens {4..7} or {0..3}
-        float a1[4][R];
-#pragma unroll
-        for (int j = 0; j < 4; ++j)
-#pragma unroll
-            for (int h = 0; h < R; ++h) {
-                const float mine = b4 ? part[4 + j][h] : part[j][h];
-                const float other = b4 ? part[j][h] : part[4 + j][h];
-                a1[j][h] = mine + __shfl_xor_sync(FULL, other, 16);
-            }
-        float a2[2][R];
+        float a1[2][R];   // xor 16: keep tokens {2,3} (bit set) or {0,1}
 #pragma unroll
         for (int j = 0; j < 2; ++j)
 #pragma unroll
             for (int h = 0; h < R; ++h) {
-                const float mine = b3 ? a1[2 + j][h] : a1[j][h];
-                const float other = b3 ? a1[j][h] : a1[2 + j][h];
-                a2[j][h] = mine + __shfl_xor_sync(FULL, other, 8);
+                const float mine = b4 ? part[2 + j][h] : part[j][h];
+                const float other = b4 ? part[j][h] : part[2 + j][h];
+                a1[j][h] = mine + __shfl_xor_sync(FULL, other, 16);
             }
-        float a3[8];
+        float a2[8];      // xor 8: keep token {1} or {0}
 #pragma unroll
         for (int h = 0; h < R; ++h) {
-            const float mine = b2 ? a2[1][h] : a2[0][h];
-            const float other = b2 ? a2[0][h] : a2[1][h];
-            a3[h] = mine + __shfl_xor_sync(FULL, other, 4);
+            const float mine = b3 ? a1[1][h] : a1[0][h];
+            const float other = b3 ? a1[0][h] : a1[1][h];
+            a2[h] = mine + __shfl_xor_sync(FULL, other, 8);
         }
 #pragma unroll
-        for (int h = R; h < 8; ++h) a3[h] = 0.f;
-        // reduce-scatter over heads: xor 2 keeps heads {4..7} or {0..3}, xor 1 a pair
-        float a4[4];
+        for (int h = R; h < 8; ++h) a2[h] = 0.f;
+        float a3[4];      // xor 4: keep heads {4..7} or {0..3}
 #pragma unroll
         for (int j = 0; j < 4; ++j) {
-            const float mine = b1 ? a3[4 + j] : a3[j];
-            const float other = b1 ? a3[j] : a3[4 + j];
-            a4[j] = (4 + j < R || j < R) ? mine + __shfl_xor_sync(FULL, other, 2) : 0.f;
+            const float mine = b2 ? a2[4 + j] : a2[j];
+            const float other = b2 ? a2[j] : a2[4 + j];
+            a3[j] = j < R ? mine + __shfl_xor_sync(FULL, other, 4) : 0.f;
         }
+        float a4[2];      // xor 2: keep heads {2,3} or {0,1} of those
 #pragma unroll
         for (int j = 0; j < 2; ++j) {
-            const float mine = b0 ? a4[2 + j] : a4[j];
-            const float other = b0 ? a4[j] : a4[2 + j];
-            sc[r][j] = mine + __shfl_xor_sync(FULL, other, 1);
+            const float mine = b1 ? a3[2 + j] : a3[j];
+            const float other = b1 ? a3[j] : a3[2 + j];
+            a4[j] = j < R ? mine + __shfl_xor_sync(FULL, other, 2) : 0.f;
         }
-        if (r * 8 + (lane >> 2) >= nv) { sc[r][0] = -INFINITY; sc[r][1] = -INFINITY; }
+        const float mine = b0 ? a4[1] : a4[0];
+        const float other = b0 ? a4[0] : a4[1];
+        const float s = mine + __shfl_xor_sync(FULL, other, 1);
+        sc[r] = r * 4 + tl < nv ? s : -INFINITY;
     }
 
-    // tile max of the lane's two heads, then of every head in every lane
-    float tA = sc[0][0], tB = sc[0][1];
+    // lazy rescale: only when some score exceeds its head's reference by 2^8
+    bool need = false;
 #pragma unroll
-    for (int r = 1; r < ROUNDS; ++r) { tA = fmaxf(tA, sc[r][0]); tB = fmaxf(tB, sc[r][1]); }
+    for (int r = 0; r < ROUNDS; ++r) need |= sc[r] > st.mo + kRescaleLog2;
+    if (__any_sync(FULL, need)) {
+        float tm = sc[0];
 #pragma unroll
-    for (int off = 4; off < 32; off <<= 1) {
-        tA = fmaxf(tA, __shfl_xor_sync(FULL, tA, off));
-        tB = fmaxf(tB, __shfl_xor_sync(FULL, tB, off));
-    }
-    float alpha[R];
+        for (int r = 1; r < ROUNDS; ++r) tm = fmaxf(tm, sc[r]);
+        tm = fmaxf(tm, __shfl_xor_sync(FULL, tm, 8));
+        tm = fmaxf(tm, __shfl_xor_sync(FULL, tm, 16));
+        const float mnew = fmaxf(st.mo, tm);
+        st.l *= fast_exp2(st.mo - mnew);
+        st.mo = mnew;
 #pragma unroll
-    for (int k = 0; k < 4; ++k) {
-        const float xa = __shfl_sync(FULL, tA, k);
-        const float xb = __shfl_sync(FULL, tB, k);
-        if (2 * k < R) {
-            const float mn = fmaxf(st.m[2 * k], xa);
-            alpha[2 * k] = fast_exp2(st.m[2 * k] - mn);
-            st.m[2 * k] = mn;
+        for (int h = 0; h < R; ++h) {
+            const float mh = __shfl_sync(FULL, mnew, h);
+            const float alpha = fast_exp2(st.m[h] - mh);
+            st.m[h] = mh;
+#pragma unroll
+            for (int j = 0; j < VEC; ++j) st.o[h][j] *= alpha;
         }
-        if (2 * k + 1 < R) {
-            const float mn = fmaxf(st.m[2 * k + 1], xb);
-            alpha[2 * k + 1] = fast_exp2(st.m[2 * k + 1] - mn);
-            st.m[2 * k + 1] = mn;
-        }
-    }
-    {
-        const float nA = fmaxf(st.mA, tA), nB = fmaxf(st.mB, tB);
-        st.lA *= fast_exp2(st.mA - nA);
-        st.lB *= fast_exp2(st.mB - nB);
-        st.mA = nA;
-        st.mB = nB;
     }
 #pragma unroll
     for (int r = 0; r < ROUNDS; ++r) {
-        const float pa = fast_exp2(sc[r][0] - st.mA);
-        const float pb = fast_exp2(sc[r][1] - st.mB);
-        st.lA += pa;
-        st.lB += pb;
-        *reinterpret_cast<float2 *>(pbuf + (r * 8 + (lane >> 2)) * 8 + 2 * (lane & 3)) = make_float2(pa, pb);
+        const float p = fast_exp2(sc[r] - st.mo);
+        st.l += p;
+        pbuf[(r * 4 + tl) * 8 + (lane & 7)] = p;
     }
-#pragma unroll
-    for (int h = 0; h < R; ++h)
-#pragma unroll
-        for (int j = 0; j < VEC; ++j) st.o[h][j] *= alpha[h];
     __syncwarp();
 
     auto pv_row = [&](int t) {
@@ -190,14 +182,7 @@ __device__ __forceinline__ void process_tile(WarpState<D, R, TT> &st, const floa
         const float4 p1 = *reinterpret_cast<const float4 *>(pbuf + t * 8 + 4);
         const float pr[8] = {p0.x, p0.y, p0.z, p0.w, p1.x, p1.y, p1.z, p1.w};
         float vv[VEC];
-        const float *vr = Vs + t * D + lane * VEC;
-        if constexpr (VEC == 4) {
-            const float4 x = *reinterpret_cast<const float4 *>(vr);
-            vv[0] = x.x; vv[1] = x.y; vv[2] = x.z; vv[3] = x.w;
-        } else {
-            const float2 x = *reinterpret_cast<const float2 *>(vr);
-            vv[0] = x.x; vv[1] = x.y;
-        }
+        load_row<VEC>(Vs + t * D + lane * VEC, vv);
 #pragma unroll
         for (int h = 0; h < R; ++h)
 #pragma unroll
@@ -212,20 +197,19 @@ __device__ __forceinline__ void process_tile(WarpState<D, R, TT> &st, const floa
     __syncwarp();
 }
 
-template <int D, int R, int NW, int TT, int S>
-__global__ void __launch_bounds__((NW + 1) * 32, 1) attn_decode_kernel(const __grid_constant__ DecodeParams p) {
+template <int D, int R, int NW, int TT, int SPW>
+__global__ void __launch_bounds__(NW * 32, 1) attn_decode_kernel(const __grid_constant__ DecodeParams p) {
     constexpr int VEC = D / 32;
     constexpr int HALF = D / 2;
-    constexpr int NT = (NW + 1) * 32;
-    using SM = DecodeSmem<D, NW, TT, S>;
+    constexpr int NT = NW * 32;
+    using SM = DecodeSmem<D, NW, TT, SPW>;
     extern __shared__ __align__(128) float smem[];
     float *stages = smem;
     float *newk = stages + SM::stage_floats;
-    float *newv = newk + 8 * D;
-    float *pbuf_all = newv + 8 * D;
-    uint64_t *full = reinterpret_cast<uint64_t *>(pbuf_all + SM::pbuf_floats);
-    uint64_t *empty = full + S;
-    __shared__ int s_last;
+    float *newv = newk + 4 * D;
+    float *pbuf_all = newv + 4 * D;
+    uint64_t *full = reinterpret_cast<uint64_t *>(reinterpret_cast<char *>(smem) + SM::bar_off);
+    int *pages = reinterpret_cast<int *>(full + NW * SPW);
 
     const int split = blockIdx.x, g = blockIdx.y, qi = blockIdx.z;
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
@@ -248,134 +232,127 @@ __global__ void __launch_bounds__((NW + 1) * 32, 1) attn_decode_kernel(const __g
     const int u_end = min(count, u_begin + ST);
     const int n_tiles = u_end > u_begin ? (u_end - u_begin + TT - 1) / TT : 0;
     const bool do_new = own_new && split == n_splits - 1;
+    const int lp_first = u_begin / P;
+    const int n_pages_split = n_tiles > 0 ? (u_end - 1) / P - lp_first + 1 : 0;
     const int *pt = kv.page_table + (size_t)seq * kv.pt_stride;
 
-    if (tid == 0) {
-        for (int s = 0; s < S; ++s) {
-            mbar_init(&full[s], 1);
-            mbar_init(&empty[s], 1);
+    // page ids of this split (checked; the host keeps a split within
+    // kSplitPagesMax pages), barrier init
+    for (int j = tid; j < n_pages_split && j < kSplitPagesMax; j += NT) {
+        int ph = pt[lp_first + j];
+        if (ph < 0 || ph >= kv.n_pages) {
+            raise_error(p.err, DEV_BAD_PAGE);
+            ph = 0;
         }
-        mbar_fence_init();
+        pages[j] = ph;
     }
+    if (lane == 0)
+        for (int s = 0; s < SPW; ++s) mbar_init(&full[warp * SPW + s], 1);
+    if (tid == 0) mbar_fence_init();
     __syncthreads();
 
+    // this warp's tiles: i = warp, warp + NW, ...; its j-th tile uses stage j % SPW
+    const int my_tiles = n_tiles > warp ? (n_tiles - warp + NW - 1) / NW : 0;
     const float *kbase = kv.k + (size_t)g * P * D;
-    WarpState<D, R, TT> st;
-    if (warp == NW) {
-        // ------------------------------------------------------------ producer
-        if (lane == 0) {
-            // walks the page table as it goes: the raw id of the next page is
-            // loaded when a page is entered and checked only when it is used,
-            // one page (P/TT tiles) later, so the load latency stays hidden
-            auto checked = [&](int ph) {
-                if (ph < 0 || ph >= kv.n_pages) {
-                    raise_error(p.err, DEV_BAD_PAGE);
-                    ph = 0;
-                }
-                return ph;
-            };
-            const int last_lp = n_tiles > 0 ? (u_end - 1) / P : 0;
-            const uint64_t pol = l2_evict_first_policy();
-            int cur_lp = u_begin / P;
-            int cur_ph = n_tiles > 0 ? checked(pt[cur_lp]) : 0;
-            int next_raw = cur_lp < last_lp ? pt[cur_lp + 1] : 0;
-            for (int i = 0; i < n_tiles; ++i) {
-                const int s = i % S;
-                if (i >= S && !mbar_wait(&empty[s], ((i / S) - 1) & 1, p.err, DEV_WAIT_EMPTY_TIMEOUT)) break;
-                const int u0 = u_begin + i * TT;
-                const int nv = min(TT, u_end - u0);
-                const int lp = u0 / P;
-                if (lp != cur_lp) {
-                    cur_lp = lp;
-                    cur_ph = checked(next_raw);
-                    if (lp < last_lp) next_raw = pt[lp + 1];
-                }
-                const int off = u0 - lp * P;
-                const float *src = kbase + ((size_t)cur_ph * kv.G * P + off) * D;
-                const uint32_t bytes = (uint32_t)(nv * D * 4);
-                float *dst = stages + (size_t)s * 2 * SM::TILE_F;
-                mbar_arrive_expect_tx(&full[s], 2 * bytes);
-                bulk_g2s(dst, src, bytes, &full[s], pol);
-                bulk_g2s(dst + SM::TILE_F, src + kv.v_off, bytes, &full[s], pol);
+    float *my_stages = stages + (size_t)warp * SPW * 2 * SM::TILE_F;
+    uint64_t *my_full = full + warp * SPW;
+    const uint64_t pol = l2_evict_first_policy();
+    auto issue = [&](int j) {   // lane 0 only
+        const int i = warp + j * NW;
+        const int u0 = u_begin + i * TT;
+        const int nv = min(TT, u_end - u0);
+        const int lp = u0 / P;
+        const int off = u0 - lp * P;
+        const int pj = min(lp - lp_first, kSplitPagesMax - 1);
+        const float *src = kbase + ((size_t)pages[pj] * kv.G * P + off) * D;
+        const uint32_t bytes = (uint32_t)(nv * D * 4);
+        float *dst = my_stages + (size_t)(j % SPW) * 2 * SM::TILE_F;
+        uint64_t *bar = my_full + (j % SPW);
+        fence_proxy_async_smem();
+        mbar_arrive_expect_tx(bar, 2 * bytes);
+        bulk_g2s(dst, src, bytes, bar, pol);
+        bulk_g2s(dst + SM::TILE_F, src + kv.v_off, bytes, bar, pol);
+    };
+    // KV of this layer is streamed before waiting for the preceding kernel only
+    // when the host knows that kernel wrote no KV of this layer; every kernel
+    // earlier than that one has completed, because each decode kernel lets its
+    // successor start only after its own wait returned
+    if (p.prefetch_ok && lane == 0)
+        for (int j = 0; j < SPW && j < my_tiles; ++j) issue(j);
+    grid_dep_wait();
+    grid_dep_launch();
+    if (!p.prefetch_ok && lane == 0)
+        for (int j = 0; j < SPW && j < my_tiles; ++j) issue(j);
+
+    WarpState<D, R> st;
+    const float2 *cs = p.rope + (size_t)pos * HALF;
+    const float *qsrc = p.q + (size_t)qi * p.H * D + (size_t)g * R * D;
+#pragma unroll
+    for (int h = 0; h < R; ++h)
+#pragma unroll
+        for (int j = 0; j < VEC; ++j) {
+            const int i = lane * VEC + j;
+            const float x = __ldg(qsrc + h * D + i);
+            const float y = __ldg(qsrc + h * D + (i ^ HALF));
+            const float2 a = __ldg(cs + (i & (HALF - 1)));
+            const float r = i < HALF ? rope_lo(x, y, a.x, a.y) : rope_hi(y, x, a.x, a.y);
+            st.q[h][j] = r * p.scale_log2;
+            st.o[h][j] = 0.f;
+        }
+#pragma unroll
+    for (int h = 0; h < R; ++h) st.m[h] = -INFINITY;
+    st.mo = -INFINITY;
+    st.l = 0.f;
+    float *pbuf = pbuf_all + (size_t)warp * TT * 8;
+
+    if (do_new && warp == 0) {
+        // the token at pos: rotate k, stage k/v as a 1-token tile, append to the cache
+        const float *ks = p.k_new + (size_t)qi * kv.G * D + (size_t)g * D;
+        const float *vs = p.v_new + (size_t)qi * kv.G * D + (size_t)g * D;
+        const int lp = (pos / P) / NS, off = pos % P;
+        const int ph = pt[lp];
+        const bool ok = ph >= 0 && ph < kv.n_pages;
+        if (!ok && lane == 0) raise_error(p.err, DEV_BAD_PAGE);
+        float *kd = kv.k + (((size_t)(ok ? ph : 0) * kv.G + g) * P + off) * D;
+#pragma unroll
+        for (int j = 0; j < VEC; ++j) {
+            const int i = lane * VEC + j;
+            const float x = __ldg(ks + i), y = __ldg(ks + (i ^ HALF));
+            const float2 a = __ldg(cs + (i & (HALF - 1)));
+            const float kr = i < HALF ? rope_lo(x, y, a.x, a.y) : rope_hi(y, x, a.x, a.y);
+            const float vr = __ldg(vs + i);
+            newk[i] = kr;
+            newv[i] = vr;
+            if (ok) {
+                kd[i] = kr;
+                kd[i + kv.v_off] = vr;
             }
         }
-    } else {
-        // ------------------------------------------------------------ consumers
-        const float2 *cs = p.rope + (size_t)pos * HALF;
-        const float *qsrc = p.q + (size_t)qi * p.H * D + (size_t)g * R * D;
-#pragma unroll
-        for (int h = 0; h < R; ++h)
-#pragma unroll
-            for (int j = 0; j < VEC; ++j) {
-                const int i = lane * VEC + j;
-                const float x = __ldg(qsrc + h * D + i);
-                const float y = __ldg(qsrc + h * D + (i ^ HALF));
-                const float2 a = __ldg(cs + (i & (HALF - 1)));
-                const float r = i < HALF ? rope_lo(x, y, a.x, a.y) : rope_hi(y, x, a.x, a.y);
-                st.q[h][j] = r * p.scale_log2;
-                st.o[h][j] = 0.f;
-            }
-#pragma unroll
-        for (int h = 0; h < R; ++h) st.m[h] = -INFINITY;
-        st.mA = st.mB = -INFINITY;
-        st.lA = st.lB = 0.f;
-        float *pbuf = pbuf_all + (size_t)warp * TT * 8;
-
-        if (do_new && warp == 0) {
-            // the token at pos: rotate k, stage k/v as a 1-token tile, append to the cache
-            const float *ks = p.k_new + (size_t)qi * kv.G * D + (size_t)g * D;
-            const float *vs = p.v_new + (size_t)qi * kv.G * D + (size_t)g * D;
-            const int lp = (pos / P) / NS, off = pos % P;
-            const int ph = pt[lp];
-            const bool ok = ph >= 0 && ph < kv.n_pages;
-            if (!ok && lane == 0) raise_error(p.err, DEV_BAD_PAGE);
-            float *kd = kv.k + (((size_t)(ok ? ph : 0) * kv.G + g) * P + off) * D;
-#pragma unroll
-            for (int j = 0; j < VEC; ++j) {
-                const int i = lane * VEC + j;
-                const float x = __ldg(ks + i), y = __ldg(ks + (i ^ HALF));
-                const float2 a = __ldg(cs + (i & (HALF - 1)));
-                const float kr = i < HALF ? rope_lo(x, y, a.x, a.y) : rope_hi(y, x, a.x, a.y);
-                const float vr = __ldg(vs + i);
-                newk[i] = kr;
-                newv[i] = vr;
-                if (ok) {
-                    kd[i] = kr;
-                    kd[i + kv.v_off] = vr;
-                }
-            }
-            __syncwarp();
-            process_tile<D, R, TT>(st, newk, newv, 1, pbuf, lane);
-        }
-
-        for (int i = warp; i < n_tiles; i += NW) {
-            const int s = i % S;
-            if (!mbar_wait(&full[s], (i / S) & 1, p.err, DEV_WAIT_FULL_TIMEOUT)) break;
-            const int nv = min(TT, u_end - (u_begin + i * TT));
-            const float *tile = stages + (size_t)s * 2 * SM::TILE_F;
-            process_tile<D, R, TT>(st, tile, tile + SM::TILE_F, nv, pbuf, lane);
-            if (lane == 0) mbar_arrive(&empty[s]);
-        }
-
-        // lane-partial sums -> per head pair (lanes with equal lane & 3)
-#pragma unroll
-        for (int off = 4; off < 32; off <<= 1) {
-            st.lA += __shfl_xor_sync(FULL, st.lA, off);
-            st.lB += __shfl_xor_sync(FULL, st.lB, off);
-        }
+        __syncwarp();
+        process_tile<D, R, 4>(st, newk, newv, 1, pbuf, lane);
     }
+
+    for (int j = 0; j < my_tiles; ++j) {
+        const int s = j % SPW;
+        if (!mbar_wait(my_full + s, (j / SPW) & 1, p.err, DEV_WAIT_FULL_TIMEOUT)) break;
+        const int nv = min(TT, u_end - (u_begin + (warp + j * NW) * TT));
+        const float *tile = my_stages + (size_t)s * 2 * SM::TILE_F;
+        process_tile<D, R, TT>(st, tile, tile + SM::TILE_F, nv, pbuf, lane);
+        if (lane == 0 && j + SPW < my_tiles) issue(j + SPW);
+    }
+
+    // lane-partial sums -> per head (lanes with equal lane & 7); lane h < 8 then holds head h
+    st.l += __shfl_xor_sync(FULL, st.l, 8);
+    st.l += __shfl_xor_sync(FULL, st.l, 16);
     __syncthreads();   // every tile consumed: the stage memory is free
-    if (warp < NW) {
+    {
         float *cm = stages;              // [NW][8]
         float *cl = cm + NW * 8;         // [NW][8]
         float *co = cl + NW * 8;         // [NW][R][D]
+        if (lane < R) cl[warp * 8 + lane] = st.l;
         if (lane == 0)
 #pragma unroll
             for (int h = 0; h < R; ++h) cm[warp * 8 + h] = st.m[h];
-        if (lane < 4) {
-            cl[warp * 8 + 2 * lane] = st.lA;
-            cl[warp * 8 + 2 * lane + 1] = st.lB;
-        }
 #pragma unroll
         for (int h = 0; h < R; ++h)
 #pragma unroll
@@ -387,8 +364,7 @@ __global__ void __launch_bounds__((NW + 1) * 32, 1) attn_decode_kernel(const __g
     const float *cm = stages;
     const float *cl = cm + NW * 8;
     const float *co = cl + NW * 8;
-    const int Hq = p.H;
-    const size_t qh0 = (size_t)qi * Hq + (size_t)g * R;     // first query head of the group
+    const size_t qh0 = (size_t)qi * p.H + (size_t)g * R;     // first query head of the group
     const size_t part_base = ((size_t)qi * kv.G + g) * p.max_splits;
     for (int idx = tid; idx < R * D; idx += NT) {
         const int h = idx / D;
@@ -412,60 +388,110 @@ __global__ void __launch_bounds__((NW + 1) * 32, 1) attn_decode_kernel(const __g
             if (idx - h * D == 0) p.part_ml[(part_base + split) * R + h] = make_float2(M, L);
         }
     }
-    if (n_splits == 1) return;
-
-    // ---------------------------------------------------------------- split merge
-    __threadfence();
-    __syncthreads();
-    if (tid == 0) {
-        const unsigned prev = atomicAdd(&p.counters[(size_t)qi * kv.G + g], 1u);
-        s_last = prev == (unsigned)(n_splits - 1);
-    }
-    __syncthreads();
-    if (!s_last) return;
-    __threadfence();
-    float *wts = stages;                       // [n_splits][8] split weights
-    float *linv = wts + (size_t)n_splits * 8;  // [8] 1/L per head
-    float *mh = linv + 8;                      // [8] merged max per head
-    for (int h = warp; h < R; h += NW + 1) {
-        float M = -INFINITY;
-        for (int s = lane; s < n_splits; s += 32) M = fmaxf(M, __ldcg(&p.part_ml[(part_base + s) * R + h]).x);
-#pragma unroll
-        for (int off = 16; off > 0; off >>= 1) M = fmaxf(M, __shfl_xor_sync(FULL, M, off));
-        float L = 0.f;
-        for (int s = lane; s < n_splits; s += 32) {
-            const float2 ml = __ldcg(&p.part_ml[(part_base + s) * R + h]);
-            const float w = M == -INFINITY ? 0.f : fast_exp2(ml.x - M);
-            wts[s * 8 + h] = w;
-            L = fmaf(ml.y, w, L);
-        }
-#pragma unroll
-        for (int off = 16; off > 0; off >>= 1) L += __shfl_xor_sync(FULL, L, off);
-        if (lane == 0) {
-            linv[h] = L > 0.f ? 1.f / L : 0.f;
-            mh[h] = L > 0.f ? M + __log2f(L) : -INFINITY;
-        }
-    }
-    __syncthreads();
-    for (int idx = tid; idx < R * D; idx += NT) {
-        const int h = idx / D;
-        float O = 0.f;
-        for (int s = 0; s < n_splits; ++s) O = fmaf(wts[s * 8 + h], __ldcg(&p.part_o[(part_base + s) * R * D + idx]), O);
-        p.out[qh0 * D + idx] = O * linv[h];
-        if (p.lse && idx - h * D == 0) p.lse[qh0 + h] = mh[h];
-    }
-    if (tid == 0) p.counters[(size_t)qi * kv.G + g] = 0u;
 }
 
-// Tuning of the decode pipeline: 8 consumer warps, 8-token tiles, 16 stages
-// (two per consumer warp, so each warp's next tile loads while it computes).
-constexpr int kNW = 8, kTT = 8, kS = 16;
-static_assert(kS % kNW == 0, "a warp's tiles must cycle through its own stages");
+// Merges the per-split partials of one query head (one CTA, one thread per
+// dim): out = sum_s 2^(m_s - M) o_s / sum_s 2^(m_s - M) l_s. Launched right
+// after the decode kernel with a programmatic dependency; waits for it first.
+template <int D, int R>
+__global__ void __launch_bounds__(D) split_merge_kernel(const __grid_constant__ DecodeParams p) {
+    constexpr int CH = 64;   // partial values in flight per thread
+    __shared__ float w[kMaxSplits];
+    __shared__ float red[D / 32];
+    __shared__ float s_M, s_L;
+    grid_dep_wait();
+    grid_dep_launch();
+    const int h = blockIdx.x % R, g = blockIdx.x / R, qi = blockIdx.y, tid = threadIdx.x;
+    const int pos = p.contiguous ? p.pos0 + qi : p.pos[qi];
+    const PagedKv &kv = p.kv;
+    const int P = kv.P, NS = kv.shard_count, rank = kv.shard_rank;
+    const int limit = p.append_new ? pos : pos + 1;
+    const int F = limit / P, rem = limit - F * P;
+    const int nfull_local = F > rank ? (F - rank + NS - 1) / NS : 0;
+    const int count = nfull_local * P + ((F % NS == rank) ? rem : 0);
+    const int n_splits = (count + p.split_tokens - 1) / p.split_tokens;
+    if (n_splits <= 1) return;   // the decode kernel wrote this output directly
+    const size_t base = ((size_t)qi * kv.G + g) * p.max_splits;
+    const float *po = p.part_o + base * R * D + (size_t)h * D + tid;
+
+    float v[CH];
+#pragma unroll
+    for (int s = 0; s < CH; ++s) v[s] = s < n_splits ? __ldcg(po + (size_t)s * R * D) : 0.f;
+    // split weights: block max of the split maxima, then 2^(m_s - M)
+    float M = -INFINITY;
+    for (int s = tid; s < n_splits; s += D) M = fmaxf(M, __ldcg(&p.part_ml[(base + s) * R + h]).x);
+#pragma unroll
+    for (int off = 16; off > 0; off >>= 1) M = fmaxf(M, __shfl_xor_sync(FULL, M, off));
+    if ((tid & 31) == 0) red[tid >> 5] = M;
+    __syncthreads();
+    if (tid == 0) {
+        float m = red[0];
+        for (int i = 1; i < D / 32; ++i) m = fmaxf(m, red[i]);
+        s_M = m;
+    }
+    __syncthreads();
+    M = s_M;
+    float L = 0.f;
+    for (int s = tid; s < n_splits; s += D) {
+        const float2 ml = __ldcg(&p.part_ml[(base + s) * R + h]);
+        const float ws = M == -INFINITY ? 0.f : fast_exp2(ml.x - M);
+        w[s] = ws;
+        L = fmaf(ml.y, ws, L);
+    }
+#pragma unroll
+    for (int off = 16; off > 0; off >>= 1) L += __shfl_xor_sync(FULL, L, off);
+    __syncthreads();
+    if ((tid & 31) == 0) red[tid >> 5] = L;
+    __syncthreads();
+    if (tid == 0) {
+        float l = 0.f;
+        for (int i = 0; i < D / 32; ++i) l += red[i];
+        s_L = l;
+    }
+    __syncthreads();
+    L = s_L;
+    float a0 = 0.f, a1 = 0.f, a2 = 0.f, a3 = 0.f;
+#pragma unroll
+    for (int s = 0; s < CH; s += 4) {
+        if (s < n_splits) a0 = fmaf(w[s], v[s], a0);
+        if (s + 1 < n_splits) a1 = fmaf(w[s + 1], v[s + 1], a1);
+        if (s + 2 < n_splits) a2 = fmaf(w[s + 2], v[s + 2], a2);
+        if (s + 3 < n_splits) a3 = fmaf(w[s + 3], v[s + 3], a3);
+    }
+    for (int c0 = CH; c0 < n_splits; c0 += CH) {
+#pragma unroll
+        for (int s = 0; s < CH; ++s) v[s] = c0 + s < n_splits ? __ldcg(po + (size_t)(c0 + s) * R * D) : 0.f;
+#pragma unroll
+        for (int s = 0; s < CH; ++s)
+            if (c0 + s < n_splits) a0 = fmaf(w[c0 + s], v[s], a0);
+    }
+    const float acc = (a0 + a1) + (a2 + a3);
+    const size_t qh = (size_t)qi * p.H + (size_t)g * R + h;
+    p.out[qh * D + tid] = L > 0.f ? acc / L : 0.f;
+    if (p.lse && tid == 0) p.lse[qh] = L > 0.f ? M + __log2f(L) : -INFINITY;
+}
+
+#ifndef KORE_DECODE_NW
+#define KORE_DECODE_NW 8
+#endif
+#ifndef KORE_DECODE_TT
+#define KORE_DECODE_TT 8
+#endif
+#ifndef KORE_DECODE_SPW
+#define KORE_DECODE_SPW 3
+#endif
+// Decode pipeline shape: NW warps per CTA, TT-token tiles, SPW stages per warp.
+constexpr int kNW = KORE_DECODE_NW, kTT = KORE_DECODE_TT, kSPW = KORE_DECODE_SPW;
+static_assert(kTT % 4 == 0, "tiles are processed in 4-token rounds");
+static_assert(64 % kTT == 0, "a tile must not cross a page (pages are multiples of 64 positions)");
+static_assert(DecodeSmem<128, kNW, kTT, kSPW>::bytes <= 227 * 1024, "decode stages exceed shared memory");
+static_assert(DecodeSmem<64, kNW, kTT, kSPW>::stage_floats >= (size_t)kMaxSplits * 8 + 16 + 8 * 64 + 64,
+              "split merge needs room for the weights and one staged partial");
 
 template <int D, int R>
 cudaError_t launch_dr(const DecodeParams &p, int grid_x, cudaStream_t s) {
-    using SM = DecodeSmem<D, kNW, kTT, kS>;
-    auto kern = attn_decode_kernel<D, R, kNW, kTT, kS>;
+    using SM = DecodeSmem<D, kNW, kTT, kSPW>;
+    auto kern = attn_decode_kernel<D, R, kNW, kTT, kSPW>;
     static bool configured[64] = {};
     int dev = 0;
     cudaGetDevice(&dev);
@@ -474,9 +500,23 @@ cudaError_t launch_dr(const DecodeParams &p, int grid_x, cudaStream_t s) {
         if (e != cudaSuccess) return e;
         if (dev >= 0 && dev < 64) configured[dev] = true;
     }
-    dim3 grid(grid_x, p.kv.G, p.n_q);
-    kern<<<grid, (kNW + 1) * 32, SM::bytes, s>>>(p);
-    return cudaGetLastError();
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(grid_x, p.kv.G, p.n_q);
+    cfg.blockDim = dim3(kNW * 32);
+    cfg.dynamicSmemBytes = SM::bytes;
+    cfg.stream = s;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    cudaError_t e = cudaLaunchKernelEx(&cfg, kern, p);
+    if (e != cudaSuccess || grid_x == 1) return e;
+    cudaLaunchConfig_t mcfg = cfg;
+    mcfg.gridDim = dim3(p.kv.G * R, p.n_q);
+    mcfg.blockDim = dim3(D);
+    mcfg.dynamicSmemBytes = 0;
+    return cudaLaunchKernelEx(&mcfg, split_merge_kernel<D, R>, p);
 }
 
 template <int D>
@@ -503,14 +543,16 @@ cudaError_t launch_attn_decode(const DecodeParams &p, int n_rep, int grid_x, cud
 }
 
 int decode_ctas_per_sm(int head_dim, int) {
-    const size_t b = head_dim == 128 ? DecodeSmem<128, kNW, kTT, kS>::bytes : DecodeSmem<64, kNW, kTT, kS>::bytes;
-    return b * 2 <= 227 * 1024 ? 2 : 1;
+    const size_t b = head_dim == 128 ? DecodeSmem<128, kNW, kTT, kSPW>::bytes : DecodeSmem<64, kNW, kTT, kSPW>::bytes;
+    return b * 2 <= 227 * 1024 && kNW <= 8 ? 2 : 1;
 }
 
 int decode_tile_tokens() { return kTT; }
 
+int decode_split_pages_max() { return kSplitPagesMax; }
+
 size_t decode_smem_bytes(int head_dim) {
-    return head_dim == 128 ? DecodeSmem<128, kNW, kTT, kS>::bytes : DecodeSmem<64, kNW, kTT, kS>::bytes;
+    return head_dim == 128 ? DecodeSmem<128, kNW, kTT, kSPW>::bytes : DecodeSmem<64, kNW, kTT, kSPW>::bytes;
 }
 
 }  // namespace kore

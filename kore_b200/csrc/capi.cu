@@ -41,13 +41,13 @@ struct kore_cuda_ctx {
     float *part_o = nullptr;
     float2 *part_ml = nullptr;
     size_t part_slots = 0;      // (query, kv head, split) slots of split scratch
-    unsigned *counters = nullptr;
     int *err_d = nullptr;
     float *dev_stage = nullptr;
     size_t dev_stage_floats = 0;
     float *host_stage = nullptr;
     size_t host_stage_floats = 0;
     int *host_err = nullptr;
+    int last_kv_layer = -1;     // layer whose KV the most recent kernel of this context wrote
     std::string msg;
 };
 
@@ -182,7 +182,6 @@ int finish(kore_cuda_ctx *c) {
     const int e = *c->host_err;
     if (e != DEV_OK) {
         CK(cudaMemsetAsync(c->err_d, 0, sizeof(int), c->stream));
-        CK(cudaMemsetAsync(c->counters, 0, sizeof(unsigned) * kMaxBatch * c->G, c->stream));
         CK(cudaStreamSynchronize(c->stream));
         return fail(c, KORE_CUDA_EDEVICE, "device error %d (%s)", e,
                     e == DEV_BAD_PAGE ? "page table entry outside the pool"
@@ -203,6 +202,7 @@ int run_append(kore_cuda_ctx *c, int seq, int layer, int pos0, int n, const floa
     ap.pos0 = pos0;
     ap.n = n;
     CK(launch_kv_append(ap, c->stream));
+    c->last_kv_layer = layer;
     return KORE_CUDA_OK;
 }
 
@@ -226,7 +226,6 @@ int run_decode(kore_cuda_ctx *c, int layer, int n_q, bool contiguous, int seq0, 
     p.rope = c->rope_d;
     p.part_o = c->part_o;
     p.part_ml = c->part_ml;
-    p.counters = c->counters;
     p.err = c->err_d;
     p.scale_log2 = (1.0f / std::sqrt((float)c->D)) * 1.4426950408889634f;
     p.H = c->H;
@@ -254,7 +253,7 @@ int run_decode(kore_cuda_ctx *c, int layer, int n_q, bool contiguous, int seq0, 
     st = std::max<long long>(st, (max_count + kMaxSplits - 1) / kMaxSplits);
     int grid_x;
     if (n_q > kMaxBatch) {
-        st = std::max(max_count, TT);   // one split per query: no scratch, no counters
+        st = std::max(max_count, TT);   // one split per query: no scratch
     }
     for (;;) {
         st = (st + TT - 1) / TT * TT;
@@ -262,10 +261,24 @@ int run_decode(kore_cuda_ctx *c, int layer, int n_q, bool contiguous, int seq0, 
         if (grid_x == 1 || (size_t)n_q * c->G * grid_x <= c->part_slots) break;
         st *= 2;
     }
+    // a split may span at most decode_split_pages_max() pages
+    const long long st_cap = (long long)(decode_split_pages_max() - 1) * c->P / TT * TT;
+    if (st > st_cap) {
+        st = st_cap;
+        grid_x = std::max(1, (int)((max_count + st - 1) / st));
+        if (n_q > kMaxBatch && grid_x > 1)
+            return fail(c, KORE_CUDA_EINVAL, "prefill of %d tokens over %d positions exceeds one launch", n_q, max_count);
+        if ((size_t)n_q * c->G * grid_x > c->part_slots)
+            return fail(c, KORE_CUDA_EINVAL, "decode batch too large for the split scratch");
+    }
     if (grid_x > kMaxSplits) return fail(c, KORE_CUDA_EINVAL, "too many splits for one decode launch");
     p.split_tokens = (int)st;
     p.max_splits = grid_x;
+    p.prefetch_ok = c->last_kv_layer != layer;
     CK(launch_attn_decode(p, c->R, grid_x, c->stream));
+    // with more than one split the last kernel launched is the split merge,
+    // which writes no KV and starts its successor only once the decode is done
+    c->last_kv_layer = (append_new && grid_x == 1) ? layer : -1;
     return KORE_CUDA_OK;
 }
 
@@ -298,7 +311,6 @@ void kore_cuda_destroy(kore_cuda_ctx *c) {
         cudaFree(c->rope_d);
         cudaFree(c->part_o);
         cudaFree(c->part_ml);
-        cudaFree(c->counters);
         cudaFree(c->err_d);
         cudaFree(c->dev_stage);
         if (c->host_stage) cudaFreeHost(c->host_stage);
@@ -387,8 +399,6 @@ int kore_cuda_create(kore_cuda_ctx **out, const kore_cuda_cfg *cfg) {
     c->part_slots = kPartSlots;
     CKB(cudaMalloc(&c->part_o, c->part_slots * c->R * c->D * sizeof(float)));
     CKB(cudaMalloc(&c->part_ml, c->part_slots * c->R * sizeof(float2)));
-    CKB(cudaMalloc(&c->counters, sizeof(unsigned) * kMaxBatch * c->G));
-    CKB(cudaMemsetAsync(c->counters, 0, sizeof(unsigned) * kMaxBatch * c->G, c->stream));
     CKB(cudaMalloc(&c->err_d, sizeof(int)));
     CKB(cudaMemsetAsync(c->err_d, 0, sizeof(int), c->stream));
     CKB(cudaMallocHost(&c->host_err, sizeof(int)));
@@ -607,6 +617,7 @@ int kore_cuda_set_stream(kore_cuda_ctx *c, void *stream) {
     if (c->own_stream) cudaStreamDestroy(c->stream);
     c->stream = (cudaStream_t)stream;
     c->own_stream = false;
+    c->last_kv_layer = -1;   // the old stream was drained above: nothing of ours is in flight
     return KORE_CUDA_OK;
 }
 

@@ -81,6 +81,13 @@ __device__ __forceinline__ bool mbar_wait(uint64_t *bar, uint32_t parity, int *e
 
 // ---------------------------------------------------------------- bulk copy
 
+// Orders this thread's earlier generic-proxy accesses of shared memory before
+// later async-proxy (bulk copy) accesses: a stage that was just read is only
+// then refilled.
+__device__ __forceinline__ void fence_proxy_async_smem() {
+    asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+}
+
 // Creates an L2 policy that marks lines as first to evict: streamed K/V are
 // read exactly once per launch.
 __device__ __forceinline__ uint64_t l2_evict_first_policy() {
@@ -100,6 +107,14 @@ __device__ __forceinline__ void bulk_g2s(void *dst, const void *src, uint32_t by
         "l"(src), "r"(bytes), "r"(smem_u32(bar)), "l"(policy)
         : "memory");
 }
+
+// ---------------------------------------------------------------- dependent launch
+
+// Programmatic dependent launch: wait until the preceding kernel in the stream
+// has completed and its writes are visible (a no-op when this launch has no
+// programmatic dependency), and allow the next kernel to be scheduled.
+__device__ __forceinline__ void grid_dep_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+__device__ __forceinline__ void grid_dep_launch() { asm volatile("griddepcontrol.launch_dependents;" ::: "memory"); }
 
 // ---------------------------------------------------------------- math
 
