@@ -177,6 +177,57 @@ int kore_cuda_sync(kore_cuda_ctx *ctx);
 void *kore_cuda_stream(kore_cuda_ctx *ctx);
 int kore_cuda_set_stream(kore_cuda_ctx *ctx, void *stream);
 
+/*
+ * Decode for callers that cannot allocate GPU memory.
+ *
+ * No counterpart in the reference: kore has no GPU code, and this entry point
+ * is an addition of this library. Some hosts own all device memory themselves
+ * and forbid allocations once they run: an inference server that carves
+ * every buffer out of its own pre-reserved pool (so that a stray cudaMalloc
+ * cannot fragment memory or stall its other streams), or a plugin whose host
+ * hands it device buffers and a stream but no permission to allocate. Such a
+ * caller cannot create a context (kore_cuda_create allocates the KV pool,
+ * the RoPE tables and split scratch). Here it lays the paged KV cache out
+ * itself, in a context's layout (kore_cuda_kv_view), and passes every input
+ * and output; the call allocates nothing. The KV-split scratch it needs is a
+ * fixed array inside the library, KORE_CUDA_NOALLOC_SCRATCH_BYTES on every
+ * GPU that loads the library, held until the process exits.
+ *
+ *  - The first call on a device looks up the array's device address (a
+ *    one-time set-up done with that device current); make that first call
+ *    before any stream capture.
+ *  - All calls on a device share the one array and it keeps the last call's
+ *    contents, so calls that overlap on the GPU (on different streams, or from
+ *    host threads without ordering) race and corrupt each other's results:
+ *    serialise them. Nothing in it has to start at zero: a call writes every
+ *    slot it later reads.
+ *  - A geometry whose split scratch would exceed the array is refused with
+ *    KORE_CUDA_EINVAL and a message (kore_cuda_last_error(NULL)).
+ */
+#define KORE_CUDA_NOALLOC_SCRATCH_BYTES (2359296)   /* 2.25 MiB */
+
+typedef struct kore_cuda_kv_view {
+    float *k_pages;         /* device [n_pages][n_head_kv][page_tokens][head_dim], post-RoPE keys */
+    float *v_pages;         /* device, same layout, values */
+    const int *page_table;  /* device [n_table]: physical page of logical page j */
+    int n_table;
+    int n_pages;
+    int page_tokens;        /* a multiple of 64 */
+    int n_head, n_head_kv, head_dim;   /* as in kore_cuda_cfg */
+    const float *rope_cs;   /* device [n_rope][head_dim/2][2]: (cos, sin) per position, kore.cpp:1405-1410 */
+    int n_rope;
+} kore_cuda_kv_view;
+
+/* One decode step of the sequence described by kv: RoPE of q and k at pos,
+ * append of k/v at pos (written into kv's pages), attention over positions
+ * 0..pos, output to out [n_head*head_dim]. q, k, v, out and dev_status are
+ * device pointers; dev_status (optional, zeroed by the caller) receives a
+ * non-zero code if a kernel meets a page id outside the pool. Ordered on
+ * `stream` (a cudaStream_t; NULL for the default stream); returns without
+ * synchronising. */
+int kore_cuda_attn_decode_noalloc(const kore_cuda_kv_view *kv, int pos, const float *q, const float *k,
+                                  const float *v, float *out, int *dev_status, void *stream);
+
 #ifdef __cplusplus
 }
 #endif

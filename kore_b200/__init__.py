@@ -19,7 +19,7 @@ import numpy as np
 
 from .build import LIB, INCLUDE
 
-__all__ = ["KoreCuda", "KoreCudaError", "load_library", "declared_symbols", "STATUS"]
+__all__ = ["KoreCuda", "KoreCudaError", "KvView", "load_library", "declared_symbols", "STATUS"]
 
 STATUS = {
     0: "KORE_CUDA_OK", -1: "KORE_CUDA_EINVAL", -2: "KORE_CUDA_ERANGE", -3: "KORE_CUDA_ENOMEM",
@@ -40,6 +40,17 @@ class _Cfg(ctypes.Structure):
         ("page_tokens", ctypes.c_int), ("n_pages", ctypes.c_int), ("rope_base", ctypes.c_float),
         ("inv_freq", ctypes.POINTER(ctypes.c_float)), ("device", ctypes.c_int),
         ("shard_rank", ctypes.c_int), ("shard_count", ctypes.c_int),
+    ]
+
+
+class KvView(ctypes.Structure):
+    """kore_cuda_kv_view: a caller-owned paged KV cache for the no-allocation
+    decode entry point (all pointers are device addresses)."""
+    _fields_ = [
+        ("k_pages", ctypes.c_void_p), ("v_pages", ctypes.c_void_p), ("page_table", ctypes.c_void_p),
+        ("n_table", ctypes.c_int), ("n_pages", ctypes.c_int), ("page_tokens", ctypes.c_int),
+        ("n_head", ctypes.c_int), ("n_head_kv", ctypes.c_int), ("head_dim", ctypes.c_int),
+        ("rope_cs", ctypes.c_void_p), ("n_rope", ctypes.c_int),
     ]
 
 
@@ -87,6 +98,7 @@ def load_library(path: str = LIB):
     L.kore_cuda_attn_decode_partial_dev.argtypes = [_vp, _i, _i, _i, _vp, _vp, _vp, _vp]
     L.kore_cuda_lse_merge_dev.argtypes = [_vp, _i, _vp, _vp]
     L.kore_cuda_kv_read.argtypes = [_vp, _i, _i, _i, _i, _vp, _vp]
+    L.kore_cuda_attn_decode_noalloc.argtypes = [ctypes.POINTER(KvView), _i, _vp, _vp, _vp, _vp, _vp, _vp]
     L.kore_cuda_sync.argtypes = [_vp]
     L.kore_cuda_stream.argtypes = [_vp]
     L.kore_cuda_stream.restype = _vp

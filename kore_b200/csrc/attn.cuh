@@ -60,6 +60,7 @@ int decode_tile_tokens();
 int decode_split_pages_max();
 size_t decode_smem_bytes(int head_dim);
 cudaError_t launch_kv_append(const AppendParams &p, cudaStream_t s);
+void set_ctxless_error(const char *msg);
 cudaError_t launch_lse_merge(const float *parts, int n_parts, int H, int D, float *out, cudaStream_t s);
 
 }  // namespace kore

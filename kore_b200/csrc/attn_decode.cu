@@ -41,8 +41,14 @@
 // (positions split over GPUs) the output is the normalised partial plus its
 // log2-domain log-sum-exp.
 
+#include "../../include/kore_cuda.h"
 #include "attn.cuh"
 #include "common.cuh"
+
+#include <algorithm>
+#include <cstdio>
+#include <cstring>
+#include <mutex>
 
 namespace kore {
 namespace {
@@ -555,4 +561,124 @@ size_t decode_smem_bytes(int head_dim) {
     return head_dim == 128 ? DecodeSmem<128, kNW, kTT, kSPW>::bytes : DecodeSmem<64, kNW, kTT, kSPW>::bytes;
 }
 
+// ---------------------------------------------------------------- no-allocation decode
+//
+// kore_cuda_attn_decode_noalloc runs the decode and split-merge kernels above
+// for callers that cannot allocate device memory (see include/kore_cuda.h);
+// their KV-split scratch is this fixed array instead of a context's buffers.
+
+namespace {
+
+constexpr size_t kNoallocFloats = KORE_CUDA_NOALLOC_SCRATCH_BYTES / sizeof(float);
+constexpr size_t kNoallocPartFloats = (size_t)1 << 19;                          // split outputs: 2 MiB
+constexpr size_t kNoallocMlPairs = (kNoallocFloats - kNoallocPartFloats) / 2;   // split (max, sum) pairs
+static_assert(kNoallocFloats > kNoallocPartFloats, "scratch layout");
+
+static __device__ __align__(256) float g_noalloc_scratch[kNoallocFloats];
+
+struct NoallocDevice {
+    float *scratch = nullptr;   // device address of g_noalloc_scratch on this device
+    int num_sms = 0;
+};
+std::mutex g_noalloc_mu;
+NoallocDevice g_noalloc_dev[64];
+
+int noalloc_fail(int code, const char *fmt, long long a = 0, long long b = 0) {
+    char buf[256];
+    snprintf(buf, sizeof buf, fmt, a, b);
+    set_ctxless_error(buf);
+    return code;
+}
+
+}  // namespace
 }  // namespace kore
+
+extern "C" int kore_cuda_attn_decode_noalloc(const kore_cuda_kv_view *kv, int pos, const float *q, const float *k,
+                                             const float *v, float *out, int *dev_status, void *stream) {
+    using namespace kore;
+    if (!kv || !q || !k || !v || !out || !kv->k_pages || !kv->v_pages || !kv->page_table || !kv->rope_cs)
+        return noalloc_fail(KORE_CUDA_EINVAL, "null argument");
+    const int H = kv->n_head, G = kv->n_head_kv, D = kv->head_dim, P = kv->page_tokens;
+    if (G <= 0 || H <= 0 || H % G || H / G > 8 || (D != 64 && D != 128))
+        return noalloc_fail(KORE_CUDA_EINVAL, "unsupported geometry: n_head %lld, n_head_kv %lld", H, G);
+    if (P <= 0 || P % 64 || kv->n_pages <= 0)
+        return noalloc_fail(KORE_CUDA_EINVAL, "page_tokens %lld must be a positive multiple of 64", P);
+    if ((reinterpret_cast<uintptr_t>(kv->k_pages) | reinterpret_cast<uintptr_t>(kv->v_pages)) & 15)
+        return noalloc_fail(KORE_CUDA_EINVAL, "page pools must be 16-byte aligned");
+    if (pos < 0 || pos >= kv->n_rope || pos / P >= kv->n_table)
+        return noalloc_fail(KORE_CUDA_ERANGE, "position %lld outside the RoPE table or the page table", pos);
+
+    int dev = 0;
+    if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64)
+        return noalloc_fail(KORE_CUDA_ECUDA, "no current CUDA device");
+    NoallocDevice nd;
+    {
+        std::lock_guard<std::mutex> lk(g_noalloc_mu);
+        NoallocDevice &d = g_noalloc_dev[dev];
+        if (!d.scratch) {   // once per device, with that device current
+            void *ptr = nullptr;
+            cudaError_t e = cudaGetSymbolAddress(&ptr, g_noalloc_scratch);
+            if (e != cudaSuccess)
+                return noalloc_fail(KORE_CUDA_ECUDA, "cudaGetSymbolAddress of the scratch array failed (error %lld)",
+                                    (long long)e);
+            e = cudaDeviceGetAttribute(&d.num_sms, cudaDevAttrMultiProcessorCount, dev);
+            if (e != cudaSuccess)
+                return noalloc_fail(KORE_CUDA_ECUDA, "cudaDeviceGetAttribute failed (error %lld)", (long long)e);
+            d.scratch = static_cast<float *>(ptr);
+        }
+        nd = d;
+    }
+
+    const int R = H / G, TT = decode_tile_tokens();
+    const int count = pos;   // cached positions 0..pos-1; the token at pos comes from k/v
+    // splits: enough CTAs to fill the GPU, within the scratch array and the
+    // per-split page list
+    long long splits = std::max(1, (nd.num_sms + G - 1) / G);
+    const long long cap_o = (long long)(kNoallocPartFloats / ((size_t)G * R * D));
+    const long long cap_ml = (long long)(kNoallocMlPairs / ((size_t)G * R));
+    splits = std::min(std::min(splits, (long long)kMaxSplits), std::min(cap_o, cap_ml));
+    long long st = (count + splits - 1) / splits;
+    st = std::max<long long>((st + TT - 1) / TT * TT, 4 * TT);
+    const long long st_cap = (long long)(decode_split_pages_max() - 1) * P / TT * TT;
+    if (st > st_cap) st = st_cap;
+    const int grid_x = std::max(1, (int)((count + st - 1) / st));
+    if ((size_t)G * grid_x * R * D > kNoallocPartFloats || (size_t)G * grid_x * R > kNoallocMlPairs ||
+        grid_x > kMaxSplits)
+        return noalloc_fail(KORE_CUDA_EINVAL, "%lld cached positions need more split scratch than the %lld-byte array",
+                            count, (long long)KORE_CUDA_NOALLOC_SCRATCH_BYTES);
+
+    DecodeParams p;
+    memset(&p, 0, sizeof p);
+    p.kv.k = kv->k_pages;
+    p.kv.v_off = (long long)(kv->v_pages - kv->k_pages);
+    p.kv.page_table = kv->page_table;
+    p.kv.pt_stride = kv->n_table;
+    p.kv.P = P;
+    p.kv.G = G;
+    p.kv.D = D;
+    p.kv.n_pages = kv->n_pages;
+    p.kv.shard_rank = 0;
+    p.kv.shard_count = 1;
+    p.q = q;
+    p.k_new = k;
+    p.v_new = v;
+    p.out = out;
+    p.lse = nullptr;
+    p.rope = reinterpret_cast<const float2 *>(kv->rope_cs);
+    p.part_o = nd.scratch;
+    p.part_ml = reinterpret_cast<float2 *>(nd.scratch + kNoallocPartFloats);
+    p.err = dev_status;
+    p.scale_log2 = (1.0f / sqrtf((float)D)) * 1.4426950408889634f;
+    p.H = H;
+    p.n_q = 1;
+    p.split_tokens = (int)st;
+    p.max_splits = grid_x;
+    p.append_new = 1;
+    p.contiguous = 1;
+    p.seq0 = 0;
+    p.pos0 = pos;
+    p.prefetch_ok = 0;   // nothing is known about the previous kernel on the caller's stream
+    const cudaError_t e = launch_attn_decode(p, R, grid_x, static_cast<cudaStream_t>(stream));
+    if (e != cudaSuccess) return noalloc_fail(KORE_CUDA_ECUDA, "decode launch failed (error %lld)", (long long)e);
+    return KORE_CUDA_OK;
+}

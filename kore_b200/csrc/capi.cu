@@ -55,6 +55,15 @@ namespace {
 
 thread_local std::string g_create_msg = "no error";
 
+}  // namespace
+
+namespace kore {
+// Message for calls that have no context (read with kore_cuda_last_error(NULL)).
+void set_ctxless_error(const char *msg) { g_create_msg = msg; }
+}  // namespace kore
+
+namespace {
+
 int fail(kore_cuda_ctx *c, int code, const char *fmt, ...) {
     char buf[512];
     va_list ap;
