@@ -129,7 +129,10 @@ def run_ours(args, rank: int, world: int, dist) -> dict | None:
     dev = torch.device("cuda", int(os.environ.get("LOCAL_RANK", 0)))
     torch.cuda.set_device(dev)
     ctx = K.KoreCuda(L, H, G, D, CTX, device=dev.index, shard_rank=rank, shard_count=world)
-    stream = torch.cuda.ExternalStream(ctx.stream, device=dev)
+    # the context runs on a torch-owned stream, so tensors used on it (and by
+    # NCCL) outlive nothing they depend on when the context is closed
+    stream = torch.cuda.Stream(device=dev)
+    ctx.set_stream(stream.cuda_stream)
 
     # seeded N(0,1) cache: all rows generated on the device per layer; each
     # shard stores the rows of the pages it holds

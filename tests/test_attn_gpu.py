@@ -196,3 +196,40 @@ def test_errors_are_codes_not_crashes():
     assert e.value.code == -2
     out = g.decode(0, 0, 0, q, k, v)            # the context is still usable
     assert np.isfinite(out).all()
+
+
+# ------------------------------------------------------------------ KV positions split over GPUs
+
+@pytest.mark.parametrize("n_shards,pos", [(2, 3000), (3, 2049), (8, 700), (8, 100)])
+def test_kv_sharded_decode_partials_merge_to_the_full_result(n_shards, pos):
+    """Config 4's multi-GPU split, emulated with one context per shard on one
+    GPU: each shard holds pages j = rank (mod N) and returns its partial; the
+    LSE merge of the partials must equal kore's single softmax. With pos 100
+    and 8 shards, seven shards hold no position at all."""
+    import torch
+    H, G, d = 28, 4, 128
+    ctxs = [make_ctx(H, G, d, 4096, shard_rank=r, shard_count=n_shards) for r in range(n_shards)]
+    o = O.OracleLayer(H, G, d, 4096)
+    k, v = normal(70 + n_shards, (pos, G * d), (pos, G * d))
+    for c in ctxs:
+        c.append(0, 0, 0, k, v)
+    o.fill(0, k, v)
+    q1, k1, v1 = normal(71, (H * d,), (G * d,), (G * d,))
+    dev = torch.device("cuda", 0)
+    tq, tk, tv = (torch.from_numpy(x).to(dev) for x in (q1, k1, v1))
+    parts = torch.empty(n_shards, ctxs[0].part_floats, device=dev)
+    for r, c in enumerate(ctxs):
+        c.decode_partial_dev(0, 0, pos, tq, tk, tv, parts[r])
+        c.sync()
+    out = torch.empty(H * d, device=dev)
+    ctxs[0].lse_merge_dev(n_shards, parts, out)
+    ctxs[0].sync()
+    assert_attn_close(out.cpu().numpy().reshape(H, d), o.decode(pos, q1, k1, v1), f"{n_shards} shards")
+    # each row is stored by exactly one shard, the new one included
+    rows = np.zeros((pos + 1, G * d), np.float32)
+    for r, c in enumerate(ctxs):
+        kr, _ = c.kv_read(0, 0, 0, pos + 1)
+        owned = (np.arange(pos + 1) // 256) % n_shards == r
+        assert not kr[~owned].any()
+        rows[owned] = kr[owned]
+    np.testing.assert_array_equal(rows, o.kc[:pos + 1])
