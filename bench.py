@@ -8,15 +8,16 @@ token through all 28 layers: RoPE of q/k at position 32768, append of k/v,
 attention over positions 0..32768.
 
   value  device-resident: q/k/v already in HBM, CUDA events on the context's
-         stream around K replays of a CUDA graph holding one step (1 GPU;
-         eager launches at N > 1); GB/s of algorithmic bytes
+         stream around K replays of a CUDA graph holding one step; max over
+         ranks; GB/s of algorithmic bytes
          (per layer: 2*(pos+1)*512*4 K/V + 2*28*128*4 q/out + 2*512*4 append).
   e2e    the same steps through the host-buffer C entry point
          kore_cuda_attn_decode (kore's call: host q/k/v in, host out back),
          wall clock, copies included.
 At N > 1 the KV positions are split over the GPUs by page (round robin); each
-layer's partial outputs and log-sum-exps are all-gathered over NCCL and
-merged. The cache is fixed (strong scaling).
+layer's partial outputs and log-sum-exps are pushed to every peer over NVLink
+peer memory and merged on every rank (kore_cuda_attn_decode_sharded_dev), one
+exchange per layer. The cache is fixed (strong scaling).
 
 ``--impl reference`` times kore's own CPU attention (the reference compiled
 in place, oracle/_ref) on this host: kore.cpp forward() per layer on its
@@ -150,17 +151,19 @@ def run_ours(args, rank: int, world: int, dist) -> dict | None:
         vn = torch.randn(L, KVD, device=dev, generator=gen)
         out = torch.empty(L, H * D, device=dev)
         part = torch.empty(L, ctx.part_floats, device=dev)
-        parts = torch.empty(L, world, ctx.part_floats, device=dev)
     ctx.sync()
+
+    if world > 1:
+        from kore_b200.shard import exchange_handles
+        exchange_handles(ctx, dist)     # exchange buffers mapped over CUDA IPC
 
     def step():
         for layer in range(L):
             if world == 1:
                 ctx.decode_dev(0, layer, POS, q[layer], kn[layer], vn[layer], out[layer])
             else:
-                ctx.decode_partial_dev(0, layer, POS, q[layer], kn[layer], vn[layer], part[layer])
-                dist.all_gather_into_tensor(parts[layer], part[layer])
-                ctx.lse_merge_dev(world, parts[layer], out[layer])
+                # partial on this rank's pages, pushed to the peers over NVLink, merged on every rank
+                ctx.decode_sharded_dev(0, layer, POS, q[layer], kn[layer], vn[layer], out[layer])
 
     def barrier():
         if world > 1:
@@ -173,18 +176,18 @@ def run_ours(args, rank: int, world: int, dist) -> dict | None:
     ctx.sync()
     barrier()
 
-    # one decode step of all layers captured once as a CUDA graph (1 GPU): the
-    # per-layer launches then cost no host time inside the timed region
-    graph = None
-    if world == 1:
-        graph = torch.cuda.CUDAGraph()
-        with torch.cuda.graph(graph, stream=stream):
-            step()
-        with torch.cuda.stream(stream):
-            for _ in range(3):
-                graph.replay()
-        ctx.sync()
-    run = graph.replay if graph is not None else step
+    # one decode step of all layers captured once as a CUDA graph: the
+    # per-layer launches then cost no host time inside the timed region (the
+    # cross-GPU exchange keeps its epochs on the device, so replays stay in step)
+    graph = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(graph, stream=stream):
+        step()
+    barrier()
+    with torch.cuda.stream(stream):
+        for _ in range(3):
+            graph.replay()
+    ctx.sync()
+    run = graph.replay
 
     clocks = ClockSampler(dev.index)
     clocks.start()
@@ -247,9 +250,7 @@ def run_ours(args, rank: int, world: int, dist) -> dict | None:
                     q[layer].copy_(hq[layer], non_blocking=True)
                     kn[layer].copy_(hk[layer], non_blocking=True)
                     vn[layer].copy_(hv[layer], non_blocking=True)
-                    ctx.decode_partial_dev(0, layer, POS, q[layer], kn[layer], vn[layer], part[layer])
-                    dist.all_gather_into_tensor(parts[layer], part[layer])
-                    ctx.lse_merge_dev(world, parts[layer], out[layer])
+                    ctx.decode_sharded_dev(0, layer, POS, q[layer], kn[layer], vn[layer], out[layer])
                     ho[layer].copy_(out[layer], non_blocking=True)
                     stream.synchronize()
         e2e_ms = (time.perf_counter() - t0) * 1e3 / args.e2e_steps
@@ -281,7 +282,7 @@ def run_ours(args, rank: int, world: int, dist) -> dict | None:
                    "kv_split": f"pages round-robin over {world} GPU(s)" if world > 1 else "none"},
         "e2e": {"value": round(e2e_gbs, 1), "unit": "GB/s", "ms_per_step": round(e2e_ms, 4),
                 "h2d_bytes_per_step": L * (H * D + 2 * KVD) * 4, "d2h_bytes_per_step": L * H * D * 4},
-        "roofline": {"bound": "hbm", "kernel": "attn_decode_kernel<128,7,8,8,3> + split_merge_kernel<128,7>",
+        "roofline": {"bound": "hbm", "kernel": "attn_decode_kernel<128,7,8,8,3> + split_merge_kernel<128,7>" + (" + peer_exchange_kernel" if world > 1 else ""),
                      "achieved": round(achieved, 1), "peak": peaks["hbm_gbs"], "peak_source": peaks["source"],
                      "unit": "GB/s", "frac": round(achieved / peaks["hbm_gbs"], 4), "traffic": load_traffic(),
                      "launch_ms": round(layer_ms, 5), "launch_ms_isolated": round(iso_ms, 5),

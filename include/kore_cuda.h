@@ -23,9 +23,10 @@
  *    (kore.cpp:1400, :1490).
  *  - Host-pointer entry points copy their inputs to the device, run on the
  *    context's stream, copy the output back and return once it is valid.
- *  - *_dev entry points take device pointers, are ordered on the context's
- *    stream and return without synchronising; kore_cuda_sync() waits and
- *    reports any error raised on the device since the last check.
+ *  - *_dev entry points take device pointers (q, k, v 16-byte aligned, as
+ *    any cudaMalloc'd row of n_head*head_dim floats is), are ordered on the
+ *    context's stream and return without synchronising; kore_cuda_sync()
+ *    waits and reports any error raised on the device since the last check.
  *  - A context is not re-entrant: one host thread at a time (kore calls
  *    attention from its main thread, or from the HTTP handler under the
  *    session mutex, kore.cpp:2600).
@@ -161,6 +162,24 @@ int kore_cuda_attn_decode_batch_dev(kore_cuda_ctx *ctx, int layer, int n_seq, co
 int kore_cuda_attn_decode_partial_dev(kore_cuda_ctx *ctx, int seq, int layer, int pos,
                                       const float *q, const float *k, const float *v, float *part);
 int kore_cuda_lse_merge_dev(kore_cuda_ctx *ctx, int n_parts, const float *parts, float *out);
+
+/*
+ * The same split with the exchange done by this library over NVLink peer
+ * memory instead of by the caller. Each rank exports its exchange buffer
+ * (kore_cuda_peer_handle: a CUDA IPC handle of KORE_CUDA_PEER_HANDLE_BYTES),
+ * the caller passes all ranks' handles, in rank order, to every rank
+ * (kore_cuda_peer_open), and then kore_cuda_attn_decode_sharded_dev runs one
+ * layer's decode step on every rank and leaves the full merged output
+ * [n_head*head_dim] on every rank: the partial, a push of it into every
+ * peer's memory with a flag, a bounded wait (2 s, then KORE_CUDA_EDEVICE from
+ * kore_cuda_sync) for the peers' partials, and the merge. Every rank must make
+ * the same sequence of calls. One process per GPU; shard_count <= 8.
+ */
+#define KORE_CUDA_PEER_HANDLE_BYTES 64
+int kore_cuda_peer_handle(kore_cuda_ctx *ctx, void *handle);
+int kore_cuda_peer_open(kore_cuda_ctx *ctx, const void *handles);
+int kore_cuda_attn_decode_sharded_dev(kore_cuda_ctx *ctx, int seq, int layer, int pos,
+                                      const float *q, const float *k, const float *v, float *out);
 
 /* Copies positions pos0..pos0+n-1 of (seq, layer) back to the host in kore's
  * row layout, k_out/v_out [n][n_head_kv*head_dim] (post-RoPE keys), so that a

@@ -97,6 +97,9 @@ def load_library(path: str = LIB):
         getattr(L, n).argtypes = [_vp, _i, _i, _ip, _ip, _vp, _vp, _vp, _vp]
     L.kore_cuda_attn_decode_partial_dev.argtypes = [_vp, _i, _i, _i, _vp, _vp, _vp, _vp]
     L.kore_cuda_lse_merge_dev.argtypes = [_vp, _i, _vp, _vp]
+    L.kore_cuda_peer_handle.argtypes = [_vp, ctypes.c_char_p]
+    L.kore_cuda_peer_open.argtypes = [_vp, ctypes.c_char_p]
+    L.kore_cuda_attn_decode_sharded_dev.argtypes = [_vp, _i, _i, _i, _vp, _vp, _vp, _vp]
     L.kore_cuda_kv_read.argtypes = [_vp, _i, _i, _i, _i, _vp, _vp]
     L.kore_cuda_attn_decode_noalloc.argtypes = [ctypes.POINTER(KvView), _i, _vp, _vp, _vp, _vp, _vp, _vp]
     L.kore_cuda_sync.argtypes = [_vp]
@@ -257,6 +260,23 @@ class KoreCuda:
 
     def lse_merge_dev(self, n_parts: int, parts, out) -> None:
         self._ck(self._L.kore_cuda_lse_merge_dev(self._h, n_parts, _dptr(parts), _dptr(out)))
+
+    PEER_HANDLE_BYTES = 64
+
+    def peer_handle(self) -> bytes:
+        """This rank's exchange-buffer handle, to be given to every rank's peer_open."""
+        buf = ctypes.create_string_buffer(self.PEER_HANDLE_BYTES)
+        self._ck(self._L.kore_cuda_peer_handle(self._h, buf))
+        return buf.raw
+
+    def peer_open(self, handles: list[bytes]) -> None:
+        blob = b"".join(handles)
+        self._ck(self._L.kore_cuda_peer_open(self._h, ctypes.c_char_p(blob)))
+
+    def decode_sharded_dev(self, seq: int, layer: int, pos: int, q, k, v, out) -> None:
+        """KV-sharded decode with the exchange over peer memory: full output on every rank."""
+        self._ck(self._L.kore_cuda_attn_decode_sharded_dev(self._h, seq, layer, pos, _dptr(q), _dptr(k),
+                                                           _dptr(v), _dptr(out)))
 
     @property
     def part_floats(self) -> int:

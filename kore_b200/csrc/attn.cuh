@@ -52,15 +52,35 @@ struct AppendParams {
     int seq, pos0, n;
 };
 
+constexpr int kMaxRanks = 8;
+
+// One layer's cross-GPU exchange of KV-sharded decode partials (peer_exchange.cu).
+// Exchange buffer of each rank (bytes): slots [2 parities][n_ranks][H*D + H]
+// floats, then at flag_off flags [2][n_ranks][H] u32, then at epoch_off the
+// per-head epochs [H] u32; all zero at creation.
+struct ExchangeParams {
+    const float *local;            // this rank's packed partial [H*D outputs][H lse] (one split)
+    const float *part_o;           // or its splits, merged here when n_splits > 1
+    const float2 *part_ml;         //   (decode split scratch of query 0)
+    int n_splits, max_splits, n_rep;
+    float *own;                    // this rank's exchange buffer
+    float *peers[kMaxRanks];       // every rank's exchange buffer as mapped here (own included)
+    size_t flag_off, epoch_off;
+    float *out;                    // merged output [H*D]
+    int *err;
+    int n_ranks, rank, H, D;
+};
+
 // Launch helpers (attn_decode.cu, kv_append.cu). Return cudaGetLastError().
-// Decode kernel, followed (when grid_x > 1) by the split-merge kernel.
-cudaError_t launch_attn_decode(const DecodeParams &p, int n_rep, int grid_x, cudaStream_t s);
+// Decode kernel, followed (when grid_x > 1 and merge) by the split-merge kernel.
+cudaError_t launch_attn_decode(const DecodeParams &p, int n_rep, int grid_x, cudaStream_t s, bool merge = true);
 int decode_ctas_per_sm(int head_dim, int n_rep);
 int decode_tile_tokens();
 int decode_split_pages_max();
 size_t decode_smem_bytes(int head_dim);
 cudaError_t launch_kv_append(const AppendParams &p, cudaStream_t s);
 void set_ctxless_error(const char *msg);
+cudaError_t launch_peer_exchange(const ExchangeParams &p, cudaStream_t s);
 cudaError_t launch_lse_merge(const float *parts, int n_parts, int H, int D, float *out, cudaStream_t s);
 
 }  // namespace kore

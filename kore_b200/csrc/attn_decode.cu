@@ -44,6 +44,7 @@
 #include "../../include/kore_cuda.h"
 #include "attn.cuh"
 #include "common.cuh"
+#include "split_merge.cuh"
 
 #include <algorithm>
 #include <cstdio>
@@ -63,7 +64,9 @@ struct DecodeSmem {
     static constexpr size_t stage_floats = (size_t)NW * SPW * 2 * TILE_F;
     static constexpr size_t new_floats = 2 * 4 * D;
     static constexpr size_t pbuf_floats = (size_t)NW * TT * 8;
-    static constexpr size_t bar_off = (stage_floats + new_floats + pbuf_floats) * 4;
+    // q of the whole group (up to 8 heads), the RoPE row of pos, new k and v
+    static constexpr size_t qsm_floats = (size_t)11 * D;
+    static constexpr size_t bar_off = (stage_floats + new_floats + pbuf_floats + qsm_floats) * 4;
     static constexpr size_t bytes = bar_off + (size_t)NW * SPW * 8 + kSplitPagesMax * 4;
 };
 
@@ -214,6 +217,7 @@ __global__ void __launch_bounds__(NW * 32, 1) attn_decode_kernel(const __grid_co
     float *newk = stages + SM::stage_floats;
     float *newv = newk + 4 * D;
     float *pbuf_all = newv + 4 * D;
+    float *qsm = pbuf_all + SM::pbuf_floats;   // [R*D q][D: HALF (cos, sin)][D k_new][D v_new]
     uint64_t *full = reinterpret_cast<uint64_t *>(reinterpret_cast<char *>(smem) + SM::bar_off);
     int *pages = reinterpret_cast<int *>(full + NW * SPW);
 
@@ -280,9 +284,11 @@ __global__ void __launch_bounds__(NW * 32, 1) attn_decode_kernel(const __grid_co
         bulk_g2s(dst + SM::TILE_F, src + kv.v_off, bytes, bar, pol);
     };
     // KV of this layer is streamed before waiting for the preceding kernel only
-    // when the host knows that kernel wrote no KV of this layer; every kernel
-    // earlier than that one has completed, because each decode kernel lets its
-    // successor start only after its own wait returned
+    // when the host knows that no kernel still possibly running writes KV of
+    // this layer: a decode kernel lets its successor (a split-merge or
+    // exchange kernel, or the next decode) start only after its own wait
+    // returned, and a split-merge or exchange kernel lets the next decode start
+    // at once, so at most the previous decode and its merge can still run
     if (p.prefetch_ok && lane == 0)
         for (int j = 0; j < SPW && j < my_tiles; ++j) issue(j);
     grid_dep_wait();
@@ -290,17 +296,36 @@ __global__ void __launch_bounds__(NW * 32, 1) attn_decode_kernel(const __grid_co
     if (!p.prefetch_ok && lane == 0)
         for (int j = 0; j < SPW && j < my_tiles; ++j) issue(j);
 
+    // q of the group, the RoPE row and the new token's k/v: loaded once per
+    // CTA with 16-byte loads (every warp of every split reads the same few
+    // lines, so per-warp loads would pile onto a handful of L2 lines)
+    {
+        const float4 *q4 = reinterpret_cast<const float4 *>(p.q + (size_t)qi * p.H * D + (size_t)g * R * D);
+        float4 *d4 = reinterpret_cast<float4 *>(qsm);
+        for (int i = tid; i < R * D / 4; i += NT) d4[i] = __ldg(q4 + i);
+        const float4 *c4 = reinterpret_cast<const float4 *>(p.rope + (size_t)pos * HALF);
+        for (int i = tid; i < D / 4; i += NT) d4[R * D / 4 + i] = __ldg(c4 + i);
+        if (do_new) {
+            const float4 *k4 = reinterpret_cast<const float4 *>(p.k_new + (size_t)qi * kv.G * D + (size_t)g * D);
+            const float4 *v4 = reinterpret_cast<const float4 *>(p.v_new + (size_t)qi * kv.G * D + (size_t)g * D);
+            for (int i = tid; i < D / 4; i += NT) {
+                d4[(R + 1) * D / 4 + i] = __ldg(k4 + i);
+                d4[(R + 2) * D / 4 + i] = __ldg(v4 + i);
+            }
+        }
+    }
+    __syncthreads();
+    const float2 *cs = reinterpret_cast<const float2 *>(qsm + R * D);
+
     WarpState<D, R> st;
-    const float2 *cs = p.rope + (size_t)pos * HALF;
-    const float *qsrc = p.q + (size_t)qi * p.H * D + (size_t)g * R * D;
 #pragma unroll
     for (int h = 0; h < R; ++h)
 #pragma unroll
         for (int j = 0; j < VEC; ++j) {
             const int i = lane * VEC + j;
-            const float x = __ldg(qsrc + h * D + i);
-            const float y = __ldg(qsrc + h * D + (i ^ HALF));
-            const float2 a = __ldg(cs + (i & (HALF - 1)));
+            const float x = qsm[h * D + i];
+            const float y = qsm[h * D + (i ^ HALF)];
+            const float2 a = cs[i & (HALF - 1)];
             const float r = i < HALF ? rope_lo(x, y, a.x, a.y) : rope_hi(y, x, a.x, a.y);
             st.q[h][j] = r * p.scale_log2;
             st.o[h][j] = 0.f;
@@ -313,8 +338,8 @@ __global__ void __launch_bounds__(NW * 32, 1) attn_decode_kernel(const __grid_co
 
     if (do_new && warp == 0) {
         // the token at pos: rotate k, stage k/v as a 1-token tile, append to the cache
-        const float *ks = p.k_new + (size_t)qi * kv.G * D + (size_t)g * D;
-        const float *vs = p.v_new + (size_t)qi * kv.G * D + (size_t)g * D;
+        const float *ks = qsm + (R + 1) * D;
+        const float *vs = qsm + (R + 2) * D;
         const int lp = (pos / P) / NS, off = pos % P;
         const int ph = pt[lp];
         const bool ok = ph >= 0 && ph < kv.n_pages;
@@ -323,10 +348,10 @@ __global__ void __launch_bounds__(NW * 32, 1) attn_decode_kernel(const __grid_co
 #pragma unroll
         for (int j = 0; j < VEC; ++j) {
             const int i = lane * VEC + j;
-            const float x = __ldg(ks + i), y = __ldg(ks + (i ^ HALF));
-            const float2 a = __ldg(cs + (i & (HALF - 1)));
+            const float x = ks[i], y = ks[i ^ HALF];
+            const float2 a = cs[i & (HALF - 1)];
             const float kr = i < HALF ? rope_lo(x, y, a.x, a.y) : rope_hi(y, x, a.x, a.y);
-            const float vr = __ldg(vs + i);
+            const float vr = vs[i];
             newk[i] = kr;
             newv[i] = vr;
             if (ok) {
@@ -401,12 +426,12 @@ __global__ void __launch_bounds__(NW * 32, 1) attn_decode_kernel(const __grid_co
 // after the decode kernel with a programmatic dependency; waits for it first.
 template <int D, int R>
 __global__ void __launch_bounds__(D) split_merge_kernel(const __grid_constant__ DecodeParams p) {
-    constexpr int CH = 64;   // partial values in flight per thread
-    __shared__ float w[kMaxSplits];
-    __shared__ float red[D / 32];
-    __shared__ float s_M, s_L;
-    grid_dep_wait();
+    // the next decode may start as soon as this kernel is resident: it only
+    // prefetches KV of a layer that neither this kernel nor the decode before
+    // it writes (checked on the host), and waits for this kernel before
+    // anything else
     grid_dep_launch();
+    grid_dep_wait();
     const int h = blockIdx.x % R, g = blockIdx.x / R, qi = blockIdx.y, tid = threadIdx.x;
     const int pos = p.contiguous ? p.pos0 + qi : p.pos[qi];
     const PagedKv &kv = p.kv;
@@ -418,63 +443,12 @@ __global__ void __launch_bounds__(D) split_merge_kernel(const __grid_constant__ 
     const int n_splits = (count + p.split_tokens - 1) / p.split_tokens;
     if (n_splits <= 1) return;   // the decode kernel wrote this output directly
     const size_t base = ((size_t)qi * kv.G + g) * p.max_splits;
-    const float *po = p.part_o + base * R * D + (size_t)h * D + tid;
-
-    float v[CH];
-#pragma unroll
-    for (int s = 0; s < CH; ++s) v[s] = s < n_splits ? __ldcg(po + (size_t)s * R * D) : 0.f;
-    // split weights: block max of the split maxima, then 2^(m_s - M)
-    float M = -INFINITY;
-    for (int s = tid; s < n_splits; s += D) M = fmaxf(M, __ldcg(&p.part_ml[(base + s) * R + h]).x);
-#pragma unroll
-    for (int off = 16; off > 0; off >>= 1) M = fmaxf(M, __shfl_xor_sync(FULL, M, off));
-    if ((tid & 31) == 0) red[tid >> 5] = M;
-    __syncthreads();
-    if (tid == 0) {
-        float m = red[0];
-        for (int i = 1; i < D / 32; ++i) m = fmaxf(m, red[i]);
-        s_M = m;
-    }
-    __syncthreads();
-    M = s_M;
-    float L = 0.f;
-    for (int s = tid; s < n_splits; s += D) {
-        const float2 ml = __ldcg(&p.part_ml[(base + s) * R + h]);
-        const float ws = M == -INFINITY ? 0.f : fast_exp2(ml.x - M);
-        w[s] = ws;
-        L = fmaf(ml.y, ws, L);
-    }
-#pragma unroll
-    for (int off = 16; off > 0; off >>= 1) L += __shfl_xor_sync(FULL, L, off);
-    __syncthreads();
-    if ((tid & 31) == 0) red[tid >> 5] = L;
-    __syncthreads();
-    if (tid == 0) {
-        float l = 0.f;
-        for (int i = 0; i < D / 32; ++i) l += red[i];
-        s_L = l;
-    }
-    __syncthreads();
-    L = s_L;
-    float a0 = 0.f, a1 = 0.f, a2 = 0.f, a3 = 0.f;
-#pragma unroll
-    for (int s = 0; s < CH; s += 4) {
-        if (s < n_splits) a0 = fmaf(w[s], v[s], a0);
-        if (s + 1 < n_splits) a1 = fmaf(w[s + 1], v[s + 1], a1);
-        if (s + 2 < n_splits) a2 = fmaf(w[s + 2], v[s + 2], a2);
-        if (s + 3 < n_splits) a3 = fmaf(w[s + 3], v[s + 3], a3);
-    }
-    for (int c0 = CH; c0 < n_splits; c0 += CH) {
-#pragma unroll
-        for (int s = 0; s < CH; ++s) v[s] = c0 + s < n_splits ? __ldcg(po + (size_t)(c0 + s) * R * D) : 0.f;
-#pragma unroll
-        for (int s = 0; s < CH; ++s)
-            if (c0 + s < n_splits) a0 = fmaf(w[c0 + s], v[s], a0);
-    }
-    const float acc = (a0 + a1) + (a2 + a3);
+    float o, lse;
+    merge_head_splits<D>(p.part_o + base * R * D + (size_t)h * D + tid, (size_t)R * D, p.part_ml + base * R + h,
+                         (size_t)R, n_splits, o, lse);
     const size_t qh = (size_t)qi * p.H + (size_t)g * R + h;
-    p.out[qh * D + tid] = L > 0.f ? acc / L : 0.f;
-    if (p.lse && tid == 0) p.lse[qh] = L > 0.f ? M + __log2f(L) : -INFINITY;
+    p.out[qh * D + tid] = o;
+    if (p.lse && tid == 0) p.lse[qh] = lse;
 }
 
 #ifndef KORE_DECODE_NW
@@ -495,7 +469,7 @@ static_assert(DecodeSmem<64, kNW, kTT, kSPW>::stage_floats >= (size_t)kMaxSplits
               "split merge needs room for the weights and one staged partial");
 
 template <int D, int R>
-cudaError_t launch_dr(const DecodeParams &p, int grid_x, cudaStream_t s) {
+cudaError_t launch_dr(const DecodeParams &p, int grid_x, cudaStream_t s, bool merge) {
     using SM = DecodeSmem<D, kNW, kTT, kSPW>;
     auto kern = attn_decode_kernel<D, R, kNW, kTT, kSPW>;
     static bool configured[64] = {};
@@ -517,7 +491,7 @@ cudaError_t launch_dr(const DecodeParams &p, int grid_x, cudaStream_t s) {
     cfg.attrs = attr;
     cfg.numAttrs = 1;
     cudaError_t e = cudaLaunchKernelEx(&cfg, kern, p);
-    if (e != cudaSuccess || grid_x == 1) return e;
+    if (e != cudaSuccess || grid_x == 1 || !merge) return e;
     cudaLaunchConfig_t mcfg = cfg;
     mcfg.gridDim = dim3(p.kv.G * R, p.n_q);
     mcfg.blockDim = dim3(D);
@@ -526,25 +500,25 @@ cudaError_t launch_dr(const DecodeParams &p, int grid_x, cudaStream_t s) {
 }
 
 template <int D>
-cudaError_t launch_d(const DecodeParams &p, int n_rep, int grid_x, cudaStream_t s) {
+cudaError_t launch_d(const DecodeParams &p, int n_rep, int grid_x, cudaStream_t s, bool merge) {
     switch (n_rep) {
-        case 1: return launch_dr<D, 1>(p, grid_x, s);
-        case 2: return launch_dr<D, 2>(p, grid_x, s);
-        case 3: return launch_dr<D, 3>(p, grid_x, s);
-        case 4: return launch_dr<D, 4>(p, grid_x, s);
-        case 5: return launch_dr<D, 5>(p, grid_x, s);
-        case 6: return launch_dr<D, 6>(p, grid_x, s);
-        case 7: return launch_dr<D, 7>(p, grid_x, s);
-        case 8: return launch_dr<D, 8>(p, grid_x, s);
+        case 1: return launch_dr<D, 1>(p, grid_x, s, merge);
+        case 2: return launch_dr<D, 2>(p, grid_x, s, merge);
+        case 3: return launch_dr<D, 3>(p, grid_x, s, merge);
+        case 4: return launch_dr<D, 4>(p, grid_x, s, merge);
+        case 5: return launch_dr<D, 5>(p, grid_x, s, merge);
+        case 6: return launch_dr<D, 6>(p, grid_x, s, merge);
+        case 7: return launch_dr<D, 7>(p, grid_x, s, merge);
+        case 8: return launch_dr<D, 8>(p, grid_x, s, merge);
         default: return cudaErrorInvalidValue;
     }
 }
 
 }  // namespace
 
-cudaError_t launch_attn_decode(const DecodeParams &p, int n_rep, int grid_x, cudaStream_t s) {
-    if (p.kv.D == 128) return launch_d<128>(p, n_rep, grid_x, s);
-    if (p.kv.D == 64) return launch_d<64>(p, n_rep, grid_x, s);
+cudaError_t launch_attn_decode(const DecodeParams &p, int n_rep, int grid_x, cudaStream_t s, bool merge) {
+    if (p.kv.D == 128) return launch_d<128>(p, n_rep, grid_x, s, merge);
+    if (p.kv.D == 64) return launch_d<64>(p, n_rep, grid_x, s, merge);
     return cudaErrorInvalidValue;
 }
 
@@ -605,6 +579,9 @@ extern "C" int kore_cuda_attn_decode_noalloc(const kore_cuda_kv_view *kv, int po
         return noalloc_fail(KORE_CUDA_EINVAL, "page_tokens %lld must be a positive multiple of 64", P);
     if ((reinterpret_cast<uintptr_t>(kv->k_pages) | reinterpret_cast<uintptr_t>(kv->v_pages)) & 15)
         return noalloc_fail(KORE_CUDA_EINVAL, "page pools must be 16-byte aligned");
+    if ((reinterpret_cast<uintptr_t>(q) | reinterpret_cast<uintptr_t>(k) | reinterpret_cast<uintptr_t>(v) |
+         reinterpret_cast<uintptr_t>(kv->rope_cs)) & 15)
+        return noalloc_fail(KORE_CUDA_EINVAL, "q, k, v and rope_cs must be 16-byte aligned");
     if (pos < 0 || pos >= kv->n_rope || pos / P >= kv->n_table)
         return noalloc_fail(KORE_CUDA_ERANGE, "position %lld outside the RoPE table or the page table", pos);
 

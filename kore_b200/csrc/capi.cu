@@ -48,6 +48,11 @@ struct kore_cuda_ctx {
     size_t host_stage_floats = 0;
     int *host_err = nullptr;
     int last_kv_layer = -1;     // layer whose KV the most recent kernel of this context wrote
+    // cross-GPU exchange of KV-sharded partials (peer_exchange.cu)
+    float *xbuf = nullptr;      // this rank's exchange buffer, shared with the peers over CUDA IPC
+    size_t x_flag_off = 0, x_epoch_off = 0, x_local_off = 0, x_bytes = 0;
+    float *peers[kMaxRanks] = {};
+    bool peers_open = false;
     std::string msg;
 };
 
@@ -219,11 +224,13 @@ int run_append(kore_cuda_ctx *c, int seq, int layer, int pos0, int n, const floa
 // (seq0, pos0 + i); otherwise seqs[i], poss[i] (host arrays, n_q <= kMaxBatch).
 int run_decode(kore_cuda_ctx *c, int layer, int n_q, bool contiguous, int seq0, int pos0, const int *seqs,
                const int *poss, const float *q, const float *k, const float *v, float *out, float *lse,
-               bool append_new) {
+               bool append_new, bool launch_merge = true, int *grid_out = nullptr) {
     if (n_q <= 0) return fail(c, KORE_CUDA_EINVAL, "no queries");
     if (!contiguous && n_q > kMaxBatch)
         return fail(c, KORE_CUDA_EINVAL, "decode batch of %d exceeds %d sequences per call", n_q, kMaxBatch);
     if (n_q > 65535) return fail(c, KORE_CUDA_EINVAL, "%d queries exceed one launch", n_q);
+    if ((reinterpret_cast<uintptr_t>(q) | reinterpret_cast<uintptr_t>(k) | reinterpret_cast<uintptr_t>(v)) & 15)
+        return fail(c, KORE_CUDA_EINVAL, "q, k and v must be 16-byte aligned device buffers");
     DecodeParams p;
     memset(&p, 0, sizeof p);
     p.kv = layer_kv(c, layer);
@@ -284,10 +291,11 @@ int run_decode(kore_cuda_ctx *c, int layer, int n_q, bool contiguous, int seq0, 
     p.split_tokens = (int)st;
     p.max_splits = grid_x;
     p.prefetch_ok = c->last_kv_layer != layer;
-    CK(launch_attn_decode(p, c->R, grid_x, c->stream));
-    // with more than one split the last kernel launched is the split merge,
-    // which writes no KV and starts its successor only once the decode is done
-    c->last_kv_layer = (append_new && grid_x == 1) ? layer : -1;
+    CK(launch_attn_decode(p, c->R, grid_x, c->stream, launch_merge));
+    if (grid_out) *grid_out = grid_x;
+    // the decode (and its split merge, which lets the next kernel start at
+    // once) may still run when the next kernel starts: it wrote this layer's KV
+    c->last_kv_layer = append_new ? layer : -1;
     return KORE_CUDA_OK;
 }
 
@@ -315,6 +323,9 @@ void kore_cuda_destroy(kore_cuda_ctx *c) {
     {
         DeviceGuard dg(c->cfg.device);
         if (c->stream) cudaStreamSynchronize(c->stream);
+        for (int r = 0; r < kMaxRanks; ++r)
+            if (c->peers[r] && c->peers[r] != c->xbuf) cudaIpcCloseMemHandle(c->peers[r]);
+        cudaFree(c->xbuf);
         cudaFree(c->kv);
         cudaFree(c->pt_d);
         cudaFree(c->rope_d);
@@ -546,6 +557,87 @@ int kore_cuda_lse_merge_dev(kore_cuda_ctx *c, int n_parts, const float *parts, f
     if (!parts || !out || n_parts <= 0) return fail(c, KORE_CUDA_EINVAL, "bad merge arguments");
     DeviceGuard dg(c->cfg.device);
     CK(launch_lse_merge(parts, n_parts, c->H, c->D, out, c->stream));
+    return KORE_CUDA_OK;
+}
+
+static size_t align256(size_t b) { return (b + 255) / 256 * 256; }
+
+int kore_cuda_peer_handle(kore_cuda_ctx *c, void *handle) {
+    if (!c || !handle) return KORE_CUDA_EINVAL;
+    if (c->NS < 2 || c->NS > kMaxRanks)
+        return fail(c, KORE_CUDA_EINVAL, "peer exchange needs 2..%d shards (context has %d)", kMaxRanks, c->NS);
+    DeviceGuard dg(c->cfg.device);
+    if (!c->xbuf) {
+        const size_t PF = (size_t)c->H * c->D + c->H;
+        c->x_flag_off = align256(2 * (size_t)c->NS * PF * sizeof(float));
+        c->x_epoch_off = c->x_flag_off + align256(2 * (size_t)c->NS * c->H * sizeof(unsigned));
+        c->x_local_off = c->x_epoch_off + align256((size_t)c->H * sizeof(unsigned));
+        c->x_bytes = c->x_local_off + align256(PF * sizeof(float));
+        CK(cudaMalloc(&c->xbuf, c->x_bytes));
+        CK(cudaMemset(c->xbuf, 0, c->x_bytes));
+        CK(cudaDeviceSynchronize());
+    }
+    cudaIpcMemHandle_t h;
+    CK(cudaIpcGetMemHandle(&h, c->xbuf));
+    static_assert(sizeof(h) == KORE_CUDA_PEER_HANDLE_BYTES, "IPC handle size");
+    memcpy(handle, &h, sizeof h);
+    return KORE_CUDA_OK;
+}
+
+int kore_cuda_peer_open(kore_cuda_ctx *c, const void *handles) {
+    if (!c || !handles) return KORE_CUDA_EINVAL;
+    if (!c->xbuf) return fail(c, KORE_CUDA_ESTATE, "call kore_cuda_peer_handle first");
+    DeviceGuard dg(c->cfg.device);
+    for (int r = 0; r < c->NS; ++r) {
+        if (r == c->rank) {
+            c->peers[r] = c->xbuf;
+            continue;
+        }
+        if (c->peers[r]) continue;
+        cudaIpcMemHandle_t h;
+        memcpy(&h, static_cast<const char *>(handles) + (size_t)r * KORE_CUDA_PEER_HANDLE_BYTES, sizeof h);
+        void *ptr = nullptr;
+        CK(cudaIpcOpenMemHandle(&ptr, h, cudaIpcMemLazyEnablePeerAccess));
+        c->peers[r] = static_cast<float *>(ptr);
+    }
+    c->peers_open = true;
+    return KORE_CUDA_OK;
+}
+
+int kore_cuda_attn_decode_sharded_dev(kore_cuda_ctx *c, int seq, int layer, int pos, const float *q, const float *k,
+                                      const float *v, float *out) {
+    if (!c) return KORE_CUDA_EINVAL;
+    if (!q || !k || !v || !out) return fail(c, KORE_CUDA_EINVAL, "null q, k, v or out");
+    if (!c->peers_open) return fail(c, KORE_CUDA_ESTATE, "peer exchange not set up (kore_cuda_peer_open)");
+    if (int rc = check_range(c, seq, layer, pos, 1)) return rc;
+    DeviceGuard dg(c->cfg.device);
+    if (int rc = ensure_pages(c, seq, pos + 1)) return rc;
+    float *local = reinterpret_cast<float *>(reinterpret_cast<char *>(c->xbuf) + c->x_local_off);
+    int n_splits = 1;   // the splits are merged by the exchange kernel itself
+    if (int rc = run_decode(c, layer, 1, true, seq, pos, nullptr, nullptr, q, k, v, local,
+                            local + (size_t)c->H * c->D, true, false, &n_splits))
+        return rc;
+    note_len(c, seq, layer, pos + 1);
+    ExchangeParams xp;
+    memset(&xp, 0, sizeof xp);
+    xp.local = local;
+    xp.part_o = c->part_o;
+    xp.part_ml = c->part_ml;
+    xp.n_splits = n_splits;
+    xp.max_splits = n_splits;
+    xp.n_rep = c->R;
+    xp.own = c->xbuf;
+    for (int r = 0; r < c->NS; ++r) xp.peers[r] = c->peers[r];
+    xp.flag_off = c->x_flag_off;
+    xp.epoch_off = c->x_epoch_off;
+    xp.out = out;
+    xp.err = c->err_d;
+    xp.n_ranks = c->NS;
+    xp.rank = c->rank;
+    xp.H = c->H;
+    xp.D = c->D;
+    CK(launch_peer_exchange(xp, c->stream));
+    c->last_kv_layer = layer;   // the decode may still run when the next kernel starts
     return KORE_CUDA_OK;
 }
 

@@ -13,6 +13,7 @@ enum DeviceError : int {
     DEV_WAIT_FULL_TIMEOUT = 1,    // consumer waited too long for a tile copy
     DEV_WAIT_EMPTY_TIMEOUT = 2,   // producer waited too long for a free stage
     DEV_BAD_PAGE = 3,             // page table entry outside the pool
+    DEV_PEER_TIMEOUT = 4,         // a peer GPU's partial did not arrive in time
 };
 
 __device__ __forceinline__ void raise_error(int *err, int code) {
