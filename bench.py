@@ -60,6 +60,10 @@ def parse():
     ap.add_argument("--e2e-steps", type=int, default=100)
     ap.add_argument("--layers", type=int, default=28, help="fewer layers: a small case for ncu captures")
     ap.add_argument("--pos", type=int, default=32768, help="decode position (cached rows per layer)")
+    ap.add_argument("--prefill-steps", type=int, default=5)
+    ap.add_argument("--prefill-layers", type=int, default=28)
+    ap.add_argument("--no-prefill", action="store_true")
+    ap.add_argument("--prefill-only", action="store_true", help="measure only the prefill (development)")
     a = ap.parse_args()
     global L, POS, CTX
     L, POS, CTX = a.layers, a.pos, a.pos + 1
@@ -294,7 +298,71 @@ def run_ours(args, rank: int, world: int, dist) -> dict | None:
     }
     if not args.no_cpu_baseline and world == 1:
         line["cpu_baseline"] = cpu_baseline_sample()
+    if not args.no_prefill and world == 1:
+        line["prefill"] = run_prefill(args, torch.device("cuda", 0), peaks)
     return line
+
+
+def prefill_pairs(pos0: int, n: int) -> int:
+    """Unmasked (query, key) pairs of a causal chunk: sum over z of pos0 + z + 1."""
+    return n * (pos0 + 1) + n * (n - 1) // 2
+
+
+def run_prefill(args, dev, peaks) -> dict:
+    """Config 3: a 2048-token chunk appended onto 4096 cached rows, 28 layers,
+    7B shape; one step = the chunk through every layer (append, operand
+    split, tensor-core attention), re-run at the same positions each step."""
+    import torch
+    import kore_b200 as K
+    P0, N, LP = 4096, 2048, args.prefill_layers
+    ctx = K.KoreCuda(LP, H, G, D, P0 + N, device=dev.index)
+    stream = torch.cuda.Stream(device=dev)
+    ctx.set_stream(stream.cuda_stream)
+    gen = torch.Generator(device=dev)
+    with torch.cuda.stream(stream):
+        for layer in range(LP):
+            gen.manual_seed(2000 + layer)
+            k = torch.randn(P0, KVD, device=dev, generator=gen)
+            v = torch.randn(P0, KVD, device=dev, generator=gen)
+            ctx.append_dev(0, layer, 0, P0, k, v)
+        gen.manual_seed(9)
+        q = torch.randn(LP, N, H * D, device=dev, generator=gen)
+        kc = torch.randn(LP, N, KVD, device=dev, generator=gen)
+        vc = torch.randn(LP, N, KVD, device=dev, generator=gen)
+        out = torch.empty(LP, N, H * D, device=dev)
+    ctx.sync()
+
+    def step():
+        for layer in range(LP):
+            ctx.prefill_dev(0, layer, P0, N, q[layer], kc[layer], vc[layer], out[layer])
+
+    with torch.cuda.stream(stream):
+        for _ in range(2):
+            step()
+    ctx.sync()
+    steps = args.prefill_steps
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    with torch.cuda.stream(stream):
+        e0.record(stream)
+        for _ in range(steps):
+            step()
+        e1.record(stream)
+    e1.synchronize()
+    ctx.sync()
+    ms = e0.elapsed_time(e1) / steps
+    flops = 4 * D * prefill_pairs(P0, N) * H * LP
+    tflops = flops / (ms * 1e-3) / 1e12
+    ctx.close()
+    # the tensor pipe runs three bf16 MMAs per fp32-accurate product
+    peak_eq = peaks["bf16_tflops"] / 3
+    return {"metric": "prefill attn TFLOP/s (7B, 2048-token chunk onto 4096, 28 layers)",
+            "value": round(tflops, 1), "unit": "TFLOP/s", "ms_per_step": round(ms, 4), "steps": steps,
+            "layers": LP, "flop_per_step": flops,
+            "roofline": {"bound": "tensor", "achieved": round(tflops, 1), "peak": round(peak_eq, 1),
+                         "unit": "TFLOP/s", "frac": round(tflops / peak_eq, 4), "peak_source": peaks["source"],
+                         "peak_note": "measured bf16 dense peak / 3: each fp32-accurate product is three bf16 "
+                                      "MMAs (hi*hi + hi*mid + mid*hi)"},
+            "kernels": "kv_append_kernel + kv_split_kernel + prefill_kernel (tcgen05, TMEM)"}
 
 
 def load_peaks() -> dict:
@@ -427,6 +495,10 @@ def main():
         torch.cuda.set_device(int(os.environ.get("LOCAL_RANK", 0)))
         dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120),
                                 device_id=torch.device("cuda", int(os.environ.get("LOCAL_RANK", 0))))
+    if args.prefill_only:
+        import torch
+        print(json.dumps(run_prefill(args, torch.device("cuda", 0), load_peaks())), flush=True)
+        return
     try:
         line = run_ours(args, rank, world, dist)
         if line is not None:

@@ -54,6 +54,19 @@ struct AppendParams {
 
 constexpr int kMaxRanks = 8;
 
+// One prefill chunk of one layer (attn_prefill.cu).
+struct PrefillParams {
+    PagedKv kv;                // the layer (unsharded)
+    void *split;               // K/V operand tiles: [G][tiles][tile bytes]
+    int tiles;                 // capacity of `split` per KV head, in 64-key tiles
+    const float *q;            // [n][H*D] pre-RoPE
+    float *out;                // [n][H*D]
+    const float2 *rope;
+    int *err;
+    float scale_log2;
+    int seq, pos0, n, H, n_rep;
+};
+
 // One layer's cross-GPU exchange of KV-sharded decode partials (peer_exchange.cu).
 // Exchange buffer of each rank (bytes): slots [2 parities][n_ranks][H*D + H]
 // floats, then at flag_off flags [2][n_ranks][H] u32, then at epoch_off the
@@ -80,6 +93,9 @@ int decode_split_pages_max();
 size_t decode_smem_bytes(int head_dim);
 cudaError_t launch_kv_append(const AppendParams &p, cudaStream_t s);
 void set_ctxless_error(const char *msg);
+size_t prefill_tile_bytes(int head_dim);
+int prefill_tile_keys();
+cudaError_t launch_prefill(const PrefillParams &p, cudaStream_t s);
 cudaError_t launch_peer_exchange(const ExchangeParams &p, cudaStream_t s);
 cudaError_t launch_lse_merge(const float *parts, int n_parts, int H, int D, float *out, cudaStream_t s);
 

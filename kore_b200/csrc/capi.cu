@@ -53,6 +53,9 @@ struct kore_cuda_ctx {
     size_t x_flag_off = 0, x_epoch_off = 0, x_local_off = 0, x_bytes = 0;
     float *peers[kMaxRanks] = {};
     bool peers_open = false;
+    // prefill: K/V operand tiles of the current chunk's layer (attn_prefill.cu)
+    void *split = nullptr;
+    int split_tiles = 0;        // capacity per KV head, in tiles of prefill_tile_keys() positions
     std::string msg;
 };
 
@@ -326,6 +329,7 @@ void kore_cuda_destroy(kore_cuda_ctx *c) {
         for (int r = 0; r < kMaxRanks; ++r)
             if (c->peers[r] && c->peers[r] != c->xbuf) cudaIpcCloseMemHandle(c->peers[r]);
         cudaFree(c->xbuf);
+        cudaFree(c->split);
         cudaFree(c->kv);
         cudaFree(c->pt_d);
         cudaFree(c->rope_d);
@@ -485,7 +489,32 @@ int kore_cuda_attn_prefill_dev(kore_cuda_ctx *c, int seq, int layer, int pos0, i
     if (int rc = ensure_pages(c, seq, pos0 + n)) return rc;
     if (int rc = run_append(c, seq, layer, pos0, n, k, v)) return rc;
     note_len(c, seq, layer, pos0 + n);
-    return run_decode(c, layer, n, true, seq, pos0, nullptr, nullptr, q, nullptr, nullptr, out, nullptr, false);
+    if ((reinterpret_cast<uintptr_t>(q) | reinterpret_cast<uintptr_t>(out)) & 15)
+        return fail(c, KORE_CUDA_EINVAL, "q and out must be 16-byte aligned device buffers");
+    const int tk = prefill_tile_keys();
+    if (!c->split) {   // operand tiles for a whole context, allocated on the first prefill
+        const int tiles = (c->cfg.ctx_max + tk - 1) / tk;
+        CK(cudaMalloc(&c->split, (size_t)c->G * tiles * prefill_tile_bytes(c->D)));
+        c->split_tiles = tiles;
+    }
+    PrefillParams pp;
+    memset(&pp, 0, sizeof pp);
+    pp.kv = layer_kv(c, layer);
+    pp.split = c->split;
+    pp.tiles = c->split_tiles;
+    pp.q = q;
+    pp.out = out;
+    pp.rope = c->rope_d;
+    pp.err = c->err_d;
+    pp.scale_log2 = (1.0f / std::sqrt((float)c->D)) * 1.4426950408889634f;
+    pp.seq = seq;
+    pp.pos0 = pos0;
+    pp.n = n;
+    pp.H = c->H;
+    pp.n_rep = c->R;
+    CK(launch_prefill(pp, c->stream));
+    c->last_kv_layer = -1;   // the prefill kernels write no KV and end before their successor starts
+    return KORE_CUDA_OK;
 }
 
 int kore_cuda_attn_prefill(kore_cuda_ctx *c, int seq, int layer, int pos0, int n, const float *q, const float *k,

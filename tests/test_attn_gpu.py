@@ -233,3 +233,21 @@ def test_kv_sharded_decode_partials_merge_to_the_full_result(n_shards, pos):
         assert not kr[~owned].any()
         rows[owned] = kr[owned]
     np.testing.assert_array_equal(rows, o.kc[:pos + 1])
+
+
+def test_cfg3_7b_prefill_2048_onto_4096_sampled_rows():
+    """Config 3 shape: a 2048-token chunk appended onto 4096 cached rows. Row z
+    of a prefill equals a decode at position 4096+z over the same cache, so the
+    oracle checks a sample of rows (tile edges included) by its decode."""
+    H, G, d = 28, 4, 128
+    pos0, n = 4096, 2048
+    g = make_ctx(H, G, d, pos0 + n)
+    o = O.OracleLayer(H, G, d, pos0 + n)
+    fill_both(g, o, 0, 0, pos0, 3000)
+    q, k, v = normal(3001, (n, H * d), (n, G * d), (n, G * d))
+    out = g.prefill(0, 0, pos0, q, k, v)
+    o.fill(pos0, k, v)
+    for z in (0, 1, 63, 64, 127, 128, 129, 1000, 1023, 1024, 1535, 2046, 2047):
+        assert_attn_close(out[z], o.decode(pos0 + z, q[z], k[z], v[z]), f"prefill row {z}")
+    kr, vr = g.kv_read(0, 0, pos0, n)
+    np.testing.assert_array_equal(kr, o.kc[pos0:pos0 + n])
