@@ -29,8 +29,9 @@
 //                 (O in tensor memory is rescaled only when a score exceeds
 //                 the reference by 2^8), P split into the P operand.
 //                 Epilogue: O / l to global memory.
-//     warp 4      producer: one 64 KB tile (K hi/mid, V^T hi/mid) per stage,
-//                 two stages, bulk copies completing on mbarriers.
+//     warps 4, 6  producers: K hi/mid and V^T hi/mid of a tile in separate
+//                 two-stage rings (a K stage frees as soon as its S is done),
+//                 bulk copies completing on mbarriers.
 //     warp 5      allocates tensor memory; one lane issues the MMAs:
 //                 S[j%2] = Q K_j^T (128 x 64), then O += P_j V_j (128 x d),
 //                 issuing S for tile j+1 before O for tile j so that the
@@ -81,11 +82,12 @@ struct PrefillSmem {
     static constexpr uint32_t Q_PART = (uint32_t)QATOMS * kRows * 128;   // one of hi/mid
     static constexpr uint32_t K_PART = (uint32_t)QATOMS * kKeys * 128;
     static constexpr uint32_t V_PART = (uint32_t)D * 128;                // V^T: d rows x 64 keys
-    static constexpr uint32_t TILE = 2 * K_PART + 2 * V_PART;            // one stage / one global tile
+    static constexpr uint32_t TILE = 2 * K_PART + 2 * V_PART;            // one global tile: K half, V half
     static constexpr uint32_t P_PART = (uint32_t)kRows * 128;
     static constexpr uint32_t q_off = 0;
-    static constexpr uint32_t kv_off = 2 * Q_PART;
-    static constexpr uint32_t p_off = kv_off + kStages * TILE;
+    static constexpr uint32_t k_off = 2 * Q_PART;                         // K ring: kStages x (hi, mid)
+    static constexpr uint32_t v_off = k_off + kStages * 2 * K_PART;       // V ring: kStages x (hi, mid)
+    static constexpr uint32_t p_off = v_off + kStages * 2 * V_PART;
     static constexpr uint32_t bar_off = p_off + 2 * P_PART;
     static constexpr uint32_t bytes = bar_off + 256 + 1024;   // barriers, TMEM base, alignment slack
     static constexpr uint32_t TMEM_COLS = D == 128 ? 256 : 256; // S0, S1 (64 each) and O (d)
@@ -219,23 +221,25 @@ __global__ void __launch_bounds__(256) kv_split_kernel(const __grid_constant__ P
 // ---------------------------------------------------------------- attention
 
 template <int D>
-__global__ void __launch_bounds__(192, 1) prefill_kernel(const __grid_constant__ PrefillParams p) {
+__global__ void __launch_bounds__(224, 1) prefill_kernel(const __grid_constant__ PrefillParams p) {
     using SM = PrefillSmem<D>;
     constexpr int HALF = D / 2;
     extern __shared__ uint8_t smem_raw[];
     uint8_t *smem = reinterpret_cast<uint8_t *>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~(uintptr_t)1023);
     const uint32_t sbase = smem_u32(smem);
     uint64_t *bars = reinterpret_cast<uint64_t *>(smem + SM::bar_off);
-    uint64_t *kv_full = bars;              // [2] producer -> MMA
-    uint64_t *kv_empty = bars + 2;         // [2] MMA commit -> producer
+    uint64_t *k_full = bars;               // [2] K producer -> MMA
+    uint64_t *k_empty = bars + 2;          // [2] MMA commit (after S) -> K producer
     uint64_t *s_full = bars + 4;           // [2] MMA commit -> softmax
     uint64_t *s_empty = bars + 6;          // [2] softmax (4 warps) -> MMA
     uint64_t *p_full = bars + 8;           // softmax (4 warps) -> MMA
     uint64_t *pv_done = bars + 9;          // MMA commit -> softmax
     uint64_t *q_ready = bars + 10;         // softmax (4 warps) -> MMA
     uint64_t *mma_drained = bars + 11;     // MMA commit -> MMA issuer, before TMEM is freed
-    uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(bars + 12);
-    int *abort_flag = reinterpret_cast<int *>(bars + 13);
+    uint64_t *v_full = bars + 12;          // [2] V producer -> MMA
+    uint64_t *v_empty = bars + 14;         // [2] MMA commit (after O) -> V producer
+    uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(bars + 16);
+    int *abort_flag = reinterpret_cast<int *>(bars + 17);
 
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int qt = gridDim.x - 1 - blockIdx.x;   // heaviest (last) query tiles first
@@ -249,8 +253,10 @@ __global__ void __launch_bounds__(192, 1) prefill_kernel(const __grid_constant__
 
     if (threadIdx.x == 0) {
         for (int i = 0; i < 2; ++i) {
-            mbar_init(&kv_full[i], 1);
-            mbar_init(&kv_empty[i], 1);
+            mbar_init(&k_full[i], 1);
+            mbar_init(&k_empty[i], 1);
+            mbar_init(&v_full[i], 1);
+            mbar_init(&v_empty[i], 1);
             mbar_init(&s_full[i], 1);
             mbar_init(&s_empty[i], 4);
         }
@@ -271,8 +277,7 @@ __global__ void __launch_bounds__(192, 1) prefill_kernel(const __grid_constant__
     __syncthreads();
     tc_fence_after();
     const uint32_t tmem = *tmem_slot;
-    const uint32_t t_s[2] = {tmem, tmem + 64};
-    const uint32_t t_o = tmem + 128;
+    const uint32_t t_o = tmem + 128;   // S buffer b at tmem + 64 * b
 
     auto bounded_wait = [&](uint64_t *bar, uint32_t parity) -> bool {
         if (*reinterpret_cast<volatile int *>(abort_flag)) return false;
@@ -281,19 +286,28 @@ __global__ void __launch_bounds__(192, 1) prefill_kernel(const __grid_constant__
         return false;
     };
 
-    if (warp == 4) {
-        // ------------------------------------------------------------ producer
+    if (warp == 4 || warp == 6) {
+        // ------------------------------------------------------------ producers
+        // warp 4 streams the K halves of the tiles, warp 6 the V^T halves: a K
+        // stage is free again once its S = Q K^T is done, long before the P.V
+        // that frees a V stage, so K runs a whole tile ahead
         if (lane == 0) {
-            const uint8_t *src0 = reinterpret_cast<const uint8_t *>(p.split) + (size_t)g * p.tiles * SM::TILE;
+            const bool is_k = warp == 4;
+            const uint32_t half = is_k ? 2 * SM::K_PART : 2 * SM::V_PART;
+            uint64_t *full = is_k ? k_full : v_full;
+            uint64_t *empty = is_k ? k_empty : v_empty;
+            const uint8_t *src0 = reinterpret_cast<const uint8_t *>(p.split) + (size_t)g * p.tiles * SM::TILE +
+                                  (is_k ? 0 : 2 * SM::K_PART);
+            uint8_t *ring = smem + (is_k ? SM::k_off : SM::v_off);
             for (int j = 0; j < n_tiles; ++j) {
                 const int s = j & 1;
-                if (j >= 2 && !bounded_wait(&kv_empty[s], ((j >> 1) - 1) & 1)) break;
-                uint8_t *dst = smem + SM::kv_off + s * SM::TILE;
-                mbar_arrive_expect_tx(&kv_full[s], SM::TILE);
+                if (j >= 2 && !bounded_wait(&empty[s], ((j >> 1) - 1) & 1)) break;
+                uint8_t *dst = ring + s * half;
+                mbar_arrive_expect_tx(&full[s], half);
 #pragma unroll
-                for (int part = 0; part < 4; ++part)   // kept in L2: every query tile and head reads it
-                    bulk_g2s_plain(dst + part * (SM::TILE / 4), src0 + (size_t)j * SM::TILE + part * (SM::TILE / 4),
-                                   SM::TILE / 4, &kv_full[s]);
+                for (int part = 0; part < 2; ++part)   // kept in L2: every query tile and head reads it
+                    bulk_g2s_plain(dst + part * (half / 2), src0 + (size_t)j * SM::TILE + part * (half / 2), half / 2,
+                                   &full[s]);
             }
         }
     } else if (warp == 5) {
@@ -304,27 +318,29 @@ __global__ void __launch_bounds__(192, 1) prefill_kernel(const __grid_constant__
             bool ok = bounded_wait(q_ready, 0);
             auto issue_s = [&](int j) -> bool {
                 const int s = j & 1;
-                if (!bounded_wait(&kv_full[s], (j >> 1) & 1)) return false;
+                if (!bounded_wait(&k_full[s], (j >> 1) & 1)) return false;
                 if (j >= 2 && !bounded_wait(&s_empty[s], ((j >> 1) - 1) & 1)) return false;
                 tc_fence_after();
-                const uint32_t kb = sbase + SM::kv_off + s * SM::TILE;
+                const uint32_t kb = sbase + SM::k_off + s * 2 * SM::K_PART;
 #pragma unroll
                 for (int kk = 0; kk < D / 16; ++kk) {
                     const uint32_t qo = (kk >> 2) * (kRows * 128) + (kk & 3) * 32;
                     const uint32_t ko = (kk >> 2) * (kKeys * 128) + (kk & 3) * 32;
-                    tc_mma(t_s[s], sdesc(qs + qo), sdesc(kb + ko), ID_S, kk > 0);                      // hi*hi
-                    tc_mma(t_s[s], sdesc(qs + qo), sdesc(kb + SM::K_PART + ko), ID_S, 1);              // hi*mid
-                    tc_mma(t_s[s], sdesc(qs + SM::Q_PART + qo), sdesc(kb + ko), ID_S, 1);              // mid*hi
+                    tc_mma(tmem + 64 * s, sdesc(qs + qo), sdesc(kb + ko), ID_S, kk > 0);                      // hi*hi
+                    tc_mma(tmem + 64 * s, sdesc(qs + qo), sdesc(kb + SM::K_PART + ko), ID_S, 1);              // hi*mid
+                    tc_mma(tmem + 64 * s, sdesc(qs + SM::Q_PART + qo), sdesc(kb + ko), ID_S, 1);              // mid*hi
                 }
                 tc_commit(&s_full[s]);
+                tc_commit(&k_empty[s]);
                 return true;
             };
             if (ok && n_tiles > 0) ok = issue_s(0);
             for (int j = 0; ok && j < n_tiles; ++j) {
                 if (j + 1 < n_tiles && !issue_s(j + 1)) break;
                 if (!bounded_wait(p_full, j & 1)) break;
+                if (!bounded_wait(&v_full[j & 1], (j >> 1) & 1)) break;
                 tc_fence_after();
-                const uint32_t vb = sbase + SM::kv_off + (j & 1) * SM::TILE + 2 * SM::K_PART;
+                const uint32_t vb = sbase + SM::v_off + (j & 1) * 2 * SM::V_PART;
 #pragma unroll
                 for (int kk = 0; kk < kKeys / 16; ++kk) {
                     const uint32_t o = kk * 32;
@@ -333,7 +349,7 @@ __global__ void __launch_bounds__(192, 1) prefill_kernel(const __grid_constant__
                     tc_mma(t_o, sdesc(ps + SM::P_PART + o), sdesc(vb + o), ID_O, 1);                   // mid*hi
                 }
                 tc_commit(pv_done);
-                tc_commit(&kv_empty[j & 1]);
+                tc_commit(&v_empty[j & 1]);
             }
             // tensor memory is released below only after every MMA issued here is done
             tc_commit(mma_drained);
@@ -385,8 +401,8 @@ __global__ void __launch_bounds__(192, 1) prefill_kernel(const __grid_constant__
             if (!bounded_wait(&s_full[s], (j >> 1) & 1)) { ok = false; break; }
             tc_fence_after();
             float sv[64];
-            tc_ld32(t_s[s] + lane_off, *reinterpret_cast<float(*)[32]>(sv));
-            tc_ld32(t_s[s] + lane_off + 32, *reinterpret_cast<float(*)[32]>(sv + 32));
+            tc_ld32(tmem + 64 * s + lane_off, *reinterpret_cast<float(*)[32]>(sv));
+            tc_ld32(tmem + 64 * s + lane_off + 32, *reinterpret_cast<float(*)[32]>(sv + 32));
             tc_wait_ld();
             tc_fence_before();
             __syncwarp();
@@ -396,35 +412,41 @@ __global__ void __launch_bounds__(192, 1) prefill_kernel(const __grid_constant__
                 for (int i = 0; i < 64; ++i)
                     if (j * kKeys + i > lim) sv[i] = -INFINITY;
             }
-            float mx = sv[0];
+            // row maximum as a tree (8 independent chains, then pairs)
+            float mx8[8];
 #pragma unroll
-            for (int i = 1; i < 64; ++i) mx = fmaxf(mx, sv[i]);
+            for (int c = 0; c < 8; ++c) mx8[c] = sv[c];
+#pragma unroll
+            for (int i = 8; i < 64; ++i) mx8[i & 7] = fmaxf(mx8[i & 7], sv[i]);
+            const float mx = fmaxf(fmaxf(fmaxf(mx8[0], mx8[1]), fmaxf(mx8[2], mx8[3])),
+                                   fmaxf(fmaxf(mx8[4], mx8[5]), fmaxf(mx8[6], mx8[7])));
             const bool need = mx > m_ref + kRescale;
-            // O and P belong to the previous tile's P.V until it completes
-            if (j > 0 && !bounded_wait(pv_done, (j - 1) & 1)) { ok = false; break; }
-            if (__any_sync(FULLMASK, need)) {
-                const float m_new = need ? mx : m_ref;
-                const float alpha = fast_exp2(m_ref - m_new);   // 0 for the first tile, 1 where not needed
-                l *= alpha;
-                m_ref = m_new;
-                if (j > 0) {
-                    tc_fence_after();
-#pragma unroll
-                    for (int c0 = 0; c0 < D; c0 += 32) {
-                        float o[32];
-                        tc_ld32(t_o + lane_off + c0, o);
-                        tc_wait_ld();
-#pragma unroll
-                        for (int i = 0; i < 32; ++i) o[i] *= alpha;
-                        tc_st32(t_o + lane_off + c0, o);
-                    }
-                    tc_wait_st();
-                }
-            }
+            const bool any_need = __any_sync(FULLMASK, need);
+            const float m_new = need ? mx : m_ref;
+            const float alpha = fast_exp2(m_ref - m_new);   // 0 for the first tile, 1 where not needed
+            // probabilities first (registers only), overlapping the previous tile's P.V
+            float l8[8] = {0, 0, 0, 0, 0, 0, 0, 0};
 #pragma unroll
             for (int i = 0; i < 64; ++i) {
-                sv[i] = fast_exp2(sv[i] - m_ref);   // probabilities, in place
-                l += sv[i];
+                sv[i] = fast_exp2(sv[i] - m_new);
+                l8[i & 7] += sv[i];
+            }
+            l = fmaf(l, alpha, ((l8[0] + l8[1]) + (l8[2] + l8[3])) + ((l8[4] + l8[5]) + (l8[6] + l8[7])));
+            m_ref = m_new;
+            // O and the P buffer belong to the previous tile's P.V until it completes
+            if (j > 0 && !bounded_wait(pv_done, (j - 1) & 1)) { ok = false; break; }
+            if (any_need && j > 0) {
+                tc_fence_after();
+#pragma unroll
+                for (int c0 = 0; c0 < D; c0 += 32) {
+                    float o[32];
+                    tc_ld32(t_o + lane_off + c0, o);
+                    tc_wait_ld();
+#pragma unroll
+                    for (int i = 0; i < 32; ++i) o[i] *= alpha;
+                    tc_st32(t_o + lane_off + c0, o);
+                }
+                tc_wait_st();
             }
 #pragma unroll
             for (int c = 0; c < 8; ++c) {
@@ -484,7 +506,7 @@ cudaError_t launch_prefill_d(const PrefillParams &p, cudaStream_t s) {
         if (dev >= 0 && dev < 64) configured[dev] = true;
     }
     const int q_tiles = (p.n + kRows - 1) / kRows;
-    prefill_kernel<D><<<dim3(q_tiles, p.H), 192, SM::bytes, s>>>(p);
+    prefill_kernel<D><<<dim3(q_tiles, p.H), 224, SM::bytes, s>>>(p);
     return cudaGetLastError();
 }
 
