@@ -30,14 +30,18 @@
 //                 the reference by 2^8), P split into the P operand.
 //                 Epilogue: O / l to global memory.
 //     warps 4, 6  producers: K hi/mid and V^T hi/mid of a tile in separate
-//                 two-stage rings (a K stage frees as soon as its S is done),
-//                 bulk copies completing on mbarriers.
+//                 three-stage rings (a K stage frees as soon as its S is
+//                 done), bulk copies completing on mbarriers.
 //     warp 5      allocates tensor memory; one lane issues the MMAs:
-//                 S[j%2] = Q K_j^T (128 x 64), then O += P_j V_j (128 x d),
-//                 issuing S for tile j+1 before O for tile j so that the
-//                 softmax of tile j overlaps it. tcgen05.commit signals
-//                 completion to the softmax warps and frees K/V stages.
-//   Tensor memory: S double buffer (2 x 64 columns) and O (d columns).
+//                 S[j%4] = Q K_j^T (128 x 64), then O += P_j V_j (128 x d),
+//                 issuing S for tile j+2 before O for tile j so that the
+//                 softmax of tiles j+1, j+2 overlaps it. tcgen05.commit
+//                 signals completion to the softmax warps and frees K/V
+//                 stages and S buffers.
+//   Tensor memory: Q hi/mid (the A operand of S = Q K^T), four S buffers (64
+//   columns each; a tile's P hi/mid, the A operand of O += P V, overwrites
+//   its S) and O (d columns): 512 columns. Only K and V^T are read from
+//   shared memory, which halves the operand traffic per MMA.
 // Every mbarrier wait is bounded (2 s), after which the CTA records an error
 // and drains out; tensor memory is always released.
 
@@ -51,7 +55,8 @@ namespace {
 
 constexpr int kRows = 128;        // query rows per CTA (TMEM lanes)
 constexpr int kKeys = 64;         // keys per tile
-constexpr int kStages = 2;
+constexpr int kStages = 3;        // K and V ring stages
+constexpr int kBufs = 4;          // S/P buffers in tensor memory
 constexpr float kRescale = 8.0f;  // log2-domain slack before O is rescaled
 constexpr unsigned FULLMASK = 0xffffffffu;
 
@@ -78,19 +83,21 @@ __host__ __device__ constexpr uint32_t idesc_bf16(int M, int N) {
 
 template <int D>
 struct PrefillSmem {
-    static constexpr int QATOMS = D / 64;                        // 64-element K atoms of Q and K
-    static constexpr uint32_t Q_PART = (uint32_t)QATOMS * kRows * 128;   // one of hi/mid
-    static constexpr uint32_t K_PART = (uint32_t)QATOMS * kKeys * 128;
+    static constexpr int QATOMS = D / 64;                                // 64-element K atoms of K
+    static constexpr uint32_t K_PART = (uint32_t)QATOMS * kKeys * 128;   // one of hi/mid
     static constexpr uint32_t V_PART = (uint32_t)D * 128;                // V^T: d rows x 64 keys
     static constexpr uint32_t TILE = 2 * K_PART + 2 * V_PART;            // one global tile: K half, V half
-    static constexpr uint32_t P_PART = (uint32_t)kRows * 128;
-    static constexpr uint32_t q_off = 0;
-    static constexpr uint32_t k_off = 2 * Q_PART;                         // K ring: kStages x (hi, mid)
-    static constexpr uint32_t v_off = k_off + kStages * 2 * K_PART;       // V ring: kStages x (hi, mid)
-    static constexpr uint32_t p_off = v_off + kStages * 2 * V_PART;
-    static constexpr uint32_t bar_off = p_off + 2 * P_PART;
-    static constexpr uint32_t bytes = bar_off + 256 + 1024;   // barriers, TMEM base, alignment slack
-    static constexpr uint32_t TMEM_COLS = D == 128 ? 256 : 256; // S0, S1 (64 each) and O (d)
+    static constexpr uint32_t k_off = 0;                                 // K ring: kStages x (hi, mid)
+    static constexpr uint32_t v_off = k_off + kStages * 2 * K_PART;      // V ring: kStages x (hi, mid)
+    static constexpr uint32_t bar_off = v_off + kStages * 2 * V_PART;
+    // barriers, TMEM base, alignment slack; at least 116 KB so that one CTA
+    // holds an SM (a second would only wait in tcgen05.alloc for the 512
+    // tensor-memory columns the first holds)
+    static constexpr uint32_t bytes = bar_off + 512 + 1024 > 116u * 1024 ? bar_off + 512 + 1024 : 116u * 1024;
+    // tensor memory columns: Q hi/mid as MMA A operand (bf16 pairs), kBufs S
+    // buffers (fp32; the tile's P hi/mid, bf16 pairs, overwrite them), O
+    static constexpr uint32_t T_Q = 0, T_S = 128, T_O = T_S + kBufs * 64;
+    static constexpr uint32_t TMEM_COLS = 512;
 };
 
 // ---------------------------------------------------------------- tcgen05 helpers
@@ -104,6 +111,17 @@ __device__ __forceinline__ void tc_mma(uint32_t d_tmem, uint64_t a, uint64_t b, 
         "setp.ne.b32 p, %4, 0;\n\t"
         "tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n\t}" ::"r"(d_tmem),
         "l"(a), "l"(b), "r"(idesc), "r"(acc)
+        : "memory");
+}
+
+// A operand from tensor memory (bf16 pairs, row m in lane m, element k in
+// column k/2, even k in the low half), B from shared memory.
+__device__ __forceinline__ void tc_mma_ts(uint32_t d_tmem, uint32_t a_tmem, uint64_t b, uint32_t idesc, uint32_t acc) {
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t"
+        "setp.ne.b32 p, %4, 0;\n\t"
+        "tcgen05.mma.cta_group::1.kind::f16 [%0], [%1], %2, %3, p;\n\t}" ::"r"(d_tmem),
+        "r"(a_tmem), "l"(b), "r"(idesc), "r"(acc)
         : "memory");
 }
 
@@ -141,6 +159,27 @@ __device__ __forceinline__ void tc_st32(uint32_t taddr, const float (&v)[32]) {
         "r"(__float_as_uint(v[24])), "r"(__float_as_uint(v[25])), "r"(__float_as_uint(v[26])), "r"(__float_as_uint(v[27])),
         "r"(__float_as_uint(v[28])), "r"(__float_as_uint(v[29])), "r"(__float_as_uint(v[30])), "r"(__float_as_uint(v[31]))
         : "memory");
+}
+
+__device__ __forceinline__ void tc_st32u(uint32_t taddr, const uint32_t (&v)[32]) {
+    asm volatile(
+        "tcgen05.st.sync.aligned.32x32b.x32.b32 [%0], {%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,%16,"
+        "%17,%18,%19,%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31,%32};" ::"r"(taddr),
+        "r"(v[0]), "r"(v[1]), "r"(v[2]), "r"(v[3]), "r"(v[4]), "r"(v[5]), "r"(v[6]), "r"(v[7]), "r"(v[8]), "r"(v[9]),
+        "r"(v[10]), "r"(v[11]), "r"(v[12]), "r"(v[13]), "r"(v[14]), "r"(v[15]), "r"(v[16]), "r"(v[17]), "r"(v[18]),
+        "r"(v[19]), "r"(v[20]), "r"(v[21]), "r"(v[22]), "r"(v[23]), "r"(v[24]), "r"(v[25]), "r"(v[26]), "r"(v[27]),
+        "r"(v[28]), "r"(v[29]), "r"(v[30]), "r"(v[31])
+        : "memory");
+}
+
+// hi/mid bf16 split of 2 fp32 values, each part packed as one 32-bit word
+// (first value in the low half)
+__device__ __forceinline__ void split2(float x0, float x1, uint32_t &hi, uint32_t &mid) {
+    const __nv_bfloat162 a = __floats2bfloat162_rn(x0, x1);
+    const float2 af = __bfloat1622float2(a);
+    const __nv_bfloat162 b = __floats2bfloat162_rn(x0 - af.x, x1 - af.y);
+    hi = *reinterpret_cast<const uint32_t *>(&a);
+    mid = *reinterpret_cast<const uint32_t *>(&b);
 }
 
 __device__ __forceinline__ void tc_wait_ld() { asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory"); }
@@ -228,18 +267,22 @@ __global__ void __launch_bounds__(224, 1) prefill_kernel(const __grid_constant__
     uint8_t *smem = reinterpret_cast<uint8_t *>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~(uintptr_t)1023);
     const uint32_t sbase = smem_u32(smem);
     uint64_t *bars = reinterpret_cast<uint64_t *>(smem + SM::bar_off);
-    uint64_t *k_full = bars;               // [2] K producer -> MMA
-    uint64_t *k_empty = bars + 2;          // [2] MMA commit (after S) -> K producer
-    uint64_t *s_full = bars + 4;           // [2] MMA commit -> softmax
-    uint64_t *s_empty = bars + 6;          // [2] softmax (4 warps) -> MMA
-    uint64_t *p_full = bars + 8;           // softmax (4 warps) -> MMA
-    uint64_t *pv_done = bars + 9;          // MMA commit -> softmax
-    uint64_t *q_ready = bars + 10;         // softmax (4 warps) -> MMA
-    uint64_t *mma_drained = bars + 11;     // MMA commit -> MMA issuer, before TMEM is freed
-    uint64_t *v_full = bars + 12;          // [2] V producer -> MMA
-    uint64_t *v_empty = bars + 14;         // [2] MMA commit (after O) -> V producer
-    uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(bars + 16);
-    int *abort_flag = reinterpret_cast<int *>(bars + 17);
+    uint64_t *k_full = bars;               // [3] K producer -> MMA
+    uint64_t *k_empty = bars + 3;          // [3] MMA commit (after S) -> K producer
+    uint64_t *v_full = bars + 6;           // [3] V producer -> MMA
+    uint64_t *v_empty = bars + 9;          // [3] MMA commit (after O) -> V producer
+    uint64_t *s_full = bars + 12;          // [4] MMA commit -> softmax: S of a buffer is ready
+    // p_free[b]: MMA commit after O += P_j V_j (b = j % 4) -> MMA (buffer b
+    // may take S again) and softmax (O holds every tile up to j). A parity
+    // wait is exact only within one phase of the barrier's count; when the
+    // softmax waits for P.V j-1 (or the last one), the P.V of j-5 is known to
+    // be complete (it precedes the S it has just read), so it is.
+    uint64_t *p_free = bars + 16;          // [4]
+    uint64_t *p_full = bars + 20;          // [4] softmax (4 warps) -> MMA: P of a buffer written
+    uint64_t *q_ready = bars + 24;         // softmax (4 warps) -> MMA
+    uint64_t *mma_drained = bars + 25;     // MMA commit -> MMA issuer, before TMEM is freed
+    uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(bars + 26);
+    int *abort_flag = reinterpret_cast<int *>(bars + 27);
 
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int qt = gridDim.x - 1 - blockIdx.x;   // heaviest (last) query tiles first
@@ -252,22 +295,23 @@ __global__ void __launch_bounds__(224, 1) prefill_kernel(const __grid_constant__
     const int first_masked = (p.pos0 + z0) / kKeys;              // tiles from here need the mask
 
     if (threadIdx.x == 0) {
-        for (int i = 0; i < 2; ++i) {
+        for (int i = 0; i < kStages; ++i) {
             mbar_init(&k_full[i], 1);
             mbar_init(&k_empty[i], 1);
             mbar_init(&v_full[i], 1);
             mbar_init(&v_empty[i], 1);
-            mbar_init(&s_full[i], 1);
-            mbar_init(&s_empty[i], 4);
         }
-        mbar_init(p_full, 4);
-        mbar_init(pv_done, 1);
+        for (int i = 0; i < kBufs; ++i) {
+            mbar_init(&s_full[i], 1);
+            mbar_init(&p_free[i], 1);
+            mbar_init(&p_full[i], 4);
+        }
         mbar_init(q_ready, 4);
         mbar_init(mma_drained, 1);
         *abort_flag = 0;
         mbar_fence_init();
     }
-    if (warp == 5) {   // tensor memory: S0 | S1 | O
+    if (warp == 5) {
         asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(tmem_slot)),
                      "r"(SM::TMEM_COLS)
                      : "memory");
@@ -277,7 +321,7 @@ __global__ void __launch_bounds__(224, 1) prefill_kernel(const __grid_constant__
     __syncthreads();
     tc_fence_after();
     const uint32_t tmem = *tmem_slot;
-    const uint32_t t_o = tmem + 128;   // S buffer b at tmem + 64 * b
+    const uint32_t t_q = tmem + SM::T_Q, t_o = tmem + SM::T_O;   // S buffer b at tmem + T_S + 64 * b
 
     auto bounded_wait = [&](uint64_t *bar, uint32_t parity) -> bool {
         if (*reinterpret_cast<volatile int *>(abort_flag)) return false;
@@ -290,7 +334,7 @@ __global__ void __launch_bounds__(224, 1) prefill_kernel(const __grid_constant__
         // ------------------------------------------------------------ producers
         // warp 4 streams the K halves of the tiles, warp 6 the V^T halves: a K
         // stage is free again once its S = Q K^T is done, long before the P.V
-        // that frees a V stage, so K runs a whole tile ahead
+        // that frees a V stage, so K runs ahead of V
         if (lane == 0) {
             const bool is_k = warp == 4;
             const uint32_t half = is_k ? 2 * SM::K_PART : 2 * SM::V_PART;
@@ -300,8 +344,8 @@ __global__ void __launch_bounds__(224, 1) prefill_kernel(const __grid_constant__
                                   (is_k ? 0 : 2 * SM::K_PART);
             uint8_t *ring = smem + (is_k ? SM::k_off : SM::v_off);
             for (int j = 0; j < n_tiles; ++j) {
-                const int s = j & 1;
-                if (j >= 2 && !bounded_wait(&empty[s], ((j >> 1) - 1) & 1)) break;
+                const int s = j % kStages;
+                if (j >= kStages && !bounded_wait(&empty[s], ((j / kStages) - 1) & 1)) break;
                 uint8_t *dst = ring + s * half;
                 mbar_arrive_expect_tx(&full[s], half);
 #pragma unroll
@@ -313,43 +357,45 @@ __global__ void __launch_bounds__(224, 1) prefill_kernel(const __grid_constant__
     } else if (warp == 5) {
         // ------------------------------------------------------------ MMA issuer
         if (lane == 0) {
-            const uint32_t qs = sbase + SM::q_off, ps = sbase + SM::p_off;
             constexpr uint32_t ID_S = idesc_bf16(kRows, kKeys), ID_O = idesc_bf16(kRows, D);
             bool ok = bounded_wait(q_ready, 0);
-            auto issue_s = [&](int j) -> bool {
-                const int s = j & 1;
-                if (!bounded_wait(&k_full[s], (j >> 1) & 1)) return false;
-                if (j >= 2 && !bounded_wait(&s_empty[s], ((j >> 1) - 1) & 1)) return false;
+            tc_fence_after();
+            auto issue_s = [&](int j) -> bool {   // S_j = Q K_j^T into buffer j % kBufs
+                const int s = j % kStages, b = j % kBufs;
+                if (!bounded_wait(&k_full[s], (j / kStages) & 1)) return false;
+                if (j >= kBufs && !bounded_wait(&p_free[b], ((j / kBufs) - 1) & 1)) return false;
                 tc_fence_after();
                 const uint32_t kb = sbase + SM::k_off + s * 2 * SM::K_PART;
+                const uint32_t ts = tmem + SM::T_S + 64 * b;
 #pragma unroll
                 for (int kk = 0; kk < D / 16; ++kk) {
-                    const uint32_t qo = (kk >> 2) * (kRows * 128) + (kk & 3) * 32;
                     const uint32_t ko = (kk >> 2) * (kKeys * 128) + (kk & 3) * 32;
-                    tc_mma(tmem + 64 * s, sdesc(qs + qo), sdesc(kb + ko), ID_S, kk > 0);                      // hi*hi
-                    tc_mma(tmem + 64 * s, sdesc(qs + qo), sdesc(kb + SM::K_PART + ko), ID_S, 1);              // hi*mid
-                    tc_mma(tmem + 64 * s, sdesc(qs + SM::Q_PART + qo), sdesc(kb + ko), ID_S, 1);              // mid*hi
+                    tc_mma_ts(ts, t_q + kk * 8, sdesc(kb + ko), ID_S, kk > 0);                        // hi*hi
+                    tc_mma_ts(ts, t_q + kk * 8, sdesc(kb + SM::K_PART + ko), ID_S, 1);                // hi*mid
+                    tc_mma_ts(ts, t_q + HALF + kk * 8, sdesc(kb + ko), ID_S, 1);                      // mid*hi
                 }
-                tc_commit(&s_full[s]);
+                tc_commit(&s_full[b]);
                 tc_commit(&k_empty[s]);
                 return true;
             };
-            if (ok && n_tiles > 0) ok = issue_s(0);
+            for (int j = 0; ok && j < 2 && j < n_tiles; ++j) ok = issue_s(j);
             for (int j = 0; ok && j < n_tiles; ++j) {
-                if (j + 1 < n_tiles && !issue_s(j + 1)) break;
-                if (!bounded_wait(p_full, j & 1)) break;
-                if (!bounded_wait(&v_full[j & 1], (j >> 1) & 1)) break;
+                if (j + 2 < n_tiles && !issue_s(j + 2)) break;
+                const int s = j % kStages, b = j % kBufs;
+                if (!bounded_wait(&p_full[b], (j / kBufs) & 1)) break;
+                if (!bounded_wait(&v_full[s], (j / kStages) & 1)) break;
                 tc_fence_after();
-                const uint32_t vb = sbase + SM::v_off + (j & 1) * 2 * SM::V_PART;
+                const uint32_t vb = sbase + SM::v_off + s * 2 * SM::V_PART;
+                const uint32_t tp = tmem + SM::T_S + 64 * b;   // P hi in columns 0-31, P mid in 32-63
 #pragma unroll
                 for (int kk = 0; kk < kKeys / 16; ++kk) {
                     const uint32_t o = kk * 32;
-                    tc_mma(t_o, sdesc(ps + o), sdesc(vb + o), ID_O, (j > 0 || kk > 0));               // hi*hi
-                    tc_mma(t_o, sdesc(ps + o), sdesc(vb + SM::V_PART + o), ID_O, 1);                   // hi*mid
-                    tc_mma(t_o, sdesc(ps + SM::P_PART + o), sdesc(vb + o), ID_O, 1);                   // mid*hi
+                    tc_mma_ts(t_o, tp + kk * 8, sdesc(vb + o), ID_O, (j > 0 || kk > 0));               // hi*hi
+                    tc_mma_ts(t_o, tp + kk * 8, sdesc(vb + SM::V_PART + o), ID_O, 1);                  // hi*mid
+                    tc_mma_ts(t_o, tp + 32 + kk * 8, sdesc(vb + o), ID_O, 1);                          // mid*hi
                 }
-                tc_commit(pv_done);
-                tc_commit(&v_empty[j & 1]);
+                tc_commit(&p_free[b]);
+                tc_commit(&v_empty[s]);
             }
             // tensor memory is released below only after every MMA issued here is done
             tc_commit(mma_drained);
@@ -362,7 +408,7 @@ __global__ void __launch_bounds__(224, 1) prefill_kernel(const __grid_constant__
         const bool valid = t < rows;
         const int lim = p.pos0 + z;                 // last key this row attends to
         const uint32_t lane_off = (uint32_t)(warp * 32) << 16;
-        // Q row: RoPE at its position, scale, hi/mid split into the swizzled operand
+        // Q row: RoPE at its position, scale, hi/mid split into tensor memory
         {
             float qv[D];
             const float *qsrc = p.q + ((size_t)z * p.H + h) * D;
@@ -379,34 +425,31 @@ __global__ void __launch_bounds__(224, 1) prefill_kernel(const __grid_constant__
                 qv[i] = rope_lo(x0, x1, a.x, a.y) * p.scale_log2;
                 qv[i + HALF] = rope_hi(x0, x1, a.x, a.y) * p.scale_log2;
             }
-            uint8_t *qs = smem + SM::q_off;
 #pragma unroll
-            for (int c = 0; c < D / 8; ++c) {
-                uint4 hi, mid;
-                split8(qv + c * 8, hi, mid);
-                const uint32_t off = (uint32_t)(c >> 3) * (kRows * 128) + sw128(t, c & 7);
-                *reinterpret_cast<uint4 *>(qs + off) = hi;
-                *reinterpret_cast<uint4 *>(qs + SM::Q_PART + off) = mid;
+            for (int c0 = 0; c0 < HALF; c0 += 32) {   // 32 columns = 64 elements per store
+                uint32_t hi[32], mid[32];
+#pragma unroll
+                for (int i = 0; i < 32; ++i) split2(qv[2 * (c0 + i)], qv[2 * (c0 + i) + 1], hi[i], mid[i]);
+                tc_st32u(t_q + lane_off + c0, hi);
+                tc_st32u(t_q + lane_off + HALF + c0, mid);
             }
+            tc_wait_st();
         }
-        fence_proxy_async_smem();
+        tc_fence_before();
         __syncwarp();
         if (lane == 0) mbar_arrive(q_ready);
 
         float m_ref = -INFINITY, l = 0.f;
-        uint8_t *ps = smem + SM::p_off;
         bool ok = true;
         for (int j = 0; j < n_tiles; ++j) {
-            const int s = j & 1;
-            if (!bounded_wait(&s_full[s], (j >> 1) & 1)) { ok = false; break; }
+            const int b = j % kBufs;
+            const uint32_t ts = tmem + SM::T_S + 64 * b + lane_off;
+            if (!bounded_wait(&s_full[b], (j / kBufs) & 1)) { ok = false; break; }
             tc_fence_after();
             float sv[64];
-            tc_ld32(tmem + 64 * s + lane_off, *reinterpret_cast<float(*)[32]>(sv));
-            tc_ld32(tmem + 64 * s + lane_off + 32, *reinterpret_cast<float(*)[32]>(sv + 32));
+            tc_ld32(ts, *reinterpret_cast<float(*)[32]>(sv));
+            tc_ld32(ts + 32, *reinterpret_cast<float(*)[32]>(sv + 32));
             tc_wait_ld();
-            tc_fence_before();
-            __syncwarp();
-            if (lane == 0) mbar_arrive(&s_empty[s]);
             if (j >= first_masked) {
 #pragma unroll
                 for (int i = 0; i < 64; ++i)
@@ -424,7 +467,6 @@ __global__ void __launch_bounds__(224, 1) prefill_kernel(const __grid_constant__
             const bool any_need = __any_sync(FULLMASK, need);
             const float m_new = need ? mx : m_ref;
             const float alpha = fast_exp2(m_ref - m_new);   // 0 for the first tile, 1 where not needed
-            // probabilities first (registers only), overlapping the previous tile's P.V
             float l8[8] = {0, 0, 0, 0, 0, 0, 0, 0};
 #pragma unroll
             for (int i = 0; i < 64; ++i) {
@@ -433,9 +475,17 @@ __global__ void __launch_bounds__(224, 1) prefill_kernel(const __grid_constant__
             }
             l = fmaf(l, alpha, ((l8[0] + l8[1]) + (l8[2] + l8[3])) + ((l8[4] + l8[5]) + (l8[6] + l8[7])));
             m_ref = m_new;
-            // O and the P buffer belong to the previous tile's P.V until it completes
-            if (j > 0 && !bounded_wait(pv_done, (j - 1) & 1)) { ok = false; break; }
+            // P of this tile into its own S buffer (S has been read above)
+            {
+                uint32_t hi[32], mid[32];
+#pragma unroll
+                for (int i = 0; i < 32; ++i) split2(sv[2 * i], sv[2 * i + 1], hi[i], mid[i]);
+                tc_st32u(ts, hi);
+                tc_st32u(ts + 32, mid);
+            }
+            // O is stable only once the previous tile's P.V is done
             if (any_need && j > 0) {
+                if (!bounded_wait(&p_free[(j - 1) % kBufs], ((j - 1) / kBufs) & 1)) { ok = false; break; }
                 tc_fence_after();
 #pragma unroll
                 for (int c0 = 0; c0 < D; c0 += 32) {
@@ -446,23 +496,14 @@ __global__ void __launch_bounds__(224, 1) prefill_kernel(const __grid_constant__
                     for (int i = 0; i < 32; ++i) o[i] *= alpha;
                     tc_st32(t_o + lane_off + c0, o);
                 }
-                tc_wait_st();
             }
-#pragma unroll
-            for (int c = 0; c < 8; ++c) {
-                uint4 hi, mid;
-                split8(sv + c * 8, hi, mid);
-                const uint32_t off = sw128(t, c);
-                *reinterpret_cast<uint4 *>(ps + off) = hi;
-                *reinterpret_cast<uint4 *>(ps + SM::P_PART + off) = mid;
-            }
-            fence_proxy_async_smem();
+            tc_wait_st();
             tc_fence_before();
             __syncwarp();
-            if (lane == 0) mbar_arrive(p_full);
+            if (lane == 0) mbar_arrive(&p_full[b]);
         }
         // epilogue: O / l
-        if (ok && n_tiles > 0 && bounded_wait(pv_done, (n_tiles - 1) & 1)) {
+        if (ok && n_tiles > 0 && bounded_wait(&p_free[(n_tiles - 1) % kBufs], ((n_tiles - 1) / kBufs) & 1)) {
             tc_fence_after();
             const float inv = l > 0.f ? 1.f / l : 0.f;
             float *dst = p.out + ((size_t)z * p.H + h) * D;
