@@ -34,9 +34,10 @@
 //                 done), bulk copies completing on mbarriers.
 //     warp 5      allocates tensor memory; one lane issues the MMAs:
 //                 S[j%4] = Q K_j^T (128 x 64), then O += P_j V_j (128 x d),
-//                 issuing S for tile j+2 before O for tile j so that the
-//                 softmax of tiles j+1, j+2 overlaps it. tcgen05.commit
-//                 signals completion to the softmax warps and frees K/V
+//                 issuing S for tile j+2 together with O for tile j after a
+//                 single wait point per tile, so that the softmax of tiles
+//                 j+1, j+2 overlaps them. Two tcgen05.commits per tile
+//                 signal completion to the softmax warps and free K/V
 //                 stages and S buffers.
 //   Tensor memory: Q hi/mid (the A operand of S = Q K^T), four S buffers (64
 //   columns each; a tile's P hi/mid, the A operand of O += P V, overwrites
@@ -267,22 +268,27 @@ __global__ void __launch_bounds__(224, 1) prefill_kernel(const __grid_constant__
     uint8_t *smem = reinterpret_cast<uint8_t *>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~(uintptr_t)1023);
     const uint32_t sbase = smem_u32(smem);
     uint64_t *bars = reinterpret_cast<uint64_t *>(smem + SM::bar_off);
+    // Two commits per tile carry every completion (each commit and each
+    // mbarrier access of the MMA thread costs tensor-pipe time):
+    //   s_full[j % 4]  after S_j = Q K_j^T: the softmax may read S_j, and the
+    //                  K stage of tile j may take tile j + 3;
+    //   p_free[j % 4]  after O += P_j V_j: S buffer j % 4 may take S_{j+4},
+    //                  the V stage of tile j may take tile j + 3, and O holds
+    //                  every tile up to j.
+    // A parity wait is exact only within one phase of the barrier's count.
+    // Every wait below is: each waiter has already seen the completion four
+    // tiles earlier on the same barrier (or it is the first), and the
+    // completion four tiles later needs something the waiter has not done
+    // yet (the next K or V tile, or the next P).
     uint64_t *k_full = bars;               // [3] K producer -> MMA
-    uint64_t *k_empty = bars + 3;          // [3] MMA commit (after S) -> K producer
-    uint64_t *v_full = bars + 6;           // [3] V producer -> MMA
-    uint64_t *v_empty = bars + 9;          // [3] MMA commit (after O) -> V producer
-    uint64_t *s_full = bars + 12;          // [4] MMA commit -> softmax: S of a buffer is ready
-    // p_free[b]: MMA commit after O += P_j V_j (b = j % 4) -> MMA (buffer b
-    // may take S again) and softmax (O holds every tile up to j). A parity
-    // wait is exact only within one phase of the barrier's count; when the
-    // softmax waits for P.V j-1 (or the last one), the P.V of j-5 is known to
-    // be complete (it precedes the S it has just read), so it is.
-    uint64_t *p_free = bars + 16;          // [4]
-    uint64_t *p_full = bars + 20;          // [4] softmax (4 warps) -> MMA: P of a buffer written
-    uint64_t *q_ready = bars + 24;         // softmax (4 warps) -> MMA
-    uint64_t *mma_drained = bars + 25;     // MMA commit -> MMA issuer, before TMEM is freed
-    uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(bars + 26);
-    int *abort_flag = reinterpret_cast<int *>(bars + 27);
+    uint64_t *v_full = bars + 3;           // [3] V producer -> MMA
+    uint64_t *s_full = bars + 6;           // [4]
+    uint64_t *p_free = bars + 10;          // [4]
+    uint64_t *p_full = bars + 14;          // [4] softmax (4 warps) -> MMA: P of a buffer written
+    uint64_t *q_ready = bars + 18;         // softmax (4 warps) -> MMA
+    uint64_t *mma_drained = bars + 19;     // MMA commit -> MMA issuer, before TMEM is freed
+    uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(bars + 20);
+    int *abort_flag = reinterpret_cast<int *>(bars + 21);
 
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int qt = gridDim.x - 1 - blockIdx.x;   // heaviest (last) query tiles first
@@ -297,9 +303,7 @@ __global__ void __launch_bounds__(224, 1) prefill_kernel(const __grid_constant__
     if (threadIdx.x == 0) {
         for (int i = 0; i < kStages; ++i) {
             mbar_init(&k_full[i], 1);
-            mbar_init(&k_empty[i], 1);
             mbar_init(&v_full[i], 1);
-            mbar_init(&v_empty[i], 1);
         }
         for (int i = 0; i < kBufs; ++i) {
             mbar_init(&s_full[i], 1);
@@ -323,7 +327,10 @@ __global__ void __launch_bounds__(224, 1) prefill_kernel(const __grid_constant__
     const uint32_t tmem = *tmem_slot;
     const uint32_t t_q = tmem + SM::T_Q, t_o = tmem + SM::T_O;   // S buffer b at tmem + T_S + 64 * b
 
+    // a completed phase costs one try_wait; the abort flag is read only on
+    // the slow path
     auto bounded_wait = [&](uint64_t *bar, uint32_t parity) -> bool {
+        if (mbar_try_wait(bar, parity)) return true;
         if (*reinterpret_cast<volatile int *>(abort_flag)) return false;
         if (mbar_wait(bar, parity, p.err, DEV_WAIT_FULL_TIMEOUT)) return true;
         *reinterpret_cast<volatile int *>(abort_flag) = 1;
@@ -339,13 +346,14 @@ __global__ void __launch_bounds__(224, 1) prefill_kernel(const __grid_constant__
             const bool is_k = warp == 4;
             const uint32_t half = is_k ? 2 * SM::K_PART : 2 * SM::V_PART;
             uint64_t *full = is_k ? k_full : v_full;
-            uint64_t *empty = is_k ? k_empty : v_empty;
+            uint64_t *done = is_k ? s_full : p_free;   // tile j - kStages no longer needs the stage
             const uint8_t *src0 = reinterpret_cast<const uint8_t *>(p.split) + (size_t)g * p.tiles * SM::TILE +
                                   (is_k ? 0 : 2 * SM::K_PART);
             uint8_t *ring = smem + (is_k ? SM::k_off : SM::v_off);
             for (int j = 0; j < n_tiles; ++j) {
                 const int s = j % kStages;
-                if (j >= kStages && !bounded_wait(&empty[s], ((j / kStages) - 1) & 1)) break;
+                const int jp = j - kStages;
+                if (jp >= 0 && !bounded_wait(&done[jp % kBufs], (jp / kBufs) & 1)) break;
                 uint8_t *dst = ring + s * half;
                 mbar_arrive_expect_tx(&full[s], half);
 #pragma unroll
@@ -360,13 +368,9 @@ __global__ void __launch_bounds__(224, 1) prefill_kernel(const __grid_constant__
             constexpr uint32_t ID_S = idesc_bf16(kRows, kKeys), ID_O = idesc_bf16(kRows, D);
             bool ok = bounded_wait(q_ready, 0);
             tc_fence_after();
-            auto issue_s = [&](int j) -> bool {   // S_j = Q K_j^T into buffer j % kBufs
-                const int s = j % kStages, b = j % kBufs;
-                if (!bounded_wait(&k_full[s], (j / kStages) & 1)) return false;
-                if (j >= kBufs && !bounded_wait(&p_free[b], ((j / kBufs) - 1) & 1)) return false;
-                tc_fence_after();
-                const uint32_t kb = sbase + SM::k_off + s * 2 * SM::K_PART;
-                const uint32_t ts = tmem + SM::T_S + 64 * b;
+            auto issue_s = [&](int j) {   // S_j = Q K_j^T into buffer j % kBufs
+                const uint32_t kb = sbase + SM::k_off + (j % kStages) * 2 * SM::K_PART;
+                const uint32_t ts = tmem + SM::T_S + 64 * (j % kBufs);
 #pragma unroll
                 for (int kk = 0; kk < D / 16; ++kk) {
                     const uint32_t ko = (kk >> 2) * (kKeys * 128) + (kk & 3) * 32;
@@ -374,19 +378,11 @@ __global__ void __launch_bounds__(224, 1) prefill_kernel(const __grid_constant__
                     tc_mma_ts(ts, t_q + kk * 8, sdesc(kb + SM::K_PART + ko), ID_S, 1);                // hi*mid
                     tc_mma_ts(ts, t_q + HALF + kk * 8, sdesc(kb + ko), ID_S, 1);                      // mid*hi
                 }
-                tc_commit(&s_full[b]);
-                tc_commit(&k_empty[s]);
-                return true;
+                tc_commit(&s_full[j % kBufs]);
             };
-            for (int j = 0; ok && j < 2 && j < n_tiles; ++j) ok = issue_s(j);
-            for (int j = 0; ok && j < n_tiles; ++j) {
-                if (j + 2 < n_tiles && !issue_s(j + 2)) break;
-                const int s = j % kStages, b = j % kBufs;
-                if (!bounded_wait(&p_full[b], (j / kBufs) & 1)) break;
-                if (!bounded_wait(&v_full[s], (j / kStages) & 1)) break;
-                tc_fence_after();
-                const uint32_t vb = sbase + SM::v_off + s * 2 * SM::V_PART;
-                const uint32_t tp = tmem + SM::T_S + 64 * b;   // P hi in columns 0-31, P mid in 32-63
+            auto issue_pv = [&](int j) {   // O += P_j V_j, P_j in buffer j % kBufs
+                const uint32_t vb = sbase + SM::v_off + (j % kStages) * 2 * SM::V_PART;
+                const uint32_t tp = tmem + SM::T_S + 64 * (j % kBufs);   // P hi in columns 0-31, P mid in 32-63
 #pragma unroll
                 for (int kk = 0; kk < kKeys / 16; ++kk) {
                     const uint32_t o = kk * 32;
@@ -394,8 +390,27 @@ __global__ void __launch_bounds__(224, 1) prefill_kernel(const __grid_constant__
                     tc_mma_ts(t_o, tp + kk * 8, sdesc(vb + SM::V_PART + o), ID_O, 1);                  // hi*mid
                     tc_mma_ts(t_o, tp + 32 + kk * 8, sdesc(vb + o), ID_O, 1);                          // mid*hi
                 }
-                tc_commit(&p_free[b]);
-                tc_commit(&v_empty[s]);
+                tc_commit(&p_free[j % kBufs]);
+            };
+            for (int j = 0; ok && j < 2 && j < n_tiles; ++j) {
+                ok = bounded_wait(&k_full[j % kStages], (j / kStages) & 1);
+                if (ok) issue_s(j);
+            }
+            // One wait point per tile: the first mbarrier access after a burst
+            // of MMAs waits for the burst to drain from the issue queue, so
+            // every wait of an iteration is taken at once, then S two tiles
+            // ahead and O for this tile are issued back to back.
+            for (int j = 0; ok && j < n_tiles; ++j) {
+                const int j2 = j + 2;
+                ok = bounded_wait(&p_full[j % kBufs], (j / kBufs) & 1) &&
+                     bounded_wait(&v_full[j % kStages], (j / kStages) & 1);
+                if (ok && j2 < n_tiles)
+                    ok = bounded_wait(&k_full[j2 % kStages], (j2 / kStages) & 1) &&
+                         (j2 < kBufs || bounded_wait(&p_free[j2 % kBufs], ((j2 / kBufs) - 1) & 1));
+                if (!ok) break;
+                tc_fence_after();
+                if (j2 < n_tiles) issue_s(j2);
+                issue_pv(j);
             }
             // tensor memory is released below only after every MMA issued here is done
             tc_commit(mma_drained);
