@@ -58,7 +58,7 @@ constexpr int kMaxRanks = 8;
 struct PrefillParams {
     PagedKv kv;                // the layer (unsharded)
     void *split;               // K/V operand tiles: [G][tiles][tile bytes]
-    int tiles;                 // capacity of `split` per KV head, in 64-key tiles
+    int tiles;                 // capacity of `split` per KV head, in tiles of prefill_tile_keys() keys
     const float *q;            // [n][H*D] pre-RoPE
     float *out;                // [n][H*D]
     const float2 *rope;

@@ -14,35 +14,37 @@
 // tf32 MMAs would cost twice that).
 //
 // Data path.
-//   kv_split_kernel   converts this layer's K (as [key][d]) and V (transposed,
-//                     [d][key]) for positions 0..pos0+n-1, 64 keys per tile,
-//                     into hi/mid bf16 tiles laid out in global memory exactly
-//                     as the MMA reads them from shared memory (K-major,
-//                     128-byte swizzle), so the attention kernel fetches a
-//                     tile with plain bulk copies. Keys past the last position
-//                     are zero, so they never reach an output through 0 * NaN.
+//   kv_split_kernel   converts this layer's K and V for positions
+//                     0..pos0+n-1, 128 keys per tile, into hi/mid bf16 operand
+//                     images laid out in global memory exactly as the MMA
+//                     reads them from shared memory (K-major, 128-byte
+//                     swizzle): per tile, K as d/64 chunks [128 keys][64 d]
+//                     and V^T as two chunks [d][64 keys], so the attention
+//                     kernel fetches each with one bulk copy. Keys past the
+//                     last position are zero, so they never reach an output
+//                     through 0 * NaN.
 //   prefill_kernel    one CTA per (128-row query tile, query head):
 //     warps 0-3   softmax: thread t owns query row t. Prologue: RoPE of its q
-//                 row, scale by log2(e)/sqrt(d), hi/mid split into the Q
-//                 operand. Per key tile: S row from tensor memory, causal
-//                 mask, online softmax with a lazily moved reference maximum
-//                 (O in tensor memory is rescaled only when a score exceeds
-//                 the reference by 2^8), P split into the P operand.
-//                 Epilogue: O / l to global memory.
-//     warps 4, 6  producers: K hi/mid and V^T hi/mid of a tile in separate
-//                 three-stage rings (a K stage frees as soon as its S is
-//                 done), bulk copies completing on mbarriers.
-//     warp 5      allocates tensor memory; one lane issues the MMAs:
-//                 S[j%4] = Q K_j^T (128 x 64), then O += P_j V_j (128 x d),
-//                 issuing S for tile j+2 together with O for tile j after a
-//                 single wait point per tile, so that the softmax of tiles
-//                 j+1, j+2 overlaps them. Two tcgen05.commits per tile
-//                 signal completion to the softmax warps and free K/V
-//                 stages and S buffers.
-//   Tensor memory: Q hi/mid (the A operand of S = Q K^T), four S buffers (64
-//   columns each; a tile's P hi/mid, the A operand of O += P V, overwrites
-//   its S) and O (d columns): 512 columns. Only K and V^T are read from
-//   shared memory, which halves the operand traffic per MMA.
+//                 row, scale by log2(e)/sqrt(d), hi/mid split into tensor
+//                 memory (the A operand of S = Q K^T). Per key tile: S row
+//                 from tensor memory, causal mask, online softmax with a
+//                 lazily moved reference maximum (O in tensor memory is
+//                 rescaled only when a score exceeds the reference by 2^8),
+//                 P hi/mid written over the tile's S (the A operand of
+//                 O += P V). Epilogue: O / l to global memory.
+//     warp 4      producer: the operand chunks of every MMA group, in the
+//                 order the MMAs consume them, into a three-stage ring of
+//                 bulk copies completing on mbarriers.
+//     warp 5      allocates tensor memory; one lane issues the MMAs in the
+//                 order S_0, S_1, O+=P_0V_0, S_2, O+=P_1V_1, S_3, ...:
+//                 S_j = Q K_j^T (128 x 128) into buffer j % 2, O += P_j V_j
+//                 (128 x d). Two tcgen05.commits per tile carry every
+//                 completion (softmax, ring stages, buffer reuse).
+//   Tensor memory (512 columns): Q hi/mid, S/P buffers 0 and 1, O.
+//   MMA issue is the limit of this kernel, so the design keeps the MMA
+//   thread's work minimal: 48 MMAs of N = 128 per 128 keys and two wait
+//   points (its first mbarrier access after a burst of MMAs waits for the
+//   burst to leave the issue queue, so every such access costs pipe time).
 // Every mbarrier wait is bounded (2 s), after which the CTA records an error
 // and drains out; tensor memory is always released.
 
@@ -55,9 +57,8 @@ namespace kore {
 namespace {
 
 constexpr int kRows = 128;        // query rows per CTA (TMEM lanes)
-constexpr int kKeys = 64;         // keys per tile
-constexpr int kStages = 3;        // K and V ring stages
-constexpr int kBufs = 4;          // S/P buffers in tensor memory
+constexpr int kKeys = 128;        // keys per tile
+constexpr int kStages = 3;        // operand ring stages (one MMA group each)
 constexpr float kRescale = 8.0f;  // log2-domain slack before O is rescaled
 constexpr unsigned FULLMASK = 0xffffffffu;
 
@@ -71,7 +72,9 @@ __device__ __forceinline__ uint32_t sw128(int r, int c) {
 }
 
 // Shared-memory matrix descriptor: K-major, 128-byte swizzle, 8-row groups
-// 1024 bytes apart (stride byte offset), Blackwell descriptor version 1.
+// 1024 bytes apart (stride byte offset), Blackwell descriptor version 1. The
+// start address is its low 14 bits (address / 16), so adding offset / 16 to
+// a descriptor moves its start within shared memory.
 __device__ __forceinline__ uint64_t sdesc(uint32_t saddr) {
     return (uint64_t)((saddr >> 4) & 0x3FFF) | ((uint64_t)1 << 16) | ((uint64_t)(1024 >> 4) << 32) |
            ((uint64_t)1 << 46) | ((uint64_t)2 << 61);
@@ -84,20 +87,22 @@ __host__ __device__ constexpr uint32_t idesc_bf16(int M, int N) {
 
 template <int D>
 struct PrefillSmem {
-    static constexpr int QATOMS = D / 64;                                // 64-element K atoms of K
-    static constexpr uint32_t K_PART = (uint32_t)QATOMS * kKeys * 128;   // one of hi/mid
-    static constexpr uint32_t V_PART = (uint32_t)D * 128;                // V^T: d rows x 64 keys
-    static constexpr uint32_t TILE = 2 * K_PART + 2 * V_PART;            // one global tile: K half, V half
-    static constexpr uint32_t k_off = 0;                                 // K ring: kStages x (hi, mid)
-    static constexpr uint32_t v_off = k_off + kStages * 2 * K_PART;      // V ring: kStages x (hi, mid)
-    static constexpr uint32_t bar_off = v_off + kStages * 2 * V_PART;
+    static constexpr int QATOMS = D / 64;                       // 64-element K atoms of d
+    static constexpr uint32_t KCH = (uint32_t)kKeys * 128 * 2;   // K chunk: [128 keys][64 d] hi, then mid
+    static constexpr uint32_t VCH = (uint32_t)D * 128 * 2;       // V^T chunk: [d][64 keys] hi, then mid
+    static constexpr uint32_t K_BYTES = QATOMS * KCH;            // all K chunks of a tile
+    static constexpr uint32_t V_BYTES = 2 * VCH;                 // both V^T chunks of a tile
+    static constexpr uint32_t TILE = K_BYTES + V_BYTES;          // one global tile
+    static constexpr uint32_t STAGE = K_BYTES > V_BYTES ? K_BYTES : V_BYTES;
+    static constexpr uint32_t ring_off = 0;
+    static constexpr uint32_t bar_off = ring_off + kStages * STAGE;
     // barriers, TMEM base, alignment slack; at least 116 KB so that one CTA
     // holds an SM (a second would only wait in tcgen05.alloc for the 512
     // tensor-memory columns the first holds)
     static constexpr uint32_t bytes = bar_off + 512 + 1024 > 116u * 1024 ? bar_off + 512 + 1024 : 116u * 1024;
-    // tensor memory columns: Q hi/mid as MMA A operand (bf16 pairs), kBufs S
-    // buffers (fp32; the tile's P hi/mid, bf16 pairs, overwrite them), O
-    static constexpr uint32_t T_Q = 0, T_S = 128, T_O = T_S + kBufs * 64;
+    // tensor memory columns: Q hi/mid (bf16 pairs), two S buffers (fp32; a
+    // tile's P hi/mid, bf16 pairs, overwrite its S), O
+    static constexpr uint32_t T_Q = 0, T_S = 128, T_O = 384;
     static constexpr uint32_t TMEM_COLS = 512;
 };
 
@@ -203,22 +208,25 @@ __device__ __forceinline__ void split8(const float *x, uint4 &hi, uint4 &mid) {
 
 // ---------------------------------------------------------------- K/V split pre-pass
 
-// One CTA per (64-key tile, KV head): gathers the tile's K and V rows from the
-// paged pool and writes the four operand images (K hi, K mid, V^T hi, V^T
-// mid) of the tile to split + (g * tiles + j) * TILE.
+// One CTA per (128-key tile, KV head, half of the tile's keys): gathers 64
+// keys' K and V rows from the paged pool and writes their part of the tile's
+// operand images at split + (g * tiles + j) * TILE: rows 64*half.. of every K
+// chunk, and V^T chunk `half`.
 template <int D>
 __global__ void __launch_bounds__(256) kv_split_kernel(const __grid_constant__ PrefillParams p) {
     using SM = PrefillSmem<D>;
-    __shared__ float vs[kKeys][D + 1];
-    const int j = blockIdx.x, g = blockIdx.y, tid = threadIdx.x;
+    constexpr int HK = kKeys / 2;   // keys per CTA
+    __shared__ float vs[HK][D + 1];
+    const int j = blockIdx.x, g = blockIdx.y, half = blockIdx.z, tid = threadIdx.x;
     const PagedKv &kv = p.kv;
     const int n_keys = p.pos0 + p.n;
     const int *pt = kv.page_table + (size_t)p.seq * kv.pt_stride;
     uint8_t *tile = reinterpret_cast<uint8_t *>(p.split) + ((size_t)g * p.tiles + j) * SM::TILE;
     constexpr int CH = D / 8;   // 16-byte bf16 chunks per K row
-    // K: row = key, 8 d values per chunk; V rows staged in shared memory
-    for (int w = tid; w < kKeys * CH; w += blockDim.x) {
-        const int r = w / CH, c = w - r * CH;
+    // K: row = key, 8 d values per 16-byte chunk; V rows staged in shared memory
+    for (int w = tid; w < HK * CH; w += blockDim.x) {
+        const int rl = w / CH, c = w - rl * CH;
+        const int r = half * HK + rl;   // row within the tile
         const int key = j * kKeys + r;
         float x[8] = {0, 0, 0, 0, 0, 0, 0, 0}, y[8] = {0, 0, 0, 0, 0, 0, 0, 0};
         if (key < n_keys) {
@@ -236,15 +244,16 @@ __global__ void __launch_bounds__(256) kv_split_kernel(const __grid_constant__ P
             y[0] = e.x; y[1] = e.y; y[2] = e.z; y[3] = e.w; y[4] = f.x; y[5] = f.y; y[6] = f.z; y[7] = f.w;
         }
 #pragma unroll
-        for (int i = 0; i < 8; ++i) vs[r][c * 8 + i] = y[i];
+        for (int i = 0; i < 8; ++i) vs[rl][c * 8 + i] = y[i];
         uint4 hi, mid;
         split8(x, hi, mid);
-        const uint32_t off = (uint32_t)(c >> 3) * (kKeys * 128) + sw128(r, c & 7);
+        const uint32_t off = (uint32_t)(c >> 3) * SM::KCH + sw128(r, c & 7);
         *reinterpret_cast<uint4 *>(tile + off) = hi;
-        *reinterpret_cast<uint4 *>(tile + SM::K_PART + off) = mid;
+        *reinterpret_cast<uint4 *>(tile + off + SM::KCH / 2) = mid;
     }
     __syncthreads();
-    // V^T: row = d, 8 keys per chunk
+    // V^T chunk `half`: row = d, 8 keys per 16-byte chunk
+    uint8_t *vch = tile + SM::K_BYTES + half * SM::VCH;
     for (int w = tid; w < D * 8; w += blockDim.x) {
         const int r = w >> 3, c = w & 7;
         float x[8];
@@ -252,43 +261,42 @@ __global__ void __launch_bounds__(256) kv_split_kernel(const __grid_constant__ P
         for (int i = 0; i < 8; ++i) x[i] = vs[c * 8 + i][r];
         uint4 hi, mid;
         split8(x, hi, mid);
-        const uint32_t off = 2 * SM::K_PART + sw128(r, c);
-        *reinterpret_cast<uint4 *>(tile + off) = hi;
-        *reinterpret_cast<uint4 *>(tile + SM::V_PART + off) = mid;
+        const uint32_t off = sw128(r, c);
+        *reinterpret_cast<uint4 *>(vch + off) = hi;
+        *reinterpret_cast<uint4 *>(vch + SM::VCH / 2 + off) = mid;
     }
 }
 
 // ---------------------------------------------------------------- attention
 
 template <int D>
-__global__ void __launch_bounds__(224, 1) prefill_kernel(const __grid_constant__ PrefillParams p) {
+__global__ void __launch_bounds__(192, 1) prefill_kernel(const __grid_constant__ PrefillParams p) {
     using SM = PrefillSmem<D>;
     constexpr int HALF = D / 2;
     extern __shared__ uint8_t smem_raw[];
     uint8_t *smem = reinterpret_cast<uint8_t *>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~(uintptr_t)1023);
     const uint32_t sbase = smem_u32(smem);
     uint64_t *bars = reinterpret_cast<uint64_t *>(smem + SM::bar_off);
-    // Two commits per tile carry every completion (each commit and each
-    // mbarrier access of the MMA thread costs tensor-pipe time):
-    //   s_full[j % 4]  after S_j = Q K_j^T: the softmax may read S_j, and the
-    //                  K stage of tile j may take tile j + 3;
-    //   p_free[j % 4]  after O += P_j V_j: S buffer j % 4 may take S_{j+4},
-    //                  the V stage of tile j may take tile j + 3, and O holds
-    //                  every tile up to j.
+    // MMA groups run in the order S_0, S_1, then for j = 0..n_tiles-1:
+    // O += P_j V_j, S_{j+2} (while j + 2 < n_tiles); group i's operands sit in
+    // ring stage i % 3. Two commits per tile carry every completion:
+    //   s_full[j % 2]   after S_j: the softmax may read S_j; its ring stage
+    //                   is free;
+    //   pv_done[j % 2]  after O += P_j V_j: S buffer j % 2 may take S_{j+2},
+    //                   O holds every tile up to j; its ring stage is free.
     // A parity wait is exact only within one phase of the barrier's count.
-    // Every wait below is: each waiter has already seen the completion four
-    // tiles earlier on the same barrier (or it is the first), and the
-    // completion four tiles later needs something the waiter has not done
-    // yet (the next K or V tile, or the next P).
-    uint64_t *k_full = bars;               // [3] K producer -> MMA
-    uint64_t *v_full = bars + 3;           // [3] V producer -> MMA
-    uint64_t *s_full = bars + 6;           // [4]
-    uint64_t *p_free = bars + 10;          // [4]
-    uint64_t *p_full = bars + 14;          // [4] softmax (4 warps) -> MMA: P of a buffer written
-    uint64_t *q_ready = bars + 18;         // softmax (4 warps) -> MMA
-    uint64_t *mma_drained = bars + 19;     // MMA commit -> MMA issuer, before TMEM is freed
-    uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(bars + 20);
-    int *abort_flag = reinterpret_cast<int *>(bars + 21);
+    // Each wait below is: its waiter has already seen (or ordered after)
+    // the completion two uses earlier on the same barrier, and the one two
+    // uses later needs something the waiter has not done yet (the next
+    // stage's operands, the next P, or the next S it issues itself).
+    uint64_t *full = bars;              // [3] producer -> MMA: a group's operands landed
+    uint64_t *s_full = bars + 3;        // [2]
+    uint64_t *pv_done = bars + 5;       // [2]
+    uint64_t *p_full = bars + 7;        // [2] softmax (4 warps) -> MMA: P_j written
+    uint64_t *q_ready = bars + 9;       // softmax (4 warps) -> MMA
+    uint64_t *mma_drained = bars + 10;  // MMA commit -> MMA issuer, before TMEM is freed
+    uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(bars + 11);
+    int *abort_flag = reinterpret_cast<int *>(bars + 12);
 
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int qt = gridDim.x - 1 - blockIdx.x;   // heaviest (last) query tiles first
@@ -301,13 +309,10 @@ __global__ void __launch_bounds__(224, 1) prefill_kernel(const __grid_constant__
     const int first_masked = (p.pos0 + z0) / kKeys;              // tiles from here need the mask
 
     if (threadIdx.x == 0) {
-        for (int i = 0; i < kStages; ++i) {
-            mbar_init(&k_full[i], 1);
-            mbar_init(&v_full[i], 1);
-        }
-        for (int i = 0; i < kBufs; ++i) {
+        for (int i = 0; i < kStages; ++i) mbar_init(&full[i], 1);
+        for (int i = 0; i < 2; ++i) {
             mbar_init(&s_full[i], 1);
-            mbar_init(&p_free[i], 1);
+            mbar_init(&pv_done[i], 1);
             mbar_init(&p_full[i], 4);
         }
         mbar_init(q_ready, 4);
@@ -325,7 +330,7 @@ __global__ void __launch_bounds__(224, 1) prefill_kernel(const __grid_constant__
     __syncthreads();
     tc_fence_after();
     const uint32_t tmem = *tmem_slot;
-    const uint32_t t_q = tmem + SM::T_Q, t_o = tmem + SM::T_O;   // S buffer b at tmem + T_S + 64 * b
+    const uint32_t t_q = tmem + SM::T_Q, t_o = tmem + SM::T_O;   // S buffer b at tmem + T_S + 128 * b
 
     // a completed phase costs one try_wait; the abort flag is read only on
     // the slow path
@@ -337,86 +342,96 @@ __global__ void __launch_bounds__(224, 1) prefill_kernel(const __grid_constant__
         return false;
     };
 
-    if (warp == 4 || warp == 6) {
-        // ------------------------------------------------------------ producers
-        // warp 4 streams the K halves of the tiles, warp 6 the V^T halves: a K
-        // stage is free again once its S = Q K^T is done, long before the P.V
-        // that frees a V stage, so K runs ahead of V
+    if (warp == 4) {
+        // ------------------------------------------------------------ producer
         if (lane == 0) {
-            const bool is_k = warp == 4;
-            const uint32_t half = is_k ? 2 * SM::K_PART : 2 * SM::V_PART;
-            uint64_t *full = is_k ? k_full : v_full;
-            uint64_t *done = is_k ? s_full : p_free;   // tile j - kStages no longer needs the stage
-            const uint8_t *src0 = reinterpret_cast<const uint8_t *>(p.split) + (size_t)g * p.tiles * SM::TILE +
-                                  (is_k ? 0 : 2 * SM::K_PART);
-            uint8_t *ring = smem + (is_k ? SM::k_off : SM::v_off);
-            for (int j = 0; j < n_tiles; ++j) {
-                const int s = j % kStages;
-                const int jp = j - kStages;
-                if (jp >= 0 && !bounded_wait(&done[jp % kBufs], (jp / kBufs) & 1)) break;
-                uint8_t *dst = ring + s * half;
-                mbar_arrive_expect_tx(&full[s], half);
-#pragma unroll
-                for (int part = 0; part < 2; ++part)   // kept in L2: every query tile and head reads it
-                    bulk_g2s_plain(dst + part * (half / 2), src0 + (size_t)j * SM::TILE + part * (half / 2), half / 2,
-                                   &full[s]);
-            }
+            const uint8_t *src0 = reinterpret_cast<const uint8_t *>(p.split) + (size_t)g * p.tiles * SM::TILE;
+            int gi = 0;
+            int h0 = 0, h1 = 0, h2 = 0;   // the last three groups, as 2 * tile + (1 for S, 0 for O)
+            auto load = [&](bool is_s, int j) -> bool {
+                const int st = gi % kStages;
+                if (gi >= kStages) {   // the group that used this stage is done
+                    const int jj = h0 >> 1;
+                    uint64_t *bar = (h0 & 1) ? &s_full[jj & 1] : &pv_done[jj & 1];
+                    if (!bounded_wait(bar, (jj >> 1) & 1)) return false;
+                }
+                h0 = h1;
+                h1 = h2;
+                h2 = 2 * j + (is_s ? 1 : 0);
+                const uint32_t bytes = is_s ? SM::K_BYTES : SM::V_BYTES;
+                uint8_t *dst = smem + SM::ring_off + st * SM::STAGE;
+                const uint8_t *src = src0 + (size_t)j * SM::TILE + (is_s ? 0 : SM::K_BYTES);
+                mbar_arrive_expect_tx(&full[st], bytes);
+                for (uint32_t o = 0; o < bytes; o += 16384)   // kept in L2: every query tile and head reads it
+                    bulk_g2s_plain(dst + o, src + o, 16384, &full[st]);
+                ++gi;
+                return true;
+            };
+            bool ok = load(true, 0) && (n_tiles < 2 || load(true, 1));
+            for (int j = 0; ok && j < n_tiles; ++j) ok = load(false, j) && (j + 2 >= n_tiles || load(true, j + 2));
         }
     } else if (warp == 5) {
         // ------------------------------------------------------------ MMA issuer
         if (lane == 0) {
             constexpr uint32_t ID_S = idesc_bf16(kRows, kKeys), ID_O = idesc_bf16(kRows, D);
-            bool ok = bounded_wait(q_ready, 0);
-            tc_fence_after();
-            auto issue_s = [&](int j) {   // S_j = Q K_j^T into buffer j % kBufs
-                const uint32_t kb = sbase + SM::k_off + (j % kStages) * 2 * SM::K_PART;
-                const uint32_t ts = tmem + SM::T_S + 64 * (j % kBufs);
+            int gi = 0;
+            auto wait_full = [&]() { return bounded_wait(&full[gi % kStages], (gi / kStages) & 1); };
+            auto issue_s = [&](int j) {   // S_j = Q K_j^T into buffer j % 2
+                const uint64_t kd = sdesc(sbase + SM::ring_off + (gi % kStages) * SM::STAGE);
+                const uint32_t ts = tmem + SM::T_S + 128 * (j & 1);
 #pragma unroll
                 for (int kk = 0; kk < D / 16; ++kk) {
-                    const uint32_t ko = (kk >> 2) * (kKeys * 128) + (kk & 3) * 32;
-                    tc_mma_ts(ts, t_q + kk * 8, sdesc(kb + ko), ID_S, kk > 0);                        // hi*hi
-                    tc_mma_ts(ts, t_q + kk * 8, sdesc(kb + SM::K_PART + ko), ID_S, 1);                // hi*mid
-                    tc_mma_ts(ts, t_q + HALF + kk * 8, sdesc(kb + ko), ID_S, 1);                      // mid*hi
+                    constexpr uint32_t MID = SM::KCH / 2 / 16;
+                    const uint32_t o = ((kk >> 2) * SM::KCH + (kk & 3) * 32) / 16;
+                    tc_mma_ts(ts, t_q + kk * 8, kd + o, ID_S, kk > 0);                 // hi*hi
+                    tc_mma_ts(ts, t_q + kk * 8, kd + o + MID, ID_S, 1);                // hi*mid
+                    tc_mma_ts(ts, t_q + HALF + kk * 8, kd + o, ID_S, 1);               // mid*hi
                 }
-                tc_commit(&s_full[j % kBufs]);
+                tc_commit(&s_full[j & 1]);
+                ++gi;
             };
-            auto issue_pv = [&](int j) {   // O += P_j V_j, P_j in buffer j % kBufs
-                const uint32_t vb = sbase + SM::v_off + (j % kStages) * 2 * SM::V_PART;
-                const uint32_t tp = tmem + SM::T_S + 64 * (j % kBufs);   // P hi in columns 0-31, P mid in 32-63
+            auto issue_pv = [&](int j) {   // O += P_j V_j, P_j in buffer j % 2
+                const uint64_t vd = sdesc(sbase + SM::ring_off + (gi % kStages) * SM::STAGE);
+                // P of keys 16kk..16kk+15: hi in columns 16kk..+7, mid in 16kk+8..+15
+                const uint32_t tp = tmem + SM::T_S + 128 * (j & 1);
 #pragma unroll
                 for (int kk = 0; kk < kKeys / 16; ++kk) {
-                    const uint32_t o = kk * 32;
-                    tc_mma_ts(t_o, tp + kk * 8, sdesc(vb + o), ID_O, (j > 0 || kk > 0));               // hi*hi
-                    tc_mma_ts(t_o, tp + kk * 8, sdesc(vb + SM::V_PART + o), ID_O, 1);                  // hi*mid
-                    tc_mma_ts(t_o, tp + 32 + kk * 8, sdesc(vb + o), ID_O, 1);                          // mid*hi
+                    constexpr uint32_t MID = SM::VCH / 2 / 16;
+                    const uint32_t o = ((kk >> 2) * SM::VCH + (kk & 3) * 32) / 16;
+                    tc_mma_ts(t_o, tp + 16 * kk, vd + o, ID_O, (j > 0 || kk > 0));    // hi*hi
+                    tc_mma_ts(t_o, tp + 16 * kk, vd + o + MID, ID_O, 1);               // hi*mid
+                    tc_mma_ts(t_o, tp + 16 * kk + 8, vd + o, ID_O, 1);                 // mid*hi
                 }
-                tc_commit(&p_free[j % kBufs]);
+                tc_commit(&pv_done[j & 1]);
+                ++gi;
             };
-            for (int j = 0; ok && j < 2 && j < n_tiles; ++j) {
-                ok = bounded_wait(&k_full[j % kStages], (j / kStages) & 1);
-                if (ok) issue_s(j);
+            bool ok = bounded_wait(q_ready, 0) && wait_full();
+            if (ok) {
+                tc_fence_after();
+                issue_s(0);
             }
-            // One wait point per tile: the first mbarrier access after a burst
-            // of MMAs waits for the burst to drain from the issue queue, so
-            // every wait of an iteration is taken at once, then S two tiles
-            // ahead and O for this tile are issued back to back.
+            if (ok && n_tiles > 1) {
+                ok = wait_full();
+                if (ok) issue_s(1);
+            }
             for (int j = 0; ok && j < n_tiles; ++j) {
-                const int j2 = j + 2;
-                ok = bounded_wait(&p_full[j % kBufs], (j / kBufs) & 1) &&
-                     bounded_wait(&v_full[j % kStages], (j / kStages) & 1);
-                if (ok && j2 < n_tiles)
-                    ok = bounded_wait(&k_full[j2 % kStages], (j2 / kStages) & 1) &&
-                         (j2 < kBufs || bounded_wait(&p_free[j2 % kBufs], ((j2 / kBufs) - 1) & 1));
+                ok = bounded_wait(&p_full[j & 1], (j >> 1) & 1) && wait_full();
                 if (!ok) break;
                 tc_fence_after();
-                if (j2 < n_tiles) issue_s(j2);
                 issue_pv(j);
+                if (j + 2 < n_tiles) {
+                    // buffer j % 2 takes S_{j+2} only once O += P_j V_j has read it
+                    ok = bounded_wait(&pv_done[j & 1], (j >> 1) & 1) && wait_full();
+                    if (!ok) break;
+                    tc_fence_after();
+                    issue_s(j + 2);
+                }
             }
             // tensor memory is released below only after every MMA issued here is done
             tc_commit(mma_drained);
             mbar_wait(mma_drained, 0, p.err, DEV_WAIT_FULL_TIMEOUT);
         }
-    } else {
+    } else if (warp < 4) {
         // ------------------------------------------------------------ softmax (warps 0-3)
         const int t = threadIdx.x;                  // query row, TMEM lane
         const int z = z0 + t;
@@ -454,53 +469,82 @@ __global__ void __launch_bounds__(224, 1) prefill_kernel(const __grid_constant__
         __syncwarp();
         if (lane == 0) mbar_arrive(q_ready);
 
+        // causal mask of 64 scores of keys key0..key0+63
+        auto mask64 = [&](float (&v)[64], int key0) {
+#pragma unroll
+            for (int i = 0; i < 64; ++i)
+                if (key0 + i > lim) v[i] = -INFINITY;
+        };
+        auto max64 = [](const float (&v)[64]) {   // a tree: 8 independent chains, then pairs
+            float m8[8];
+#pragma unroll
+            for (int c = 0; c < 8; ++c) m8[c] = v[c];
+#pragma unroll
+            for (int i = 8; i < 64; ++i) m8[i & 7] = fmaxf(m8[i & 7], v[i]);
+            return fmaxf(fmaxf(fmaxf(m8[0], m8[1]), fmaxf(m8[2], m8[3])), fmaxf(fmaxf(m8[4], m8[5]), fmaxf(m8[6], m8[7])));
+        };
+        // P of 64 keys from their scores, written over them: for each 16 keys,
+        // 8 columns of hi pairs then 8 of mid pairs; returns the sum of P
+        auto p64 = [&](float (&v)[64], uint32_t col, float m) {
+            float l8[8] = {0, 0, 0, 0, 0, 0, 0, 0};
+#pragma unroll
+            for (int i = 0; i < 64; ++i) {
+                v[i] = fast_exp2(v[i] - m);
+                l8[i & 7] += v[i];
+            }
+#pragma unroll
+            for (int s = 0; s < 2; ++s) {
+                uint32_t w[32];
+#pragma unroll
+                for (int gq = 0; gq < 2; ++gq)
+#pragma unroll
+                    for (int i = 0; i < 8; ++i) {
+                        const int k = 32 * s + 16 * gq + 2 * i;
+                        split2(v[k], v[k + 1], w[16 * gq + i], w[16 * gq + 8 + i]);
+                    }
+                tc_st32u(col + 32 * s, w);
+            }
+            return ((l8[0] + l8[1]) + (l8[2] + l8[3])) + ((l8[4] + l8[5]) + (l8[6] + l8[7]));
+        };
+
         float m_ref = -INFINITY, l = 0.f;
         bool ok = true;
         for (int j = 0; j < n_tiles; ++j) {
-            const int b = j % kBufs;
-            const uint32_t ts = tmem + SM::T_S + 64 * b + lane_off;
-            if (!bounded_wait(&s_full[b], (j / kBufs) & 1)) { ok = false; break; }
+            const int b = j & 1;
+            const uint32_t ts = tmem + SM::T_S + 128 * b + lane_off;
+            if (!bounded_wait(&s_full[b], (j >> 1) & 1)) { ok = false; break; }
             tc_fence_after();
+            const bool masked = j >= first_masked;
+            const int key0 = j * kKeys;
             float sv[64];
+            // pass 1: the row maximum over keys 0-63 (scores dropped) and
+            // 64-127 (kept for pass 2)
             tc_ld32(ts, *reinterpret_cast<float(*)[32]>(sv));
             tc_ld32(ts + 32, *reinterpret_cast<float(*)[32]>(sv + 32));
             tc_wait_ld();
-            if (j >= first_masked) {
-#pragma unroll
-                for (int i = 0; i < 64; ++i)
-                    if (j * kKeys + i > lim) sv[i] = -INFINITY;
-            }
-            // row maximum as a tree (8 independent chains, then pairs)
-            float mx8[8];
-#pragma unroll
-            for (int c = 0; c < 8; ++c) mx8[c] = sv[c];
-#pragma unroll
-            for (int i = 8; i < 64; ++i) mx8[i & 7] = fmaxf(mx8[i & 7], sv[i]);
-            const float mx = fmaxf(fmaxf(fmaxf(mx8[0], mx8[1]), fmaxf(mx8[2], mx8[3])),
-                                   fmaxf(fmaxf(mx8[4], mx8[5]), fmaxf(mx8[6], mx8[7])));
+            if (masked) mask64(sv, key0);
+            float mx = max64(sv);
+            tc_ld32(ts + 64, *reinterpret_cast<float(*)[32]>(sv));
+            tc_ld32(ts + 96, *reinterpret_cast<float(*)[32]>(sv + 32));
+            tc_wait_ld();
+            if (masked) mask64(sv, key0 + 64);
+            mx = fmaxf(mx, max64(sv));
             const bool need = mx > m_ref + kRescale;
             const bool any_need = __any_sync(FULLMASK, need);
             const float m_new = need ? mx : m_ref;
             const float alpha = fast_exp2(m_ref - m_new);   // 0 for the first tile, 1 where not needed
-            float l8[8] = {0, 0, 0, 0, 0, 0, 0, 0};
-#pragma unroll
-            for (int i = 0; i < 64; ++i) {
-                sv[i] = fast_exp2(sv[i] - m_new);
-                l8[i & 7] += sv[i];
-            }
-            l = fmaf(l, alpha, ((l8[0] + l8[1]) + (l8[2] + l8[3])) + ((l8[4] + l8[5]) + (l8[6] + l8[7])));
+            // pass 2: keys 64-127 from registers, then keys 0-63 again
+            float ls = p64(sv, ts + 64, m_new);
+            tc_ld32(ts, *reinterpret_cast<float(*)[32]>(sv));
+            tc_ld32(ts + 32, *reinterpret_cast<float(*)[32]>(sv + 32));
+            tc_wait_ld();
+            if (masked) mask64(sv, key0);
+            ls += p64(sv, ts, m_new);
+            l = fmaf(l, alpha, ls);
             m_ref = m_new;
-            // P of this tile into its own S buffer (S has been read above)
-            {
-                uint32_t hi[32], mid[32];
-#pragma unroll
-                for (int i = 0; i < 32; ++i) split2(sv[2 * i], sv[2 * i + 1], hi[i], mid[i]);
-                tc_st32u(ts, hi);
-                tc_st32u(ts + 32, mid);
-            }
             // O is stable only once the previous tile's P.V is done
             if (any_need && j > 0) {
-                if (!bounded_wait(&p_free[(j - 1) % kBufs], ((j - 1) / kBufs) & 1)) { ok = false; break; }
+                if (!bounded_wait(&pv_done[(j - 1) & 1], ((j - 1) >> 1) & 1)) { ok = false; break; }
                 tc_fence_after();
 #pragma unroll
                 for (int c0 = 0; c0 < D; c0 += 32) {
@@ -518,7 +562,7 @@ __global__ void __launch_bounds__(224, 1) prefill_kernel(const __grid_constant__
             if (lane == 0) mbar_arrive(&p_full[b]);
         }
         // epilogue: O / l
-        if (ok && n_tiles > 0 && bounded_wait(&p_free[(n_tiles - 1) % kBufs], ((n_tiles - 1) / kBufs) & 1)) {
+        if (ok && n_tiles > 0 && bounded_wait(&pv_done[(n_tiles - 1) & 1], ((n_tiles - 1) >> 1) & 1)) {
             tc_fence_after();
             const float inv = l > 0.f ? 1.f / l : 0.f;
             float *dst = p.out + ((size_t)z * p.H + h) * D;
@@ -550,7 +594,7 @@ cudaError_t launch_prefill_d(const PrefillParams &p, cudaStream_t s) {
     using SM = PrefillSmem<D>;
     const int tiles_needed = (p.pos0 + p.n + kKeys - 1) / kKeys;
     if (tiles_needed > p.tiles) return cudaErrorInvalidValue;
-    kv_split_kernel<D><<<dim3(tiles_needed, p.kv.G), 256, 0, s>>>(p);
+    kv_split_kernel<D><<<dim3(tiles_needed, p.kv.G, 2), 256, 0, s>>>(p);
     cudaError_t e = cudaGetLastError();
     if (e != cudaSuccess) return e;
     static bool configured[64] = {};
@@ -562,7 +606,7 @@ cudaError_t launch_prefill_d(const PrefillParams &p, cudaStream_t s) {
         if (dev >= 0 && dev < 64) configured[dev] = true;
     }
     const int q_tiles = (p.n + kRows - 1) / kRows;
-    prefill_kernel<D><<<dim3(q_tiles, p.H), 224, SM::bytes, s>>>(p);
+    prefill_kernel<D><<<dim3(q_tiles, p.H), 192, SM::bytes, s>>>(p);
     return cudaGetLastError();
 }
 
