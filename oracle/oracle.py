@@ -6,7 +6,10 @@ this module. It loads
 * ``oracle/_build/libkore_oracle.so`` — the C restatement of kore's attention
   (kore_attn_oracle.c), and
 * ``oracle/_ref/libkore_ref.so`` — the reference engine itself (kore.cpp,
-  compiled in place by oracle/Makefile) driven through ref_harness.cpp.
+  compiled in place by oracle/Makefile) driven through ref_harness.cpp, and
+* ``oracle/_ref/libkore_engine.so`` — the reference engine with
+  engine_harness.cpp: greedy decoding on a random-init model, by kore and by
+  kore with its attention regions on the CUDA library.
 
 Both are built by ``make -C oracle``; the reference library is optional (it
 needs the reference sources at build time) and ``ref_available()`` says
@@ -23,6 +26,7 @@ import numpy as np
 HERE = os.path.dirname(os.path.abspath(__file__))
 ORACLE_SO = os.path.join(HERE, "_build", "libkore_oracle.so")
 REF_SO = os.path.join(HERE, "_ref", "libkore_ref.so")
+ENGINE_SO = os.path.join(HERE, "_ref", "libkore_engine.so")
 
 _f32p = ctypes.POINTER(ctypes.c_float)
 _oracle = None
@@ -216,3 +220,78 @@ def seeded_inputs(seed: int, *shapes):
     """N(0,1) fp32 arrays from one numpy Generator (PCG64) seeded with `seed`."""
     g = np.random.default_rng(seed)
     return [g.standard_normal(s, dtype=np.float32) for s in shapes]
+
+
+_engine = None
+
+
+def engine_available() -> bool:
+    return os.path.exists(ENGINE_SO)
+
+
+def engine_lib():
+    global _engine
+    if _engine is None:
+        L = ctypes.CDLL(ENGINE_SO)
+        vp, ip, fp = ctypes.c_void_p, ctypes.POINTER(ctypes.c_int), ctypes.POINTER(ctypes.c_float)
+        L.keng_create.restype = vp
+        L.keng_create.argtypes = [ctypes.c_int] * 7 + [ctypes.c_ulonglong, ctypes.c_int]
+        L.keng_destroy.argtypes = [vp]
+        L.keng_error.restype = ctypes.c_char_p
+        L.keng_error.argtypes = [vp]
+        L.keng_ctx.argtypes = [vp]
+        L.keng_chunk.argtypes = [vp]
+        L.keng_generate_ref.argtypes = [vp, ip, ctypes.c_int, ctypes.c_int, ip, fp]
+        L.keng_attach_cuda.argtypes = [vp, ctypes.c_char_p, ctypes.c_int]
+        L.keng_generate_cuda.argtypes = [vp, ip, ctypes.c_int, ctypes.c_int, ip]
+        _engine = L
+    return _engine
+
+
+class GreedyEngine:
+    """A seeded random-init Qwen2-style model inside the reference engine, with
+    greedy generation by kore itself (``generate_ref``) and by kore with its
+    attention on the CUDA library (``generate_cuda``, after ``attach_cuda``)."""
+
+    def __init__(self, n_layer: int, n_embd: int, n_head: int, n_head_kv: int, n_ff: int, n_vocab: int,
+                 ctx: int, seed: int = 12345, threads: int = 0):
+        threads = threads or os.cpu_count() or 1
+        self.n_vocab = n_vocab
+        self.h = engine_lib().keng_create(n_layer, n_embd, n_head, n_head_kv, n_ff, n_vocab, ctx, seed, threads)
+        if not self.h:
+            raise RuntimeError("kore engine_init refused the model")
+
+    def __del__(self):
+        h = getattr(self, "h", None)
+        if h:
+            engine_lib().keng_destroy(h)
+            self.h = None
+
+    @property
+    def chunk(self) -> int:
+        return engine_lib().keng_chunk(self.h)
+
+    def _err(self) -> str:
+        return engine_lib().keng_error(self.h).decode()
+
+    def generate_ref(self, prompt, n_gen: int):
+        p = np.ascontiguousarray(prompt, np.int32)
+        ids = np.zeros(n_gen, np.int32)
+        margins = np.zeros(n_gen, np.float32)
+        ip = ctypes.POINTER(ctypes.c_int)
+        if engine_lib().keng_generate_ref(self.h, p.ctypes.data_as(ip), len(p), n_gen, ids.ctypes.data_as(ip),
+                                          _fp(margins)) != n_gen:
+            raise RuntimeError(self._err())
+        return ids, margins
+
+    def attach_cuda(self, lib_path: str, device: int = 0) -> None:
+        if engine_lib().keng_attach_cuda(self.h, lib_path.encode(), device):
+            raise RuntimeError(self._err())
+
+    def generate_cuda(self, prompt, n_gen: int):
+        p = np.ascontiguousarray(prompt, np.int32)
+        ids = np.zeros(n_gen, np.int32)
+        ip = ctypes.POINTER(ctypes.c_int)
+        if engine_lib().keng_generate_cuda(self.h, p.ctypes.data_as(ip), len(p), n_gen, ids.ctypes.data_as(ip)) != n_gen:
+            raise RuntimeError(self._err())
+        return ids
