@@ -291,6 +291,26 @@ __global__ void __launch_bounds__(NW * 32, 1) attn_decode_kernel(const __grid_co
     // at once, so at most the previous decode and its merge can still run
     if (p.prefetch_ok && lane == 0)
         for (int j = 0; j < SPW && j < my_tiles; ++j) issue(j);
+    // and the positions after those first ring stages, up to the host's L2
+    // budget, are asked into L2: HBM keeps streaming this layer's K/V while
+    // the preceding kernels (the last layer's merge or exchange) finish
+    if (p.prefetch_ok && tid == NT - 1 && p.l2_prefetch_tokens > 0) {
+        const int a = min(u_end, u_begin + SPW * NW * TT);
+        const int b = min(u_end, u_begin + p.l2_prefetch_tokens);
+        for (int u = a; u < b;) {
+            const int lp = u / P, off = u - lp * P;
+            const int n = min(b - u, P - off);   // within one page
+            const int pj = min(lp - lp_first, kSplitPagesMax - 1);
+            const char *src = reinterpret_cast<const char *>(kbase + ((size_t)pages[pj] * kv.G * P + off) * D);
+            const uint32_t bytes = (uint32_t)n * D * 4;
+            for (uint32_t o = 0; o < bytes; o += 65536u) {
+                const uint32_t c = min(65536u, bytes - o);
+                bulk_prefetch_l2(src + o, c);
+                bulk_prefetch_l2(src + (size_t)kv.v_off * 4 + o, c);
+            }
+            u += n;
+        }
+    }
     grid_dep_wait();
     grid_dep_launch();
     if (!p.prefetch_ok && lane == 0)
@@ -655,6 +675,7 @@ extern "C" int kore_cuda_attn_decode_noalloc(const kore_cuda_kv_view *kv, int po
     p.seq0 = 0;
     p.pos0 = pos;
     p.prefetch_ok = 0;   // nothing is known about the previous kernel on the caller's stream
+    p.l2_prefetch_tokens = 0;
     const cudaError_t e = launch_attn_decode(p, R, grid_x, static_cast<cudaStream_t>(stream));
     if (e != cudaSuccess) return noalloc_fail(KORE_CUDA_ECUDA, "decode launch failed (error %lld)", (long long)e);
     return KORE_CUDA_OK;

@@ -27,6 +27,10 @@ struct kore_cuda_ctx {
     int pages_per_seq = 0;      // local page-table stride
     int n_pages = 0;
     int num_sms = 148;
+    // L2 budget of the decode's early fetch (KORE_CUDA_L2_PREFETCH_MB). Off by
+    // default: on B200 it measured slower at 32 and 64 MB, on one GPU and on
+    // two (the prefetched lines did not outlive their wait)
+    long long l2_prefetch_bytes = 0;
     cudaStream_t stream = nullptr;
     bool own_stream = false;
     float *kv = nullptr;        // [n_layer][2][n_pages][G][P][D]
@@ -294,6 +298,12 @@ int run_decode(kore_cuda_ctx *c, int layer, int n_q, bool contiguous, int seq0, 
     p.split_tokens = (int)st;
     p.max_splits = grid_x;
     p.prefetch_ok = c->last_kv_layer != layer;
+    if (p.prefetch_ok && c->l2_prefetch_bytes > 0) {
+        // L2 budget of the early fetch over all CTAs of the launch (a part of
+        // the 126 MB L2, so that the prefetched lines outlive their wait)
+        const long long per_token = (long long)n_q * c->G * grid_x * 2 * c->D * 4;
+        p.l2_prefetch_tokens = (int)std::min<long long>(st, c->l2_prefetch_bytes / per_token / TT * TT);
+    }
     CK(launch_attn_decode(p, c->R, grid_x, c->stream, launch_merge));
     if (grid_out) *grid_out = grid_x;
     // the decode (and its split merge, which lets the next kernel start at
@@ -396,6 +406,7 @@ int kore_cuda_create(kore_cuda_ctx **out, const kore_cuda_cfg *cfg) {
         if (rc_) return bail(rc_);                                                                 \
     } while (0)
     CKB(cudaDeviceGetAttribute(&c->num_sms, cudaDevAttrMultiProcessorCount, f.device));
+    if (const char *mb = getenv("KORE_CUDA_L2_PREFETCH_MB")) c->l2_prefetch_bytes = std::max(0ll, atoll(mb)) << 20;
     CKB(cudaStreamCreateWithFlags(&c->stream, cudaStreamNonBlocking));
     c->own_stream = true;
 

@@ -125,6 +125,12 @@ __device__ __forceinline__ void bulk_g2s_plain(void *dst, const void *src, uint3
                  : "memory");
 }
 
+// Asks L2 to fetch [src, src + bytes) from HBM, with no destination and no
+// completion to wait for (16-byte aligned address, size a multiple of 16).
+__device__ __forceinline__ void bulk_prefetch_l2(const void *src, uint32_t bytes) {
+    asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(src), "r"(bytes) : "memory");
+}
+
 // ---------------------------------------------------------------- math
 
 __device__ __forceinline__ float fast_exp2(float x) {
