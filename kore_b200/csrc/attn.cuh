@@ -81,7 +81,7 @@ struct ExchangeParams {
     int n_splits, max_splits, n_rep;
     float *own;                    // this rank's exchange buffer
     float *peers[kMaxRanks];       // every rank's exchange buffer as mapped here (own included)
-    size_t flag_off, epoch_off;
+    size_t epoch_off;              // per-head epochs in `own`; the (value, epoch) slots start at 0
     float *out;                    // merged output [H*D]
     int *err;
     int n_ranks, rank, H, D;

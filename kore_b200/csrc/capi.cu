@@ -54,7 +54,11 @@ struct kore_cuda_ctx {
     int last_kv_layer = -1;     // layer whose KV the most recent kernel of this context wrote
     // cross-GPU exchange of KV-sharded partials (peer_exchange.cu)
     float *xbuf = nullptr;      // this rank's exchange buffer, shared with the peers over CUDA IPC
-    size_t x_flag_off = 0, x_epoch_off = 0, x_local_off = 0, x_bytes = 0;
+    size_t x_epoch_off = 0, x_local_off = 0, x_bytes = 0;
+    // whether the decode after a sharded decode may fetch KV while the peer
+    // exchange still runs (KORE_CUDA_SHARD_PREFETCH=0 turns it off)
+    bool shard_prefetch = true;
+    bool hold_prefetch = false;   // set: the next decode waits before its first KV fetch
     float *peers[kMaxRanks] = {};
     bool peers_open = false;
     // prefill: K/V operand tiles of the current chunk's layer (attn_prefill.cu)
@@ -297,7 +301,8 @@ int run_decode(kore_cuda_ctx *c, int layer, int n_q, bool contiguous, int seq0, 
     if (grid_x > kMaxSplits) return fail(c, KORE_CUDA_EINVAL, "too many splits for one decode launch");
     p.split_tokens = (int)st;
     p.max_splits = grid_x;
-    p.prefetch_ok = c->last_kv_layer != layer;
+    p.prefetch_ok = !c->hold_prefetch && c->last_kv_layer != layer;
+    c->hold_prefetch = false;
     if (p.prefetch_ok && c->l2_prefetch_bytes > 0) {
         // L2 budget of the early fetch over all CTAs of the launch (a part of
         // the 126 MB L2, so that the prefetched lines outlive their wait)
@@ -407,6 +412,7 @@ int kore_cuda_create(kore_cuda_ctx **out, const kore_cuda_cfg *cfg) {
     } while (0)
     CKB(cudaDeviceGetAttribute(&c->num_sms, cudaDevAttrMultiProcessorCount, f.device));
     if (const char *mb = getenv("KORE_CUDA_L2_PREFETCH_MB")) c->l2_prefetch_bytes = std::max(0ll, atoll(mb)) << 20;
+    if (const char *sp = getenv("KORE_CUDA_SHARD_PREFETCH")) c->shard_prefetch = atoi(sp) != 0;
     CKB(cudaStreamCreateWithFlags(&c->stream, cudaStreamNonBlocking));
     c->own_stream = true;
 
@@ -608,9 +614,10 @@ int kore_cuda_peer_handle(kore_cuda_ctx *c, void *handle) {
         return fail(c, KORE_CUDA_EINVAL, "peer exchange needs 2..%d shards (context has %d)", kMaxRanks, c->NS);
     DeviceGuard dg(c->cfg.device);
     if (!c->xbuf) {
+        // [2 parity sets][rank][head][head_dim + 1] (value, epoch) pairs, the
+        // per-head epochs, this rank's own partial
         const size_t PF = (size_t)c->H * c->D + c->H;
-        c->x_flag_off = align256(2 * (size_t)c->NS * PF * sizeof(float));
-        c->x_epoch_off = c->x_flag_off + align256(2 * (size_t)c->NS * c->H * sizeof(unsigned));
+        c->x_epoch_off = align256(2 * (size_t)c->NS * c->H * (c->D + 1) * 2 * sizeof(unsigned));
         c->x_local_off = c->x_epoch_off + align256((size_t)c->H * sizeof(unsigned));
         c->x_bytes = c->x_local_off + align256(PF * sizeof(float));
         CK(cudaMalloc(&c->xbuf, c->x_bytes));
@@ -668,7 +675,6 @@ int kore_cuda_attn_decode_sharded_dev(kore_cuda_ctx *c, int seq, int layer, int 
     xp.n_rep = c->R;
     xp.own = c->xbuf;
     for (int r = 0; r < c->NS; ++r) xp.peers[r] = c->peers[r];
-    xp.flag_off = c->x_flag_off;
     xp.epoch_off = c->x_epoch_off;
     xp.out = out;
     xp.err = c->err_d;
@@ -678,6 +684,7 @@ int kore_cuda_attn_decode_sharded_dev(kore_cuda_ctx *c, int seq, int layer, int 
     xp.D = c->D;
     CK(launch_peer_exchange(xp, c->stream));
     c->last_kv_layer = layer;   // the decode may still run when the next kernel starts
+    c->hold_prefetch = !c->shard_prefetch;
     return KORE_CUDA_OK;
 }
 

@@ -3,21 +3,25 @@
 //
 // A decode step on a context whose KV positions are split over N GPUs leaves
 // each rank's partial result — output normalised by its own softmax sum, and
-// the log2-domain log-sum-exp per query head — in a local buffer. Every
-// rank's exchange buffer is mapped into every other rank (CUDA IPC), so this
-// kernel, one CTA per query head:
-//   1. stores the partial into this rank's slot of every peer's buffer (plain
-//      NVLink stores, no multicast), then raises a per-(rank, head) flag there
-//      with a system-scope release;
-//   2. waits, bounded by 2 s of %globaltimer, for every peer's flag in its own
-//      buffer (system-scope acquire);
-//   3. merges the N partials: out = sum_r 2^(L_r - L) O_r, L = log2 sum 2^L_r,
+// the log2-domain log-sum-exp per query head — in a local buffer (or as the
+// decode's unmerged splits). Every rank's exchange buffer is mapped into
+// every other rank (CUDA IPC), so this kernel, one CTA per query head:
+//   1. merges this rank's splits of head h (when the decode left several);
+//   2. stores the head's partial into this rank's slot of every peer's buffer
+//      as 8-byte (value, epoch) pairs — plain NVLink stores, no multicast:
+//      each pair is written by one store, so a reader that sees the epoch
+//      sees the value with it, and no fence or flag is needed;
+//   3. polls, bounded by 2 s of %globaltimer, its own buffer until every
+//      peer's pairs for head h carry this step's epoch (system-scope relaxed
+//      8-byte loads);
+//   4. merges the N partials: out = sum_r 2^(L_r - L) O_r, L = log2 sum 2^L_r,
 //      which is kore's single softmax (kore.cpp:1437-1454) regrouped by shard.
-// The flag value is a per-head epoch kept on the device (the CTA of head h is
+// The epoch is a per-head counter kept on the device (the CTA of head h is
 // its only reader and writer), so a CUDA graph can replay the step. Two slot
 // sets, selected by the epoch's parity, stop a fast rank from overwriting a
-// slot that a peer has not read yet: it can reuse a set only after receiving
-// the peer's next partial, which the peer sends after finishing this one.
+// slot that a peer has not read yet: it writes a set again only after
+// receiving the peer's next partial, which the peer sends in a later kernel,
+// after this one's reads of that set completed.
 
 #include "attn.cuh"
 #include "common.cuh"
@@ -26,21 +30,36 @@
 namespace kore {
 namespace {
 
-__device__ __forceinline__ unsigned ld_acquire_sys(const unsigned *p) {
-    unsigned v;
-    asm volatile("ld.acquire.sys.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+__device__ __forceinline__ void st_pair_sys(uint2 *p, uint32_t value, uint32_t epoch) {
+    asm volatile("st.relaxed.sys.global.v2.b32 [%0], {%1, %2};" ::"l"(p), "r"(value), "r"(epoch) : "memory");
+}
+
+__device__ __forceinline__ uint2 ld_pair_sys(const uint2 *p) {
+    uint2 v;
+    asm volatile("ld.relaxed.sys.global.v2.b32 {%0, %1}, [%2];" : "=r"(v.x), "=r"(v.y) : "l"(p) : "memory");
     return v;
 }
 
-__device__ __forceinline__ void st_release_sys(unsigned *p, unsigned v) {
-    asm volatile("st.release.sys.global.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
+// Waits (bounded) until the pair at p carries `epoch`; returns its value.
+__device__ __forceinline__ float await_pair(const uint2 *p, uint32_t epoch, int *err) {
+    uint2 v = ld_pair_sys(p);
+    if (v.y == epoch) return __uint_as_float(v.x);
+    const uint64_t t0 = global_ns();
+    for (;;) {
+        v = ld_pair_sys(p);
+        if (v.y == epoch) return __uint_as_float(v.x);
+        if (global_ns() - t0 > kWaitNs) {
+            raise_error(err, DEV_PEER_TIMEOUT);
+            return 0.f;
+        }
+    }
 }
 
 template <int D>
 __global__ void __launch_bounds__(D) peer_exchange_kernel(const __grid_constant__ ExchangeParams p) {
     const int h = blockIdx.x, tid = threadIdx.x;
     const int N = p.n_ranks, me = p.rank, H = p.H;
-    const size_t PF = (size_t)H * D + H;
+    constexpr int SLOT = D + 1;   // pairs per (rank, head): D outputs, then the LSE
     __shared__ unsigned s_epoch;
     __shared__ float s_lse[kMaxRanks];
 
@@ -65,55 +84,43 @@ __global__ void __launch_bounds__(D) peer_exchange_kernel(const __grid_constant_
         lse_me = __ldcg(p.local + (size_t)H * D + h);
     }
 
-    // 1. push it to every peer, then raise this rank's flag there
+    // 1. push it to every peer: one 8-byte (value, epoch) store per element
     for (int r = 0; r < N; ++r) {
         if (r == me) continue;
-        float *dst = p.peers[r] + ((size_t)par * N + me) * PF;
-        dst[(size_t)h * D + tid] = o_me;
-        if (tid == 0) dst[(size_t)H * D + h] = lse_me;
-    }
-    __syncthreads();
-    if (tid == 0) {
-        __threadfence_system();
-        for (int r = 0; r < N; ++r) {
-            if (r == me) continue;
-            unsigned *flags = reinterpret_cast<unsigned *>(reinterpret_cast<char *>(p.peers[r]) + p.flag_off);
-            st_release_sys(flags + ((size_t)par * N + me) * H + h, e);
-        }
+        uint2 *dst = reinterpret_cast<uint2 *>(p.peers[r]) + (((size_t)par * N + me) * H + h) * SLOT;
+        st_pair_sys(dst + tid, __float_as_uint(o_me), e);
+        if (tid == 0) st_pair_sys(dst + D, __float_as_uint(lse_me), e);
     }
 
-    // 2. wait for every peer's partial of head h (bounded)
-    if (tid < N && tid != me) {
-        const unsigned *flag =
-            reinterpret_cast<const unsigned *>(reinterpret_cast<const char *>(p.own) + p.flag_off) +
-            ((size_t)par * N + tid) * H + h;
-        const uint64_t t0 = global_ns();
-        while ((int)(ld_acquire_sys(flag) - e) < 0) {
-            if (global_ns() - t0 > kWaitNs) {
-                raise_error(p.err, DEV_PEER_TIMEOUT);
-                break;
-            }
-            __nanosleep(64);
+    // 2. collect every peer's element tid (thread 0 also the LSEs)
+    const uint2 *own = reinterpret_cast<const uint2 *>(p.own);
+    float x[kMaxRanks];
+#pragma unroll
+    for (int r = 0; r < kMaxRanks; ++r) {
+        x[r] = 0.f;
+        if (r < N && r != me) {
+            const uint2 *src = own + (((size_t)par * N + r) * H + h) * SLOT;
+            x[r] = await_pair(src + tid, e, p.err);
+            if (tid == 0) s_lse[r] = await_pair(src + D, e, p.err);
         }
     }
+    if (tid == 0) s_lse[me] = lse_me;
     __syncthreads();
 
     // 3. merge the N partials of head h
-    if (tid < N) s_lse[tid] = tid == me ? lse_me : __ldcg(p.own + ((size_t)par * N + tid) * PF + (size_t)H * D + h);
-    __syncthreads();
     float M = -INFINITY;
     for (int r = 0; r < N; ++r) M = fmaxf(M, s_lse[r]);
     float acc = 0.f, wsum = 0.f;
     if (M != -INFINITY) {
-        for (int r = 0; r < N; ++r) {
+#pragma unroll
+        for (int r = 0; r < kMaxRanks; ++r) {
+            if (r >= N) break;
             const float w = fast_exp2(s_lse[r] - M);
             wsum += w;
-            const float x = r == me ? o_me : __ldcg(p.own + ((size_t)par * N + r) * PF + (size_t)h * D + tid);
-            acc = fmaf(w, x, acc);
+            acc = fmaf(w, r == me ? o_me : x[r], acc);
         }
     }
     p.out[(size_t)h * D + tid] = wsum > 0.f ? acc / wsum : 0.f;
-    __syncthreads();
     if (tid == 0) epochs[h] = e;
 }
 
