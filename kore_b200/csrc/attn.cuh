@@ -38,6 +38,8 @@ struct DecodeParams {
     int contiguous;            // 1: query i is (seq0, pos0 + i); 0: seq[i], pos[i]
     int prefetch_ok;           // 1: the preceding kernel in the stream wrote no KV of this layer,
                                //    so KV tiles may be fetched before waiting for it
+    int prefetch_stages;       // with prefetch_ok: ring stages per warp fetched before the wait
+                               //    (the rest right after it)
     int l2_prefetch_tokens;    // with prefetch_ok: positions of each split (from its start) that
                                //    are asked into L2 before the wait, so that HBM keeps streaming
                                //    while the preceding kernels finish

@@ -289,8 +289,9 @@ __global__ void __launch_bounds__(NW * 32, 1) attn_decode_kernel(const __grid_co
     // exchange kernel, or the next decode) start only after its own wait
     // returned, and a split-merge or exchange kernel lets the next decode start
     // at once, so at most the previous decode and its merge can still run
-    if (p.prefetch_ok && lane == 0)
-        for (int j = 0; j < SPW && j < my_tiles; ++j) issue(j);
+    const int pre = p.prefetch_ok ? min(SPW, p.prefetch_stages) : 0;
+    if (lane == 0)
+        for (int j = 0; j < pre && j < my_tiles; ++j) issue(j);
     // and the positions after those first ring stages, up to the host's L2
     // budget, are asked into L2: HBM keeps streaming this layer's K/V while
     // the preceding kernels (the last layer's merge or exchange) finish
@@ -313,8 +314,8 @@ __global__ void __launch_bounds__(NW * 32, 1) attn_decode_kernel(const __grid_co
     }
     grid_dep_wait();
     grid_dep_launch();
-    if (!p.prefetch_ok && lane == 0)
-        for (int j = 0; j < SPW && j < my_tiles; ++j) issue(j);
+    if (lane == 0)
+        for (int j = pre; j < SPW && j < my_tiles; ++j) issue(j);
 
     // q of the group, the RoPE row and the new token's k/v: loaded once per
     // CTA with 16-byte loads (every warp of every split reads the same few

@@ -59,6 +59,7 @@ struct kore_cuda_ctx {
     // exchange still runs (KORE_CUDA_SHARD_PREFETCH=0 turns it off)
     bool shard_prefetch = true;
     bool hold_prefetch = false;   // set: the next decode waits before its first KV fetch
+    int prefetch_stages = 3;      // ring stages fetched early (KORE_CUDA_PREFETCH_STAGES)
     float *peers[kMaxRanks] = {};
     bool peers_open = false;
     // prefill: K/V operand tiles of the current chunk's layer (attn_prefill.cu)
@@ -302,6 +303,7 @@ int run_decode(kore_cuda_ctx *c, int layer, int n_q, bool contiguous, int seq0, 
     p.split_tokens = (int)st;
     p.max_splits = grid_x;
     p.prefetch_ok = !c->hold_prefetch && c->last_kv_layer != layer;
+    p.prefetch_stages = c->prefetch_stages;
     c->hold_prefetch = false;
     if (p.prefetch_ok && c->l2_prefetch_bytes > 0) {
         // L2 budget of the early fetch over all CTAs of the launch (a part of
@@ -413,6 +415,7 @@ int kore_cuda_create(kore_cuda_ctx **out, const kore_cuda_cfg *cfg) {
     CKB(cudaDeviceGetAttribute(&c->num_sms, cudaDevAttrMultiProcessorCount, f.device));
     if (const char *mb = getenv("KORE_CUDA_L2_PREFETCH_MB")) c->l2_prefetch_bytes = std::max(0ll, atoll(mb)) << 20;
     if (const char *sp = getenv("KORE_CUDA_SHARD_PREFETCH")) c->shard_prefetch = atoi(sp) != 0;
+    if (const char *ps = getenv("KORE_CUDA_PREFETCH_STAGES")) c->prefetch_stages = std::max(0, atoi(ps));
     CKB(cudaStreamCreateWithFlags(&c->stream, cudaStreamNonBlocking));
     c->own_stream = true;
 

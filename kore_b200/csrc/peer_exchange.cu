@@ -64,10 +64,12 @@ __global__ void __launch_bounds__(D) peer_exchange_kernel(const __grid_constant_
     __shared__ float s_lse[kMaxRanks];
 
     grid_dep_launch();     // the next decode may prefetch KV of its own layer meanwhile
-    grid_dep_wait();       // this rank's partial is complete and visible
-
+    // the epoch of head h was last written by this CTA's predecessor, the
+    // exchange of the previous step, which finished before the decode this
+    // kernel depends on started: it can be read before the wait
     unsigned *epochs = reinterpret_cast<unsigned *>(reinterpret_cast<char *>(p.own) + p.epoch_off);
     if (tid == 0) s_epoch = epochs[h] + 1u;
+    grid_dep_wait();       // this rank's partial is complete and visible
     __syncthreads();
     const unsigned e = s_epoch;
     const int par = e & 1u;
