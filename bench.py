@@ -63,6 +63,8 @@ def parse():
     ap.add_argument("--prefill-steps", type=int, default=5)
     ap.add_argument("--prefill-layers", type=int, default=28)
     ap.add_argument("--no-prefill", action="store_true")
+    ap.add_argument("--no-batched", action="store_true", help="skip the config-5 batched decode line")
+    ap.add_argument("--batched-steps", type=int, default=20)
     ap.add_argument("--prefill-only", action="store_true", help="measure only the prefill (development)")
     a = ap.parse_args()
     global L, POS, CTX
@@ -303,6 +305,117 @@ def run_ours(args, rank: int, world: int, dist) -> dict | None:
     return line
 
 
+# config 5: Qwen2.5-3B-shaped batched decode of many independent sequences
+B_SEQS, B_LAYERS, B_H, B_G = 64, 36, 16, 2
+B_KVD = B_G * D
+
+
+def batched_lengths() -> np.ndarray:
+    """Cached positions of the 64 sequences, ~U{1024..32768}, seeded."""
+    return np.random.default_rng(5).integers(1024, 32769, B_SEQS)
+
+
+def batched_seq_bytes(length: int) -> int:
+    """Algorithmic bytes of one sequence's decode step over all layers."""
+    return B_LAYERS * (2 * (length + 1) * B_KVD * 4 + 2 * B_H * D * 4 + 2 * B_KVD * 4)
+
+
+def run_batched(args, rank: int, world: int, dist, peaks) -> dict | None:
+    """Config 5: 64 sequences of ragged length decode one token each through 36
+    layers (3B shape). The sequences are split over the GPUs longest-first
+    (kore_b200.shard.assign_sequences); each GPU holds only its sequences'
+    pages and runs one batched decode launch per layer, with no data-path
+    collective. value = all ranks' algorithmic bytes / max-over-ranks time."""
+    import torch
+    import kore_b200 as K
+    from kore_b200.shard import assign_sequences
+    dev = torch.device("cuda", int(os.environ.get("LOCAL_RANK", 0)))
+    lengths = batched_lengths()
+    mine = assign_sequences(lengths, world)[rank]
+    P = 256
+    n_pages = sum((int(lengths[i]) + 1 + P - 1) // P for i in mine)
+    ctx = K.KoreCuda(B_LAYERS, B_H, B_G, D, int(lengths.max()) + 1, max_seqs=len(mine), n_pages=n_pages,
+                     device=dev.index)
+    stream = torch.cuda.Stream(device=dev)
+    ctx.set_stream(stream.cuda_stream)
+    gen = torch.Generator(device=dev)
+    n = len(mine)
+    pos = np.array([int(lengths[i]) for i in mine], np.int32)
+    seqs = np.arange(n, dtype=np.int32)
+    with torch.cuda.stream(stream):
+        # one seeded block of rows per layer; every sequence appends its own
+        # prefix of it into its own pages
+        for layer in range(B_LAYERS):
+            gen.manual_seed(100000 + layer)
+            k = torch.randn(int(lengths.max()), B_KVD, device=dev, generator=gen)
+            v = torch.randn(int(lengths.max()), B_KVD, device=dev, generator=gen)
+            for j in range(len(mine)):
+                ctx.append_dev(j, layer, 0, int(pos[j]), k[:int(pos[j])], v[:int(pos[j])])
+            del k, v
+        gen.manual_seed(11 + rank)
+        q = torch.randn(B_LAYERS, n, B_H * D, device=dev, generator=gen)
+        kn = torch.randn(B_LAYERS, n, B_KVD, device=dev, generator=gen)
+        vn = torch.randn(B_LAYERS, n, B_KVD, device=dev, generator=gen)
+        out = torch.empty(B_LAYERS, n, B_H * D, device=dev)
+    ctx.sync()
+
+    def step():
+        for layer in range(B_LAYERS):
+            ctx.decode_batch_dev(layer, seqs, pos, q[layer], kn[layer], vn[layer], out[layer])
+
+    def barrier():
+        if dist is not None:
+            dist.barrier()
+        torch.cuda.synchronize(dev)
+
+    with torch.cuda.stream(stream):
+        for _ in range(3):
+            step()
+    ctx.sync()
+    graph = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(graph, stream=stream):
+        step()
+    with torch.cuda.stream(stream):
+        graph.replay()
+    ctx.sync()
+    steps = args.batched_steps
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    barrier()
+    with torch.cuda.stream(stream):
+        e0.record(stream)
+        for _ in range(steps):
+            graph.replay()
+        e1.record(stream)
+    e1.synchronize()
+    ms = e0.elapsed_time(e1) / steps
+    barrier()
+    t = torch.tensor([ms], device=dev, dtype=torch.float64)
+    if dist is not None:
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    ms = t.item()
+    del graph
+    ctx.close()
+    if rank != 0:
+        return None
+    total = sum(batched_seq_bytes(int(x)) for x in lengths)
+    gbs = total / (ms * 1e-3) / 1e9
+    return {
+        "metric": "batched decode attn HBM GB/s (cfg5: 3B shape, 64 sequences, 36 layers)",
+        "value": round(gbs, 1), "unit": "GB/s", "n_gpus": world, "steps": steps, "warmup": 3,
+        "ms_per_step": round(ms, 4), "higher_is_better": True, "scaling": "strong" if world > 1 else "weak",
+        "config": {"workload": "cfg5: 64 sequences, cached lengths ~U{1024..32768} (seed 5), 16Q/2KV heads, "
+                               "d128, 36 layers, 256-token pages, one token per sequence per step",
+                   "kv_bytes_per_step": int(total), "assignment": "longest-first to the least-loaded GPU",
+                   "cache": "per layer one seeded N(0,1) block; each sequence holds its prefix in its own pages",
+                   "l2": f"{total / 1e9:.0f} GB of KV per step > L2, no flush needed"},
+        "roofline": {"bound": "hbm", "achieved": round(gbs, 1), "peak": round(peaks["hbm_gbs"] * world, 1),
+                     "peak_source": peaks["source"], "unit": "GB/s",
+                     "frac": round(gbs / (peaks["hbm_gbs"] * world), 4),
+                     "note": "peak = measured HBM GB/s x GPUs"},
+        "gpu_launches": steps * B_LAYERS * 2,
+    }
+
+
 def prefill_pairs(pos0: int, n: int) -> int:
     """Unmasked (query, key) pairs of a causal chunk: sum over z of pos0 + z + 1."""
     return n * (pos0 + 1) + n * (n - 1) // 2
@@ -501,6 +614,11 @@ def main():
         return
     try:
         line = run_ours(args, rank, world, dist)
+        if not args.no_batched:
+            import torch
+            batched = run_batched(args, rank, world, dist, load_peaks())
+            if line is not None:
+                line["batched"] = batched
         if line is not None:
             print(json.dumps(line), flush=True)
     finally:
