@@ -169,6 +169,15 @@ __device__ __forceinline__ void tc_st32u(uint32_t taddr, const uint32_t (&v)[32]
         : "memory");
 }
 
+__device__ __forceinline__ void tc_st16u(uint32_t taddr, const uint32_t (&v)[16]) {
+    asm volatile(
+        "tcgen05.st.sync.aligned.32x32b.x16.b32 [%0], {%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,%16};" ::"r"(
+            taddr),
+        "r"(v[0]), "r"(v[1]), "r"(v[2]), "r"(v[3]), "r"(v[4]), "r"(v[5]), "r"(v[6]), "r"(v[7]), "r"(v[8]), "r"(v[9]),
+        "r"(v[10]), "r"(v[11]), "r"(v[12]), "r"(v[13]), "r"(v[14]), "r"(v[15])
+        : "memory");
+}
+
 // hi/mid bf16 split of 2 fp32 values, each part packed as one 32-bit word
 // (first value in the low half)
 __device__ __forceinline__ void split2(float x0, float x1, uint32_t &hi, uint32_t &mid) {
@@ -429,30 +438,46 @@ __global__ void __launch_bounds__(192, 1) prefill_kernel(const __grid_constant__
         const bool valid = t < rows;
         const int lim = p.pos0 + z;                 // last key this row attends to
         const uint32_t lane_off = (uint32_t)(warp * 32) << 16;
-        // Q row: RoPE at its position, scale, hi/mid split into tensor memory
+        // Q row: RoPE at its position, scale, hi/mid split into tensor memory.
+        // In phases of (up to) 32 rotation pairs, each issuing all its 16-byte
+        // loads (the pair's q elements and the (cos, sin) table entries) before
+        // using any, so that the row costs one memory round trip per phase
         {
-            float qv[D];
-            const float *qsrc = p.q + ((size_t)z * p.H + h) * D;
-            const float2 *cs = p.rope + (size_t)(valid ? lim : 0) * HALF;
+            constexpr int PH = HALF < 32 ? HALF : 32;
+            const float4 zero = make_float4(0.f, 0.f, 0.f, 0.f);
+            const float4 *q4 = reinterpret_cast<const float4 *>(p.q + ((size_t)z * p.H + h) * D);
+            const float4 *cs4 = reinterpret_cast<const float4 *>(p.rope + (size_t)(valid ? lim : 0) * HALF);
 #pragma unroll
-            for (int i = 0; i < D; i += 4) {
-                const float4 a = valid ? __ldg(reinterpret_cast<const float4 *>(qsrc + i)) : make_float4(0, 0, 0, 0);
-                qv[i] = a.x; qv[i + 1] = a.y; qv[i + 2] = a.z; qv[i + 3] = a.w;
-            }
+            for (int ph = 0; ph < HALF / PH; ++ph) {
+                const int e0 = ph * PH;
+                float4 a[PH / 4], b[PH / 4], c[PH / 2];   // q[e0..], q[HALF+e0..], (cos, sin) x2
 #pragma unroll
-            for (int i = 0; i < HALF; ++i) {
-                const float2 a = __ldg(cs + i);
-                const float x0 = qv[i], x1 = qv[i + HALF];
-                qv[i] = rope_lo(x0, x1, a.x, a.y) * p.scale_log2;
-                qv[i + HALF] = rope_hi(x0, x1, a.x, a.y) * p.scale_log2;
-            }
+                for (int i = 0; i < PH / 4; ++i) {
+                    a[i] = valid ? __ldg(q4 + e0 / 4 + i) : zero;
+                    b[i] = valid ? __ldg(q4 + (HALF + e0) / 4 + i) : zero;
+                }
 #pragma unroll
-            for (int c0 = 0; c0 < HALF; c0 += 32) {   // 32 columns = 64 elements per store
-                uint32_t hi[32], mid[32];
+                for (int i = 0; i < PH / 2; ++i) c[i] = __ldg(cs4 + e0 / 2 + i);
+                float lo[PH], hi[PH];
 #pragma unroll
-                for (int i = 0; i < 32; ++i) split2(qv[2 * (c0 + i)], qv[2 * (c0 + i) + 1], hi[i], mid[i]);
-                tc_st32u(t_q + lane_off + c0, hi);
-                tc_st32u(t_q + lane_off + HALF + c0, mid);
+                for (int i = 0; i < PH; ++i) {
+                    const float4 &qa = a[i / 4], &qb = b[i / 4], &cc = c[i / 2];
+                    const float x0 = (i & 3) == 0 ? qa.x : (i & 3) == 1 ? qa.y : (i & 3) == 2 ? qa.z : qa.w;
+                    const float x1 = (i & 3) == 0 ? qb.x : (i & 3) == 1 ? qb.y : (i & 3) == 2 ? qb.z : qb.w;
+                    const float co = (i & 1) ? cc.z : cc.x, si = (i & 1) ? cc.w : cc.y;
+                    lo[i] = rope_lo(x0, x1, co, si) * p.scale_log2;
+                    hi[i] = rope_hi(x0, x1, co, si) * p.scale_log2;
+                }
+                // column k of Q hi (mid: + HALF) holds elements 2k, 2k+1
+                uint32_t wh[PH / 2], wm[PH / 2];
+#pragma unroll
+                for (int i = 0; i < PH / 2; ++i) split2(lo[2 * i], lo[2 * i + 1], wh[i], wm[i]);
+                tc_st16u(t_q + lane_off + e0 / 2, wh);
+                tc_st16u(t_q + lane_off + HALF + e0 / 2, wm);
+#pragma unroll
+                for (int i = 0; i < PH / 2; ++i) split2(hi[2 * i], hi[2 * i + 1], wh[i], wm[i]);
+                tc_st16u(t_q + lane_off + (HALF + e0) / 2, wh);
+                tc_st16u(t_q + lane_off + HALF + (HALF + e0) / 2, wm);
             }
             tc_wait_st();
         }
