@@ -60,6 +60,9 @@ struct kore_cuda_ctx {
     bool shard_prefetch = true;
     bool hold_prefetch = false;   // set: the next decode waits before its first KV fetch
     int prefetch_stages = 3;      // ring stages fetched early (KORE_CUDA_PREFETCH_STAGES)
+    // batched decode: split-length factor chosen for the last batch shape
+    long long split_key[3] = {-1, -1, -1};
+    double split_f = 1.0;
     float *peers[kMaxRanks] = {};
     bool peers_open = false;
     // prefill: K/V operand tiles of the current chunk's layer (attn_prefill.cu)
@@ -264,6 +267,8 @@ int run_decode(kore_cuda_ctx *c, int layer, int n_q, bool contiguous, int seq0, 
     p.pos0 = pos0;
     long long total = 0;
     int max_count = 0;
+    std::vector<int> counts;
+    if (!contiguous) counts.resize((size_t)n_q);
     for (int i = 0; i < n_q; ++i) {
         const int ps = contiguous ? pos0 + i : poss[i];
         if (!contiguous) {
@@ -271,6 +276,7 @@ int run_decode(kore_cuda_ctx *c, int layer, int n_q, bool contiguous, int seq0, 
             p.pos[i] = ps;
         }
         const int cnt = local_count(c, append_new ? ps : ps + 1);
+        if (!contiguous) counts[(size_t)i] = cnt;
         total += cnt;
         max_count = std::max(max_count, cnt);
     }
@@ -282,6 +288,58 @@ int run_decode(kore_cuda_ctx *c, int layer, int n_q, bool contiguous, int seq0, 
     int grid_x;
     if (n_q > kMaxBatch) {
         st = std::max(max_count, TT);   // one split per query: no scratch
+    } else if (!contiguous && n_q > 1) {
+        // A batch of ragged sequences: the split length decides how the CTAs
+        // (one per split, KV head and sequence, dispatched split-fastest in
+        // launch order) pack onto the SMs; a count just above a whole number
+        // of waves leaves most SMs idle for one more CTA. A few lengths are
+        // scored by replaying that in-order dispatch onto `target` slots,
+        // each CTA costing its positions plus a fixed start-up cost, and
+        // the one that finishes first is kept.
+        const long long st_cap_b = std::max<long long>((long long)(decode_split_pages_max() - 1) * c->P / TT * TT, TT);
+        const long long ovh = 32 * TT;
+        std::vector<long long> slots;
+        auto makespan = [&](long long s) {
+            slots.assign((size_t)target, 0);
+            std::make_heap(slots.begin(), slots.end(), std::greater<long long>());
+            long long end = 0;
+            for (int i = 0; i < n_q; ++i) {
+                const long long n = counts[(size_t)i];
+                const long long ns = std::max<long long>(1, (n + s - 1) / s);
+                for (int g = 0; g < c->G; ++g)
+                    for (long long k = 0; k < ns; ++k) {
+                        std::pop_heap(slots.begin(), slots.end(), std::greater<long long>());
+                        const long long t = slots.back() + std::min(s, n - k * s) + ovh;
+                        slots.back() = t;
+                        std::push_heap(slots.begin(), slots.end(), std::greater<long long>());
+                        end = std::max(end, t);
+                    }
+            }
+            return end;
+        };
+        auto length = [&](double f) {
+            const long long s = (long long)(st * f);
+            return std::min<long long>(std::max<long long>((s + TT - 1) / TT * TT, TT), st_cap_b);
+        };
+        // the choice moves slowly as the sequences grow: it is kept until the
+        // batch size, or the total or largest count in 1024-position buckets,
+        // changes
+        const long long key[3] = {n_q, total >> 10, max_count >> 10};
+        if (key[0] != c->split_key[0] || key[1] != c->split_key[1] || key[2] != c->split_key[2]) {
+            double best_f = 1.0;
+            long long best_t = -1;
+            for (int k = 0; k <= 26; ++k) {
+                const double f = k < 26 ? 1.0 + 0.05 * k : 3.0;
+                const long long t = makespan(length(f));
+                if (best_t < 0 || t < best_t) {
+                    best_t = t;
+                    best_f = f;
+                }
+            }
+            c->split_f = best_f;
+            for (int i = 0; i < 3; ++i) c->split_key[i] = key[i];
+        }
+        st = length(c->split_f);
     }
     for (;;) {
         st = (st + TT - 1) / TT * TT;
