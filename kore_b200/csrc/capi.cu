@@ -205,8 +205,13 @@ int grow_stage(kore_cuda_ctx *c, size_t floats) {
 }
 
 // Reads and clears the device error word (stream-ordered, then synchronises).
-int finish(kore_cuda_ctx *c) {
-    CK(cudaMemcpyAsync(c->host_err, c->err_d, sizeof(int), cudaMemcpyDeviceToHost, c->stream));
+// Waits for the stream after `extra` bytes following the device error word
+// (kErrPad on) were queued for copying back with it; reports a device error.
+constexpr size_t kErrPad = 256;   // bytes from the device error word to the decode output behind it
+
+int finish(kore_cuda_ctx *c, size_t extra = 0) {
+    CK(cudaMemcpyAsync(c->host_err, c->err_d, extra ? kErrPad + extra : sizeof(int), cudaMemcpyDeviceToHost,
+                       c->stream));
     CK(cudaStreamSynchronize(c->stream));
     const int e = *c->host_err;
     if (e != DEV_OK) {
@@ -501,9 +506,12 @@ int kore_cuda_create(kore_cuda_ctx **out, const kore_cuda_cfg *cfg) {
     c->part_slots = kPartSlots;
     CKB(cudaMalloc(&c->part_o, c->part_slots * c->R * c->D * sizeof(float)));
     CKB(cudaMalloc(&c->part_ml, c->part_slots * c->R * sizeof(float2)));
-    CKB(cudaMalloc(&c->err_d, sizeof(int)));
+    // the device error word heads a buffer that also receives one sequence's
+    // decode output, so that the host-buffer decode fetches both with one copy
+    const size_t err_bytes = kErrPad + (size_t)c->H * c->D * sizeof(float);
+    CKB(cudaMalloc(&c->err_d, err_bytes));
     CKB(cudaMemsetAsync(c->err_d, 0, sizeof(int), c->stream));
-    CKB(cudaMallocHost(&c->host_err, sizeof(int)));
+    CKB(cudaMallocHost(&c->host_err, err_bytes));
     CKB(cudaStreamSynchronize(c->stream));
 #undef CKB
     c->msg = "no error";
@@ -759,10 +767,19 @@ static int decode_host(kore_cuda_ctx *c, int n_seq, const float *q, const float 
     memcpy(hs + nq, k, nk * sizeof(float));
     memcpy(hs + nq + nk, v, nk * sizeof(float));
     CK(cudaMemcpyAsync(ds, hs, (nq + 2 * nk) * sizeof(float), cudaMemcpyHostToDevice, c->stream));
+    if (!batch) {
+        // one sequence: the output lands right behind the error word and both
+        // come back in one copy
+        float *dout = reinterpret_cast<float *>(reinterpret_cast<char *>(c->err_d) + kErrPad);
+        if (int rc = kore_cuda_attn_decode_dev(c, seq_ids[0], layer, pos[0], ds, ds + nq, ds + nq + nk, dout))
+            return rc;
+        if (int rc2 = finish(c, nq * sizeof(float))) return rc2;
+        memcpy(out, reinterpret_cast<const char *>(c->host_err) + kErrPad, nq * sizeof(float));
+        return KORE_CUDA_OK;
+    }
     float *dout = ds + nq + 2 * nk;
-    int rc = batch ? kore_cuda_attn_decode_batch_dev(c, layer, n_seq, seq_ids, pos, ds, ds + nq, ds + nq + nk, dout)
-                   : kore_cuda_attn_decode_dev(c, seq_ids[0], layer, pos[0], ds, ds + nq, ds + nq + nk, dout);
-    if (rc) return rc;
+    if (int rc = kore_cuda_attn_decode_batch_dev(c, layer, n_seq, seq_ids, pos, ds, ds + nq, ds + nq + nk, dout))
+        return rc;
     CK(cudaMemcpyAsync(hs + nq + 2 * nk, dout, nq * sizeof(float), cudaMemcpyDeviceToHost, c->stream));
     if (int rc2 = finish(c)) return rc2;
     memcpy(out, hs + nq + 2 * nk, nq * sizeof(float));
