@@ -191,6 +191,50 @@ __device__ __forceinline__ void split2(float x0, float x1, uint32_t &hi, uint32_
 __device__ __forceinline__ void tc_wait_ld() { asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory"); }
 __device__ __forceinline__ void tc_wait_st() { asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory"); }
 
+// Packed fp32 pairs (Blackwell's two-lane fp32 add/sub/mul: each lane rounds
+// as the scalar instruction does) and a three-input max, to cut the softmax's
+// instruction count.
+__device__ __forceinline__ unsigned long long pk2(float a, float b) {
+    unsigned long long u;
+    asm("mov.b64 %0, {%1, %2};" : "=l"(u) : "f"(a), "f"(b));
+    return u;
+}
+__device__ __forceinline__ void upk2(unsigned long long u, float &a, float &b) {
+    asm("mov.b64 {%0, %1}, %2;" : "=f"(a), "=f"(b) : "l"(u));
+}
+__device__ __forceinline__ unsigned long long sub2(unsigned long long a, unsigned long long b) {
+    unsigned long long r;
+    asm("sub.rn.f32x2 %0, %1, %2;" : "=l"(r) : "l"(a), "l"(b));
+    return r;
+}
+__device__ __forceinline__ unsigned long long add2(unsigned long long a, unsigned long long b) {
+    unsigned long long r;
+    asm("add.rn.f32x2 %0, %1, %2;" : "=l"(r) : "l"(a), "l"(b));
+    return r;
+}
+__device__ __forceinline__ unsigned long long mul2(unsigned long long a, unsigned long long b) {
+    unsigned long long r;
+    asm("mul.rn.f32x2 %0, %1, %2;" : "=l"(r) : "l"(a), "l"(b));
+    return r;
+}
+__device__ __forceinline__ float max3(float a, float b, float c) {
+    float r;
+    asm("max.f32 %0, %1, %2, %3;" : "=f"(r) : "f"(a), "f"(b), "f"(c));
+    return r;
+}
+
+// split2 with the residual formed by one packed subtraction (the bf16 -> fp32
+// widening of hi is exact: its 16 bits moved to the top half)
+__device__ __forceinline__ void split2p(float x0, float x1, uint32_t &hi, uint32_t &mid) {
+    const __nv_bfloat162 a = __floats2bfloat162_rn(x0, x1);
+    const uint32_t ab = *reinterpret_cast<const uint32_t *>(&a);
+    float r0, r1;
+    upk2(sub2(pk2(x0, x1), pk2(__uint_as_float(ab << 16), __uint_as_float(ab & 0xFFFF0000u))), r0, r1);
+    const __nv_bfloat162 b = __floats2bfloat162_rn(r0, r1);
+    hi = ab;
+    mid = *reinterpret_cast<const uint32_t *>(&b);
+}
+
 // hi/mid bf16 split of 8 consecutive fp32 values, packed as two 16-byte chunks
 __device__ __forceinline__ void split8(const float *x, uint4 &hi, uint4 &mid) {
     uint32_t h[4], m[4];
@@ -491,23 +535,31 @@ __global__ void __launch_bounds__(192, 1) prefill_kernel(const __grid_constant__
             for (int i = 0; i < 64; ++i)
                 if (key0 + i > lim) v[i] = -INFINITY;
         };
-        auto max64 = [](const float (&v)[64]) {   // a tree: 8 independent chains, then pairs
+        auto max64 = [](const float (&v)[64]) {   // 8 independent chains of three-input maxima
             float m8[8];
 #pragma unroll
             for (int c = 0; c < 8; ++c) m8[c] = v[c];
 #pragma unroll
-            for (int i = 8; i < 64; ++i) m8[i & 7] = fmaxf(m8[i & 7], v[i]);
-            return fmaxf(fmaxf(fmaxf(m8[0], m8[1]), fmaxf(m8[2], m8[3])), fmaxf(fmaxf(m8[4], m8[5]), fmaxf(m8[6], m8[7])));
+            for (int i = 8; i < 64; i += 2) m8[(i >> 1) & 7] = max3(m8[(i >> 1) & 7], v[i], v[i + 1]);
+            return max3(max3(m8[0], m8[1], m8[2]), max3(m8[3], m8[4], m8[5]), fmaxf(m8[6], m8[7]));
         };
         // P of 64 keys from their scores, written over them: for each 16 keys,
         // 8 columns of hi pairs then 8 of mid pairs; returns the sum of P
         auto p64 = [&](float (&v)[64], uint32_t col, float m) {
-            float l8[8] = {0, 0, 0, 0, 0, 0, 0, 0};
+            // sums in 8 chains (keys = c mod 8), as pairs: acc[j] holds chains 2j, 2j+1
+            const unsigned long long mm = pk2(m, m);
+            unsigned long long acc[4] = {0ull, 0ull, 0ull, 0ull};
 #pragma unroll
-            for (int i = 0; i < 64; ++i) {
-                v[i] = fast_exp2(v[i] - m);
-                l8[i & 7] += v[i];
+            for (int i = 0; i < 32; ++i) {
+                float a0, a1;
+                upk2(sub2(pk2(v[2 * i], v[2 * i + 1]), mm), a0, a1);
+                v[2 * i] = fast_exp2(a0);
+                v[2 * i + 1] = fast_exp2(a1);
+                acc[i & 3] = add2(acc[i & 3], pk2(v[2 * i], v[2 * i + 1]));
             }
+            float l8[8];
+#pragma unroll
+            for (int j = 0; j < 4; ++j) upk2(acc[j], l8[2 * j], l8[2 * j + 1]);
 #pragma unroll
             for (int s = 0; s < 2; ++s) {
                 uint32_t w[32];
@@ -516,7 +568,7 @@ __global__ void __launch_bounds__(192, 1) prefill_kernel(const __grid_constant__
 #pragma unroll
                     for (int i = 0; i < 8; ++i) {
                         const int k = 32 * s + 16 * gq + 2 * i;
-                        split2(v[k], v[k + 1], w[16 * gq + i], w[16 * gq + 8 + i]);
+                        split2p(v[k], v[k + 1], w[16 * gq + i], w[16 * gq + 8 + i]);
                     }
                 tc_st32u(col + 32 * s, w);
             }
@@ -568,7 +620,7 @@ __global__ void __launch_bounds__(192, 1) prefill_kernel(const __grid_constant__
                     tc_ld32(t_o + lane_off + c0, o);
                     tc_wait_ld();
 #pragma unroll
-                    for (int i = 0; i < 32; ++i) o[i] *= alpha;
+                    for (int i = 0; i < 32; i += 2) upk2(mul2(pk2(o[i], o[i + 1]), pk2(alpha, alpha)), o[i], o[i + 1]);
                     tc_st32(t_o + lane_off + c0, o);
                 }
             }
