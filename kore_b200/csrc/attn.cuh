@@ -1,6 +1,8 @@
 // attn.cuh — parameter blocks and launchers of the attention kernels.
 #pragma once
 
+#include <vector>
+
 #include <cuda_runtime.h>
 
 namespace kore {
@@ -70,6 +72,12 @@ struct PrefillParams {
     int *err;
     float scale_log2;
     int seq, pos0, n, H, n_rep;
+    // work list (prefill_plan): one int4 per CTA = {query head, query tile,
+    // key tiles t0 | t1 << 16, split slot * 2 + part or -1}
+    const int4 *items;
+    float *part;               // [split slots][2 parts][kRows][D + 1]: a split half's O / l and LSE
+    int *counters;             // [split slots]: halves done; reset to 0 by the merging half
+    int n_items;
 };
 
 // One layer's cross-GPU exchange of KV-sharded decode partials (peer_exchange.cu).
@@ -99,6 +107,13 @@ size_t decode_smem_bytes(int head_dim);
 cudaError_t launch_kv_append(const AppendParams &p, cudaStream_t s);
 void set_ctxless_error(const char *msg);
 size_t prefill_tile_bytes(int head_dim);
+// bytes of one split slot of PrefillParams::part
+size_t prefill_slot_bytes(int head_dim);
+// Work list of a prefill chunk (pos0, n) over H heads on num_sms SMs: one
+// item per (query head, 128-row query tile), the heaviest ones possibly split
+// in two key ranges, in the dispatch order that finishes first by a replay of
+// the in-order CTA dispatch. Returns the number of split slots used.
+int prefill_plan(int pos0, int n, int H, int num_sms, std::vector<int4> &items);
 int prefill_tile_keys();
 cudaError_t launch_prefill(const PrefillParams &p, cudaStream_t s);
 cudaError_t launch_peer_exchange(const ExchangeParams &p, cudaStream_t s);

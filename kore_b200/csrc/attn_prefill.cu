@@ -23,7 +23,12 @@
 //                     kernel fetches each with one bulk copy. Keys past the
 //                     last position are zero, so they never reach an output
 //                     through 0 * NaN.
-//   prefill_kernel    one CTA per (128-row query tile, query head):
+//   prefill_kernel    one CTA per work item (prefill_plan): a (128-row query
+//                 tile, query head) over all its key tiles, or, for the
+//                 heaviest query tiles, over one of two key ranges. With
+//                 3 waves of 148 CTAs the last wave's few CTAs set the time;
+//                 splitting the longest tiles and ordering the items by a
+//                 replay of the in-order CTA dispatch levels the SMs' ends.
 //     warps 0-3   softmax: thread t owns query row t. Prologue: RoPE of its q
 //                 row, scale by log2(e)/sqrt(d), hi/mid split into tensor
 //                 memory (the A operand of S = Q K^T). Per key tile: S row
@@ -31,7 +36,10 @@
 //                 lazily moved reference maximum (O in tensor memory is
 //                 rescaled only when a score exceeds the reference by 2^8),
 //                 P hi/mid written over the tile's S (the A operand of
-//                 O += P V). Epilogue: O / l to global memory.
+//                 O += P V). Epilogue: O / l to global memory; a split half
+//                 writes O / l and its log-sum-exp to its slot, and the
+//                 second half to finish (an atomic count per slot) merges
+//                 both into the output.
 //     warp 4      producer: the operand chunks of every MMA group, in the
 //                 order the MMAs consume them, into a three-stage ring of
 //                 bulk copies completing on mbarriers.
@@ -52,6 +60,12 @@
 #include "common.cuh"
 
 #include <cuda_bf16.h>
+
+#include <algorithm>
+#include <climits>
+#include <cmath>
+#include <functional>
+#include <vector>
 
 namespace kore {
 namespace {
@@ -341,15 +355,19 @@ __global__ void __launch_bounds__(192, 1) prefill_kernel(const __grid_constant__
     uint64_t *mma_drained = bars + 10;  // MMA commit -> MMA issuer, before TMEM is freed
     uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(bars + 11);
     int *abort_flag = reinterpret_cast<int *>(bars + 12);
+    int *arrival = reinterpret_cast<int *>(bars + 13);   // split halves: 1 for the second to finish
 
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    const int qt = gridDim.x - 1 - blockIdx.x;   // heaviest (last) query tiles first
-    const int h = blockIdx.y;
+    // work item (prefill_plan): query head, query tile, key tiles [t0, t1),
+    // and for a query tile split in two key ranges its slot and half
+    const int4 item = p.items[blockIdx.x];
+    const int h = item.x, qt = item.y;
+    const int t0 = item.z & 0xFFFF, t1 = (int)((unsigned)item.z >> 16);
+    const int slot = item.w < 0 ? -1 : item.w >> 1, part = item.w & 1;
     const int g = h / p.n_rep;
     const int z0 = qt * kRows;
     const int rows = min(kRows, p.n - z0);
-    const int last_key = p.pos0 + z0 + rows - 1;                // causal limit of the last row
-    const int n_tiles = last_key / kKeys + 1;
+    const int n_tiles = t1 - t0;                                 // key tiles of this CTA
     const int first_masked = (p.pos0 + z0) / kKeys;              // tiles from here need the mask
 
     if (threadIdx.x == 0) {
@@ -404,7 +422,7 @@ __global__ void __launch_bounds__(192, 1) prefill_kernel(const __grid_constant__
                 h2 = 2 * j + (is_s ? 1 : 0);
                 const uint32_t bytes = is_s ? SM::K_BYTES : SM::V_BYTES;
                 uint8_t *dst = smem + SM::ring_off + st * SM::STAGE;
-                const uint8_t *src = src0 + (size_t)j * SM::TILE + (is_s ? 0 : SM::K_BYTES);
+                const uint8_t *src = src0 + (size_t)(t0 + j) * SM::TILE + (is_s ? 0 : SM::K_BYTES);
                 mbar_arrive_expect_tx(&full[st], bytes);
                 for (uint32_t o = 0; o < bytes; o += 16384)   // kept in L2: every query tile and head reads it
                     bulk_g2s_plain(dst + o, src + o, 16384, &full[st]);
@@ -582,8 +600,8 @@ __global__ void __launch_bounds__(192, 1) prefill_kernel(const __grid_constant__
             const uint32_t ts = tmem + SM::T_S + 128 * b + lane_off;
             if (!bounded_wait(&s_full[b], (j >> 1) & 1)) { ok = false; break; }
             tc_fence_after();
-            const bool masked = j >= first_masked;
-            const int key0 = j * kKeys;
+            const bool masked = t0 + j >= first_masked;
+            const int key0 = (t0 + j) * kKeys;
             float sv[64];
             // pass 1: the row maximum over keys 0-63 (scores dropped) and
             // 64-127 (kept for pass 2)
@@ -600,14 +618,17 @@ __global__ void __launch_bounds__(192, 1) prefill_kernel(const __grid_constant__
             const bool need = mx > m_ref + kRescale;
             const bool any_need = __any_sync(FULLMASK, need);
             const float m_new = need ? mx : m_ref;
-            const float alpha = fast_exp2(m_ref - m_new);   // 0 for the first tile, 1 where not needed
+            // 0 for the first tile, 1 where not needed; a row with no key yet
+            // (every key so far masked) keeps 1 and P = 0
+            const float alpha = m_new == -INFINITY ? 1.f : fast_exp2(m_ref - m_new);
+            const float m_use = m_new == -INFINITY ? 0.f : m_new;
             // pass 2: keys 64-127 from registers, then keys 0-63 again
-            float ls = p64(sv, ts + 64, m_new);
+            float ls = p64(sv, ts + 64, m_use);
             tc_ld32(ts, *reinterpret_cast<float(*)[32]>(sv));
             tc_ld32(ts + 32, *reinterpret_cast<float(*)[32]>(sv + 32));
             tc_wait_ld();
             if (masked) mask64(sv, key0);
-            ls += p64(sv, ts, m_new);
+            ls += p64(sv, ts, m_use);
             l = fmaf(l, alpha, ls);
             m_ref = m_new;
             // O is stable only once the previous tile's P.V is done
@@ -629,22 +650,76 @@ __global__ void __launch_bounds__(192, 1) prefill_kernel(const __grid_constant__
             __syncwarp();
             if (lane == 0) mbar_arrive(&p_full[b]);
         }
-        // epilogue: O / l
-        if (ok && n_tiles > 0 && bounded_wait(&pv_done[(n_tiles - 1) & 1], ((n_tiles - 1) >> 1) & 1)) {
-            tc_fence_after();
-            const float inv = l > 0.f ? 1.f / l : 0.f;
-            float *dst = p.out + ((size_t)z * p.H + h) * D;
+        // epilogue: O / l to the output, or for a split query tile to its half's
+        // slot, the second half to finish merging both into the output. The
+        // split path's barriers are taken by all four softmax warps whatever
+        // happened before (a warp whose wait gave up has already raised the
+        // error; the results are then not used).
+        const bool epi = ok && n_tiles > 0 && bounded_wait(&pv_done[(n_tiles - 1) & 1], ((n_tiles - 1) >> 1) & 1);
+        if (epi) tc_fence_after();
+        const float inv = l > 0.f ? 1.f / l : 0.f;
+        float *dst = p.out + ((size_t)z * p.H + h) * D;
+        if (slot < 0) {
+            if (epi) {
 #pragma unroll
-            for (int c0 = 0; c0 < D; c0 += 32) {
-                float o[32];
-                tc_ld32(t_o + lane_off + c0, o);
-                tc_wait_ld();
-                if (valid) {
+                for (int c0 = 0; c0 < D; c0 += 32) {
+                    float o[32];
+                    tc_ld32(t_o + lane_off + c0, o);
+                    tc_wait_ld();
+                    if (valid) {
+#pragma unroll
+                        for (int i = 0; i < 32; i += 4)
+                            *reinterpret_cast<float4 *>(dst + c0 + i) =
+                                make_float4(o[i] * inv, o[i + 1] * inv, o[i + 2] * inv, o[i + 3] * inv);
+                    }
+                }
+            }
+        } else {
+            // a half's slot: [kRows][D] outputs normalised by its own sum, then
+            // [kRows] log2-domain log-sum-exps
+            const float lse = l > 0.f ? m_ref + __log2f(l) : -INFINITY;
+            float *mine = p.part + ((size_t)slot * 2 + part) * kRows * (D + 1);
+            const float *other = p.part + ((size_t)slot * 2 + (part ^ 1)) * kRows * (D + 1);
+            if (epi) {
+#pragma unroll
+                for (int c0 = 0; c0 < D; c0 += 32) {
+                    float o[32];
+                    tc_ld32(t_o + lane_off + c0, o);
+                    tc_wait_ld();
 #pragma unroll
                     for (int i = 0; i < 32; i += 4)
-                        *reinterpret_cast<float4 *>(dst + c0 + i) =
+                        *reinterpret_cast<float4 *>(mine + (size_t)t * D + c0 + i) =
                             make_float4(o[i] * inv, o[i + 1] * inv, o[i + 2] * inv, o[i + 3] * inv);
                 }
+                mine[kRows * D + t] = lse;
+            }
+            __threadfence();
+            asm volatile("bar.sync 1, 128;" ::: "memory");   // the four softmax warps
+            if (t == 0) *arrival = atomicAdd(p.counters + slot, 1);
+            asm volatile("bar.sync 1, 128;" ::: "memory");
+            if (*reinterpret_cast<volatile int *>(arrival) == 1) {
+                __threadfence();
+                const float lo = __ldcg(other + kRows * D + t);
+                const float M = fmaxf(lse, lo);
+                const float wm = M == -INFINITY ? 0.f : fast_exp2(lse - M);
+                const float wo = M == -INFINITY ? 0.f : fast_exp2(lo - M);
+                const float inv2 = wm + wo > 0.f ? 1.f / (wm + wo) : 0.f;
+#pragma unroll
+                for (int c0 = 0; c0 < D; c0 += 32) {
+                    float o[32];
+                    tc_ld32(t_o + lane_off + c0, o);
+                    tc_wait_ld();
+                    if (valid) {
+#pragma unroll
+                        for (int i = 0; i < 32; i += 4) {
+                            const float4 x = __ldcg(reinterpret_cast<const float4 *>(other + (size_t)t * D + c0 + i));
+                            *reinterpret_cast<float4 *>(dst + c0 + i) = make_float4(
+                                (wm * o[i] * inv + wo * x.x) * inv2, (wm * o[i + 1] * inv + wo * x.y) * inv2,
+                                (wm * o[i + 2] * inv + wo * x.z) * inv2, (wm * o[i + 3] * inv + wo * x.w) * inv2);
+                        }
+                    }
+                }
+                if (t == 0) p.counters[slot] = 0;   // ready for the next call
             }
         }
     }
@@ -673,12 +748,87 @@ cudaError_t launch_prefill_d(const PrefillParams &p, cudaStream_t s) {
         if (e != cudaSuccess) return e;
         if (dev >= 0 && dev < 64) configured[dev] = true;
     }
-    const int q_tiles = (p.n + kRows - 1) / kRows;
-    prefill_kernel<D><<<dim3(q_tiles, p.H), 192, SM::bytes, s>>>(p);
+    if (p.n_items <= 0 || !p.items) return cudaErrorInvalidValue;
+    prefill_kernel<D><<<dim3(p.n_items), 192, SM::bytes, s>>>(p);
     return cudaGetLastError();
 }
 
 }  // namespace
+
+int prefill_plan(int pos0, int n, int H, int num_sms, std::vector<int4> &items) {
+    const int q_tiles = (n + kRows - 1) / kRows;
+    std::vector<int> nt(q_tiles), fm(q_tiles);
+    int max_nt = 0;
+    for (int qt = 0; qt < q_tiles; ++qt) {
+        const int z0 = qt * kRows, rows = std::min(kRows, n - z0);
+        nt[qt] = (pos0 + z0 + rows - 1) / kKeys + 1;
+        fm[qt] = (pos0 + z0) / kKeys;   // keys below this tile are unmasked for every row
+        max_nt = std::max(max_nt, nt[qt]);
+    }
+    struct Work {
+        int h, qt, t0, t1, split;
+    };
+    // A query tile with at least `thr` key tiles is split at its middle, but
+    // no later than its first masked tile: the first half is then unmasked
+    // and every row has keys in the second.
+    auto build = [&](int thr, std::vector<Work> &w) {
+        w.clear();
+        int slots = 0;
+        for (int h = 0; h < H; ++h)
+            for (int qt = q_tiles - 1; qt >= 0; --qt) {
+                const int mid = std::min(nt[qt] / 2, fm[qt]);
+                if (nt[qt] >= thr && mid >= 4 && nt[qt] - mid >= 4) {
+                    w.push_back({h, qt, 0, mid, 2 * slots});
+                    w.push_back({h, qt, mid, nt[qt], 2 * slots + 1});
+                    ++slots;
+                } else {
+                    w.push_back({h, qt, 0, nt[qt], -1});
+                }
+            }
+        return slots;
+    };
+    // completion time of the work in launch order, each SM taking the next
+    // CTA when it frees, a CTA costing its key tiles plus a start-up cost
+    const long long ovh = 4;
+    std::vector<long long> sm;
+    auto makespan = [&](const std::vector<Work> &w) {
+        sm.assign((size_t)std::max(1, num_sms), 0);
+        std::make_heap(sm.begin(), sm.end(), std::greater<long long>());
+        long long end = 0;
+        for (const Work &x : w) {
+            std::pop_heap(sm.begin(), sm.end(), std::greater<long long>());
+            sm.back() += ovh + (x.t1 - x.t0);
+            end = std::max(end, sm.back());
+            std::push_heap(sm.begin(), sm.end(), std::greater<long long>());
+        }
+        return end;
+    };
+    std::vector<Work> best, w;
+    long long best_t = -1;
+    for (const double f : {2.0, 1.0, 0.95, 0.9, 0.85, 0.8, 0.7}) {
+        const int thr = f > 1.5 ? INT_MAX : (int)std::ceil(f * max_nt);
+        build(thr, w);
+        for (int order = 0; order < 2; ++order) {
+            if (order == 1)   // heaviest first over all heads (the build order is per head)
+                std::stable_sort(w.begin(), w.end(),
+                                 [](const Work &a, const Work &b) { return a.t1 - a.t0 > b.t1 - b.t0; });
+            const long long t = makespan(w);
+            if (best_t < 0 || t < best_t) {
+                best_t = t;
+                best = w;
+            }
+        }
+    }
+    items.clear();
+    int slots = 0;
+    for (const Work &x : best) {
+        items.push_back(make_int4(x.h, x.qt, x.t0 | (x.t1 << 16), x.split));
+        if (x.split >= 0) slots = std::max(slots, x.split / 2 + 1);
+    }
+    return slots;
+}
+
+size_t prefill_slot_bytes(int head_dim) { return (size_t)2 * kRows * (head_dim + 1) * sizeof(float); }
 
 size_t prefill_tile_bytes(int head_dim) {
     return head_dim == 128 ? PrefillSmem<128>::TILE : PrefillSmem<64>::TILE;

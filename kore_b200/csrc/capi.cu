@@ -68,6 +68,14 @@ struct kore_cuda_ctx {
     // prefill: K/V operand tiles of the current chunk's layer (attn_prefill.cu)
     void *split = nullptr;
     int split_tiles = 0;        // capacity per KV head, in tiles of prefill_tile_keys() positions
+    // prefill work list of the last chunk shape (prefill_plan), its split
+    // halves' slots and arrival counters
+    int pf_pos0 = -1, pf_n = -1, pf_items_n = 0;
+    int4 *pf_items = nullptr;
+    size_t pf_items_cap = 0;
+    float *pf_part = nullptr;
+    int *pf_counters = nullptr;
+    int pf_slots_cap = 0;
     std::string msg;
 };
 
@@ -216,6 +224,8 @@ int finish(kore_cuda_ctx *c, size_t extra = 0) {
     const int e = *c->host_err;
     if (e != DEV_OK) {
         CK(cudaMemsetAsync(c->err_d, 0, sizeof(int), c->stream));
+        // a prefill that gave up may have left a split half's arrival counted
+        if (c->pf_counters) CK(cudaMemsetAsync(c->pf_counters, 0, c->pf_slots_cap * sizeof(int), c->stream));
         CK(cudaStreamSynchronize(c->stream));
         return fail(c, KORE_CUDA_EDEVICE, "device error %d (%s)", e,
                     e == DEV_BAD_PAGE ? "page table entry outside the pool"
@@ -410,6 +420,9 @@ void kore_cuda_destroy(kore_cuda_ctx *c) {
             if (c->peers[r] && c->peers[r] != c->xbuf) cudaIpcCloseMemHandle(c->peers[r]);
         cudaFree(c->xbuf);
         cudaFree(c->split);
+        cudaFree(c->pf_items);
+        cudaFree(c->pf_part);
+        cudaFree(c->pf_counters);
         cudaFree(c->kv);
         cudaFree(c->pt_d);
         cudaFree(c->rope_d);
@@ -583,8 +596,41 @@ int kore_cuda_attn_prefill_dev(kore_cuda_ctx *c, int seq, int layer, int pos0, i
         CK(cudaMalloc(&c->split, (size_t)c->G * tiles * prefill_tile_bytes(c->D)));
         c->split_tiles = tiles;
     }
+    if (pos0 != c->pf_pos0 || n != c->pf_n) {
+        // a new chunk shape: plan its work list; the kernels still queued may
+        // read the old one, so the stream is drained before it is replaced
+        std::vector<int4> items;
+        const int slots = prefill_plan(pos0, n, c->H, c->num_sms, items);
+        CK(cudaStreamSynchronize(c->stream));
+        if (items.size() > c->pf_items_cap) {
+            cudaFree(c->pf_items);
+            c->pf_items = nullptr;
+            c->pf_items_cap = 0;
+            CK(cudaMalloc(&c->pf_items, items.size() * sizeof(int4)));
+            c->pf_items_cap = items.size();
+        }
+        if (slots > c->pf_slots_cap) {
+            cudaFree(c->pf_part);
+            cudaFree(c->pf_counters);
+            c->pf_part = nullptr;
+            c->pf_counters = nullptr;
+            c->pf_slots_cap = 0;
+            CK(cudaMalloc(&c->pf_part, (size_t)slots * prefill_slot_bytes(c->D)));
+            CK(cudaMalloc(&c->pf_counters, (size_t)slots * sizeof(int)));
+            CK(cudaMemset(c->pf_counters, 0, (size_t)slots * sizeof(int)));
+            c->pf_slots_cap = slots;
+        }
+        CK(cudaMemcpy(c->pf_items, items.data(), items.size() * sizeof(int4), cudaMemcpyHostToDevice));
+        c->pf_items_n = (int)items.size();
+        c->pf_pos0 = pos0;
+        c->pf_n = n;
+    }
     PrefillParams pp;
     memset(&pp, 0, sizeof pp);
+    pp.items = c->pf_items;
+    pp.n_items = c->pf_items_n;
+    pp.part = c->pf_part;
+    pp.counters = c->pf_counters;
     pp.kv = layer_kv(c, layer);
     pp.split = c->split;
     pp.tiles = c->split_tiles;
