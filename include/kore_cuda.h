@@ -146,6 +146,66 @@ int kore_cuda_attn_decode_batch_dev(kore_cuda_ctx *ctx, int layer, int n_seq, co
                                     float *out);
 
 /*
+ * The attention block with its quantised projections on the GPU.
+ *
+ * kore's decode step wraps the attention region in four projections
+ * (kore.cpp:1418-1423 and :1456-1457): the normed hidden state xb is
+ * quantised to Q8_K (quantize_row_q8_K, kore.cpp:422-447), multiplied by Wq,
+ * Wk and Wv (GGUF Q4_K or Q6_K blocks, matvec_mt, kore.cpp:649-682) and
+ * bias-added, the attention runs, and its output is quantised again and
+ * multiplied by Wo. With the weights uploaded once, the whole block runs on
+ * the device: the host passes xb and gets Wo*att back, instead of moving
+ * q, k, v and att across PCIe around every attention call.
+ *
+ * Results equal kore's own bit for bit: the Q8_K quantisation exactly, the
+ * products in the lane and summation order of kore's AVX2 kernels
+ * (kore.cpp:540-640, the ones kore runs on every AVX2/FMA CPU), the bias add
+ * as kore.cpp:1422-1423.
+ */
+#define KORE_CUDA_Q4_K 12   /* GGUF tensor type ids (kore.cpp:161) */
+#define KORE_CUDA_Q6_K 14
+
+typedef struct kore_cuda_qmat {
+    int type;           /* KORE_CUDA_Q4_K (144-byte blocks) or KORE_CUDA_Q6_K (210-byte blocks) */
+    int rows;           /* output values */
+    int cols;           /* input values, a multiple of 256 */
+    const void *data;   /* host, rows * cols/256 blocks in GGUF order (Tensor::data, kore.cpp:168) */
+} kore_cuda_qmat;
+
+/* Uploads one layer's attention projections (Layer::wq/wk/wv/wo, bq/bk/bv,
+ * kore.cpp:1246-1249) into device memory, replacing any earlier upload:
+ *   wq [n_head*head_dim x n_embd], wk, wv [n_head_kv*head_dim x n_embd],
+ *   wo [n_embd x n_head*head_dim], with n_embd = n_head*head_dim a multiple of
+ *   256 (engine_init's own condition, kore.cpp:1283);
+ *   bq [n_head*head_dim], bk, bv [n_head_kv*head_dim] fp32 host arrays, or
+ *   NULL for none. Synchronous. */
+int kore_cuda_set_attn_weights(kore_cuda_ctx *ctx, int layer, const kore_cuda_qmat *wq,
+                               const kore_cuda_qmat *wk, const kore_cuda_qmat *wv,
+                               const kore_cuda_qmat *wo, const float *bq, const float *bk,
+                               const float *bv);
+
+/* kore's mv() with quant() (kore.cpp:1388-1394) for one uploaded matrix of
+ * `layer` (which: 0 = wq, 1 = wk, 2 = wv, 3 = wo): out = W * quantize(x),
+ * plus the matrix's bias for wq/wk/wv. x [cols] and out [rows] are host
+ * arrays. */
+int kore_cuda_qmatvec(kore_cuda_ctx *ctx, int layer, int which, const float *x, float *out);
+
+/* One decode step of the attention block, kore.cpp:1419-1457 from the
+ * quantisation of xb to o = Wo * att: q/k/v projections + biases, RoPE,
+ * append of k/v at pos, attention over positions 0..pos (as
+ * kore_cuda_attn_decode), the quantisation of att and Wo.
+ *   xb: [n_embd] (kore's e.xb after the attention rmsnorm)
+ *   o:  [n_embd] (kore's e.o, before the residual add)
+ * On a context with shard_count > 1 the attention is the peer-exchange split
+ * (kore_cuda_attn_decode_sharded_dev; kore_cuda_peer_open first) and every
+ * rank computes the projections. The _dev form takes 16-byte aligned device
+ * pointers and is stream-ordered. */
+int kore_cuda_attn_block_decode(kore_cuda_ctx *ctx, int seq, int layer, int pos, const float *xb,
+                                float *o);
+int kore_cuda_attn_block_decode_dev(kore_cuda_ctx *ctx, int seq, int layer, int pos,
+                                    const float *xb, float *o);
+
+/*
  * KV-sequence split over GPUs (cfg.shard_count > 1). Each context holds the
  * positions of every page j with j % shard_count == shard_rank; a decode step
  * then runs in two parts:

@@ -54,6 +54,11 @@ class KvView(ctypes.Structure):
     ]
 
 
+class _QMat(ctypes.Structure):
+    """kore_cuda_qmat: one quantised weight matrix in host memory."""
+    _fields_ = [("type", ctypes.c_int), ("rows", ctypes.c_int), ("cols", ctypes.c_int), ("data", ctypes.c_void_p)]
+
+
 _lib = None
 _vp = ctypes.c_void_p
 _ip = ctypes.POINTER(ctypes.c_int)
@@ -102,6 +107,10 @@ def load_library(path: str = LIB):
     L.kore_cuda_attn_decode_sharded_dev.argtypes = [_vp, _i, _i, _i, _vp, _vp, _vp, _vp]
     L.kore_cuda_kv_read.argtypes = [_vp, _i, _i, _i, _i, _vp, _vp]
     L.kore_cuda_attn_decode_noalloc.argtypes = [ctypes.POINTER(KvView), _i, _vp, _vp, _vp, _vp, _vp, _vp]
+    L.kore_cuda_set_attn_weights.argtypes = [_vp, _i] + [ctypes.POINTER(_QMat)] * 4 + [_vp] * 3
+    L.kore_cuda_qmatvec.argtypes = [_vp, _i, _i, _vp, _vp]
+    for n in ("kore_cuda_attn_block_decode", "kore_cuda_attn_block_decode_dev"):
+        getattr(L, n).argtypes = [_vp, _i, _i, _i, _vp, _vp]
     L.kore_cuda_sync.argtypes = [_vp]
     L.kore_cuda_stream.argtypes = [_vp]
     L.kore_cuda_stream.restype = _vp
@@ -285,3 +294,34 @@ class KoreCuda:
     def prefill_dev(self, seq: int, layer: int, pos0: int, n: int, q, k, v, out) -> None:
         self._ck(self._L.kore_cuda_attn_prefill_dev(self._h, seq, layer, pos0, n, _dptr(q), _dptr(k), _dptr(v),
                                                     _dptr(out)))
+
+    # ---------------------------------------------------------------- attention block with its projections
+    def set_attn_weights(self, layer: int, wq, wk, wv, wo, bq=None, bk=None, bv=None) -> None:
+        """Uploads one layer's Wq, Wk, Wv, Wo (``qweights.QMat``) and biases."""
+        mats = [_QMat(m.type, m.rows, m.cols, m.data.ctypes.data) for m in (wq, wk, wv, wo)]
+        keep = [m.data for m in (wq, wk, wv, wo)]
+        if bq is None:
+            b = [None, None, None]
+        else:
+            b = [_host(bq, self.H * self.d), _host(bk, self.kvd), _host(bv, self.kvd)]
+        ptrs = [x.ctypes.data if x is not None else None for x in b]
+        self._ck(self._L.kore_cuda_set_attn_weights(self._h, layer, *[ctypes.byref(m) for m in mats], *ptrs))
+        del keep
+
+    def qmatvec(self, layer: int, which: int, x) -> np.ndarray:
+        """kore's mv() + quant() with an uploaded matrix (0 wq, 1 wk, 2 wv, 3 wo)."""
+        rows = self.H * self.d if which in (0, 3) else self.kvd
+        x = _host(x, self.H * self.d)
+        out = np.empty(rows, np.float32)
+        self._ck(self._L.kore_cuda_qmatvec(self._h, layer, which, x.ctypes.data, out.ctypes.data))
+        return out
+
+    def attn_block_decode(self, seq: int, layer: int, pos: int, xb) -> np.ndarray:
+        """kore.cpp:1419-1457 for one token: xb [n_embd] -> Wo*att [n_embd]."""
+        xb = _host(xb, self.H * self.d)
+        o = np.empty(self.H * self.d, np.float32)
+        self._ck(self._L.kore_cuda_attn_block_decode(self._h, seq, layer, pos, xb.ctypes.data, o.ctypes.data))
+        return o
+
+    def attn_block_decode_dev(self, seq: int, layer: int, pos: int, xb, o) -> None:
+        self._ck(self._L.kore_cuda_attn_block_decode_dev(self._h, seq, layer, pos, _dptr(xb), _dptr(o)))

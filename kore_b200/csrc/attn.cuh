@@ -1,6 +1,8 @@
 // attn.cuh — parameter blocks and launchers of the attention kernels.
 #pragma once
 
+#include <cstddef>
+#include <cstdint>
 #include <vector>
 
 #include <cuda_runtime.h>
@@ -109,6 +111,32 @@ void set_ctxless_error(const char *msg);
 size_t prefill_tile_bytes(int head_dim);
 // bytes of one split slot of PrefillParams::part
 size_t prefill_slot_bytes(int head_dim);
+// One weight matrix of a product launch: rows of GGUF blocks (type 12 = Q4_K,
+// 14 = Q6_K), out[r] = row r . x (+ bias[r]). The buffer holding w extends
+// at least 8 bytes past the matrix.
+struct QSeg {
+    const uint8_t *w;
+    const float *bias;
+    float *out;
+    int type, rows;
+};
+// Products of up to three matrices with one fp32 vector x [cols] (16-byte
+// aligned), quantised to Q8_K inside the kernel (proj.cu); `grid` CTAs, one
+// per SM. Every segment's row count is a multiple of 4; slot_bytes is what
+// qmatvec_smem_bytes gives for cols and the largest block size of the
+// segments; err receives DEV_WAIT_FULL_TIMEOUT if a weight copy never lands.
+struct QMatvecParams {
+    QSeg seg[3];
+    int n_seg;
+    int cols;
+    int slot_bytes;
+    const float *x;
+    int *err;
+};
+constexpr size_t kQmatvecMaxSmem = 227 * 1024;
+size_t qmatvec_smem_bytes(int cols, int max_block_bytes, int *slot_bytes);
+cudaError_t launch_qmatvec(const QMatvecParams &p, int grid, cudaStream_t s);
+
 // Work list of a prefill chunk (pos0, n) over H heads on num_sms SMs: one
 // item per (query head, 128-row query tile), the heaviest ones possibly split
 // in two key ranges, in the dispatch order that finishes first by a replay of

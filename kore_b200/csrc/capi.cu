@@ -76,6 +76,18 @@ struct kore_cuda_ctx {
     float *pf_part = nullptr;
     int *pf_counters = nullptr;
     int pf_slots_cap = 0;
+    // attention-block projections (proj.cu): per layer wq | wk | wv | wo in
+    // GGUF blocks, each 256-byte aligned with padding behind, and bq | bk | bv
+    struct LayerProj {
+        uint8_t *w = nullptr;
+        float *bias = nullptr;
+        bool has_bias = false;
+        int type[4] = {0, 0, 0, 0};
+        int rows[4] = {0, 0, 0, 0};
+        size_t off[4] = {0, 0, 0, 0};
+    };
+    std::vector<LayerProj> proj;
+    float *blk = nullptr;       // q [H*D] | k [kvd] | v [kvd] | att [H*D]
     std::string msg;
 };
 
@@ -423,6 +435,11 @@ void kore_cuda_destroy(kore_cuda_ctx *c) {
         cudaFree(c->pf_items);
         cudaFree(c->pf_part);
         cudaFree(c->pf_counters);
+        for (auto &lp : c->proj) {
+            cudaFree(lp.w);
+            cudaFree(lp.bias);
+        }
+        cudaFree(c->blk);
         cudaFree(c->kv);
         cudaFree(c->pt_d);
         cudaFree(c->rope_d);
@@ -846,6 +863,167 @@ int kore_cuda_attn_decode_batch(kore_cuda_ctx *c, int layer, int n_seq, const in
     if (!seq_ids || !pos || !q || !k || !v || !out) return fail(c, KORE_CUDA_EINVAL, "null argument");
     if (n_seq <= 0 || n_seq > kMaxBatch) return fail(c, KORE_CUDA_EINVAL, "n_seq %d outside [1, %d]", n_seq, kMaxBatch);
     return decode_host(c, n_seq, q, k, v, out, seq_ids, pos, layer, true);
+}
+
+// ---------------------------------------------------------------- attention block projections
+
+static size_t qmat_bytes(int type, int rows, int cols) {
+    return (size_t)rows * (size_t)(cols / 256) * (type == KORE_CUDA_Q4_K ? 144 : 210);
+}
+
+static int check_qmat(kore_cuda_ctx *c, const kore_cuda_qmat *m, const char *name, int rows, int cols) {
+    if (!m || !m->data) return fail(c, KORE_CUDA_EINVAL, "%s: null matrix or data", name);
+    if (m->type != KORE_CUDA_Q4_K && m->type != KORE_CUDA_Q6_K)
+        return fail(c, KORE_CUDA_EINVAL, "%s: type %d is neither Q4_K (12) nor Q6_K (14)", name, m->type);
+    if (m->rows != rows || m->cols != cols)
+        return fail(c, KORE_CUDA_EINVAL, "%s is %d x %d, expected %d x %d", name, m->rows, m->cols, rows, cols);
+    return KORE_CUDA_OK;
+}
+
+static const kore_cuda_ctx::LayerProj *layer_proj(kore_cuda_ctx *c, int layer) {
+    if (layer < 0 || layer >= (int)c->proj.size() || !c->proj[(size_t)layer].w) return nullptr;
+    return &c->proj[(size_t)layer];
+}
+
+// One product launch over up to three of a layer's matrices (which: 0 wq,
+// 1 wk, 2 wv, 3 wo) with the fp32 vector x (quantised in the kernel),
+// results to outs.
+static int launch_proj(kore_cuda_ctx *c, const kore_cuda_ctx::LayerProj &lp, const int *which, int n, const float *x,
+                       float *const *outs) {
+    const int E = c->H * c->D;
+    QMatvecParams mp;
+    memset(&mp, 0, sizeof mp);
+    mp.x = x;
+    mp.cols = E;
+    for (int i = 0; i < n; ++i) {
+        const int w = which[i];
+        QSeg &g = mp.seg[i];
+        g.w = lp.w + lp.off[w];
+        g.type = lp.type[w];
+        g.rows = lp.rows[w];
+        g.out = outs[i];
+        g.bias = (w < 3 && lp.has_bias) ? lp.bias + (w == 0 ? 0 : (w == 1 ? E : E + c->kvd)) : nullptr;
+    }
+    mp.n_seg = n;
+    int bb = 0;
+    for (int i = 0; i < n; ++i) bb = std::max(bb, mp.seg[i].type == KORE_CUDA_Q4_K ? 144 : 210);
+    qmatvec_smem_bytes(E, bb, &mp.slot_bytes);
+    mp.err = c->err_d;
+    CK(launch_qmatvec(mp, c->num_sms, c->stream));
+    return KORE_CUDA_OK;
+}
+
+int kore_cuda_set_attn_weights(kore_cuda_ctx *c, int layer, const kore_cuda_qmat *wq, const kore_cuda_qmat *wk,
+                               const kore_cuda_qmat *wv, const kore_cuda_qmat *wo, const float *bq, const float *bk,
+                               const float *bv) {
+    if (!c) return KORE_CUDA_EINVAL;
+    if (layer < 0 || layer >= c->cfg.n_layer)
+        return fail(c, KORE_CUDA_ERANGE, "layer %d outside [0, %d)", layer, c->cfg.n_layer);
+    const int E = c->H * c->D;
+    if (E % 256) return fail(c, KORE_CUDA_EINVAL, "n_embd = %d is not a multiple of 256", E);
+    if ((bq == nullptr) != (bk == nullptr) || (bq == nullptr) != (bv == nullptr))
+        return fail(c, KORE_CUDA_EINVAL, "bq, bk and bv must be all given or all NULL");
+    const kore_cuda_qmat *m[4] = {wq, wk, wv, wo};
+    const int rows[4] = {E, c->kvd, c->kvd, E};
+    const char *names[4] = {"wq", "wk", "wv", "wo"};
+    for (int i = 0; i < 4; ++i)
+        if (int rc = check_qmat(c, m[i], names[i], rows[i], E)) return rc;
+    if (qmatvec_smem_bytes(E, 210, nullptr) > kQmatvecMaxSmem)
+        return fail(c, KORE_CUDA_EINVAL, "n_embd = %d: a product launch's staging exceeds shared memory", E);
+    DeviceGuard dg(c->cfg.device);
+    if (c->proj.empty()) c->proj.resize((size_t)c->cfg.n_layer);
+    auto &lp = c->proj[(size_t)layer];
+    // kernels still queued may read this layer's previous weights
+    CK(cudaStreamSynchronize(c->stream));
+    cudaFree(lp.w);
+    cudaFree(lp.bias);
+    lp = kore_cuda_ctx::LayerProj();
+    size_t off[4], total = 0;
+    for (int i = 0; i < 4; ++i) {
+        off[i] = total;
+        total += align256(qmat_bytes(m[i]->type, rows[i], E) + 16);   // the product kernel reads up to 8 bytes past a matrix
+    }
+    uint8_t *w = nullptr;
+    CK(cudaMalloc(&w, total));
+    lp.w = w;
+    for (int i = 0; i < 4; ++i) CK(cudaMemcpy(w + off[i], m[i]->data, qmat_bytes(m[i]->type, rows[i], E), cudaMemcpyHostToDevice));
+    if (bq) {
+        float *b = nullptr;
+        CK(cudaMalloc(&b, (size_t)(E + 2 * c->kvd) * sizeof(float)));
+        lp.bias = b;
+        CK(cudaMemcpy(b, bq, (size_t)E * sizeof(float), cudaMemcpyHostToDevice));
+        CK(cudaMemcpy(b + E, bk, (size_t)c->kvd * sizeof(float), cudaMemcpyHostToDevice));
+        CK(cudaMemcpy(b + E + c->kvd, bv, (size_t)c->kvd * sizeof(float), cudaMemcpyHostToDevice));
+        lp.has_bias = true;
+    }
+    if (!c->blk) {
+        CK(cudaMalloc(&c->blk, (size_t)(2 * E + 2 * c->kvd) * sizeof(float)));
+    }
+    for (int i = 0; i < 4; ++i) {
+        lp.type[i] = m[i]->type;
+        lp.rows[i] = rows[i];
+        lp.off[i] = off[i];
+    }
+    return KORE_CUDA_OK;
+}
+
+int kore_cuda_qmatvec(kore_cuda_ctx *c, int layer, int which, const float *x, float *out) {
+    if (!c) return KORE_CUDA_EINVAL;
+    if (!x || !out) return fail(c, KORE_CUDA_EINVAL, "null x or out");
+    if (which < 0 || which > 3) return fail(c, KORE_CUDA_EINVAL, "which = %d is not 0 (wq), 1 (wk), 2 (wv) or 3 (wo)", which);
+    const kore_cuda_ctx::LayerProj *lp = layer_proj(c, layer);
+    if (!lp) return fail(c, KORE_CUDA_ESTATE, "no attention weights for layer %d (kore_cuda_set_attn_weights)", layer);
+    DeviceGuard dg(c->cfg.device);
+    const int E = c->H * c->D, rows = lp->rows[which];
+    if (int rc = grow_stage(c, (size_t)E + rows)) return rc;
+    float *hs = c->host_stage, *ds = c->dev_stage;
+    memcpy(hs, x, (size_t)E * sizeof(float));
+    CK(cudaMemcpyAsync(ds, hs, (size_t)E * sizeof(float), cudaMemcpyHostToDevice, c->stream));
+    float *od = ds + E;
+    if (int rc = launch_proj(c, *lp, &which, 1, ds, &od)) return rc;
+    CK(cudaMemcpyAsync(hs + E, od, (size_t)rows * sizeof(float), cudaMemcpyDeviceToHost, c->stream));
+    if (int rc = finish(c)) return rc;
+    memcpy(out, hs + E, (size_t)rows * sizeof(float));
+    return KORE_CUDA_OK;
+}
+
+int kore_cuda_attn_block_decode_dev(kore_cuda_ctx *c, int seq, int layer, int pos, const float *xb, float *o) {
+    if (!c) return KORE_CUDA_EINVAL;
+    if (!xb || !o) return fail(c, KORE_CUDA_EINVAL, "null xb or o");
+    if ((reinterpret_cast<uintptr_t>(xb) | reinterpret_cast<uintptr_t>(o)) & 15)
+        return fail(c, KORE_CUDA_EINVAL, "xb and o must be 16-byte aligned device buffers");
+    if (int rc = check_range(c, seq, layer, pos, 1)) return rc;
+    const kore_cuda_ctx::LayerProj *lp = layer_proj(c, layer);
+    if (!lp) return fail(c, KORE_CUDA_ESTATE, "no attention weights for layer %d (kore_cuda_set_attn_weights)", layer);
+    if (c->NS > 1 && !c->peers_open)
+        return fail(c, KORE_CUDA_ESTATE, "a KV-split context needs kore_cuda_peer_open before the attention block");
+    DeviceGuard dg(c->cfg.device);
+    const int E = c->H * c->D;
+    float *q = c->blk, *k = q + E, *v = k + c->kvd, *att = v + c->kvd;
+    const int qkv[3] = {0, 1, 2};
+    float *const outs[3] = {q, k, v};
+    if (int rc = launch_proj(c, *lp, qkv, 3, xb, outs)) return rc;
+    if (int rc = c->NS > 1 ? kore_cuda_attn_decode_sharded_dev(c, seq, layer, pos, q, k, v, att)
+                           : kore_cuda_attn_decode_dev(c, seq, layer, pos, q, k, v, att))
+        return rc;
+    const int wo = 3;
+    return launch_proj(c, *lp, &wo, 1, att, &o);
+}
+
+int kore_cuda_attn_block_decode(kore_cuda_ctx *c, int seq, int layer, int pos, const float *xb, float *o) {
+    if (!c) return KORE_CUDA_EINVAL;
+    if (!xb || !o) return fail(c, KORE_CUDA_EINVAL, "null xb or o");
+    DeviceGuard dg(c->cfg.device);
+    const int E = c->H * c->D;
+    if (int rc = grow_stage(c, (size_t)E)) return rc;
+    memcpy(c->host_stage, xb, (size_t)E * sizeof(float));
+    CK(cudaMemcpyAsync(c->dev_stage, c->host_stage, (size_t)E * sizeof(float), cudaMemcpyHostToDevice, c->stream));
+    // the output lands right behind the error word and both come back in one copy
+    float *dout = reinterpret_cast<float *>(reinterpret_cast<char *>(c->err_d) + kErrPad);
+    if (int rc = kore_cuda_attn_block_decode_dev(c, seq, layer, pos, c->dev_stage, dout)) return rc;
+    if (int rc = finish(c, (size_t)E * sizeof(float))) return rc;
+    memcpy(o, reinterpret_cast<const char *>(c->host_err) + kErrPad, (size_t)E * sizeof(float));
+    return KORE_CUDA_OK;
 }
 
 int kore_cuda_kv_read(kore_cuda_ctx *c, int seq, int layer, int pos0, int n, float *k_out, float *v_out) {

@@ -1,5 +1,6 @@
 // engine_harness.cpp — greedy token-ID parity: the REFERENCE engine against
-// the same engine with its attention regions served by the CUDA library.
+// the same engine with its attention regions, or its whole attention blocks,
+// served by the CUDA library.
 //
 // TEST INFRASTRUCTURE ONLY. oracle/Makefile compiles this file with kore's own
 // flags (build.sh:10, -std=c++20 -O3 -pthread) into
@@ -9,7 +10,7 @@
 // A seeded random-init Qwen2-style model is built in memory: the tensors
 // engine_init asks for (kore.cpp:1316-1330), projection weights as Q4_K blocks
 // of random nibbles and scales (valid by construction: every byte pattern
-// decodes), norms near 1 and biases as F32, token embeddings as F32. Two
+// decodes), norms near 1 and biases as F32, token embeddings as F32. Three
 // greedy decoders then run on it:
 //   * the reference: kore's forward_batch() over the prompt in chunks of
 //     e.bsz tokens, then forward() + sample_token(temp 0) per generated token
@@ -21,7 +22,12 @@
 //     each to kore_cuda_attn_decode / kore_cuda_attn_prefill, resolved from
 //     the library with dlopen. The projections see the same inputs in the
 //     same order, so the only arithmetic that differs is the attention's.
-// The test compares the two ID sequences; the reference's top-1/top-2 logit
+//   * the CUDA block path: as the CUDA path, but each decode step's whole
+//     attention block (kore.cpp:1419-1457: Q8_K quantisation of xb, the
+//     Wq/Wk/Wv products and biases, the attention, the quantisation of att
+//     and Wo) is one call to kore_cuda_attn_block_decode, with kore's own
+//     weight tensors uploaded once by kore_cuda_set_attn_weights.
+// The test compares the ID sequences; the reference's top-1/top-2 logit
 // margin per step is returned so that a mismatch can be told apart from a
 // near tie.
 
@@ -45,6 +51,10 @@ using fn_last_error = const char *(*)(const kore_cuda_ctx *);
 using fn_seq_reset = int (*)(kore_cuda_ctx *, int);
 using fn_decode = int (*)(kore_cuda_ctx *, int, int, int, const float *, const float *, const float *, float *);
 using fn_prefill = int (*)(kore_cuda_ctx *, int, int, int, int, const float *, const float *, const float *, float *);
+using fn_set_weights = int (*)(kore_cuda_ctx *, int, const kore_cuda_qmat *, const kore_cuda_qmat *,
+                               const kore_cuda_qmat *, const kore_cuda_qmat *, const float *, const float *,
+                               const float *);
+using fn_block = int (*)(kore_cuda_ctx *, int, int, int, const float *, float *);
 
 struct Harness {
     Model m;
@@ -59,6 +69,9 @@ struct Harness {
     fn_seq_reset seq_reset = nullptr;
     fn_decode decode = nullptr;
     fn_prefill prefill = nullptr;
+    fn_set_weights set_weights = nullptr;
+    fn_block block = nullptr;
+    bool weights_up = false;
 };
 
 uint16_t f32_to_f16(float f) {   // round to nearest, normal and subnormal range
@@ -173,6 +186,68 @@ bool cuda_forward(Harness &hx, int token, int pos, bool want_logits) {
         quant(e, e.xb.data(), e.xq_e.data(), E);
         mv(e, *e.out_w, e.xb.data(), e.xq_e.data(), e.logits.data());
     }
+    return true;
+}
+
+// kore's forward() with the whole attention block (kore.cpp:1419-1457: the
+// quantisation of xb, the q/k/v projections and biases, the attention, the
+// quantisation of att and Wo) in one library call, xb in and e.o out.
+bool cuda_forward_block(Harness &hx, int token, int pos, bool want_logits) {
+    Engine &e = hx.e;
+    const Hparams &h = e.hp;
+    const int E = (int)h.n_embd, FF = (int)h.n_ff;
+    if (token < 0 || token >= e.n_vocab || pos < 0 || pos >= e.ctx) return false;
+    if (!get_row(*e.tok_embd, (uint64_t)token, e.emb)) return false;
+    std::copy(e.emb.begin(), e.emb.begin() + E, e.x.begin());
+    for (uint32_t l = 0; l < h.n_layer; l++) {
+        const Layer &L = e.layers[l];
+        rmsnorm(e.xb.data(), e.x.data(), L.attn_norm, E, h.rms_eps);
+        if (hx.block(hx.ctx, 0, (int)l, pos, e.xb.data(), e.o.data()) != KORE_CUDA_OK) {
+            hx.err = hx.last_error(hx.ctx);
+            return false;
+        }
+        for (int i = 0; i < E; i++) e.x[(size_t)i] += e.o[(size_t)i];
+        rmsnorm(e.xb.data(), e.x.data(), L.ffn_norm, E, h.rms_eps);
+        quant(e, e.xb.data(), e.xq_e.data(), E);
+        mv(e, *L.w_gate, e.xb.data(), e.xq_e.data(), e.gate.data());
+        mv(e, *L.w_up, e.xb.data(), e.xq_e.data(), e.up.data());
+        for (int i = 0; i < FF; i++) {
+            const float g = e.gate[(size_t)i];
+            e.gate[(size_t)i] = g / (1.0f + std::exp(-g)) * e.up[(size_t)i];
+        }
+        quant(e, e.gate.data(), e.xq_f.data(), FF);
+        mv(e, *L.w_down, e.gate.data(), e.xq_f.data(), e.o.data());
+        for (int i = 0; i < E; i++) e.x[(size_t)i] += e.o[(size_t)i];
+    }
+    if (want_logits) {
+        rmsnorm(e.xb.data(), e.x.data(), e.out_norm, E, h.rms_eps);
+        quant(e, e.xb.data(), e.xq_e.data(), E);
+        mv(e, *e.out_w, e.xb.data(), e.xq_e.data(), e.logits.data());
+    }
+    return true;
+}
+
+kore_cuda_qmat as_qmat(const Tensor &t) {
+    kore_cuda_qmat m;
+    m.type = (int)t.type;
+    m.cols = (int)t.dims[0];
+    m.rows = (int)(t.dims[1] * t.dims[2] * t.dims[3]);
+    m.data = t.data;
+    return m;
+}
+
+// Uploads every layer's attention projections and biases (kore's own tensors).
+bool upload_attn_weights(Harness &hx) {
+    if (hx.weights_up) return true;
+    for (uint32_t l = 0; l < hx.e.hp.n_layer; l++) {
+        const Layer &L = hx.e.layers[l];
+        const kore_cuda_qmat q = as_qmat(*L.wq), k = as_qmat(*L.wk), v = as_qmat(*L.wv), o = as_qmat(*L.wo);
+        if (hx.set_weights(hx.ctx, (int)l, &q, &k, &v, &o, L.bq, L.bk, L.bv) != KORE_CUDA_OK) {
+            hx.err = hx.last_error(hx.ctx);
+            return false;
+        }
+    }
+    hx.weights_up = true;
     return true;
 }
 
@@ -341,6 +416,8 @@ int keng_attach_cuda(void *h, const char *lib_path, int device) {
     hx.seq_reset = (fn_seq_reset)dlsym(hx.lib, "kore_cuda_seq_reset");
     hx.decode = (fn_decode)dlsym(hx.lib, "kore_cuda_attn_decode");
     hx.prefill = (fn_prefill)dlsym(hx.lib, "kore_cuda_attn_prefill");
+    hx.set_weights = (fn_set_weights)dlsym(hx.lib, "kore_cuda_set_attn_weights");
+    hx.block = (fn_block)dlsym(hx.lib, "kore_cuda_attn_block_decode");
     if (!cfg_default || !create || !hx.destroy || !hx.last_error || !hx.seq_reset || !hx.decode || !hx.prefill) {
         hx.err = "missing symbol in the CUDA library";
         return -1;
@@ -375,6 +452,26 @@ int keng_generate_cuda(void *h, const int *prompt, int n_prompt, int n_gen, int 
         hx, prompt, n_prompt, n_gen, ids, nullptr,
         [&](const int *t, int nb, int p0, bool last) { return cuda_forward_batch(hx, t, nb, p0, last); },
         [&](int tok, int pos) { return cuda_forward(hx, tok, pos, true); });
+}
+
+// Greedy IDs with the attention block of every decode step on the GPU,
+// projections included (the prompt's chunks as in keng_generate_cuda).
+int keng_generate_cuda_block(void *h, const int *prompt, int n_prompt, int n_gen, int *ids) {
+    Harness &hx = *(Harness *)h;
+    hx.err.clear();
+    if (!hx.ctx || !hx.set_weights || !hx.block) {
+        hx.err = "no CUDA context with the attention-block entry points (keng_attach_cuda)";
+        return -1;
+    }
+    if (!upload_attn_weights(hx)) return -1;
+    if (hx.seq_reset(hx.ctx, 0) != KORE_CUDA_OK) {
+        hx.err = hx.last_error(hx.ctx);
+        return -1;
+    }
+    return generate(
+        hx, prompt, n_prompt, n_gen, ids, nullptr,
+        [&](const int *t, int nb, int p0, bool last) { return cuda_forward_batch(hx, t, nb, p0, last); },
+        [&](int tok, int pos) { return cuda_forward_block(hx, tok, pos, true); });
 }
 
 }  // extern "C"

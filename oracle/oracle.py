@@ -3,8 +3,9 @@
 Only tests/, ``__graft_entry__.smoke()`` and bench.py's CPU-baseline leg import
 this module. It loads
 
-* ``oracle/_build/libkore_oracle.so`` — the C restatement of kore's attention
-  (kore_attn_oracle.c), and
+* ``oracle/_build/libkore_oracle.so`` — the C restatements of kore's attention
+  (kore_attn_oracle.c) and of its Q8_K / Q4_K / Q6_K projections
+  (kore_proj_oracle.c), and
 * ``oracle/_ref/libkore_ref.so`` — the reference engine itself (kore.cpp,
   compiled in place by oracle/Makefile) driven through ref_harness.cpp, and
 * ``oracle/_ref/libkore_engine.so`` — the reference engine with
@@ -63,6 +64,12 @@ def lib():
         L.korc_attn_prefill.argtypes = ([ctypes.c_int] * 3 + [_f32p, ctypes.c_int, ctypes.c_int]
                                         + [_f32p] * 7 + [ctypes.c_int])
         L.korc_argmax.argtypes = [_f32p, ctypes.c_int]
+        vp = ctypes.c_void_p
+        L.korc_q8k_quantize.argtypes = [vp, ctypes.c_int, vp, vp, vp]
+        for n in ("korc_dot_q4k", "korc_dot_q6k"):
+            getattr(L, n).argtypes = [ctypes.c_int, vp, vp, vp, vp, ctypes.c_int]
+            getattr(L, n).restype = ctypes.c_float
+        L.korc_qmatvec.argtypes = [ctypes.c_int] * 3 + [vp] * 4 + [ctypes.c_int]
         _oracle = L
     return _oracle
 
@@ -91,8 +98,60 @@ def ref_lib():
         L.kref_prefill.argtypes = [ctypes.c_void_p, ctypes.c_int, ctypes.c_int, _f32p, _f32p, _f32p, _f32p]
         L.kref_argmax.argtypes = [_f32p, ctypes.c_int]
         L.kref_now_ms.restype = ctypes.c_double
+        vp = ctypes.c_void_p
+        L.kref_q8k_quantize.argtypes = [vp, ctypes.c_int, vp, vp, vp]
+        L.kref_qdot.argtypes = [ctypes.c_int, ctypes.c_int, vp, vp, vp, vp, ctypes.c_int]
+        L.kref_qdot.restype = ctypes.c_float
         _ref = L
     return _ref
+
+
+# ----------------------------------------------------------------- projections (kore_proj_oracle.c)
+
+def _q8k_call(fn, x: np.ndarray):
+    x = np.ascontiguousarray(x, np.float32).reshape(-1)
+    n = x.size
+    d = np.zeros(n // 256, np.float32)
+    qs = np.zeros(n, np.int8)
+    bs = np.zeros(n // 16, np.int16)
+    fn(x.ctypes.data, n, d.ctypes.data, qs.ctypes.data, bs.ctypes.data)
+    return d, qs, bs
+
+
+def q8k_quantize(x: np.ndarray):
+    """kore.cpp:422-447 restated: (d [n/256], qs [n] int8, bsums [n/16] int16)."""
+    return _q8k_call(lib().korc_q8k_quantize, x)
+
+
+def ref_q8k_quantize(x: np.ndarray):
+    """The reference's own quantize_row_q8_K."""
+    return _q8k_call(ref_lib().kref_q8k_quantize, x)
+
+
+def qdot(qtype: int, wrow: np.ndarray, xq, avx2: bool = True) -> np.float32:
+    """One row (uint8 blocks) against Q8_K xq, restated (AVX2 lane order or scalar)."""
+    d, qs, bs = xq
+    fn = lib().korc_dot_q4k if qtype == 12 else lib().korc_dot_q6k
+    return np.float32(fn(qs.size, wrow.ctypes.data, d.ctypes.data, qs.ctypes.data, bs.ctypes.data, int(avx2)))
+
+
+def ref_qdot(qtype: int, wrow: np.ndarray, xq, avx2: bool = True) -> np.float32:
+    """The reference's own dot_q4_K_q8_K / dot_q6_K_q8_K (its AVX2 kernel if avx2 and the CPU has it)."""
+    d, qs, bs = xq
+    return np.float32(ref_lib().kref_qdot(qtype, qs.size, wrow.ctypes.data, d.ctypes.data, qs.ctypes.data,
+                                          bs.ctypes.data, int(avx2)))
+
+
+def qmatvec(m, x: np.ndarray, bias=None, avx2: bool = True) -> np.ndarray:
+    """kore's mv() + quant() (+ bias) restated: m has .type, .rows, .cols, .data (uint8)."""
+    x = np.ascontiguousarray(x, np.float32).reshape(-1)
+    assert x.size == m.cols
+    out = np.empty(m.rows, np.float32)
+    b = None if bias is None else np.ascontiguousarray(bias, np.float32)
+    rc = lib().korc_qmatvec(m.type, m.rows, m.cols, m.data.ctypes.data, x.ctypes.data,
+                            None if b is None else b.ctypes.data, out.ctypes.data, int(avx2))
+    assert rc == 0
+    return out
 
 
 # ----------------------------------------------------------------- restatement
@@ -244,14 +303,17 @@ def engine_lib():
         L.keng_generate_ref.argtypes = [vp, ip, ctypes.c_int, ctypes.c_int, ip, fp]
         L.keng_attach_cuda.argtypes = [vp, ctypes.c_char_p, ctypes.c_int]
         L.keng_generate_cuda.argtypes = [vp, ip, ctypes.c_int, ctypes.c_int, ip]
+        L.keng_generate_cuda_block.argtypes = [vp, ip, ctypes.c_int, ctypes.c_int, ip]
         _engine = L
     return _engine
 
 
 class GreedyEngine:
     """A seeded random-init Qwen2-style model inside the reference engine, with
-    greedy generation by kore itself (``generate_ref``) and by kore with its
-    attention on the CUDA library (``generate_cuda``, after ``attach_cuda``)."""
+    greedy generation by kore itself (``generate_ref``), by kore with its
+    attention on the CUDA library (``generate_cuda``, after ``attach_cuda``)
+    and by kore with each decode step's whole attention block, projections
+    included, on the CUDA library (``generate_cuda_block``)."""
 
     def __init__(self, n_layer: int, n_embd: int, n_head: int, n_head_kv: int, n_ff: int, n_vocab: int,
                  ctx: int, seed: int = 12345, threads: int = 0):
@@ -293,5 +355,14 @@ class GreedyEngine:
         ids = np.zeros(n_gen, np.int32)
         ip = ctypes.POINTER(ctypes.c_int)
         if engine_lib().keng_generate_cuda(self.h, p.ctypes.data_as(ip), len(p), n_gen, ids.ctypes.data_as(ip)) != n_gen:
+            raise RuntimeError(self._err())
+        return ids
+
+    def generate_cuda_block(self, prompt, n_gen: int):
+        p = np.ascontiguousarray(prompt, np.int32)
+        ids = np.zeros(n_gen, np.int32)
+        ip = ctypes.POINTER(ctypes.c_int)
+        if engine_lib().keng_generate_cuda_block(self.h, p.ctypes.data_as(ip), len(p), n_gen,
+                                                 ids.ctypes.data_as(ip)) != n_gen:
             raise RuntimeError(self._err())
         return ids

@@ -188,4 +188,32 @@ int kref_argmax(const float *logits, int n) {
 
 double kref_now_ms(void) { return now_ms(); }
 
+// kore's own Q8_K quantisation (kore.cpp:422-447), unpacked into the arrays
+// d[n/256], qs[n], bsums[n/16].
+void kref_q8k_quantize(const float *x, int n, float *d, int8_t *qs, int16_t *bsums) {
+    std::vector<BlockQ8K> y((size_t)(n / 256));
+    quantize_row_q8_K(x, y.data(), n);
+    for (size_t i = 0; i < y.size(); i++) {
+        d[i] = y[i].d;
+        memcpy(qs + 256 * i, y[i].qs, 256);
+        memcpy(bsums + 16 * i, y[i].bsums, sizeof(y[i].bsums));
+    }
+}
+
+// kore's own dot product of one quantised row (type 12 = Q4_K, 14 = Q6_K)
+// with Q8_K x given as arrays: the AVX2 kernel (kore.cpp:540-640) when avx2
+// is set and the CPU has AVX2/FMA, else the scalar one (kore.cpp:451-507).
+float kref_qdot(int type, int n, const uint8_t *w, const float *d, const int8_t *qs, const int16_t *bsums,
+                int avx2) {
+    std::vector<BlockQ8K> y((size_t)(n / 256));
+    for (size_t i = 0; i < y.size(); i++) {
+        y[i].d = d[i];
+        memcpy(y[i].qs, qs + 256 * i, 256);
+        memcpy(y[i].bsums, bsums + 16 * i, sizeof(y[i].bsums));
+    }
+    const bool v = avx2 && cpu_has_avx2();
+    if (type == GGML_Q4_K) return v ? dot_q4_K_q8_K_avx2(n, w, y.data()) : dot_q4_K_q8_K_ref(n, w, y.data());
+    return v ? dot_q6_K_q8_K_avx2(n, w, y.data()) : dot_q6_K_q8_K_ref(n, w, y.data());
+}
+
 }  // extern "C"

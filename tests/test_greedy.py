@@ -56,3 +56,24 @@ def test_greedy_ids_identical(geo):
     assert mismatch.size == 0, (
         f"{name}: first mismatch at step {mismatch[0]} (ref {ref[mismatch[0]]}, cuda {got[mismatch[0]]}, "
         f"reference top-1/top-2 margin there {margins[mismatch[0]]:.3g}; min margin {margins.min():.3g})")
+
+
+@pytest.mark.gpu
+@needs_engine
+@pytest.mark.parametrize("geo", GEOMETRIES, ids=[g[0] for g in GEOMETRIES])
+def test_greedy_ids_identical_with_attention_block_on_gpu(geo):
+    """Each decode step's whole attention block on the GPU: the Q8_K
+    quantisations and the Q4_K Wq/Wk/Wv/Wo products (bit-exact with kore's
+    AVX2 kernels) and the attention (within tolerance)."""
+    import torch
+    assert torch.cuda.is_available()
+    name, L, E, H, G, FF, V, n_prompt, n_gen = geo
+    eng = O.GreedyEngine(L, E, H, G, FF, V, ctx=n_prompt + n_gen + 8, seed=12345)
+    prompt = np.random.default_rng(2024).integers(0, V, n_prompt)
+    ref, margins = eng.generate_ref(prompt, n_gen)
+    eng.attach_cuda(LIB, 0)
+    got = eng.generate_cuda_block(prompt, n_gen)
+    mismatch = np.nonzero(ref != got)[0]
+    assert mismatch.size == 0, (
+        f"{name}: first mismatch at step {mismatch[0]} (ref {ref[mismatch[0]]}, cuda {got[mismatch[0]]}, "
+        f"reference top-1/top-2 margin there {margins[mismatch[0]]:.3g}; min margin {margins.min():.3g})")
