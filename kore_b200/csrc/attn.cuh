@@ -122,7 +122,7 @@ struct QSeg {
 };
 // Products of up to three matrices with one fp32 vector x [cols] (16-byte
 // aligned), quantised to Q8_K inside the kernel (proj.cu); `grid` CTAs, one
-// per SM. Every segment's row count is a multiple of 4; slot_bytes is what
+// per SM. Every segment's row count is even; slot_bytes is what
 // qmatvec_smem_bytes gives for cols and the largest block size of the
 // segments; err receives DEV_WAIT_FULL_TIMEOUT if a weight copy never lands.
 struct QMatvecParams {
