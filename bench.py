@@ -67,6 +67,7 @@ def parse():
     ap.add_argument("--batched-steps", type=int, default=20)
     ap.add_argument("--no-block", action="store_true", help="skip the attention-block (with projections) line")
     ap.add_argument("--block-steps", type=int, default=100)
+    ap.add_argument("--block-only", action="store_true", help="measure only the attention block (development)")
     ap.add_argument("--prefill-only", action="store_true", help="measure only the prefill (development)")
     a = ap.parse_args()
     global L, POS, CTX
@@ -310,6 +311,31 @@ def run_ours(args, rank: int, world: int, dist) -> dict | None:
     if not args.no_prefill and world == 1:
         line["prefill"] = run_prefill(args, torch.device("cuda", 0), peaks)
     return line
+
+
+def run_block_only(args) -> dict:
+    """The attention-block line alone, on a context set up as run_ours sets it up."""
+    import torch
+    import kore_b200 as K
+
+    dev = torch.device("cuda", 0)
+    torch.cuda.set_device(dev)
+    ctx = K.KoreCuda(L, H, G, D, CTX, device=0)
+    stream = torch.cuda.Stream(device=dev)
+    ctx.set_stream(stream.cuda_stream)
+    gen = torch.Generator(device=dev)
+    with torch.cuda.stream(stream):
+        for layer in range(L):
+            gen.manual_seed(1000 + layer)
+            k = torch.randn(POS, KVD, device=dev, generator=gen)
+            v = torch.randn(POS, KVD, device=dev, generator=gen)
+            ctx.append_dev(0, layer, 0, POS, k, v)
+            del k, v
+    ctx.sync()
+    try:
+        return run_block(args, ctx, stream, dev)
+    finally:
+        ctx.close()
 
 
 def run_block(args, ctx, stream, dev) -> dict:
@@ -706,6 +732,9 @@ def main():
     if args.prefill_only:
         import torch
         print(json.dumps(run_prefill(args, torch.device("cuda", 0), load_peaks())), flush=True)
+        return
+    if args.block_only:
+        print(json.dumps(run_block_only(args)), flush=True)
         return
     try:
         line = run_ours(args, rank, world, dist)
