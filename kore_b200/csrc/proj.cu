@@ -311,11 +311,11 @@ __device__ __forceinline__ int find_seg(const QMatvecParams &p, int g, int &row)
 
 // One CTA per SM, kWarps warps. A warp takes groups of 2 consecutive rows
 // (16 lanes per row: lane (h2, k) computes AVX2 lane k over one half of the
-// blocks), group gw first and then every TW-th; every segment's row count is
-// even, so a group lies in one segment and its rows are one contiguous byte
-// range, which one bulk copy brings into the warp's shared-memory slot. The
-// first group's copy is issued before the dependency wait (weights do not
-// depend on the preceding kernel).
+// blocks), group warp*grid + cta first and then every TW-th. Every segment's
+// row count is even, so a group lies in one segment and its rows are one
+// contiguous byte range, which one bulk copy brings into the warp's
+// shared-memory slot. The first group's copy is issued before the dependency
+// wait (weights do not depend on the preceding kernel).
 __global__ void __launch_bounds__(32 * kWarps) qmatvec_kernel(const __grid_constant__ QMatvecParams p) {
     extern __shared__ __align__(16) uint8_t smem[];
     const int nb = p.cols / 256, hb = (nb + 1) >> 1;
@@ -334,7 +334,9 @@ __global__ void __launch_bounds__(32 * kWarps) qmatvec_kernel(const __grid_const
     int R = 0;
     for (int s = 0; s < p.n_seg; ++s) R += p.seg[s].rows;
     const int n_groups = R / 2, TW = (int)gridDim.x * kWarps;
-    const int gg0 = (int)blockIdx.x * kWarps + warp;
+    // groups warp-major over the grid: consecutive groups (and so each
+    // matrix's rows, e.g. a Q6_K Wv among Q4_K ones) spread over all SMs
+    const int gg0 = warp * (int)gridDim.x + (int)blockIdx.x;
     if (lane == 0) {
         mbar_init(bar, 1);
         mbar_fence_init();
