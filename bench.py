@@ -307,6 +307,16 @@ def run_ours(args, rank: int, world: int, dist) -> dict | None:
     if not args.no_cpu_baseline and world == 1:
         line["cpu_baseline"] = cpu_baseline_sample()
     if block is not None:
+        proj_ms = block.pop("_cpu_proj_ms", None)
+        att = line.get("cpu_baseline", {}).get("attention_ms")
+        if proj_ms is not None and att is not None:
+            per_layer = block["weight_bytes_per_step"] / L + layer_bytes(POS)
+            block["cpu_baseline"] = {
+                "value": round(per_layer / ((att + proj_ms) * 1e-3) / 1e9, 3), "unit": "GB/s", "cores": 1,
+                "kind": "reference",
+                "sample": f"1 of 28 layers: kore's attention at pos {POS} ({att:.1f} ms, as cpu_baseline) + "
+                          f"kore's quantize_row_q8_K + matvec_mt of Wq, Wk, Wv, Wo on 1 thread "
+                          f"(best of 3, {proj_ms:.2f} ms)"}
         line["attn_block"] = block
     if not args.no_prefill and world == 1:
         line["prefill"] = run_prefill(args, torch.device("cuda", 0), peaks)
@@ -333,7 +343,9 @@ def run_block_only(args) -> dict:
             del k, v
     ctx.sync()
     try:
-        return run_block(args, ctx, stream, dev)
+        d = run_block(args, ctx, stream, dev)
+        d.pop("_cpu_proj_ms", None)
+        return d
     finally:
         ctx.close()
 
@@ -352,11 +364,14 @@ def run_block(args, ctx, stream, dev) -> dict:
     E = H * D
     rng = np.random.default_rng(77)
     w_bytes = 0
+    mats0 = None
     for layer in range(L):
         mats = [random_qmat(t, r, E, rng) for t, r in ((Q4_K, E), (Q4_K, KVD), (Q6_K, KVD), (Q4_K, E))]
         w_bytes += sum(m.nbytes for m in mats)
         b = [rng.standard_normal(n).astype(np.float32) for n in (E, KVD, KVD)]
         ctx.set_attn_weights(layer, *mats, *b)
+        if mats0 is None:
+            mats0 = mats
     gen = torch.Generator(device=dev)
     gen.manual_seed(78)
     with torch.cuda.stream(stream):
@@ -406,6 +421,15 @@ def run_block(args, ctx, stream, dev) -> dict:
         for layer in range(L):
             ctx.attn_block_decode(0, layer, POS, hx[layer])
     e2e_ms = (time.perf_counter() - t0) * 1e3 / n_e2e
+    # CPU leg: kore's own quantize + matvec_mt of one layer's four matrices on
+    # one core (the compiled reference), added to its one-core attention time
+    # by the caller
+    cpu_proj_ms = None
+    if not args.no_cpu_baseline:
+        from oracle import oracle as O
+        if O.ref_available():
+            x = np.random.default_rng(79).standard_normal(E).astype(np.float32)
+            cpu_proj_ms = sum(O.ref_qmatvec_ms(m, x, 1, 3)[0] for m in mats0)
     kv_bytes = L * layer_bytes(POS)
     step_bytes = kv_bytes + w_bytes
     peaks = load_peaks()
@@ -423,6 +447,7 @@ def run_block(args, ctx, stream, dev) -> dict:
                      "kernels": "qmatvec_kernel (QKV) + attn_decode_kernel + split_merge_kernel + qmatvec_kernel (Wo)"},
         "gpu_launches": steps * L * 4,
         "clocks": clk,
+        "_cpu_proj_ms": cpu_proj_ms,
     }
 
 
@@ -657,7 +682,7 @@ def cpu_baseline_sample() -> dict:
     t = min(_ref_decode_ms(e, POS) for _ in range(3))
     att = max(t - base, 1e-6)
     return {"value": round(layer_bytes(POS) / (att * 1e-3) / 1e9, 3), "unit": "GB/s", "cores": 1,
-            "kind": "reference",
+            "kind": "reference", "attention_ms": round(att, 3),
             "sample": f"1 of 28 layers, decode at pos {POS}, kore forward() best of 3 = {t:.1f} ms "
                       f"minus forward() at pos 0 = {base:.1f} ms; attention {att:.1f} ms"}
 

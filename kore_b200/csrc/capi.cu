@@ -880,9 +880,12 @@ static int check_qmat(kore_cuda_ctx *c, const kore_cuda_qmat *m, const char *nam
     return KORE_CUDA_OK;
 }
 
+// A layer's uploaded projections, or null. The matrix types are set last by
+// kore_cuda_set_attn_weights, so an upload that failed part-way is not one.
 static const kore_cuda_ctx::LayerProj *layer_proj(kore_cuda_ctx *c, int layer) {
-    if (layer < 0 || layer >= (int)c->proj.size() || !c->proj[(size_t)layer].w) return nullptr;
-    return &c->proj[(size_t)layer];
+    if (layer < 0 || layer >= (int)c->proj.size()) return nullptr;
+    const kore_cuda_ctx::LayerProj &lp = c->proj[(size_t)layer];
+    return lp.w && lp.type[0] && lp.type[3] ? &lp : nullptr;
 }
 
 // One product launch over up to three of a layer's matrices (which: 0 wq,

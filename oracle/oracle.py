@@ -102,6 +102,8 @@ def ref_lib():
         L.kref_q8k_quantize.argtypes = [vp, ctypes.c_int, vp, vp, vp]
         L.kref_qdot.argtypes = [ctypes.c_int, ctypes.c_int, vp, vp, vp, vp, ctypes.c_int]
         L.kref_qdot.restype = ctypes.c_float
+        L.kref_qmatvec_ms.argtypes = [ctypes.c_int] * 3 + [vp] * 3 + [ctypes.c_int] * 2
+        L.kref_qmatvec_ms.restype = ctypes.c_double
         _ref = L
     return _ref
 
@@ -140,6 +142,15 @@ def ref_qdot(qtype: int, wrow: np.ndarray, xq, avx2: bool = True) -> np.float32:
     d, qs, bs = xq
     return np.float32(ref_lib().kref_qdot(qtype, qs.size, wrow.ctypes.data, d.ctypes.data, qs.ctypes.data,
                                           bs.ctypes.data, int(avx2)))
+
+
+def ref_qmatvec_ms(m, x: np.ndarray, threads: int = 1, reps: int = 3):
+    """kore's own quantize + matvec_mt of m with x: (best ms, output)."""
+    x = np.ascontiguousarray(x, np.float32).reshape(-1)
+    out = np.empty(m.rows, np.float32)
+    ms = ref_lib().kref_qmatvec_ms(m.type, m.rows, m.cols, m.data.ctypes.data, x.ctypes.data, out.ctypes.data,
+                                   threads, reps)
+    return ms, out
 
 
 def qmatvec(m, x: np.ndarray, bias=None, avx2: bool = True) -> np.ndarray:

@@ -216,4 +216,28 @@ float kref_qdot(int type, int n, const uint8_t *w, const float *d, const int8_t 
     return v ? dot_q6_K_q8_K_avx2(n, w, y.data()) : dot_q6_K_q8_K_ref(n, w, y.data());
 }
 
+// kore's own mv() + quant() for one quantised matrix (quantize_row_q8_K and
+// matvec_mt with n_threads threads, kore.cpp:422-447, :679-682; its AVX2
+// kernels when the CPU has them): out = W x, best wall time of `reps` runs in ms.
+double kref_qmatvec_ms(int type, int rows, int cols, const uint8_t *data, const float *x, float *out,
+                       int n_threads, int reps) {
+    Tensor t;
+    t.type = (uint32_t)type;
+    t.n_dims = 2;
+    t.dims[0] = (uint64_t)cols;
+    t.dims[1] = (uint64_t)rows;
+    t.nbytes = (uint64_t)rows * (uint64_t)(cols / 256) * (type == GGML_Q4_K ? 144 : 210);
+    t.data = data;
+    std::vector<BlockQ8K> xq((size_t)(cols / 256));
+    const bool avx2 = cpu_has_avx2();
+    double best = 1e30;
+    for (int r = 0; r < reps; r++) {
+        const double t0 = now_ms();
+        quantize_row_q8_K(x, xq.data(), cols);
+        matvec_mt(t, xq.data(), out, avx2, (unsigned)(n_threads > 0 ? n_threads : 1));
+        best = std::min(best, now_ms() - t0);
+    }
+    return best;
+}
+
 }  // extern "C"

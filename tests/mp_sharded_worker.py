@@ -1,7 +1,9 @@
 """Worker of tests/test_multigpu.py (one process per GPU, launched by
 torch.distributed.run): a KV-sharded context per GPU, handles exchanged over
 gloo, decode steps through kore_cuda_attn_decode_sharded_dev compared with
-the oracle on every rank."""
+the oracle on every rank, then the attention block with its projections on
+the same split (kore_cuda_attn_block_decode_dev): identical on every rank,
+its projections bit-exact and its attention within tolerance of the oracle."""
 import datetime
 import os
 import sys
@@ -44,6 +46,36 @@ def main():
             ctx.sync()
             assert_attn_close(out.cpu().numpy().reshape(H, d), oras[layer].decode(pos, q, k, v),
                               f"rank {rank} step {step} layer {layer}")
+    # the attention block on the split: every rank computes the projections
+    from kore_b200.qweights import Q4_K, Q6_K, random_qmat
+    E, kvd = H * d, G * d
+    rng = np.random.default_rng(700)   # the same weights on every rank
+    mats, biases = [], []
+    for layer in range(2):
+        m = [random_qmat(t, r, E, rng) for t, r in ((Q4_K, E), (Q4_K, kvd), (Q6_K, kvd), (Q4_K, E))]
+        b = [rng.standard_normal(n).astype(np.float32) for n in (E, kvd, kvd)]
+        ctx.set_attn_weights(layer, *m, *b)
+        mats.append(m)
+        biases.append(b)
+    o_dev = torch.empty(E, device=dev)
+    for step in range(2):
+        for layer in range(2):
+            pos = cached + 3 + step
+            xb = normal(800 + 10 * step + layer, (E,))[0]
+            txb = torch.from_numpy(xb).to(dev)
+            torch.cuda.synchronize()
+            ctx.attn_block_decode_dev(0, layer, pos, txb, o_dev)
+            ctx.sync()
+            got = o_dev.cpu().numpy()
+            everyone = [None] * world
+            dist.all_gather_object(everyone, got.view(np.uint32).tobytes())
+            assert all(e == everyone[0] for e in everyone), f"step {step} layer {layer}: ranks disagree"
+            m, (bq, bk, bv) = mats[layer], biases[layer]
+            rq, rk, rv = O.qmatvec(m[0], xb, bq), O.qmatvec(m[1], xb, bk), O.qmatvec(m[2], xb, bv)
+            ratt = oras[layer].decode(pos, rq, rk, rv)
+            ref = O.qmatvec(m[3], ratt.reshape(-1))
+            err = float(np.abs(got.astype(np.float64) - ref).max())
+            assert err <= 2e-2 * max(1.0, float(np.abs(ref).max())), (rank, step, layer, err)
     dist.barrier()
     ctx.close()
     dist.destroy_process_group()

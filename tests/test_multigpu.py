@@ -5,7 +5,8 @@
   count.
 * GPU (2 GPUs, skipped with fewer): KV-sharded decode with the exchange over
   NVLink peer memory (kore_cuda_attn_decode_sharded_dev), one process per
-  GPU, checked against the oracle on every rank.
+  GPU, checked against the oracle on every rank, and the attention block with
+  its projections on the same split (kore_cuda_attn_block_decode_dev).
 """
 import datetime
 import os
