@@ -25,14 +25,15 @@
 // computes AVX2 lane k over half h of the row's blocks, and the second
 // half's lane continues the first half's fused multiply-add chains (one
 // shuffle), so the float order stays kore's. The 2 rows are one contiguous
-// byte range: one bulk copy per warp stages them in shared memory, issued before the kernel waits for
-// its predecessor (programmatic dependent launch), since weights do not
-// depend on it. Meanwhile every CTA quantises the fp32 input vector to Q8_K
-// in shared memory itself (14 KB at 7B: cheaper than a kernel boundary),
-// transposed so that each lane reads its 8 words of a block with two 16-byte
-// loads on distinct banks. The per-block loop is compact, which keeps this
-// short-lived kernel out of instruction-cache misses. Memory-bound:
-// algorithmic bytes = the weight bytes (+ the small vector), read once.
+// byte range: one bulk copy per warp stages them in shared memory, issued
+// before the kernel waits for its predecessor (programmatic dependent
+// launch), since weights do not depend on it. Meanwhile every CTA quantises
+// the fp32 input vector to Q8_K in shared memory itself (14 KB at 7B: cheaper
+// than a kernel boundary), transposed so that each lane reads its 8 words of
+// a block with two 16-byte loads on distinct banks. The per-block loop is
+// compact, which keeps this short-lived kernel out of instruction-cache
+// misses. Memory-bound: algorithmic bytes = the weight bytes (+ the small
+// vector), read once.
 
 #include "attn.cuh"
 #include "common.cuh"
