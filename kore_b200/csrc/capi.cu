@@ -48,7 +48,8 @@ struct kore_cuda_ctx {
     int *err_d = nullptr;
     float *dev_stage = nullptr;
     size_t dev_stage_floats = 0;
-    float *host_stage = nullptr;
+    float *host_stage = nullptr;        // pinned, mapped into the device's address space
+    const float *host_stage_dev = nullptr;   // its device address (null: copies go through the copy engine)
     size_t host_stage_floats = 0;
     int *host_err = nullptr;
     int last_kv_layer = -1;     // layer whose KV the most recent kernel of this context wrote
@@ -217,10 +218,51 @@ int grow_stage(kore_cuda_ctx *c, size_t floats) {
     if (floats > c->host_stage_floats) {
         if (c->host_stage) cudaFreeHost(c->host_stage);
         c->host_stage = nullptr;
+        c->host_stage_dev = nullptr;
         c->host_stage_floats = 0;
-        CK(cudaMallocHost(&c->host_stage, floats * sizeof(float)));
+        CK(cudaHostAlloc(reinterpret_cast<void **>(&c->host_stage), floats * sizeof(float), cudaHostAllocMapped));
         c->host_stage_floats = floats;
+        void *d = nullptr;
+        if (cudaHostGetDevicePointer(&d, c->host_stage, 0) == cudaSuccess) c->host_stage_dev = static_cast<const float *>(d);
+        else cudaGetLastError();   // not mapped: stage_in uses the copy engine
     }
+    return KORE_CUDA_OK;
+}
+
+// Copies a small host-path input (q/k/v of a decode step, xb of an attention
+// block) from the mapped pinned staging into device memory. As one kernel
+// launched with a programmatic dependency that lets the next kernel start at
+// once, the decode (or projection) after it fetches its first K/V tiles (or
+// weights) while these reads cross the host link; it reads the inputs only
+// after its dependency wait. The kernel itself waits for its predecessor
+// before writing, so every kernel before it has completed by the time that
+// wait returns, as after a copy-engine copy.
+__global__ void stage_in_kernel(const float4 *__restrict__ src, float4 *__restrict__ dst, int n4) {
+    grid_dep_launch();
+    grid_dep_wait();
+    for (int i = blockIdx.x * blockDim.x + threadIdx.x; i < n4; i += gridDim.x * blockDim.x) dst[i] = src[i];
+}
+
+// The first `floats` of the host staging (16-byte multiple) to the device
+// staging, on the context's stream.
+int stage_in(kore_cuda_ctx *c, size_t floats) {
+    const size_t bytes = floats * sizeof(float);
+    if (!c->host_stage_dev || bytes % 16 || bytes > ((size_t)1 << 20)) {
+        CK(cudaMemcpyAsync(c->dev_stage, c->host_stage, bytes, cudaMemcpyHostToDevice, c->stream));
+        return KORE_CUDA_OK;
+    }
+    const int n4 = (int)(bytes / 16);
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3((unsigned)std::min(64, (n4 + 1023) / 1024));
+    cfg.blockDim = dim3(256);
+    cfg.stream = c->stream;
+    cudaLaunchAttribute attr;
+    attr.id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr.val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = &attr;
+    cfg.numAttrs = 1;
+    CK(cudaLaunchKernelEx(&cfg, stage_in_kernel, reinterpret_cast<const float4 *>(c->host_stage_dev),
+                          reinterpret_cast<float4 *>(c->dev_stage), n4));
     return KORE_CUDA_OK;
 }
 
@@ -829,7 +871,7 @@ static int decode_host(kore_cuda_ctx *c, int n_seq, const float *q, const float 
     memcpy(hs, q, nq * sizeof(float));
     memcpy(hs + nq, k, nk * sizeof(float));
     memcpy(hs + nq + nk, v, nk * sizeof(float));
-    CK(cudaMemcpyAsync(ds, hs, (nq + 2 * nk) * sizeof(float), cudaMemcpyHostToDevice, c->stream));
+    if (int rc = stage_in(c, nq + 2 * nk)) return rc;
     if (!batch) {
         // one sequence: the output lands right behind the error word and both
         // come back in one copy
@@ -1020,7 +1062,7 @@ int kore_cuda_attn_block_decode(kore_cuda_ctx *c, int seq, int layer, int pos, c
     const int E = c->H * c->D;
     if (int rc = grow_stage(c, (size_t)E)) return rc;
     memcpy(c->host_stage, xb, (size_t)E * sizeof(float));
-    CK(cudaMemcpyAsync(c->dev_stage, c->host_stage, (size_t)E * sizeof(float), cudaMemcpyHostToDevice, c->stream));
+    if (int rc = stage_in(c, (size_t)E)) return rc;
     // the output lands right behind the error word and both come back in one copy
     float *dout = reinterpret_cast<float *>(reinterpret_cast<char *>(c->err_d) + kErrPad);
     if (int rc = kore_cuda_attn_block_decode_dev(c, seq, layer, pos, c->dev_stage, dout)) return rc;
