@@ -454,6 +454,33 @@ int keng_generate_cuda(void *h, const int *prompt, int n_prompt, int n_gen, int 
         [&](int tok, int pos) { return cuda_forward(hx, tok, pos, true); });
 }
 
+// kore's own forward() of one token at `pos` (kore.cpp:1397-1480) on the
+// harness's engine, logits copied out (n_vocab floats). Positions must come
+// in order from 0 (forward() appends to the engine's cache).
+int keng_forward(void *h, int token, int pos, float *logits) {
+    Harness &hx = *(Harness *)h;
+    if (!forward(hx.e, token, pos, true)) return -1;
+    memcpy(logits, hx.e.logits.data(), hx.e.logits.size() * sizeof(float));
+    return 0;
+}
+
+// A tensor of the harness's model by GGUF name: its data, type and shape
+// (cols = dims[0], rows = the rest), or nullptr.
+const void *keng_tensor(void *h, const char *name, int *type, int *rows, int *cols) {
+    Harness &hx = *(Harness *)h;
+    const auto it = hx.m.tensors.find(name);
+    if (it == hx.m.tensors.end()) return nullptr;
+    const Tensor &t = it->second;
+    *type = (int)t.type;
+    *cols = (int)t.dims[0];
+    *rows = (int)(t.dims[1] * t.dims[2] * t.dims[3]);
+    return t.data;
+}
+
+const float *keng_inv_freq(void *h) { return ((Harness *)h)->e.inv_freq.data(); }
+int keng_avx2(void *h) { return ((Harness *)h)->e.avx2 ? 1 : 0; }
+float keng_rms_eps(void *h) { return ((Harness *)h)->e.hp.rms_eps; }
+
 // Greedy IDs with the attention block of every decode step on the GPU,
 // projections included (the prompt's chunks as in keng_generate_cuda).
 int keng_generate_cuda_block(void *h, const int *prompt, int n_prompt, int n_gen, int *ids) {

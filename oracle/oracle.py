@@ -43,6 +43,26 @@ def build(ref_dir: str | None = None) -> None:
         subprocess.run(["make", "-s", "-C", HERE, "ref", f"KORE_REF_DIR={ref_dir}"], check=True)
 
 
+class KorcQW(ctypes.Structure):
+    """korc_qw (kore_step_oracle.h)."""
+    _fields_ = [("type", ctypes.c_int), ("rows", ctypes.c_int), ("cols", ctypes.c_int), ("data", ctypes.c_void_p)]
+
+
+class KorcLayer(ctypes.Structure):
+    """korc_layer (kore_step_oracle.h)."""
+    _fields_ = [("attn_norm", ctypes.c_void_p), ("ffn_norm", ctypes.c_void_p), ("bq", ctypes.c_void_p),
+                ("bk", ctypes.c_void_p), ("bv", ctypes.c_void_p)] + \
+               [(n, KorcQW) for n in ("wq", "wk", "wv", "wo", "w_gate", "w_up", "w_down")]
+
+
+class KorcModel(ctypes.Structure):
+    """korc_model (kore_step_oracle.h)."""
+    _fields_ = [("n_layer", ctypes.c_int), ("n_embd", ctypes.c_int), ("n_ff", ctypes.c_int),
+                ("n_head", ctypes.c_int), ("n_head_kv", ctypes.c_int), ("n_vocab", ctypes.c_int),
+                ("rms_eps", ctypes.c_float), ("tok_embd", ctypes.c_void_p), ("out_norm", ctypes.c_void_p),
+                ("out_w", KorcQW), ("layers", ctypes.POINTER(KorcLayer)), ("inv_freq", ctypes.c_void_p)]
+
+
 def _fp(a: np.ndarray):
     assert a.dtype == np.float32 and a.flags.c_contiguous
     return a.ctypes.data_as(_f32p)
@@ -70,6 +90,7 @@ def lib():
             getattr(L, n).argtypes = [ctypes.c_int, vp, vp, vp, vp, ctypes.c_int]
             getattr(L, n).restype = ctypes.c_float
         L.korc_qmatvec.argtypes = [ctypes.c_int] * 3 + [vp] * 4 + [ctypes.c_int]
+        L.korc_decode_step.argtypes = [ctypes.POINTER(KorcModel), vp, vp, ctypes.c_int, ctypes.c_int, vp, ctypes.c_int]
         _oracle = L
     return _oracle
 
@@ -315,6 +336,14 @@ def engine_lib():
         L.keng_attach_cuda.argtypes = [vp, ctypes.c_char_p, ctypes.c_int]
         L.keng_generate_cuda.argtypes = [vp, ip, ctypes.c_int, ctypes.c_int, ip]
         L.keng_generate_cuda_block.argtypes = [vp, ip, ctypes.c_int, ctypes.c_int, ip]
+        L.keng_forward.argtypes = [vp, ctypes.c_int, ctypes.c_int, fp]
+        L.keng_tensor.argtypes = [vp, ctypes.c_char_p, ip, ip, ip]
+        L.keng_tensor.restype = vp
+        L.keng_inv_freq.argtypes = [vp]
+        L.keng_inv_freq.restype = vp
+        L.keng_avx2.argtypes = [vp]
+        L.keng_rms_eps.argtypes = [vp]
+        L.keng_rms_eps.restype = ctypes.c_float
         _engine = L
     return _engine
 
@@ -377,3 +406,61 @@ class GreedyEngine:
                                                  ids.ctypes.data_as(ip)) != n_gen:
             raise RuntimeError(self._err())
         return ids
+
+    # ---- the reference's own decode step and model, for pinning the step restatement
+    def forward_ref(self, token: int, pos: int) -> np.ndarray:
+        """kore's forward() of one token at pos (positions in order from 0): its logits."""
+        out = np.empty(self.n_vocab, np.float32)
+        if engine_lib().keng_forward(self.h, token, pos, _fp(out)):
+            raise RuntimeError("kore forward() refused the token or position")
+        return out
+
+    def tensor(self, name: str):
+        """(type, rows, cols, data address) of one of the model's tensors."""
+        t, r, c = ctypes.c_int(), ctypes.c_int(), ctypes.c_int()
+        p = engine_lib().keng_tensor(self.h, name.encode(), ctypes.byref(t), ctypes.byref(r), ctypes.byref(c))
+        if not p:
+            raise KeyError(name)
+        return t.value, r.value, c.value, p
+
+
+class StepOracle:
+    """The step restatement (korc_decode_step) over a GreedyEngine's own
+    weights, with its own per-layer KV cache."""
+
+    def __init__(self, eng: GreedyEngine, n_layer: int, n_embd: int, n_head: int, n_head_kv: int, n_ff: int,
+                 n_vocab: int, ctx: int):
+        L = engine_lib()
+        kvd = n_head_kv * (n_embd // n_head)
+
+        def qw(name):
+            t, r, c, p = eng.tensor(name)
+            return KorcQW(t, r, c, p)
+
+        def f32(name):
+            return eng.tensor(name)[3]
+
+        self.layers = (KorcLayer * n_layer)()
+        for l in range(n_layer):
+            b = f"blk.{l}."
+            self.layers[l] = KorcLayer(f32(b + "attn_norm.weight"), f32(b + "ffn_norm.weight"),
+                                       f32(b + "attn_q.bias"), f32(b + "attn_k.bias"), f32(b + "attn_v.bias"),
+                                       *[qw(b + n + ".weight") for n in ("attn_q", "attn_k", "attn_v", "attn_output",
+                                                                           "ffn_gate", "ffn_up", "ffn_down")])
+        self.model = KorcModel(n_layer, n_embd, n_ff, n_head, n_head_kv, n_vocab, L.keng_rms_eps(eng.h),
+                               f32("token_embd.weight"), f32("output_norm.weight"), qw("output.weight"),
+                               self.layers, L.keng_inv_freq(eng.h))
+        self.avx2 = L.keng_avx2(eng.h)
+        self.kc = [np.zeros((ctx, kvd), np.float32) for _ in range(n_layer)]
+        self.vc = [np.zeros((ctx, kvd), np.float32) for _ in range(n_layer)]
+        self._kp = (ctypes.c_void_p * n_layer)(*[a.ctypes.data for a in self.kc])
+        self._vp = (ctypes.c_void_p * n_layer)(*[a.ctypes.data for a in self.vc])
+        self.n_vocab = n_vocab
+        self.eng = eng   # keeps the weights alive
+
+    def step(self, token: int, pos: int) -> np.ndarray:
+        out = np.empty(self.n_vocab, np.float32)
+        if lib().korc_decode_step(ctypes.byref(self.model), self._kp, self._vp, token, pos, out.ctypes.data,
+                                  self.avx2):
+            raise RuntimeError("korc_decode_step refused its arguments")
+        return out
