@@ -5,6 +5,8 @@ ABI in ``include/kore_cuda.h``). This module binds it with ctypes and mirrors
 kore's per-layer attention call: ``decode`` replaces kore.cpp:1424-1455 and
 ``prefill`` kore.cpp:1527-1563, with kore's host buffers (numpy arrays here);
 the ``*_dev`` forms take device tensors and stay on the context's stream.
+``set_attn_weights`` + ``attn_block_decode`` run a decode step's whole
+attention block (kore.cpp:1418-1457), its Q4_K / Q6_K projections included.
 
 There is no fallback: if the library is missing, importing this module works
 but creating a context raises, naming the build command.
