@@ -1,27 +1,37 @@
 """bench.py — decode attention throughput of the B200 kore path.
 
-Workload (the metric's "@7B ctx 32k"): Qwen2.5-7B-shaped
-attention, 28 layers, 28 query / 4 KV heads, head_dim 128, one sequence,
-fp32 KV cache of 32768 seeded N(0,1) rows per layer (3.5 GiB, far larger than
-the 126 MB L2, so no L2 flush is needed between steps). One step = one decode
-token through all 28 layers: RoPE of q/k at position 32768, append of k/v,
-attention over positions 0..32768.
+Headline workload (the metric's "@7B ctx 32k"):
+Qwen2.5-7B-shaped attention, 28 layers, 28 query / 4 KV heads, head_dim 128,
+one sequence, fp32 KV cache of 32768 seeded N(0,1) rows per layer (3.5 GiB,
+far larger than the 126 MB L2, so no L2 flush is needed between steps). One
+step = one decode token through all 28 layers: RoPE of q/k at position 32768,
+append of k/v, attention over positions 0..32768.
 
   value  device-resident: q/k/v already in HBM, CUDA events on the context's
          stream around K replays of a CUDA graph holding one step; max over
          ranks; GB/s of algorithmic bytes
          (per layer: 2*(pos+1)*512*4 K/V + 2*28*128*4 q/out + 2*512*4 append).
   e2e    the same steps through the host-buffer C entry point
-         kore_cuda_attn_decode (kore's call: host q/k/v in, host out back),
-         wall clock, copies included.
+         kore_cuda_attn_decode (kore's call: host q/k/v in, host out back;
+         kore_cuda_attn_decode_sharded at N > 1), wall clock, copies included.
+  parity at N = 1 layer 0's output against kore's own forward() (the
+         reference compiled in place) on the same cache and inputs, inside the
+         CPU-baseline leg; at N > 1 against the unsharded decode of the same
+         layer rebuilt on each rank's GPU. A failed check exits non-zero.
 At N > 1 the KV positions are split over the GPUs by page (round robin); each
 layer's partial outputs and log-sum-exps are pushed to every peer over NVLink
 peer memory and merged on every rank (kore_cuda_attn_decode_sharded_dev), one
 exchange per layer. The cache is fixed (strong scaling).
 
+Further lines on the same JSON object (N = 1 unless stated): ``cfg1`` (the
+0.5B layer: prefill 128, then 64 decodes; microseconds per call), ``cfg2``
+(7B, 28 layers, decode at 8192), ``attn_block`` (the attention block with its
+quantised projections), ``prefill`` (config 3, tensor cores) and ``batched``
+(config 5, every N).
+
 ``--impl reference`` times kore's own CPU attention (the reference compiled
-in place, oracle/_ref) on this host: kore.cpp forward() per layer on its
-fp32 cache, layers fanned over the host's cores.
+in place, oracle/_ref) on this host: full 28-layer steps of kore.cpp forward()
+per layer on its fp32 cache, the layers fanned over the host's cores.
 """
 from __future__ import annotations
 
@@ -44,10 +54,11 @@ L = 28          # layers (--layers overrides, for small profiling cases)
 POS = 32768     # decode position (--pos overrides)
 CTX = POS + 1
 KVD = G * D
+ABS_TOL, REL_TOL = 2e-3, 1e-3   # per head: max-abs, and max-abs / max |reference|
 
 
-def layer_bytes(pos: int) -> int:
-    return 2 * (pos + 1) * KVD * 4 + 2 * H * D * 4 + 2 * KVD * 4
+def layer_bytes(pos: int, h: int = H, kvd: int = KVD, d: int = D) -> int:
+    return 2 * (pos + 1) * kvd * 4 + 2 * h * d * 4 + 2 * kvd * 4
 
 
 def parse():
@@ -67,6 +78,7 @@ def parse():
     ap.add_argument("--batched-steps", type=int, default=20)
     ap.add_argument("--no-block", action="store_true", help="skip the attention-block (with projections) line")
     ap.add_argument("--block-steps", type=int, default=100)
+    ap.add_argument("--no-cfg12", action="store_true", help="skip the config-1 and config-2 lines")
     ap.add_argument("--block-only", action="store_true", help="measure only the attention block (development)")
     ap.add_argument("--prefill-only", action="store_true", help="measure only the prefill (development)")
     a = ap.parse_args()
@@ -130,15 +142,52 @@ class ClockSampler:
                 "reasons": sorted(reasons), "samples": len(mhz)}
 
 
-# ---------------------------------------------------------------- our arm
+def head_errors(out, ref):
+    """Worst (max-abs, max-abs / max |ref|) over the heads (rows of D values)."""
+    o = np.asarray(out, np.float64).reshape(-1, D)
+    r = np.asarray(ref, np.float64).reshape(-1, D)
+    err = np.abs(o - r).max(axis=1)
+    mag = np.maximum(np.abs(r).max(axis=1), 1e-30)
+    return float(err.max()), float((err / mag).max())
 
-def run_ours(args, rank: int, world: int, dist) -> dict | None:
+
+def parity_entry(out, ref, against: str) -> dict:
+    a, r = head_errors(out, ref)
+    ok = bool(np.isfinite(np.asarray(out)).all()) and a <= ABS_TOL and r <= REL_TOL
+    return {"max_abs": a, "max_rel": r, "ok": ok, "tol": {"abs": ABS_TOL, "rel": REL_TOL}, "against": against}
+
+
+def cfg4_config(world: int, pos: int = None, layers: int = None) -> dict:
+    pos = POS if pos is None else pos
+    layers = L if layers is None else layers
+    name = "cfg4" if pos == 32768 else ("cfg2" if pos == 8192 else "decode")
+    return {"workload": f"{name}: Qwen2.5-7B-shaped decode at position {pos}, {layers} layers, batch 1",
+            "kv_bytes_per_step": layers * layer_bytes(pos), "l2": f"inputs {layers * layer_bytes(pos) / 2**30:.2f} GiB "
+            "> L2, no flush needed",
+            "kv_split": f"pages round-robin over {world} GPU(s)" if world > 1 else "none"}
+
+
+def layer_rows(torch, dev, layer: int, n: int):
+    """The seeded N(0,1) pre-RoPE k and v rows of one layer, generated on `dev`."""
+    gen = torch.Generator(device=dev)
+    gen.manual_seed(1000 + layer)
+    k = torch.randn(n, KVD, device=dev, generator=gen)
+    v = torch.randn(n, KVD, device=dev, generator=gen)
+    return k, v
+
+
+# ---------------------------------------------------------------- our arm: 7B decode (cfg4, cfg2)
+
+def run_decode(args, rank: int, world: int, dist, pos: int, layers: int, steps: int, e2e_steps: int,
+               want_block: bool) -> dict | None:
+    """Decode at `pos` through `layers` layers of the 7B shape, at N = world
+    GPUs (the KV positions split by page). Returns rank 0's line."""
     import torch
     import kore_b200 as K
 
     dev = torch.device("cuda", int(os.environ.get("LOCAL_RANK", 0)))
     torch.cuda.set_device(dev)
-    ctx = K.KoreCuda(L, H, G, D, CTX, device=dev.index, shard_rank=rank, shard_count=world)
+    ctx = K.KoreCuda(layers, H, G, D, pos + 1, device=dev.index, shard_rank=rank, shard_count=world)
     # the context runs on a torch-owned stream, so tensors used on it (and by
     # NCCL) outlive nothing they depend on when the context is closed
     stream = torch.cuda.Stream(device=dev)
@@ -148,18 +197,16 @@ def run_ours(args, rank: int, world: int, dist) -> dict | None:
     # shard stores the rows of the pages it holds
     gen = torch.Generator(device=dev)
     with torch.cuda.stream(stream):
-        for layer in range(L):
-            gen.manual_seed(1000 + layer)
-            k = torch.randn(POS, KVD, device=dev, generator=gen)
-            v = torch.randn(POS, KVD, device=dev, generator=gen)
-            ctx.append_dev(0, layer, 0, POS, k, v)
+        for layer in range(layers):
+            k, v = layer_rows(torch, dev, layer, pos)
+            ctx.append_dev(0, layer, 0, pos, k, v)
             del k, v
         gen.manual_seed(7)
-        q = torch.randn(L, H * D, device=dev, generator=gen)
-        kn = torch.randn(L, KVD, device=dev, generator=gen)
-        vn = torch.randn(L, KVD, device=dev, generator=gen)
-        out = torch.empty(L, H * D, device=dev)
-        part = torch.empty(L, ctx.part_floats, device=dev)
+        q = torch.randn(layers, H * D, device=dev, generator=gen)
+        kn = torch.randn(layers, KVD, device=dev, generator=gen)
+        vn = torch.randn(layers, KVD, device=dev, generator=gen)
+        out = torch.empty(layers, H * D, device=dev)
+        part = torch.empty(layers, ctx.part_floats, device=dev)
     ctx.sync()
 
     if world > 1:
@@ -167,12 +214,12 @@ def run_ours(args, rank: int, world: int, dist) -> dict | None:
         exchange_handles(ctx, dist)     # exchange buffers mapped over CUDA IPC
 
     def step():
-        for layer in range(L):
+        for layer in range(layers):
             if world == 1:
-                ctx.decode_dev(0, layer, POS, q[layer], kn[layer], vn[layer], out[layer])
+                ctx.decode_dev(0, layer, pos, q[layer], kn[layer], vn[layer], out[layer])
             else:
                 # partial on this rank's pages, pushed to the peers over NVLink, merged on every rank
-                ctx.decode_sharded_dev(0, layer, POS, q[layer], kn[layer], vn[layer], out[layer])
+                ctx.decode_sharded_dev(0, layer, pos, q[layer], kn[layer], vn[layer], out[layer])
 
     def barrier():
         if world > 1:
@@ -180,7 +227,7 @@ def run_ours(args, rank: int, world: int, dist) -> dict | None:
         torch.cuda.synchronize(dev)
 
     with torch.cuda.stream(stream):
-        for _ in range(args.warmup):
+        for _ in range(max(3, args.warmup)):
             step()
     ctx.sync()
     barrier()
@@ -196,7 +243,6 @@ def run_ours(args, rank: int, world: int, dist) -> dict | None:
         for _ in range(3):
             graph.replay()
     ctx.sync()
-    run = graph.replay
 
     clocks = ClockSampler(dev.index)
     clocks.start()
@@ -206,8 +252,8 @@ def run_ours(args, rank: int, world: int, dist) -> dict | None:
     t_begin = time.time()
     with torch.cuda.stream(stream):
         e0.record(stream)
-        for _ in range(args.steps):
-            run()
+        for _ in range(steps):
+            graph.replay()
         e1.record(stream)
     e1.synchronize()
     t_end = time.time()
@@ -219,112 +265,124 @@ def run_ours(args, rank: int, world: int, dist) -> dict | None:
 
     # isolated per-launch durations (events around every layer's call, which
     # also removes the overlap between consecutive layers)
-    n_ev = min(args.steps, 50)
-    evs = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(n_ev * L)]
+    n_ev = min(steps, 50)
+    evs = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(n_ev * layers)]
     with torch.cuda.stream(stream):
         for s in range(n_ev):
-            for layer in range(L):
-                a, b = evs[s * L + layer]
+            for layer in range(layers):
+                a, b = evs[s * layers + layer]
                 a.record(stream)
                 if world == 1:
-                    ctx.decode_dev(0, layer, POS, q[layer], kn[layer], vn[layer], out[layer])
+                    ctx.decode_dev(0, layer, pos, q[layer], kn[layer], vn[layer], out[layer])
                 else:
-                    ctx.decode_partial_dev(0, layer, POS, q[layer], kn[layer], vn[layer], part[layer])
+                    ctx.decode_partial_dev(0, layer, pos, q[layer], kn[layer], vn[layer], part[layer])
                 b.record(stream)
     torch.cuda.synchronize(dev)
     iso_ms = sum(a.elapsed_time(b) for a, b in evs) / len(evs)
 
-    # end to end through the host-buffer entry point (kore's own call shape)
-    e2e_ms = None
-    if world == 1:
-        hq, hk, hv = q.cpu().numpy(), kn.cpu().numpy(), vn.cpu().numpy()
-        ho = np.empty((L, H * D), np.float32)
-        for layer in range(L):
-            ho[layer] = ctx.decode(0, layer, POS, hq[layer], hk[layer], hv[layer]).reshape(-1)
-        t0 = time.perf_counter()
-        for _ in range(args.e2e_steps):
-            for layer in range(L):
-                ho[layer] = ctx.decode(0, layer, POS, hq[layer], hk[layer], hv[layer]).reshape(-1)
-        e2e_ms = (time.perf_counter() - t0) * 1e3 / args.e2e_steps
-    else:
-        # host buffers per layer: pinned copies in, merged output back
-        hq = q.cpu().pin_memory()
-        hk, hv = kn.cpu().pin_memory(), vn.cpu().pin_memory()
-        ho = torch.empty(L, H * D).pin_memory()
-        barrier()
-        t0 = time.perf_counter()
-        with torch.cuda.stream(stream):
-            for _ in range(args.e2e_steps):
-                for layer in range(L):
-                    q[layer].copy_(hq[layer], non_blocking=True)
-                    kn[layer].copy_(hk[layer], non_blocking=True)
-                    vn[layer].copy_(hv[layer], non_blocking=True)
-                    ctx.decode_sharded_dev(0, layer, POS, q[layer], kn[layer], vn[layer], out[layer])
-                    ho[layer].copy_(out[layer], non_blocking=True)
-                    stream.synchronize()
-        e2e_ms = (time.perf_counter() - t0) * 1e3 / args.e2e_steps
+    # end to end through the host-buffer entry point (kore's own call shape):
+    # q/k/v in from host memory, the merged output back, one call per layer
+    hq, hk, hv = q.cpu().numpy(), kn.cpu().numpy(), vn.cpu().numpy()
+    ho = np.empty((layers, H * D), np.float32)
+    call = ctx.decode if world == 1 else ctx.decode_sharded
+    for layer in range(layers):
+        ho[layer] = call(0, layer, pos, hq[layer], hk[layer], hv[layer]).reshape(-1)
+    barrier()
+    t0 = time.perf_counter()
+    for _ in range(e2e_steps):
+        for layer in range(layers):
+            ho[layer] = call(0, layer, pos, hq[layer], hk[layer], hv[layer]).reshape(-1)
+    e2e_ms = (time.perf_counter() - t0) * 1e3 / e2e_steps
+    barrier()
 
-    t = torch.tensor([ms, iso_ms, e2e_ms], device=dev, dtype=torch.float64)
+    # parity at N > 1: layer 0 rebuilt unsharded on this GPU from the same
+    # seeds, decoded with the same q/k/v, against the merged sharded output
+    parity = None
+    if world > 1:
+        full = K.KoreCuda(1, H, G, D, pos + 1, device=dev.index)
+        k0, v0 = layer_rows(torch, dev, 0, pos)
+        full.append_dev(0, 0, 0, pos, k0, v0)
+        del k0, v0
+        ref = torch.empty(H * D, device=dev)
+        full.decode_dev(0, 0, pos, q[0], kn[0], vn[0], ref)
+        full.sync()
+        full.close()
+        parity = parity_entry(ho[0], ref.cpu().numpy(), "the unsharded decode of layer 0 on the same GPU "
+                              "(same seeded cache and q/k/v), on every rank")
+
+    t = torch.tensor([ms, iso_ms, e2e_ms, 0.0 if parity is None or parity["ok"] else 1.0,
+                      0.0 if parity is None else parity["max_abs"], 0.0 if parity is None else parity["max_rel"]],
+                     device=dev, dtype=torch.float64)
     if world > 1:
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
-    ms, iso_ms, e2e_ms = t.tolist()
+    ms, iso_ms, e2e_ms, bad, pa, pr = t.tolist()
+    if parity is not None:
+        parity.update(max_abs=pa, max_rel=pr, ok=bad == 0.0, ranks=world)
+
     block = None
-    if world == 1 and not args.no_block:
+    if want_block and world == 1 and not args.no_block:
         block = run_block(args, ctx, stream, dev)
+    layer0 = ho[0].copy()
     ctx.close()
     if rank != 0:
         return None
 
-    step_bytes = L * layer_bytes(POS)
-    ms_step = ms / args.steps
+    step_bytes = layers * layer_bytes(pos)
+    ms_step = ms / steps
     gbs = step_bytes / (ms_step * 1e-3) / 1e9
     e2e_gbs = step_bytes / (e2e_ms * 1e-3) / 1e9
     peaks = load_peaks()
-    launch_bytes = layer_bytes(POS) / world
-    layer_ms = ms_step / L          # one layer's decode (+ split merge) inside the timed region
+    launch_bytes = layer_bytes(pos) / world
+    layer_ms = ms_step / layers          # one layer's decode (+ split merge or exchange) inside the timed region
     achieved = launch_bytes / (layer_ms * 1e-3) / 1e9
     line = {
-        "metric": "decode attn HBM GB/s @7B ctx 32k (28 layers, 28Q/4KV, d128, fp32 KV)",
-        "value": round(gbs, 1), "unit": "GB/s", "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
+        "metric": f"decode attn HBM GB/s @7B ctx {pos // 1024}k ({layers} layers, 28Q/4KV, d128, fp32 KV)",
+        "value": round(gbs, 1), "unit": "GB/s", "n_gpus": world, "steps": steps, "warmup": max(3, args.warmup),
         "ms_per_step": round(ms_step, 5), "higher_is_better": True,
         "scaling": "strong" if world > 1 else "weak",
         "vs_baseline": None, "dtype": "f32", "data": "synthetic (seeded N(0,1) q/k/v and KV cache)",
-        "config": {"workload": f"cfg4: Qwen2.5-7B-shaped decode at position {POS}, {L} layers, batch 1",
-                   "kv_bytes_per_step": step_bytes, "l2": "inputs 3.5 GiB > L2, no flush needed",
-                   "kv_split": f"pages round-robin over {world} GPU(s)" if world > 1 else "none"},
+        "config": cfg4_config(world, pos, layers),
         "e2e": {"value": round(e2e_gbs, 1), "unit": "GB/s", "ms_per_step": round(e2e_ms, 4),
-                "h2d_bytes_per_step": L * (H * D + 2 * KVD) * 4, "d2h_bytes_per_step": L * H * D * 4},
-        "roofline": {"bound": "hbm", "kernel": "attn_decode_kernel<128,7,8,8,3> + split_merge_kernel<128,7>" + (" + peer_exchange_kernel" if world > 1 else ""),
+                "h2d_bytes_per_step": layers * (H * D + 2 * KVD) * 4, "d2h_bytes_per_step": layers * H * D * 4,
+                "call": "kore_cuda_attn_decode" if world == 1 else "kore_cuda_attn_decode_sharded"},
+        "roofline": {"bound": "hbm",
+                     "kernel": "attn_decode_kernel<128,7,8,8,3> + " + ("split_merge_kernel<128,7>" if world == 1
+                                                                       else "peer_exchange_kernel<128>"),
                      "achieved": round(achieved, 1), "peak": peaks["hbm_gbs"], "peak_source": peaks["source"],
-                     "unit": "GB/s", "frac": round(achieved / peaks["hbm_gbs"], 4), "traffic": load_traffic(),
+                     "unit": "GB/s", "frac": round(achieved / peaks["hbm_gbs"], 4),
+                     "traffic": load_traffic() if pos == 32768 and world == 1 else None,
                      "launch_ms": round(layer_ms, 5), "launch_ms_isolated": round(iso_ms, 5),
                      "algorithmic_bytes_per_launch": int(launch_bytes),
                      "timing": "launch_ms = timed region / (steps x layers), CUDA events on the context stream; "
                                "launch_ms_isolated = events around each layer's call (no inter-layer overlap)"},
-        "gpu_launches": args.steps * L * (3 if world > 1 else 2),
+        "gpu_launches": steps * layers * 2,
         "clocks": clk,
     }
-    if not args.no_cpu_baseline and world == 1:
-        line["cpu_baseline"] = cpu_baseline_sample()
+    if world == 1:
+        if not args.no_cpu_baseline:
+            cb, par = cpu_baseline_sample(pos, layer0, hq[0], hk[0], hv[0])
+            line["cpu_baseline"] = cb
+            if par is not None:
+                parity = par
+    if parity is not None:
+        line["parity"] = parity
     if block is not None:
         proj_ms = block.pop("_cpu_proj_ms", None)
         att = line.get("cpu_baseline", {}).get("attention_ms")
         if proj_ms is not None and att is not None:
-            per_layer = block["weight_bytes_per_step"] / L + layer_bytes(POS)
+            per_layer = block["weight_bytes_per_step"] / layers + layer_bytes(pos)
             block["cpu_baseline"] = {
                 "value": round(per_layer / ((att + proj_ms) * 1e-3) / 1e9, 3), "unit": "GB/s", "cores": 1,
                 "kind": "reference",
-                "sample": f"1 of 28 layers: kore's attention at pos {POS} ({att:.1f} ms, as cpu_baseline) + "
+                "sample": f"1 of 28 layers: kore's attention at pos {pos} ({att:.1f} ms, as cpu_baseline) + "
                           f"kore's quantize_row_q8_K + matvec_mt of Wq, Wk, Wv, Wo on 1 thread "
                           f"(best of 3, {proj_ms:.2f} ms)"}
         line["attn_block"] = block
-    if not args.no_prefill and world == 1:
-        line["prefill"] = run_prefill(args, torch.device("cuda", 0), peaks)
     return line
 
 
 def run_block_only(args) -> dict:
-    """The attention-block line alone, on a context set up as run_ours sets it up."""
+    """The attention-block line alone, on a context set up as run_decode sets it up."""
     import torch
     import kore_b200 as K
 
@@ -333,12 +391,9 @@ def run_block_only(args) -> dict:
     ctx = K.KoreCuda(L, H, G, D, CTX, device=0)
     stream = torch.cuda.Stream(device=dev)
     ctx.set_stream(stream.cuda_stream)
-    gen = torch.Generator(device=dev)
     with torch.cuda.stream(stream):
         for layer in range(L):
-            gen.manual_seed(1000 + layer)
-            k = torch.randn(POS, KVD, device=dev, generator=gen)
-            v = torch.randn(POS, KVD, device=dev, generator=gen)
+            k, v = layer_rows(torch, dev, layer, POS)
             ctx.append_dev(0, layer, 0, POS, k, v)
             del k, v
     ctx.sync()
@@ -358,7 +413,6 @@ def run_block(args, ctx, stream, dev) -> dict:
     for Wv), one set per layer, so each step streams every layer's weights
     and KV from HBM."""
     import torch
-    import kore_b200 as K
     from kore_b200.qweights import Q4_K, Q6_K, random_qmat
 
     E = H * D
@@ -382,8 +436,9 @@ def run_block(args, ctx, stream, dev) -> dict:
         for layer in range(L):
             ctx.attn_block_decode_dev(0, layer, POS, xb[layer], o[layer])
 
+    warm = max(3, args.warmup)
     with torch.cuda.stream(stream):
-        for _ in range(max(3, args.warmup)):
+        for _ in range(warm):
             step()
     ctx.sync()
     graph = torch.cuda.CUDAGraph()
@@ -438,8 +493,8 @@ def run_block(args, ctx, stream, dev) -> dict:
     return {
         "metric": "attention block (Q8_K + Wq/Wk/Wv + attention + Wo) GB/s of KV + weights @7B ctx 32k",
         "value": round(step_bytes / (ms * 1e-3) / 1e9, 1), "unit": "GB/s", "ms_per_step": round(ms, 5),
-        "steps": steps, "layers": L, "weight_bytes_per_step": int(w_bytes), "kv_bytes_per_step": int(kv_bytes),
-        "weights": "Q4_K wq/wk/wo, Q6_K wv (seeded synthetic GGUF blocks)",
+        "steps": steps, "warmup": warm, "layers": L, "weight_bytes_per_step": int(w_bytes),
+        "kv_bytes_per_step": int(kv_bytes), "weights": "Q4_K wq/wk/wo, Q6_K wv (seeded synthetic GGUF blocks)",
         "e2e": {"value": round(step_bytes / (e2e_ms * 1e-3) / 1e9, 1), "unit": "GB/s", "ms_per_step": round(e2e_ms, 4),
                 "h2d_bytes_per_step": L * E * 4, "d2h_bytes_per_step": L * E * 4},
         "roofline": {"bound": "hbm", "achieved": round(achieved, 1), "peak": peaks["hbm_gbs"],
@@ -451,7 +506,152 @@ def run_block(args, ctx, stream, dev) -> dict:
     }
 
 
-# config 5: Qwen2.5-3B-shaped batched decode of many independent sequences
+# ---------------------------------------------------------------- config 1: the 0.5B layer
+
+C1_H, C1_G, C1_D, C1_PRE, C1_DEC = 14, 2, 64, 128, 64
+
+
+def run_cfg1(args) -> dict:
+    """Config 1: one Qwen2.5-0.5B-shaped attention layer (14Q/2KV, d 64):
+    prefill 128 tokens at positions 0..127, then 64 decode steps at 128..191,
+    fresh seeded N(0,1) q/k/v per call. One step = that whole workload (65
+    calls), re-run at the same positions (the prefill from position 0
+    overwrites the cache, as kore's re-prefill does). Latency-bound: the
+    line reports microseconds per call. `value`: device-resident inputs, one
+    CUDA graph replay per step, CUDA events; `e2e`: kore's host-buffer calls
+    (kore_cuda_attn_prefill / kore_cuda_attn_decode), each returning once its
+    output is on the host, wall clock."""
+    import torch
+    import kore_b200 as K
+
+    dev = torch.device("cuda", 0)
+    hd, kvd = C1_H * C1_D, C1_G * C1_D
+    n_calls = 1 + C1_DEC
+    ctx = K.KoreCuda(1, C1_H, C1_G, C1_D, C1_PRE + C1_DEC, device=0)
+    stream = torch.cuda.Stream(device=dev)
+    ctx.set_stream(stream.cuda_stream)
+    rng = np.random.default_rng(12345)
+    hq = rng.standard_normal((C1_PRE + C1_DEC, hd), dtype=np.float32)
+    hk = rng.standard_normal((C1_PRE + C1_DEC, kvd), dtype=np.float32)
+    hv = rng.standard_normal((C1_PRE + C1_DEC, kvd), dtype=np.float32)
+    with torch.cuda.stream(stream):
+        q, k, v = (torch.from_numpy(a).to(dev) for a in (hq, hk, hv))
+        out = torch.empty(C1_PRE + C1_DEC, hd, device=dev)
+
+    def step():
+        ctx.prefill_dev(0, 0, 0, C1_PRE, q[:C1_PRE], k[:C1_PRE], v[:C1_PRE], out[:C1_PRE])
+        for i in range(C1_DEC):
+            p = C1_PRE + i
+            ctx.decode_dev(0, 0, p, q[p], k[p], v[p], out[p])
+
+    warm = max(3, args.warmup)
+    with torch.cuda.stream(stream):
+        for _ in range(warm):
+            step()
+    ctx.sync()
+    graph = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(graph, stream=stream):
+        step()
+    with torch.cuda.stream(stream):
+        graph.replay()
+    ctx.sync()
+    steps = max(20, args.steps // 10)
+    clocks = ClockSampler(0)
+    clocks.start()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    torch.cuda.synchronize(dev)
+    t_begin = time.time()
+    with torch.cuda.stream(stream):
+        e0.record(stream)
+        for _ in range(steps):
+            graph.replay()
+        e1.record(stream)
+    e1.synchronize()
+    t_end = time.time()
+    clk = clocks.stop(t_begin, t_end)
+    ms = e0.elapsed_time(e1) / steps
+    del graph
+    # the pieces, device side: the prefill call alone and one decode call
+    ev = [torch.cuda.Event(enable_timing=True) for _ in range(n_calls + 1)]
+    with torch.cuda.stream(stream):
+        ev[0].record(stream)
+        ctx.prefill_dev(0, 0, 0, C1_PRE, q[:C1_PRE], k[:C1_PRE], v[:C1_PRE], out[:C1_PRE])
+        ev[1].record(stream)
+        for i in range(C1_DEC):
+            p = C1_PRE + i
+            ctx.decode_dev(0, 0, p, q[p], k[p], v[p], out[p])
+            ev[2 + i].record(stream)
+    torch.cuda.synchronize(dev)
+    pre_us = ev[0].elapsed_time(ev[1]) * 1e3
+    dec_us = ev[1].elapsed_time(ev[-1]) * 1e3 / C1_DEC
+    # end to end: kore's host-buffer calls
+    def e2e_once():
+        ctx.prefill(0, 0, 0, hq[:C1_PRE], hk[:C1_PRE], hv[:C1_PRE])
+        for i in range(C1_DEC):
+            p = C1_PRE + i
+            ctx.decode(0, 0, p, hq[p], hk[p], hv[p])
+    for _ in range(3):
+        e2e_once()
+    n_e2e = 20
+    t0 = time.perf_counter()
+    for _ in range(n_e2e):
+        e2e_once()
+    e2e_ms = (time.perf_counter() - t0) * 1e3 / n_e2e
+    ctx.close()
+    line = {
+        "metric": "cfg1 attention latency, microseconds per call (0.5B layer: prefill 128, then 64 decodes)",
+        "value": round(ms * 1e3 / n_calls, 2), "unit": "us/call", "higher_is_better": False,
+        "steps": steps, "warmup": warm, "ms_per_step": round(ms, 5), "dtype": "f32",
+        "data": "synthetic (seeded N(0,1) q/k/v, numpy seed 12345)",
+        "config": {"workload": "cfg1: Qwen2.5-0.5B-shaped attention layer, 14Q/2KV, d64, prefill 128 tokens at "
+                               "0..127 then 64 decode steps at 128..191, RoPE theta 1e6", "calls_per_step": n_calls},
+        "device_us": {"prefill_128": round(pre_us, 2), "decode_mean": round(dec_us, 2),
+                      "timing": "device: CUDA graph of one step (65 calls), events around K replays; the pieces "
+                                "from events around each call of one ungraphed step"},
+        "e2e": {"value": round(e2e_ms * 1e3 / n_calls, 2), "unit": "us/call", "ms_per_step": round(e2e_ms, 4),
+                "h2d_bytes_per_step": (C1_PRE + C1_DEC) * (hd + 2 * kvd) * 4,
+                "d2h_bytes_per_step": (C1_PRE + C1_DEC) * hd * 4},
+        "roofline": {"bound": "latency", "note": "29.6 MFLOP of prefill and <= 0.2 MB per decode: launch and "
+                                                 "dependency latency bound, far from HBM or tensor limits"},
+        "gpu_launches": steps * (3 + C1_DEC * 1),
+        "clocks": clk,
+    }
+    if not args.no_cpu_baseline:
+        line["cpu_baseline"] = cfg1_cpu_baseline(hq, hk, hv)
+    return line
+
+
+def cfg1_cpu_baseline(hq, hk, hv) -> dict:
+    """kore's own attention (forward_batch() per prompt token, then forward()
+    per decode token; the reference compiled in place) on one core for the
+    same 65 calls, minus the non-attention part of forward() (its time at
+    position 0), microseconds per call."""
+    from oracle import oracle as O
+    if not O.ref_available():
+        return {"value": None, "unavailable": "oracle/_ref not built"}
+    e = O.RefLayer(C1_H, C1_G, C1_D, C1_PRE + C1_DEC)
+    best = None
+    for _ in range(3):
+        t0 = time.perf_counter()
+        e.prefill(0, hq[:C1_PRE], hk[:C1_PRE], hv[:C1_PRE])
+        for i in range(C1_DEC):
+            p = C1_PRE + i
+            e.decode(p, hq[p], hk[p], hv[p])
+        t = (time.perf_counter() - t0) * 1e3
+        best = t if best is None else min(best, t)
+    t0 = time.perf_counter()
+    for _ in range(20):
+        e.decode(0, hq[0], hk[0], hv[0])
+    base = (time.perf_counter() - t0) * 1e3 / 20
+    att = max(best - (C1_PRE + C1_DEC) * base, 1e-6)
+    return {"value": round(att * 1e3 / (1 + C1_DEC), 2), "unit": "us/call", "cores": 1, "kind": "reference",
+            "sample": f"the whole workload, best of 3: {best:.2f} ms minus {C1_PRE + C1_DEC} x forward() at pos 0 "
+                      f"({base:.3f} ms); kore's prefill token by token (forward_batch nb = 1, the same attention "
+                      f"arithmetic per token)"}
+
+
+# ---------------------------------------------------------------- config 5: batched decode
+
 B_SEQS, B_LAYERS, B_H, B_G = 64, 36, 16, 2
 B_KVD = B_G * D
 
@@ -514,8 +714,9 @@ def run_batched(args, rank: int, world: int, dist, peaks) -> dict | None:
             dist.barrier()
         torch.cuda.synchronize(dev)
 
+    warm = max(3, args.warmup)
     with torch.cuda.stream(stream):
-        for _ in range(3):
+        for _ in range(warm):
             step()
     ctx.sync()
     graph = torch.cuda.CUDAGraph()
@@ -526,13 +727,18 @@ def run_batched(args, rank: int, world: int, dist, peaks) -> dict | None:
     ctx.sync()
     steps = args.batched_steps
     e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    clocks = ClockSampler(dev.index)
+    clocks.start()
     barrier()
+    t_begin = time.time()
     with torch.cuda.stream(stream):
         e0.record(stream)
         for _ in range(steps):
             graph.replay()
         e1.record(stream)
     e1.synchronize()
+    t_end = time.time()
+    clk = clocks.stop(t_begin, t_end)
     ms = e0.elapsed_time(e1) / steps
     barrier()
     t = torch.tensor([ms], device=dev, dtype=torch.float64)
@@ -547,7 +753,7 @@ def run_batched(args, rank: int, world: int, dist, peaks) -> dict | None:
     gbs = total / (ms * 1e-3) / 1e9
     return {
         "metric": "batched decode attn HBM GB/s (cfg5: 3B shape, 64 sequences, 36 layers)",
-        "value": round(gbs, 1), "unit": "GB/s", "n_gpus": world, "steps": steps, "warmup": 3,
+        "value": round(gbs, 1), "unit": "GB/s", "n_gpus": world, "steps": steps, "warmup": warm,
         "ms_per_step": round(ms, 4), "higher_is_better": True, "scaling": "strong" if world > 1 else "weak",
         "config": {"workload": "cfg5: 64 sequences, cached lengths ~U{1024..32768} (seed 5), 16Q/2KV heads, "
                                "d128, 36 layers, 256-token pages, one token per sequence per step",
@@ -559,6 +765,7 @@ def run_batched(args, rank: int, world: int, dist, peaks) -> dict | None:
                      "frac": round(gbs / (peaks["hbm_gbs"] * world), 4),
                      "note": "peak = measured HBM GB/s x GPUs"},
         "gpu_launches": steps * B_LAYERS * 2,
+        "clocks": clk,
     }
 
 
@@ -595,18 +802,24 @@ def run_prefill(args, dev, peaks) -> dict:
         for layer in range(LP):
             ctx.prefill_dev(0, layer, P0, N, q[layer], kc[layer], vc[layer], out[layer])
 
+    warm = 3
     with torch.cuda.stream(stream):
-        for _ in range(2):
+        for _ in range(warm):
             step()
     ctx.sync()
     steps = args.prefill_steps
     e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    clocks = ClockSampler(dev.index)
+    clocks.start()
+    t_begin = time.time()
     with torch.cuda.stream(stream):
         e0.record(stream)
         for _ in range(steps):
             step()
         e1.record(stream)
     e1.synchronize()
+    t_end = time.time()
+    clk = clocks.stop(t_begin, t_end)
     ctx.sync()
     ms = e0.elapsed_time(e1) / steps
     flops = 4 * D * prefill_pairs(P0, N) * H * LP
@@ -616,12 +829,15 @@ def run_prefill(args, dev, peaks) -> dict:
     peak_eq = peaks["bf16_tflops"] / 3
     return {"metric": "prefill attn TFLOP/s (7B, 2048-token chunk onto 4096, 28 layers)",
             "value": round(tflops, 1), "unit": "TFLOP/s", "ms_per_step": round(ms, 4), "steps": steps,
-            "layers": LP, "flop_per_step": flops,
+            "warmup": warm, "layers": LP, "flop_per_step": flops,
             "roofline": {"bound": "tensor", "achieved": round(tflops, 1), "peak": round(peak_eq, 1),
                          "unit": "TFLOP/s", "frac": round(tflops / peak_eq, 4), "peak_source": peaks["source"],
                          "peak_note": "measured bf16 dense peak / 3: each fp32-accurate product is three bf16 "
-                                      "MMAs (hi*hi + hi*mid + mid*hi)"},
-            "kernels": "kv_append_kernel + kv_split_kernel + prefill_kernel (tcgen05, TMEM)"}
+                                      "MMAs (hi*hi + hi*mid + mid*hi)",
+                         "frac_of_bf16_peak": round(tflops / peaks["bf16_tflops"], 4),
+                         "bf16_peak": peaks["bf16_tflops"]},
+            "kernels": "kv_append_kernel + kv_split_kernel + prefill_kernel (tcgen05, TMEM)",
+            "clocks": clk}
 
 
 def load_peaks() -> dict:
@@ -644,50 +860,60 @@ def load_traffic():
         return None
 
 
-# ---------------------------------------------------------------- reference arm (CPU)
+# ---------------------------------------------------------------- CPU legs (the reference compiled in place)
 
-def _ref_layer_engines(n: int, threads: int = 1):
+def _ref_engine_with_rows(k_rows: np.ndarray, v_rows: np.ndarray, pos: int, threads: int = 1):
     from oracle import oracle as O
-    engines = []
-    for i in range(n):
-        e = O.RefLayer(H, G, D, CTX, threads=threads)
-        g = np.random.default_rng(100 + i)
-        for p0 in range(0, POS, 4096):
-            k = g.standard_normal((4096, KVD), dtype=np.float32)
-            v = g.standard_normal((4096, KVD), dtype=np.float32)
-            e.fill(p0, k, v)
-        engines.append(e)
-    return engines
+    e = O.RefLayer(H, G, D, pos + 1, threads=threads)
+    for p0 in range(0, pos, 4096):
+        e.fill(p0, k_rows[p0:p0 + 4096], v_rows[p0:p0 + 4096])
+    return e
 
 
-def _ref_decode_ms(e, pos: int, reps: int = 1) -> float:
-    from oracle import oracle as O
-    q, k, v = O.seeded_inputs(5, (H * D,), (KVD,), (KVD,))
+def _ref_decode_ms(e, pos: int, q, k, v, reps: int = 1) -> float:
     t0 = time.perf_counter()
     for _ in range(reps):
         e.decode(pos, q, k, v)
     return (time.perf_counter() - t0) * 1e3 / reps
 
 
-def cpu_baseline_sample() -> dict:
+def cpu_baseline_sample(pos: int, gpu_layer0, q0, k0, v0):
     """kore's own decode attention (forward() of the compiled reference) on 1
-    core, one layer at position 32768, minus the same forward() at position 0
-    (embedding, norms and zero-weight projections, i.e. everything that is
-    not attention)."""
+    core, one layer at `pos` over the same cache rows and q/k/v as the GPU's
+    layer 0, minus the same forward() at position 0 (embedding, norms and
+    zero-weight projections, i.e. everything that is not attention). Its
+    output is also the N = 1 parity check of the GPU's layer 0. Returns
+    (cpu_baseline, parity or None)."""
     from oracle import oracle as O
     if not O.ref_available():
-        return {"value": None, "unavailable": "oracle/_ref not built"}
-    e = _ref_layer_engines(1)[0]
-    base = _ref_decode_ms(e, 0, reps=3)
-    t = min(_ref_decode_ms(e, POS) for _ in range(3))
+        return {"value": None, "unavailable": "oracle/_ref not built"}, None
+    import torch
+    dev = torch.device("cuda", 0)
+    kr, vr = layer_rows(torch, dev, 0, pos)
+    e = _ref_engine_with_rows(kr.cpu().numpy(), vr.cpu().numpy(), pos)
+    del kr, vr
+    base = _ref_decode_ms(e, 0, q0, k0, v0, reps=3)
+    ts = []
+    for _ in range(3):
+        ts.append(_ref_decode_ms(e, pos, q0, k0, v0))
+    t = min(ts)
+    ref = e.decode(pos, q0, k0, v0)
     att = max(t - base, 1e-6)
-    return {"value": round(layer_bytes(POS) / (att * 1e-3) / 1e9, 3), "unit": "GB/s", "cores": 1,
-            "kind": "reference", "attention_ms": round(att, 3),
-            "sample": f"1 of 28 layers, decode at pos {POS}, kore forward() best of 3 = {t:.1f} ms "
-                      f"minus forward() at pos 0 = {base:.1f} ms; attention {att:.1f} ms"}
+    cb = {"value": round(layer_bytes(pos) / (att * 1e-3) / 1e9, 3), "unit": "GB/s", "cores": 1,
+          "kind": "reference", "attention_ms": round(att, 3),
+          "sample": f"1 of 28 layers, decode at pos {pos}, kore forward() best of 3 = {t:.1f} ms "
+                    f"minus forward() at pos 0 = {base:.1f} ms; attention {att:.1f} ms"}
+    par = parity_entry(gpu_layer0, ref.reshape(-1), "kore's own forward() (oracle/_ref) on the same cache rows "
+                       "and q/k/v as the GPU's layer 0")
+    return cb, par
 
 
 def run_reference(args, rank: int, world: int) -> dict | None:
+    """The reference arm: kore's own CPU attention for the headline workload.
+    Each step is a full 28-layer decode at POS: 28 kore forward() calls, one
+    per layer, fanned over the host's cores (kore's attention is
+    single-threaded, so one forward() per core is all the parallelism its code
+    has), minus the non-attention part of each forward()."""
     if rank != 0:
         return None
     from oracle import oracle as O
@@ -695,14 +921,24 @@ def run_reference(args, rank: int, world: int) -> dict | None:
         return {"impl": "reference", "unavailable": "oracle/_ref/libkore_ref.so not built (needs the reference sources)"}
     cores = len(os.sched_getaffinity(0))
     T = max(1, min(cores, L))
-    engines = _ref_layer_engines(T)
-    base = _ref_decode_ms(engines[0], 0, reps=3)
-    from oracle import oracle as O2
-    q, k, v = O2.seeded_inputs(5, (H * D,), (KVD,), (KVD,))
+    engines = []
+    for i in range(T):
+        g = np.random.default_rng(100 + i)
+        rows_k = g.standard_normal((POS, KVD), dtype=np.float32)
+        rows_v = g.standard_normal((POS, KVD), dtype=np.float32)
+        engines.append(_ref_engine_with_rows(rows_k, rows_v, POS))
+        del rows_k, rows_v
+    q, k, v = O.seeded_inputs(5, (H * D,), (KVD,), (KVD,))
+    base = _ref_decode_ms(engines[0], 0, q, k, v, reps=3)
+    one_core_att = max(min(_ref_decode_ms(engines[0], POS, q, k, v) for _ in range(2)) - base, 1e-6)
+    per_thread = (L + T - 1) // T
+
+    def worker(t):
+        for layer in range(t, L, T):
+            engines[t].decode(POS, q, k, v)
 
     def one_step():
-        # T layers at once, one per core: kore's attention is single-threaded
-        ths = [threading.Thread(target=e.decode, args=(POS, q, k, v)) for e in engines]
+        ths = [threading.Thread(target=worker, args=(t,)) for t in range(T)]
         t0 = time.perf_counter()
         for th in ths:
             th.start()
@@ -710,27 +946,36 @@ def run_reference(args, rank: int, world: int) -> dict | None:
             th.join()
         return (time.perf_counter() - t0) * 1e3
 
-    budget_s = 150.0
+    budget_s = 240.0
     first = one_step()
-    n_total = args.warmup + args.steps
-    steps = max(1, min(args.steps, int(budget_s * 1e3 / max(first, 1.0)) - min(args.warmup, 2)))
-    warm = min(args.warmup, 2)
+    steps = max(1, min(args.steps, int(budget_s * 1e3 / max(first, 1.0)) - args.warmup))
+    warm = args.warmup
     for _ in range(max(0, warm - 1)):
         one_step()
     times = [one_step() for _ in range(steps)]
     ms = sum(times) / len(times)
-    att_ms = max(ms - base, 1e-6)   # non-attention part of forward() runs in parallel too
-    v_gbs = T * layer_bytes(POS) / (att_ms * 1e-3) / 1e9
+    att_ms = max(ms - per_thread * base, 1e-6)   # each thread ran per_thread non-attention parts too
+    step_bytes = L * layer_bytes(POS)
+    v_gbs = step_bytes / (att_ms * 1e-3) / 1e9
+    one_gbs = layer_bytes(POS) / (one_core_att * 1e-3) / 1e9
     return {
-        "impl": "reference", "metric": "decode attn HBM GB/s @7B ctx 32k (28 layers, 28Q/4KV, d128, fp32 KV)",
+        "impl": "reference", "metric": f"decode attn HBM GB/s @7B ctx {POS // 1024}k ({L} layers, 28Q/4KV, d128, fp32 KV)",
         "value": round(v_gbs, 3), "unit": "GB/s", "n_gpus": world, "steps": steps, "warmup": warm,
         "steps_requested": args.steps, "ms_per_step": round(att_ms, 3), "higher_is_better": True,
-        "scaling": "weak", "vs_baseline": None, "dtype": "f32", "data": "synthetic (seeded N(0,1))",
-        "config": {"workload": "cfg4: Qwen2.5-7B-shaped decode at position 32768, 28 layers, batch 1"},
+        "scaling": "strong" if world > 1 else "weak", "vs_baseline": None, "dtype": "f32",
+        "data": "synthetic (seeded N(0,1))", "config": cfg4_config(world),
+        "readings": {
+            "i_reference_as_is_1_core": {"value": round(one_gbs, 3), "unit": "GB/s",
+                                         "ms_per_step": round(L * one_core_att, 1),
+                                         "note": "kore's attention runs on one core whatever --threads is: "
+                                                 f"{L} layers x {one_core_att:.1f} ms"},
+            "ii_layers_fanned_over_cores": {"value": round(v_gbs, 3), "unit": "GB/s", "cores": T,
+                                            "ms_per_step": round(att_ms, 1),
+                                            "note": "the line's value: one kore forward() per core at a time"}},
         "cpu_baseline": {"value": round(v_gbs, 3), "unit": "GB/s", "cores": T, "kind": "reference",
-                         "sample": f"each step: {T} of the 28 layers decoded concurrently, one kore forward() "
-                                   f"per core (kore's attention is single-threaded), minus forward() at pos 0 "
-                                   f"({base:.1f} ms); {steps} of {n_total} requested steps within {budget_s:.0f} s"},
+                         "sample": f"each step: all {L} layers decoded at pos {POS}, one kore forward() per layer, "
+                                   f"{T} at a time (one per core), minus {per_thread} x forward() at pos 0 "
+                                   f"({base:.1f} ms) per thread; {steps} timed steps after {warm} warm-up"},
         "e2e": {"value": round(v_gbs, 3), "unit": "GB/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
     }
 
@@ -761,18 +1006,30 @@ def main():
     if args.block_only:
         print(json.dumps(run_block_only(args)), flush=True)
         return
+    ok = True
     try:
-        line = run_ours(args, rank, world, dist)
+        line = run_decode(args, rank, world, dist, POS, L, args.steps, args.e2e_steps, want_block=True)
         if not args.no_batched:
-            import torch
             batched = run_batched(args, rank, world, dist, load_peaks())
             if line is not None:
                 line["batched"] = batched
+        if line is not None and world == 1:
+            import torch
+            if not args.no_cfg12:
+                line["cfg2"] = run_decode(args, 0, 1, None, 8192, 28, max(200, args.steps), max(10, args.e2e_steps),
+                                          want_block=False)
+                line["cfg1"] = run_cfg1(args)
+            if not args.no_prefill:
+                line["prefill"] = run_prefill(args, torch.device("cuda", 0), load_peaks())
         if line is not None:
+            ok = all(x.get("parity", {}).get("ok", True) for x in (line, line.get("cfg2") or {}))
             print(json.dumps(line), flush=True)
     finally:
         if dist is not None:
             dist.destroy_process_group()
+    if not ok:
+        print("bench: parity check failed (see the line's parity object)", file=sys.stderr, flush=True)
+        sys.exit(3)
 
 
 if __name__ == "__main__":

@@ -240,6 +240,10 @@ int kore_cuda_peer_handle(kore_cuda_ctx *ctx, void *handle);
 int kore_cuda_peer_open(kore_cuda_ctx *ctx, const void *handles);
 int kore_cuda_attn_decode_sharded_dev(kore_cuda_ctx *ctx, int seq, int layer, int pos,
                                       const float *q, const float *k, const float *v, float *out);
+/* The same with kore's host buffers (as kore_cuda_attn_decode): q/k/v in,
+ * the merged output back, on every rank. */
+int kore_cuda_attn_decode_sharded(kore_cuda_ctx *ctx, int seq, int layer, int pos,
+                                  const float *q, const float *k, const float *v, float *out);
 
 /* Copies positions pos0..pos0+n-1 of (seq, layer) back to the host in kore's
  * row layout, k_out/v_out [n][n_head_kv*head_dim] (post-RoPE keys), so that a
@@ -250,6 +254,17 @@ int kore_cuda_kv_read(kore_cuda_ctx *ctx, int seq, int layer, int pos0, int n,
 /* Waits for the context's stream; returns KORE_CUDA_EDEVICE if a kernel
  * raised its error flag since the last check. */
 int kore_cuda_sync(kore_cuda_ctx *ctx);
+
+/* Limit of every bounded wait inside the decode and peer-exchange kernels of
+ * this context (a K/V tile copy, a peer GPU's partial), in nanoseconds of the
+ * GPU's global timer; 0 restores the default of 2 s. A kernel whose wait runs
+ * out records the failure, waits for its own copies still in flight and
+ * returns; the next kore_cuda_sync (or host-buffer call) reports
+ * KORE_CUDA_EDEVICE with a message naming the wait, and the context stays
+ * usable. kore has no counterpart (its attention cannot wait on anything):
+ * this is the failure detection of the multi-GPU split, where a rank that
+ * died or fell behind would otherwise leave its peers waiting. */
+int kore_cuda_set_wait_limit(kore_cuda_ctx *ctx, unsigned long long nanoseconds);
 
 /* The context's stream (a cudaStream_t) and a way to replace it with the
  * caller's (for interop with an engine that already owns a stream). */
@@ -273,8 +288,10 @@ int kore_cuda_set_stream(kore_cuda_ctx *ctx, void *stream);
  * GPU that loads the library, held until the process exits.
  *
  *  - The first call on a device looks up the array's device address (a
- *    one-time set-up done with that device current); make that first call
- *    before any stream capture.
+ *    one-time set-up done with that device current, repeated for each CUDA
+ *    context the caller makes current on it); make that first call before any
+ *    stream capture. The address belongs to the context it was looked up in:
+ *    after cudaDeviceReset, reload the library before calling again.
  *  - All calls on a device share the one array and it keeps the last call's
  *    contents, so calls that overlap on the GPU (on different streams, or from
  *    host threads without ordering) race and corrupt each other's results:
@@ -300,10 +317,13 @@ typedef struct kore_cuda_kv_view {
 /* One decode step of the sequence described by kv: RoPE of q and k at pos,
  * append of k/v at pos (written into kv's pages), attention over positions
  * 0..pos, output to out [n_head*head_dim]. q, k, v, out and dev_status are
- * device pointers; dev_status (optional, zeroed by the caller) receives a
- * non-zero code if a kernel meets a page id outside the pool. Ordered on
- * `stream` (a cudaStream_t; NULL for the default stream); returns without
- * synchronising. */
+ * device pointers; dev_status (optional, zeroed by the caller) receives the
+ * first failure a kernel meets: 3 for a page id outside the pool, 1 for a
+ * K/V tile copy that did not land within 2 s. Ordered on `stream` (a
+ * cudaStream_t; NULL for the default stream); returns without synchronising.
+ * Every input (pages, page table, q/k/v, RoPE table) may be written by the
+ * kernel just before on the stream, even one that lets its dependents start
+ * early: this call reads nothing before that kernel has completed. */
 int kore_cuda_attn_decode_noalloc(const kore_cuda_kv_view *kv, int pos, const float *q, const float *k,
                                   const float *v, float *out, int *dev_status, void *stream);
 

@@ -107,6 +107,7 @@ def load_library(path: str = LIB):
     L.kore_cuda_peer_handle.argtypes = [_vp, ctypes.c_char_p]
     L.kore_cuda_peer_open.argtypes = [_vp, ctypes.c_char_p]
     L.kore_cuda_attn_decode_sharded_dev.argtypes = [_vp, _i, _i, _i, _vp, _vp, _vp, _vp]
+    L.kore_cuda_attn_decode_sharded.argtypes = [_vp, _i, _i, _i, _vp, _vp, _vp, _vp]
     L.kore_cuda_kv_read.argtypes = [_vp, _i, _i, _i, _i, _vp, _vp]
     L.kore_cuda_attn_decode_noalloc.argtypes = [ctypes.POINTER(KvView), _i, _vp, _vp, _vp, _vp, _vp, _vp]
     L.kore_cuda_set_attn_weights.argtypes = [_vp, _i] + [ctypes.POINTER(_QMat)] * 4 + [_vp] * 3
@@ -114,6 +115,7 @@ def load_library(path: str = LIB):
     for n in ("kore_cuda_attn_block_decode", "kore_cuda_attn_block_decode_dev"):
         getattr(L, n).argtypes = [_vp, _i, _i, _i, _vp, _vp]
     L.kore_cuda_sync.argtypes = [_vp]
+    L.kore_cuda_set_wait_limit.argtypes = [_vp, ctypes.c_ulonglong]
     L.kore_cuda_stream.argtypes = [_vp]
     L.kore_cuda_stream.restype = _vp
     L.kore_cuda_set_stream.argtypes = [_vp, _vp]
@@ -194,6 +196,10 @@ class KoreCuda:
 
     def sync(self) -> None:
         self._ck(self._L.kore_cuda_sync(self._h))
+
+    def set_wait_limit(self, seconds: float) -> None:
+        """Limit of the decode and exchange kernels' bounded waits (0: the 2 s default)."""
+        self._ck(self._L.kore_cuda_set_wait_limit(self._h, int(seconds * 1e9)))
 
     def seq_reset(self, seq: int) -> None:
         self._ck(self._L.kore_cuda_seq_reset(self._h, seq))
@@ -288,6 +294,16 @@ class KoreCuda:
         """KV-sharded decode with the exchange over peer memory: full output on every rank."""
         self._ck(self._L.kore_cuda_attn_decode_sharded_dev(self._h, seq, layer, pos, _dptr(q), _dptr(k),
                                                            _dptr(v), _dptr(out)))
+
+    def decode_sharded(self, seq: int, layer: int, pos: int, q, k, v) -> np.ndarray:
+        """KV-sharded decode with kore's host buffers: the merged output on every rank."""
+        q = _host(q, self.H * self.d)
+        k = _host(k, self.kvd)
+        v = _host(v, self.kvd)
+        out = np.empty(self.H * self.d, np.float32)
+        self._ck(self._L.kore_cuda_attn_decode_sharded(self._h, seq, layer, pos, q.ctypes.data, k.ctypes.data,
+                                                       v.ctypes.data, out.ctypes.data))
+        return out.reshape(self.H, self.d)
 
     @property
     def part_floats(self) -> int:

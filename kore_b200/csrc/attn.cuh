@@ -36,6 +36,7 @@ struct DecodeParams {
     float *part_o;             // split scratch [n_q][G][max_splits][R][D]
     float2 *part_ml;           // split scratch [n_q][G][max_splits][R] (max, sum)
     int *err;                  // device error word
+    unsigned long long wait_ns;   // limit of each bounded wait for a K/V tile (then DEV_WAIT_FULL_TIMEOUT)
     float scale_log2;          // (1/sqrt(D)) * log2(e)
     int H, n_q, split_tokens, max_splits;
     int append_new;            // 1: the token at pos comes from k_new/v_new and is appended
@@ -96,6 +97,7 @@ struct ExchangeParams {
     size_t epoch_off;              // per-head epochs in `own`; the (value, epoch) slots start at 0
     float *out;                    // merged output [H*D]
     int *err;
+    unsigned long long wait_ns;    // limit of the wait for a peer's partial (then DEV_PEER_TIMEOUT)
     int n_ranks, rank, H, D;
 };
 
@@ -108,6 +110,12 @@ int decode_split_pages_max();
 size_t decode_smem_bytes(int head_dim);
 cudaError_t launch_kv_append(const AppendParams &p, cudaStream_t s);
 void set_ctxless_error(const char *msg);
+// The CUDA context current on this thread (the device's primary context
+// unless the caller made another one current), as an opaque key; 0 if none.
+uintptr_t current_cuda_context();
+// Sets a kernel's dynamic shared memory limit once per CUDA context (the
+// attribute belongs to the kernel as loaded in one context). Thread-safe.
+cudaError_t ensure_smem_limit(const void *kernel, int bytes);
 size_t prefill_tile_bytes(int head_dim);
 // bytes of one split slot of PrefillParams::part
 size_t prefill_slot_bytes(int head_dim);

@@ -50,6 +50,7 @@
 #include <cstdio>
 #include <cstring>
 #include <mutex>
+#include <vector>
 
 namespace kore {
 namespace {
@@ -246,6 +247,11 @@ __global__ void __launch_bounds__(NW * 32, 1) attn_decode_kernel(const __grid_co
     const int n_pages_split = n_tiles > 0 ? (u_end - 1) / P - lp_first + 1 : 0;
     const int *pt = kv.page_table + (size_t)seq * kv.pt_stride;
 
+    // Without prefetch_ok nothing is known about the preceding kernel on the
+    // stream: it may still be writing the page table (a caller's kernel that
+    // let this one start early), so every input is read after the wait.
+    if (!p.prefetch_ok) grid_dep_wait();
+
     // page ids of this split (checked; the host keeps a split within
     // kSplitPagesMax pages), barrier init
     for (int j = tid; j < n_pages_split && j < kSplitPagesMax; j += NT) {
@@ -312,7 +318,7 @@ __global__ void __launch_bounds__(NW * 32, 1) attn_decode_kernel(const __grid_co
             u += n;
         }
     }
-    grid_dep_wait();
+    if (p.prefetch_ok) grid_dep_wait();
     grid_dep_launch();
     if (lane == 0)
         for (int j = pre; j < SPW && j < my_tiles; ++j) issue(j);
@@ -386,7 +392,13 @@ __global__ void __launch_bounds__(NW * 32, 1) attn_decode_kernel(const __grid_co
 
     for (int j = 0; j < my_tiles; ++j) {
         const int s = j % SPW;
-        if (!mbar_wait(my_full + s, (j / SPW) & 1, p.err, DEV_WAIT_FULL_TIMEOUT)) break;
+        if (!__all_sync(FULL, mbar_wait(my_full + s, (j / SPW) & 1, p.err, DEV_WAIT_FULL_TIMEOUT, p.wait_ns))) {
+            // gave up (the error word says so): tiles j .. j+SPW-1 may still be
+            // landing in this warp's stages; wait for them before the stage
+            // memory is reused below or the block exits
+            for (int t = j; t < my_tiles && t < j + SPW; ++t) mbar_drain(my_full + t % SPW, (t / SPW) & 1);
+            break;
+        }
         const int nv = min(TT, u_end - (u_begin + (warp + j * NW) * TT));
         const float *tile = my_stages + (size_t)s * 2 * SM::TILE_F;
         process_tile<D, R, TT>(st, tile, tile + SM::TILE_F, nv, pbuf, lane);
@@ -507,14 +519,7 @@ template <int D, int R, int NW, int SPW>
 cudaError_t launch_shape(const DecodeParams &p, int grid_x, cudaStream_t s, bool merge) {
     using SM = DecodeSmem<D, NW, kTT, SPW>;
     auto kern = attn_decode_kernel<D, R, NW, kTT, SPW>;
-    static bool configured[64] = {};
-    int dev = 0;
-    cudaGetDevice(&dev);
-    if (dev < 0 || dev >= 64 || !configured[dev]) {
-        cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)SM::bytes);
-        if (e != cudaSuccess) return e;
-        if (dev >= 0 && dev < 64) configured[dev] = true;
-    }
+    if (cudaError_t e = ensure_smem_limit(reinterpret_cast<const void *>(kern), (int)SM::bytes)) return e;
     cudaLaunchConfig_t cfg = {};
     cfg.gridDim = dim3(grid_x, p.kv.G, p.n_q);
     cfg.blockDim = dim3(NW * 32);
@@ -591,12 +596,16 @@ static_assert(kNoallocFloats > kNoallocPartFloats, "scratch layout");
 
 static __device__ __align__(256) float g_noalloc_scratch[kNoallocFloats];
 
+// The array's device address, looked up once per device and CUDA context
+// (the library's device code, the array with it, is loaded per context).
 struct NoallocDevice {
-    float *scratch = nullptr;   // device address of g_noalloc_scratch on this device
+    int dev = -1;
+    uintptr_t cuda_ctx = 0;
+    float *scratch = nullptr;   // device address of g_noalloc_scratch in that context
     int num_sms = 0;
 };
 std::mutex g_noalloc_mu;
-NoallocDevice g_noalloc_dev[64];
+std::vector<NoallocDevice> g_noalloc_dev;
 
 int noalloc_fail(int code, const char *fmt, long long a = 0, long long b = 0) {
     char buf[256];
@@ -626,25 +635,33 @@ extern "C" int kore_cuda_attn_decode_noalloc(const kore_cuda_kv_view *kv, int po
     if (pos < 0 || pos >= kv->n_rope || pos / P >= kv->n_table)
         return noalloc_fail(KORE_CUDA_ERANGE, "position %lld outside the RoPE table or the page table", pos);
 
+    const uintptr_t vdiff = reinterpret_cast<uintptr_t>(kv->v_pages) - reinterpret_cast<uintptr_t>(kv->k_pages);
+    if (vdiff % 16)
+        return noalloc_fail(KORE_CUDA_EINVAL, "v_pages - k_pages must be a multiple of 16 bytes");
+
     int dev = 0;
-    if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64)
+    if (cudaGetDevice(&dev) != cudaSuccess || dev < 0)
         return noalloc_fail(KORE_CUDA_ECUDA, "no current CUDA device");
+    const uintptr_t cctx = current_cuda_context();
     NoallocDevice nd;
     {
         std::lock_guard<std::mutex> lk(g_noalloc_mu);
-        NoallocDevice &d = g_noalloc_dev[dev];
-        if (!d.scratch) {   // once per device, with that device current
+        for (const NoallocDevice &d : g_noalloc_dev)
+            if (d.dev == dev && d.cuda_ctx == cctx) nd = d;
+        if (!nd.scratch) {   // set-up: once per device (and context), with that device current
             void *ptr = nullptr;
             cudaError_t e = cudaGetSymbolAddress(&ptr, g_noalloc_scratch);
             if (e != cudaSuccess)
                 return noalloc_fail(KORE_CUDA_ECUDA, "cudaGetSymbolAddress of the scratch array failed (error %lld)",
                                     (long long)e);
-            e = cudaDeviceGetAttribute(&d.num_sms, cudaDevAttrMultiProcessorCount, dev);
+            e = cudaDeviceGetAttribute(&nd.num_sms, cudaDevAttrMultiProcessorCount, dev);
             if (e != cudaSuccess)
                 return noalloc_fail(KORE_CUDA_ECUDA, "cudaDeviceGetAttribute failed (error %lld)", (long long)e);
-            d.scratch = static_cast<float *>(ptr);
+            nd.dev = dev;
+            nd.cuda_ctx = cctx;
+            nd.scratch = static_cast<float *>(ptr);
+            g_noalloc_dev.push_back(nd);
         }
-        nd = d;
     }
 
     const int R = H / G, TT = decode_tile_tokens();
@@ -668,7 +685,9 @@ extern "C" int kore_cuda_attn_decode_noalloc(const kore_cuda_kv_view *kv, int po
     DecodeParams p;
     memset(&p, 0, sizeof p);
     p.kv.k = kv->k_pages;
-    p.kv.v_off = (long long)(kv->v_pages - kv->k_pages);
+    // the distance between the pools in floats, from their byte addresses
+    // (two separate allocations: no pointer difference between them)
+    p.kv.v_off = (long long)(intptr_t)vdiff / (long long)sizeof(float);
     p.kv.page_table = kv->page_table;
     p.kv.pt_stride = kv->n_table;
     p.kv.P = P;
@@ -686,6 +705,7 @@ extern "C" int kore_cuda_attn_decode_noalloc(const kore_cuda_kv_view *kv, int po
     p.part_o = nd.scratch;
     p.part_ml = reinterpret_cast<float2 *>(nd.scratch + kNoallocPartFloats);
     p.err = dev_status;
+    p.wait_ns = kWaitNs;
     p.scale_log2 = (1.0f / sqrtf((float)D)) * 1.4426950408889634f;
     p.H = H;
     p.n_q = 1;

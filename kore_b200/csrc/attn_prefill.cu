@@ -740,14 +740,8 @@ cudaError_t launch_prefill_d(const PrefillParams &p, cudaStream_t s) {
     kv_split_kernel<D><<<dim3(tiles_needed, p.kv.G, 2), 256, 0, s>>>(p);
     cudaError_t e = cudaGetLastError();
     if (e != cudaSuccess) return e;
-    static bool configured[64] = {};
-    int dev = 0;
-    cudaGetDevice(&dev);
-    if (dev < 0 || dev >= 64 || !configured[dev]) {
-        e = cudaFuncSetAttribute(prefill_kernel<D>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)SM::bytes);
-        if (e != cudaSuccess) return e;
-        if (dev >= 0 && dev < 64) configured[dev] = true;
-    }
+    e = ensure_smem_limit(reinterpret_cast<const void *>(prefill_kernel<D>), (int)SM::bytes);
+    if (e != cudaSuccess) return e;
     if (p.n_items <= 0 || !p.items) return cudaErrorInvalidValue;
     prefill_kernel<D><<<dim3(p.n_items), 192, SM::bytes, s>>>(p);
     return cudaGetLastError();

@@ -16,7 +16,9 @@
 #include <cstdarg>
 #include <cstdio>
 #include <cstring>
+#include <mutex>
 #include <string>
+#include <utility>
 #include <vector>
 
 using namespace kore;
@@ -31,6 +33,8 @@ struct kore_cuda_ctx {
     // default: on B200 it measured slower at 32 and 64 MB, on one GPU and on
     // two (the prefetched lines did not outlive their wait)
     long long l2_prefetch_bytes = 0;
+    // limit of the decode and exchange kernels' bounded waits (kore_cuda_set_wait_limit)
+    unsigned long long wait_ns = kWaitNs;
     cudaStream_t stream = nullptr;
     bool own_stream = false;
     float *kv = nullptr;        // [n_layer][2][n_pages][G][P][D]
@@ -101,6 +105,39 @@ thread_local std::string g_create_msg = "no error";
 namespace kore {
 // Message for calls that have no context (read with kore_cuda_last_error(NULL)).
 void set_ctxless_error(const char *msg) { g_create_msg = msg; }
+
+uintptr_t current_cuda_context() {
+    // the driver's cuCtxGetCurrent, resolved once through the runtime (the
+    // library links the static runtime only)
+    using get_current_fn = int (*)(void **);
+    static get_current_fn fn = []() -> get_current_fn {
+        void *f = nullptr;
+        cudaDriverEntryPointQueryResult q;
+        if (cudaGetDriverEntryPoint("cuCtxGetCurrent", &f, cudaEnableDefault, &q) != cudaSuccess ||
+            q != cudaDriverEntryPointSuccess) {
+            cudaGetLastError();
+            return nullptr;
+        }
+        return reinterpret_cast<get_current_fn>(f);
+    }();
+    void *c = nullptr;
+    if (!fn || fn(&c) != 0) return 0;
+    return reinterpret_cast<uintptr_t>(c);
+}
+
+cudaError_t ensure_smem_limit(const void *kernel, int bytes) {
+    static std::mutex mu;
+    static std::vector<std::pair<const void *, uintptr_t>> done;
+    int dev = 0;
+    if (cudaError_t e = cudaGetDevice(&dev)) return e;   // makes the device's primary context current if none is
+    const uintptr_t ctx = current_cuda_context();
+    std::lock_guard<std::mutex> lk(mu);
+    for (const auto &d : done)
+        if (d.first == kernel && d.second == ctx && ctx != 0) return cudaSuccess;
+    const cudaError_t e = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, bytes);
+    if (e == cudaSuccess && ctx != 0) done.emplace_back(kernel, ctx);
+    return e;
+}
 }  // namespace kore
 
 namespace {
@@ -271,6 +308,16 @@ int stage_in(kore_cuda_ctx *c, size_t floats) {
 // (kErrPad on) were queued for copying back with it; reports a device error.
 constexpr size_t kErrPad = 256;   // bytes from the device error word to the decode output behind it
 
+const char *device_error_text(int e) {
+    switch (e) {
+        case DEV_WAIT_FULL_TIMEOUT: return "bounded wait for a K/V tile or weight copy expired";
+        case DEV_WAIT_EMPTY_TIMEOUT: return "bounded wait for a free stage expired";
+        case DEV_BAD_PAGE: return "page table entry outside the pool";
+        case DEV_PEER_TIMEOUT: return "a peer GPU's partial did not arrive within the wait limit";
+        default: return "unknown device error code";
+    }
+}
+
 int finish(kore_cuda_ctx *c, size_t extra = 0) {
     CK(cudaMemcpyAsync(c->host_err, c->err_d, extra ? kErrPad + extra : sizeof(int), cudaMemcpyDeviceToHost,
                        c->stream));
@@ -281,10 +328,7 @@ int finish(kore_cuda_ctx *c, size_t extra = 0) {
         // a prefill that gave up may have left a split half's arrival counted
         if (c->pf_counters) CK(cudaMemsetAsync(c->pf_counters, 0, c->pf_slots_cap * sizeof(int), c->stream));
         CK(cudaStreamSynchronize(c->stream));
-        return fail(c, KORE_CUDA_EDEVICE, "device error %d (%s)", e,
-                    e == DEV_BAD_PAGE ? "page table entry outside the pool"
-                                      : (e == DEV_WAIT_FULL_TIMEOUT ? "bounded wait for a K/V tile expired"
-                                                                    : "bounded wait for a free stage expired"));
+        return fail(c, KORE_CUDA_EDEVICE, "device error %d (%s)", e, device_error_text(e));
     }
     return KORE_CUDA_OK;
 }
@@ -327,6 +371,7 @@ int run_decode(kore_cuda_ctx *c, int layer, int n_q, bool contiguous, int seq0, 
     p.part_o = c->part_o;
     p.part_ml = c->part_ml;
     p.err = c->err_d;
+    p.wait_ns = c->wait_ns;
     p.scale_log2 = (1.0f / std::sqrt((float)c->D)) * 1.4426950408889634f;
     p.H = c->H;
     p.n_q = n_q;
@@ -852,6 +897,7 @@ int kore_cuda_attn_decode_sharded_dev(kore_cuda_ctx *c, int seq, int layer, int 
     xp.epoch_off = c->x_epoch_off;
     xp.out = out;
     xp.err = c->err_d;
+    xp.wait_ns = c->wait_ns;
     xp.n_ranks = c->NS;
     xp.rank = c->rank;
     xp.H = c->H;
@@ -863,7 +909,7 @@ int kore_cuda_attn_decode_sharded_dev(kore_cuda_ctx *c, int seq, int layer, int 
 }
 
 static int decode_host(kore_cuda_ctx *c, int n_seq, const float *q, const float *k, const float *v, float *out,
-                       const int *seq_ids, const int *pos, int layer, bool batch) {
+                       const int *seq_ids, const int *pos, int layer, bool batch, bool sharded = false) {
     DeviceGuard dg(c->cfg.device);
     const size_t nq = (size_t)n_seq * c->H * c->D, nk = (size_t)n_seq * c->kvd;
     if (int rc = grow_stage(c, 2 * nq + 2 * nk)) return rc;
@@ -876,7 +922,8 @@ static int decode_host(kore_cuda_ctx *c, int n_seq, const float *q, const float 
         // one sequence: the output lands right behind the error word and both
         // come back in one copy
         float *dout = reinterpret_cast<float *>(reinterpret_cast<char *>(c->err_d) + kErrPad);
-        if (int rc = kore_cuda_attn_decode_dev(c, seq_ids[0], layer, pos[0], ds, ds + nq, ds + nq + nk, dout))
+        if (int rc = sharded ? kore_cuda_attn_decode_sharded_dev(c, seq_ids[0], layer, pos[0], ds, ds + nq, ds + nq + nk, dout)
+                             : kore_cuda_attn_decode_dev(c, seq_ids[0], layer, pos[0], ds, ds + nq, ds + nq + nk, dout))
             return rc;
         if (int rc2 = finish(c, nq * sizeof(float))) return rc2;
         memcpy(out, reinterpret_cast<const char *>(c->host_err) + kErrPad, nq * sizeof(float));
@@ -897,6 +944,15 @@ int kore_cuda_attn_decode(kore_cuda_ctx *c, int seq, int layer, int pos, const f
     if (!q || !k || !v || !out) return fail(c, KORE_CUDA_EINVAL, "null q, k, v or out");
     if (int rc = check_range(c, seq, layer, pos, 1)) return rc;
     return decode_host(c, 1, q, k, v, out, &seq, &pos, layer, false);
+}
+
+int kore_cuda_attn_decode_sharded(kore_cuda_ctx *c, int seq, int layer, int pos, const float *q, const float *k,
+                                  const float *v, float *out) {
+    if (!c) return KORE_CUDA_EINVAL;
+    if (!q || !k || !v || !out) return fail(c, KORE_CUDA_EINVAL, "null q, k, v or out");
+    if (!c->peers_open) return fail(c, KORE_CUDA_ESTATE, "peer exchange not set up (kore_cuda_peer_open)");
+    if (int rc = check_range(c, seq, layer, pos, 1)) return rc;
+    return decode_host(c, 1, q, k, v, out, &seq, &pos, layer, false, true);
 }
 
 int kore_cuda_attn_decode_batch(kore_cuda_ctx *c, int layer, int n_seq, const int *seq_ids, const int *pos,
@@ -1094,6 +1150,12 @@ int kore_cuda_kv_read(kore_cuda_ctx *c, int seq, int layer, int pos0, int n, flo
         }
     }
     CK(cudaStreamSynchronize(c->stream));
+    return KORE_CUDA_OK;
+}
+
+int kore_cuda_set_wait_limit(kore_cuda_ctx *c, unsigned long long nanoseconds) {
+    if (!c) return KORE_CUDA_EINVAL;
+    c->wait_ns = nanoseconds ? nanoseconds : kWaitNs;
     return KORE_CUDA_OK;
 }
 

@@ -62,21 +62,41 @@ __device__ __forceinline__ uint64_t global_ns() {
     return t;
 }
 
-// Bounded wait on a phase of an mbarrier: gives up after kWaitNs of wall time
-// (checked every 64 polls) or kWaitPolls polls, whichever comes first, records
-// `code` in the error word and returns false. A healthy pipeline waits
+// Bounded wait on a phase of an mbarrier: gives up after `limit_ns` of wall
+// time (checked every 64 polls) or kWaitPolls polls, whichever comes first,
+// records `code` in the error word and returns false. A healthy pipeline waits
 // microseconds; the bound only turns a lost copy into an error the host sees.
-constexpr uint64_t kWaitNs = 2000000000ull;   // 2 s
+// kWaitNs is the default limit (a context can set another one for the decode
+// and exchange kernels); kDrainNs bounds the wait a kernel that gave up makes
+// for its own copies still in flight before it exits.
+constexpr uint64_t kWaitNs = 2000000000ull;    // 2 s
+constexpr uint64_t kDrainNs = 2000000000ull;   // 2 s
 constexpr uint32_t kWaitPolls = 1u << 26;
 
-__device__ __forceinline__ bool mbar_wait(uint64_t *bar, uint32_t parity, int *err, int code) {
+__device__ __forceinline__ bool mbar_wait(uint64_t *bar, uint32_t parity, int *err, int code,
+                                          uint64_t limit_ns = kWaitNs) {
     if (mbar_try_wait(bar, parity)) return true;
     const uint64_t t0 = global_ns();
     for (uint32_t it = 1; it < kWaitPolls; ++it) {
         if (mbar_try_wait(bar, parity)) return true;
-        if ((it & 63) == 0 && global_ns() - t0 > kWaitNs) break;
+        if ((it & 7) == 0 && global_ns() - t0 > limit_ns) break;
     }
     raise_error(err, code);
+    return false;
+}
+
+// Waits, bounded by kDrainNs and without recording an error, for a phase of
+// an mbarrier whose bulk copy is in flight: a kernel that gave up calls this
+// for every copy it issued and never consumed, so that no copy lands in the
+// shared memory of a block that has exited. Returns false if even this wait
+// expired (the error word already holds the first failure).
+__device__ __forceinline__ bool mbar_drain(uint64_t *bar, uint32_t parity) {
+    if (mbar_try_wait(bar, parity)) return true;
+    const uint64_t t0 = global_ns();
+    for (uint32_t it = 1; it < kWaitPolls; ++it) {
+        if (mbar_try_wait(bar, parity)) return true;
+        if ((it & 63) == 0 && global_ns() - t0 > kDrainNs) break;
+    }
     return false;
 }
 

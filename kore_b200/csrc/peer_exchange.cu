@@ -8,12 +8,15 @@
 // every other rank (CUDA IPC), so this kernel, one CTA per query head:
 //   1. merges this rank's splits of head h (when the decode left several);
 //   2. stores the head's partial into this rank's slot of every peer's buffer
-//      as 8-byte (value, epoch) pairs — plain NVLink stores, no multicast:
-//      each pair is written by one store, so a reader that sees the epoch
-//      sees the value with it, and no fence or flag is needed;
-//   3. polls, bounded by 2 s of %globaltimer, its own buffer until every
-//      peer's pairs for head h carry this step's epoch (system-scope relaxed
-//      8-byte loads);
+//      as (value, epoch) pairs packed into one 64-bit word each (value in the
+//      low half) — plain NVLink stores, no multicast. Each word is written by
+//      one scalar st.relaxed.sys.b64 and read by one scalar ld.relaxed.sys.b64,
+//      which the PTX memory model makes single-copy atomic, so a reader that
+//      sees this step's epoch sees this step's value with it, and no fence or
+//      flag is needed;
+//   3. polls its own buffer, bounded by the context's wait limit (2 s unless
+//      set otherwise) of %globaltimer, until every peer's words for head h
+//      carry this step's epoch;
 //   4. merges the N partials: out = sum_r 2^(L_r - L) O_r, L = log2 sum 2^L_r,
 //      which is kore's single softmax (kore.cpp:1437-1454) regrouped by shard.
 // The epoch is a per-head counter kept on the device (the CTA of head h is
@@ -30,25 +33,28 @@
 namespace kore {
 namespace {
 
-__device__ __forceinline__ void st_pair_sys(uint2 *p, uint32_t value, uint32_t epoch) {
-    asm volatile("st.relaxed.sys.global.v2.b32 [%0], {%1, %2};" ::"l"(p), "r"(value), "r"(epoch) : "memory");
+// One (value, epoch) pair as a single 64-bit word: one scalar access, which
+// is single-copy atomic (a vector access of two 32-bit halves would not be).
+__device__ __forceinline__ void st_pair_sys(uint64_t *p, uint32_t value, uint32_t epoch) {
+    const uint64_t w = (uint64_t)value | ((uint64_t)epoch << 32);
+    asm volatile("st.relaxed.sys.global.b64 [%0], %1;" ::"l"(p), "l"(w) : "memory");
 }
 
-__device__ __forceinline__ uint2 ld_pair_sys(const uint2 *p) {
-    uint2 v;
-    asm volatile("ld.relaxed.sys.global.v2.b32 {%0, %1}, [%2];" : "=r"(v.x), "=r"(v.y) : "l"(p) : "memory");
-    return v;
+__device__ __forceinline__ uint64_t ld_pair_sys(const uint64_t *p) {
+    uint64_t w;
+    asm volatile("ld.relaxed.sys.global.b64 %0, [%1];" : "=l"(w) : "l"(p) : "memory");
+    return w;
 }
 
-// Waits (bounded) until the pair at p carries `epoch`; returns its value.
-__device__ __forceinline__ float await_pair(const uint2 *p, uint32_t epoch, int *err) {
-    uint2 v = ld_pair_sys(p);
-    if (v.y == epoch) return __uint_as_float(v.x);
+// Waits (bounded by limit_ns) until the word at p carries `epoch`; returns its value.
+__device__ __forceinline__ float await_pair(const uint64_t *p, uint32_t epoch, int *err, uint64_t limit_ns) {
+    uint64_t w = ld_pair_sys(p);
+    if ((uint32_t)(w >> 32) == epoch) return __uint_as_float((uint32_t)w);
     const uint64_t t0 = global_ns();
     for (;;) {
-        v = ld_pair_sys(p);
-        if (v.y == epoch) return __uint_as_float(v.x);
-        if (global_ns() - t0 > kWaitNs) {
+        w = ld_pair_sys(p);
+        if ((uint32_t)(w >> 32) == epoch) return __uint_as_float((uint32_t)w);
+        if (global_ns() - t0 > limit_ns) {
             raise_error(err, DEV_PEER_TIMEOUT);
             return 0.f;
         }
@@ -86,24 +92,24 @@ __global__ void __launch_bounds__(D) peer_exchange_kernel(const __grid_constant_
         lse_me = __ldcg(p.local + (size_t)H * D + h);
     }
 
-    // 1. push it to every peer: one 8-byte (value, epoch) store per element
+    // 1. push it to every peer: one 64-bit (value, epoch) store per element
     for (int r = 0; r < N; ++r) {
         if (r == me) continue;
-        uint2 *dst = reinterpret_cast<uint2 *>(p.peers[r]) + (((size_t)par * N + me) * H + h) * SLOT;
+        uint64_t *dst = reinterpret_cast<uint64_t *>(p.peers[r]) + (((size_t)par * N + me) * H + h) * SLOT;
         st_pair_sys(dst + tid, __float_as_uint(o_me), e);
         if (tid == 0) st_pair_sys(dst + D, __float_as_uint(lse_me), e);
     }
 
     // 2. collect every peer's element tid (thread 0 also the LSEs)
-    const uint2 *own = reinterpret_cast<const uint2 *>(p.own);
+    const uint64_t *own = reinterpret_cast<const uint64_t *>(p.own);
     float x[kMaxRanks];
 #pragma unroll
     for (int r = 0; r < kMaxRanks; ++r) {
         x[r] = 0.f;
         if (r < N && r != me) {
-            const uint2 *src = own + (((size_t)par * N + r) * H + h) * SLOT;
-            x[r] = await_pair(src + tid, e, p.err);
-            if (tid == 0) s_lse[r] = await_pair(src + D, e, p.err);
+            const uint64_t *src = own + (((size_t)par * N + r) * H + h) * SLOT;
+            x[r] = await_pair(src + tid, e, p.err, p.wait_ns);
+            if (tid == 0) s_lse[r] = await_pair(src + D, e, p.err, p.wait_ns);
         }
     }
     if (tid == 0) s_lse[me] = lse_me;

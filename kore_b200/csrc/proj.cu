@@ -373,8 +373,11 @@ __global__ void __launch_bounds__(32 * kWarps) qmatvec_kernel(const __grid_const
             delta = issue(gg);
         }
         const bool ok = mbar_wait(bar, phase, p.err, DEV_WAIT_FULL_TIMEOUT);
+        if (!__all_sync(0xffffffffu, ok)) {
+            mbar_drain(bar, phase);   // the copy may still land: not into a block that has exited
+            break;
+        }
         phase ^= 1;
-        if (!__all_sync(0xffffffffu, ok)) break;
         int row;
         const QSeg &sg = p.seg[find_seg(p, 2 * gg + rr, row)];
         float r;
@@ -418,15 +421,8 @@ cudaError_t launch_qmatvec(const QMatvecParams &p, int grid, cudaStream_t s) {
     int slot = 0;
     const size_t smem = qmatvec_smem_bytes(p.cols, bb, &slot);
     if (slot != p.slot_bytes || smem > kQmatvecMaxSmem) return cudaErrorInvalidValue;
-    static bool configured[64] = {};
-    int dev = 0;
-    cudaGetDevice(&dev);
-    if (dev < 0 || dev >= 64 || !configured[dev]) {
-        cudaError_t e =
-            cudaFuncSetAttribute(qmatvec_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kQmatvecMaxSmem);
-        if (e != cudaSuccess) return e;
-        if (dev >= 0 && dev < 64) configured[dev] = true;
-    }
+    if (cudaError_t e = ensure_smem_limit(reinterpret_cast<const void *>(qmatvec_kernel), (int)kQmatvecMaxSmem))
+        return e;
     cudaLaunchConfig_t cfg = {};
     cfg.gridDim = dim3(grid);
     cfg.blockDim = dim3(32 * kWarps);

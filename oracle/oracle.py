@@ -35,12 +35,18 @@ _ref = None
 
 
 def build(ref_dir: str | None = None) -> None:
-    """Compile the restatement and, when the reference sources exist, the
-    reference harness."""
+    """Compile the restatement and, when a reference checkout is named (the
+    argument, else the KORE_REF_DIR environment variable) and holds kore.cpp,
+    the reference harness. Without one the prebuilt oracle/_ref libraries, if
+    any, stay as they are."""
     subprocess.run(["make", "-s", "-C", HERE, "oracle"], check=True)
-    ref_dir = ref_dir or os.environ.get("KORE_REF_DIR", "/root/reference")
-    if os.path.exists(os.path.join(ref_dir, "kore.cpp")):
-        subprocess.run(["make", "-s", "-C", HERE, "ref", f"KORE_REF_DIR={ref_dir}"], check=True)
+    ref_dir = ref_dir or os.environ.get("KORE_REF_DIR")
+    if not ref_dir:
+        print("oracle: KORE_REF_DIR is not set; the reference harness (oracle/_ref) is not rebuilt")
+        return
+    if not os.path.exists(os.path.join(ref_dir, "kore.cpp")):
+        raise FileNotFoundError(f"KORE_REF_DIR={ref_dir} holds no kore.cpp")
+    subprocess.run(["make", "-s", "-C", HERE, "ref", f"KORE_REF_DIR={ref_dir}"], check=True)
 
 
 class KorcQW(ctypes.Structure):

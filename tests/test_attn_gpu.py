@@ -252,3 +252,32 @@ def test_cfg3_7b_prefill_2048_onto_4096_sampled_rows():
         assert_attn_close(out[z], o.decode(pos0 + z, q[z], k[z], v[z]), f"prefill row {z}")
     kr, vr = g.kv_read(0, 0, pos0, n)
     np.testing.assert_array_equal(kr, o.kc[pos0:pos0 + n])
+
+
+def test_cfg5_full_shape_batched_decode():
+    """Config 5 at the bench's own shape: the 64 cached lengths ~U{1024..32768}
+    (seed 5), 16Q/2KV heads, d 128, 256-token pages, one layer, all 64
+    sequences in one batched decode call (the split-length choice and the
+    replay of ragged splits at full size). Checked against the oracle on 10
+    sequences: the shortest, the longest and 8 in between. Every sequence
+    holds a prefix of one seeded block of rows, as in the bench."""
+    H, G, d = 16, 2, 128
+    lens = np.random.default_rng(5).integers(1024, 32769, 64)
+    Lmax = int(lens.max())
+    n = lens.size
+    g = make_ctx(H, G, d, Lmax + 1, max_seqs=n, n_pages=int(sum((int(x) + 256) // 256 for x in lens)))
+    k, v = normal(5005, (Lmax, G * d), (Lmax, G * d))
+    for s, ln in enumerate(lens):
+        g.append(0 + s, 0, 0, k[:int(ln)], v[:int(ln)])
+    q, kn, vn = normal(5006, (n, H * d), (n, G * d), (n, G * d))
+    out = g.decode_batch(0, np.arange(n, dtype=np.int32), lens.astype(np.int32), q, kn, vn)
+    order = np.argsort(lens, kind="stable")
+    check = sorted(set([int(order[0]), int(order[-1])] + [int(order[i]) for i in np.linspace(1, n - 2, 8).astype(int)]))
+    o = O.OracleLayer(H, G, d, Lmax + 1)
+    o.fill(0, k, v)
+    for s in sorted(check, key=lambda s: int(lens[s])):
+        p = int(lens[s])
+        saved = o.kc[p].copy(), o.vc[p].copy()        # the oracle's decode writes row p
+        ref = o.decode(p, q[s], kn[s], vn[s])
+        o.kc[p], o.vc[p] = saved
+        assert_attn_close(out[s], ref, f"cfg5 sequence {s}, {p} cached positions")

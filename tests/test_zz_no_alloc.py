@@ -89,3 +89,63 @@ def test_noalloc_decode_refuses_bad_arguments_with_a_message():
     rc = lib.kore_cuda_attn_decode_noalloc(ctypes.byref(view), 1, q.data_ptr(), kv.data_ptr(), kv.data_ptr(),
                                            out.data_ptr(), None, None)
     assert rc == -1 and b"geometry" in lib.kore_cuda_last_error(None)
+
+
+@pytest.mark.parametrize("pos", [0, 20])
+def test_noalloc_decode_short_contexts_match_the_oracle(pos):
+    """Position 0 (no cached position: the one new row) and a context short
+    enough for a single split, whose decode kernel writes the output itself
+    with no split merge; checked against the oracle directly, two calls in a
+    row (the second reads the row the first appended into the caller's
+    pages)."""
+    import torch
+    lib = K.load_library()
+    H, G, D, P = 28, 4, 128, 64
+    n_rope = pos + 2
+    o = O.OracleLayer(H, G, D, n_rope)
+    rows_k = np.zeros((max(pos, 1), G * D), np.float32)
+    rows_v = np.zeros((max(pos, 1), G * D), np.float32)
+    if pos:
+        kp, vp = normal(910, (pos, G * D), (pos, G * D))
+        o.fill(0, kp, vp)
+        rows_k, rows_v = o.kc[:pos].copy(), o.vc[:pos].copy()
+    view, keep = _caller_owned_cache(torch, H, G, D, P, rows_k, rows_v, n_rope)
+    dev = torch.device("cuda", 0)
+    for step, p in enumerate((pos, pos + 1)):
+        q, k, v = normal(911 + step, (H * D,), (G * D,), (G * D,))
+        want = o.decode(p, q, k, v)
+        tq, tk, tv = (torch.from_numpy(x).to(dev) for x in (q, k, v))
+        out = torch.full((H * D,), float("nan"), device=dev)
+        status = torch.zeros(1, dtype=torch.int32, device=dev)
+        torch.cuda.synchronize()
+        rc = lib.kore_cuda_attn_decode_noalloc(ctypes.byref(view), p, tq.data_ptr(), tk.data_ptr(),
+                                               tv.data_ptr(), out.data_ptr(), status.data_ptr(), None)
+        torch.cuda.synchronize()
+        assert rc == 0, lib.kore_cuda_last_error(None).decode()
+        assert int(status.item()) == 0
+        assert_attn_close(out.cpu().numpy().reshape(H, D), want, f"no-alloc decode at {p}")
+
+
+def test_noalloc_decode_refuses_a_geometry_beyond_the_scratch_array():
+    """32 KV heads of 8 query heads each, 64-token pages: past ~130000 cached
+    positions the splits' partial outputs no longer fit the fixed array, and
+    the call must say so instead of launching. (The host refuses before any
+    device memory is read, so small placeholder buffers stand in for the
+    pools.)"""
+    import torch
+    lib = K.load_library()
+    H, G, D, P = 256, 32, 128, 64
+    pos = 200000
+    dev = torch.device("cuda", 0)
+    pool = torch.zeros(4096, device=dev)
+    table = torch.zeros(16, dtype=torch.int32, device=dev)
+    view = K.KvView(pool.data_ptr(), pool.data_ptr() + 8192, table.data_ptr(), pos // P + 1, 4, P, H, G, D,
+                    pool.data_ptr(), pos + 1)
+    q = torch.zeros(H * D, device=dev)
+    kv = torch.zeros(G * D, device=dev)
+    out = torch.zeros(H * D, device=dev)
+    rc = lib.kore_cuda_attn_decode_noalloc(ctypes.byref(view), pos, q.data_ptr(), kv.data_ptr(), kv.data_ptr(),
+                                           out.data_ptr(), None, None)
+    assert rc == -1
+    msg = lib.kore_cuda_last_error(None).decode()
+    assert "split scratch" in msg and "2359296" in msg, msg
