@@ -206,6 +206,68 @@ int kore_cuda_attn_block_decode_dev(kore_cuda_ctx *ctx, int seq, int layer, int 
                                     const float *xb, float *o);
 
 /*
+ * The whole decode step on the GPU.
+ *
+ * kore's forward() (kore.cpp:1397-1480) for one token and its greedy choice
+ * (sample_token at temperature 0, kore.cpp:1601-1603), all on the device:
+ * the token's embedding row (get_row, kore.cpp:384-407), per layer the
+ * attention block above with its RMSNorm (kore.cpp:1367-1372) and residual
+ * add, the SwiGLU feed-forward (kore.cpp:1460-1471) with its RMSNorm and
+ * residual add, then the output RMSNorm, the logits (kore.cpp:1474-1478) and
+ * their argmax (the first index of the largest logit). With the weights
+ * uploaded once (kore_cuda_set_model), a step moves a token id in and a token
+ * id out, instead of crossing PCIe around every layer.
+ *
+ * Arithmetic is kore's own in every step but the attention (which is within
+ * the attention tolerance, as kore_cuda_attn_decode): the Q8_K quantisations
+ * and the Q4_K / Q6_K products bit for bit (as kore_cuda_qmatvec), the
+ * RMSNorm with kore's double-precision sum of squares, the SwiGLU with the
+ * C library's expf as kore calls it, the residual adds and the embedding
+ * dequantisation with kore's rounding. A step at position 0 (one key: the
+ * attention is exact too) therefore gives kore's logits bit for bit.
+ */
+#define KORE_CUDA_F32 0     /* GGUF tensor type ids of the embedding tables get_row reads */
+#define KORE_CUDA_F16 1
+#define KORE_CUDA_BF16 30
+
+typedef struct kore_cuda_layer_weights {
+    kore_cuda_qmat wq, wk, wv, wo;    /* as kore_cuda_set_attn_weights (Layer::wq.., kore.cpp:1246-1249) */
+    const float *bq, *bk, *bv;        /* host, or all NULL */
+    const float *attn_norm;           /* host [n_embd] (Layer::attn_norm) */
+    const float *ffn_norm;            /* host [n_embd] (Layer::ffn_norm) */
+    kore_cuda_qmat w_gate, w_up;      /* [n_ff x n_embd], Q4_K or Q6_K */
+    kore_cuda_qmat w_down;            /* [n_embd x n_ff], Q4_K or Q6_K */
+} kore_cuda_layer_weights;
+
+typedef struct kore_cuda_model {
+    int n_ff;                         /* hp.n_ff, a multiple of 256 */
+    int n_vocab;                      /* rows of tok_embd and out_w */
+    float rms_eps;                    /* hp.rms_eps */
+    kore_cuda_qmat tok_embd;          /* [n_vocab x n_embd]: type F32, F16, BF16, Q4_K or Q6_K */
+    const float *out_norm;            /* host [n_embd] (Engine::out_norm) */
+    kore_cuda_qmat out_w;             /* [n_vocab x n_embd], Q4_K or Q6_K (Engine::out_w) */
+    const kore_cuda_layer_weights *layers;   /* [n_layer] */
+} kore_cuda_model;
+
+/* Uploads the whole model (every layer's attention projections as
+ * kore_cuda_set_attn_weights does, norms, feed-forward weights, embedding
+ * table, output norm and matrix), replacing any earlier upload. Synchronous. */
+int kore_cuda_set_model(kore_cuda_ctx *ctx, const kore_cuda_model *model);
+
+/* One decode step of sequence `seq`: `token` at `pos` through every layer
+ * (appending its k/v at pos in every layer's cache), then the greedy next
+ * token into *next_token; logits [n_vocab] (host, optional) receives the
+ * logits as kore's e.logits. Returns KORE_CUDA_ERANGE for a token outside the
+ * vocabulary or a bad position, as forward() returns false (kore.cpp:1400).
+ * On a context with shard_count > 1 every rank makes the same calls. */
+int kore_cuda_decode_step(kore_cuda_ctx *ctx, int seq, int token, int pos, int *next_token, float *logits);
+/* The same, stream-ordered: token and next_token are device ints (they may be
+ * the same int, so that steps chain on the device), logits an optional device
+ * [n_vocab]. A token outside the vocabulary is reported by kore_cuda_sync. */
+int kore_cuda_decode_step_dev(kore_cuda_ctx *ctx, int seq, const int *token, int pos, int *next_token,
+                              float *logits);
+
+/*
  * KV-sequence split over GPUs (cfg.shard_count > 1). Each context holds the
  * positions of every page j with j % shard_count == shard_rank; a decode step
  * then runs in two parts:

@@ -61,6 +61,35 @@ class _QMat(ctypes.Structure):
     _fields_ = [("type", ctypes.c_int), ("rows", ctypes.c_int), ("cols", ctypes.c_int), ("data", ctypes.c_void_p)]
 
 
+class _LayerW(ctypes.Structure):
+    """kore_cuda_layer_weights."""
+    _fields_ = ([(n, _QMat) for n in ("wq", "wk", "wv", "wo")]
+                + [(n, ctypes.c_void_p) for n in ("bq", "bk", "bv", "attn_norm", "ffn_norm")]
+                + [(n, _QMat) for n in ("w_gate", "w_up", "w_down")])
+
+
+class _Model(ctypes.Structure):
+    """kore_cuda_model."""
+    _fields_ = [("n_ff", ctypes.c_int), ("n_vocab", ctypes.c_int), ("rms_eps", ctypes.c_float),
+                ("tok_embd", _QMat), ("out_norm", ctypes.c_void_p), ("out_w", _QMat),
+                ("layers", ctypes.POINTER(_LayerW))]
+
+
+def _addr(a) -> int | None:
+    """Host address of an array argument: an int is taken as an address, None as NULL."""
+    if a is None or isinstance(a, int):
+        return a
+    if not (isinstance(a, np.ndarray) and a.flags.c_contiguous):
+        raise ValueError("expected a C-contiguous numpy array or an address")
+    return a.ctypes.data
+
+
+def _qm(m) -> _QMat:
+    """kore_cuda_qmat of a matrix with .type, .rows, .cols and .data (array) or .addr (address)."""
+    addr = getattr(m, "addr", None)
+    return _QMat(m.type, m.rows, m.cols, addr if addr is not None else _addr(m.data))
+
+
 _lib = None
 _vp = ctypes.c_void_p
 _ip = ctypes.POINTER(ctypes.c_int)
@@ -114,6 +143,9 @@ def load_library(path: str = LIB):
     L.kore_cuda_qmatvec.argtypes = [_vp, _i, _i, _vp, _vp]
     for n in ("kore_cuda_attn_block_decode", "kore_cuda_attn_block_decode_dev"):
         getattr(L, n).argtypes = [_vp, _i, _i, _i, _vp, _vp]
+    L.kore_cuda_set_model.argtypes = [_vp, ctypes.POINTER(_Model)]
+    L.kore_cuda_decode_step.argtypes = [_vp, _i, _i, _i, _ip, _vp]
+    L.kore_cuda_decode_step_dev.argtypes = [_vp, _i, _vp, _i, _vp, _vp]
     L.kore_cuda_sync.argtypes = [_vp]
     L.kore_cuda_set_wait_limit.argtypes = [_vp, ctypes.c_ulonglong]
     L.kore_cuda_stream.argtypes = [_vp]
@@ -340,6 +372,42 @@ class KoreCuda:
         o = np.empty(self.H * self.d, np.float32)
         self._ck(self._L.kore_cuda_attn_block_decode(self._h, seq, layer, pos, xb.ctypes.data, o.ctypes.data))
         return o
+
+    # ---------------------------------------------------------------- the whole decode step
+    def set_model(self, n_ff: int, n_vocab: int, rms_eps: float, tok_embd, out_norm, out_w, layers) -> None:
+        """Uploads the whole model. tok_embd/out_w and the layers' matrices have
+        .type/.rows/.cols and .data (uint8 array) or .addr; out_norm and each
+        layer's attn_norm, ffn_norm, bq, bk, bv are float32 arrays or addresses.
+        layers: one dict per layer with keys wq wk wv wo w_gate w_up w_down
+        bq bk bv attn_norm ffn_norm."""
+        arr = (_LayerW * len(layers))()
+        keep = []
+        for i, Lw in enumerate(layers):
+            vals = {k: Lw[k] for k in Lw}
+            keep.append(vals)
+            arr[i] = _LayerW(*[_qm(vals[n]) for n in ("wq", "wk", "wv", "wo")],
+                             *[_addr(vals.get(n)) for n in ("bq", "bk", "bv", "attn_norm", "ffn_norm")],
+                             *[_qm(vals[n]) for n in ("w_gate", "w_up", "w_down")])
+        m = _Model(n_ff, n_vocab, rms_eps, _qm(tok_embd), _addr(out_norm), _qm(out_w), arr)
+        self._ck(self._L.kore_cuda_set_model(self._h, ctypes.byref(m)))
+        self.n_vocab = n_vocab
+        del keep
+
+    def decode_step(self, seq: int, token: int, pos: int, want_logits: bool = False):
+        """kore's forward() + greedy sample_token for one token: (next token, logits or None)."""
+        nxt = ctypes.c_int(-1)
+        logits = np.empty(self.n_vocab, np.float32) if want_logits else None
+        self._ck(self._L.kore_cuda_decode_step(self._h, seq, token, pos, ctypes.byref(nxt),
+                                               logits.ctypes.data if want_logits else None))
+        return nxt.value, logits
+
+    def decode_step_dev(self, seq: int, token, pos: int, next_token, logits=None) -> None:
+        """Stream-ordered step: token / next_token are int32 CUDA tensors of one element."""
+        for t in (token, next_token):
+            if not (t.is_cuda and str(t.dtype) == "torch.int32"):
+                raise ValueError("token and next_token must be int32 CUDA tensors")
+        self._ck(self._L.kore_cuda_decode_step_dev(self._h, seq, token.data_ptr(), pos, next_token.data_ptr(),
+                                                   _dptr(logits) if logits is not None else None))
 
     def attn_block_decode_dev(self, seq: int, layer: int, pos: int, xb, o) -> None:
         self._ck(self._L.kore_cuda_attn_block_decode_dev(self._h, seq, layer, pos, _dptr(xb), _dptr(o)))

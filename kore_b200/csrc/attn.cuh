@@ -121,29 +121,67 @@ size_t prefill_tile_bytes(int head_dim);
 size_t prefill_slot_bytes(int head_dim);
 // One weight matrix of a product launch: rows of GGUF blocks (type 12 = Q4_K,
 // 14 = Q6_K), out[r] = row r . x (+ bias[r]). The buffer holding w extends
-// at least 8 bytes past the matrix.
+// at least 16 bytes past the matrix.
 struct QSeg {
     const uint8_t *w;
     const float *bias;
     float *out;
     int type, rows;
 };
+// What a product launch does with its input vector and its rows (proj.cu).
+enum QInMode : int {
+    QIN_QUANT = 0,     // quantise x to Q8_K
+    QIN_RMSNORM = 1,   // quantise RMSNorm(x) * norm_w (kore.cpp:1367-1372)
+};
+enum QOutMode : int {
+    QOUT_STORE = 0,      // out[r] = row (+ bias[r])
+    QOUT_RESIDUAL = 1,   // out[r] = resid[r] + row (the residual add; out may be resid)
+    QOUT_SWIGLU = 2,     // paired segments: seg[0].out[i] = SwiGLU(seg 0 row i, seg 1 row i)
+    QOUT_ARGMAX = 3,     // out[r] = row, and *argmax = max over rows of the (value, first row) key
+};
 // Products of up to three matrices with one fp32 vector x [cols] (16-byte
-// aligned), quantised to Q8_K inside the kernel (proj.cu); `grid` CTAs, one
-// per SM. Every segment's row count is even; slot_bytes is what
-// qmatvec_smem_bytes gives for cols and the largest block size of the
-// segments; err receives DEV_WAIT_FULL_TIMEOUT if a weight copy never lands.
+// aligned), quantised to Q8_K inside the kernel; `grid` CTAs, one per SM.
+// stages and row_slot are what qmatvec_config gives for cols and the largest
+// block size of the segments; err receives DEV_WAIT_FULL_TIMEOUT if a weight
+// copy never lands.
 struct QMatvecParams {
     QSeg seg[3];
     int n_seg;
     int cols;
-    int slot_bytes;
+    int pair_segments;            // 1: group i = row i of seg 0 and of seg 1 (equal row counts)
+    int in_mode, out_mode;
+    int stages, row_slot;
     const float *x;
+    const float *norm_w;          // QIN_RMSNORM weight [cols], 16-byte aligned
+    float eps;                    // QIN_RMSNORM epsilon
+    const float *resid;           // QOUT_RESIDUAL
+    unsigned long long *argmax;   // QOUT_ARGMAX: orderable (value << 32 | ~row) key, zeroed beforehand
     int *err;
+    unsigned long long exp_tab[32];   // QOUT_SWIGLU: bits(2^(i/32)) - (i << 47), from the host's exp2
 };
 constexpr size_t kQmatvecMaxSmem = 227 * 1024;
-size_t qmatvec_smem_bytes(int cols, int max_block_bytes, int *slot_bytes);
+// Ring stages per warp and bytes per row slot for a launch over cols with
+// the given largest block size; returns the dynamic shared memory it needs.
+size_t qmatvec_config(int cols, int max_block_bytes, int *stages, int *row_slot);
 cudaError_t launch_qmatvec(const QMatvecParams &p, int grid, cudaStream_t s);
+
+// The embedding row of a token (step.cu): x = get_row(table, token)
+// (kore.cpp:384-407) for table type 0 (F32), 1 (F16), 30 (BF16), 12 (Q4_K)
+// or 14 (Q6_K); the token comes from token_dev when set, else `token`; also
+// clears *key (the argmax key the step's logits product fills).
+struct EmbedParams {
+    const uint8_t *table;
+    size_t row_bytes;
+    int type, n_vocab, n_embd, token;
+    const int *token_dev;
+    float *x;
+    unsigned long long *key;
+    int *err;
+};
+cudaError_t launch_embed(const EmbedParams &p, cudaStream_t s);
+// token = the index in an argmax key (-1 for an empty key), after the
+// preceding kernel (programmatic dependency).
+cudaError_t launch_token(const unsigned long long *key, int *token, cudaStream_t s);
 
 // Work list of a prefill chunk (pos0, n) over H heads on num_sms SMs: one
 // item per (query head, 128-row query tile), the heaviest ones possibly split

@@ -93,6 +93,31 @@ struct kore_cuda_ctx {
     };
     std::vector<LayerProj> proj;
     float *blk = nullptr;       // q [H*D] | k [kvd] | v [kvd] | att [H*D]
+    // the rest of the model for the device-resident decode step
+    // (kore_cuda_set_model): embedding table, per-layer norms and
+    // feed-forward weights, output norm and logits matrix, step buffers
+    struct LayerFfn {
+        float *norms = nullptr;   // attn_norm [E] | ffn_norm [E]
+        uint8_t *w = nullptr;     // w_gate | w_up | w_down, 256-byte aligned, padded
+        int type[3] = {0, 0, 0};
+        size_t off[3] = {0, 0, 0};
+    };
+    struct Model {
+        bool ready = false;
+        int n_ff = 0, n_vocab = 0, tok_type = 0, out_type = 0;
+        float eps = 0.f;
+        size_t tok_row_bytes = 0;
+        uint8_t *tok = nullptr;
+        float *out_norm = nullptr;
+        uint8_t *out_w = nullptr;
+        std::vector<LayerFfn> layers;
+        float *x = nullptr;       // residual stream [E]
+        float *act = nullptr;     // SwiGLU output [n_ff]
+        float *logits = nullptr;  // [n_vocab]
+        unsigned long long *key = nullptr;   // argmax key of the logits
+        int *token = nullptr;     // [2]: a step's input and output token (device-side steps)
+        unsigned long long exp_tab[32] = {};
+    } model;
     std::string msg;
 };
 
@@ -314,6 +339,7 @@ const char *device_error_text(int e) {
         case DEV_WAIT_EMPTY_TIMEOUT: return "bounded wait for a free stage expired";
         case DEV_BAD_PAGE: return "page table entry outside the pool";
         case DEV_PEER_TIMEOUT: return "a peer GPU's partial did not arrive within the wait limit";
+        case DEV_BAD_TOKEN: return "token id outside the vocabulary";
         default: return "unknown device error code";
     }
 }
@@ -526,6 +552,18 @@ void kore_cuda_destroy(kore_cuda_ctx *c) {
             cudaFree(lp.w);
             cudaFree(lp.bias);
         }
+        for (auto &lf : c->model.layers) {
+            cudaFree(lf.norms);
+            cudaFree(lf.w);
+        }
+        cudaFree(c->model.tok);
+        cudaFree(c->model.out_norm);
+        cudaFree(c->model.out_w);
+        cudaFree(c->model.x);
+        cudaFree(c->model.act);
+        cudaFree(c->model.logits);
+        cudaFree(c->model.key);
+        cudaFree(c->model.token);
         cudaFree(c->blk);
         cudaFree(c->kv);
         cudaFree(c->pt_d);
@@ -986,11 +1024,25 @@ static const kore_cuda_ctx::LayerProj *layer_proj(kore_cuda_ctx *c, int layer) {
     return lp.w && lp.type[0] && lp.type[3] ? &lp : nullptr;
 }
 
+// One product launch whose segments, vectors and modes are filled in: the
+// ring shape for its widest block, the error word, then the launch.
+static int launch_products(kore_cuda_ctx *c, QMatvecParams &mp) {
+    int bb = 0;
+    for (int i = 0; i < mp.n_seg; ++i) bb = std::max(bb, mp.seg[i].type == KORE_CUDA_Q4_K ? 144 : 210);
+    if (qmatvec_config(mp.cols, bb, &mp.stages, &mp.row_slot) > kQmatvecMaxSmem)
+        return fail(c, KORE_CUDA_EINVAL, "a product over %d columns does not fit in shared memory", mp.cols);
+    mp.err = c->err_d;
+    CK(launch_qmatvec(mp, c->num_sms, c->stream));
+    return KORE_CUDA_OK;
+}
+
 // One product launch over up to three of a layer's matrices (which: 0 wq,
-// 1 wk, 2 wv, 3 wo) with the fp32 vector x (quantised in the kernel),
-// results to outs.
+// 1 wk, 2 wv, 3 wo) with the fp32 vector x (quantised in the kernel, after
+// an RMSNorm with norm_w when given), results to outs (plus the biases of
+// wq/wk/wv), or added to `resid` when given.
 static int launch_proj(kore_cuda_ctx *c, const kore_cuda_ctx::LayerProj &lp, const int *which, int n, const float *x,
-                       float *const *outs) {
+                       float *const *outs, const float *norm_w = nullptr, float eps = 0.f,
+                       const float *resid = nullptr) {
     const int E = c->H * c->D;
     QMatvecParams mp;
     memset(&mp, 0, sizeof mp);
@@ -1006,12 +1058,12 @@ static int launch_proj(kore_cuda_ctx *c, const kore_cuda_ctx::LayerProj &lp, con
         g.bias = (w < 3 && lp.has_bias) ? lp.bias + (w == 0 ? 0 : (w == 1 ? E : E + c->kvd)) : nullptr;
     }
     mp.n_seg = n;
-    int bb = 0;
-    for (int i = 0; i < n; ++i) bb = std::max(bb, mp.seg[i].type == KORE_CUDA_Q4_K ? 144 : 210);
-    qmatvec_smem_bytes(E, bb, &mp.slot_bytes);
-    mp.err = c->err_d;
-    CK(launch_qmatvec(mp, c->num_sms, c->stream));
-    return KORE_CUDA_OK;
+    mp.in_mode = norm_w ? QIN_RMSNORM : QIN_QUANT;
+    mp.norm_w = norm_w;
+    mp.eps = eps;
+    mp.out_mode = resid ? QOUT_RESIDUAL : QOUT_STORE;
+    mp.resid = resid;
+    return launch_products(c, mp);
 }
 
 int kore_cuda_set_attn_weights(kore_cuda_ctx *c, int layer, const kore_cuda_qmat *wq, const kore_cuda_qmat *wk,
@@ -1029,7 +1081,7 @@ int kore_cuda_set_attn_weights(kore_cuda_ctx *c, int layer, const kore_cuda_qmat
     const char *names[4] = {"wq", "wk", "wv", "wo"};
     for (int i = 0; i < 4; ++i)
         if (int rc = check_qmat(c, m[i], names[i], rows[i], E)) return rc;
-    if (qmatvec_smem_bytes(E, 210, nullptr) > kQmatvecMaxSmem)
+    if (qmatvec_config(E, 210, nullptr, nullptr) > kQmatvecMaxSmem)
         return fail(c, KORE_CUDA_EINVAL, "n_embd = %d: a product launch's staging exceeds shared memory", E);
     DeviceGuard dg(c->cfg.device);
     if (c->proj.empty()) c->proj.resize((size_t)c->cfg.n_layer);
@@ -1124,6 +1176,237 @@ int kore_cuda_attn_block_decode(kore_cuda_ctx *c, int seq, int layer, int pos, c
     if (int rc = kore_cuda_attn_block_decode_dev(c, seq, layer, pos, c->dev_stage, dout)) return rc;
     if (int rc = finish(c, (size_t)E * sizeof(float))) return rc;
     memcpy(o, reinterpret_cast<const char *>(c->host_err) + kErrPad, (size_t)E * sizeof(float));
+    return KORE_CUDA_OK;
+}
+
+// ---------------------------------------------------------------- the whole decode step on the device
+
+static size_t row_bytes_of(int type, int cols) {
+    switch (type) {
+        case KORE_CUDA_F32: return (size_t)cols * 4;
+        case KORE_CUDA_F16:
+        case KORE_CUDA_BF16: return (size_t)cols * 2;
+        case KORE_CUDA_Q4_K: return (size_t)(cols / 256) * 144;
+        case KORE_CUDA_Q6_K: return (size_t)(cols / 256) * 210;
+        default: return 0;
+    }
+}
+
+int kore_cuda_set_model(kore_cuda_ctx *c, const kore_cuda_model *m) {
+    if (!c) return KORE_CUDA_EINVAL;
+    if (!m || !m->layers || !m->out_norm || !m->tok_embd.data || !m->out_w.data)
+        return fail(c, KORE_CUDA_EINVAL, "null model, layers, out_norm, tok_embd or out_w");
+    const int E = c->H * c->D, FF = m->n_ff, V = m->n_vocab;
+    if (E % 256 || FF <= 0 || FF % 256 || V <= 0)
+        return fail(c, KORE_CUDA_EINVAL, "n_embd %d and n_ff %d must be multiples of 256 (kore.cpp:1283), n_vocab %d > 0",
+                    E, FF, V);
+    if (!(m->rms_eps >= 0.f)) return fail(c, KORE_CUDA_EINVAL, "rms_eps must be non-negative");
+    const kore_cuda_qmat &te = m->tok_embd;
+    if (row_bytes_of(te.type, E) == 0 || ((te.type == KORE_CUDA_Q4_K || te.type == KORE_CUDA_Q6_K) && E % 256))
+        return fail(c, KORE_CUDA_EINVAL, "tok_embd: type %d is none of F32, F16, BF16, Q4_K, Q6_K", te.type);
+    if (te.rows != V || te.cols != E)
+        return fail(c, KORE_CUDA_EINVAL, "tok_embd is %d x %d, expected %d x %d", te.rows, te.cols, V, E);
+    if (int rc = check_qmat(c, &m->out_w, "output", V, E)) return rc;
+    for (int l = 0; l < c->cfg.n_layer; ++l) {
+        const kore_cuda_layer_weights &L = m->layers[l];
+        if (!L.attn_norm || !L.ffn_norm) return fail(c, KORE_CUDA_EINVAL, "layer %d: null norm weights", l);
+        if (int rc = check_qmat(c, &L.w_gate, "ffn_gate", FF, E)) return rc;
+        if (int rc = check_qmat(c, &L.w_up, "ffn_up", FF, E)) return rc;
+        if (int rc = check_qmat(c, &L.w_down, "ffn_down", E, FF)) return rc;
+    }
+    if (qmatvec_config(FF, 210, nullptr, nullptr) > kQmatvecMaxSmem)
+        return fail(c, KORE_CUDA_EINVAL, "n_ff = %d: the down product's input does not fit in shared memory", FF);
+    DeviceGuard dg(c->cfg.device);
+    CK(cudaStreamSynchronize(c->stream));
+    auto &M = c->model;
+    M.ready = false;
+    for (int l = 0; l < c->cfg.n_layer; ++l) {
+        const kore_cuda_layer_weights &L = m->layers[l];
+        if (int rc = kore_cuda_set_attn_weights(c, l, &L.wq, &L.wk, &L.wv, &L.wo, L.bq, L.bk, L.bv)) return rc;
+    }
+    M.layers.resize((size_t)c->cfg.n_layer);
+    for (int l = 0; l < c->cfg.n_layer; ++l) {
+        const kore_cuda_layer_weights &L = m->layers[l];
+        auto &lf = M.layers[(size_t)l];
+        cudaFree(lf.norms);
+        cudaFree(lf.w);
+        lf = kore_cuda_ctx::LayerFfn();
+        CK(cudaMalloc(&lf.norms, (size_t)2 * E * sizeof(float)));
+        CK(cudaMemcpy(lf.norms, L.attn_norm, (size_t)E * sizeof(float), cudaMemcpyHostToDevice));
+        CK(cudaMemcpy(lf.norms + E, L.ffn_norm, (size_t)E * sizeof(float), cudaMemcpyHostToDevice));
+        const kore_cuda_qmat *w[3] = {&L.w_gate, &L.w_up, &L.w_down};
+        size_t total = 0;
+        for (int i = 0; i < 3; ++i) {
+            lf.off[i] = total;
+            total += align256(qmat_bytes(w[i]->type, w[i]->rows, w[i]->cols) + 16);   // the product kernel reads past a row's end
+        }
+        CK(cudaMalloc(&lf.w, total));
+        for (int i = 0; i < 3; ++i) {
+            CK(cudaMemcpy(lf.w + lf.off[i], w[i]->data, qmat_bytes(w[i]->type, w[i]->rows, w[i]->cols),
+                          cudaMemcpyHostToDevice));
+            lf.type[i] = w[i]->type;
+        }
+    }
+    cudaFree(M.tok);
+    cudaFree(M.out_norm);
+    cudaFree(M.out_w);
+    M.tok = nullptr;
+    M.out_norm = nullptr;
+    M.out_w = nullptr;
+    M.tok_row_bytes = row_bytes_of(te.type, E);
+    CK(cudaMalloc(&M.tok, (size_t)V * M.tok_row_bytes));
+    CK(cudaMemcpy(M.tok, te.data, (size_t)V * M.tok_row_bytes, cudaMemcpyHostToDevice));
+    CK(cudaMalloc(&M.out_norm, (size_t)E * sizeof(float)));
+    CK(cudaMemcpy(M.out_norm, m->out_norm, (size_t)E * sizeof(float), cudaMemcpyHostToDevice));
+    const size_t ob = qmat_bytes(m->out_w.type, V, E);
+    CK(cudaMalloc(&M.out_w, align256(ob + 16)));
+    CK(cudaMemcpy(M.out_w, m->out_w.data, ob, cudaMemcpyHostToDevice));
+    if (M.n_vocab != V || !M.logits) {
+        cudaFree(M.logits);
+        M.logits = nullptr;
+        CK(cudaMalloc(&M.logits, (size_t)V * sizeof(float)));
+    }
+    if (M.n_ff != FF || !M.act) {
+        cudaFree(M.act);
+        M.act = nullptr;
+        CK(cudaMalloc(&M.act, (size_t)FF * sizeof(float)));
+    }
+    if (!M.x) CK(cudaMalloc(&M.x, (size_t)E * sizeof(float)));
+    if (!M.key) CK(cudaMalloc(&M.key, sizeof(unsigned long long)));
+    if (!M.token) CK(cudaMalloc(&M.token, 2 * sizeof(int)));
+    // 2^(i/32) as the C library's exp2 rounds it, exponent bits taken out:
+    // the table of the expf that kore's SwiGLU calls (proj.cu, kore_expf)
+    for (int i = 0; i < 32; ++i) {
+        const double t = std::exp2((double)i / 32.0);
+        unsigned long long b;
+        memcpy(&b, &t, sizeof b);
+        M.exp_tab[i] = b - ((unsigned long long)i << 47);
+    }
+    M.n_ff = FF;
+    M.n_vocab = V;
+    M.eps = m->rms_eps;
+    M.tok_type = te.type;
+    M.out_type = m->out_w.type;
+    M.ready = true;
+    return KORE_CUDA_OK;
+}
+
+// kore's forward() for one token (kore.cpp:1397-1480) and the greedy choice
+// of sample_token (kore.cpp:1601-1603), every step on the device:
+//   embedding row of the token                        embed_kernel
+//   per layer: RMSNorm + Q8_K + Wq/Wk/Wv + biases      qmatvec (RMSNORM in, STORE out)
+//              RoPE, append, attention                 attn_decode (+ split merge or peer exchange)
+//              Q8_K(att) + Wo + residual add           qmatvec (QUANT in, RESIDUAL out)
+//              RMSNorm + Q8_K + gate/up + SwiGLU        qmatvec (RMSNORM in, paired, SWIGLU out)
+//              Q8_K + down + residual add              qmatvec (QUANT in, RESIDUAL out)
+//   RMSNorm + Q8_K + output matrix + argmax            qmatvec (RMSNORM in, ARGMAX out)
+//   the token from the argmax key                     token_kernel
+static int run_step(kore_cuda_ctx *c, int seq, int token, const int *token_dev, int pos, int *next_dev,
+                    float *logits_dev) {
+    auto &M = c->model;
+    const int E = c->H * c->D, FF = M.n_ff, NL = c->cfg.n_layer;
+    float *q = c->blk, *k = q + E, *v = k + c->kvd, *att = v + c->kvd;
+    EmbedParams ep;
+    memset(&ep, 0, sizeof ep);
+    ep.table = M.tok;
+    ep.row_bytes = M.tok_row_bytes;
+    ep.type = M.tok_type;
+    ep.n_vocab = M.n_vocab;
+    ep.n_embd = E;
+    ep.token = token;
+    ep.token_dev = token_dev;
+    ep.x = M.x;
+    ep.key = M.key;
+    ep.err = c->err_d;
+    CK(launch_embed(ep, c->stream));
+    c->last_kv_layer = -1;
+    for (int l = 0; l < NL; ++l) {
+        const kore_cuda_ctx::LayerProj &lp = c->proj[(size_t)l];
+        const kore_cuda_ctx::LayerFfn &lf = M.layers[(size_t)l];
+        const int qkv[3] = {0, 1, 2};
+        float *const outs[3] = {q, k, v};
+        if (int rc = launch_proj(c, lp, qkv, 3, M.x, outs, lf.norms, M.eps)) return rc;
+        if (int rc = c->NS > 1 ? kore_cuda_attn_decode_sharded_dev(c, seq, l, pos, q, k, v, att)
+                               : kore_cuda_attn_decode_dev(c, seq, l, pos, q, k, v, att))
+            return rc;
+        const int wo = 3;
+        float *const xo[1] = {M.x};
+        if (int rc = launch_proj(c, lp, &wo, 1, att, xo, nullptr, 0.f, M.x)) return rc;
+        QMatvecParams mp;
+        memset(&mp, 0, sizeof mp);
+        mp.n_seg = 2;
+        mp.cols = E;
+        mp.seg[0] = QSeg{lf.w + lf.off[0], nullptr, M.act, lf.type[0], FF};
+        mp.seg[1] = QSeg{lf.w + lf.off[1], nullptr, M.act, lf.type[1], FF};
+        mp.pair_segments = 1;
+        mp.in_mode = QIN_RMSNORM;
+        mp.x = M.x;
+        mp.norm_w = lf.norms + E;
+        mp.eps = M.eps;
+        mp.out_mode = QOUT_SWIGLU;
+        memcpy(mp.exp_tab, M.exp_tab, sizeof mp.exp_tab);
+        if (int rc = launch_products(c, mp)) return rc;
+        memset(&mp, 0, sizeof mp);
+        mp.n_seg = 1;
+        mp.cols = FF;
+        mp.seg[0] = QSeg{lf.w + lf.off[2], nullptr, M.x, lf.type[2], E};
+        mp.in_mode = QIN_QUANT;
+        mp.x = M.act;
+        mp.out_mode = QOUT_RESIDUAL;
+        mp.resid = M.x;
+        if (int rc = launch_products(c, mp)) return rc;
+    }
+    QMatvecParams mp;
+    memset(&mp, 0, sizeof mp);
+    mp.n_seg = 1;
+    mp.cols = E;
+    mp.seg[0] = QSeg{M.out_w, nullptr, logits_dev ? logits_dev : M.logits, M.out_type, M.n_vocab};
+    mp.in_mode = QIN_RMSNORM;
+    mp.x = M.x;
+    mp.norm_w = M.out_norm;
+    mp.eps = M.eps;
+    mp.out_mode = QOUT_ARGMAX;
+    mp.argmax = M.key;
+    if (int rc = launch_products(c, mp)) return rc;
+    CK(launch_token(M.key, next_dev, c->stream));
+    return KORE_CUDA_OK;
+}
+
+static int check_step(kore_cuda_ctx *c, int seq, int pos) {
+    if (!c->model.ready || c->proj.size() != (size_t)c->cfg.n_layer)
+        return fail(c, KORE_CUDA_ESTATE, "no model on the device (kore_cuda_set_model)");
+    for (int l = 0; l < c->cfg.n_layer; ++l) {
+        if (int rc = check_range(c, seq, l, pos, 1)) return rc;
+        if (!layer_proj(c, l)) return fail(c, KORE_CUDA_ESTATE, "layer %d has no attention weights", l);
+    }
+    if (c->NS > 1 && !c->peers_open)
+        return fail(c, KORE_CUDA_ESTATE, "a KV-split context needs kore_cuda_peer_open before a decode step");
+    return KORE_CUDA_OK;
+}
+
+int kore_cuda_decode_step_dev(kore_cuda_ctx *c, int seq, const int *token, int pos, int *next_token, float *logits) {
+    if (!c) return KORE_CUDA_EINVAL;
+    if (!token || !next_token) return fail(c, KORE_CUDA_EINVAL, "null token or next_token");
+    if (int rc = check_step(c, seq, pos)) return rc;
+    DeviceGuard dg(c->cfg.device);
+    return run_step(c, seq, 0, token, pos, next_token, logits);
+}
+
+int kore_cuda_decode_step(kore_cuda_ctx *c, int seq, int token, int pos, int *next_token, float *logits) {
+    if (!c) return KORE_CUDA_EINVAL;
+    if (!next_token) return fail(c, KORE_CUDA_EINVAL, "null next_token");
+    if (int rc = check_step(c, seq, pos)) return rc;
+    if (token < 0 || token >= c->model.n_vocab)   // forward() returns false (kore.cpp:1400)
+        return fail(c, KORE_CUDA_ERANGE, "token %d outside the vocabulary of %d", token, c->model.n_vocab);
+    DeviceGuard dg(c->cfg.device);
+    // the next token lands right behind the error word and both come back in one copy
+    int *dnext = reinterpret_cast<int *>(reinterpret_cast<char *>(c->err_d) + kErrPad);
+    if (int rc = run_step(c, seq, token, nullptr, pos, dnext, nullptr)) return rc;
+    if (logits)
+        CK(cudaMemcpyAsync(logits, c->model.logits, (size_t)c->model.n_vocab * sizeof(float), cudaMemcpyDeviceToHost,
+                           c->stream));
+    if (int rc = finish(c, sizeof(int))) return rc;
+    memcpy(next_token, reinterpret_cast<const char *>(c->host_err) + kErrPad, sizeof(int));
     return KORE_CUDA_OK;
 }
 

@@ -14,6 +14,7 @@ enum DeviceError : int {
     DEV_WAIT_EMPTY_TIMEOUT = 2,   // producer waited too long for a free stage
     DEV_BAD_PAGE = 3,             // page table entry outside the pool
     DEV_PEER_TIMEOUT = 4,         // a peer GPU's partial did not arrive in time
+    DEV_BAD_TOKEN = 5,            // token id outside the vocabulary (device-side token)
 };
 
 __device__ __forceinline__ void raise_error(int *err, int code) {
@@ -63,7 +64,7 @@ __device__ __forceinline__ uint64_t global_ns() {
 }
 
 // Bounded wait on a phase of an mbarrier: gives up after `limit_ns` of wall
-// time (checked every 64 polls) or kWaitPolls polls, whichever comes first,
+// time (checked every 8 polls) or kWaitPolls polls, whichever comes first,
 // records `code` in the error word and returns false. A healthy pipeline waits
 // microseconds; the bound only turns a lost copy into an error the host sees.
 // kWaitNs is the default limit (a context can set another one for the decode

@@ -1,9 +1,19 @@
-// proj.cu — kore's quantised projections on the GPU: Q8_K quantisation of an
-// activation vector and the Q4_K / Q6_K matrix-vector products, sm_100a.
+// proj.cu — kore's quantised products on the GPU: Q8_K quantisation of an
+// activation vector and the Q4_K / Q6_K matrix-vector products, sm_100a,
+// with the steps of kore's decode step that sit around them fused in.
 //
-// Replaces mv() + quant() of kore's decode step (kore.cpp:1388-1394) for the
-// attention block's projections (kore.cpp:1418-1423 q/k/v + bias, :1456-1457
-// Wo): out[r] = row r of W . quantize_q8_K(x) (+ bias[r]).
+// Replaces mv() + quant() of kore's decode step (kore.cpp:1388-1394):
+// out[r] = row r of W . quantize_q8_K(x), for the attention projections
+// (kore.cpp:1418-1423 q/k/v + bias, :1456-1457 Wo), the feed-forward
+// products (:1462-1471 gate, up, down) and the logits (:1475-1478). What kore
+// does next to a product is folded into the same kernel:
+//   input   the plain vector, or RMSNorm(x) (kore.cpp:1367-1372) computed from
+//           the residual stream by every block itself;
+//   output  the row plus its bias; the residual add x[r] += row (kore.cpp:1457,
+//           :1471); the SwiGLU of a gate row and the same up row,
+//           g / (1 + exp(-g)) * u (kore.cpp:1465-1468); or the logits with
+//           their greedy argmax (sample_token at temperature 0,
+//           kore.cpp:1601-1603: the first index of the largest value).
 //
 // Exactness. The Q8_K quantisation (kore.cpp:422-447) is reproduced bit for
 // bit: the first value of largest magnitude, an IEEE division for the scale,
@@ -15,25 +25,42 @@
 // exact integers; each lane then accumulates d * lane in block order with one
 // fused multiply-add, and the lanes are summed in kore's horizontal-sum order.
 // Every float operation below is an explicit round-to-nearest intrinsic, so
-// the compiler fuses nothing that kore does not. Results equal kore's bit for
-// bit; tests/test_proj_gpu.py checks it against the oracle, which is pinned
-// to the reference's compiled kernels.
+// the compiler fuses nothing that kore does not.
+//  * RMSNorm: kore sums the squares in double, sequentially. Every square of
+//    a float is exact in double, so a tree sum differs from kore's sum by at
+//    most (n + log2 n) units of 2^-53 of the sum; the block checks that the
+//    mean, rounded to float as kore rounds it, cannot change within that
+//    bound, and otherwise (about one vector in 10^5) sums sequentially in
+//    kore's order. Then (float) mean + eps, sqrtf, 1/x, (x * scale) * w.
+//  * SwiGLU: kore's std::exp is the C library's expf, which on glibc (2.27
+//    and later) is the table-driven method of ARM's optimized-routines
+//    (Szabolcs Nagy): x * 32/ln2 = k + r with the reduced argument formed by
+//    one fused multiply-add, 2^(k/32) from a 32-entry table of 2^(i/32), a
+//    cubic in r, all in double, one rounding to float at the end. It is
+//    restated here (kore_expf) with the table built on the host from exp2;
+//    the restatement was checked against the host's expf on all 2^32 floats
+//    (identical except NaN payloads).
+// Results equal kore's bit for bit; the tests check them against the oracle,
+// which is pinned to the reference's compiled code.
 //
 // Data path. Weights stay in HBM in the GGUF block layout (Q4_K: 144-byte
-// blocks, Q6_K: 210-byte blocks, row-major). One CTA of 16 warps per SM; a
-// warp takes 2 consecutive rows at a time, 16 lanes per row: lane (h, k)
-// computes AVX2 lane k over half h of the row's blocks, and the second
-// half's lane continues the first half's fused multiply-add chains (one
-// shuffle), so the float order stays kore's. The 2 rows are one contiguous
-// byte range: one bulk copy per warp stages them in shared memory, issued
-// before the kernel waits for its predecessor (programmatic dependent
-// launch), since weights do not depend on it. Meanwhile every CTA quantises
-// the fp32 input vector to Q8_K in shared memory itself (14 KB at 7B: cheaper
-// than a kernel boundary), transposed so that each lane reads its 8 words of
-// a block with two 16-byte loads on distinct banks. The per-block loop is
-// compact, which keeps this short-lived kernel out of instruction-cache
-// misses. Memory-bound: algorithmic bytes = the weight bytes (+ the small
-// vector), read once.
+// blocks, Q6_K: 210-byte blocks, row-major). One CTA of 16 warps per SM. A
+// warp takes a group of 2 rows at a time (2 consecutive rows, or row i of
+// two matrices for the SwiGLU pair), 16 lanes per row: lane (h, k) computes
+// AVX2 lane k over half h of the blocks of each chunk, and the second half's
+// lane continues the first half's fused multiply-add chains (one shuffle
+// each way per chunk), so the float order stays kore's. Rows are streamed in
+// chunks of kChunk blocks through a ring of stages per warp (one bulk copy
+// per row and chunk, mbarrier completion), refilled as soon as a chunk has
+// been consumed and running on into the warp's next group, so long rows (the
+// 18944-wide down projection) fit and every warp keeps several copies in
+// flight. The first stages are issued before the kernel waits for its
+// predecessor (programmatic dependent launch): weights do not depend on it.
+// Meanwhile every CTA builds the Q8_K input in shared memory itself (14 KB
+// at 7B, 28 KB for the feed-forward width: cheaper than a kernel boundary),
+// transposed so that each lane reads its 8 words of a block with two 16-byte
+// loads on distinct banks. Memory-bound: algorithmic bytes = the weight
+// bytes (+ the small vectors), read once.
 
 #include "attn.cuh"
 #include "common.cuh"
@@ -44,6 +71,8 @@ namespace kore {
 namespace {
 
 constexpr int kWarps = 16;   // warps per CTA (one CTA per SM)
+constexpr int kChunk = 8;    // blocks of a row per ring stage
+constexpr unsigned FULLW = 0xffffffffu;
 
 __device__ __forceinline__ float half_bits(uint32_t h) { return __half2float(__ushort_as_half((unsigned short)h)); }
 
@@ -58,14 +87,11 @@ __device__ __forceinline__ float half_bits(uint32_t h) { return __half2float(__u
 constexpr int kQ8Row = 48;
 constexpr int kQ8Block = 8 * kQ8Row;   // 384 bytes
 
-// One warp quantises one 256-value block of x (lane l: values 8l..8l+7) into
-// a staged Q8_K block: transposed qs, its scale, its 16 group sums and the 8
-// sums of adjacent group pairs.
-__device__ __forceinline__ void q8k_block(const float *__restrict__ x, int lane, uint8_t *qt, float *xd,
-                                          int16_t *bsums, int16_t *pairs) {
-    const float4 *src = reinterpret_cast<const float4 *>(x + 8 * lane);
-    const float4 a = src[0], b = src[1];
-    const float v[8] = {a.x, a.y, a.z, a.w, b.x, b.y, b.z, b.w};
+// One warp quantises one 256-value block (lane l holds values 8l..8l+7 in v)
+// into a staged Q8_K block: transposed qs, its scale, its 16 group sums and
+// the 8 sums of adjacent group pairs.
+__device__ __forceinline__ void q8k_block(const float (&v)[8], int lane, uint8_t *qt, float *xd, int16_t *bsums,
+                                          int16_t *pairs) {
     // the first value of largest magnitude (strict >, in index order)
     float amax = 0.f, maxv = 0.f;
     int idx = 1 << 30;
@@ -80,9 +106,9 @@ __device__ __forceinline__ void q8k_block(const float *__restrict__ x, int lane,
     }
 #pragma unroll
     for (int o = 16; o > 0; o >>= 1) {
-        const float am = __shfl_xor_sync(0xffffffffu, amax, o);
-        const float mv = __shfl_xor_sync(0xffffffffu, maxv, o);
-        const int ix = __shfl_xor_sync(0xffffffffu, idx, o);
+        const float am = __shfl_xor_sync(FULLW, amax, o);
+        const float mv = __shfl_xor_sync(FULLW, maxv, o);
+        const int ix = __shfl_xor_sync(FULLW, idx, o);
         if (am > amax || (am == amax && ix < idx)) {
             amax = am;
             maxv = mv;
@@ -106,7 +132,7 @@ __device__ __forceinline__ void q8k_block(const float *__restrict__ x, int lane,
     int s = 0;
 #pragma unroll
     for (int i = 0; i < 8; ++i) s += q[i];
-    s += __shfl_xor_sync(0xffffffffu, s, 1);
+    s += __shfl_xor_sync(FULLW, s, 1);
     const uint32_t w0 = (uint32_t)(q[0] & 0xFF) | (uint32_t)(q[1] & 0xFF) << 8 | (uint32_t)(q[2] & 0xFF) << 16 |
                         (uint32_t)(q[3] & 0xFF) << 24;
     const uint32_t w1 = (uint32_t)(q[4] & 0xFF) | (uint32_t)(q[5] & 0xFF) << 8 | (uint32_t)(q[6] & 0xFF) << 16 |
@@ -117,9 +143,60 @@ __device__ __forceinline__ void q8k_block(const float *__restrict__ x, int lane,
     *reinterpret_cast<uint32_t *>(qt + (wb & 7) * kQ8Row + 4 * (wb >> 3)) = w1;
     if ((lane & 1) == 0) bsums[lane >> 1] = (int16_t)s;
     // bsums[2j] + bsums[2j+1] as int16 (the Q4_K minimum terms' operands, kore.cpp:563-567)
-    const int s2 = (int)(int16_t)s + (int)(int16_t)__shfl_xor_sync(0xffffffffu, s, 2);
+    const int s2 = (int)(int16_t)s + (int)(int16_t)__shfl_xor_sync(FULLW, s, 2);
     if ((lane & 3) == 0) pairs[lane >> 2] = (int16_t)s2;
     if (lane == 0) *xd = d;
+}
+
+// ---------------------------------------------------------------- RMSNorm and SwiGLU
+
+// The float kore's rmsnorm (kore.cpp:1369-1370) makes of its sequential
+// double sum of squares, (float)(ss / n), from a sum S of the same squares
+// in another order: exact when the float cannot change within the two sums'
+// error bounds ((n + log2 n) * 2^-53 of the sum, with margin), else NaN
+// (the caller then sums sequentially).
+__device__ __forceinline__ float mean_square_float(double S, int n) {
+    const double v = __ddiv_rn(S, (double)n);
+    const float f = __double2float_rn(v);
+    const double lo = ((double)f + (double)nextafterf(f, -INFINITY)) * 0.5;
+    const double hi = ((double)f + (double)nextafterf(f, INFINITY)) * 0.5;
+    const double m = v * (double)(n + 64) * 0x1p-52;
+    return (v - m > lo && v + m < hi) ? f : __int_as_float(0x7fffffff);
+}
+
+// kore's std::exp(float): the table-driven expf of the C library (see the
+// header), restated with each double operation rounded as the library does.
+// tab[i] = bits(2^(i/32)) - (i << 47).
+__device__ __forceinline__ float kore_expf(float x, const unsigned long long *tab) {
+    if (x != x) return x + x;
+    if (x > 0x1.62e42ep6f) return __int_as_float(0x7f800000);   // overflow: +inf
+    if (x < -0x1.9fe368p6f) return 0.0f;                          // below half the smallest subnormal
+    constexpr double kShift = 0x1.8p52, kInvLn2N = 0x1.71547652b82fep+0 * 32;
+    constexpr double kC0 = 0x1.c6af84b912394p-5 / 32768, kC1 = 0x1.ebfce50fac4f3p-3 / 1024,
+                     kC2 = 0x1.62e42ff0c52d6p-1 / 32;
+    const double xd = (double)x;
+    double kd = __dadd_rn(__dmul_rn(kInvLn2N, xd), kShift);
+    const unsigned long long ki = (unsigned long long)__double_as_longlong(kd);
+    kd = __dsub_rn(kd, kShift);
+    const double r = __fma_rn(kInvLn2N, xd, -kd);
+    const double s = __longlong_as_double((long long)(tab[ki & 31] + (ki << 47)));
+    const double r2 = __dmul_rn(r, r);
+    const double y = __dadd_rn(__dmul_rn(__dadd_rn(__dmul_rn(kC0, r), kC1), r2), __dadd_rn(__dmul_rn(kC2, r), 1.0));
+    return __double2float_rn(__dmul_rn(y, s));
+}
+
+// kore.cpp:1465-1468: g / (1 + exp(-g)) * u.
+__device__ __forceinline__ float kore_swiglu(float g, float u, const unsigned long long *tab) {
+    return __fmul_rn(__fdiv_rn(g, __fadd_rn(1.0f, kore_expf(-g, tab))), u);
+}
+
+// Orderable key of (value, row) for the greedy argmax: larger value first,
+// then smaller row (std::max_element keeps the first of equal maxima; -0
+// equals +0 there, so it is keyed as +0).
+__device__ __forceinline__ unsigned long long argmax_key(float v, int row) {
+    const uint32_t u = __float_as_uint(v == 0.f ? 0.f : v);
+    const uint32_t o = (u & 0x80000000u) ? ~u : (u | 0x80000000u);
+    return ((unsigned long long)o << 32) | (unsigned long long)(0xFFFFFFFFu - (uint32_t)row);
 }
 
 // ---------------------------------------------------------------- products
@@ -251,141 +328,258 @@ __device__ __forceinline__ void take(const Terms &t, float &acc, float &accm) {
 
 // The row's dot product from its lanes' chains: kore's horizontal sums over
 // the row's 8 lanes, ((a0+a4)+(a2+a6)) + ((a1+a5)+(a3+a7)), plus for Q4_K
-// ((m0+m2)+(m1+m3)), for Q6_K the offset sum. Valid on lane 0 of the group.
-template <int TYPE>
-__device__ __forceinline__ float row_sum(float acc, float accm) {
-    const float t4 = __fadd_rn(acc, __shfl_down_sync(0xffffffffu, acc, 4, 8));
-    const float t2 = __fadd_rn(t4, __shfl_down_sync(0xffffffffu, t4, 2, 8));
-    const float a = __fadd_rn(t2, __shfl_down_sync(0xffffffffu, t2, 1, 8));
-    float m = accm;
-    if (TYPE == 12) {
-        const float m2 = __fadd_rn(accm, __shfl_down_sync(0xffffffffu, accm, 2, 8));
-        m = __fadd_rn(m2, __shfl_down_sync(0xffffffffu, m2, 1, 8));
-    }
-    return __fadd_rn(a, m);
+// ((m0+m2)+(m1+m3)), for Q6_K the offset sum. Every lane of the warp runs
+// the same shuffles (the two rows of a group may differ in type); valid on
+// lane 0 of each 8-lane group.
+__device__ __forceinline__ float row_sum(float acc, float accm, bool q4) {
+    const float t4 = __fadd_rn(acc, __shfl_down_sync(FULLW, acc, 4, 8));
+    const float t2 = __fadd_rn(t4, __shfl_down_sync(FULLW, t4, 2, 8));
+    const float a = __fadd_rn(t2, __shfl_down_sync(FULLW, t2, 1, 8));
+    const float m2 = __fadd_rn(accm, __shfl_down_sync(FULLW, accm, 2, 8));
+    const float m4 = __fadd_rn(m2, __shfl_down_sync(FULLW, m2, 1, 8));
+    return __fadd_rn(a, q4 ? m4 : accm);
 }
 
-// The row's product from its staged bytes. Lane (h2, k) computes the terms
-// of AVX2 lane k for blocks [h2*hb, min(nb, (h2+1)*hb)); the h2 = 0 lane
-// runs the chains over its blocks, the h2 = 1 lane parks its terms in
-// `park` and, given the h2 = 0 lane's chains, continues them over its
-// blocks: block order, as kore's loop. The result is on the h2 = 1, k = 0
-// lane.
-template <int TYPE>
-__device__ __forceinline__ float row_dot(const uint8_t *row, int nb, int h2, int k, const uint8_t *q8t,
-                                         const float *xds, const int16_t *bss, const int16_t *prs, uint4 *park) {
-    constexpr int BB = TYPE == 12 ? 144 : 210;
-    const int hb = (nb + 1) >> 1, b0 = h2 * hb, b1 = min(nb, b0 + hb);
-    float acc = 0.f, accm = 0.f;
-#pragma unroll 2
-    for (int b = b0; b < b1; ++b) {
-        uint32_t w[kW];
-        lds_block<TYPE>(row + (size_t)b * BB, k, w);
-        const Terms t =
-            block_terms<TYPE>(w, k, q8t + (size_t)b * kQ8Block, bss + (size_t)b * 16, prs + (size_t)b * 8, xds[b]);
-        if (h2 == 0) take(t, acc, accm);
-        else park[b - b0] = make_uint4((uint32_t)t.s, (uint32_t)t.e, __float_as_uint(t.d), __float_as_uint(t.dm));
+// Row r (0 or 1) of group gg: its segment and row within it, or -1.
+__device__ __forceinline__ int group_row(const QMatvecParams &p, int gg, int rr, int total_rows, int &row) {
+    if (p.pair_segments) {
+        row = gg;
+        return rr;
     }
-    const float acc0 = __shfl_xor_sync(0xffffffffu, acc, 8), accm0 = __shfl_xor_sync(0xffffffffu, accm, 8);
-    if (h2 == 1) {
-        acc = acc0;
-        accm = accm0;
-        for (int b = b0; b < b1; ++b) {
-            const uint4 v = park[b - b0];
-            take(Terms{(int)v.x, (int)v.y, __uint_as_float(v.z), __uint_as_float(v.w)}, acc, accm);
-        }
-    }
-    return row_sum<TYPE>(acc, accm);
-}
-
-// Global row g of the launch (the segments' rows one after another): its
-// segment and row within it.
-__device__ __forceinline__ int find_seg(const QMatvecParams &p, int g, int &row) {
+    int g = 2 * gg + rr;
+    if (g >= total_rows) return -1;
     int s = 0;
-    row = g;
-    while (s + 1 < p.n_seg && row >= p.seg[s].rows) {
-        row -= p.seg[s].rows;
+    while (s + 1 < p.n_seg && g >= p.seg[s].rows) {
+        g -= p.seg[s].rows;
         ++s;
     }
+    row = g;
     return s;
 }
 
-// One CTA per SM, kWarps warps. A warp takes groups of 2 consecutive rows
-// (16 lanes per row: lane (h2, k) computes AVX2 lane k over one half of the
-// blocks), group warp*grid + cta first and then every TW-th. Every segment's
-// row count is even, so a group lies in one segment and its rows are one
-// contiguous byte range, which one bulk copy brings into the warp's
-// shared-memory slot. The first group's copy is issued before the dependency
-// wait (weights do not depend on the preceding kernel).
 __global__ void __launch_bounds__(32 * kWarps) qmatvec_kernel(const __grid_constant__ QMatvecParams p) {
     extern __shared__ __align__(16) uint8_t smem[];
-    const int nb = p.cols / 256, hb = (nb + 1) >> 1;
-    uint64_t *bars = reinterpret_cast<uint64_t *>(smem);                   // [kWarps]
-    uint8_t *q8t = smem + 8 * kWarps;                                     // [nb][kQ8Block]
-    float *xds = reinterpret_cast<float *>(q8t + (size_t)nb * kQ8Block);  // [nb]
-    int16_t *bss = reinterpret_cast<int16_t *>(xds + ((nb + 3) & ~3));    // [nb][16]
-    int16_t *prs = bss + (size_t)nb * 16;                                 // [nb][8]
-    uint4 *parks = reinterpret_cast<uint4 *>(prs + (size_t)nb * 8);       // [kWarps][2 rows][8 lanes][hb]
-    uint8_t *slots = reinterpret_cast<uint8_t *>(parks + (size_t)kWarps * 16 * hb);   // [kWarps][p.slot_bytes]
+    const int nb = p.cols / 256, S = p.stages;
+    const int n_chunks = (nb + kChunk - 1) / kChunk;
+    uint64_t *bars = reinterpret_cast<uint64_t *>(smem);                                  // [kWarps][S]
+    unsigned long long *wkeys = reinterpret_cast<unsigned long long *>(bars + kWarps * S);   // [kWarps]
+    double *red = reinterpret_cast<double *>(wkeys + kWarps);                            // [kWarps]
+    float *s_scale = reinterpret_cast<float *>(red + kWarps);                             // [4]
+    uint8_t *q8t = reinterpret_cast<uint8_t *>(s_scale + 4);                              // [nb][kQ8Block]
+    float *xds = reinterpret_cast<float *>(q8t + (size_t)nb * kQ8Block);                  // [nb]
+    int16_t *bss = reinterpret_cast<int16_t *>(xds + ((nb + 3) & ~3));                    // [nb][16]
+    int16_t *prs = bss + (size_t)nb * 16;                                                 // [nb][8]
+    uint8_t *slots = reinterpret_cast<uint8_t *>(prs + (size_t)nb * 8);                   // [kWarps][S][2][row_slot]
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int rr = lane >> 4, h2 = (lane >> 3) & 1, k = lane & 7;
-    uint64_t *bar = bars + warp;
-    uint8_t *slot = slots + (size_t)warp * p.slot_bytes;
-    uint4 *park = parks + ((size_t)warp * 16 + rr * 8 + k) * hb;
-    int R = 0;
-    for (int s = 0; s < p.n_seg; ++s) R += p.seg[s].rows;
-    const int n_groups = R / 2, TW = (int)gridDim.x * kWarps;
+    uint64_t *mybar = bars + warp * S;
+    const size_t stage_bytes = (size_t)2 * p.row_slot;
+    uint8_t *myslots = slots + (size_t)warp * S * stage_bytes;
+
+    int total_rows = 0;
+    for (int s = 0; s < p.n_seg; ++s) total_rows += p.seg[s].rows;
+    const int n_groups = p.pair_segments ? p.seg[0].rows : (total_rows + 1) / 2;
+    const int TW = (int)gridDim.x * kWarps;
     // groups warp-major over the grid: consecutive groups (and so each
     // matrix's rows, e.g. a Q6_K Wv among Q4_K ones) spread over all SMs
     const int gg0 = warp * (int)gridDim.x + (int)blockIdx.x;
+    const int my_groups = gg0 < n_groups ? (n_groups - gg0 + TW - 1) / TW : 0;
+    const int n_items = my_groups * n_chunks;   // (group, chunk) in order
     if (lane == 0) {
-        mbar_init(bar, 1);
+        for (int s = 0; s < S; ++s) mbar_init(mybar + s, 1);
         mbar_fence_init();
     }
     __syncwarp();
-    // the bulk copy of group gg; returns the offset of its first row in the slot
-    auto issue = [&](int gg) -> uint32_t {
-        int row0;
-        const QSeg &sg = p.seg[find_seg(p, 2 * gg, row0)];
-        const size_t rb = (size_t)nb * (sg.type == 12 ? 144 : 210);
-        const uintptr_t a = reinterpret_cast<uintptr_t>(sg.w + (size_t)row0 * rb);
-        const uintptr_t a0 = a & ~uintptr_t(15);
-        const uint32_t bytes = (uint32_t)(((a - a0) + 2 * rb + 15) & ~size_t(15));
-        if (lane == 0) {
-            fence_proxy_async_smem();
-            mbar_arrive_expect_tx(bar, bytes);
-            bulk_g2s_plain(slot, reinterpret_cast<const void *>(a0), bytes, bar);
-        }
+
+    // byte range of (segment, row)'s blocks [c0, c0 + cb) and its 16-aligned start
+    auto row_src = [&](int sg, int row, int c0, int cb, uintptr_t &a0, uint32_t &bytes) -> uint32_t {
+        const QSeg &q = p.seg[sg];
+        const size_t BB = q.type == 12 ? 144 : 210;
+        const uintptr_t a = reinterpret_cast<uintptr_t>(q.w) + ((size_t)row * nb + c0) * BB;
+        a0 = a & ~uintptr_t(15);
+        bytes = (uint32_t)(((a - a0) + cb * BB + 15) & ~uintptr_t(15));
         return (uint32_t)(a - a0);
     };
-    uint32_t delta = 0, phase = 0;
-    if (gg0 < n_groups) delta = issue(gg0);
+    // bulk copies of item it (both rows of its group, one chunk), lane 0 only
+    auto issue = [&](int it) {
+        const int gg = gg0 + (it / n_chunks) * TW, c = it % n_chunks;
+        const int c0 = c * kChunk, cb = min(kChunk, nb - c0);
+        const int s = it % S;
+        uintptr_t a0[2];
+        uint32_t by[2] = {0, 0};
+        for (int r = 0; r < 2; ++r) {
+            int row;
+            const int sg = group_row(p, gg, r, total_rows, row);
+            if (sg >= 0) row_src(sg, row, c0, cb, a0[r], by[r]);
+        }
+        fence_proxy_async_smem();
+        mbar_arrive_expect_tx(mybar + s, by[0] + by[1]);
+        for (int r = 0; r < 2; ++r)
+            if (by[r])
+                bulk_g2s_plain(myslots + s * stage_bytes + (size_t)r * p.row_slot, reinterpret_cast<const void *>(a0[r]),
+                               by[r], mybar + s);
+    };
+    if (lane == 0)
+        for (int it = 0; it < S && it < n_items; ++it) issue(it);
     grid_dep_wait();
-    // x quantised to Q8_K in shared memory, one warp per block
-    for (int b = warp; b < nb; b += kWarps)
-        q8k_block(p.x + (size_t)b * 256, lane, q8t + (size_t)b * kQ8Block, xds + b, bss + (size_t)b * 16,
-                  prs + (size_t)b * 8);
+
+    // ------------------------------------------------------------ the Q8_K input
+    float scale = 1.f;
+    if (p.in_mode == QIN_RMSNORM) {
+        // kore.cpp:1367-1372: the sum of squares, a tree here, checked and if
+        // need be redone in kore's order
+        double ss = 0.0;
+        for (int i = threadIdx.x; i < p.cols; i += 32 * kWarps) {
+            const double xi = (double)p.x[i];
+            ss = __dadd_rn(ss, __dmul_rn(xi, xi));
+        }
+#pragma unroll
+        for (int o = 16; o > 0; o >>= 1) ss = __dadd_rn(ss, __shfl_xor_sync(FULLW, ss, o));
+        if (lane == 0) red[warp] = ss;
+        __syncthreads();
+        if (threadIdx.x == 0) {
+            double S2 = 0.0;
+            for (int w = 0; w < kWarps; ++w) S2 = __dadd_rn(S2, red[w]);
+            float f = mean_square_float(S2, p.cols);
+            if (f != f && S2 == S2) {
+                double seq = 0.0;
+                for (int i = 0; i < p.cols; ++i) {
+                    const double xi = (double)p.x[i];
+                    seq = __dadd_rn(seq, __dmul_rn(xi, xi));
+                }
+                f = __double2float_rn(__ddiv_rn(seq, (double)p.cols));
+            } else if (S2 != S2) {
+                f = __double2float_rn(__ddiv_rn(S2, (double)p.cols));
+            }
+            s_scale[0] = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(f, p.eps)));
+        }
+        __syncthreads();
+        scale = s_scale[0];
+    }
+    for (int b = warp; b < nb; b += kWarps) {
+        const float4 *src = reinterpret_cast<const float4 *>(p.x + (size_t)b * 256 + 8 * lane);
+        const float4 a = src[0], c = src[1];
+        float v[8] = {a.x, a.y, a.z, a.w, c.x, c.y, c.z, c.w};
+        if (p.in_mode == QIN_RMSNORM) {
+            const float4 *ws = reinterpret_cast<const float4 *>(p.norm_w + (size_t)b * 256 + 8 * lane);
+            const float4 wa = ws[0], wc = ws[1];
+            const float w[8] = {wa.x, wa.y, wa.z, wa.w, wc.x, wc.y, wc.z, wc.w};
+#pragma unroll
+            for (int i = 0; i < 8; ++i) v[i] = __fmul_rn(__fmul_rn(v[i], scale), w[i]);
+        }
+        q8k_block(v, lane, q8t + (size_t)b * kQ8Block, xds + b, bss + (size_t)b * 16, prs + (size_t)b * 8);
+    }
     __syncthreads();
     grid_dep_launch();
-    for (int gg = gg0; gg < n_groups; gg += TW) {
-        if (gg != gg0) {
-            __syncwarp();   // every lane is done with the slot
-            delta = issue(gg);
-        }
-        const bool ok = mbar_wait(bar, phase, p.err, DEV_WAIT_FULL_TIMEOUT);
-        if (!__all_sync(0xffffffffu, ok)) {
-            mbar_drain(bar, phase);   // the copy may still land: not into a block that has exited
+
+    // ------------------------------------------------------------ the rows
+    unsigned long long best = 0;   // argmax key of this lane's rows (QOUT_ARGMAX)
+    float acc = 0.f, accm = 0.f;
+    for (int it = 0; it < n_items; ++it) {
+        const int s = it % S;
+        if (!__all_sync(FULLW, mbar_wait(mybar + s, (it / S) & 1, p.err, DEV_WAIT_FULL_TIMEOUT))) {
+            // gave up (recorded): let the copies still in flight land first
+            for (int t = it; t < n_items && t < it + S; ++t) mbar_drain(mybar + t % S, (t / S) & 1);
             break;
         }
-        phase ^= 1;
+        const int gg = gg0 + (it / n_chunks) * TW, c = it % n_chunks;
+        const int c0 = c * kChunk, cb = min(kChunk, nb - c0), half0 = (cb + 1) >> 1;
         int row;
-        const QSeg &sg = p.seg[find_seg(p, 2 * gg + rr, row)];
-        float r;
-        if (sg.type == 12) r = row_dot<12>(slot + delta + (size_t)rr * nb * 144, nb, h2, k, q8t, xds, bss, prs, park);
-        else r = row_dot<14>(slot + delta + (size_t)rr * nb * 210, nb, h2, k, q8t, xds, bss, prs, park);
-        if (h2 == 1 && k == 0) {
-            if (sg.bias) r = __fadd_rn(r, sg.bias[row]);
-            sg.out[row] = r;
+        const int sg = group_row(p, gg, rr, total_rows, row);
+        const bool valid = sg >= 0;
+        const bool q4 = valid && p.seg[sg].type == 12;
+        uintptr_t a0;
+        uint32_t by;
+        const uint32_t delta = valid ? row_src(sg, row, c0, cb, a0, by) : 0;
+        const uint8_t *blk0 = myslots + s * stage_bytes + (size_t)rr * p.row_slot + delta;
+        const int BB = q4 ? 144 : 210;
+        if (c == 0) {
+            acc = 0.f;
+            accm = 0.f;
+        }
+        // this half's blocks of the chunk: the first half feeds the chains,
+        // the second half parks its terms until the chains reach it
+        const int j0 = h2 ? half0 : 0, j1 = h2 ? cb : half0;
+        Terms park[(kChunk + 1) / 2];
+#pragma unroll
+        for (int jj = 0; jj < (kChunk + 1) / 2; ++jj) {
+            const int j = j0 + jj;
+            if (valid && j < j1) {
+                const int b = c0 + j;
+                uint32_t w[kW];
+                Terms t;
+                if (q4) {
+                    lds_block<12>(blk0 + (size_t)j * BB, k, w);
+                    t = block_terms<12>(w, k, q8t + (size_t)b * kQ8Block, bss + (size_t)b * 16, prs + (size_t)b * 8,
+                                        xds[b]);
+                } else {
+                    lds_block<14>(blk0 + (size_t)j * BB, k, w);
+                    t = block_terms<14>(w, k, q8t + (size_t)b * kQ8Block, bss + (size_t)b * 16, prs + (size_t)b * 8,
+                                        xds[b]);
+                }
+                if (h2 == 0) take(t, acc, accm);
+                else park[jj] = t;
+            }
+        }
+        {
+            const float a1 = __shfl_xor_sync(FULLW, acc, 8), m1 = __shfl_xor_sync(FULLW, accm, 8);
+            if (h2) {
+                acc = a1;
+                accm = m1;
+#pragma unroll
+                for (int jj = 0; jj < (kChunk + 1) / 2; ++jj)
+                    if (valid && j0 + jj < j1) take(park[jj], acc, accm);
+            }
+            const float a2 = __shfl_xor_sync(FULLW, acc, 8), m2 = __shfl_xor_sync(FULLW, accm, 8);
+            if (!h2) {
+                acc = a2;
+                accm = m2;
+            }
+        }
+        __syncwarp();   // every lane is done with the stage
+        if (lane == 0 && it + S < n_items) issue(it + S);
+        if (c != n_chunks - 1) continue;
+
+        // ------------------------------------------------ the group's results
+        const float r = row_sum(acc, accm, q4);
+        const float other = __shfl_xor_sync(FULLW, r, 16);   // the other row's result (lane 0 <-> 16)
+        if (h2 == 0 && k == 0 && valid) {
+            const QSeg &q = p.seg[sg];
+            switch (p.out_mode) {
+                case QOUT_STORE:
+                    q.out[row] = q.bias ? __fadd_rn(r, q.bias[row]) : r;
+                    break;
+                case QOUT_RESIDUAL:
+                    q.out[row] = __fadd_rn(p.resid[row], r);
+                    break;
+                case QOUT_SWIGLU:   // lane 0 holds the gate row, lane 16 the up row
+                    if (rr == 0) q.out[row] = kore_swiglu(r, other, p.exp_tab);
+                    break;
+                case QOUT_ARGMAX: {
+                    q.out[row] = r;
+                    int g = row;
+                    for (int s2 = 0; s2 < sg; ++s2) g += p.seg[s2].rows;
+                    const unsigned long long key = argmax_key(r, g);
+                    best = key > best ? key : best;
+                    break;
+                }
+                default:
+                    break;
+            }
+        }
+    }
+    if (p.out_mode == QOUT_ARGMAX) {
+#pragma unroll
+        for (int o = 16; o > 0; o >>= 1) {
+            const unsigned long long x = __shfl_xor_sync(FULLW, best, o);
+            best = x > best ? x : best;
+        }
+        if (lane == 0) wkeys[warp] = best;
+        __syncthreads();
+        if (threadIdx.x == 0) {
+            unsigned long long m = 0;
+            for (int w = 0; w < kWarps; ++w) m = wkeys[w] > m ? wkeys[w] : m;
+            if (m) atomicMax(p.argmax, m);
         }
     }
 }
@@ -397,30 +591,43 @@ cudaLaunchAttribute pdl_attr() {
     return a;
 }
 
+size_t fixed_smem(int nb, int stages) {
+    return (size_t)8 * kWarps * stages + 8 * kWarps + 8 * kWarps + 16 + (size_t)nb * kQ8Block +
+           (size_t)((nb + 3) & ~3) * 4 + (size_t)nb * 32 + (size_t)nb * 16;
+}
+
 }  // namespace
 
-size_t qmatvec_smem_bytes(int cols, int max_block_bytes, int *slot_bytes) {
-    const int nb = cols / 256, hb = (nb + 1) / 2;
-    // a group's copy starts up to 15 bytes before its first row and ends up to
-    // 15 bytes after its last; the Q6_K word reads reach 6 bytes past a block
-    const size_t slot = ((size_t)2 * nb * max_block_bytes + 32 + 15) & ~size_t(15);
-    if (slot_bytes) *slot_bytes = (int)slot;
-    return (size_t)8 * kWarps + (size_t)nb * kQ8Block + (size_t)((nb + 3) & ~3) * 4 + (size_t)nb * 48 +
-           (size_t)kWarps * 16 * hb * 16 + (size_t)kWarps * slot;
+size_t qmatvec_config(int cols, int max_block_bytes, int *stages, int *row_slot) {
+    const int nb = cols / 256;
+    // a row's chunk copy starts up to 15 bytes before its first block and ends
+    // up to 15 bytes after its last; the Q6_K word reads reach 6 bytes past a block
+    const int slot = (int)(((size_t)kChunk * max_block_bytes + 32 + 15) & ~size_t(15));
+    int S = 4;
+    while (S > 1 && fixed_smem(nb, S) + (size_t)kWarps * S * 2 * slot > kQmatvecMaxSmem) --S;
+    if (stages) *stages = S;
+    if (row_slot) *row_slot = slot;
+    return fixed_smem(nb, S) + (size_t)kWarps * S * 2 * slot;
 }
 
 cudaError_t launch_qmatvec(const QMatvecParams &p, int grid, cudaStream_t s) {
     if (p.n_seg <= 0 || p.n_seg > 3 || p.cols <= 0 || p.cols % 256 || !p.x || grid <= 0) return cudaErrorInvalidValue;
+    if ((reinterpret_cast<uintptr_t>(p.x) & 15) || (p.in_mode == QIN_RMSNORM && (!p.norm_w ||
+        (reinterpret_cast<uintptr_t>(p.norm_w) & 15))))
+        return cudaErrorInvalidValue;
     int bb = 0;
     for (int i = 0; i < p.n_seg; ++i) {
-        if ((p.seg[i].type != 12 && p.seg[i].type != 14) || p.seg[i].rows < 0 || p.seg[i].rows % 2 || !p.seg[i].w ||
-            !p.seg[i].out)
+        if ((p.seg[i].type != 12 && p.seg[i].type != 14) || p.seg[i].rows < 0 || !p.seg[i].w || !p.seg[i].out)
             return cudaErrorInvalidValue;
         bb = max(bb, p.seg[i].type == 12 ? 144 : 210);
     }
-    int slot = 0;
-    const size_t smem = qmatvec_smem_bytes(p.cols, bb, &slot);
-    if (slot != p.slot_bytes || smem > kQmatvecMaxSmem) return cudaErrorInvalidValue;
+    if (p.pair_segments && (p.n_seg != 2 || p.seg[0].rows != p.seg[1].rows)) return cudaErrorInvalidValue;
+    if (p.out_mode == QOUT_SWIGLU && !p.pair_segments) return cudaErrorInvalidValue;
+    if (p.out_mode == QOUT_RESIDUAL && !p.resid) return cudaErrorInvalidValue;
+    if (p.out_mode == QOUT_ARGMAX && !p.argmax) return cudaErrorInvalidValue;
+    int stages = 0, slot = 0;
+    const size_t smem = qmatvec_config(p.cols, bb, &stages, &slot);
+    if (slot != p.row_slot || stages != p.stages || smem > kQmatvecMaxSmem) return cudaErrorInvalidValue;
     if (cudaError_t e = ensure_smem_limit(reinterpret_cast<const void *>(qmatvec_kernel), (int)kQmatvecMaxSmem))
         return e;
     cudaLaunchConfig_t cfg = {};

@@ -55,6 +55,8 @@ using fn_set_weights = int (*)(kore_cuda_ctx *, int, const kore_cuda_qmat *, con
                                const kore_cuda_qmat *, const kore_cuda_qmat *, const float *, const float *,
                                const float *);
 using fn_block = int (*)(kore_cuda_ctx *, int, int, int, const float *, float *);
+using fn_set_model = int (*)(kore_cuda_ctx *, const kore_cuda_model *);
+using fn_step = int (*)(kore_cuda_ctx *, int, int, int, int *, float *);
 
 struct Harness {
     Model m;
@@ -71,7 +73,10 @@ struct Harness {
     fn_prefill prefill = nullptr;
     fn_set_weights set_weights = nullptr;
     fn_block block = nullptr;
+    fn_set_model set_model = nullptr;
+    fn_step step = nullptr;
     bool weights_up = false;
+    bool model_up = false;
 };
 
 uint16_t f32_to_f16(float f) {   // round to nearest, normal and subnormal range
@@ -251,6 +256,43 @@ bool upload_attn_weights(Harness &hx) {
     return true;
 }
 
+// Uploads the whole model (kore's own tensors) for the device-resident step.
+bool upload_model(Harness &hx) {
+    if (hx.model_up) return true;
+    const Engine &e = hx.e;
+    std::vector<kore_cuda_layer_weights> lw(e.hp.n_layer);
+    for (uint32_t l = 0; l < e.hp.n_layer; l++) {
+        const Layer &L = e.layers[l];
+        kore_cuda_layer_weights &w = lw[l];
+        w.wq = as_qmat(*L.wq);
+        w.wk = as_qmat(*L.wk);
+        w.wv = as_qmat(*L.wv);
+        w.wo = as_qmat(*L.wo);
+        w.bq = L.bq;
+        w.bk = L.bk;
+        w.bv = L.bv;
+        w.attn_norm = L.attn_norm;
+        w.ffn_norm = L.ffn_norm;
+        w.w_gate = as_qmat(*L.w_gate);
+        w.w_up = as_qmat(*L.w_up);
+        w.w_down = as_qmat(*L.w_down);
+    }
+    kore_cuda_model m;
+    m.n_ff = (int)e.hp.n_ff;
+    m.n_vocab = e.n_vocab;
+    m.rms_eps = e.hp.rms_eps;
+    m.tok_embd = as_qmat(*e.tok_embd);
+    m.out_norm = e.out_norm;
+    m.out_w = as_qmat(*e.out_w);
+    m.layers = lw.data();
+    if (hx.set_model(hx.ctx, &m) != KORE_CUDA_OK) {
+        hx.err = hx.last_error(hx.ctx);
+        return false;
+    }
+    hx.model_up = true;
+    return true;
+}
+
 bool cuda_forward_batch(Harness &hx, const int *toks, int nb, int pos0, bool want_logits) {
     Engine &e = hx.e;
     const Hparams &h = e.hp;
@@ -418,6 +460,8 @@ int keng_attach_cuda(void *h, const char *lib_path, int device) {
     hx.prefill = (fn_prefill)dlsym(hx.lib, "kore_cuda_attn_prefill");
     hx.set_weights = (fn_set_weights)dlsym(hx.lib, "kore_cuda_set_attn_weights");
     hx.block = (fn_block)dlsym(hx.lib, "kore_cuda_attn_block_decode");
+    hx.set_model = (fn_set_model)dlsym(hx.lib, "kore_cuda_set_model");
+    hx.step = (fn_step)dlsym(hx.lib, "kore_cuda_decode_step");
     if (!cfg_default || !create || !hx.destroy || !hx.last_error || !hx.seq_reset || !hx.decode || !hx.prefill) {
         hx.err = "missing symbol in the CUDA library";
         return -1;
@@ -499,6 +543,63 @@ int keng_generate_cuda_block(void *h, const int *prompt, int n_prompt, int n_gen
         hx, prompt, n_prompt, n_gen, ids, nullptr,
         [&](const int *t, int nb, int p0, bool last) { return cuda_forward_batch(hx, t, nb, p0, last); },
         [&](int tok, int pos) { return cuda_forward_block(hx, tok, pos, true); });
+}
+
+// Greedy IDs with kore's prompt flow (its chunks through the CUDA path, as in
+// keng_generate_cuda) and then every decode step wholly on the GPU
+// (kore_cuda_decode_step: embedding, every layer, logits and argmax on the
+// device; the host passes the token id and gets the next one back).
+int keng_generate_cuda_step(void *h, const int *prompt, int n_prompt, int n_gen, int *ids) {
+    Harness &hx = *(Harness *)h;
+    hx.err.clear();
+    if (!hx.ctx || !hx.set_model || !hx.step) {
+        hx.err = "no CUDA context with the decode-step entry points (keng_attach_cuda)";
+        return -1;
+    }
+    if (!upload_model(hx)) return -1;
+    Engine &e = hx.e;
+    if (n_prompt <= 0 || n_prompt + n_gen > e.ctx) {
+        hx.err = "prompt + generation exceed the context";
+        return -1;
+    }
+    if (hx.seq_reset(hx.ctx, 0) != KORE_CUDA_OK) {
+        hx.err = hx.last_error(hx.ctx);
+        return -1;
+    }
+    for (int p0 = 0; p0 < n_prompt; p0 += e.bsz) {
+        const int nb = std::min(e.bsz, n_prompt - p0);
+        if (!cuda_forward_batch(hx, prompt + p0, nb, p0, p0 + nb == n_prompt)) {
+            if (hx.err.empty()) hx.err = "prefill failed";
+            return -1;
+        }
+    }
+    ids[0] = argmax_margin(e.logits, nullptr);
+    for (int i = 1; i < n_gen; i++) {
+        if (hx.step(hx.ctx, 0, ids[i - 1], n_prompt + i - 1, &ids[i], nullptr) != KORE_CUDA_OK) {
+            hx.err = hx.last_error(hx.ctx);
+            return -1;
+        }
+    }
+    return n_gen;
+}
+
+// kore's get_row (kore.cpp:384-407) of a rows x cols table of GGUF type
+// `type` at `data`: the dequantised row into out [cols]. Returns 0 or -1.
+int keng_get_row(int type, int rows, int cols, const void *data, int row, float *out) {
+    const char *tn;
+    uint64_t blk, bpb;
+    if (!type_info((uint32_t)type, &tn, &blk, &bpb)) return -1;
+    Tensor t;
+    t.type = (uint32_t)type;
+    t.n_dims = 2;
+    t.dims[0] = (uint64_t)cols;
+    t.dims[1] = (uint64_t)rows;
+    t.nbytes = (uint64_t)rows * ((uint64_t)cols / blk * bpb);
+    t.data = (const uint8_t *)data;
+    std::vector<float> v;
+    if (!get_row(t, (uint64_t)row, v)) return -1;
+    memcpy(out, v.data(), (size_t)cols * sizeof(float));
+    return 0;
 }
 
 }  // extern "C"

@@ -342,6 +342,8 @@ def engine_lib():
         L.keng_attach_cuda.argtypes = [vp, ctypes.c_char_p, ctypes.c_int]
         L.keng_generate_cuda.argtypes = [vp, ip, ctypes.c_int, ctypes.c_int, ip]
         L.keng_generate_cuda_block.argtypes = [vp, ip, ctypes.c_int, ctypes.c_int, ip]
+        L.keng_generate_cuda_step.argtypes = [vp, ip, ctypes.c_int, ctypes.c_int, ip]
+        L.keng_get_row.argtypes = [ctypes.c_int] * 3 + [vp, ctypes.c_int, fp]
         L.keng_forward.argtypes = [vp, ctypes.c_int, ctypes.c_int, fp]
         L.keng_tensor.argtypes = [vp, ctypes.c_char_p, ip, ip, ip]
         L.keng_tensor.restype = vp
@@ -413,6 +415,17 @@ class GreedyEngine:
             raise RuntimeError(self._err())
         return ids
 
+    def generate_cuda_step(self, prompt, n_gen: int):
+        """Greedy IDs with the prompt through the CUDA attention path and every
+        decode step wholly on the GPU (kore_cuda_decode_step)."""
+        p = np.ascontiguousarray(prompt, np.int32)
+        ids = np.zeros(n_gen, np.int32)
+        ip = ctypes.POINTER(ctypes.c_int)
+        if engine_lib().keng_generate_cuda_step(self.h, p.ctypes.data_as(ip), len(p), n_gen,
+                                                ids.ctypes.data_as(ip)) != n_gen:
+            raise RuntimeError(self._err())
+        return ids
+
     # ---- the reference's own decode step and model, for pinning the step restatement
     def forward_ref(self, token: int, pos: int) -> np.ndarray:
         """kore's forward() of one token at pos (positions in order from 0): its logits."""
@@ -428,6 +441,15 @@ class GreedyEngine:
         if not p:
             raise KeyError(name)
         return t.value, r.value, c.value, p
+
+
+def ref_get_row(qtype: int, rows: int, cols: int, data, row: int) -> np.ndarray:
+    """kore's own get_row (kore.cpp:384-407) of a table (uint8 array or address)."""
+    out = np.empty(cols, np.float32)
+    addr = data if isinstance(data, int) else np.ascontiguousarray(data).ctypes.data
+    if engine_lib().keng_get_row(qtype, rows, cols, addr, row, _fp(out)):
+        raise ValueError("kore's get_row refused the table or row")
+    return out
 
 
 class StepOracle:
