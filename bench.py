@@ -26,8 +26,9 @@ exchange per layer. The cache is fixed (strong scaling).
 Further lines on the same JSON object (N = 1 unless stated): ``cfg1`` (the
 0.5B layer: prefill 128, then 64 decodes; microseconds per call), ``cfg2``
 (7B, 28 layers, decode at 8192), ``attn_block`` (the attention block with its
-quantised projections), ``prefill`` (config 3, tensor cores) and ``batched``
-(config 5, every N).
+quantised projections), ``prefill`` (config 3, tensor cores),
+``decode_step`` (kore's whole decode step on the device: 7B-shaped synthetic
+weights, the headline's cache; tokens/s) and ``batched`` (config 5, every N).
 
 ``--impl reference`` times kore's own CPU attention (the reference compiled
 in place, oracle/_ref) on this host: full 28-layer steps of kore.cpp forward()
@@ -79,6 +80,8 @@ def parse():
     ap.add_argument("--no-block", action="store_true", help="skip the attention-block (with projections) line")
     ap.add_argument("--block-steps", type=int, default=100)
     ap.add_argument("--no-cfg12", action="store_true", help="skip the config-1 and config-2 lines")
+    ap.add_argument("--no-step", action="store_true", help="skip the whole-decode-step line")
+    ap.add_argument("--step-only", action="store_true", help="measure only the whole decode step (development)")
     ap.add_argument("--block-only", action="store_true", help="measure only the attention block (development)")
     ap.add_argument("--prefill-only", action="store_true", help="measure only the prefill (development)")
     a = ap.parse_args()
@@ -650,6 +653,161 @@ def cfg1_cpu_baseline(hq, hk, hv) -> dict:
                       f"arithmetic per token)"}
 
 
+# ---------------------------------------------------------------- the whole decode step (device-resident)
+
+S_FF, S_VOCAB = 18944, 152064   # Qwen2.5-7B feed-forward width and vocabulary
+
+
+def step_model(rng):
+    """Seeded synthetic 7B-shaped GGUF weights in a Q4_K_M-like mix: Q4_K for
+    wq, wk, wo, ffn_gate, ffn_up and the embedding table, Q6_K for wv,
+    ffn_down and the output matrix. One layer's host bytes serve every layer
+    (each layer gets its own device copy, so every step streams all of them
+    from HBM)."""
+    from kore_b200.qweights import Q4_K, Q6_K, random_qmat
+    E = H * D
+    lw = dict(wq=random_qmat(Q4_K, E, E, rng), wk=random_qmat(Q4_K, KVD, E, rng), wv=random_qmat(Q6_K, KVD, E, rng),
+              wo=random_qmat(Q4_K, E, E, rng), w_gate=random_qmat(Q4_K, S_FF, E, rng),
+              w_up=random_qmat(Q4_K, S_FF, E, rng), w_down=random_qmat(Q6_K, E, S_FF, rng))
+    lw.update(bq=rng.standard_normal(E).astype(np.float32) * 0.1, bk=rng.standard_normal(KVD).astype(np.float32) * 0.1,
+              bv=rng.standard_normal(KVD).astype(np.float32) * 0.1,
+              attn_norm=(1 + 0.1 * rng.standard_normal(E)).astype(np.float32),
+              ffn_norm=(1 + 0.1 * rng.standard_normal(E)).astype(np.float32))
+    tok = random_qmat(Q4_K, S_VOCAB, E, rng, sigma=1.0)
+    out_w = random_qmat(Q6_K, S_VOCAB, E, rng)
+    out_norm = (1 + 0.1 * rng.standard_normal(E)).astype(np.float32)
+    return lw, tok, out_w, out_norm
+
+
+def run_step_line(args) -> dict:
+    """kore's whole decode step on the device (kore_cuda_decode_step) at the
+    headline's shape and position: 7B, 28 layers, KV cache of 32768 seeded
+    rows per layer, synthetic Q4_K_M-like weights. One step = one token
+    through embedding, 28 layers (RMSNorm, Q8_K, QKV, attention, Wo, residual,
+    RMSNorm, gate/up + SwiGLU, down, residual), output norm, logits and
+    argmax; the next token is chained on the device. value: tokens/s
+    (device-resident, CUDA graph of one step at position POS, events around K
+    replays); roofline over weight + KV bytes per step; e2e: the host entry
+    point kore_cuda_decode_step (token id in, next token id out) per step."""
+    import torch
+    import kore_b200 as K
+    dev = torch.device("cuda", 0)
+    E = H * D
+    ctx = K.KoreCuda(L, H, G, D, CTX, device=0)
+    stream = torch.cuda.Stream(device=dev)
+    ctx.set_stream(stream.cuda_stream)
+    rng = np.random.default_rng(81)
+    lw, tok, out_w, out_norm = step_model(rng)
+    ctx.set_model(S_FF, S_VOCAB, 1e-6, tok, out_norm, out_w, [lw] * L)
+    w_bytes = L * sum(lw[k].nbytes for k in ("wq", "wk", "wv", "wo", "w_gate", "w_up", "w_down")) + out_w.nbytes
+    with torch.cuda.stream(stream):
+        for layer in range(L):
+            k, v = layer_rows(torch, dev, layer, POS)
+            ctx.append_dev(0, layer, 0, POS, k, v)
+            del k, v
+        t = torch.tensor([17], dtype=torch.int32, device=dev)
+    ctx.sync()
+
+    def step():
+        ctx.decode_step_dev(0, t, POS, t)
+
+    warm = max(3, args.warmup)
+    with torch.cuda.stream(stream):
+        for _ in range(warm):
+            step()
+    ctx.sync()
+    graph = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(graph, stream=stream):
+        step()
+    with torch.cuda.stream(stream):
+        graph.replay()
+    ctx.sync()
+    steps = max(20, args.steps // 10)
+    clocks = ClockSampler(0)
+    clocks.start()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    torch.cuda.synchronize(dev)
+    t_begin = time.time()
+    with torch.cuda.stream(stream):
+        e0.record(stream)
+        for _ in range(steps):
+            graph.replay()
+        e1.record(stream)
+    e1.synchronize()
+    t_end = time.time()
+    ctx.sync()
+    clk = clocks.stop(t_begin, t_end)
+    ms = e0.elapsed_time(e1) / steps
+    del graph
+    # end to end: kore's call, token id in, next token id out
+    tok_id = int(t.item())
+    for _ in range(3):
+        tok_id = ctx.decode_step(0, tok_id, POS)[0]
+    n_e2e = max(10, args.e2e_steps // 5)
+    t0 = time.perf_counter()
+    for _ in range(n_e2e):
+        tok_id = ctx.decode_step(0, tok_id, POS)[0]
+    e2e_ms = (time.perf_counter() - t0) * 1e3 / n_e2e
+    ctx.close()
+    kv_bytes = L * layer_bytes(POS)
+    step_bytes = kv_bytes + w_bytes
+    peaks = load_peaks()
+    gbs = step_bytes / (ms * 1e-3) / 1e9
+    line = {
+        "metric": "decode step tokens/s @7B ctx 32k (whole model on the GPU: 28 layers + logits + argmax)",
+        "value": round(1e3 / ms, 2), "unit": "tokens/s", "ms_per_step": round(ms, 4), "steps": steps, "warmup": warm,
+        "higher_is_better": True, "dtype": "f32 (Q8_K x Q4_K/Q6_K integer products, fp32 attention)",
+        "data": "synthetic (seeded Q4_K_M-like GGUF weights, seeded N(0,1) KV cache)",
+        "config": {"workload": f"Qwen2.5-7B-shaped decode step at position {POS}: n_embd 3584, 28Q/4KV, d128, "
+                               f"n_ff {S_FF}, vocab {S_VOCAB}, {L} layers",
+                   "weights": "Q4_K wq/wk/wo/gate/up/embedding, Q6_K wv/down/output", "weight_bytes_per_step": int(w_bytes),
+                   "kv_bytes_per_step": int(kv_bytes), "l2": "8 GB per step > L2, no flush needed"},
+        "e2e": {"value": round(1e3 / e2e_ms, 2), "unit": "tokens/s", "ms_per_step": round(e2e_ms, 4),
+                "h2d_bytes_per_step": 4, "d2h_bytes_per_step": 260,
+                "call": "kore_cuda_decode_step (token id in as an argument; error word + next token id back)"},
+        "roofline": {"bound": "hbm", "achieved": round(gbs, 1), "peak": peaks["hbm_gbs"], "peak_source": peaks["source"],
+                     "unit": "GB/s", "frac": round(gbs / peaks["hbm_gbs"], 4),
+                     "algorithmic_bytes_per_step": int(step_bytes),
+                     "kernels": "embed + 28 x (qmatvec QKV, attn_decode, split_merge, qmatvec Wo, qmatvec gate/up, "
+                                "qmatvec down) + qmatvec logits + token"},
+        "gpu_launches": steps * (2 + L * 6 + 1),
+        "clocks": clk,
+    }
+    if not args.no_cpu_baseline:
+        line["cpu_baseline"] = step_cpu_baseline(lw, out_w)
+    return line
+
+
+def step_cpu_baseline(lw, out_w) -> dict:
+    """kore's own decode step on this host, composed from its own functions
+    (the reference compiled in place): per layer its attention at POS on one
+    core (kore's attention is single-threaded) plus its quantize + matvec_mt
+    of the layer's seven matrices with all host threads (kore's products are
+    threaded), 28 times, plus the output matrix."""
+    from oracle import oracle as O
+    if not O.ref_available():
+        return {"value": None, "unavailable": "oracle/_ref not built"}
+    cores = len(os.sched_getaffinity(0))
+    rng = np.random.default_rng(82)
+    E = H * D
+    x = rng.standard_normal(E).astype(np.float32)
+    xf = rng.standard_normal(S_FF).astype(np.float32)
+    mats = [(lw[k], x) for k in ("wq", "wk", "wv", "wo", "w_gate", "w_up")] + [(lw["w_down"], xf)]
+    layer_mv = sum(O.ref_qmatvec_ms(m, v, cores, 3)[0] for m, v in mats)
+    out_mv = O.ref_qmatvec_ms(out_w, x, cores, 3)[0]
+    e = _ref_engine_with_rows(*[a.astype(np.float32) for a in
+                                np.random.default_rng(100).standard_normal((2, POS, KVD), dtype=np.float32)], POS)
+    q, k, v = O.seeded_inputs(5, (H * D,), (KVD,), (KVD,))
+    base = _ref_decode_ms(e, 0, q, k, v, reps=3)
+    att = max(min(_ref_decode_ms(e, POS, q, k, v) for _ in range(2)) - base, 1e-6)
+    ms = L * (att + layer_mv) + out_mv
+    return {"value": round(1e3 / ms, 4), "unit": "tokens/s", "cores": cores, "kind": "reference",
+            "ms_per_step": round(ms, 1),
+            "sample": f"kore's own functions: attention at pos {POS} on 1 core ({att:.1f} ms per layer) + quantize "
+                      f"+ matvec_mt of one layer's 7 matrices on {cores} threads ({layer_mv:.1f} ms), x {L} layers, "
+                      f"+ the output matrix ({out_mv:.1f} ms); best of 3 each"}
+
+
 # ---------------------------------------------------------------- config 5: batched decode
 
 B_SEQS, B_LAYERS, B_H, B_G = 64, 36, 16, 2
@@ -1006,6 +1164,9 @@ def main():
     if args.block_only:
         print(json.dumps(run_block_only(args)), flush=True)
         return
+    if args.step_only:
+        print(json.dumps(run_step_line(args)), flush=True)
+        return
     ok = True
     try:
         line = run_decode(args, rank, world, dist, POS, L, args.steps, args.e2e_steps, want_block=True)
@@ -1021,6 +1182,8 @@ def main():
                 line["cfg1"] = run_cfg1(args)
             if not args.no_prefill:
                 line["prefill"] = run_prefill(args, torch.device("cuda", 0), load_peaks())
+            if not args.no_step:
+                line["decode_step"] = run_step_line(args)
         if line is not None:
             ok = all(x.get("parity", {}).get("ok", True) for x in (line, line.get("cfg2") or {}))
             print(json.dumps(line), flush=True)

@@ -267,6 +267,26 @@ int kore_cuda_decode_step(kore_cuda_ctx *ctx, int seq, int token, int pos, int *
 int kore_cuda_decode_step_dev(kore_cuda_ctx *ctx, int seq, const int *token, int pos, int *next_token,
                               float *logits);
 
+/* kore's forward_batch() (kore.cpp:1486-1598) for n prompt tokens at
+ * positions pos0..pos0+n-1 of sequence `seq`, on the device: the float
+ * projections of its prefill (matmul_batch_float, kore.cpp:783-845: each
+ * weight block dequantised to fp32, one fused multiply-add per column in
+ * column order; bit for bit kore's), the biases, RoPE, the cache append, the
+ * causal attention (as kore_cuda_attn_prefill), the residual adds, the
+ * SwiGLU feed-forward and, for the last token, the logits (optional host
+ * logits [n_vocab]) and the greedy next token (*next_token) as kore's
+ * prefill() leaves them for gen_step (kore.cpp:1720-1750). n is not limited
+ * to kore's 64-token chunk (KORE_BMAX, kore.cpp:690): chunking changes no
+ * value. Returns KORE_CUDA_ERANGE for a token outside the vocabulary. */
+int kore_cuda_prefill(kore_cuda_ctx *ctx, int seq, const int *tokens, int n, int pos0, int *next_token,
+                      float *logits);
+
+/* kore's matmul_batch_float (kore.cpp:783-845), the float product of its
+ * prefill, of B host rows x [B][cols] with one uploaded matrix of `layer`
+ * (which: 0 wq, 1 wk, 2 wv, 3 wo, 4 ffn_gate, 5 ffn_up, 6 ffn_down; 4-6 after
+ * kore_cuda_set_model): out [B][rows] host, bit for bit kore's (no bias). */
+int kore_cuda_matmul_batch(kore_cuda_ctx *ctx, int layer, int which, int B, const float *x, float *out);
+
 /*
  * KV-sequence split over GPUs (cfg.shard_count > 1). Each context holds the
  * positions of every page j with j % shard_count == shard_rank; a decode step

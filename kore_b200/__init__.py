@@ -146,6 +146,8 @@ def load_library(path: str = LIB):
     L.kore_cuda_set_model.argtypes = [_vp, ctypes.POINTER(_Model)]
     L.kore_cuda_decode_step.argtypes = [_vp, _i, _i, _i, _ip, _vp]
     L.kore_cuda_decode_step_dev.argtypes = [_vp, _i, _vp, _i, _vp, _vp]
+    L.kore_cuda_prefill.argtypes = [_vp, _i, _ip, _i, _i, _ip, _vp]
+    L.kore_cuda_matmul_batch.argtypes = [_vp, _i, _i, _i, _vp, _vp]
     L.kore_cuda_sync.argtypes = [_vp]
     L.kore_cuda_set_wait_limit.argtypes = [_vp, ctypes.c_ulonglong]
     L.kore_cuda_stream.argtypes = [_vp]
@@ -400,6 +402,23 @@ class KoreCuda:
         self._ck(self._L.kore_cuda_decode_step(self._h, seq, token, pos, ctypes.byref(nxt),
                                                logits.ctypes.data if want_logits else None))
         return nxt.value, logits
+
+    def prefill_tokens(self, seq: int, tokens, pos0: int, want_logits: bool = False):
+        """kore's forward_batch() of prompt tokens at pos0.. on the device: (next token, logits or None)."""
+        toks = np.ascontiguousarray(tokens, np.int32)
+        nxt = ctypes.c_int(-1)
+        logits = np.empty(self.n_vocab, np.float32) if want_logits else None
+        self._ck(self._L.kore_cuda_prefill(self._h, seq, toks.ctypes.data_as(_ip), toks.size, pos0, ctypes.byref(nxt),
+                                           logits.ctypes.data if want_logits else None))
+        return nxt.value, logits
+
+    def matmul_batch(self, layer: int, which: int, x, rows: int) -> np.ndarray:
+        """kore's matmul_batch_float of rows x [B][cols] with an uploaded matrix: [B][rows]."""
+        x = np.ascontiguousarray(x, np.float32)
+        B = x.shape[0]
+        out = np.empty((B, rows), np.float32)
+        self._ck(self._L.kore_cuda_matmul_batch(self._h, layer, which, B, x.ctypes.data, out.ctypes.data))
+        return out
 
     def decode_step_dev(self, seq: int, token, pos: int, next_token, logits=None) -> None:
         """Stream-ordered step: token / next_token are int32 CUDA tensors of one element."""

@@ -165,20 +165,39 @@ constexpr size_t kQmatvecMaxSmem = 227 * 1024;
 size_t qmatvec_config(int cols, int max_block_bytes, int *stages, int *row_slot);
 cudaError_t launch_qmatvec(const QMatvecParams &p, int grid, cudaStream_t s);
 
-// The embedding row of a token (step.cu): x = get_row(table, token)
-// (kore.cpp:384-407) for table type 0 (F32), 1 (F16), 30 (BF16), 12 (Q4_K)
-// or 14 (Q6_K); the token comes from token_dev when set, else `token`; also
-// clears *key (the argmax key the step's logits product fills).
+// The embedding rows of n_tokens tokens (step.cu): row z of x =
+// get_row(table, token z) (kore.cpp:384-407) for table type 0 (F32), 1 (F16),
+// 30 (BF16), 12 (Q4_K) or 14 (Q6_K); the tokens come from token_dev [n_tokens]
+// when set, else the one `token`; also clears *key (the argmax key the
+// step's logits product fills).
 struct EmbedParams {
     const uint8_t *table;
     size_t row_bytes;
-    int type, n_vocab, n_embd, token;
+    int type, n_vocab, n_embd, token, n_tokens;
     const int *token_dev;
     float *x;
     unsigned long long *key;
     int *err;
 };
 cudaError_t launch_embed(const EmbedParams &p, cudaStream_t s);
+// kore's matmul_batch_float (kore.cpp:783-845) on B tokens (batch_proj.cu):
+// out[b * out_stride + r] = the fused multiply-add chain over the columns of
+// the dequantised row r of seg[0] and x[b] (+ bias, or added to resid at the
+// same place); with pair, seg[0].out[b * out_stride + i] = SwiGLU of gate row
+// i (seg 0) and up row i (seg 1).
+struct BatchMatmulParams {
+    QSeg seg[2];
+    int pair;
+    int cols, B;
+    const float *x;          // [B][cols]
+    int out_mode;            // QOUT_STORE or QOUT_RESIDUAL (ignored with pair)
+    const float *resid;
+    int out_stride;
+    unsigned long long exp_tab[32];
+};
+cudaError_t launch_batch_matmul(const BatchMatmulParams &p, cudaStream_t s);
+// out[row] = kore's rmsnorm of x[row] times w, for `rows` rows of n values.
+cudaError_t launch_rmsnorm_rows(const float *x, const float *w, float *out, int rows, int n, float eps, cudaStream_t s);
 // token = the index in an argmax key (-1 for an empty key), after the
 // preceding kernel (programmatic dependency).
 cudaError_t launch_token(const unsigned long long *key, int *token, cudaStream_t s);

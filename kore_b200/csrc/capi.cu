@@ -117,6 +117,12 @@ struct kore_cuda_ctx {
         unsigned long long *key = nullptr;   // argmax key of the logits
         int *token = nullptr;     // [2]: a step's input and output token (device-side steps)
         unsigned long long exp_tab[32] = {};
+        // forward_batch buffers for up to pf_cap tokens: x, normed x, q, k, v,
+        // attention output, SwiGLU output, token ids
+        int pf_cap = 0;
+        float *bx = nullptr, *bxb = nullptr, *bq = nullptr, *bk = nullptr, *bv = nullptr, *batt = nullptr,
+              *bact = nullptr;
+        int *btok = nullptr;
     } model;
     std::string msg;
 };
@@ -564,6 +570,9 @@ void kore_cuda_destroy(kore_cuda_ctx *c) {
         cudaFree(c->model.logits);
         cudaFree(c->model.key);
         cudaFree(c->model.token);
+        for (void *b : {(void *)c->model.bx, (void *)c->model.bxb, (void *)c->model.bq, (void *)c->model.bk,
+                        (void *)c->model.bv, (void *)c->model.batt, (void *)c->model.bact, (void *)c->model.btok})
+            cudaFree(b);
         cudaFree(c->blk);
         cudaFree(c->kv);
         cudaFree(c->pt_d);
@@ -1314,6 +1323,7 @@ static int run_step(kore_cuda_ctx *c, int seq, int token, const int *token_dev, 
     ep.n_vocab = M.n_vocab;
     ep.n_embd = E;
     ep.token = token;
+    ep.n_tokens = 1;
     ep.token_dev = token_dev;
     ep.x = M.x;
     ep.key = M.key;
@@ -1405,6 +1415,169 @@ int kore_cuda_decode_step(kore_cuda_ctx *c, int seq, int token, int pos, int *ne
     if (logits)
         CK(cudaMemcpyAsync(logits, c->model.logits, (size_t)c->model.n_vocab * sizeof(float), cudaMemcpyDeviceToHost,
                            c->stream));
+    if (int rc = finish(c, sizeof(int))) return rc;
+    memcpy(next_token, reinterpret_cast<const char *>(c->host_err) + kErrPad, sizeof(int));
+    return KORE_CUDA_OK;
+}
+
+// ---------------------------------------------------------------- the whole prefill on the device
+
+static int grow_prefill(kore_cuda_ctx *c, int n) {
+    auto &M = c->model;
+    if (n <= M.pf_cap) return KORE_CUDA_OK;
+    float **fb[7] = {&M.bx, &M.bxb, &M.bq, &M.bk, &M.bv, &M.batt, &M.bact};
+    for (float **b : fb) {
+        cudaFree(*b);
+        *b = nullptr;
+    }
+    cudaFree(M.btok);
+    M.btok = nullptr;
+    M.pf_cap = 0;
+    const int cap = (n + 63) / 64 * 64;
+    const size_t E = (size_t)c->H * c->D, kvd = (size_t)c->kvd, FF = (size_t)M.n_ff;
+    const size_t floats[7] = {E, E, E, kvd, kvd, E, FF};
+    for (int i = 0; i < 7; ++i) CK(cudaMalloc(fb[i], floats[i] * cap * sizeof(float)));
+    CK(cudaMalloc(&M.btok, (size_t)cap * sizeof(int)));
+    M.pf_cap = cap;
+    return KORE_CUDA_OK;
+}
+
+static int launch_bmm(kore_cuda_ctx *c, const uint8_t *w, int type, int rows, int cols, int B, const float *x,
+                      float *out, const float *bias, const float *resid) {
+    BatchMatmulParams bp;
+    memset(&bp, 0, sizeof bp);
+    bp.seg[0] = QSeg{w, bias, out, type, rows};
+    bp.cols = cols;
+    bp.B = B;
+    bp.x = x;
+    bp.out_mode = resid ? QOUT_RESIDUAL : QOUT_STORE;
+    bp.resid = resid;
+    bp.out_stride = rows;
+    CK(launch_batch_matmul(bp, c->stream));
+    return KORE_CUDA_OK;
+}
+
+// kore's matmul_batch_float (kore.cpp:783-845) of B host rows with one of
+// layer's uploaded matrices (0 wq, 1 wk, 2 wv, 3 wo, 4 ffn_gate, 5 ffn_up,
+// 6 ffn_down; 4-6 need kore_cuda_set_model): out [B][rows] host.
+int kore_cuda_matmul_batch(kore_cuda_ctx *c, int layer, int which, int B, const float *x, float *out) {
+    if (!c) return KORE_CUDA_EINVAL;
+    if (!x || !out || B <= 0) return fail(c, KORE_CUDA_EINVAL, "null x or out, or B <= 0");
+    if (which < 0 || which > 6) return fail(c, KORE_CUDA_EINVAL, "which = %d outside 0..6", which);
+    const kore_cuda_ctx::LayerProj *lp = layer_proj(c, layer);
+    if (!lp) return fail(c, KORE_CUDA_ESTATE, "no attention weights for layer %d", layer);
+    if (which > 3 && (!c->model.ready || layer >= (int)c->model.layers.size()))
+        return fail(c, KORE_CUDA_ESTATE, "no feed-forward weights (kore_cuda_set_model)");
+    const int E = c->H * c->D, FF = c->model.n_ff;
+    const uint8_t *w;
+    int type, rows, cols;
+    if (which < 4) {
+        w = lp->w + lp->off[which];
+        type = lp->type[which];
+        rows = lp->rows[which];
+        cols = E;
+    } else {
+        const auto &lf = c->model.layers[(size_t)layer];
+        w = lf.w + lf.off[which - 4];
+        type = lf.type[which - 4];
+        rows = which == 6 ? E : FF;
+        cols = which == 6 ? FF : E;
+    }
+    DeviceGuard dg(c->cfg.device);
+    const size_t nx = (size_t)B * cols, no = (size_t)B * rows;
+    if (int rc = grow_stage(c, nx + no)) return rc;
+    CK(cudaMemcpyAsync(c->dev_stage, x, nx * sizeof(float), cudaMemcpyHostToDevice, c->stream));
+    if (int rc = launch_bmm(c, w, type, rows, cols, B, c->dev_stage, c->dev_stage + nx, nullptr, nullptr)) return rc;
+    CK(cudaMemcpyAsync(out, c->dev_stage + nx, no * sizeof(float), cudaMemcpyDeviceToHost, c->stream));
+    return finish(c);
+}
+
+// kore's forward_batch() (kore.cpp:1486-1598) for n prompt tokens at pos0..,
+// every step on the device, then the greedy next token (the argmax of the
+// last token's logits, kore.cpp:1594-1597 and :1601-1603):
+//   embedding rows                                      embed_kernel
+//   per layer: RMSNorm rows                             rmsnorm_rows_kernel
+//              Wq/Wk/Wv float products + biases          batch_matmul_kernel (kore's FMA chains)
+//              RoPE, append, causal attention            the prefill path (kore_cuda_attn_prefill_dev)
+//              Wo product + residual add                batch_matmul_kernel
+//              RMSNorm rows, gate/up + SwiGLU            rmsnorm_rows_kernel, batch_matmul_kernel (paired)
+//              down product + residual add              batch_matmul_kernel
+//   last row: RMSNorm + Q8_K + output matrix + argmax    qmatvec (as the decode step)
+// Unlike kore, n is not limited to its 64-token chunk: every product column
+// and every attention row is independent of the chunk it is computed in.
+int kore_cuda_prefill(kore_cuda_ctx *c, int seq, const int *tokens, int n, int pos0, int *next_token, float *logits) {
+    if (!c) return KORE_CUDA_EINVAL;
+    if (!tokens || !next_token || n <= 0) return fail(c, KORE_CUDA_EINVAL, "null tokens or next_token, or n <= 0");
+    if (!c->model.ready || c->proj.size() != (size_t)c->cfg.n_layer)
+        return fail(c, KORE_CUDA_ESTATE, "no model on the device (kore_cuda_set_model)");
+    if (c->NS > 1) return fail(c, KORE_CUDA_EINVAL, "prefill on a KV-sharded context is not supported");
+    for (int l = 0; l < c->cfg.n_layer; ++l)
+        if (int rc = check_range(c, seq, l, pos0, n)) return rc;
+    auto &M = c->model;
+    for (int z = 0; z < n; ++z)   // forward_batch returns false (kore.cpp:1496)
+        if (tokens[z] < 0 || tokens[z] >= M.n_vocab)
+            return fail(c, KORE_CUDA_ERANGE, "token %d (row %d) outside the vocabulary of %d", tokens[z], z, M.n_vocab);
+    DeviceGuard dg(c->cfg.device);
+    if (int rc = grow_prefill(c, n)) return rc;
+    const int E = c->H * c->D, FF = M.n_ff, kvd = c->kvd;
+    CK(cudaMemcpyAsync(M.btok, tokens, (size_t)n * sizeof(int), cudaMemcpyHostToDevice, c->stream));
+    EmbedParams ep;
+    memset(&ep, 0, sizeof ep);
+    ep.table = M.tok;
+    ep.row_bytes = M.tok_row_bytes;
+    ep.type = M.tok_type;
+    ep.n_vocab = M.n_vocab;
+    ep.n_embd = E;
+    ep.n_tokens = n;
+    ep.token_dev = M.btok;
+    ep.x = M.bx;
+    ep.key = M.key;
+    ep.err = c->err_d;
+    CK(launch_embed(ep, c->stream));
+    for (int l = 0; l < c->cfg.n_layer; ++l) {
+        const kore_cuda_ctx::LayerProj &lp = c->proj[(size_t)l];
+        const kore_cuda_ctx::LayerFfn &lf = M.layers[(size_t)l];
+        const float *bias = lp.has_bias ? lp.bias : nullptr;
+        CK(launch_rmsnorm_rows(M.bx, lf.norms, M.bxb, n, E, M.eps, c->stream));
+        if (int rc = launch_bmm(c, lp.w + lp.off[0], lp.type[0], E, E, n, M.bxb, M.bq, bias, nullptr)) return rc;
+        if (int rc = launch_bmm(c, lp.w + lp.off[1], lp.type[1], kvd, E, n, M.bxb, M.bk, bias ? bias + E : nullptr,
+                                nullptr))
+            return rc;
+        if (int rc = launch_bmm(c, lp.w + lp.off[2], lp.type[2], kvd, E, n, M.bxb, M.bv,
+                                bias ? bias + E + kvd : nullptr, nullptr))
+            return rc;
+        if (int rc = kore_cuda_attn_prefill_dev(c, seq, l, pos0, n, M.bq, M.bk, M.bv, M.batt)) return rc;
+        if (int rc = launch_bmm(c, lp.w + lp.off[3], lp.type[3], E, E, n, M.batt, M.bx, nullptr, M.bx)) return rc;
+        CK(launch_rmsnorm_rows(M.bx, lf.norms + E, M.bxb, n, E, M.eps, c->stream));
+        BatchMatmulParams bp;
+        memset(&bp, 0, sizeof bp);
+        bp.seg[0] = QSeg{lf.w + lf.off[0], nullptr, M.bact, lf.type[0], FF};
+        bp.seg[1] = QSeg{lf.w + lf.off[1], nullptr, M.bact, lf.type[1], FF};
+        bp.pair = 1;
+        bp.cols = E;
+        bp.B = n;
+        bp.x = M.bxb;
+        bp.out_stride = FF;
+        memcpy(bp.exp_tab, M.exp_tab, sizeof bp.exp_tab);
+        CK(launch_batch_matmul(bp, c->stream));
+        if (int rc = launch_bmm(c, lf.w + lf.off[2], lf.type[2], E, FF, n, M.bact, M.bx, nullptr, M.bx)) return rc;
+    }
+    QMatvecParams mp;
+    memset(&mp, 0, sizeof mp);
+    mp.n_seg = 1;
+    mp.cols = E;
+    mp.seg[0] = QSeg{M.out_w, nullptr, M.logits, M.out_type, M.n_vocab};
+    mp.in_mode = QIN_RMSNORM;
+    mp.x = M.bx + (size_t)(n - 1) * E;
+    mp.norm_w = M.out_norm;
+    mp.eps = M.eps;
+    mp.out_mode = QOUT_ARGMAX;
+    mp.argmax = M.key;
+    if (int rc = launch_products(c, mp)) return rc;
+    int *dnext = reinterpret_cast<int *>(reinterpret_cast<char *>(c->err_d) + kErrPad);
+    CK(launch_token(M.key, dnext, c->stream));
+    if (logits)
+        CK(cudaMemcpyAsync(logits, M.logits, (size_t)M.n_vocab * sizeof(float), cudaMemcpyDeviceToHost, c->stream));
     if (int rc = finish(c, sizeof(int))) return rc;
     memcpy(next_token, reinterpret_cast<const char *>(c->host_err) + kErrPad, sizeof(int));
     return KORE_CUDA_OK;

@@ -64,6 +64,7 @@
 
 #include "attn.cuh"
 #include "common.cuh"
+#include "kore_math.cuh"
 
 #include <cuda_fp16.h>
 
@@ -146,48 +147,6 @@ __device__ __forceinline__ void q8k_block(const float (&v)[8], int lane, uint8_t
     const int s2 = (int)(int16_t)s + (int)(int16_t)__shfl_xor_sync(FULLW, s, 2);
     if ((lane & 3) == 0) pairs[lane >> 2] = (int16_t)s2;
     if (lane == 0) *xd = d;
-}
-
-// ---------------------------------------------------------------- RMSNorm and SwiGLU
-
-// The float kore's rmsnorm (kore.cpp:1369-1370) makes of its sequential
-// double sum of squares, (float)(ss / n), from a sum S of the same squares
-// in another order: exact when the float cannot change within the two sums'
-// error bounds ((n + log2 n) * 2^-53 of the sum, with margin), else NaN
-// (the caller then sums sequentially).
-__device__ __forceinline__ float mean_square_float(double S, int n) {
-    const double v = __ddiv_rn(S, (double)n);
-    const float f = __double2float_rn(v);
-    const double lo = ((double)f + (double)nextafterf(f, -INFINITY)) * 0.5;
-    const double hi = ((double)f + (double)nextafterf(f, INFINITY)) * 0.5;
-    const double m = v * (double)(n + 64) * 0x1p-52;
-    return (v - m > lo && v + m < hi) ? f : __int_as_float(0x7fffffff);
-}
-
-// kore's std::exp(float): the table-driven expf of the C library (see the
-// header), restated with each double operation rounded as the library does.
-// tab[i] = bits(2^(i/32)) - (i << 47).
-__device__ __forceinline__ float kore_expf(float x, const unsigned long long *tab) {
-    if (x != x) return x + x;
-    if (x > 0x1.62e42ep6f) return __int_as_float(0x7f800000);   // overflow: +inf
-    if (x < -0x1.9fe368p6f) return 0.0f;                          // below half the smallest subnormal
-    constexpr double kShift = 0x1.8p52, kInvLn2N = 0x1.71547652b82fep+0 * 32;
-    constexpr double kC0 = 0x1.c6af84b912394p-5 / 32768, kC1 = 0x1.ebfce50fac4f3p-3 / 1024,
-                     kC2 = 0x1.62e42ff0c52d6p-1 / 32;
-    const double xd = (double)x;
-    double kd = __dadd_rn(__dmul_rn(kInvLn2N, xd), kShift);
-    const unsigned long long ki = (unsigned long long)__double_as_longlong(kd);
-    kd = __dsub_rn(kd, kShift);
-    const double r = __fma_rn(kInvLn2N, xd, -kd);
-    const double s = __longlong_as_double((long long)(tab[ki & 31] + (ki << 47)));
-    const double r2 = __dmul_rn(r, r);
-    const double y = __dadd_rn(__dmul_rn(__dadd_rn(__dmul_rn(kC0, r), kC1), r2), __dadd_rn(__dmul_rn(kC2, r), 1.0));
-    return __double2float_rn(__dmul_rn(y, s));
-}
-
-// kore.cpp:1465-1468: g / (1 + exp(-g)) * u.
-__device__ __forceinline__ float kore_swiglu(float g, float u, const unsigned long long *tab) {
-    return __fmul_rn(__fdiv_rn(g, __fadd_rn(1.0f, kore_expf(-g, tab))), u);
 }
 
 // Orderable key of (value, row) for the greedy argmax: larger value first,
@@ -425,37 +384,7 @@ __global__ void __launch_bounds__(32 * kWarps) qmatvec_kernel(const __grid_const
 
     // ------------------------------------------------------------ the Q8_K input
     float scale = 1.f;
-    if (p.in_mode == QIN_RMSNORM) {
-        // kore.cpp:1367-1372: the sum of squares, a tree here, checked and if
-        // need be redone in kore's order
-        double ss = 0.0;
-        for (int i = threadIdx.x; i < p.cols; i += 32 * kWarps) {
-            const double xi = (double)p.x[i];
-            ss = __dadd_rn(ss, __dmul_rn(xi, xi));
-        }
-#pragma unroll
-        for (int o = 16; o > 0; o >>= 1) ss = __dadd_rn(ss, __shfl_xor_sync(FULLW, ss, o));
-        if (lane == 0) red[warp] = ss;
-        __syncthreads();
-        if (threadIdx.x == 0) {
-            double S2 = 0.0;
-            for (int w = 0; w < kWarps; ++w) S2 = __dadd_rn(S2, red[w]);
-            float f = mean_square_float(S2, p.cols);
-            if (f != f && S2 == S2) {
-                double seq = 0.0;
-                for (int i = 0; i < p.cols; ++i) {
-                    const double xi = (double)p.x[i];
-                    seq = __dadd_rn(seq, __dmul_rn(xi, xi));
-                }
-                f = __double2float_rn(__ddiv_rn(seq, (double)p.cols));
-            } else if (S2 != S2) {
-                f = __double2float_rn(__ddiv_rn(S2, (double)p.cols));
-            }
-            s_scale[0] = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(f, p.eps)));
-        }
-        __syncthreads();
-        scale = s_scale[0];
-    }
+    if (p.in_mode == QIN_RMSNORM) scale = block_rms_scale(p.x, p.cols, p.eps, red, s_scale);   // kore.cpp:1367-1372
     for (int b = warp; b < nb; b += kWarps) {
         const float4 *src = reinterpret_cast<const float4 *>(p.x + (size_t)b * 256 + 8 * lane);
         const float4 a = src[0], c = src[1];

@@ -16,56 +16,20 @@
 
 #include "attn.cuh"
 #include "common.cuh"
-
-#include <cuda_fp16.h>
+#include "kore_math.cuh"
 
 namespace kore {
 namespace {
 
-__device__ __forceinline__ float f16_at(const uint8_t *p) {
-    return __half2float(__ushort_as_half((unsigned short)(p[0] | (p[1] << 8))));
-}
-
-// kore's get_scale_min_k4 (kore.cpp:327-335): the 6-bit scale and min of
-// sub-block j from the 12 packed bytes q.
-__device__ __forceinline__ void scale_min_k4(int j, const uint8_t *q, int &sc, int &mn) {
-    if (j < 4) {
-        sc = q[j] & 63;
-        mn = q[j + 4] & 63;
-    } else {
-        sc = (q[j + 4] & 0x0F) | ((q[j - 4] >> 6) << 4);
-        mn = (q[j + 4] >> 4) | ((q[j] >> 6) << 4);
-    }
-}
-
-// Value j (0..255) of a Q4_K block (kore.cpp:337-354).
-__device__ __forceinline__ float q4k_value(const uint8_t *b, int j) {
-    const int chunk = j >> 6, jj = j & 63, l = jj & 31;
-    int sc, mn;
-    scale_min_k4(2 * chunk + (jj >> 5), b + 4, sc, mn);
-    const float d1 = __fmul_rn(f16_at(b), (float)sc), m1 = __fmul_rn(f16_at(b + 2), (float)mn);
-    const int q = b[16 + 32 * chunk + l];
-    const int nib = jj < 32 ? (q & 0x0F) : (q >> 4);
-    return __fsub_rn(__fmul_rn(d1, (float)nib), m1);
-}
-
-// Value j (0..255) of a Q6_K block (kore.cpp:359-381).
-__device__ __forceinline__ float q6k_value(const uint8_t *b, int j) {
-    const int half = j >> 7, jj = j & 127, g = jj >> 5, l = jj & 31;
-    const uint8_t *ql = b + 64 * half, *qh = b + 128 + 32 * half;
-    const int8_t *sc = reinterpret_cast<const int8_t *>(b + 192 + 8 * half);
-    const int lo = (g & 1) ? ql[l + 32] : ql[l];
-    const int q = (((g & 2) ? (lo >> 4) : (lo & 0x0F)) | (((qh[l] >> (2 * g)) & 3) << 4)) - 32;
-    return __fmul_rn(__fmul_rn(f16_at(b + 208), (float)sc[(l >> 4) + 2 * g]), (float)q);
-}
-
 __global__ void __launch_bounds__(256) embed_kernel(const __grid_constant__ EmbedParams p) {
-    int t = p.token_dev ? *p.token_dev : p.token;
+    const int z = blockIdx.y;   // token z of the batch: row z of x
+    int t = p.token_dev ? p.token_dev[z] : p.token;
     if (t < 0 || t >= p.n_vocab) {
         if (threadIdx.x == 0) raise_error(p.err, DEV_BAD_TOKEN);
         t = 0;
     }
     const uint8_t *row = p.table + (size_t)t * p.row_bytes;
+    float *x = p.x + (size_t)z * p.n_embd;
     for (int i = blockIdx.x * blockDim.x + threadIdx.x; i < p.n_embd; i += gridDim.x * blockDim.x) {
         float v;
         switch (p.type) {
@@ -75,9 +39,9 @@ __global__ void __launch_bounds__(256) embed_kernel(const __grid_constant__ Embe
             case 12: v = q4k_value(row + (size_t)(i >> 8) * 144, i & 255); break;
             default: v = q6k_value(row + (size_t)(i >> 8) * 210, i & 255); break;
         }
-        p.x[i] = v;
+        x[i] = v;
     }
-    if (blockIdx.x == 0 && threadIdx.x == 0 && p.key) *p.key = 0ull;
+    if (blockIdx.x == 0 && blockIdx.y == 0 && threadIdx.x == 0 && p.key) *p.key = 0ull;
 }
 
 __global__ void token_kernel(const unsigned long long *key, int *token) {
@@ -91,7 +55,9 @@ __global__ void token_kernel(const unsigned long long *key, int *token) {
 cudaError_t launch_embed(const EmbedParams &p, cudaStream_t s) {
     if (!p.table || !p.x || p.n_embd <= 0 || p.n_vocab <= 0) return cudaErrorInvalidValue;
     if (p.type != 0 && p.type != 1 && p.type != 30 && p.type != 12 && p.type != 14) return cudaErrorInvalidValue;
-    embed_kernel<<<(p.n_embd + 255) / 256 < 32 ? (p.n_embd + 255) / 256 : 32, 256, 0, s>>>(p);
+    if (p.n_tokens <= 0 || p.n_tokens > 65535 || (p.n_tokens > 1 && !p.token_dev)) return cudaErrorInvalidValue;
+    const dim3 grid((p.n_embd + 255) / 256 < 32 ? (p.n_embd + 255) / 256 : 32, p.n_tokens);
+    embed_kernel<<<grid, 256, 0, s>>>(p);
     return cudaGetLastError();
 }
 

@@ -602,4 +602,29 @@ int keng_get_row(int type, int rows, int cols, const void *data, int row, float 
     return 0;
 }
 
+// kore's own forward_batch() (kore.cpp:1486-1598) of nb <= e.bsz tokens at
+// pos0 (positions before pos0 already in the engine's cache): the last
+// token's logits into logits [n_vocab]. Returns 0 or -1.
+int keng_forward_batch(void *h, const int *toks, int nb, int pos0, float *logits) {
+    Harness &hx = *(Harness *)h;
+    if (!forward_batch(hx.e, toks, nb, pos0, true)) return -1;
+    memcpy(logits, hx.e.logits.data(), hx.e.logits.size() * sizeof(float));
+    return 0;
+}
+
+// kore's own matmul_batch_float (kore.cpp:783-845) with the engine's AVX2
+// choice: out [B][rows] = rows x [B][cols] of a GGUF matrix at `data`.
+int keng_matmul_batch(void *h, int type, int rows, int cols, const void *data, const float *x, int B, float *out) {
+    Harness &hx = *(Harness *)h;
+    Tensor t;
+    t.type = (uint32_t)type;
+    t.n_dims = 2;
+    t.dims[0] = (uint64_t)cols;
+    t.dims[1] = (uint64_t)rows;
+    t.data = (const uint8_t *)data;
+    std::vector<float> xt((size_t)((B + 7) & ~7) * cols);
+    matmul_batch_float(t, x, B, xt.data(), out, hx.e.avx2, hx.e.nth);
+    return 0;
+}
+
 }  // extern "C"

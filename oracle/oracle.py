@@ -344,6 +344,8 @@ def engine_lib():
         L.keng_generate_cuda_block.argtypes = [vp, ip, ctypes.c_int, ctypes.c_int, ip]
         L.keng_generate_cuda_step.argtypes = [vp, ip, ctypes.c_int, ctypes.c_int, ip]
         L.keng_get_row.argtypes = [ctypes.c_int] * 3 + [vp, ctypes.c_int, fp]
+        L.keng_forward_batch.argtypes = [vp, ip, ctypes.c_int, ctypes.c_int, fp]
+        L.keng_matmul_batch.argtypes = [vp] + [ctypes.c_int] * 3 + [vp, fp, ctypes.c_int, fp]
         L.keng_forward.argtypes = [vp, ctypes.c_int, ctypes.c_int, fp]
         L.keng_tensor.argtypes = [vp, ctypes.c_char_p, ip, ip, ip]
         L.keng_tensor.restype = vp
@@ -432,6 +434,24 @@ class GreedyEngine:
         out = np.empty(self.n_vocab, np.float32)
         if engine_lib().keng_forward(self.h, token, pos, _fp(out)):
             raise RuntimeError("kore forward() refused the token or position")
+        return out
+
+    def forward_batch_ref(self, tokens, pos0: int) -> np.ndarray:
+        """kore's forward_batch() of up to e.bsz tokens at pos0: the last token's logits."""
+        t = np.ascontiguousarray(tokens, np.int32)
+        out = np.empty(self.n_vocab, np.float32)
+        if engine_lib().keng_forward_batch(self.h, t.ctypes.data_as(ctypes.POINTER(ctypes.c_int)), t.size, pos0,
+                                           _fp(out)):
+            raise RuntimeError("kore forward_batch() refused the tokens or positions")
+        return out
+
+    def matmul_batch_ref(self, m, x: np.ndarray) -> np.ndarray:
+        """kore's matmul_batch_float of rows x [B][cols] with matrix m (.type .rows .cols, .data or .addr)."""
+        x = np.ascontiguousarray(x, np.float32)
+        out = np.empty((x.shape[0], m.rows), np.float32)
+        addr = getattr(m, "addr", None)
+        addr = addr if addr is not None else m.data.ctypes.data
+        engine_lib().keng_matmul_batch(self.h, m.type, m.rows, m.cols, addr, _fp(x), x.shape[0], _fp(out))
         return out
 
     def tensor(self, name: str):
