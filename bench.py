@@ -798,8 +798,9 @@ def step_cpu_baseline(lw, out_w) -> dict:
     e = _ref_engine_with_rows(*[a.astype(np.float32) for a in
                                 np.random.default_rng(100).standard_normal((2, POS, KVD), dtype=np.float32)], POS)
     q, k, v = O.seeded_inputs(5, (H * D,), (KVD,), (KVD,))
+    t = min(_ref_decode_ms(e, POS, q, k, v) for _ in range(2))
     base = _ref_decode_ms(e, 0, q, k, v, reps=3)
-    att = max(min(_ref_decode_ms(e, POS, q, k, v) for _ in range(2)) - base, 1e-6)
+    att = max(t - base, 1e-6)
     ms = L * (att + layer_mv) + out_mv
     return {"value": round(1e3 / ms, 4), "unit": "tokens/s", "cores": cores, "kind": "reference",
             "ms_per_step": round(ms, 1),
@@ -1050,12 +1051,9 @@ def cpu_baseline_sample(pos: int, gpu_layer0, q0, k0, v0):
     kr, vr = layer_rows(torch, dev, 0, pos)
     e = _ref_engine_with_rows(kr.cpu().numpy(), vr.cpu().numpy(), pos)
     del kr, vr
+    ref = e.decode(pos, q0, k0, v0)   # before any forward() at position 0, which rewrites row 0
+    t = min(_ref_decode_ms(e, pos, q0, k0, v0) for _ in range(3))
     base = _ref_decode_ms(e, 0, q0, k0, v0, reps=3)
-    ts = []
-    for _ in range(3):
-        ts.append(_ref_decode_ms(e, pos, q0, k0, v0))
-    t = min(ts)
-    ref = e.decode(pos, q0, k0, v0)
     att = max(t - base, 1e-6)
     cb = {"value": round(layer_bytes(pos) / (att * 1e-3) / 1e9, 3), "unit": "GB/s", "cores": 1,
           "kind": "reference", "attention_ms": round(att, 3),
@@ -1087,8 +1085,9 @@ def run_reference(args, rank: int, world: int) -> dict | None:
         engines.append(_ref_engine_with_rows(rows_k, rows_v, POS))
         del rows_k, rows_v
     q, k, v = O.seeded_inputs(5, (H * D,), (KVD,), (KVD,))
+    t1 = min(_ref_decode_ms(engines[0], POS, q, k, v) for _ in range(2))
     base = _ref_decode_ms(engines[0], 0, q, k, v, reps=3)
-    one_core_att = max(min(_ref_decode_ms(engines[0], POS, q, k, v) for _ in range(2)) - base, 1e-6)
+    one_core_att = max(t1 - base, 1e-6)
     per_thread = (L + T - 1) // T
 
     def worker(t):

@@ -93,6 +93,13 @@ int kore_cuda_seq_reset(kore_cuda_ctx *ctx, int seq);
  * that may be appended. */
 int kore_cuda_seq_len(const kore_cuda_ctx *ctx, int seq, int layer);
 
+/* Keeps the first n positions of a sequence in every layer and gives the
+ * pages wholly past them back to the pool: a conversation rebuilt shorter
+ * (condense, kore.cpp:1760-1799) then appends from n. kore itself only
+ * overwrites from position 0 and leaves the stale rows, which its attention
+ * never reads again (kore.cpp:1763-1765); dropping them frees the pages. */
+int kore_cuda_seq_truncate(kore_cuda_ctx *ctx, int seq, int n);
+
 /*
  * RoPE + append of n tokens at positions pos0..pos0+n-1 of (seq, layer):
  * k is rotated with the tables of its position and stored, v is stored as
@@ -286,6 +293,57 @@ int kore_cuda_prefill(kore_cuda_ctx *ctx, int seq, const int *tokens, int n, int
  * (which: 0 wq, 1 wk, 2 wv, 3 wo, 4 ffn_gate, 5 ffn_up, 6 ffn_down; 4-6 after
  * kore_cuda_set_model): out [B][rows] host, bit for bit kore's (no bias). */
 int kore_cuda_matmul_batch(kore_cuda_ctx *ctx, int layer, int which, int B, const float *x, float *out);
+
+/*
+ * Many chat sessions over one context (the model uploaded with
+ * kore_cuda_set_model): kore's ChatSession, prefill(), gen_step() and
+ * condense() (kore.cpp:1674-1799) with every session a sequence of the
+ * shared page pool (cfg.max_seqs sessions at most).
+ *  - open: admits a session (a free sequence slot, emptied); close: retires
+ *    it and frees its pages.
+ *  - submit: a turn's token ids, appended after the session's conversation
+ *    at the next step (kore's prefill(), with its length check: the turn must
+ *    leave room in the context); max_new bounds the tokens generated for it
+ *    (0: until eos/bos or a full context).
+ *  - step: one round: every submitted turn is prefilled on the device
+ *    (kore_cuda_prefill), then every generating session takes one greedy
+ *    gen_step: the token sampled from its last logits is reported, and
+ *    unless it is eos/bos or the context is full it is appended and run
+ *    through the whole model (kore_cuda_decode_step_dev). The sessions'
+ *    steps are queued back to back with their tokens kept on the device;
+ *    the host reads the next tokens back once per round. events receives
+ *    one entry per session that was generating.
+ *  - condense: rebuilds a session's cache from position 0 over the token ids
+ *    given (kore's re-prefill of {system + summary} + recent tail,
+ *    kore.cpp:1786-1797); the session stops generating until its next turn.
+ * Not re-entrant: one host thread at a time, as the context.
+ */
+typedef struct kore_cuda_server kore_cuda_server;
+
+enum kore_cuda_event_status {
+    KORE_CUDA_EV_TOKEN = 0,   /* token generated and appended */
+    KORE_CUDA_EV_END = 1,     /* eos or bos sampled (not appended): the session stops generating */
+    KORE_CUDA_EV_FULL = 2,    /* the context is full (token not appended): the session stops */
+    KORE_CUDA_EV_LIMIT = 3    /* token generated and appended; the turn's max_new is reached */
+};
+
+typedef struct kore_cuda_event {
+    int session;
+    int token;
+    int status;               /* kore_cuda_event_status */
+} kore_cuda_event;
+
+int kore_cuda_server_create(kore_cuda_server **out, kore_cuda_ctx *ctx, int eos_token, int bos_token);
+void kore_cuda_server_destroy(kore_cuda_server *srv);
+const char *kore_cuda_server_last_error(const kore_cuda_server *srv);
+int kore_cuda_server_open(kore_cuda_server *srv, int *session);
+int kore_cuda_server_close(kore_cuda_server *srv, int session);
+int kore_cuda_server_submit(kore_cuda_server *srv, int session, const int *ids, int n, int max_new);
+int kore_cuda_server_step(kore_cuda_server *srv, kore_cuda_event *events, int max_events, int *n_events);
+int kore_cuda_server_condense(kore_cuda_server *srv, int session, const int *ids, int n);
+/* The session's conversation (every token in its cache): copies up to cap
+ * ids and returns the length, or KORE_CUDA_ERANGE for a session not open. */
+int kore_cuda_server_history(const kore_cuda_server *srv, int session, int *ids, int cap);
 
 /*
  * KV-sequence split over GPUs (cfg.shard_count > 1). Each context holds the

@@ -21,7 +21,7 @@ import numpy as np
 
 from .build import LIB, INCLUDE
 
-__all__ = ["KoreCuda", "KoreCudaError", "KvView", "load_library", "declared_symbols", "STATUS"]
+__all__ = ["KoreCuda", "KoreCudaError", "KvView", "Server", "load_library", "declared_symbols", "STATUS"]
 
 STATUS = {
     0: "KORE_CUDA_OK", -1: "KORE_CUDA_EINVAL", -2: "KORE_CUDA_ERANGE", -3: "KORE_CUDA_ENOMEM",
@@ -73,6 +73,14 @@ class _Model(ctypes.Structure):
     _fields_ = [("n_ff", ctypes.c_int), ("n_vocab", ctypes.c_int), ("rms_eps", ctypes.c_float),
                 ("tok_embd", _QMat), ("out_norm", ctypes.c_void_p), ("out_w", _QMat),
                 ("layers", ctypes.POINTER(_LayerW))]
+
+
+class _Event(ctypes.Structure):
+    """kore_cuda_event."""
+    _fields_ = [("session", ctypes.c_int), ("token", ctypes.c_int), ("status", ctypes.c_int)]
+
+
+EV_TOKEN, EV_END, EV_FULL, EV_LIMIT = 0, 1, 2, 3
 
 
 def _addr(a) -> int | None:
@@ -148,6 +156,18 @@ def load_library(path: str = LIB):
     L.kore_cuda_decode_step_dev.argtypes = [_vp, _i, _vp, _i, _vp, _vp]
     L.kore_cuda_prefill.argtypes = [_vp, _i, _ip, _i, _i, _ip, _vp]
     L.kore_cuda_matmul_batch.argtypes = [_vp, _i, _i, _i, _vp, _vp]
+    L.kore_cuda_seq_truncate.argtypes = [_vp, _i, _i]
+    L.kore_cuda_server_create.argtypes = [ctypes.POINTER(_vp), _vp, _i, _i]
+    L.kore_cuda_server_destroy.argtypes = [_vp]
+    L.kore_cuda_server_destroy.restype = None
+    L.kore_cuda_server_last_error.argtypes = [_vp]
+    L.kore_cuda_server_last_error.restype = ctypes.c_char_p
+    L.kore_cuda_server_open.argtypes = [_vp, _ip]
+    L.kore_cuda_server_close.argtypes = [_vp, _i]
+    L.kore_cuda_server_submit.argtypes = [_vp, _i, _ip, _i, _i]
+    L.kore_cuda_server_step.argtypes = [_vp, ctypes.POINTER(_Event), _i, _ip]
+    L.kore_cuda_server_condense.argtypes = [_vp, _i, _ip, _i]
+    L.kore_cuda_server_history.argtypes = [_vp, _i, _ip, _i]
     L.kore_cuda_sync.argtypes = [_vp]
     L.kore_cuda_set_wait_limit.argtypes = [_vp, ctypes.c_ulonglong]
     L.kore_cuda_stream.argtypes = [_vp]
@@ -237,6 +257,9 @@ class KoreCuda:
 
     def seq_reset(self, seq: int) -> None:
         self._ck(self._L.kore_cuda_seq_reset(self._h, seq))
+
+    def seq_truncate(self, seq: int, n: int) -> None:
+        self._ck(self._L.kore_cuda_seq_truncate(self._h, seq, n))
 
     def seq_len(self, seq: int, layer: int) -> int:
         r = self._L.kore_cuda_seq_len(self._h, seq, layer)
@@ -430,3 +453,61 @@ class KoreCuda:
 
     def attn_block_decode_dev(self, seq: int, layer: int, pos: int, xb, o) -> None:
         self._ck(self._L.kore_cuda_attn_block_decode_dev(self._h, seq, layer, pos, _dptr(xb), _dptr(o)))
+
+
+class Server:
+    """Many chat sessions over one KoreCuda context with its model uploaded
+    (kore_cuda_server_*): kore's ChatSession / prefill() / gen_step() /
+    condense() with every session a sequence of the shared page pool."""
+
+    def __init__(self, ctx: KoreCuda, eos: int = -1, bos: int = -1):
+        self._L = ctx._L
+        self.ctx = ctx
+        h = _vp()
+        rc = self._L.kore_cuda_server_create(ctypes.byref(h), ctx._h, eos, bos)
+        if rc:
+            raise KoreCudaError(rc, self._L.kore_cuda_server_last_error(None).decode())
+        self._h = h
+        self._ev = (_Event * 4096)()
+
+    def _ck(self, rc: int) -> None:
+        if rc:
+            raise KoreCudaError(rc, self._L.kore_cuda_server_last_error(self._h).decode())
+
+    def close(self) -> None:
+        if getattr(self, "_h", None):
+            self._L.kore_cuda_server_destroy(self._h)
+            self._h = None
+
+    def __del__(self):
+        self.close()
+
+    def open(self) -> int:
+        s = ctypes.c_int(-1)
+        self._ck(self._L.kore_cuda_server_open(self._h, ctypes.byref(s)))
+        return s.value
+
+    def close_session(self, session: int) -> None:
+        self._ck(self._L.kore_cuda_server_close(self._h, session))
+
+    def submit(self, session: int, ids, max_new: int = 0) -> None:
+        ids = np.ascontiguousarray(ids, np.int32)
+        self._ck(self._L.kore_cuda_server_submit(self._h, session, ids.ctypes.data_as(_ip), ids.size, max_new))
+
+    def step(self) -> list[tuple[int, int, int]]:
+        """One round: [(session, token, status)] for every session that was generating."""
+        n = ctypes.c_int(0)
+        self._ck(self._L.kore_cuda_server_step(self._h, self._ev, len(self._ev), ctypes.byref(n)))
+        return [(self._ev[i].session, self._ev[i].token, self._ev[i].status) for i in range(n.value)]
+
+    def condense(self, session: int, ids) -> None:
+        ids = np.ascontiguousarray(ids, np.int32)
+        self._ck(self._L.kore_cuda_server_condense(self._h, session, ids.ctypes.data_as(_ip), ids.size))
+
+    def history(self, session: int) -> list[int]:
+        n = self._L.kore_cuda_server_history(self._h, session, None, 0)
+        if n < 0:
+            raise KoreCudaError(n, "session not open")
+        buf = np.zeros(max(n, 1), np.int32)
+        self._L.kore_cuda_server_history(self._h, session, buf.ctypes.data_as(_ip), n)
+        return buf[:n].tolist()

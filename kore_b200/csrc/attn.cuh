@@ -7,6 +7,8 @@
 
 #include <cuda_runtime.h>
 
+struct kore_cuda_ctx;
+
 namespace kore {
 
 constexpr int kMaxBatch = 256;    // queries per decode launch given by (seq, pos) list
@@ -110,6 +112,9 @@ int decode_split_pages_max();
 size_t decode_smem_bytes(int head_dim);
 cudaError_t launch_kv_append(const AppendParams &p, cudaStream_t s);
 void set_ctxless_error(const char *msg);
+// A context's limits for the session server: positions per sequence,
+// sequences, the uploaded model's vocabulary (0 without a model), device.
+bool ctx_limits(const kore_cuda_ctx *c, int *ctx_max, int *max_seqs, int *n_vocab, int *device);
 // The CUDA context current on this thread (the device's primary context
 // unless the caller made another one current), as an opaque key; 0 if none.
 uintptr_t current_cuda_context();

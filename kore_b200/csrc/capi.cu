@@ -134,6 +134,15 @@ thread_local std::string g_create_msg = "no error";
 }  // namespace
 
 namespace kore {
+bool ctx_limits(const kore_cuda_ctx *c, int *ctx_max, int *max_seqs, int *n_vocab, int *device) {
+    if (!c) return false;
+    *ctx_max = c->cfg.ctx_max;
+    *max_seqs = c->cfg.max_seqs;
+    *n_vocab = c->model.ready ? c->model.n_vocab : 0;
+    *device = c->cfg.device;
+    return true;
+}
+
 // Message for calls that have no context (read with kore_cuda_last_error(NULL)).
 void set_ctxless_error(const char *msg) { g_create_msg = msg; }
 
@@ -695,6 +704,30 @@ int kore_cuda_seq_reset(kore_cuda_ctx *c, int seq) {
     for (int l = 0; l < c->cfg.n_layer; ++l) c->seq_len[(size_t)seq * c->cfg.n_layer + l] = 0;
     DeviceGuard dg(c->cfg.device);
     CK(cudaMemcpyAsync(c->pt_d + (size_t)seq * c->pages_per_seq, row, (size_t)c->pages_per_seq * sizeof(int),
+                       cudaMemcpyHostToDevice, c->stream));
+    return KORE_CUDA_OK;
+}
+
+int kore_cuda_seq_truncate(kore_cuda_ctx *c, int seq, int n) {
+    if (!c) return KORE_CUDA_EINVAL;
+    if (seq < 0 || seq >= c->cfg.max_seqs) return fail(c, KORE_CUDA_ERANGE, "seq %d outside [0, %d)", seq, c->cfg.max_seqs);
+    if (n < 0) return fail(c, KORE_CUDA_EINVAL, "n = %d is negative", n);
+    for (int l = 0; l < c->cfg.n_layer; ++l) {
+        int &len = c->seq_len[(size_t)seq * c->cfg.n_layer + l];
+        len = std::min(len, n);
+    }
+    // pages wholly past the kept positions go back to the pool
+    const int keep = local_pages(c, (n + c->P - 1) / c->P);
+    int *row = c->pt_h.data() + (size_t)seq * c->pages_per_seq;
+    if (c->seq_alloc[seq] <= keep) return KORE_CUDA_OK;
+    for (int j = c->seq_alloc[seq] - 1; j >= keep; --j) {
+        c->free_pages.push_back(row[j]);
+        row[j] = -1;
+    }
+    const int had = c->seq_alloc[seq];
+    c->seq_alloc[seq] = keep;
+    DeviceGuard dg(c->cfg.device);
+    CK(cudaMemcpyAsync(c->pt_d + (size_t)seq * c->pages_per_seq + keep, row + keep, (size_t)(had - keep) * sizeof(int),
                        cudaMemcpyHostToDevice, c->stream));
     return KORE_CUDA_OK;
 }

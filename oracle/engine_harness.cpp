@@ -627,4 +627,27 @@ int keng_matmul_batch(void *h, int type, int rows, int cols, const void *data, c
     return 0;
 }
 
+// One turn of kore's chat flow on the harness's engine: prefill() of ids at
+// base (kore.cpp:1720-1737: forward_batch over chunks of e.bsz, the last with
+// logits) and then n_gen of its gen_step()s at temperature 0 (kore.cpp:
+// 1742-1756: sample_token, append, forward() for the next logits). The
+// generated ids go to out. Returns n_gen, or -1 when kore refuses.
+int keng_turn_ref(void *h, const int *ids, int n, int base, int n_gen, int *out) {
+    Harness &hx = *(Harness *)h;
+    Engine &e = hx.e;
+    if (n <= 0 || base + n >= e.ctx) return -1;
+    for (int i = 0; i < n; i += e.bsz) {
+        const int nb = std::min(e.bsz, n - i);
+        if (!forward_batch(e, ids + i, nb, base + i, i + nb == n)) return -1;
+    }
+    int pos = base + n;
+    for (int g = 0; g < n_gen; g++) {
+        std::mt19937 rng(0);
+        const int tok = sample_token(e.logits, 0.0f, 40, rng);
+        out[g] = tok;
+        if (pos >= e.ctx || !forward(e, tok, pos++, true)) return -1;
+    }
+    return n_gen;
+}
+
 }  // extern "C"

@@ -345,6 +345,7 @@ def engine_lib():
         L.keng_generate_cuda_step.argtypes = [vp, ip, ctypes.c_int, ctypes.c_int, ip]
         L.keng_get_row.argtypes = [ctypes.c_int] * 3 + [vp, ctypes.c_int, fp]
         L.keng_forward_batch.argtypes = [vp, ip, ctypes.c_int, ctypes.c_int, fp]
+        L.keng_turn_ref.argtypes = [vp, ip, ctypes.c_int, ctypes.c_int, ctypes.c_int, ip]
         L.keng_matmul_batch.argtypes = [vp] + [ctypes.c_int] * 3 + [vp, fp, ctypes.c_int, fp]
         L.keng_forward.argtypes = [vp, ctypes.c_int, ctypes.c_int, fp]
         L.keng_tensor.argtypes = [vp, ctypes.c_char_p, ip, ip, ip]
@@ -445,13 +446,28 @@ class GreedyEngine:
             raise RuntimeError("kore forward_batch() refused the tokens or positions")
         return out
 
+    def turn_ref(self, ids, base: int, n_gen: int) -> list[int]:
+        """kore's prefill() of ids at base, then n_gen greedy gen_step()s: the generated ids."""
+        t = np.ascontiguousarray(ids, np.int32)
+        out = np.zeros(max(n_gen, 1), np.int32)
+        ip = ctypes.POINTER(ctypes.c_int)
+        if engine_lib().keng_turn_ref(self.h, t.ctypes.data_as(ip), t.size, base, n_gen, out.ctypes.data_as(ip)) != n_gen:
+            raise RuntimeError("kore refused the turn")
+        return out[:n_gen].tolist()
+
     def matmul_batch_ref(self, m, x: np.ndarray) -> np.ndarray:
         """kore's matmul_batch_float of rows x [B][cols] with matrix m (.type .rows .cols, .data or .addr)."""
         x = np.ascontiguousarray(x, np.float32)
         out = np.empty((x.shape[0], m.rows), np.float32)
         addr = getattr(m, "addr", None)
         addr = addr if addr is not None else m.data.ctypes.data
-        engine_lib().keng_matmul_batch(self.h, m.type, m.rows, m.cols, addr, _fp(x), x.shape[0], _fp(out))
+        # kore's kernel takes at most KORE_BMAX = 64 rows at a time (kore.cpp:690); every
+        # output row depends on its own input row only
+        for b0 in range(0, x.shape[0], 64):
+            xs = np.ascontiguousarray(x[b0:b0 + 64])
+            os_ = np.empty((xs.shape[0], m.rows), np.float32)
+            engine_lib().keng_matmul_batch(self.h, m.type, m.rows, m.cols, addr, _fp(xs), xs.shape[0], _fp(os_))
+            out[b0:b0 + xs.shape[0]] = os_
         return out
 
     def tensor(self, name: str):

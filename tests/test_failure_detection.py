@@ -54,8 +54,12 @@ def test_tile_wait_limit_expires_then_the_context_recovers():
     assert seen.code == -6 and "K/V tile" in str(seen), str(seen)
     g.set_wait_limit(0)             # back to the default
     g.sync()                        # the error was reported once and cleared
+    want = o.decode(pos, q1, k1, v1)
     got = g.decode(0, 0, pos, q1, k1, v1)
-    assert_attn_close(got, o.decode(pos, q1, k1, v1), "decode after a timed-out call")
+    assert_attn_close(got, want, "decode after a timed-out call")
+    kr, vr = g.kv_read(0, 0, pos - 3, 4)   # the cache around the appended row is intact
+    np.testing.assert_array_equal(kr, o.kc[pos - 3:pos + 1])
+    np.testing.assert_array_equal(vr, o.vc[pos - 3:pos + 1])
     g.close()
 
 
