@@ -120,7 +120,11 @@ int kore_cuda_kv_append_dev(kore_cuda_ctx *ctx, int seq, int layer, int pos0, in
  * 0..pos0+z for query row z.
  *   q: [n][n_head*head_dim], k, v: [n][n_head_kv*head_dim]   (pre-RoPE)
  *   out: [n][n_head*head_dim]                                 (e.batt rows)
- * n is not limited to kore's 64-token batch (KORE_BMAX, kore.cpp:690).
+ * n is not limited to kore's 64-token batch (KORE_BMAX, kore.cpp:690). On a
+ * context with shard_count > 1 (after kore_cuda_peer_open; every rank makes
+ * the same call) each rank stores the rows of its own pages, attends the
+ * queries over its own positions, and the partials are merged over NVLink
+ * peer memory as the sharded decode merges them; every rank gets all of out.
  */
 int kore_cuda_attn_prefill(kore_cuda_ctx *ctx, int seq, int layer, int pos0, int n,
                            const float *q, const float *k, const float *v, float *out);
@@ -362,6 +366,15 @@ int kore_cuda_server_history(const kore_cuda_server *srv, int session, int *ids,
 int kore_cuda_attn_decode_partial_dev(kore_cuda_ctx *ctx, int seq, int layer, int pos,
                                       const float *q, const float *k, const float *v, float *part);
 int kore_cuda_lse_merge_dev(kore_cuda_ctx *ctx, int n_parts, const float *parts, float *out);
+/* The same for a prefill chunk (kore.cpp:1527-1563): the owner of each of
+ * positions pos0..pos0+n-1 appends its k/v, and `part` receives this shard's
+ * causal partial of the n queries, outputs [n][n_head*head_dim] then
+ * log2-domain LSEs [n][n_head] (n <= 256). kore_cuda_lse_merge_batch_dev
+ * merges n_parts such partials of n_q queries (one after another) into out
+ * [n_q][n_head*head_dim]. */
+int kore_cuda_attn_prefill_partial_dev(kore_cuda_ctx *ctx, int seq, int layer, int pos0, int n,
+                                       const float *q, const float *k, const float *v, float *part);
+int kore_cuda_lse_merge_batch_dev(kore_cuda_ctx *ctx, int n_parts, int n_q, const float *parts, float *out);
 
 /*
  * The same split with the exchange done by this library over NVLink peer

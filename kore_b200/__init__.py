@@ -141,6 +141,8 @@ def load_library(path: str = LIB):
         getattr(L, n).argtypes = [_vp, _i, _i, _ip, _ip, _vp, _vp, _vp, _vp]
     L.kore_cuda_attn_decode_partial_dev.argtypes = [_vp, _i, _i, _i, _vp, _vp, _vp, _vp]
     L.kore_cuda_lse_merge_dev.argtypes = [_vp, _i, _vp, _vp]
+    L.kore_cuda_attn_prefill_partial_dev.argtypes = [_vp, _i, _i, _i, _i, _vp, _vp, _vp, _vp]
+    L.kore_cuda_lse_merge_batch_dev.argtypes = [_vp, _i, _i, _vp, _vp]
     L.kore_cuda_peer_handle.argtypes = [_vp, ctypes.c_char_p]
     L.kore_cuda_peer_open.argtypes = [_vp, ctypes.c_char_p]
     L.kore_cuda_attn_decode_sharded_dev.argtypes = [_vp, _i, _i, _i, _vp, _vp, _vp, _vp]
@@ -334,6 +336,14 @@ class KoreCuda:
 
     def lse_merge_dev(self, n_parts: int, parts, out) -> None:
         self._ck(self._L.kore_cuda_lse_merge_dev(self._h, n_parts, _dptr(parts), _dptr(out)))
+
+    def prefill_partial_dev(self, seq: int, layer: int, pos0: int, n: int, q, k, v, part) -> None:
+        """KV-sharded prefill chunk: this shard's partial, outputs [n][H*d] then LSEs [n][H]."""
+        self._ck(self._L.kore_cuda_attn_prefill_partial_dev(self._h, seq, layer, pos0, n, _dptr(q), _dptr(k), _dptr(v),
+                                                            _dptr(part)))
+
+    def lse_merge_batch_dev(self, n_parts: int, n_q: int, parts, out) -> None:
+        self._ck(self._L.kore_cuda_lse_merge_batch_dev(self._h, n_parts, n_q, _dptr(parts), _dptr(out)))
 
     PEER_HANDLE_BYTES = 64
 

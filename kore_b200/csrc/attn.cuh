@@ -85,22 +85,38 @@ struct PrefillParams {
     int n_items;
 };
 
-// One layer's cross-GPU exchange of KV-sharded decode partials (peer_exchange.cu).
-// Exchange buffer of each rank (bytes): slots [2 parities][n_ranks][H*D + H]
-// floats, then at flag_off flags [2][n_ranks][H] u32, then at epoch_off the
-// per-head epochs [H] u32; all zero at creation.
+// Query slots of a rank's exchange buffer: one decode step uses one, a
+// prefill chunk on a KV-split context is exchanged in pieces of this many.
+constexpr int kExchangeQueries = 64;
+
+// Positions of query `pos` that a shard holds (as PagedKv's page split) and
+// the number of splits its decode runs over them (at least 1): the count the
+// decode kernel, its split merge and the exchange all derive the same way.
+__host__ __device__ inline int shard_count_below(int limit, int P, int NS, int rank) {
+    const int F = limit / P, rem = limit - F * P;
+    const int nfull_local = F > rank ? (F - rank + NS - 1) / NS : 0;
+    return nfull_local * P + ((F % NS == rank) ? rem : 0);
+}
+
+// One layer's cross-GPU exchange of KV-sharded decode partials (peer_exchange.cu),
+// for n_q consecutive queries (positions pos0 + i).
+// Exchange buffer of each rank: (value, epoch) words [2 parities][n_ranks]
+// [kExchangeQueries][H][D + 1] u64 at 0, the epochs [kExchangeQueries][H] u32
+// at epoch_off; all zero at creation.
 struct ExchangeParams {
-    const float *local;            // this rank's packed partial [H*D outputs][H lse] (one split)
-    const float *part_o;           // or its splits, merged here when n_splits > 1
-    const float2 *part_ml;         //   (decode split scratch of query 0)
-    int n_splits, max_splits, n_rep;
+    const float *local;            // this rank's partials: outputs [kExchangeQueries][H*D], then
+                                   //   log2-domain LSEs [kExchangeQueries][H] (queries with one split)
+    const float *part_o;           // or their splits, merged here (decode split scratch)
+    const float2 *part_ml;
+    int max_splits, split_tokens, n_rep;
+    int pos0, append_new, P;       // the queries' positions and how the decode counted them
     float *own;                    // this rank's exchange buffer
     float *peers[kMaxRanks];       // every rank's exchange buffer as mapped here (own included)
-    size_t epoch_off;              // per-head epochs in `own`; the (value, epoch) slots start at 0
-    float *out;                    // merged output [H*D]
+    size_t epoch_off;              // per-(query, head) epochs in `own`
+    float *out;                    // merged outputs [n_q][H*D]
     int *err;
     unsigned long long wait_ns;    // limit of the wait for a peer's partial (then DEV_PEER_TIMEOUT)
-    int n_ranks, rank, H, D;
+    int n_ranks, rank, H, D, n_q;
 };
 
 // Launch helpers (attn_decode.cu, kv_append.cu). Return cudaGetLastError().
@@ -215,6 +231,8 @@ int prefill_plan(int pos0, int n, int H, int num_sms, std::vector<int4> &items);
 int prefill_tile_keys();
 cudaError_t launch_prefill(const PrefillParams &p, cudaStream_t s);
 cudaError_t launch_peer_exchange(const ExchangeParams &p, cudaStream_t s);
-cudaError_t launch_lse_merge(const float *parts, int n_parts, int H, int D, float *out, cudaStream_t s);
+// Merges n_parts partials of n_q queries each (part r: outputs [n_q][H*D]
+// then LSEs [n_q][H], parts one after another) into out [n_q][H*D].
+cudaError_t launch_lse_merge(const float *parts, int n_parts, int n_q, int H, int D, float *out, cudaStream_t s);
 
 }  // namespace kore

@@ -231,9 +231,7 @@ __global__ void __launch_bounds__(NW * 32, 1) attn_decode_kernel(const __grid_co
 
     // cached positions read here: [0, limit) of those this shard holds
     const int limit = p.append_new ? pos : pos + 1;
-    const int F = limit / P, rem = limit - F * P;
-    const int nfull_local = F > rank ? (F - rank + NS - 1) / NS : 0;
-    const int count = nfull_local * P + ((F % NS == rank) ? rem : 0);
+    const int count = shard_count_below(limit, P, NS, rank);
     const bool own_new = p.append_new && ((pos / P) % NS == rank);
     const int ST = p.split_tokens;
     int n_splits = (count + ST - 1) / ST;
@@ -469,10 +467,7 @@ __global__ void __launch_bounds__(D) split_merge_kernel(const __grid_constant__ 
     const int pos = p.contiguous ? p.pos0 + qi : p.pos[qi];
     const PagedKv &kv = p.kv;
     const int P = kv.P, NS = kv.shard_count, rank = kv.shard_rank;
-    const int limit = p.append_new ? pos : pos + 1;
-    const int F = limit / P, rem = limit - F * P;
-    const int nfull_local = F > rank ? (F - rank + NS - 1) / NS : 0;
-    const int count = nfull_local * P + ((F % NS == rank) ? rem : 0);
+    const int count = shard_count_below(p.append_new ? pos : pos + 1, P, NS, rank);
     const int n_splits = (count + p.split_tokens - 1) / p.split_tokens;
     if (n_splits <= 1) return;   // the decode kernel wrote this output directly
     const size_t base = ((size_t)qi * kv.G + g) * p.max_splits;

@@ -393,7 +393,7 @@ int run_append(kore_cuda_ctx *c, int seq, int layer, int pos0, int n, const floa
 // (seq0, pos0 + i); otherwise seqs[i], poss[i] (host arrays, n_q <= kMaxBatch).
 int run_decode(kore_cuda_ctx *c, int layer, int n_q, bool contiguous, int seq0, int pos0, const int *seqs,
                const int *poss, const float *q, const float *k, const float *v, float *out, float *lse,
-               bool append_new, bool launch_merge = true, int *grid_out = nullptr) {
+               bool append_new, bool launch_merge = true, int *grid_out = nullptr, int *st_out = nullptr) {
     if (n_q <= 0) return fail(c, KORE_CUDA_EINVAL, "no queries");
     if (!contiguous && n_q > kMaxBatch)
         return fail(c, KORE_CUDA_EINVAL, "decode batch of %d exceeds %d sequences per call", n_q, kMaxBatch);
@@ -526,6 +526,7 @@ int run_decode(kore_cuda_ctx *c, int layer, int n_q, bool contiguous, int seq0, 
     }
     CK(launch_attn_decode(p, c->R, grid_x, c->stream, launch_merge));
     if (grid_out) *grid_out = grid_x;
+    if (st_out) *st_out = (int)st;
     // the decode (and its split merge, which lets the next kernel start at
     // once) may still run when the next kernel starts: it wrote this layer's KV
     c->last_kv_layer = append_new ? layer : -1;
@@ -762,13 +763,20 @@ int kore_cuda_kv_append(kore_cuda_ctx *c, int seq, int layer, int pos0, int n, c
     return finish(c);
 }
 
+static int prefill_sharded(kore_cuda_ctx *c, int seq, int layer, int pos0, int n, const float *q, const float *k,
+                           const float *v, float *out);
+
 int kore_cuda_attn_prefill_dev(kore_cuda_ctx *c, int seq, int layer, int pos0, int n, const float *q, const float *k,
                                const float *v, float *out) {
     if (!c) return KORE_CUDA_EINVAL;
     if (!q || !k || !v || !out) return fail(c, KORE_CUDA_EINVAL, "null q, k, v or out");
-    if (c->NS > 1) return fail(c, KORE_CUDA_EINVAL, "prefill on a KV-sharded context is not supported");
     if (int rc = check_range(c, seq, layer, pos0, n)) return rc;
     DeviceGuard dg(c->cfg.device);
+    if (c->NS > 1) {
+        if ((reinterpret_cast<uintptr_t>(q) | reinterpret_cast<uintptr_t>(out)) & 15)
+            return fail(c, KORE_CUDA_EINVAL, "q and out must be 16-byte aligned device buffers");
+        return prefill_sharded(c, seq, layer, pos0, n, q, k, v, out);
+    }
     if (int rc = ensure_pages(c, seq, pos0 + n)) return rc;
     if (int rc = run_append(c, seq, layer, pos0, n, k, v)) return rc;
     note_len(c, seq, layer, pos0 + n);
@@ -901,7 +909,7 @@ int kore_cuda_lse_merge_dev(kore_cuda_ctx *c, int n_parts, const float *parts, f
     if (!c) return KORE_CUDA_EINVAL;
     if (!parts || !out || n_parts <= 0) return fail(c, KORE_CUDA_EINVAL, "bad merge arguments");
     DeviceGuard dg(c->cfg.device);
-    CK(launch_lse_merge(parts, n_parts, c->H, c->D, out, c->stream));
+    CK(launch_lse_merge(parts, n_parts, 1, c->H, c->D, out, c->stream));
     return KORE_CUDA_OK;
 }
 
@@ -913,11 +921,12 @@ int kore_cuda_peer_handle(kore_cuda_ctx *c, void *handle) {
         return fail(c, KORE_CUDA_EINVAL, "peer exchange needs 2..%d shards (context has %d)", kMaxRanks, c->NS);
     DeviceGuard dg(c->cfg.device);
     if (!c->xbuf) {
-        // [2 parity sets][rank][head][head_dim + 1] (value, epoch) pairs, the
-        // per-head epochs, this rank's own partial
-        const size_t PF = (size_t)c->H * c->D + c->H;
-        c->x_epoch_off = align256(2 * (size_t)c->NS * c->H * (c->D + 1) * 2 * sizeof(unsigned));
-        c->x_local_off = c->x_epoch_off + align256((size_t)c->H * sizeof(unsigned));
+        // [2 parity sets][rank][query slot][head][head_dim + 1] (value, epoch)
+        // words, the per-(query slot, head) epochs, this rank's own partials
+        const size_t Q = kExchangeQueries;
+        const size_t PF = Q * ((size_t)c->H * c->D + c->H);
+        c->x_epoch_off = align256(2 * (size_t)c->NS * Q * c->H * (c->D + 1) * sizeof(unsigned long long));
+        c->x_local_off = c->x_epoch_off + align256(Q * c->H * sizeof(unsigned));
         c->x_bytes = c->x_local_off + align256(PF * sizeof(float));
         CK(cudaMalloc(&c->xbuf, c->x_bytes));
         CK(cudaMemset(c->xbuf, 0, c->x_bytes));
@@ -950,28 +959,21 @@ int kore_cuda_peer_open(kore_cuda_ctx *c, const void *handles) {
     return KORE_CUDA_OK;
 }
 
-int kore_cuda_attn_decode_sharded_dev(kore_cuda_ctx *c, int seq, int layer, int pos, const float *q, const float *k,
-                                      const float *v, float *out) {
-    if (!c) return KORE_CUDA_EINVAL;
-    if (!q || !k || !v || !out) return fail(c, KORE_CUDA_EINVAL, "null q, k, v or out");
-    if (!c->peers_open) return fail(c, KORE_CUDA_ESTATE, "peer exchange not set up (kore_cuda_peer_open)");
-    if (int rc = check_range(c, seq, layer, pos, 1)) return rc;
-    DeviceGuard dg(c->cfg.device);
-    if (int rc = ensure_pages(c, seq, pos + 1)) return rc;
-    float *local = reinterpret_cast<float *>(reinterpret_cast<char *>(c->xbuf) + c->x_local_off);
-    int n_splits = 1;   // the splits are merged by the exchange kernel itself
-    if (int rc = run_decode(c, layer, 1, true, seq, pos, nullptr, nullptr, q, k, v, local,
-                            local + (size_t)c->H * c->D, true, false, &n_splits))
-        return rc;
-    note_len(c, seq, layer, pos + 1);
+// One exchange (peer_exchange.cu) of n_q consecutive queries' partials left
+// by run_decode (grid_x splits, not merged) in the local slots.
+static int launch_exchange(kore_cuda_ctx *c, int n_q, int pos0, bool append_new, int grid_x, int split_tokens,
+                           float *out) {
     ExchangeParams xp;
     memset(&xp, 0, sizeof xp);
-    xp.local = local;
+    xp.local = reinterpret_cast<float *>(reinterpret_cast<char *>(c->xbuf) + c->x_local_off);
     xp.part_o = c->part_o;
     xp.part_ml = c->part_ml;
-    xp.n_splits = n_splits;
-    xp.max_splits = n_splits;
+    xp.max_splits = grid_x;
+    xp.split_tokens = split_tokens;
     xp.n_rep = c->R;
+    xp.pos0 = pos0;
+    xp.append_new = append_new ? 1 : 0;
+    xp.P = c->P;
     xp.own = c->xbuf;
     for (int r = 0; r < c->NS; ++r) xp.peers[r] = c->peers[r];
     xp.epoch_off = c->x_epoch_off;
@@ -982,9 +984,78 @@ int kore_cuda_attn_decode_sharded_dev(kore_cuda_ctx *c, int seq, int layer, int 
     xp.rank = c->rank;
     xp.H = c->H;
     xp.D = c->D;
+    xp.n_q = n_q;
     CK(launch_peer_exchange(xp, c->stream));
+    return KORE_CUDA_OK;
+}
+
+int kore_cuda_attn_decode_sharded_dev(kore_cuda_ctx *c, int seq, int layer, int pos, const float *q, const float *k,
+                                      const float *v, float *out) {
+    if (!c) return KORE_CUDA_EINVAL;
+    if (!q || !k || !v || !out) return fail(c, KORE_CUDA_EINVAL, "null q, k, v or out");
+    if (!c->peers_open) return fail(c, KORE_CUDA_ESTATE, "peer exchange not set up (kore_cuda_peer_open)");
+    if (int rc = check_range(c, seq, layer, pos, 1)) return rc;
+    DeviceGuard dg(c->cfg.device);
+    if (int rc = ensure_pages(c, seq, pos + 1)) return rc;
+    float *local = reinterpret_cast<float *>(reinterpret_cast<char *>(c->xbuf) + c->x_local_off);
+    int grid_x = 1, st = 0;   // the splits are merged by the exchange kernel itself
+    if (int rc = run_decode(c, layer, 1, true, seq, pos, nullptr, nullptr, q, k, v, local,
+                            local + (size_t)kExchangeQueries * c->H * c->D, true, false, &grid_x, &st))
+        return rc;
+    note_len(c, seq, layer, pos + 1);
+    if (int rc = launch_exchange(c, 1, pos, true, grid_x, st, out)) return rc;
     c->last_kv_layer = layer;   // the decode may still run when the next kernel starts
     c->hold_prefetch = !c->shard_prefetch;
+    return KORE_CUDA_OK;
+}
+
+// A prefill chunk on a KV-split context: every rank stores the chunk's rows
+// of the pages it holds, attends the chunk's queries over its own positions
+// (the split decode kernel, one query per position, causal by its count) and
+// the exchange merges the ranks' partials, kExchangeQueries queries at a time.
+static int prefill_sharded(kore_cuda_ctx *c, int seq, int layer, int pos0, int n, const float *q, const float *k,
+                           const float *v, float *out) {
+    if (!c->peers_open)
+        return fail(c, KORE_CUDA_ESTATE, "a KV-split context needs kore_cuda_peer_open before a prefill");
+    if (int rc = ensure_pages(c, seq, pos0 + n)) return rc;
+    if (int rc = run_append(c, seq, layer, pos0, n, k, v)) return rc;
+    note_len(c, seq, layer, pos0 + n);
+    float *local = reinterpret_cast<float *>(reinterpret_cast<char *>(c->xbuf) + c->x_local_off);
+    for (int z0 = 0; z0 < n; z0 += kExchangeQueries) {
+        const int m = std::min(kExchangeQueries, n - z0);
+        const float *qz = q + (size_t)z0 * c->H * c->D;
+        int grid_x = 1, st = 0;
+        if (int rc = run_decode(c, layer, m, true, seq, pos0 + z0, nullptr, nullptr, qz, qz, qz, local,
+                                local + (size_t)kExchangeQueries * c->H * c->D, false, false, &grid_x, &st))
+            return rc;
+        if (int rc = launch_exchange(c, m, pos0 + z0, false, grid_x, st, out + (size_t)z0 * c->H * c->D)) return rc;
+    }
+    c->last_kv_layer = layer;
+    c->hold_prefetch = !c->shard_prefetch;
+    return KORE_CUDA_OK;
+}
+
+int kore_cuda_attn_prefill_partial_dev(kore_cuda_ctx *c, int seq, int layer, int pos0, int n, const float *q,
+                                       const float *k, const float *v, float *part) {
+    if (!c) return KORE_CUDA_EINVAL;
+    if (!q || !k || !v || !part) return fail(c, KORE_CUDA_EINVAL, "null q, k, v or part");
+    if (int rc = check_range(c, seq, layer, pos0, n)) return rc;
+    if (n > kMaxBatch) return fail(c, KORE_CUDA_EINVAL, "a partial prefill takes at most %d queries", kMaxBatch);
+    DeviceGuard dg(c->cfg.device);
+    if (int rc = ensure_pages(c, seq, pos0 + n)) return rc;
+    if (int rc = run_append(c, seq, layer, pos0, n, k, v)) return rc;
+    note_len(c, seq, layer, pos0 + n);
+    if (int rc = run_decode(c, layer, n, true, seq, pos0, nullptr, nullptr, q, q, q, part,
+                            part + (size_t)n * c->H * c->D, false))
+        return rc;
+    return KORE_CUDA_OK;
+}
+
+int kore_cuda_lse_merge_batch_dev(kore_cuda_ctx *c, int n_parts, int n_q, const float *parts, float *out) {
+    if (!c) return KORE_CUDA_EINVAL;
+    if (!parts || !out || n_parts <= 0 || n_q <= 0) return fail(c, KORE_CUDA_EINVAL, "bad merge arguments");
+    DeviceGuard dg(c->cfg.device);
+    CK(launch_lse_merge(parts, n_parts, n_q, c->H, c->D, out, c->stream));
     return KORE_CUDA_OK;
 }
 
@@ -1543,7 +1614,8 @@ int kore_cuda_prefill(kore_cuda_ctx *c, int seq, const int *tokens, int n, int p
     if (!tokens || !next_token || n <= 0) return fail(c, KORE_CUDA_EINVAL, "null tokens or next_token, or n <= 0");
     if (!c->model.ready || c->proj.size() != (size_t)c->cfg.n_layer)
         return fail(c, KORE_CUDA_ESTATE, "no model on the device (kore_cuda_set_model)");
-    if (c->NS > 1) return fail(c, KORE_CUDA_EINVAL, "prefill on a KV-sharded context is not supported");
+    if (c->NS > 1 && !c->peers_open)
+        return fail(c, KORE_CUDA_ESTATE, "a KV-split context needs kore_cuda_peer_open before a prefill");
     for (int l = 0; l < c->cfg.n_layer; ++l)
         if (int rc = check_range(c, seq, l, pos0, n)) return rc;
     auto &M = c->model;

@@ -79,7 +79,12 @@ __device__ __forceinline__ bool mbar_wait(uint64_t *bar, uint32_t parity, int *e
     if (mbar_try_wait(bar, parity)) return true;
     const uint64_t t0 = global_ns();
     for (uint32_t it = 1; it < kWaitPolls; ++it) {
-        if (mbar_try_wait(bar, parity)) return true;
+        // a try_wait may itself suspend until the phase completes: a wait that
+        // ends after its limit counts as expired even if the copy landed
+        if (mbar_try_wait(bar, parity)) {
+            if (global_ns() - t0 <= limit_ns) return true;
+            break;
+        }
         if ((it & 7) == 0 && global_ns() - t0 > limit_ns) break;
     }
     raise_error(err, code);

@@ -8,8 +8,9 @@
 // performs, regrouped by shard. Shards holding none of a head's positions
 // carry L_r = -inf and weigh nothing.
 //
-// Packed layout of a partial: [H*D floats of O][H floats of L], so that one
-// all-gather moves a rank's whole contribution.
+// Packed layout of a partial of n_q queries: [n_q][H*D] floats of O, then
+// [n_q][H] floats of L, so that one all-gather moves a rank's whole
+// contribution.
 
 #include "attn.cuh"
 #include "common.cuh"
@@ -17,28 +18,32 @@
 namespace kore {
 namespace {
 
-__global__ void lse_merge_kernel(const float *__restrict__ parts, int n_parts, int H, int D, float *__restrict__ out) {
-    const int h = blockIdx.x;
-    const size_t stride = (size_t)H * D + H;
+__global__ void lse_merge_kernel(const float *__restrict__ parts, int n_parts, int n_q, int H, int D,
+                                 float *__restrict__ out) {
+    const int h = blockIdx.x, qi = blockIdx.y;
+    const size_t stride = (size_t)n_q * ((size_t)H * D + H);          // one part
+    const size_t o_off = (size_t)qi * H * D + (size_t)h * D;          // this (query, head) in a part
+    const size_t l_off = (size_t)n_q * H * D + (size_t)qi * H + h;
     float M = -INFINITY;
-    for (int r = 0; r < n_parts; ++r) M = fmaxf(M, parts[r * stride + (size_t)H * D + h]);
+    for (int r = 0; r < n_parts; ++r) M = fmaxf(M, parts[r * stride + l_off]);
     for (int i = threadIdx.x; i < D; i += blockDim.x) {
         float acc = 0.f, wsum = 0.f;
         if (M != -INFINITY) {
             for (int r = 0; r < n_parts; ++r) {
-                const float w = fast_exp2(parts[r * stride + (size_t)H * D + h] - M);
+                const float w = fast_exp2(parts[r * stride + l_off] - M);
                 wsum += w;
-                acc = fmaf(w, parts[r * stride + (size_t)h * D + i], acc);
+                acc = fmaf(w, parts[r * stride + o_off + i], acc);
             }
         }
-        out[(size_t)h * D + i] = wsum > 0.f ? acc / wsum : 0.f;
+        out[o_off + i] = wsum > 0.f ? acc / wsum : 0.f;
     }
 }
 
 }  // namespace
 
-cudaError_t launch_lse_merge(const float *parts, int n_parts, int H, int D, float *out, cudaStream_t s) {
-    lse_merge_kernel<<<H, D, 0, s>>>(parts, n_parts, H, D, out);
+cudaError_t launch_lse_merge(const float *parts, int n_parts, int n_q, int H, int D, float *out, cudaStream_t s) {
+    if (n_q <= 0 || n_q > 65535) return cudaErrorInvalidValue;
+    lse_merge_kernel<<<dim3(H, n_q), D, 0, s>>>(parts, n_parts, n_q, H, D, out);
     return cudaGetLastError();
 }
 

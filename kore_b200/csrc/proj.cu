@@ -50,11 +50,13 @@
 // AVX2 lane k over half h of the blocks of each chunk, and the second half's
 // lane continues the first half's fused multiply-add chains (one shuffle
 // each way per chunk), so the float order stays kore's. Rows are streamed in
-// chunks of kChunk blocks through a ring of stages per warp (one bulk copy
-// per row and chunk, mbarrier completion), refilled as soon as a chunk has
-// been consumed and running on into the warp's next group, so long rows (the
-// 18944-wide down projection) fit and every warp keeps several copies in
-// flight. The first stages are issued before the kernel waits for its
+// chunks (a whole row of up to 16 blocks, else 8 blocks) through a ring of
+// stages per warp (one bulk copy per row and chunk, issued by the row's first
+// lane, mbarrier completion), refilled as soon as a chunk has been consumed
+// and running on into the warp's next group, so long rows (the 18944-wide
+// down projection) fit and every warp keeps several copies in flight. A
+// launch whose matrices share one block format runs a kernel compiled for
+// that format alone. The first stages are issued before the kernel waits for its
 // predecessor (programmatic dependent launch): weights do not depend on it.
 // Meanwhile every CTA builds the Q8_K input in shared memory itself (14 KB
 // at 7B, 28 KB for the feed-forward width: cheaper than a kernel boundary),
@@ -68,11 +70,12 @@
 
 #include <cuda_fp16.h>
 
+#include <type_traits>
+
 namespace kore {
 namespace {
 
 constexpr int kWarps = 16;   // warps per CTA (one CTA per SM)
-constexpr int kChunk = 8;    // blocks of a row per ring stage
 constexpr unsigned FULLW = 0xffffffffu;
 
 __device__ __forceinline__ float half_bits(uint32_t h) { return __half2float(__ushort_as_half((unsigned short)h)); }
@@ -316,10 +319,15 @@ __device__ __forceinline__ int group_row(const QMatvecParams &p, int gg, int rr,
     return s;
 }
 
+// One product launch. TYPES: 12 or 14 when every segment is Q4_K or Q6_K
+// (the kernel then carries one format's code only), 0 for a mix (each group
+// lies in one segment, so the branch is uniform over a warp). CB: blocks of
+// a row per ring stage.
+template <int TYPES, int CB>
 __global__ void __launch_bounds__(32 * kWarps) qmatvec_kernel(const __grid_constant__ QMatvecParams p) {
     extern __shared__ __align__(16) uint8_t smem[];
     const int nb = p.cols / 256, S = p.stages;
-    const int n_chunks = (nb + kChunk - 1) / kChunk;
+    const int n_chunks = (nb + CB - 1) / CB;
     uint64_t *bars = reinterpret_cast<uint64_t *>(smem);                                  // [kWarps][S]
     unsigned long long *wkeys = reinterpret_cast<unsigned long long *>(bars + kWarps * S);   // [kWarps]
     double *red = reinterpret_cast<double *>(wkeys + kWarps);                            // [kWarps]
@@ -350,36 +358,45 @@ __global__ void __launch_bounds__(32 * kWarps) qmatvec_kernel(const __grid_const
     }
     __syncwarp();
 
-    // byte range of (segment, row)'s blocks [c0, c0 + cb) and its 16-aligned start
-    auto row_src = [&](int sg, int row, int c0, int cb, uintptr_t &a0, uint32_t &bytes) -> uint32_t {
+    // The byte range of row rr of group gg, chunk c: its 16-aligned start and
+    // the copy's length (0 when the group has no such row).
+    auto chunk_src = [&](int gg, int r, int c, uintptr_t &a0, uint32_t &bytes) -> uint32_t {
+        int row;
+        const int sg = group_row(p, gg, r, total_rows, row);
+        if (sg < 0) {
+            bytes = 0;
+            return 0;
+        }
         const QSeg &q = p.seg[sg];
-        const size_t BB = q.type == 12 ? 144 : 210;
+        const size_t BB = TYPES == 12 ? 144 : (TYPES == 14 ? 210 : (q.type == 12 ? 144 : 210));
+        const int c0 = c * CB, cb = min(CB, nb - c0);
         const uintptr_t a = reinterpret_cast<uintptr_t>(q.w) + ((size_t)row * nb + c0) * BB;
         a0 = a & ~uintptr_t(15);
         bytes = (uint32_t)(((a - a0) + cb * BB + 15) & ~uintptr_t(15));
         return (uint32_t)(a - a0);
     };
-    // bulk copies of item it (both rows of its group, one chunk), lane 0 only
+    // bulk copies of item it: lane 0 arms the stage's barrier with both rows'
+    // bytes, then lanes 0 and 16 each copy their row's chunk
     auto issue = [&](int it) {
-        const int gg = gg0 + (it / n_chunks) * TW, c = it % n_chunks;
-        const int c0 = c * kChunk, cb = min(kChunk, nb - c0);
-        const int s = it % S;
-        uintptr_t a0[2];
-        uint32_t by[2] = {0, 0};
-        for (int r = 0; r < 2; ++r) {
-            int row;
-            const int sg = group_row(p, gg, r, total_rows, row);
-            if (sg >= 0) row_src(sg, row, c0, cb, a0[r], by[r]);
+        const int gg = gg0 + (it / n_chunks) * TW, c = it % n_chunks, s = it % S;
+        uintptr_t a0 = 0, b0 = 0;
+        uint32_t by = 0, by_other = 0;
+        if ((lane & 15) == 0) {
+            chunk_src(gg, rr, c, a0, by);
+            chunk_src(gg, rr ^ 1, c, b0, by_other);
+            if (lane == 0) {
+                fence_proxy_async_smem();
+                mbar_arrive_expect_tx(mybar + s, by + by_other);
+            }
         }
-        fence_proxy_async_smem();
-        mbar_arrive_expect_tx(mybar + s, by[0] + by[1]);
-        for (int r = 0; r < 2; ++r)
-            if (by[r])
-                bulk_g2s_plain(myslots + s * stage_bytes + (size_t)r * p.row_slot, reinterpret_cast<const void *>(a0[r]),
-                               by[r], mybar + s);
+        __syncwarp();
+        if ((lane & 15) == 0 && by) {
+            if (lane == 16) fence_proxy_async_smem();
+            bulk_g2s_plain(myslots + s * stage_bytes + (size_t)rr * p.row_slot, reinterpret_cast<const void *>(a0), by,
+                           mybar + s);
+        }
     };
-    if (lane == 0)
-        for (int it = 0; it < S && it < n_items; ++it) issue(it);
+    for (int it = 0; it < S && it < n_items; ++it) issue(it);
     grid_dep_wait();
 
     // ------------------------------------------------------------ the Q8_K input
@@ -404,70 +421,70 @@ __global__ void __launch_bounds__(32 * kWarps) qmatvec_kernel(const __grid_const
     // ------------------------------------------------------------ the rows
     unsigned long long best = 0;   // argmax key of this lane's rows (QOUT_ARGMAX)
     float acc = 0.f, accm = 0.f;
-    for (int it = 0; it < n_items; ++it) {
-        const int s = it % S;
-        if (!__all_sync(FULLW, mbar_wait(mybar + s, (it / S) & 1, p.err, DEV_WAIT_FULL_TIMEOUT))) {
-            // gave up (recorded): let the copies still in flight land first
-            for (int t = it; t < n_items && t < it + S; ++t) mbar_drain(mybar + t % S, (t / S) & 1);
-            break;
-        }
-        const int gg = gg0 + (it / n_chunks) * TW, c = it % n_chunks;
-        const int c0 = c * kChunk, cb = min(kChunk, nb - c0), half0 = (cb + 1) >> 1;
+    int it = 0;
+    for (int t = 0; t < my_groups; ++t) {
+        const int gg = gg0 + t * TW;
         int row;
         const int sg = group_row(p, gg, rr, total_rows, row);
         const bool valid = sg >= 0;
-        const bool q4 = valid && p.seg[sg].type == 12;
-        uintptr_t a0;
-        uint32_t by;
-        const uint32_t delta = valid ? row_src(sg, row, c0, cb, a0, by) : 0;
-        const uint8_t *blk0 = myslots + s * stage_bytes + (size_t)rr * p.row_slot + delta;
-        const int BB = q4 ? 144 : 210;
-        if (c == 0) {
-            acc = 0.f;
-            accm = 0.f;
-        }
-        // this half's blocks of the chunk: the first half feeds the chains,
-        // the second half parks its terms until the chains reach it
-        const int j0 = h2 ? half0 : 0, j1 = h2 ? cb : half0;
-        Terms park[(kChunk + 1) / 2];
+        const bool q4 = TYPES == 12 || (TYPES == 0 && valid && p.seg[sg].type == 12);
+        const uint8_t *wrow = valid ? p.seg[sg].w + (size_t)row * nb * (q4 ? 144 : 210) : nullptr;
+        acc = 0.f;
+        accm = 0.f;
+        bool gave_up = false;
+        for (int c = 0; c < n_chunks; ++c, ++it) {
+            const int s = it % S;
+            if (!__all_sync(FULLW, mbar_wait(mybar + s, (it / S) & 1, p.err, DEV_WAIT_FULL_TIMEOUT))) {
+                // gave up (recorded): let the copies still in flight land first
+                for (int u = it; u < n_items && u < it + S; ++u) mbar_drain(mybar + u % S, (u / S) & 1);
+                gave_up = true;
+                break;
+            }
+            const int c0 = c * CB, cb = min(CB, nb - c0), half0 = (cb + 1) >> 1;
+            const uintptr_t a = reinterpret_cast<uintptr_t>(wrow) + (size_t)c0 * (q4 ? 144 : 210);
+            const uint8_t *blk0 = myslots + s * stage_bytes + (size_t)rr * p.row_slot + (a & 15);
+            // this half's blocks of the chunk: the first half feeds the
+            // chains, the second half parks its terms until the chains reach it
+            const int j0 = h2 ? half0 : 0, j1 = h2 ? cb : half0;
+            Terms park[(CB + 1) / 2];
+            auto run_half = [&](auto type_tag) {
+                constexpr int T = decltype(type_tag)::value;
+                constexpr int BB = T == 12 ? 144 : 210;
 #pragma unroll
-        for (int jj = 0; jj < (kChunk + 1) / 2; ++jj) {
-            const int j = j0 + jj;
-            if (valid && j < j1) {
-                const int b = c0 + j;
-                uint32_t w[kW];
-                Terms t;
-                if (q4) {
-                    lds_block<12>(blk0 + (size_t)j * BB, k, w);
-                    t = block_terms<12>(w, k, q8t + (size_t)b * kQ8Block, bss + (size_t)b * 16, prs + (size_t)b * 8,
-                                        xds[b]);
-                } else {
-                    lds_block<14>(blk0 + (size_t)j * BB, k, w);
-                    t = block_terms<14>(w, k, q8t + (size_t)b * kQ8Block, bss + (size_t)b * 16, prs + (size_t)b * 8,
-                                        xds[b]);
+                for (int jj = 0; jj < (CB + 1) / 2; ++jj) {
+                    const int j = j0 + jj;
+                    if (valid && j < j1) {
+                        const int b = c0 + j;
+                        uint32_t w[kW];
+                        lds_block<T>(blk0 + (size_t)j * BB, k, w);
+                        const Terms tm = block_terms<T>(w, k, q8t + (size_t)b * kQ8Block, bss + (size_t)b * 16,
+                                                        prs + (size_t)b * 8, xds[b]);
+                        if (h2 == 0) take(tm, acc, accm);
+                        else park[jj] = tm;
+                    }
                 }
-                if (h2 == 0) take(t, acc, accm);
-                else park[jj] = t;
-            }
-        }
-        {
-            const float a1 = __shfl_xor_sync(FULLW, acc, 8), m1 = __shfl_xor_sync(FULLW, accm, 8);
-            if (h2) {
-                acc = a1;
-                accm = m1;
+            };
+            if (q4) run_half(std::integral_constant<int, 12>());
+            else run_half(std::integral_constant<int, 14>());
+            {
+                const float a1 = __shfl_xor_sync(FULLW, acc, 8), m1 = __shfl_xor_sync(FULLW, accm, 8);
+                if (h2) {
+                    acc = a1;
+                    accm = m1;
 #pragma unroll
-                for (int jj = 0; jj < (kChunk + 1) / 2; ++jj)
-                    if (valid && j0 + jj < j1) take(park[jj], acc, accm);
+                    for (int jj = 0; jj < (CB + 1) / 2; ++jj)
+                        if (valid && j0 + jj < j1) take(park[jj], acc, accm);
+                }
+                const float a2 = __shfl_xor_sync(FULLW, acc, 8), m2 = __shfl_xor_sync(FULLW, accm, 8);
+                if (!h2) {
+                    acc = a2;
+                    accm = m2;
+                }
             }
-            const float a2 = __shfl_xor_sync(FULLW, acc, 8), m2 = __shfl_xor_sync(FULLW, accm, 8);
-            if (!h2) {
-                acc = a2;
-                accm = m2;
-            }
+            __syncwarp();   // every lane is done with the stage
+            if (it + S < n_items) issue(it + S);
         }
-        __syncwarp();   // every lane is done with the stage
-        if (lane == 0 && it + S < n_items) issue(it + S);
-        if (c != n_chunks - 1) continue;
+        if (gave_up) break;
 
         // ------------------------------------------------ the group's results
         const float r = row_sum(acc, accm, q4);
@@ -527,11 +544,21 @@ size_t fixed_smem(int nb, int stages) {
 
 }  // namespace
 
+// Blocks per ring stage: a whole row of up to 16 blocks when two stages of
+// that size fit beside the Q8_K input (one chunk per group: the least
+// bookkeeping per block), else 8.
+static int chunk_blocks(int nb, int max_block_bytes) {
+    if (nb > 16) return 8;
+    const int slot = (int)(((size_t)16 * max_block_bytes + 32 + 15) & ~size_t(15));
+    return fixed_smem(nb, 2) + (size_t)kWarps * 2 * 2 * slot <= kQmatvecMaxSmem ? 16 : 8;
+}
+
 size_t qmatvec_config(int cols, int max_block_bytes, int *stages, int *row_slot) {
     const int nb = cols / 256;
+    const int cb = chunk_blocks(nb, max_block_bytes);
     // a row's chunk copy starts up to 15 bytes before its first block and ends
     // up to 15 bytes after its last; the Q6_K word reads reach 6 bytes past a block
-    const int slot = (int)(((size_t)kChunk * max_block_bytes + 32 + 15) & ~size_t(15));
+    const int slot = (int)(((size_t)cb * max_block_bytes + 32 + 15) & ~size_t(15));
     int S = 4;
     while (S > 1 && fixed_smem(nb, S) + (size_t)kWarps * S * 2 * slot > kQmatvecMaxSmem) --S;
     if (stages) *stages = S;
@@ -557,8 +584,16 @@ cudaError_t launch_qmatvec(const QMatvecParams &p, int grid, cudaStream_t s) {
     int stages = 0, slot = 0;
     const size_t smem = qmatvec_config(p.cols, bb, &stages, &slot);
     if (slot != p.row_slot || stages != p.stages || smem > kQmatvecMaxSmem) return cudaErrorInvalidValue;
-    if (cudaError_t e = ensure_smem_limit(reinterpret_cast<const void *>(qmatvec_kernel), (int)kQmatvecMaxSmem))
-        return e;
+    bool all4 = true, all6 = true;
+    for (int i = 0; i < p.n_seg; ++i) {
+        all4 = all4 && p.seg[i].type == 12;
+        all6 = all6 && p.seg[i].type == 14;
+    }
+    const bool wide = chunk_blocks(p.cols / 256, bb) == 16;
+    void (*kern)(QMatvecParams) = all4 ? (wide ? qmatvec_kernel<12, 16> : qmatvec_kernel<12, 8>)
+                                  : all6 ? (wide ? qmatvec_kernel<14, 16> : qmatvec_kernel<14, 8>)
+                                         : (wide ? qmatvec_kernel<0, 16> : qmatvec_kernel<0, 8>);
+    if (cudaError_t e = ensure_smem_limit(reinterpret_cast<const void *>(kern), (int)kQmatvecMaxSmem)) return e;
     cudaLaunchConfig_t cfg = {};
     cfg.gridDim = dim3(grid);
     cfg.blockDim = dim3(32 * kWarps);
@@ -567,7 +602,7 @@ cudaError_t launch_qmatvec(const QMatvecParams &p, int grid, cudaStream_t s) {
     cudaLaunchAttribute attr = pdl_attr();
     cfg.attrs = &attr;
     cfg.numAttrs = 1;
-    return cudaLaunchKernelEx(&cfg, qmatvec_kernel, p);
+    return cudaLaunchKernelEx(&cfg, kern, p);
 }
 
 }  // namespace kore

@@ -650,4 +650,25 @@ int keng_turn_ref(void *h, const int *ids, int n, int base, int n_gen, int *out)
     return n_gen;
 }
 
+// kore's forward() (kore.cpp:1397-1480) with its attention region served by
+// the attached CUDA context (cuda_forward): every other operation is kore's
+// own. Its logits isolate the attention: a device step that agrees with
+// them bit for bit agrees with kore in everything but the attention. Returns
+// 0 or -1.
+int keng_forward_cuda(void *h, int token, int pos, float *logits) {
+    Harness &hx = *(Harness *)h;
+    if (!hx.ctx || !cuda_forward(hx, token, pos, true)) return -1;
+    memcpy(logits, hx.e.logits.data(), hx.e.logits.size() * sizeof(float));
+    return 0;
+}
+
+// The same for forward_batch() (kore.cpp:1486-1598): nb <= e.bsz tokens at
+// pos0, attention through the attached CUDA context; the last token's logits.
+int keng_forward_batch_cuda(void *h, const int *toks, int nb, int pos0, float *logits) {
+    Harness &hx = *(Harness *)h;
+    if (!hx.ctx || !cuda_forward_batch(hx, toks, nb, pos0, true)) return -1;
+    memcpy(logits, hx.e.logits.data(), hx.e.logits.size() * sizeof(float));
+    return 0;
+}
+
 }  // extern "C"

@@ -346,6 +346,8 @@ def engine_lib():
         L.keng_get_row.argtypes = [ctypes.c_int] * 3 + [vp, ctypes.c_int, fp]
         L.keng_forward_batch.argtypes = [vp, ip, ctypes.c_int, ctypes.c_int, fp]
         L.keng_turn_ref.argtypes = [vp, ip, ctypes.c_int, ctypes.c_int, ctypes.c_int, ip]
+        L.keng_forward_cuda.argtypes = [vp, ctypes.c_int, ctypes.c_int, fp]
+        L.keng_forward_batch_cuda.argtypes = [vp, ip, ctypes.c_int, ctypes.c_int, fp]
         L.keng_matmul_batch.argtypes = [vp] + [ctypes.c_int] * 3 + [vp, fp, ctypes.c_int, fp]
         L.keng_forward.argtypes = [vp, ctypes.c_int, ctypes.c_int, fp]
         L.keng_tensor.argtypes = [vp, ctypes.c_char_p, ip, ip, ip]
@@ -444,6 +446,22 @@ class GreedyEngine:
         if engine_lib().keng_forward_batch(self.h, t.ctypes.data_as(ctypes.POINTER(ctypes.c_int)), t.size, pos0,
                                            _fp(out)):
             raise RuntimeError("kore forward_batch() refused the tokens or positions")
+        return out
+
+    def forward_cuda(self, token: int, pos: int) -> np.ndarray:
+        """kore's forward() with its attention on the attached CUDA context: the logits."""
+        out = np.empty(self.n_vocab, np.float32)
+        if engine_lib().keng_forward_cuda(self.h, token, pos, _fp(out)):
+            raise RuntimeError(self._err() or "kore forward() with CUDA attention failed")
+        return out
+
+    def forward_batch_cuda(self, tokens, pos0: int) -> np.ndarray:
+        """kore's forward_batch() with its attention on the attached CUDA context: the last logits."""
+        t = np.ascontiguousarray(tokens, np.int32)
+        out = np.empty(self.n_vocab, np.float32)
+        if engine_lib().keng_forward_batch_cuda(self.h, t.ctypes.data_as(ctypes.POINTER(ctypes.c_int)), t.size, pos0,
+                                                _fp(out)):
+            raise RuntimeError(self._err() or "kore forward_batch() with CUDA attention failed")
         return out
 
     def turn_ref(self, ids, base: int, n_gen: int) -> list[int]:

@@ -26,7 +26,7 @@ def main():
     local = int(os.environ.get("LOCAL_RANK", rank))
     torch.cuda.set_device(local)
     dist.init_process_group("gloo", timeout=datetime.timedelta(seconds=60))
-    H, G, d, ctx_max, cached = 28, 4, 128, 4096, 3000
+    H, G, d, ctx_max, cached = 28, 4, 128, 4096, 3000   # 3000 + 5 + 200 + 1 positions used
     ctx = K.KoreCuda(2, H, G, d, ctx_max, device=local, shard_rank=rank, shard_count=world)
     oras = [O.OracleLayer(H, G, d, ctx_max) for _ in range(2)]
     for layer in range(2):
@@ -76,6 +76,17 @@ def main():
             ref = O.qmatvec(m[3], ratt.reshape(-1))
             err = float(np.abs(got.astype(np.float64) - ref).max())
             assert err <= 2e-2 * max(1.0, float(np.abs(ref).max())), (rank, step, layer, err)
+    # a prefill chunk on the split (200 rows, across a page edge), merged over
+    # the peer exchange in pieces of 64 queries, then a decode after it
+    pos0 = cached + 5
+    for layer in range(2):
+        q, k, v = normal(900 + layer, (200, H * d), (200, G * d), (200, G * d))
+        torch.cuda.synchronize()
+        got = ctx.prefill(0, layer, pos0, q, k, v)
+        assert_attn_close(got, oras[layer].prefill(pos0, q, k, v), f"rank {rank} prefill layer {layer}")
+        q1, k1, v1 = normal(950 + layer, (H * d,), (G * d,), (G * d,))
+        got1 = ctx.decode_sharded(0, layer, pos0 + 200, q1, k1, v1)
+        assert_attn_close(got1, oras[layer].decode(pos0 + 200, q1, k1, v1), f"rank {rank} decode after prefill")
     dist.barrier()
     ctx.close()
     dist.destroy_process_group()

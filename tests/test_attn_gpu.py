@@ -281,3 +281,41 @@ def test_cfg5_full_shape_batched_decode():
         ref = o.decode(p, q[s], kn[s], vn[s])
         o.kc[p], o.vc[p] = saved
         assert_attn_close(out[s], ref, f"cfg5 sequence {s}, {p} cached positions")
+
+
+@pytest.mark.parametrize("n_shards,pos0,n", [(2, 2900, 200), (3, 0, 64), (8, 100, 37), (2, 255, 1)])
+def test_kv_sharded_prefill_partials_merge_to_the_full_result(n_shards, pos0, n):
+    """A prefill chunk on the multi-GPU split, emulated with one context per
+    shard on one GPU: every shard stores the chunk rows of its own pages and
+    returns its causal partial of the n queries; the LSE merge must equal
+    kore's prefill (kore.cpp:1542-1563) row for row."""
+    import torch
+    H, G, d = 28, 4, 128
+    ctxs = [make_ctx(H, G, d, 4096, shard_rank=r, shard_count=n_shards) for r in range(n_shards)]
+    o = O.OracleLayer(H, G, d, 4096)
+    if pos0:
+        k, v = normal(80 + n_shards, (pos0, G * d), (pos0, G * d))
+        for c in ctxs:
+            c.append(0, 0, 0, k, v)
+        o.fill(0, k, v)
+    q1, k1, v1 = normal(81 + n, (n, H * d), (n, G * d), (n, G * d))
+    ref = o.prefill(pos0, q1, k1, v1)
+    dev = torch.device("cuda", 0)
+    tq, tk, tv = (torch.from_numpy(x).to(dev) for x in (q1, k1, v1))
+    pf = n * (H * d + H)
+    parts = torch.empty(n_shards * pf, device=dev)
+    for r, c in enumerate(ctxs):
+        c.prefill_partial_dev(0, 0, pos0, n, tq, tk, tv, parts[r * pf:(r + 1) * pf])
+        c.sync()
+    out = torch.empty(n * H * d, device=dev)
+    ctxs[0].lse_merge_batch_dev(n_shards, n, parts, out)
+    ctxs[0].sync()
+    assert_attn_close(out.cpu().numpy().reshape(n, H, d), ref, f"{n_shards} shards, prefill {pos0}+{n}")
+    # each chunk row is stored by exactly one shard
+    rows = np.zeros((n, G * d), np.float32)
+    for r, c in enumerate(ctxs):
+        kr, _ = c.kv_read(0, 0, pos0, n)
+        owned = ((pos0 + np.arange(n)) // 256) % n_shards == r
+        assert not kr[~owned].any()
+        rows[owned] = kr[owned]
+    np.testing.assert_array_equal(rows, o.kc[pos0:pos0 + n])

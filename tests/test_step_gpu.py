@@ -10,10 +10,11 @@ place), whose tensors are uploaded as they are. Checks:
   quantisations, Q4_K products, biases, attention, residual adds, SwiGLU
   with the C library's expf, output norm and logits) and the token is kore's
   greedy choice; also with the embedding table in each type get_row reads;
-* positions 0..N with the tokens fed in: logits within the attention
-  tolerance of kore's forward() at every position, the greedy token
-  identical wherever kore's top-1/top-2 margin is not a near tie, and
-  bit-identical logits at most positions;
+* positions 0..N with the tokens fed in: logits bit-identical to kore's
+  control flow with its attention region on the same GPU attention (so
+  every other operation is kore's), within 2 % of kore's own logits (kore's
+  Q8_K quantisation amplifies the attention's ~1e-7 difference), and the
+  greedy token kore's wherever its top-1/top-2 margin is not a near tie;
 * greedy generation in kore's own flow (prompt in 64-token chunks, then
   decode steps): identical token IDs with every decode step on the device;
 * steps chained on the device (the next token never leaves the GPU) give
@@ -83,27 +84,39 @@ GEOMETRIES = [
 
 @pytest.mark.parametrize("geo", GEOMETRIES, ids=[g[0] for g in GEOMETRIES])
 def test_step_tracks_kore_forward(geo):
+    """Against kore's own forward() at every position: bit for bit at
+    position 0 (one key, so the attention is exact on both sides); beyond it
+    the attention differs from kore's scalar loop by ~1e-7 and kore's own
+    Q8_K quantisation of the attention output amplifies that into logit
+    differences of up to about a percent, so the logits are held to 2 % of
+    their scale and the greedy token to kore's wherever kore's top-1/top-2
+    margin is not a near tie. Against kore's control flow with its attention
+    region on the same GPU attention (keng_forward_cuda): bit for bit at
+    every position, which proves every other operation of the step is kore's."""
+    import os
     name, L, E, H, G, FF, V, steps = geo
     ctx = steps + 4
     eng = O.GreedyEngine(L, E, H, G, FF, V, ctx=ctx, seed=2026, threads=4)
+    twin = O.GreedyEngine(L, E, H, G, FF, V, ctx=ctx, seed=2026, threads=4)   # same model
+    twin.attach_cuda(os.path.join(REPO, "kore_b200", "libkore_cuda.so"), 0)
     g = device_model(eng, L, E, H, G, FF, V, ctx)
     tokens = np.random.default_rng(31).integers(0, V, steps).tolist()
-    exact = 0
     for pos, tok in enumerate(tokens):
         ref = eng.forward_ref(tok, pos)
+        iso = twin.forward_cuda(tok, pos)
         nxt, got = g.decode_step(0, tok, pos, want_logits=True)
         assert np.isfinite(got).all()
+        mism = np.nonzero(iso.view(np.uint32) != got.view(np.uint32))[0]
+        assert mism.size == 0, f"{name}, position {pos}: {mism.size} of {V} logits differ from kore with the GPU attention"
         if pos == 0:   # one key: every step of the computation is kore's own
             mism = np.nonzero(ref.view(np.uint32) != got.view(np.uint32))[0]
             assert mism.size == 0, f"{name}: {mism.size} of {V} logits differ at position 0"
         scale = max(1.0, float(np.abs(ref).max()))
         err = float(np.abs(got.astype(np.float64) - ref).max())
-        assert err <= 1e-3 * scale, f"{name}, position {pos}: max |logit error| {err:.3g} (scale {scale:.3g})"
-        exact += int(np.array_equal(ref.view(np.uint32), got.view(np.uint32)))
+        assert err <= 2e-2 * scale, f"{name}, position {pos}: max |logit error| {err:.3g} (scale {scale:.3g})"
         srt = np.sort(ref)
         if srt[-1] - srt[-2] > 2 * err:
             assert nxt == kore_argmax(ref), f"{name}, position {pos}: token {nxt} vs kore {kore_argmax(ref)}"
-    assert exact >= steps // 2, f"{name}: only {exact} of {steps} positions bit-identical"
     g.close()
 
 
