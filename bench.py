@@ -298,6 +298,33 @@ def run_decode(args, rank: int, world: int, dist, pos: int, layers: int, steps: 
     e2e_ms = (time.perf_counter() - t0) * 1e3 / e2e_steps
     barrier()
 
+    # where a host-buffer call's time goes (one GPU): the same layer calls with
+    # the inputs already on the device and a synchronisation after each (no
+    # staging), and the synchronisation alone (the error word's copy back and
+    # the stream wait), each per layer
+    breakdown = None
+    if world == 1:
+        n_b = max(5, e2e_steps // 4)
+        with torch.cuda.stream(stream):
+            t0 = time.perf_counter()
+            for _ in range(n_b):
+                for layer in range(layers):
+                    ctx.decode_dev(0, layer, pos, q[layer], kn[layer], vn[layer], out[layer])
+                    ctx.sync()
+            dev_sync_us = (time.perf_counter() - t0) * 1e6 / (n_b * layers)
+            t0 = time.perf_counter()
+            for _ in range(n_b * layers):
+                ctx.sync()
+            sync_us = (time.perf_counter() - t0) * 1e6 / (n_b * layers)
+        breakdown = {"host_call_us": round(e2e_ms * 1e3 / layers, 2),
+                     "device_inputs_call_plus_sync_us": round(dev_sync_us, 2),
+                     "sync_alone_us": round(sync_us, 2),
+                     "staging_us": round(e2e_ms * 1e3 / layers - dev_sync_us, 2),
+                     "note": "per layer: host_call = kore_cuda_attn_decode with host q/k/v/out; the second figure is "
+                             "kore_cuda_attn_decode_dev (inputs in HBM) + kore_cuda_sync after each call; sync_alone "
+                             "is kore_cuda_sync with nothing queued (error-word copy + stream wait); staging = "
+                             "host_call - the second figure (host copies, the input kernel, the output copy)"}
+
     # parity at N > 1: layer 0 rebuilt unsharded on this GPU from the same
     # seeds, decoded with the same q/k/v, against the merged sharded output
     parity = None
@@ -347,7 +374,8 @@ def run_decode(args, rank: int, world: int, dist, pos: int, layers: int, steps: 
         "config": cfg4_config(world, pos, layers),
         "e2e": {"value": round(e2e_gbs, 1), "unit": "GB/s", "ms_per_step": round(e2e_ms, 4),
                 "h2d_bytes_per_step": layers * (H * D + 2 * KVD) * 4, "d2h_bytes_per_step": layers * H * D * 4,
-                "call": "kore_cuda_attn_decode" if world == 1 else "kore_cuda_attn_decode_sharded"},
+                "call": "kore_cuda_attn_decode" if world == 1 else "kore_cuda_attn_decode_sharded",
+                "breakdown": breakdown},
         "roofline": {"bound": "hbm",
                      "kernel": "attn_decode_kernel<128,7,8,8,3> + " + ("split_merge_kernel<128,7>" if world == 1
                                                                        else "peer_exchange_kernel<128>"),

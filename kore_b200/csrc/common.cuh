@@ -76,8 +76,16 @@ constexpr uint32_t kWaitPolls = 1u << 26;
 
 __device__ __forceinline__ bool mbar_wait(uint64_t *bar, uint32_t parity, int *err, int code,
                                           uint64_t limit_ns = kWaitNs) {
-    if (mbar_try_wait(bar, parity)) return true;
-    const uint64_t t0 = global_ns();
+    // a try_wait may suspend until the phase completes: under a limit shorter
+    // than the default even the first one is timed
+    const bool timed_first = limit_ns < kWaitNs;
+    const uint64_t t_first = timed_first ? global_ns() : 0;
+    if (mbar_try_wait(bar, parity)) {
+        if (!timed_first || global_ns() - t_first <= limit_ns) return true;
+        raise_error(err, code);
+        return false;
+    }
+    const uint64_t t0 = timed_first ? t_first : global_ns();
     for (uint32_t it = 1; it < kWaitPolls; ++it) {
         // a try_wait may itself suspend until the phase completes: a wait that
         // ends after its limit counts as expired even if the copy landed

@@ -324,7 +324,7 @@ __device__ __forceinline__ int group_row(const QMatvecParams &p, int gg, int rr,
 // lies in one segment, so the branch is uniform over a warp). CB: blocks of
 // a row per ring stage.
 template <int TYPES, int CB>
-__global__ void __launch_bounds__(32 * kWarps) qmatvec_kernel(const __grid_constant__ QMatvecParams p) {
+__global__ void __launch_bounds__(32 * kWarps, 1) qmatvec_kernel(const __grid_constant__ QMatvecParams p) {
     extern __shared__ __align__(16) uint8_t smem[];
     const int nb = p.cols / 256, S = p.stages;
     const int n_chunks = (nb + CB - 1) / CB;
@@ -375,10 +375,11 @@ __global__ void __launch_bounds__(32 * kWarps) qmatvec_kernel(const __grid_const
         bytes = (uint32_t)(((a - a0) + cb * BB + 15) & ~uintptr_t(15));
         return (uint32_t)(a - a0);
     };
-    // bulk copies of item it: lane 0 arms the stage's barrier with both rows'
-    // bytes, then lanes 0 and 16 each copy their row's chunk
-    auto issue = [&](int it) {
-        const int gg = gg0 + (it / n_chunks) * TW, c = it % n_chunks, s = it % S;
+    // bulk copies of item (group t, chunk c) into stage s: lane 0 arms the
+    // stage's barrier with both rows' bytes, then lanes 0 and 16 each copy
+    // their row's chunk
+    auto issue = [&](int t, int c, int s) {
+        const int gg = gg0 + t * TW;
         uintptr_t a0 = 0, b0 = 0;
         uint32_t by = 0, by_other = 0;
         if ((lane & 15) == 0) {
@@ -396,7 +397,18 @@ __global__ void __launch_bounds__(32 * kWarps) qmatvec_kernel(const __grid_const
                            mybar + s);
         }
     };
-    for (int it = 0; it < S && it < n_items; ++it) issue(it);
+    // the next item to issue, as (group, chunk), advanced incrementally
+    int iss_t = 0, iss_c = 0;
+    auto advance = [&](int &t, int &c) {
+        if (++c == n_chunks) {
+            c = 0;
+            ++t;
+        }
+    };
+    for (int it = 0; it < S && it < n_items; ++it) {
+        issue(iss_t, iss_c, it);
+        advance(iss_t, iss_c);
+    }
     grid_dep_wait();
 
     // ------------------------------------------------------------ the Q8_K input
@@ -421,7 +433,8 @@ __global__ void __launch_bounds__(32 * kWarps) qmatvec_kernel(const __grid_const
     // ------------------------------------------------------------ the rows
     unsigned long long best = 0;   // argmax key of this lane's rows (QOUT_ARGMAX)
     float acc = 0.f, accm = 0.f;
-    int it = 0;
+    int it = 0, s = 0;
+    uint32_t ph = 0;   // item it sits in stage s = it % S with barrier parity ph = (it / S) & 1
     for (int t = 0; t < my_groups; ++t) {
         const int gg = gg0 + t * TW;
         int row;
@@ -432,9 +445,8 @@ __global__ void __launch_bounds__(32 * kWarps) qmatvec_kernel(const __grid_const
         acc = 0.f;
         accm = 0.f;
         bool gave_up = false;
-        for (int c = 0; c < n_chunks; ++c, ++it) {
-            const int s = it % S;
-            if (!__all_sync(FULLW, mbar_wait(mybar + s, (it / S) & 1, p.err, DEV_WAIT_FULL_TIMEOUT))) {
+        for (int c = 0; c < n_chunks; ++c) {
+            if (!__all_sync(FULLW, mbar_wait(mybar + s, ph, p.err, DEV_WAIT_FULL_TIMEOUT))) {
                 // gave up (recorded): let the copies still in flight land first
                 for (int u = it; u < n_items && u < it + S; ++u) mbar_drain(mybar + u % S, (u / S) & 1);
                 gave_up = true;
@@ -482,7 +494,15 @@ __global__ void __launch_bounds__(32 * kWarps) qmatvec_kernel(const __grid_const
                 }
             }
             __syncwarp();   // every lane is done with the stage
-            if (it + S < n_items) issue(it + S);
+            if (it + S < n_items) {
+                issue(iss_t, iss_c, s);   // item it + S reuses this stage
+                advance(iss_t, iss_c);
+            }
+            ++it;
+            if (++s == S) {
+                s = 0;
+                ph ^= 1u;
+            }
         }
         if (gave_up) break;
 
