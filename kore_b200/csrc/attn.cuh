@@ -140,9 +140,17 @@ cudaError_t ensure_smem_limit(const void *kernel, int bytes);
 size_t prefill_tile_bytes(int head_dim);
 // bytes of one split slot of PrefillParams::part
 size_t prefill_slot_bytes(int head_dim);
-// One weight matrix of a product launch: rows of GGUF blocks (type 12 = Q4_K,
-// 14 = Q6_K), out[r] = row r . x (+ bias[r]). The buffer holding w extends
-// at least 16 bytes past the matrix.
+// Bytes from one block of an uploaded matrix to the next. Q4_K blocks are
+// stored as GGUF has them (144 bytes, a multiple of 16); each 210-byte Q6_K
+// block is followed by 2 zero bytes, so that every block, and every 32-bit
+// word a product lane reads from it, is 4-byte aligned (the block's bytes are
+// GGUF's, unchanged).
+constexpr int kQ4Stride = 144, kQ6Stride = 212;
+__host__ __device__ constexpr int block_stride(int type) { return type == 12 ? kQ4Stride : kQ6Stride; }
+
+// One weight matrix of a product launch: rows of uploaded blocks (type 12 =
+// Q4_K, 14 = Q6_K, block_stride apart), out[r] = row r . x (+ bias[r]). The
+// buffer holding w extends at least 16 bytes past the matrix.
 struct QSeg {
     const uint8_t *w;
     const float *bias;

@@ -78,7 +78,7 @@ __global__ void __launch_bounds__(kNT) batch_matmul_kernel(const __grid_constant
             } else {
                 const QSeg &q = p.seg[sg];
                 const bool q4 = q.type == 12;
-                const uint8_t *blk = q.w + ((size_t)row * nb + i) * (q4 ? 144 : 210);
+                const uint8_t *blk = q.w + ((size_t)row * nb + i) * block_stride(q.type);
                 if (q4)
                     for (int j = j0; j < j0 + 32; ++j) dst[j] = q4k_value(blk, j);
                 else

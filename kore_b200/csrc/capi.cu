@@ -1116,8 +1116,31 @@ int kore_cuda_attn_decode_batch(kore_cuda_ctx *c, int layer, int n_seq, const in
 
 // ---------------------------------------------------------------- attention block projections
 
+// GGUF bytes of a matrix (the host layout) and bytes of its uploaded copy
+// (Q6_K blocks block_stride apart).
 static size_t qmat_bytes(int type, int rows, int cols) {
     return (size_t)rows * (size_t)(cols / 256) * (type == KORE_CUDA_Q4_K ? 144 : 210);
+}
+static size_t qmat_dev_bytes(int type, int rows, int cols) {
+    return (size_t)rows * (size_t)(cols / 256) * block_stride(type);
+}
+
+// Copies a GGUF matrix to the device in the uploaded layout: Q4_K as is, Q6_K
+// with 2 zero bytes behind every 210-byte block (through a host buffer of one
+// slice of rows at a time).
+static cudaError_t upload_qmat(uint8_t *dst, const kore_cuda_qmat &m) {
+    if (m.type == KORE_CUDA_Q4_K)
+        return cudaMemcpy(dst, m.data, qmat_bytes(m.type, m.rows, m.cols), cudaMemcpyHostToDevice);
+    const size_t nblk = (size_t)m.rows * (m.cols / 256), per = (size_t)1 << 16;
+    std::vector<uint8_t> buf(per * kQ6Stride, 0);
+    const uint8_t *src = static_cast<const uint8_t *>(m.data);
+    for (size_t b0 = 0; b0 < nblk; b0 += per) {
+        const size_t n = std::min(per, nblk - b0);
+        for (size_t b = 0; b < n; ++b) memcpy(buf.data() + b * kQ6Stride, src + (b0 + b) * 210, 210);
+        if (cudaError_t e = cudaMemcpy(dst + b0 * kQ6Stride, buf.data(), n * kQ6Stride, cudaMemcpyHostToDevice))
+            return e;
+    }
+    return cudaSuccess;
 }
 
 static int check_qmat(kore_cuda_ctx *c, const kore_cuda_qmat *m, const char *name, int rows, int cols) {
@@ -1141,7 +1164,7 @@ static const kore_cuda_ctx::LayerProj *layer_proj(kore_cuda_ctx *c, int layer) {
 // ring shape for its widest block, the error word, then the launch.
 static int launch_products(kore_cuda_ctx *c, QMatvecParams &mp) {
     int bb = 0;
-    for (int i = 0; i < mp.n_seg; ++i) bb = std::max(bb, mp.seg[i].type == KORE_CUDA_Q4_K ? 144 : 210);
+    for (int i = 0; i < mp.n_seg; ++i) bb = std::max(bb, block_stride(mp.seg[i].type));
     if (qmatvec_config(mp.cols, bb, &mp.stages, &mp.row_slot) > kQmatvecMaxSmem)
         return fail(c, KORE_CUDA_EINVAL, "a product over %d columns does not fit in shared memory", mp.cols);
     mp.err = c->err_d;
@@ -1194,7 +1217,7 @@ int kore_cuda_set_attn_weights(kore_cuda_ctx *c, int layer, const kore_cuda_qmat
     const char *names[4] = {"wq", "wk", "wv", "wo"};
     for (int i = 0; i < 4; ++i)
         if (int rc = check_qmat(c, m[i], names[i], rows[i], E)) return rc;
-    if (qmatvec_config(E, 210, nullptr, nullptr) > kQmatvecMaxSmem)
+    if (qmatvec_config(E, kQ6Stride, nullptr, nullptr) > kQmatvecMaxSmem)
         return fail(c, KORE_CUDA_EINVAL, "n_embd = %d: a product launch's staging exceeds shared memory", E);
     DeviceGuard dg(c->cfg.device);
     if (c->proj.empty()) c->proj.resize((size_t)c->cfg.n_layer);
@@ -1207,12 +1230,12 @@ int kore_cuda_set_attn_weights(kore_cuda_ctx *c, int layer, const kore_cuda_qmat
     size_t off[4], total = 0;
     for (int i = 0; i < 4; ++i) {
         off[i] = total;
-        total += align256(qmat_bytes(m[i]->type, rows[i], E) + 16);   // the product kernel reads up to 8 bytes past a matrix
+        total += align256(qmat_dev_bytes(m[i]->type, rows[i], E) + 16);   // the product kernel reads past a row's end
     }
     uint8_t *w = nullptr;
     CK(cudaMalloc(&w, total));
     lp.w = w;
-    for (int i = 0; i < 4; ++i) CK(cudaMemcpy(w + off[i], m[i]->data, qmat_bytes(m[i]->type, rows[i], E), cudaMemcpyHostToDevice));
+    for (int i = 0; i < 4; ++i) CK(upload_qmat(w + off[i], *m[i]));
     if (bq) {
         float *b = nullptr;
         CK(cudaMalloc(&b, (size_t)(E + 2 * c->kvd) * sizeof(float)));
@@ -1327,7 +1350,7 @@ int kore_cuda_set_model(kore_cuda_ctx *c, const kore_cuda_model *m) {
         if (int rc = check_qmat(c, &L.w_up, "ffn_up", FF, E)) return rc;
         if (int rc = check_qmat(c, &L.w_down, "ffn_down", E, FF)) return rc;
     }
-    if (qmatvec_config(FF, 210, nullptr, nullptr) > kQmatvecMaxSmem)
+    if (qmatvec_config(FF, kQ6Stride, nullptr, nullptr) > kQmatvecMaxSmem)
         return fail(c, KORE_CUDA_EINVAL, "n_ff = %d: the down product's input does not fit in shared memory", FF);
     DeviceGuard dg(c->cfg.device);
     CK(cudaStreamSynchronize(c->stream));
@@ -1351,12 +1374,11 @@ int kore_cuda_set_model(kore_cuda_ctx *c, const kore_cuda_model *m) {
         size_t total = 0;
         for (int i = 0; i < 3; ++i) {
             lf.off[i] = total;
-            total += align256(qmat_bytes(w[i]->type, w[i]->rows, w[i]->cols) + 16);   // the product kernel reads past a row's end
+            total += align256(qmat_dev_bytes(w[i]->type, w[i]->rows, w[i]->cols) + 16);   // the product kernel reads past a row's end
         }
         CK(cudaMalloc(&lf.w, total));
         for (int i = 0; i < 3; ++i) {
-            CK(cudaMemcpy(lf.w + lf.off[i], w[i]->data, qmat_bytes(w[i]->type, w[i]->rows, w[i]->cols),
-                          cudaMemcpyHostToDevice));
+            CK(upload_qmat(lf.w + lf.off[i], *w[i]));
             lf.type[i] = w[i]->type;
         }
     }
@@ -1371,9 +1393,8 @@ int kore_cuda_set_model(kore_cuda_ctx *c, const kore_cuda_model *m) {
     CK(cudaMemcpy(M.tok, te.data, (size_t)V * M.tok_row_bytes, cudaMemcpyHostToDevice));
     CK(cudaMalloc(&M.out_norm, (size_t)E * sizeof(float)));
     CK(cudaMemcpy(M.out_norm, m->out_norm, (size_t)E * sizeof(float), cudaMemcpyHostToDevice));
-    const size_t ob = qmat_bytes(m->out_w.type, V, E);
-    CK(cudaMalloc(&M.out_w, align256(ob + 16)));
-    CK(cudaMemcpy(M.out_w, m->out_w.data, ob, cudaMemcpyHostToDevice));
+    CK(cudaMalloc(&M.out_w, align256(qmat_dev_bytes(m->out_w.type, V, E) + 16)));
+    CK(upload_qmat(M.out_w, m->out_w));
     if (M.n_vocab != V || !M.logits) {
         cudaFree(M.logits);
         M.logits = nullptr;

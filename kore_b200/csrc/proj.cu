@@ -172,14 +172,6 @@ constexpr int kW = 11;
 
 __device__ __forceinline__ uint32_t lds_u32(const uint8_t *p) { return *reinterpret_cast<const uint32_t *>(p); }
 
-// 32-bit word at a 2-byte aligned shared-memory address: two aligned loads
-// and a byte permute.
-__device__ __forceinline__ uint32_t lds_u32_a2(const uint8_t *p) {
-    const uintptr_t a = reinterpret_cast<uintptr_t>(p);
-    const uint32_t *b = reinterpret_cast<const uint32_t *>(a & ~uintptr_t(3));
-    return __byte_perm(b[0], b[1], (a & 2) ? 0x5432 : 0x3210);
-}
-
 template <int TYPE>
 __device__ __forceinline__ void lds_block(const uint8_t *blk, int k, uint32_t (&w)[kW]) {
     if (TYPE == 12) {
@@ -190,16 +182,16 @@ __device__ __forceinline__ void lds_block(const uint8_t *blk, int k, uint32_t (&
         w[5] = h.y;
         w[6] = h.z;
         w[7] = h.w;
-    } else {
+    } else {   // uploaded Q6_K blocks are 4-byte aligned (kQ6Stride)
 #pragma unroll
         for (int h = 0; h < 2; ++h) {
-            w[3 * h + 0] = lds_u32_a2(blk + 64 * h + 4 * k);
-            w[3 * h + 1] = lds_u32_a2(blk + 64 * h + 32 + 4 * k);
-            w[3 * h + 2] = lds_u32_a2(blk + 128 + 32 * h + 4 * k);
+            w[3 * h + 0] = lds_u32(blk + 64 * h + 4 * k);
+            w[3 * h + 1] = lds_u32(blk + 64 * h + 32 + 4 * k);
+            w[3 * h + 2] = lds_u32(blk + 128 + 32 * h + 4 * k);
         }
 #pragma unroll
-        for (int i = 0; i < 4; ++i) w[6 + i] = lds_u32_a2(blk + 192 + 4 * i);
-        w[10] = lds_u32_a2(blk + 208) & 0xFFFFu;
+        for (int i = 0; i < 4; ++i) w[6 + i] = lds_u32(blk + 192 + 4 * i);   // 4-byte aligned only
+        w[10] = lds_u32(blk + 208) & 0xFFFFu;
     }
 }
 
@@ -368,7 +360,7 @@ __global__ void __launch_bounds__(32 * kWarps, 1) qmatvec_kernel(const __grid_co
             return 0;
         }
         const QSeg &q = p.seg[sg];
-        const size_t BB = TYPES == 12 ? 144 : (TYPES == 14 ? 210 : (q.type == 12 ? 144 : 210));
+        const size_t BB = TYPES ? block_stride(TYPES) : block_stride(q.type);
         const int c0 = c * CB, cb = min(CB, nb - c0);
         const uintptr_t a = reinterpret_cast<uintptr_t>(q.w) + ((size_t)row * nb + c0) * BB;
         a0 = a & ~uintptr_t(15);
@@ -441,7 +433,7 @@ __global__ void __launch_bounds__(32 * kWarps, 1) qmatvec_kernel(const __grid_co
         const int sg = group_row(p, gg, rr, total_rows, row);
         const bool valid = sg >= 0;
         const bool q4 = TYPES == 12 || (TYPES == 0 && valid && p.seg[sg].type == 12);
-        const uint8_t *wrow = valid ? p.seg[sg].w + (size_t)row * nb * (q4 ? 144 : 210) : nullptr;
+        const uint8_t *wrow = valid ? p.seg[sg].w + (size_t)row * nb * (q4 ? kQ4Stride : kQ6Stride) : nullptr;
         acc = 0.f;
         accm = 0.f;
         bool gave_up = false;
@@ -453,7 +445,7 @@ __global__ void __launch_bounds__(32 * kWarps, 1) qmatvec_kernel(const __grid_co
                 break;
             }
             const int c0 = c * CB, cb = min(CB, nb - c0), half0 = (cb + 1) >> 1;
-            const uintptr_t a = reinterpret_cast<uintptr_t>(wrow) + (size_t)c0 * (q4 ? 144 : 210);
+            const uintptr_t a = reinterpret_cast<uintptr_t>(wrow) + (size_t)c0 * (q4 ? kQ4Stride : kQ6Stride);
             const uint8_t *blk0 = myslots + s * stage_bytes + (size_t)rr * p.row_slot + (a & 15);
             // this half's blocks of the chunk: the first half feeds the
             // chains, the second half parks its terms until the chains reach it
@@ -461,7 +453,7 @@ __global__ void __launch_bounds__(32 * kWarps, 1) qmatvec_kernel(const __grid_co
             Terms park[(CB + 1) / 2];
             auto run_half = [&](auto type_tag) {
                 constexpr int T = decltype(type_tag)::value;
-                constexpr int BB = T == 12 ? 144 : 210;
+                constexpr int BB = block_stride(T);
 #pragma unroll
                 for (int jj = 0; jj < (CB + 1) / 2; ++jj) {
                     const int j = j0 + jj;
@@ -595,7 +587,7 @@ cudaError_t launch_qmatvec(const QMatvecParams &p, int grid, cudaStream_t s) {
     for (int i = 0; i < p.n_seg; ++i) {
         if ((p.seg[i].type != 12 && p.seg[i].type != 14) || p.seg[i].rows < 0 || !p.seg[i].w || !p.seg[i].out)
             return cudaErrorInvalidValue;
-        bb = max(bb, p.seg[i].type == 12 ? 144 : 210);
+        bb = max(bb, block_stride(p.seg[i].type));
     }
     if (p.pair_segments && (p.n_seg != 2 || p.seg[0].rows != p.seg[1].rows)) return cudaErrorInvalidValue;
     if (p.out_mode == QOUT_SWIGLU && !p.pair_segments) return cudaErrorInvalidValue;
