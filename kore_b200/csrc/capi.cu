@@ -66,6 +66,7 @@ struct kore_cuda_ctx {
     bool hold_prefetch = false;   // set: the next decode waits before its first KV fetch
     int prefetch_stages = 3;      // ring stages fetched early (KORE_CUDA_PREFETCH_STAGES)
     int shard_ctas = 0;           // decode CTAs aimed at on a KV-split context (KORE_CUDA_SHARD_CTAS; 0: 2 per SM)
+    int decode_ctas = 0;          // decode CTAs aimed at otherwise (KORE_CUDA_DECODE_CTAS; 0: 2 per SM)
     // batched decode: split-length factor chosen for the last batch shape
     long long split_key[3] = {-1, -1, -1};
     double split_f = 1.0;
@@ -437,10 +438,12 @@ int run_decode(kore_cuda_ctx *c, int layer, int n_q, bool contiguous, int seq0, 
         max_count = std::max(max_count, cnt);
     }
     const int TT = decode_tile_tokens();
-    // CTAs to aim for: two per SM; a KV-split context may aim lower
-    // (KORE_CUDA_SHARD_CTAS), trading CTA count for longer splits
+    // CTAs to aim for: two per SM, unless set otherwise (KORE_CUDA_DECODE_CTAS;
+    // KORE_CUDA_SHARD_CTAS on a KV-split context), trading CTA count for
+    // longer splits
     const long long target = c->NS > 1 && c->shard_ctas > 0 ? c->shard_ctas
-                                                             : (long long)c->num_sms * decode_ctas_per_sm(c->D, c->R);
+                             : c->decode_ctas > 0           ? c->decode_ctas
+                                                            : (long long)c->num_sms * decode_ctas_per_sm(c->D, c->R);
     long long st = (total * c->G + target - 1) / target;
     st = std::max<long long>(st, 4 * TT);
     st = std::max<long long>(st, (max_count + kMaxSplits - 1) / kMaxSplits);
@@ -658,6 +661,7 @@ int kore_cuda_create(kore_cuda_ctx **out, const kore_cuda_cfg *cfg) {
     if (const char *sp = getenv("KORE_CUDA_SHARD_PREFETCH")) c->shard_prefetch = atoi(sp) != 0;
     if (const char *ps = getenv("KORE_CUDA_PREFETCH_STAGES")) c->prefetch_stages = std::max(0, atoi(ps));
     if (const char *sc = getenv("KORE_CUDA_SHARD_CTAS")) c->shard_ctas = std::max(0, atoi(sc));
+    if (const char *dc = getenv("KORE_CUDA_DECODE_CTAS")) c->decode_ctas = std::max(0, atoi(dc));
     CKB(cudaStreamCreateWithFlags(&c->stream, cudaStreamNonBlocking));
     c->own_stream = true;
 
