@@ -3,7 +3,10 @@ torch.distributed.run): a KV-sharded context per GPU, handles exchanged over
 gloo, decode steps through kore_cuda_attn_decode_sharded_dev compared with
 the oracle on every rank, then the attention block with its projections on
 the same split (kore_cuda_attn_block_decode_dev): identical on every rank,
-its projections bit-exact and its attention within tolerance of the oracle."""
+its projections bit-exact and its attention within tolerance of the oracle;
+a prefill chunk on the split merged through the exchange; and the whole
+model on the split (device prefill, then decode steps): greedy IDs equal to
+kore's own on every rank."""
 import datetime
 import os
 import sys
@@ -89,6 +92,26 @@ def main():
         assert_attn_close(got1, oras[layer].decode(pos0 + 200, q1, k1, v1), f"rank {rank} decode after prefill")
     dist.barrier()
     ctx.close()
+
+    # the whole model on the split: kore's own random-init model (every rank
+    # builds the same one), its prompt prefilled on the device over the
+    # split, then decode steps; greedy IDs equal kore's own flow on every rank
+    if O.engine_available():
+        from tests.test_step_gpu import engine_model
+        L, E, Hm, Gm, FF, V, n_prompt, n_gen = 2, 1024, 8, 2, 1280, 96, 300, 12
+        eng = O.GreedyEngine(L, E, Hm, Gm, FF, V, ctx=n_prompt + n_gen + 8, seed=77, threads=2)
+        prompt = np.random.default_rng(78).integers(0, V, n_prompt)
+        ref, _ = eng.generate_ref(prompt, n_gen)
+        m = engine_model(eng, L)
+        cm = K.KoreCuda(L, Hm, Gm, E // Hm, n_prompt + n_gen + 8, device=local, shard_rank=rank, shard_count=world)
+        cm.set_model(FF, V, O.engine_lib().keng_rms_eps(eng.h), m["tok_embd"], m["out_norm"], m["out_w"], m["layers"])
+        exchange_handles(cm, dist)
+        ids = [cm.prefill_tokens(0, prompt, 0)[0]]
+        for i in range(1, n_gen):
+            ids.append(cm.decode_step(0, ids[-1], n_prompt + i - 1)[0])
+        assert ids == ref.tolist(), (rank, ids, ref.tolist())
+        dist.barrier()
+        cm.close()
     dist.destroy_process_group()
     print(f"rank {rank} ok", flush=True)
 
