@@ -644,7 +644,9 @@ def run_cfg1(args) -> dict:
                 "d2h_bytes_per_step": (C1_PRE + C1_DEC) * hd * 4},
         "roofline": {"bound": "latency", "note": "29.6 MFLOP of prefill and <= 0.2 MB per decode: launch and "
                                                  "dependency latency bound, far from HBM or tensor limits"},
-        "gpu_launches": steps * (3 + C1_DEC * 1),
+        # prefill: append, operand split, tensor-core kernel; each decode: the
+        # decode kernel and its split merge (positions 128..191 take 4-6 splits)
+        "gpu_launches": steps * (3 + C1_DEC * 2),
         "clocks": clk,
     }
     if not args.no_cpu_baseline:
