@@ -28,7 +28,9 @@ Further lines on the same JSON object (N = 1 unless stated): ``cfg1`` (the
 (7B, 28 layers, decode at 8192), ``attn_block`` (the attention block with its
 quantised projections), ``prefill`` (config 3, tensor cores),
 ``decode_step`` (kore's whole decode step on the device: 7B-shaped synthetic
-weights, the headline's cache; tokens/s) and ``batched`` (config 5, every N).
+weights, the headline's cache; tokens/s), ``prefill_model`` (kore's
+forward_batch for a 2048-token prompt through the same model on the device;
+tokens/s) and ``batched`` (config 5, every N).
 
 ``--impl reference`` times kore's own CPU attention (the reference compiled
 in place, oracle/_ref) on this host: full 28-layer steps of kore.cpp forward()
@@ -82,6 +84,7 @@ def parse():
     ap.add_argument("--no-cfg12", action="store_true", help="skip the config-1 and config-2 lines")
     ap.add_argument("--no-step", action="store_true", help="skip the whole-decode-step line")
     ap.add_argument("--step-only", action="store_true", help="measure only the whole decode step (development)")
+    ap.add_argument("--prefill-model-only", action="store_true", help="measure only the whole-model prefill")
     ap.add_argument("--block-only", action="store_true", help="measure only the attention block (development)")
     ap.add_argument("--prefill-only", action="store_true", help="measure only the prefill (development)")
     a = ap.parse_args()
@@ -816,6 +819,101 @@ def run_step_line(args) -> dict:
     return line
 
 
+PM_TOKENS = 2048   # prompt tokens of the whole-model prefill line
+
+
+def run_prefill_model(args, reuse=None) -> dict:
+    """kore's forward_batch() for a whole prompt on the device
+    (kore_cuda_prefill): a 2048-token prompt at position 0 through the
+    7B-shaped model of the decode-step line (embedding, 28 layers of RMSNorm,
+    kore's float batched products with biases / residual adds / SwiGLU, the
+    tensor-core prefill attention, then the last token's logits and greedy
+    token). value: prompt tokens/s, wall clock around the synchronous call
+    (its token ids in, the next token id out). The products are fused
+    multiply-add chains on the CUDA cores (kore's order, bit for bit), so the
+    roofline is the nominal fp32 CUDA-core peak (no measured one on this
+    pool)."""
+    import torch
+    import kore_b200 as K
+    dev = torch.device("cuda", 0)
+    ctx = K.KoreCuda(L, H, G, D, PM_TOKENS + 8, device=0)
+    rng = np.random.default_rng(81)
+    lw, tok, out_w, out_norm = reuse if reuse is not None else step_model(rng)
+    ctx.set_model(S_FF, S_VOCAB, 1e-6, tok, out_norm, out_w, [lw] * L)
+    toks = np.random.default_rng(83).integers(0, S_VOCAB, PM_TOKENS).astype(np.int32)
+    warm = max(2, min(args.warmup, 3))
+    for _ in range(warm):
+        ctx.prefill_tokens(0, toks, 0)
+    steps = 3
+    clocks = ClockSampler(0)
+    clocks.start()
+    torch.cuda.synchronize(dev)
+    t_begin = time.time()
+    t0 = time.perf_counter()
+    for _ in range(steps):
+        ctx.prefill_tokens(0, toks, 0)
+    ms = (time.perf_counter() - t0) * 1e3 / steps
+    t_end = time.time()
+    clk = clocks.stop(t_begin, t_end)
+    ctx.close()
+    E = H * D
+    fma = PM_TOKENS * L * (E * (E + 2 * KVD + E) + 3 * S_FF * E)     # the float products
+    attn_flop = 4 * D * prefill_pairs(0, PM_TOKENS) * H * L
+    tflops = 2 * fma / (ms * 1e-3) / 1e12
+    nominal = 148 * 128 * 2 * 1.965e9 / 1e12   # fp32 FMA lanes x 2 x max SM clock
+    line = {
+        "metric": "whole-model prefill tokens/s @7B (2048-token prompt, 28 layers, kore's float products bit for bit)",
+        "value": round(PM_TOKENS / (ms * 1e-3), 1), "unit": "tokens/s", "ms_per_step": round(ms, 2),
+        "steps": steps, "warmup": warm, "higher_is_better": True,
+        "config": {"workload": f"Qwen2.5-7B-shaped prefill of {PM_TOKENS} tokens at position 0: n_embd 3584, 28Q/4KV, "
+                               f"d128, n_ff {S_FF}, vocab {S_VOCAB}, {L} layers (the decode-step line's weights)",
+                   "product_fma": int(fma), "attention_flop": int(attn_flop)},
+        "e2e": {"value": round(PM_TOKENS / (ms * 1e-3), 1), "unit": "tokens/s", "ms_per_step": round(ms, 2),
+                "h2d_bytes_per_step": PM_TOKENS * 4, "d2h_bytes_per_step": 260,
+                "note": "the call is synchronous: token ids in, the next token id out; value and e2e are the same call"},
+        "roofline": {"bound": "fp32 CUDA cores (products)", "achieved": round(tflops, 1),
+                     "peak": round(nominal, 1), "unit": "TFLOP/s", "frac": round(tflops / nominal, 4),
+                     "peak_source": "nominal: 148 SMs x 128 fp32 lanes x 2 x 1965 MHz (no measured fp32 peak)",
+                     "note": "achieved counts the products' 2 x FMAs only, over the whole call's time"},
+        "gpu_launches": steps * (1 + L * 11 + 2),   # per layer: 2 norms, 5 products, append, operand split, attention
+        "clocks": clk,
+    }
+    if not args.no_cpu_baseline:
+        line["cpu_baseline"] = prefill_model_cpu_baseline(lw)
+    return line
+
+
+def prefill_model_cpu_baseline(lw) -> dict:
+    """kore's own matmul_batch_float (its prefill products) on this host for
+    one layer's seven matrices with a 64-token chunk (KORE_BMAX), all host
+    threads, scaled to the 2048-token prompt and 28 layers (the attention and
+    the rest are left out, so this is an upper bound on kore's speed)."""
+    from oracle import oracle as O
+    if not O.engine_available():
+        return {"value": None, "unavailable": "oracle/_ref/libkore_engine.so not built"}
+    cores = len(os.sched_getaffinity(0))
+    eng = O.GreedyEngine(1, 512, 4, 2, 512, 32, ctx=8, seed=1, threads=cores)
+    E = H * D
+    rng = np.random.default_rng(84)
+    xe = rng.standard_normal((64, E)).astype(np.float32)
+    xf = rng.standard_normal((64, S_FF)).astype(np.float32)
+    t = 0.0
+    for k in ("wq", "wk", "wv", "wo", "w_gate", "w_up", "w_down"):
+        x = xf if k == "w_down" else xe
+        best = None
+        for _ in range(2):
+            t0 = time.perf_counter()
+            eng.matmul_batch_ref(lw[k], x)
+            dt = time.perf_counter() - t0
+            best = dt if best is None else min(best, dt)
+        t += best
+    ms = t * 1e3 * (PM_TOKENS / 64) * L
+    return {"value": round(PM_TOKENS / (ms * 1e-3), 3), "unit": "tokens/s", "cores": cores, "kind": "reference",
+            "ms_per_step": round(ms, 1),
+            "sample": f"kore's matmul_batch_float of one layer's 7 matrices on a 64-token chunk, {cores} threads, "
+                      f"best of 2 each: {t * 1e3:.1f} ms, x {PM_TOKENS // 64} chunks x {L} layers (products only)"}
+
+
 def step_cpu_baseline(lw, out_w) -> dict:
     """kore's own decode step on this host, composed from its own functions
     (the reference compiled in place): per layer its attention at POS on one
@@ -1204,6 +1302,9 @@ def main():
     if args.step_only:
         print(json.dumps(run_step_line(args)), flush=True)
         return
+    if args.prefill_model_only:
+        print(json.dumps(run_prefill_model(args)), flush=True)
+        return
     ok = True
     try:
         line = run_decode(args, rank, world, dist, POS, L, args.steps, args.e2e_steps, want_block=True)
@@ -1221,6 +1322,7 @@ def main():
                 line["prefill"] = run_prefill(args, torch.device("cuda", 0), load_peaks())
             if not args.no_step:
                 line["decode_step"] = run_step_line(args)
+                line["prefill_model"] = run_prefill_model(args)
         if line is not None:
             ok = all(x.get("parity", {}).get("ok", True) for x in (line, line.get("cfg2") or {}))
             print(json.dumps(line), flush=True)
