@@ -10,16 +10,20 @@
 // kore selects them on every AVX2/FMA CPU). The result of an output depends
 // only on that chain, so any assignment of outputs to threads gives kore's
 // values bit for bit as long as each thread keeps the chain's order — which
-// is what batch_matmul_kernel does: a CTA holds a tile of 16 weight rows x
+// is what batch_matmul_kernel does: a CTA holds a tile of 32 weight rows x
 // up to 64 tokens, dequantises the tile's rows one block at a time into
-// shared memory with kore's rounding, stages the tokens' matching 256
-// columns transposed beside them, and each thread advances 8 chains (2 rows
-// x 4 tokens) through the block. CUDA cores, not tensor cores: a tensor-core
-// product sums in its own order and could not give kore's values.
+// shared memory with kore's rounding (each thread one row's 64 values, the
+// sub-block scales computed once), transposed so that a thread reads the 4
+// rows it serves at a column with one 16-byte load, stages the tokens'
+// matching 256 columns transposed beside them (conflict-free stores), and
+// each thread advances 16 chains (4 rows x 4 tokens) through the block; two
+// CTAs per SM overlap one's staging with the other's products. CUDA cores,
+// not tensor cores: a tensor-core product sums in its own order and could not
+// give kore's values.
 //
 // The epilogues do what forward_batch does next to each product: the bias
 // add (kore.cpp:1530-1532), the residual add x += o (:1568-1571, :1588-1591)
-// and, for the gate/up pair (a tile of 8 gate rows and the same 8 up rows),
+// and, for the gate/up pair (a tile of 16 gate rows and the same 16 up rows),
 // the SwiGLU g / (1 + exp(-g)) * u (:1578-1584) with the C library's expf.
 //
 // rmsnorm_rows_kernel: kore's rmsnorm (kore.cpp:1367-1372) of each token's
@@ -34,21 +38,66 @@
 namespace kore {
 namespace {
 
-constexpr int kRT = 16;          // weight rows per tile (pair mode: 8 gate + 8 up rows)
+constexpr int kRT = 32;          // weight rows per tile (pair mode: 16 gate + 16 up rows, interleaved)
 constexpr int kBT = 64;          // tokens per tile
-constexpr int kNT = 128;         // threads: (kRT / 2) row pairs x (kBT / 4) token quads
-constexpr int kWPitch = 257;     // shared row pitch of the dequantised weights (bank spread)
-constexpr int kXPitch = kBT + 4; // shared row pitch of the transposed tokens (16-byte rows)
+constexpr int kNT = 128;         // threads: (kRT / 4) row quads x (kBT / 4) token quads
+constexpr int kWP = kRT + 4;     // shared pitch of the transposed weights Wt[j][row] (16-byte rows)
+constexpr int kXP = kBT + 4;     // shared pitch of the transposed tokens Xs[j][token] (16-byte rows)
 
-constexpr size_t kXsFloats = (size_t)256 * kXPitch;
-constexpr size_t kBatchSmem = (kXsFloats + (size_t)kRT * kWPitch) * sizeof(float);
+constexpr size_t kXsFloats = (size_t)256 * kXP;
+constexpr size_t kBatchSmem = (kXsFloats + (size_t)256 * kWP) * sizeof(float);   // 106.5 KB: two CTAs per SM
 
-__global__ void __launch_bounds__(kNT) batch_matmul_kernel(const __grid_constant__ BatchMatmulParams p) {
+// Dequantises the 64 values [64 qq, 64 qq + 64) of a Q4_K block into Wt
+// column s (kore.cpp:337-354: d1 = d * scale, m1 = dmin * min per 32-value
+// sub-block, value = d1 * q - m1, each product and the difference rounded).
+__device__ __forceinline__ void dequant_q4k_quarter(const uint8_t *b, int qq, float *Wt, int s) {
+    int sc, mn;
+    scale_min_k4(2 * qq, b + 4, sc, mn);
+    const float d = f16_at(b), dmin = f16_at(b + 2);
+    const float d1 = __fmul_rn(d, (float)sc), m1 = __fmul_rn(dmin, (float)mn);
+    scale_min_k4(2 * qq + 1, b + 4, sc, mn);
+    const float d2 = __fmul_rn(d, (float)sc), m2 = __fmul_rn(dmin, (float)mn);
+    const uint32_t *qw = reinterpret_cast<const uint32_t *>(b + 16 + 32 * qq);
+#pragma unroll
+    for (int w = 0; w < 8; ++w) {
+        const uint32_t q = qw[w];
+#pragma unroll
+        for (int k = 0; k < 4; ++k) {
+            const int l = 4 * w + k;
+            const int byte = (q >> (8 * k)) & 0xFF;
+            Wt[(64 * qq + l) * kWP + s] = __fsub_rn(__fmul_rn(d1, (float)(byte & 0x0F)), m1);
+            Wt[(64 * qq + 32 + l) * kWP + s] = __fsub_rn(__fmul_rn(d2, (float)(byte >> 4)), m2);
+        }
+    }
+}
+
+// The same for a Q6_K block (kore.cpp:359-381: value = (d * scale) * (q - 32)).
+// Quarter qq: half qq >> 1, groups 2 (qq & 1) and 2 (qq & 1) + 1 of it.
+__device__ __forceinline__ void dequant_q6k_quarter(const uint8_t *b, int qq, float *Wt, int s) {
+    const int half = qq >> 1, g0 = 2 * (qq & 1);
+    const uint8_t *ql = b + 64 * half, *qh = b + 128 + 32 * half;
+    const int8_t *sc = reinterpret_cast<const int8_t *>(b + 192 + 8 * half);
+    const float d = f16_at(b + 208);
+#pragma unroll
+    for (int gg = 0; gg < 2; ++gg) {
+        const int g = g0 + gg;
+        const float ds0 = __fmul_rn(d, (float)sc[2 * g]), ds1 = __fmul_rn(d, (float)sc[1 + 2 * g]);
+        const uint8_t *lo_src = (g & 1) ? ql + 32 : ql;
+#pragma unroll
+        for (int l = 0; l < 32; ++l) {
+            const int lo = lo_src[l];
+            const int q = (((g & 2) ? (lo >> 4) : (lo & 0x0F)) | (((qh[l] >> (2 * g)) & 3) << 4)) - 32;
+            Wt[(128 * half + 32 * g + l) * kWP + s] = __fmul_rn(l < 16 ? ds0 : ds1, (float)q);
+        }
+    }
+}
+
+__global__ void __launch_bounds__(kNT, 2) batch_matmul_kernel(const __grid_constant__ BatchMatmulParams p) {
     extern __shared__ __align__(16) float bsm[];
-    float *Xs = bsm;               // [256][kXPitch]: the tokens' 256 columns of one block, transposed
-    float *Ws = bsm + kXsFloats;   // [kRT][kWPitch]: the tile's rows of that block, dequantised
-    const int tid = threadIdx.x;
-    const int rp = tid >> 4, bq = tid & 15;          // row pair, token quad
+    float *Xs = bsm;               // [256][kXP]: the tokens' 256 columns of one block, transposed
+    float *Wt = bsm + kXsFloats;   // [256][kWP]: the tile's rows of that block, dequantised, transposed
+    const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+    const int rq = tid >> 4, tq = tid & 15;            // row quad, token quad of this thread's 16 chains
     const int b0 = blockIdx.y * kBT;
     const int nb = p.cols / 256;
     // the tile's weight rows: slot s holds (segment, row), or none
@@ -60,74 +109,77 @@ __global__ void __launch_bounds__(kNT) batch_matmul_kernel(const __grid_constant
         row = blockIdx.x * kRT + s;
         return row < p.seg[0].rows ? 0 : -1;
     };
-    float acc[2][4];
+    // dequantisation: thread (quarter qq = warp, slot s = lane) owns 64
+    // values of one row's block, so that a warp's stores fill one Wt row
+    const int ds = lane, dqq = warp;
+    int drow;
+    const int dsg = slot_row(ds, drow);
+    const uint8_t *dbase = nullptr;
+    bool dq4 = true;
+    if (dsg >= 0) {
+        const QSeg &q = p.seg[dsg];
+        dq4 = q.type == 12;
+        dbase = q.w + (size_t)drow * nb * block_stride(q.type);
+    }
+    float acc[4][4];
 #pragma unroll
-    for (int a = 0; a < 2; ++a)
+    for (int a = 0; a < 4; ++a)
 #pragma unroll
         for (int t = 0; t < 4; ++t) acc[a][t] = 0.f;
 
     for (int i = 0; i < nb; ++i) {
-        // dequantise block i of the tile's rows, kore's rounding (8 threads per row)
-        {
-            const int s = tid >> 3, j0 = (tid & 7) * 32;
-            int row;
-            const int sg = slot_row(s, row);
-            float *dst = Ws + s * kWPitch;
-            if (sg < 0) {
-                for (int j = j0; j < j0 + 32; ++j) dst[j] = 0.f;
-            } else {
-                const QSeg &q = p.seg[sg];
-                const bool q4 = q.type == 12;
-                const uint8_t *blk = q.w + ((size_t)row * nb + i) * block_stride(q.type);
-                if (q4)
-                    for (int j = j0; j < j0 + 32; ++j) dst[j] = q4k_value(blk, j);
-                else
-                    for (int j = j0; j < j0 + 32; ++j) dst[j] = q6k_value(blk, j);
-            }
+        if (dsg < 0) {
+            for (int j = 0; j < 64; ++j) Wt[(64 * dqq + j) * kWP + ds] = 0.f;
+        } else if (dq4) {
+            dequant_q4k_quarter(dbase + (size_t)i * kQ4Stride, dqq, Wt, ds);
+        } else {
+            dequant_q6k_quarter(dbase + (size_t)i * kQ6Stride, dqq, Wt, ds);
         }
-        // the tokens' columns of block i, transposed: Xs[j][b]
-        for (int e = tid; e < kBT * 256; e += kNT) {
-            const int b = e >> 8, j = e & 255;
-            Xs[j * kXPitch + b] = b0 + b < p.B ? p.x[(size_t)(b0 + b) * p.cols + (size_t)i * 256 + j] : 0.f;
+        // the tokens' columns of block i, transposed: a warp moves 4 tokens x 8
+        // columns per pass (coalesced 32-byte reads, conflict-free stores)
+        for (int pass = 0; pass < (kBT * 256) / kNT; ++pass) {
+            const int pair = pass * 4 + warp;               // (column octet, token quad) pair, 0..511
+            const int j = (pair & 31) * 8 + (lane & 7), b = (pair >> 5) * 4 + (lane >> 3);
+            Xs[j * kXP + b] = b0 + b < p.B ? p.x[(size_t)(b0 + b) * p.cols + (size_t)i * 256 + j] : 0.f;
         }
         __syncthreads();
-        const float *w0 = Ws + (2 * rp) * kWPitch, *w1 = w0 + kWPitch;
-        const float *xs = Xs + 4 * bq;
-#pragma unroll 8
+        const float *wj = Wt + 4 * rq, *xj = Xs + 4 * tq;
+#pragma unroll 4
         for (int j = 0; j < 256; ++j) {
-            const float a = w0[j], c = w1[j];
-            const float4 xv = *reinterpret_cast<const float4 *>(xs + j * kXPitch);
-            acc[0][0] = __fmaf_rn(a, xv.x, acc[0][0]);
-            acc[0][1] = __fmaf_rn(a, xv.y, acc[0][1]);
-            acc[0][2] = __fmaf_rn(a, xv.z, acc[0][2]);
-            acc[0][3] = __fmaf_rn(a, xv.w, acc[0][3]);
-            acc[1][0] = __fmaf_rn(c, xv.x, acc[1][0]);
-            acc[1][1] = __fmaf_rn(c, xv.y, acc[1][1]);
-            acc[1][2] = __fmaf_rn(c, xv.z, acc[1][2]);
-            acc[1][3] = __fmaf_rn(c, xv.w, acc[1][3]);
+            const float4 w4 = *reinterpret_cast<const float4 *>(wj + j * kWP);
+            const float4 x4 = *reinterpret_cast<const float4 *>(xj + j * kXP);
+            const float w[4] = {w4.x, w4.y, w4.z, w4.w}, x[4] = {x4.x, x4.y, x4.z, x4.w};
+#pragma unroll
+            for (int a = 0; a < 4; ++a)
+#pragma unroll
+                for (int t = 0; t < 4; ++t) acc[a][t] = __fmaf_rn(w[a], x[t], acc[a][t]);
         }
         __syncthreads();
     }
 
     // epilogue: bias, residual add or SwiGLU, as forward_batch does next
     if (p.pair) {
-        int row;
-        if (slot_row(2 * rp, row) < 0) return;
 #pragma unroll
-        for (int t = 0; t < 4; ++t) {
-            const int b = b0 + 4 * bq + t;
-            if (b < p.B) p.seg[0].out[(size_t)b * p.out_stride + row] = kore_swiglu(acc[0][t], acc[1][t], p.exp_tab);
+        for (int a = 0; a < 4; a += 2) {   // slots 4rq + a (gate) and 4rq + a + 1 (up) of one index
+            int row;
+            if (slot_row(4 * rq + a, row) < 0) continue;
+#pragma unroll
+            for (int t = 0; t < 4; ++t) {
+                const int b = b0 + 4 * tq + t;
+                if (b < p.B)
+                    p.seg[0].out[(size_t)b * p.out_stride + row] = kore_swiglu(acc[a][t], acc[a + 1][t], p.exp_tab);
+            }
         }
         return;
     }
 #pragma unroll
-    for (int a = 0; a < 2; ++a) {
+    for (int a = 0; a < 4; ++a) {
         int row;
-        if (slot_row(2 * rp + a, row) < 0) continue;
+        if (slot_row(4 * rq + a, row) < 0) continue;
         const QSeg &q = p.seg[0];
 #pragma unroll
         for (int t = 0; t < 4; ++t) {
-            const int b = b0 + 4 * bq + t;
+            const int b = b0 + 4 * tq + t;
             if (b >= p.B) continue;
             const size_t o = (size_t)b * p.out_stride + row;
             float v = acc[a][t];
