@@ -75,19 +75,26 @@ __device__ __forceinline__ void dequant_q4k_quarter(const uint8_t *b, int qq, fl
 // Quarter qq: half qq >> 1, groups 2 (qq & 1) and 2 (qq & 1) + 1 of it.
 __device__ __forceinline__ void dequant_q6k_quarter(const uint8_t *b, int qq, float *Wt, int s) {
     const int half = qq >> 1, g0 = 2 * (qq & 1);
-    const uint8_t *ql = b + 64 * half, *qh = b + 128 + 32 * half;
+    // uploaded Q6_K blocks are 4-byte aligned (kQ6Stride): read words
+    const uint32_t *ql = reinterpret_cast<const uint32_t *>(b + 64 * half);
+    const uint32_t *qh = reinterpret_cast<const uint32_t *>(b + 128 + 32 * half);
     const int8_t *sc = reinterpret_cast<const int8_t *>(b + 192 + 8 * half);
     const float d = f16_at(b + 208);
 #pragma unroll
     for (int gg = 0; gg < 2; ++gg) {
         const int g = g0 + gg;
         const float ds0 = __fmul_rn(d, (float)sc[2 * g]), ds1 = __fmul_rn(d, (float)sc[1 + 2 * g]);
-        const uint8_t *lo_src = (g & 1) ? ql + 32 : ql;
+        const uint32_t *lo_src = (g & 1) ? ql + 8 : ql;
 #pragma unroll
-        for (int l = 0; l < 32; ++l) {
-            const int lo = lo_src[l];
-            const int q = (((g & 2) ? (lo >> 4) : (lo & 0x0F)) | (((qh[l] >> (2 * g)) & 3) << 4)) - 32;
-            Wt[(128 * half + 32 * g + l) * kWP + s] = __fmul_rn(l < 16 ? ds0 : ds1, (float)q);
+        for (int w = 0; w < 8; ++w) {
+            const uint32_t lw = lo_src[w], hw = qh[w];
+#pragma unroll
+            for (int k = 0; k < 4; ++k) {
+                const int l = 4 * w + k;
+                const int lo = (lw >> (8 * k)) & 0xFF, hi2 = ((hw >> (8 * k)) >> (2 * g)) & 3;
+                const int q = (((g & 2) ? (lo >> 4) : (lo & 0x0F)) | (hi2 << 4)) - 32;
+                Wt[(128 * half + 32 * g + l) * kWP + s] = __fmul_rn(l < 16 ? ds0 : ds1, (float)q);
+            }
         }
     }
 }
@@ -137,10 +144,21 @@ __global__ void __launch_bounds__(kNT, 2) batch_matmul_kernel(const __grid_const
         }
         // the tokens' columns of block i, transposed: a warp moves 4 tokens x 8
         // columns per pass (coalesced 32-byte reads, conflict-free stores)
-        for (int pass = 0; pass < (kBT * 256) / kNT; ++pass) {
-            const int pair = pass * 4 + warp;               // (column octet, token quad) pair, 0..511
-            const int j = (pair & 31) * 8 + (lane & 7), b = (pair >> 5) * 4 + (lane >> 3);
-            Xs[j * kXP + b] = b0 + b < p.B ? p.x[(size_t)(b0 + b) * p.cols + (size_t)i * 256 + j] : 0.f;
+        constexpr int kPasses = (kBT * 256) / kNT, kDepth = 16;   // loads in flight per thread
+        for (int p0 = 0; p0 < kPasses; p0 += kDepth) {
+            float v[kDepth];
+#pragma unroll
+            for (int u = 0; u < kDepth; ++u) {
+                const int pair = (p0 + u) * 4 + warp;       // (column octet, token quad) pair, 0..511
+                const int j = (pair & 31) * 8 + (lane & 7), b = (pair >> 5) * 4 + (lane >> 3);
+                v[u] = b0 + b < p.B ? __ldg(p.x + (size_t)(b0 + b) * p.cols + (size_t)i * 256 + j) : 0.f;
+            }
+#pragma unroll
+            for (int u = 0; u < kDepth; ++u) {
+                const int pair = (p0 + u) * 4 + warp;
+                const int j = (pair & 31) * 8 + (lane & 7), b = (pair >> 5) * 4 + (lane >> 3);
+                Xs[j * kXP + b] = v[u];
+            }
         }
         __syncthreads();
         const float *wj = Wt + 4 * rq, *xj = Xs + 4 * tq;
