@@ -144,28 +144,39 @@ __global__ void __launch_bounds__(kNT, 2) batch_matmul_kernel(const __grid_const
         }
         // the tokens' columns of block i, transposed: a warp moves 4 tokens x 8
         // columns per pass (coalesced 32-byte reads, conflict-free stores)
-        constexpr int kPasses = (kBT * 256) / kNT, kDepth = 16;   // loads in flight per thread
+        // (16-byte loads, a round of them in flight per thread); a warp moves 4
+        // tokens x 32 columns per pass, 8 lanes per token. The token index is
+        // stored XOR-swizzled by the column's quad, x' = x ^ 4 ((j >> 2) & 7),
+        // so that the scattered stores fall on distinct banks while a token
+        // quad stays one 16-byte group for the product loop
+        constexpr int kPasses = (kBT * 256) / (kNT * 4), kDepth = 16;
         for (int p0 = 0; p0 < kPasses; p0 += kDepth) {
-            float v[kDepth];
+            float4 v[kDepth];
 #pragma unroll
             for (int u = 0; u < kDepth; ++u) {
-                const int pair = (p0 + u) * 4 + warp;       // (column octet, token quad) pair, 0..511
-                const int j = (pair & 31) * 8 + (lane & 7), b = (pair >> 5) * 4 + (lane >> 3);
-                v[u] = b0 + b < p.B ? __ldg(p.x + (size_t)(b0 + b) * p.cols + (size_t)i * 256 + j) : 0.f;
+                const int pair = (p0 + u) * 4 + warp;       // (32-column group, token quad), 0..127
+                const int j = (pair & 7) * 32 + 4 * (lane & 7), b = (pair >> 3) * 4 + (lane >> 3);
+                v[u] = b0 + b < p.B ? __ldg(reinterpret_cast<const float4 *>(p.x + (size_t)(b0 + b) * p.cols +
+                                                                              (size_t)i * 256 + j))
+                                    : make_float4(0.f, 0.f, 0.f, 0.f);
             }
 #pragma unroll
             for (int u = 0; u < kDepth; ++u) {
                 const int pair = (p0 + u) * 4 + warp;
-                const int j = (pair & 31) * 8 + (lane & 7), b = (pair >> 5) * 4 + (lane >> 3);
-                Xs[j * kXP + b] = v[u];
+                const int j = (pair & 7) * 32 + 4 * (lane & 7), b = (pair >> 3) * 4 + (lane >> 3);
+                const int bs = b ^ (4 * ((j >> 2) & 7));
+                Xs[(j + 0) * kXP + bs] = v[u].x;
+                Xs[(j + 1) * kXP + bs] = v[u].y;
+                Xs[(j + 2) * kXP + bs] = v[u].z;
+                Xs[(j + 3) * kXP + bs] = v[u].w;
             }
         }
         __syncthreads();
-        const float *wj = Wt + 4 * rq, *xj = Xs + 4 * tq;
+        const float *wj = Wt + 4 * rq;
 #pragma unroll 4
         for (int j = 0; j < 256; ++j) {
             const float4 w4 = *reinterpret_cast<const float4 *>(wj + j * kWP);
-            const float4 x4 = *reinterpret_cast<const float4 *>(xj + j * kXP);
+            const float4 x4 = *reinterpret_cast<const float4 *>(Xs + j * kXP + 4 * (tq ^ ((j >> 2) & 7)));
             const float w[4] = {w4.x, w4.y, w4.z, w4.w}, x[4] = {x4.x, x4.y, x4.z, x4.w};
 #pragma unroll
             for (int a = 0; a < 4; ++a)
