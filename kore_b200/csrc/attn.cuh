@@ -12,6 +12,7 @@ struct kore_cuda_ctx;
 namespace kore {
 
 constexpr int kMaxBatch = 256;    // queries per decode launch given by (seq, pos) list
+constexpr int kMaxRanksDecode = 8;   // ranks of a KV split (kMaxRanks)
 constexpr int kMaxSplits = 256;   // KV splits per (query, kv head)
 
 // One layer's slice of the paged KV pool.
@@ -51,6 +52,18 @@ struct DecodeParams {
                                //    are asked into L2 before the wait, so that HBM keeps streaming
                                //    while the preceding kernels finish
     int seq0, pos0;
+    // A KV-split decode step (n_q = 1) with its exchange in the same launch:
+    // the grid's first max_splits * G CTAs decode, each counting its arrival
+    // per query head in x_arrivals after its partial is written; the last H
+    // CTAs (one per query head) wait for their head's splits, merge them and
+    // exchange over peer memory (exchange.cuh), writing x_out.
+    int fused_exchange;
+    int x_ranks;
+    float *x_own;                  // this rank's exchange buffer
+    float *x_peers[kMaxRanksDecode];
+    size_t x_epoch_off;
+    float *x_out;                  // merged output [H*D]
+    int *x_arrivals;               // [H] splits arrived per query head; reset by the head's exchange CTA
     int seq[kMaxBatch];
     int pos[kMaxBatch];
 };
@@ -64,7 +77,7 @@ struct AppendParams {
     int seq, pos0, n;
 };
 
-constexpr int kMaxRanks = 8;
+constexpr int kMaxRanks = kMaxRanksDecode;
 
 // One prefill chunk of one layer (attn_prefill.cu).
 struct PrefillParams {

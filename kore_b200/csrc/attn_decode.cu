@@ -44,6 +44,7 @@
 #include "../../include/kore_cuda.h"
 #include "attn.cuh"
 #include "common.cuh"
+#include "exchange.cuh"
 #include "split_merge.cuh"
 
 #include <algorithm>
@@ -207,6 +208,59 @@ __device__ __forceinline__ void process_tile(WarpState<D, R> &st, const float *_
     __syncwarp();
 }
 
+// The exchange CTA of query head h in a fused KV-split decode launch (the
+// first D threads; the others leave): waits for the head's splits to arrive,
+// merges them (as split_merge_kernel would), then exchanges and merges the
+// ranks' partials (exchange.cuh), as peer_exchange_kernel does for one query.
+template <int D, int R>
+__device__ __forceinline__ void fused_exchange_cta(const DecodeParams &p, int h) {
+    __shared__ unsigned s_epoch;
+    __shared__ float s_lse[kMaxRanks];
+    grid_dep_launch();
+    grid_dep_wait();   // the previous step's exchange (the epochs) and this step's inputs
+    const int tid = threadIdx.x;
+    if (tid >= D) return;
+    const PagedKv &kv = p.kv;
+    const int pos = p.pos0;
+    const int count = shard_count_below(p.append_new ? pos : pos + 1, kv.P, kv.shard_count, kv.shard_rank);
+    const bool own_new = p.append_new && ((pos / kv.P) % kv.shard_count == kv.shard_rank);
+    int n_splits = (count + p.split_tokens - 1) / p.split_tokens;
+    if (n_splits == 0) n_splits = 1;
+    (void)own_new;
+    unsigned *epochs = reinterpret_cast<unsigned *>(reinterpret_cast<char *>(p.x_own) + p.x_epoch_off);
+    if (tid == 0) {
+        s_epoch = epochs[h] + 1u;
+        // bounded wait for the head's n_splits partials (their writes are
+        // released by a fence before each arrival is counted)
+        int seen = 0;
+        const uint64_t t0 = global_ns();
+        for (uint32_t it = 0;; ++it) {
+            asm volatile("ld.acquire.gpu.global.b32 %0, [%1];" : "=r"(seen) : "l"(p.x_arrivals + h) : "memory");
+            if (seen >= n_splits) break;
+            if ((it & 15) == 15 && global_ns() - t0 > p.wait_ns) {
+                raise_error(p.err, DEV_WAIT_FULL_TIMEOUT);
+                break;
+            }
+        }
+        p.x_arrivals[h] = 0;   // for the next launch (stream-ordered after this one)
+    }
+    __syncthreads();
+    const unsigned e = s_epoch;
+    const int g = h / R, r = h - g * R;
+    float o_me, lse_me;
+    if (n_splits > 1) {
+        const size_t base = (size_t)g * p.max_splits;
+        merge_head_splits<D>(p.part_o + base * R * D + (size_t)r * D + tid, (size_t)R * D, p.part_ml + base * R + r,
+                             (size_t)R, n_splits, o_me, lse_me);
+    } else {
+        o_me = __ldcg(p.out + (size_t)h * D + tid);
+        lse_me = __ldcg(p.lse + h);
+    }
+    exchange_and_merge<D>(o_me, lse_me, e, p.x_own, p.x_peers, p.x_ranks, kv.shard_rank, p.H, 0, h, p.err, p.wait_ns,
+                          p.x_out, s_lse);
+    if (tid == 0) epochs[h] = e;
+}
+
 template <int D, int R, int NW, int TT, int SPW>
 __global__ void __launch_bounds__(NW * 32, 1) attn_decode_kernel(const __grid_constant__ DecodeParams p) {
     constexpr int VEC = D / 32;
@@ -222,7 +276,17 @@ __global__ void __launch_bounds__(NW * 32, 1) attn_decode_kernel(const __grid_co
     uint64_t *full = reinterpret_cast<uint64_t *>(reinterpret_cast<char *>(smem) + SM::bar_off);
     int *pages = reinterpret_cast<int *>(full + NW * SPW);
 
-    const int split = blockIdx.x, g = blockIdx.y, qi = blockIdx.z;
+    int split = blockIdx.x, g = blockIdx.y, qi = blockIdx.z;
+    if (p.fused_exchange) {   // one query; CTAs [0, max_splits * G) decode, the last H exchange
+        const int nd = p.max_splits * p.kv.G;
+        if ((int)blockIdx.x >= nd) {
+            fused_exchange_cta<D, R>(p, (int)blockIdx.x - nd);
+            return;
+        }
+        split = (int)blockIdx.x % p.max_splits;
+        g = (int)blockIdx.x / p.max_splits;
+        qi = 0;
+    }
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
     const int seq = p.contiguous ? p.seq0 : p.seq[qi];
     const int pos = p.contiguous ? p.pos0 + qi : p.pos[qi];
@@ -450,6 +514,13 @@ __global__ void __launch_bounds__(NW * 32, 1) attn_decode_kernel(const __grid_co
             if (idx - h * D == 0) p.part_ml[(part_base + split) * R + h] = make_float2(M, L);
         }
     }
+    if (p.fused_exchange) {
+        // this split's partial is written: release it to the heads' exchange CTAs
+        __threadfence();
+        __syncthreads();
+        if (tid == 0)
+            for (int h = 0; h < R; ++h) atomicAdd(p.x_arrivals + g * R + h, 1);
+    }
 }
 
 // Merges the per-split partials of one query head (one CTA, one thread per
@@ -516,7 +587,7 @@ cudaError_t launch_shape(const DecodeParams &p, int grid_x, cudaStream_t s, bool
     auto kern = attn_decode_kernel<D, R, NW, kTT, SPW>;
     if (cudaError_t e = ensure_smem_limit(reinterpret_cast<const void *>(kern), (int)SM::bytes)) return e;
     cudaLaunchConfig_t cfg = {};
-    cfg.gridDim = dim3(grid_x, p.kv.G, p.n_q);
+    cfg.gridDim = p.fused_exchange ? dim3(grid_x * p.kv.G + p.H) : dim3(grid_x, p.kv.G, p.n_q);
     cfg.blockDim = dim3(NW * 32);
     cfg.dynamicSmemBytes = SM::bytes;
     cfg.stream = s;
@@ -526,7 +597,7 @@ cudaError_t launch_shape(const DecodeParams &p, int grid_x, cudaStream_t s, bool
     cfg.attrs = attr;
     cfg.numAttrs = 1;
     cudaError_t e = cudaLaunchKernelEx(&cfg, kern, p);
-    if (e != cudaSuccess || grid_x == 1 || !merge) return e;
+    if (e != cudaSuccess || grid_x == 1 || !merge || p.fused_exchange) return e;
     cudaLaunchConfig_t mcfg = cfg;
     mcfg.gridDim = dim3(p.kv.G * R, p.n_q);
     mcfg.blockDim = dim3(D);

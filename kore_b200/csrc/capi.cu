@@ -64,6 +64,9 @@ struct kore_cuda_ctx {
     // exchange still runs (KORE_CUDA_SHARD_PREFETCH=0 turns it off)
     bool shard_prefetch = true;
     bool hold_prefetch = false;   // set: the next decode waits before its first KV fetch
+    // KV-split decode: the exchange in the decode's own launch (KORE_CUDA_FUSED_EXCHANGE=0 turns it off)
+    bool fused_exchange = true;
+    int *x_arrivals = nullptr;    // [H] arrivals per query head of the fused launch
     int prefetch_stages = 3;      // ring stages fetched early (KORE_CUDA_PREFETCH_STAGES)
     int shard_ctas = 0;           // decode CTAs aimed at on a KV-split context (KORE_CUDA_SHARD_CTAS; 0: 2 per SM)
     int decode_ctas = 0;          // decode CTAs aimed at otherwise (KORE_CUDA_DECODE_CTAS; 0: 2 per SM)
@@ -368,8 +371,10 @@ int finish(kore_cuda_ctx *c, size_t extra = 0) {
     const int e = *c->host_err;
     if (e != DEV_OK) {
         CK(cudaMemsetAsync(c->err_d, 0, sizeof(int), c->stream));
-        // a prefill that gave up may have left a split half's arrival counted
+        // a prefill that gave up may have left a split half's arrival counted,
+        // a fused exchange that gave up its head's arrivals
         if (c->pf_counters) CK(cudaMemsetAsync(c->pf_counters, 0, c->pf_slots_cap * sizeof(int), c->stream));
+        if (c->x_arrivals) CK(cudaMemsetAsync(c->x_arrivals, 0, (size_t)c->H * sizeof(int), c->stream));
         CK(cudaStreamSynchronize(c->stream));
         return fail(c, KORE_CUDA_EDEVICE, "device error %d (%s)", e, device_error_text(e));
     }
@@ -395,7 +400,8 @@ int run_append(kore_cuda_ctx *c, int seq, int layer, int pos0, int n, const floa
 // (seq0, pos0 + i); otherwise seqs[i], poss[i] (host arrays, n_q <= kMaxBatch).
 int run_decode(kore_cuda_ctx *c, int layer, int n_q, bool contiguous, int seq0, int pos0, const int *seqs,
                const int *poss, const float *q, const float *k, const float *v, float *out, float *lse,
-               bool append_new, bool launch_merge = true, int *grid_out = nullptr, int *st_out = nullptr) {
+               bool append_new, bool launch_merge = true, int *grid_out = nullptr, int *st_out = nullptr,
+               float *fused_out = nullptr) {
     if (n_q <= 0) return fail(c, KORE_CUDA_EINVAL, "no queries");
     if (!contiguous && n_q > kMaxBatch)
         return fail(c, KORE_CUDA_EINVAL, "decode batch of %d exceeds %d sequences per call", n_q, kMaxBatch);
@@ -522,6 +528,15 @@ int run_decode(kore_cuda_ctx *c, int layer, int n_q, bool contiguous, int seq0, 
     if (grid_x > kMaxSplits) return fail(c, KORE_CUDA_EINVAL, "too many splits for one decode launch");
     p.split_tokens = (int)st;
     p.max_splits = grid_x;
+    if (fused_out) {   // the exchange CTAs join this launch (peer_exchange.cu's protocol)
+        p.fused_exchange = 1;
+        p.x_ranks = c->NS;
+        p.x_own = c->xbuf;
+        for (int r = 0; r < c->NS; ++r) p.x_peers[r] = c->peers[r];
+        p.x_epoch_off = c->x_epoch_off;
+        p.x_out = fused_out;
+        p.x_arrivals = c->x_arrivals;
+    }
     p.prefetch_ok = !c->hold_prefetch && c->last_kv_layer != layer;
     p.prefetch_stages = c->prefetch_stages;
     c->hold_prefetch = false;
@@ -567,6 +582,7 @@ void kore_cuda_destroy(kore_cuda_ctx *c) {
         for (int r = 0; r < kMaxRanks; ++r)
             if (c->peers[r] && c->peers[r] != c->xbuf) cudaIpcCloseMemHandle(c->peers[r]);
         cudaFree(c->xbuf);
+        cudaFree(c->x_arrivals);
         cudaFree(c->split);
         cudaFree(c->pf_items);
         cudaFree(c->pf_part);
@@ -662,6 +678,7 @@ int kore_cuda_create(kore_cuda_ctx **out, const kore_cuda_cfg *cfg) {
     if (const char *ps = getenv("KORE_CUDA_PREFETCH_STAGES")) c->prefetch_stages = std::max(0, atoi(ps));
     if (const char *sc = getenv("KORE_CUDA_SHARD_CTAS")) c->shard_ctas = std::max(0, atoi(sc));
     if (const char *dc = getenv("KORE_CUDA_DECODE_CTAS")) c->decode_ctas = std::max(0, atoi(dc));
+    if (const char *fx = getenv("KORE_CUDA_FUSED_EXCHANGE")) c->fused_exchange = atoi(fx) != 0;
     CKB(cudaStreamCreateWithFlags(&c->stream, cudaStreamNonBlocking));
     c->own_stream = true;
 
@@ -939,6 +956,8 @@ int kore_cuda_peer_handle(kore_cuda_ctx *c, void *handle) {
         c->x_bytes = c->x_local_off + align256(PF * sizeof(float));
         CK(cudaMalloc(&c->xbuf, c->x_bytes));
         CK(cudaMemset(c->xbuf, 0, c->x_bytes));
+        CK(cudaMalloc(&c->x_arrivals, (size_t)c->H * sizeof(int)));
+        CK(cudaMemset(c->x_arrivals, 0, (size_t)c->H * sizeof(int)));
         CK(cudaDeviceSynchronize());
     }
     cudaIpcMemHandle_t h;
@@ -1007,12 +1026,14 @@ int kore_cuda_attn_decode_sharded_dev(kore_cuda_ctx *c, int seq, int layer, int 
     DeviceGuard dg(c->cfg.device);
     if (int rc = ensure_pages(c, seq, pos + 1)) return rc;
     float *local = reinterpret_cast<float *>(reinterpret_cast<char *>(c->xbuf) + c->x_local_off);
-    int grid_x = 1, st = 0;   // the splits are merged by the exchange kernel itself
+    int grid_x = 1, st = 0;   // the splits are merged by the exchange itself
     if (int rc = run_decode(c, layer, 1, true, seq, pos, nullptr, nullptr, q, k, v, local,
-                            local + (size_t)kExchangeQueries * c->H * c->D, true, false, &grid_x, &st))
+                            local + (size_t)kExchangeQueries * c->H * c->D, true, false, &grid_x, &st,
+                            c->fused_exchange ? out : nullptr))
         return rc;
     note_len(c, seq, layer, pos + 1);
-    if (int rc = launch_exchange(c, 1, pos, true, grid_x, st, out)) return rc;
+    if (!c->fused_exchange)
+        if (int rc = launch_exchange(c, 1, pos, true, grid_x, st, out)) return rc;
     c->last_kv_layer = layer;   // the decode may still run when the next kernel starts
     c->hold_prefetch = !c->shard_prefetch;
     return KORE_CUDA_OK;

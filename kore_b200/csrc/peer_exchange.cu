@@ -31,44 +31,16 @@
 
 #include "attn.cuh"
 #include "common.cuh"
+#include "exchange.cuh"
 #include "split_merge.cuh"
 
 namespace kore {
 namespace {
 
-// One (value, epoch) pair as a single 64-bit word: one scalar access, which
-// is single-copy atomic (a vector access of two 32-bit halves would not be).
-__device__ __forceinline__ void st_pair_sys(uint64_t *p, uint32_t value, uint32_t epoch) {
-    const uint64_t w = (uint64_t)value | ((uint64_t)epoch << 32);
-    asm volatile("st.relaxed.sys.global.b64 [%0], %1;" ::"l"(p), "l"(w) : "memory");
-}
-
-__device__ __forceinline__ uint64_t ld_pair_sys(const uint64_t *p) {
-    uint64_t w;
-    asm volatile("ld.relaxed.sys.global.b64 %0, [%1];" : "=l"(w) : "l"(p) : "memory");
-    return w;
-}
-
-// Waits (bounded by limit_ns) until the word at p carries `epoch`; returns its value.
-__device__ __forceinline__ float await_pair(const uint64_t *p, uint32_t epoch, int *err, uint64_t limit_ns) {
-    uint64_t w = ld_pair_sys(p);
-    if ((uint32_t)(w >> 32) == epoch) return __uint_as_float((uint32_t)w);
-    const uint64_t t0 = global_ns();
-    for (;;) {
-        w = ld_pair_sys(p);
-        if ((uint32_t)(w >> 32) == epoch) return __uint_as_float((uint32_t)w);
-        if (global_ns() - t0 > limit_ns) {
-            raise_error(err, DEV_PEER_TIMEOUT);
-            return 0.f;
-        }
-    }
-}
-
 template <int D>
 __global__ void __launch_bounds__(D) peer_exchange_kernel(const __grid_constant__ ExchangeParams p) {
     const int h = blockIdx.x, qi = blockIdx.y, tid = threadIdx.x;
     const int N = p.n_ranks, me = p.rank, H = p.H;
-    constexpr int SLOT = D + 1;   // words per (rank, query, head): D outputs, then the LSE
     constexpr int Q = kExchangeQueries;
     __shared__ unsigned s_epoch;
     __shared__ float s_lse[kMaxRanks];
@@ -82,7 +54,6 @@ __global__ void __launch_bounds__(D) peer_exchange_kernel(const __grid_constant_
     grid_dep_wait();       // this rank's partial is complete and visible
     __syncthreads();
     const unsigned e = s_epoch;
-    const int par = e & 1u;
     // this rank's partial of (qi, h): the decode's own output (one split) or
     // the merge of its splits, kept in registers
     const int pos = p.pos0 + qi;
@@ -99,43 +70,7 @@ __global__ void __launch_bounds__(D) peer_exchange_kernel(const __grid_constant_
         lse_me = __ldcg(p.local + (size_t)Q * H * D + (size_t)qi * H + h);
     }
 
-    // 1. push it to every peer: one 64-bit (value, epoch) store per element
-    for (int r = 0; r < N; ++r) {
-        if (r == me) continue;
-        uint64_t *dst = reinterpret_cast<uint64_t *>(p.peers[r]) + ((((size_t)par * N + me) * Q + qi) * H + h) * SLOT;
-        st_pair_sys(dst + tid, __float_as_uint(o_me), e);
-        if (tid == 0) st_pair_sys(dst + D, __float_as_uint(lse_me), e);
-    }
-
-    // 2. collect every peer's element tid (thread 0 also the LSEs)
-    const uint64_t *own = reinterpret_cast<const uint64_t *>(p.own);
-    float x[kMaxRanks];
-#pragma unroll
-    for (int r = 0; r < kMaxRanks; ++r) {
-        x[r] = 0.f;
-        if (r < N && r != me) {
-            const uint64_t *src = own + ((((size_t)par * N + r) * Q + qi) * H + h) * SLOT;
-            x[r] = await_pair(src + tid, e, p.err, p.wait_ns);
-            if (tid == 0) s_lse[r] = await_pair(src + D, e, p.err, p.wait_ns);
-        }
-    }
-    if (tid == 0) s_lse[me] = lse_me;
-    __syncthreads();
-
-    // 3. merge the N partials of (qi, h)
-    float M = -INFINITY;
-    for (int r = 0; r < N; ++r) M = fmaxf(M, s_lse[r]);
-    float acc = 0.f, wsum = 0.f;
-    if (M != -INFINITY) {
-#pragma unroll
-        for (int r = 0; r < kMaxRanks; ++r) {
-            if (r >= N) break;
-            const float w = fast_exp2(s_lse[r] - M);
-            wsum += w;
-            acc = fmaf(w, r == me ? o_me : x[r], acc);
-        }
-    }
-    p.out[((size_t)qi * H + h) * D + tid] = wsum > 0.f ? acc / wsum : 0.f;
+    exchange_and_merge<D>(o_me, lse_me, e, p.own, p.peers, N, me, H, qi, h, p.err, p.wait_ns, p.out, s_lse);
     if (tid == 0) epochs[qi * H + h] = e;
 }
 
