@@ -1,7 +1,10 @@
 """Builds kore_b200/libkore_cuda.so (the C-ABI library) with nvcc for sm_100a.
 
-Usage: ``python -m kore_b200.build [--force] [--verbose]``. The library is
-built in-tree so that it travels with the repository to the GPU machine.
+Usage: ``python -m kore_b200.build [--force] [--verbose] [--trace]``. The
+library is built in-tree so that it travels with the repository to the GPU
+machine. ``--trace`` builds kore_b200/libkore_cuda_trace.so instead: the same
+library compiled with KORE_TRACE, whose decode and merge CTAs record
+%globaltimer stamps (read by ``python -m kore_b200.trace_decode``).
 """
 from __future__ import annotations
 
@@ -16,6 +19,7 @@ ROOT = os.path.dirname(PKG)
 CSRC = os.path.join(PKG, "csrc")
 INCLUDE = os.path.join(ROOT, "include")
 LIB = os.path.join(PKG, "libkore_cuda.so")
+TRACE_LIB = os.path.join(PKG, "libkore_cuda_trace.so")
 
 ARCH = ["-gencode", "arch=compute_100a,code=sm_100a"]
 NVCC_FLAGS = ["-O3", "-std=c++17", "-lineinfo", "--expt-relaxed-constexpr", "-Xcompiler", "-fPIC,-O2",
@@ -33,36 +37,36 @@ def sources() -> list[str]:
     return sorted(glob.glob(os.path.join(CSRC, "*.cu")))
 
 
-def _stale() -> bool:
-    if not os.path.exists(LIB):
+def _stale(lib: str = LIB) -> bool:
+    if not os.path.exists(lib):
         return True
-    t = os.path.getmtime(LIB)
+    t = os.path.getmtime(lib)
     deps = sources() + glob.glob(os.path.join(CSRC, "*.cuh")) + glob.glob(os.path.join(INCLUDE, "*.h"))
     return any(os.path.getmtime(d) > t for d in deps)
 
 
-def build(force: bool = False, verbose: bool = False) -> str:
+def build(force: bool = False, verbose: bool = False, trace: bool = False) -> str:
     """Compiles every .cu under csrc/ into one shared library; returns its path."""
-    if not force and not _stale():
-        return LIB
-    objdir = os.path.join(PKG, "_build")
+    lib = TRACE_LIB if trace else LIB
+    if not force and not _stale(lib):
+        return lib
+    objdir = os.path.join(PKG, "_build_trace" if trace else "_build")
     os.makedirs(objdir, exist_ok=True)
     objs = []
     for src in sources():
         obj = os.path.join(objdir, os.path.basename(src)[:-3] + ".o")
-        cmd = [nvcc(), *ARCH, *NVCC_FLAGS, "-I", INCLUDE, "-c", src, "-o", obj]
+        cmd = [nvcc(), *ARCH, *NVCC_FLAGS, *(["-DKORE_TRACE"] if trace else []), "-I", INCLUDE, "-c", src, "-o", obj]
         if verbose:
             cmd += ["-Xptxas", "-v"]
             print(" ".join(cmd), flush=True)
         subprocess.run(cmd, check=True)
         objs.append(obj)
-    tmp = LIB + ".tmp"
+    tmp = lib + ".tmp"
     subprocess.run([nvcc(), *ARCH, "-shared", "-o", tmp, *objs, "-lcudart_static", "-lrt", "-ldl", "-lpthread"],
                    check=True)
-    os.replace(tmp, LIB)
-    return LIB
+    os.replace(tmp, lib)
+    return lib
 
 
 if __name__ == "__main__":
-    build(force="--force" in sys.argv, verbose="--verbose" in sys.argv)
-    print(LIB)
+    print(build(force="--force" in sys.argv, verbose="--verbose" in sys.argv, trace="--trace" in sys.argv))

@@ -32,10 +32,16 @@
 // division by the running sum cancels m_ref exactly, as in any online softmax.
 //
 // Merge: warps merge in shared memory; with one split the CTA writes the
-// normalised output, otherwise it writes (max, sum, o) to scratch and exits,
-// and split_merge_kernel — launched next with a programmatic dependency, one
-// CTA per query head with every partial load in flight at once — combines the
-// splits. (A last-arriving-CTA merge, ordered by an atomic, measured ~8 us of
+// normalised output, otherwise it writes (max, sum, o) to scratch. A
+// single-query decode then counts its arrival per query head, and one merge
+// CTA per query head at the end of the same grid waits for its head's splits
+// and combines them (fused_exchange_cta; on a KV-split context it also runs
+// the cross-GPU exchange). Otherwise split_merge_kernel — launched next with
+// a programmatic dependency, one CTA per query head with every partial load
+// in flight at once — combines the splits. The merge in the decode's own
+// launch lets the next layer's dependency wait return ~4 us earlier (traced:
+// the separate kernel's CTAs sit behind the decode grid, then wait for its
+// completion). (A last-arriving-CTA merge, ordered by an atomic, measured ~8 us of
 // serial tail per launch on B200: the release atomic drains the CTA's stores
 // and one SM then pulls every partial of its head.) In a KV-sharded context
 // (positions split over GPUs) the output is the normalised partial plus its
@@ -208,28 +214,66 @@ __device__ __forceinline__ void process_tile(WarpState<D, R> &st, const float *_
     __syncwarp();
 }
 
-// The exchange CTA of query head h in a fused KV-split decode launch (the
-// first D threads; the others leave): waits for the head's splits to arrive,
-// merges them (as split_merge_kernel would), then exchanges and merges the
-// ranks' partials (exchange.cuh), as peer_exchange_kernel does for one query.
+#ifdef KORE_TRACE
+// Trace build only (kore_b200/build.py --trace): %globaltimer stamps of every
+// decode, split-merge and merge CTA, read back with kore_trace_read. Thread 0
+// of a CTA claims a record and stamps it at fixed points (TraceRec::t).
+struct TraceRec {
+    unsigned long long t[5];   // entry, dependency wait returned, inputs staged / arrivals seen, tiles done, end
+    unsigned blk, sm, kind, pad;   // kind: 0 decode, 1 split_merge_kernel, 2 merge CTA of a fused launch
+    unsigned long long pad2;
+};
+constexpr unsigned kTraceRecs = 1u << 16;
+__device__ TraceRec g_trace[kTraceRecs];
+__device__ unsigned g_trace_n;
+__device__ __forceinline__ unsigned trace_open(unsigned kind) {
+    if (threadIdx.x != 0) return kTraceRecs;
+    const unsigned slot = atomicAdd(&g_trace_n, 1u);
+    if (slot < kTraceRecs) {
+        unsigned sm;
+        asm volatile("mov.u32 %0, %%smid;" : "=r"(sm));
+        g_trace[slot].t[0] = global_ns();
+        g_trace[slot].blk = blockIdx.x | (blockIdx.y << 16);
+        g_trace[slot].sm = sm;
+        g_trace[slot].kind = kind;
+    }
+    return slot;
+}
+__device__ __forceinline__ void trace_stamp(unsigned slot, int i) {
+    if (slot < kTraceRecs) g_trace[slot].t[i] = global_ns();
+}
+#define KTRACE_OPEN(kind) const unsigned tr_slot_ = trace_open(kind)
+#define KTRACE(i) trace_stamp(tr_slot_, i)
+#else
+#define KTRACE_OPEN(kind)
+#define KTRACE(i)
+#endif
+
+// The merge CTA of query head h at the end of a fused decode launch (the
+// first D threads; the others leave): waits for the head's splits to arrive
+// and merges them (as split_merge_kernel would). On a KV-split context it then
+// exchanges and merges the ranks' partials (exchange.cuh), as
+// peer_exchange_kernel does for one query; on one GPU it writes the output.
 template <int D, int R>
 __device__ __forceinline__ void fused_exchange_cta(const DecodeParams &p, int h) {
     __shared__ unsigned s_epoch;
     __shared__ float s_lse[kMaxRanks];
+    KTRACE_OPEN(2);
     grid_dep_launch();
     grid_dep_wait();   // the previous step's exchange (the epochs) and this step's inputs
+    KTRACE(1);
     const int tid = threadIdx.x;
     if (tid >= D) return;
     const PagedKv &kv = p.kv;
     const int pos = p.pos0;
     const int count = shard_count_below(p.append_new ? pos : pos + 1, kv.P, kv.shard_count, kv.shard_rank);
-    const bool own_new = p.append_new && ((pos / kv.P) % kv.shard_count == kv.shard_rank);
     int n_splits = (count + p.split_tokens - 1) / p.split_tokens;
     if (n_splits == 0) n_splits = 1;
-    (void)own_new;
-    unsigned *epochs = reinterpret_cast<unsigned *>(reinterpret_cast<char *>(p.x_own) + p.x_epoch_off);
+    const bool xchg = p.x_ranks > 1;
+    unsigned *epochs =
+        xchg ? reinterpret_cast<unsigned *>(reinterpret_cast<char *>(p.x_own) + p.x_epoch_off) : nullptr;
     if (tid == 0) {
-        s_epoch = epochs[h] + 1u;
+        if (xchg) s_epoch = epochs[h] + 1u;
         // bounded wait for the head's n_splits partials (their writes are
         // released by a fence before each arrival is counted)
         int seen = 0;
@@ -245,8 +289,21 @@ __device__ __forceinline__ void fused_exchange_cta(const DecodeParams &p, int h)
         p.x_arrivals[h] = 0;   // for the next launch (stream-ordered after this one)
     }
     __syncthreads();
-    const unsigned e = s_epoch;
+    KTRACE(2);
     const int g = h / R, r = h - g * R;
+    if (!xchg) {   // one GPU: the merged splits are the output (one split wrote it directly)
+        if (n_splits > 1) {
+            const size_t base = (size_t)g * p.max_splits;
+            float o, lse;
+            merge_head_splits<D>(p.part_o + base * R * D + (size_t)r * D + tid, (size_t)R * D,
+                                 p.part_ml + base * R + r, (size_t)R, n_splits, o, lse);
+            p.out[(size_t)h * D + tid] = o;
+            if (p.lse && tid == 0) p.lse[h] = lse;
+        }
+        KTRACE(4);
+        return;
+    }
+    const unsigned e = s_epoch;
     float o_me, lse_me;
     if (n_splits > 1) {
         const size_t base = (size_t)g * p.max_splits;
@@ -259,6 +316,7 @@ __device__ __forceinline__ void fused_exchange_cta(const DecodeParams &p, int h)
     exchange_and_merge<D>(o_me, lse_me, e, p.x_own, p.x_peers, p.x_ranks, kv.shard_rank, p.H, 0, h, p.err, p.wait_ns,
                           p.x_out, s_lse);
     if (tid == 0) epochs[h] = e;
+    KTRACE(4);
 }
 
 template <int D, int R, int NW, int TT, int SPW>
@@ -287,6 +345,7 @@ __global__ void __launch_bounds__(NW * 32, 1) attn_decode_kernel(const __grid_co
         g = (int)blockIdx.x / p.max_splits;
         qi = 0;
     }
+    KTRACE_OPEN(0);
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
     const int seq = p.contiguous ? p.seq0 : p.seq[qi];
     const int pos = p.contiguous ? p.pos0 + qi : p.pos[qi];
@@ -381,6 +440,7 @@ __global__ void __launch_bounds__(NW * 32, 1) attn_decode_kernel(const __grid_co
         }
     }
     if (p.prefetch_ok) grid_dep_wait();
+    KTRACE(1);
     grid_dep_launch();
     if (lane == 0)
         for (int j = pre; j < SPW && j < my_tiles; ++j) issue(j);
@@ -404,6 +464,7 @@ __global__ void __launch_bounds__(NW * 32, 1) attn_decode_kernel(const __grid_co
         }
     }
     __syncthreads();
+    KTRACE(2);
     const float2 *cs = reinterpret_cast<const float2 *>(qsm + R * D);
 
     WarpState<D, R> st;
@@ -471,6 +532,7 @@ __global__ void __launch_bounds__(NW * 32, 1) attn_decode_kernel(const __grid_co
     st.l += __shfl_xor_sync(FULL, st.l, 8);
     st.l += __shfl_xor_sync(FULL, st.l, 16);
     __syncthreads();   // every tile consumed: the stage memory is free
+    KTRACE(3);
     {
         float *cm = stages;              // [NW][8]
         float *cl = cm + NW * 8;         // [NW][8]
@@ -515,12 +577,16 @@ __global__ void __launch_bounds__(NW * 32, 1) attn_decode_kernel(const __grid_co
         }
     }
     if (p.fused_exchange) {
-        // this split's partial is written: release it to the heads' exchange CTAs
+        // this split's partial is written: release it to the heads' merge CTAs
         __threadfence();
         __syncthreads();
         if (tid == 0)
             for (int h = 0; h < R; ++h) atomicAdd(p.x_arrivals + g * R + h, 1);
     }
+#ifdef KORE_TRACE
+    __syncthreads();
+    KTRACE(4);
+#endif
 }
 
 // Merges the per-split partials of one query head (one CTA, one thread per
@@ -532,8 +598,10 @@ __global__ void __launch_bounds__(D) split_merge_kernel(const __grid_constant__ 
     // prefetches KV of a layer that neither this kernel nor the decode before
     // it writes (checked on the host), and waits for this kernel before
     // anything else
+    KTRACE_OPEN(1);
     grid_dep_launch();
     grid_dep_wait();
+    KTRACE(1);
     const int h = blockIdx.x % R, g = blockIdx.x / R, qi = blockIdx.y, tid = threadIdx.x;
     const int pos = p.contiguous ? p.pos0 + qi : p.pos[qi];
     const PagedKv &kv = p.kv;
@@ -548,6 +616,7 @@ __global__ void __launch_bounds__(D) split_merge_kernel(const __grid_constant__ 
     const size_t qh = (size_t)qi * p.H + (size_t)g * R + h;
     p.out[qh * D + tid] = o;
     if (p.lse && tid == 0) p.lse[qh] = lse;
+    KTRACE(4);
 }
 
 #ifndef KORE_DECODE_NW
@@ -787,3 +856,29 @@ extern "C" int kore_cuda_attn_decode_noalloc(const kore_cuda_kv_view *kv, int po
     if (e != cudaSuccess) return noalloc_fail(KORE_CUDA_ECUDA, "decode launch failed (error %lld)", (long long)e);
     return KORE_CUDA_OK;
 }
+
+#ifdef KORE_TRACE
+// Trace build only: the stamps of the CTAs run since the last reset, as
+// kore::TraceRec records of 64 bytes (see above), in the order the CTAs
+// claimed them. Not part of the ABI.
+extern "C" int kore_trace_read(void *host, int max_recs, int *n_recs) {
+    using namespace kore;
+    static_assert(sizeof(TraceRec) == 64, "trace record layout");
+    unsigned n = 0;
+    if (cudaDeviceSynchronize() != cudaSuccess || cudaMemcpyFromSymbol(&n, g_trace_n, sizeof n) != cudaSuccess)
+        return KORE_CUDA_ECUDA;
+    n = n < kTraceRecs ? n : kTraceRecs;
+    const unsigned m = max_recs < 0 ? 0u : ((unsigned)max_recs < n ? (unsigned)max_recs : n);
+    if (m && cudaMemcpyFromSymbol(host, g_trace, (size_t)m * sizeof(TraceRec)) != cudaSuccess) return KORE_CUDA_ECUDA;
+    if (n_recs) *n_recs = (int)m;
+    return KORE_CUDA_OK;
+}
+
+extern "C" int kore_trace_reset(void) {
+    using namespace kore;
+    const unsigned z = 0;
+    if (cudaDeviceSynchronize() != cudaSuccess || cudaMemcpyToSymbol(g_trace_n, &z, sizeof z) != cudaSuccess)
+        return KORE_CUDA_ECUDA;
+    return KORE_CUDA_OK;
+}
+#endif

@@ -66,7 +66,10 @@ struct kore_cuda_ctx {
     bool hold_prefetch = false;   // set: the next decode waits before its first KV fetch
     // KV-split decode: the exchange in the decode's own launch (KORE_CUDA_FUSED_EXCHANGE=0 turns it off)
     bool fused_exchange = true;
-    int *x_arrivals = nullptr;    // [H] arrivals per query head of the fused launch
+    // one GPU: the split merge of a single-query decode in the decode's own
+    // launch (KORE_CUDA_FUSED_MERGE=0 launches split_merge_kernel instead)
+    bool fused_merge = true;
+    int *x_arrivals = nullptr;    // [H] arrivals per query head of a fused launch
     int prefetch_stages = 3;      // ring stages fetched early (KORE_CUDA_PREFETCH_STAGES)
     int shard_ctas = 0;           // decode CTAs aimed at on a KV-split context (KORE_CUDA_SHARD_CTAS; 0: 2 per SM)
     int decode_ctas = 0;          // decode CTAs aimed at otherwise (KORE_CUDA_DECODE_CTAS; 0: 2 per SM)
@@ -536,6 +539,11 @@ int run_decode(kore_cuda_ctx *c, int layer, int n_q, bool contiguous, int seq0, 
         p.x_epoch_off = c->x_epoch_off;
         p.x_out = fused_out;
         p.x_arrivals = c->x_arrivals;
+    } else if (c->fused_merge && c->NS == 1 && n_q == 1 && contiguous && launch_merge && grid_x > 1) {
+        // one GPU: the heads' merge CTAs join this launch instead of split_merge_kernel
+        p.fused_exchange = 1;
+        p.x_ranks = 1;
+        p.x_arrivals = c->x_arrivals;
     }
     p.prefetch_ok = !c->hold_prefetch && c->last_kv_layer != layer;
     p.prefetch_stages = c->prefetch_stages;
@@ -679,6 +687,7 @@ int kore_cuda_create(kore_cuda_ctx **out, const kore_cuda_cfg *cfg) {
     if (const char *sc = getenv("KORE_CUDA_SHARD_CTAS")) c->shard_ctas = std::max(0, atoi(sc));
     if (const char *dc = getenv("KORE_CUDA_DECODE_CTAS")) c->decode_ctas = std::max(0, atoi(dc));
     if (const char *fx = getenv("KORE_CUDA_FUSED_EXCHANGE")) c->fused_exchange = atoi(fx) != 0;
+    if (const char *fm = getenv("KORE_CUDA_FUSED_MERGE")) c->fused_merge = atoi(fm) != 0;
     CKB(cudaStreamCreateWithFlags(&c->stream, cudaStreamNonBlocking));
     c->own_stream = true;
 
@@ -706,6 +715,8 @@ int kore_cuda_create(kore_cuda_ctx **out, const kore_cuda_cfg *cfg) {
     c->part_slots = kPartSlots;
     CKB(cudaMalloc(&c->part_o, c->part_slots * c->R * c->D * sizeof(float)));
     CKB(cudaMalloc(&c->part_ml, c->part_slots * c->R * sizeof(float2)));
+    CKB(cudaMalloc(&c->x_arrivals, (size_t)c->H * sizeof(int)));
+    CKB(cudaMemsetAsync(c->x_arrivals, 0, (size_t)c->H * sizeof(int), c->stream));
     // the device error word heads a buffer that also receives one sequence's
     // decode output, so that the host-buffer decode fetches both with one copy
     const size_t err_bytes = kErrPad + (size_t)c->H * c->D * sizeof(float);
@@ -956,8 +967,6 @@ int kore_cuda_peer_handle(kore_cuda_ctx *c, void *handle) {
         c->x_bytes = c->x_local_off + align256(PF * sizeof(float));
         CK(cudaMalloc(&c->xbuf, c->x_bytes));
         CK(cudaMemset(c->xbuf, 0, c->x_bytes));
-        CK(cudaMalloc(&c->x_arrivals, (size_t)c->H * sizeof(int)));
-        CK(cudaMemset(c->x_arrivals, 0, (size_t)c->H * sizeof(int)));
         CK(cudaDeviceSynchronize());
     }
     cudaIpcMemHandle_t h;

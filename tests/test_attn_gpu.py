@@ -102,6 +102,29 @@ def test_cfg4_7b_decode_at_32768():
     assert_attn_close(g.decode(0, 0, 32768, q, k, v), o.decode(32768, q, k, v), "cfg4 decode")
 
 
+@pytest.mark.parametrize("H,G,d,pos", [(28, 4, 128, 32768), (28, 4, 128, 3000), (14, 2, 64, 191),
+                                       (16, 2, 128, 5000), (28, 4, 128, 300)])
+def test_fused_split_merge_equals_separate_merge_kernel(H, G, d, pos, monkeypatch):
+    """One GPU: the merge CTAs at the end of the decode launch give the same
+    bits as split_merge_kernel (the same merge arithmetic), over repeated
+    calls (the arrival counters reset themselves), and match the oracle."""
+    ctxs = []
+    for fused in ("1", "0"):
+        monkeypatch.setenv("KORE_CUDA_FUSED_MERGE", fused)
+        ctxs.append(make_ctx(H, G, d, pos + 2, n_layer=1))
+    o = O.OracleLayer(H, G, d, pos + 2)
+    k, v = normal(60 + pos, (pos, G * d), (pos, G * d))
+    for g in ctxs:
+        for p0 in range(0, pos, 4096):
+            g.append(0, 0, p0, k[p0:p0 + 4096], v[p0:p0 + 4096])
+    o.fill(0, k, v)
+    q, kn, vn = normal(61 + pos, (H * d,), (G * d,), (G * d,))
+    outs = [[g.decode(0, 0, pos, q, kn, vn) for _ in range(3)] for g in ctxs]
+    for a in outs[0] + outs[1]:
+        np.testing.assert_array_equal(a, outs[1][0])
+    assert_attn_close(outs[0][0], o.decode(pos, q, kn, vn), f"fused merge pos {pos}")
+
+
 def test_decode_dev_matches_host_path():
     import torch
     H, G, d = 28, 4, 128
