@@ -28,7 +28,19 @@ struct PagedKv {
     int shard_rank, shard_count;
 };
 
+// An encoded TMA tensor map (the driver's 128-byte CUtensorMap), opaque here.
+struct alignas(64) TmaDesc {
+    unsigned long long w[16];
+};
+
 struct DecodeParams {
+    // Tensor-core decode (attn_decode_tc_kernel, D = 128, one query): the
+    // pools' K and V rows of 128 floats as 2-D TMA tensor maps (boxes of 32
+    // floats x 16 rows, 128-byte swizzle); row of (page, g, t) in this
+    // layer = k_row0 (v_row0) + (page*G + g)*P + t.
+    TmaDesc tm_k, tm_v;
+    long long k_row0, v_row0;
+    int tc;                    // 1: launch the tensor-core kernel
     PagedKv kv;
     const float *q;            // [n_q][H*D] pre-RoPE
     const float *k_new;        // [n_q][G*D] pre-RoPE (append_new only)
@@ -137,6 +149,7 @@ struct ExchangeParams {
 cudaError_t launch_attn_decode(const DecodeParams &p, int n_rep, int grid_x, cudaStream_t s, bool merge = true);
 int decode_ctas_per_sm(int head_dim, int n_rep);
 int decode_tile_tokens();
+int decode_tc_tile_tokens();   // tokens per tile of the tensor-core decode (split lengths are multiples)
 int decode_split_pages_max();
 size_t decode_smem_bytes(int head_dim);
 cudaError_t launch_kv_append(const AppendParams &p, cudaStream_t s);
@@ -150,6 +163,7 @@ uintptr_t current_cuda_context();
 // Sets a kernel's dynamic shared memory limit once per CUDA context (the
 // attribute belongs to the kernel as loaded in one context). Thread-safe.
 cudaError_t ensure_smem_limit(const void *kernel, int bytes);
+bool encode_kv_map(const float *base, size_t rows, TmaDesc *out);   // rows of 128 floats as a TMA tensor map
 size_t prefill_tile_bytes(int head_dim);
 // bytes of one split slot of PrefillParams::part
 size_t prefill_slot_bytes(int head_dim);

@@ -319,6 +319,51 @@ __device__ __forceinline__ void fused_exchange_cta(const DecodeParams &p, int h)
     KTRACE(4);
 }
 
+// The CTA merge of its NW warps' states, left in shared memory as cm [NW][8]
+// reference maxima, cl [NW][8] sums and co [NW][R][D] unnormalised outputs:
+// the query's normalised output (one split; plus its log2-domain LSE when
+// asked) or the split's partial (max, sum, o) in the split scratch; in a
+// fused launch the split's arrival is then counted for the heads' merge CTAs.
+template <int D, int R, int NW>
+__device__ __forceinline__ void cta_merge_write(const DecodeParams &p, const float *cm, int qi, int g, int split,
+                                                int n_splits) {
+    constexpr int NT = NW * 32;
+    const int tid = threadIdx.x;
+    const float *cl = cm + NW * 8;
+    const float *co = cl + NW * 8;
+    const size_t qh0 = (size_t)qi * p.H + (size_t)g * R;     // first query head of the group
+    const size_t part_base = ((size_t)qi * p.kv.G + g) * p.max_splits;
+    for (int idx = tid; idx < R * D; idx += NT) {
+        const int h = idx / D;
+        float M = -INFINITY;
+#pragma unroll
+        for (int w = 0; w < NW; ++w) M = fmaxf(M, cm[w * 8 + h]);
+        float L = 0.f, O = 0.f;
+        if (M != -INFINITY) {
+#pragma unroll
+            for (int w = 0; w < NW; ++w) {
+                const float e = fast_exp2(cm[w * 8 + h] - M);
+                L = fmaf(cl[w * 8 + h], e, L);
+                O = fmaf(co[(w * R + h) * D + (idx - h * D)], e, O);
+            }
+        }
+        if (n_splits == 1) {
+            p.out[qh0 * D + idx] = L > 0.f ? O / L : 0.f;
+            if (p.lse && idx - h * D == 0) p.lse[qh0 + h] = L > 0.f ? M + __log2f(L) : -INFINITY;
+        } else {
+            p.part_o[(part_base + split) * R * D + idx] = O;
+            if (idx - h * D == 0) p.part_ml[(part_base + split) * R + h] = make_float2(M, L);
+        }
+    }
+    if (p.fused_exchange) {
+        // this split's partial is written: release it to the heads' merge CTAs
+        __threadfence();
+        __syncthreads();
+        if (tid == 0)
+            for (int h = 0; h < R; ++h) atomicAdd(p.x_arrivals + g * R + h, 1);
+    }
+}
+
 template <int D, int R, int NW, int TT, int SPW>
 __global__ void __launch_bounds__(NW * 32, 1) attn_decode_kernel(const __grid_constant__ DecodeParams p) {
     constexpr int VEC = D / 32;
@@ -549,39 +594,511 @@ __global__ void __launch_bounds__(NW * 32, 1) attn_decode_kernel(const __grid_co
     __syncthreads();
 
     // ---------------------------------------------------------------- CTA merge
-    const float *cm = stages;
-    const float *cl = cm + NW * 8;
-    const float *co = cl + NW * 8;
-    const size_t qh0 = (size_t)qi * p.H + (size_t)g * R;     // first query head of the group
-    const size_t part_base = ((size_t)qi * kv.G + g) * p.max_splits;
-    for (int idx = tid; idx < R * D; idx += NT) {
-        const int h = idx / D;
-        float M = -INFINITY;
+    cta_merge_write<D, R, NW>(p, stages, qi, g, split, n_splits);
+#ifdef KORE_TRACE
+    __syncthreads();
+    KTRACE(4);
+#endif
+}
+
+// ---------------------------------------------------------------- tensor-core decode
+//
+// attn_decode_tc_kernel: the same split-KV decode for one query at D = 128,
+// with the two contractions of a tile on the tensor cores (mma.sync
+// m16n8k16, bf16 operands, fp32 accumulation). The CUDA-core kernel above
+// spends most of its issue slots on the 7-head group's FMAs and the shuffle
+// reductions of the scores (measured: at the same KV bytes a layer takes
+// 28.2 us with 7 query heads per KV head and 23.8 us with 1); here a 16-token
+// tile costs 48 MMAs, the operand splits and the fragment loads.
+//  * Precision: every fp32 operand x is split into bf16 hi = rn(x) and
+//    lo = rn(x - hi) (x = hi + lo to 2^-16 relative) and each product is
+//    hi*hi + lo*hi + hi*lo, accumulated in fp32: the error of a product is
+//    ~2^-16 relative, far inside the 1e-3 bound (as in the prefill).
+//  * Layout: a warp's stage holds a 16-token tile of K and of V, each loaded
+//    by four 2-D TMA boxes of 32 floats x 16 rows with the 128-byte swizzle:
+//    [column group q][token r][32 floats], the 16-byte chunk j of row r
+//    stored at chunk j ^ (r % 8). Every fragment load below then touches 32
+//    distinct banks.
+//  * Scores: S^T (16 tokens x 8 heads) = K (16 x 128) . Q^T, tokens on M and
+//    the group's heads on N (R <= 8 of 8 columns used); k-step s = 2q + e
+//    gives thread (g, c) the 4 dims of chunk 8q + 2c + e of its rows g, g+8
+//    (the k index of the fragment permuted onto those dims, the same
+//    permutation for Q), so one 16-byte load feeds one A register pair.
+//  * Output: O^T (128 dims x 8 heads) += V^T (128 x 16 tokens) . P^T; the
+//    probabilities move from the score fragment (tokens on rows) to the B
+//    fragment (tokens on k) with eight shuffles.
+//  * Softmax as in the CUDA-core kernel: online, the reference maximum moved
+//    lazily (when a score exceeds it by 2^8); the new token at pos is taken
+//    in fp32 by warp 0 before the tiles.
+
+constexpr int kTcTT = 16;   // tokens per tile
+
+// 2-D TMA load of one box into this CTA's shared memory (no multicast).
+__device__ __forceinline__ void tma_load_2d(void *dst, const TmaDesc *map, int x, int y, uint64_t *bar,
+                                            uint64_t policy) {
+    asm volatile(
+        "cp.async.bulk.tensor.2d.shared::cluster.global.mbarrier::complete_tx::bytes.L2::cache_hint "
+        "[%0], [%1, {%2, %3}], [%4], %5;" ::"r"(smem_u32(dst)),
+        "l"(map), "r"(x), "r"(y), "r"(smem_u32(bar)), "l"(policy)
+        : "memory");
+}
+
+// x0, x1 -> bf16x2 hi = (rn(x0), rn(x1)) and lo = (rn(x0 - hi0), rn(x1 - hi1)),
+// element 0 in the low half (the lower k index of a fragment pair).
+__device__ __forceinline__ void split_bf16x2(float x0, float x1, uint32_t &hi, uint32_t &lo) {
+    asm("cvt.rn.bf16x2.f32 %0, %1, %2;" : "=r"(hi) : "f"(x1), "f"(x0));
+    const float h0 = __uint_as_float(hi << 16), h1 = __uint_as_float(hi & 0xffff0000u);
+    asm("cvt.rn.bf16x2.f32 %0, %1, %2;" : "=r"(lo) : "f"(__fsub_rn(x1, h1)), "f"(__fsub_rn(x0, h0)));
+}
+
+// d += a . b, m16n8k16, bf16 inputs, fp32 accumulators.
+__device__ __forceinline__ void mma_16816(float (&d)[4], uint32_t a0, uint32_t a1, uint32_t a2, uint32_t a3,
+                                          uint32_t b0, uint32_t b1) {
+    asm volatile(
+        "mma.sync.aligned.m16n8k16.row.col.f32.bf16.bf16.f32 {%0, %1, %2, %3}, {%4, %5, %6, %7}, {%8, %9}, "
+        "{%0, %1, %2, %3};"
+        : "+f"(d[0]), "+f"(d[1]), "+f"(d[2]), "+f"(d[3])
+        : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1));
+}
+
+template <int R, int NW, int SPW>
+struct TcSmem {
+    static constexpr int D = 128;
+    static constexpr size_t tile_bytes = (size_t)kTcTT * D * 4;   // 8 KB: K or V of a tile
+    static constexpr size_t stage_bytes = 2 * tile_bytes;
+    static constexpr size_t stages_bytes = (size_t)NW * SPW * stage_bytes;
+    static constexpr size_t qsm_off = stages_bytes;               // q [R*D], RoPE row [D], k_new, v_new, k rotated
+    static constexpr size_t bar_off = qsm_off + (size_t)12 * D * 4;
+    static constexpr size_t pages_off = bar_off + (size_t)NW * SPW * 8;
+    static constexpr size_t bytes = pages_off + (size_t)kSplitPagesMax * 4 + 1024;   // + alignment of the stages
+    static_assert(stages_bytes >= (size_t)NW * 8 * 32 * 16 + (size_t)NW * 16 * 4, "CTA merge scratch");
+};
+
+template <int R, int NW, int SPW>
+__global__ void __launch_bounds__(NW * 32, 1) attn_decode_tc_kernel(const __grid_constant__ DecodeParams p) {
+    constexpr int D = 128, HALF = 64, TT = kTcTT, NT = NW * 32;
+    using SM = TcSmem<R, NW, SPW>;
+    extern __shared__ __align__(128) unsigned char tc_smem[];
+    // the stages start on a 1024-byte boundary: the 128-byte swizzle pattern
+    // repeats every 1024 bytes of shared memory address
+    unsigned char *base = tc_smem + ((1024u - (smem_u32(tc_smem) & 1023u)) & 1023u);
+    float *qsm = reinterpret_cast<float *>(base + SM::qsm_off);   // q [R*D], RoPE row [D], k_new [D], v_new [D]
+    uint64_t *full = reinterpret_cast<uint64_t *>(base + SM::bar_off);
+    int *pages = reinterpret_cast<int *>(base + SM::pages_off);
+
+    int split = blockIdx.x, g = blockIdx.y;
+    if (p.fused_exchange) {   // CTAs [0, max_splits * G) decode, the last H merge (and exchange)
+        const int nd = p.max_splits * p.kv.G;
+        if ((int)blockIdx.x >= nd) {
+            fused_exchange_cta<D, R>(p, (int)blockIdx.x - nd);
+            return;
+        }
+        split = (int)blockIdx.x % p.max_splits;
+        g = (int)blockIdx.x / p.max_splits;
+    }
+    KTRACE_OPEN(0);
+    const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+    const int gq = lane >> 2, cq = lane & 3;   // fragment row group, thread in group
+    const int seq = p.seq0, pos = p.pos0;
+    const PagedKv &kv = p.kv;
+    const int P = kv.P, NS = kv.shard_count, rank = kv.shard_rank;
+
+    const int limit = p.append_new ? pos : pos + 1;
+    const int count = shard_count_below(limit, P, NS, rank);
+    const bool own_new = p.append_new && ((pos / P) % NS == rank);
+    const int ST = p.split_tokens;
+    int n_splits = (count + ST - 1) / ST;
+    if (n_splits == 0) n_splits = 1;
+    if (split >= n_splits) return;
+    const int u_begin = split * ST;
+    const int u_end = min(count, u_begin + ST);
+    const int n_tiles = u_end > u_begin ? (u_end - u_begin + TT - 1) / TT : 0;
+    const bool do_new = own_new && split == n_splits - 1;
+    const int lp_first = u_begin / P;
+    const int n_pages_split = n_tiles > 0 ? (u_end - 1) / P - lp_first + 1 : 0;
+    const int *pt = kv.page_table + (size_t)seq * kv.pt_stride;
+
+    if (!p.prefetch_ok) grid_dep_wait();
+    for (int j = tid; j < n_pages_split && j < kSplitPagesMax; j += NT) {
+        int ph = pt[lp_first + j];
+        if (ph < 0 || ph >= kv.n_pages) {
+            raise_error(p.err, DEV_BAD_PAGE);
+            ph = 0;
+        }
+        pages[j] = ph;
+    }
+    if (lane == 0)
+        for (int s = 0; s < SPW; ++s) mbar_init(&full[warp * SPW + s], 1);
+    if (tid == 0) mbar_fence_init();
+    __syncthreads();
+
+    // this warp's tiles: i = warp, warp + NW, ...; its j-th tile uses stage j % SPW
+    const int my_tiles = n_tiles > warp ? (n_tiles - warp + NW - 1) / NW : 0;
+    unsigned char *my_stages = base + (size_t)warp * SPW * SM::stage_bytes;
+    uint64_t *my_full = full + warp * SPW;
+    const uint64_t pol = l2_evict_first_policy();
+    auto issue = [&](int j) {   // lane 0 only: K and V of tile j, four boxes each
+        const int i = warp + j * NW;
+        const int u0 = u_begin + i * TT;
+        const int lp = u0 / P;
+        const int off = u0 - lp * P;
+        const int pj = min(lp - lp_first, kSplitPagesMax - 1);
+        const long long row = ((long long)pages[pj] * kv.G + g) * P + off;
+        unsigned char *dst = my_stages + (size_t)(j % SPW) * SM::stage_bytes;
+        uint64_t *bar = my_full + (j % SPW);
+        fence_proxy_async_smem();
+        mbar_arrive_expect_tx(bar, (uint32_t)SM::stage_bytes);
 #pragma unroll
-        for (int w = 0; w < NW; ++w) M = fmaxf(M, cm[w * 8 + h]);
-        float L = 0.f, O = 0.f;
-        if (M != -INFINITY) {
-#pragma unroll
-            for (int w = 0; w < NW; ++w) {
-                const float e = fast_exp2(cm[w * 8 + h] - M);
-                L = fmaf(cl[w * 8 + h], e, L);
-                O = fmaf(co[(w * R + h) * D + (idx - h * D)], e, O);
+        for (int q = 0; q < 4; ++q) {
+            tma_load_2d(dst + q * 2048, &p.tm_k, 32 * q, (int)(p.k_row0 + row), bar, pol);
+            tma_load_2d(dst + SM::tile_bytes + q * 2048, &p.tm_v, 32 * q, (int)(p.v_row0 + row), bar, pol);
+        }
+    };
+    const int pre = p.prefetch_ok ? min(SPW, p.prefetch_stages) : 0;
+    if (lane == 0)
+        for (int j = 0; j < pre && j < my_tiles; ++j) issue(j);
+    if (p.prefetch_ok) grid_dep_wait();
+    KTRACE(1);
+    grid_dep_launch();
+    if (lane == 0)
+        for (int j = pre; j < SPW && j < my_tiles; ++j) issue(j);
+
+    // q of the group, the RoPE row and the new token's k/v, once per CTA
+    {
+        const float4 *q4 = reinterpret_cast<const float4 *>(p.q + (size_t)g * R * D);
+        float4 *d4 = reinterpret_cast<float4 *>(qsm);
+        for (int i = tid; i < R * D / 4; i += NT) d4[i] = __ldg(q4 + i);
+        const float4 *c4 = reinterpret_cast<const float4 *>(p.rope + (size_t)pos * HALF);
+        for (int i = tid; i < D / 4; i += NT) d4[R * D / 4 + i] = __ldg(c4 + i);
+        if (do_new) {
+            const float4 *k4 = reinterpret_cast<const float4 *>(p.k_new + (size_t)g * D);
+            const float4 *v4 = reinterpret_cast<const float4 *>(p.v_new + (size_t)g * D);
+            for (int i = tid; i < D / 4; i += NT) {
+                d4[(R + 1) * D / 4 + i] = __ldg(k4 + i);
+                d4[(R + 2) * D / 4 + i] = __ldg(v4 + i);
             }
         }
+    }
+    __syncthreads();
+    KTRACE(2);
+    const float2 *cs = reinterpret_cast<const float2 *>(qsm + R * D);
+    auto qrot = [&](int h, int d) -> float {   // q of head h, dim d: rotated at pos, scaled to log2 units
+        const float x = qsm[h * D + d], y = qsm[h * D + (d ^ HALF)];
+        const float2 a = cs[d & (HALF - 1)];
+        const float r = d < HALF ? rope_lo(x, y, a.x, a.y) : rope_hi(y, x, a.x, a.y);
+        return r * p.scale_log2;
+    };
+
+    // B fragments of Q^T for the 8 k-steps (k-step s = 2q + e: this thread's
+    // dims 32q + 8c + 4e .. +3, in the order of its K loads); heads >= R zero
+    uint32_t qb_hi[8][2], qb_lo[8][2];
+#pragma unroll
+    for (int s = 0; s < 8; ++s) {
+        const int d0 = 32 * (s >> 1) + 8 * cq + 4 * (s & 1);
+        float x[4];
+#pragma unroll
+        for (int i = 0; i < 4; ++i) x[i] = gq < R ? qrot(gq, d0 + i) : 0.f;
+        split_bf16x2(x[0], x[1], qb_hi[s][0], qb_lo[s][0]);
+        split_bf16x2(x[2], x[3], qb_hi[s][1], qb_lo[s][1]);
+    }
+
+    // O^T fragments: m-tile mt holds dims 16mt + gq (+8) of heads 2cq, 2cq+1:
+    // o[mt][0] (dim 16mt+gq, head 2cq), [1] (.., 2cq+1), [2] (dim +8, 2cq), [3] (dim +8, 2cq+1)
+    float o[8][4];
+#pragma unroll
+    for (int mt = 0; mt < 8; ++mt)
+#pragma unroll
+        for (int i = 0; i < 4; ++i) o[mt][i] = 0.f;
+    const bool hv0 = 2 * cq < R, hv1 = 2 * cq + 1 < R;   // this thread's two head columns exist
+    // reference maxima (a column without a head: +inf, so its p is 0 and it never rescales)
+    float mr0 = hv0 ? -INFINITY : INFINITY, mr1 = hv1 ? -INFINITY : INFINITY;
+    float l0 = 0.f, l1 = 0.f;   // thread-partial sums of heads 2cq, 2cq+1
+
+    if (do_new && warp == 0) {
+        // the token at pos in fp32: rotate k, append k/v to the cache, fold it in
+        const float *ks = qsm + (R + 1) * D;
+        const float *vs = qsm + (R + 2) * D;
+        const int lp = (pos / P) / NS, off = pos % P;
+        const int ph = pt[lp];
+        const bool ok = ph >= 0 && ph < kv.n_pages;
+        if (!ok && lane == 0) raise_error(p.err, DEV_BAD_PAGE);
+        float *kd = kv.k + (((size_t)(ok ? ph : 0) * kv.G + g) * P + off) * D;
+        float part[R];
+#pragma unroll
+        for (int h = 0; h < R; ++h) part[h] = 0.f;
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {
+            const int i = lane * 4 + j;
+            const float x = ks[i], y = ks[i ^ HALF];
+            const float2 a = cs[i & (HALF - 1)];
+            const float kr = i < HALF ? rope_lo(x, y, a.x, a.y) : rope_hi(y, x, a.x, a.y);
+            if (ok) {
+                kd[i] = kr;
+                kd[i + kv.v_off] = vs[i];
+            }
+#pragma unroll
+            for (int h = 0; h < R; ++h) part[h] = fmaf(qrot(h, i), kr, part[h]);
+        }
+#pragma unroll
+        for (int h = 0; h < R; ++h)
+#pragma unroll
+            for (int m = 16; m > 0; m >>= 1) part[h] += __shfl_xor_sync(FULL, part[h], m);
+        float sn0 = 0.f, sn1 = 0.f;
+#pragma unroll
+        for (int h = 0; h < R; ++h) {
+            if (h == 2 * cq) sn0 = part[h];
+            if (h == 2 * cq + 1) sn1 = part[h];
+        }
+        if (hv0) {
+            mr0 = sn0;   // the first score of this warp: exact reference
+            if (gq == 0) l0 = 1.f;
+#pragma unroll
+            for (int mt = 0; mt < 8; ++mt) {
+                o[mt][0] = vs[16 * mt + gq];
+                o[mt][2] = vs[16 * mt + gq + 8];
+            }
+        }
+        if (hv1) {
+            mr1 = sn1;
+            if (gq == 0) l1 = 1.f;
+#pragma unroll
+            for (int mt = 0; mt < 8; ++mt) {
+                o[mt][1] = vs[16 * mt + gq];
+                o[mt][3] = vs[16 * mt + gq + 8];
+            }
+        }
+    }
+
+    // per-thread byte offsets of the fragment loads within a tile (see the layout above)
+    //  K, k-step (q, e): row gq at q*2048 + gq*128 + (((2c ^ gq) ^ e) << 4); row gq+8 at +1024
+    const uint32_t kofs0 = gq * 128 + ((((2 * cq) ^ gq)) << 4);
+    const uint32_t kofs1 = kofs0 ^ 16u;
+    //  V, element (token t = 2c + i (+8), dim 16mt + gq (+8)): (mt >> 1)*2048 + t*128 +
+    //  ((chunk(dim) ^ (t & 7)) << 4) + (gq & 3)*4, chunk(dim) = 4(mt & 1) | 2(+8) | (gq >> 2)
+    uint32_t vofs[2];
+#pragma unroll
+    for (int i = 0; i < 2; ++i)
+        vofs[i] = (uint32_t)((2 * cq + i) * 128 + ((((gq >> 2) ^ (2 * cq + i)) & 7) << 4) + (gq & 3) * 4);
+
+    for (int j = 0; j < my_tiles; ++j) {
+        const int s = j % SPW;
+        if (!__all_sync(FULL, mbar_wait(my_full + s, (j / SPW) & 1, p.err, DEV_WAIT_FULL_TIMEOUT, p.wait_ns))) {
+            // gave up (the error word says so): let the copies in flight land first
+            for (int t = j; t < my_tiles && t < j + SPW; ++t) mbar_drain(my_full + t % SPW, (t / SPW) & 1);
+            break;
+        }
+        const int nv = min(TT, u_end - (u_begin + (warp + j * NW) * TT));
+        const unsigned char *Kt = my_stages + (size_t)s * SM::stage_bytes;
+        const unsigned char *Vt = Kt + SM::tile_bytes;
+
+        // S^T (16 tokens x 8 heads) = K . Q^T; the hi.hi and the two cross
+        // products in separate accumulators (independent MMA chains)
+        float sa[4] = {0.f, 0.f, 0.f, 0.f}, sb[4] = {0.f, 0.f, 0.f, 0.f}, sc[4] = {0.f, 0.f, 0.f, 0.f};
+#pragma unroll
+        for (int st = 0; st < 8; ++st) {
+            const uint32_t ko = ((st & 1) ? kofs1 : kofs0) + (uint32_t)(st >> 1) * 2048u;
+            const float4 r0 = *reinterpret_cast<const float4 *>(Kt + ko);          // token gq
+            const float4 r1 = *reinterpret_cast<const float4 *>(Kt + ko + 1024);   // token gq + 8
+            uint32_t ah[4], al[4];
+            split_bf16x2(r0.x, r0.y, ah[0], al[0]);
+            split_bf16x2(r1.x, r1.y, ah[1], al[1]);
+            split_bf16x2(r0.z, r0.w, ah[2], al[2]);
+            split_bf16x2(r1.z, r1.w, ah[3], al[3]);
+            mma_16816(sa, ah[0], ah[1], ah[2], ah[3], qb_hi[st][0], qb_hi[st][1]);
+            mma_16816(sb, al[0], al[1], al[2], al[3], qb_hi[st][0], qb_hi[st][1]);
+            mma_16816(sc, ah[0], ah[1], ah[2], ah[3], qb_lo[st][0], qb_lo[st][1]);
+        }
+        // sv: (token gq, head 2c), (gq, 2c+1), (gq+8, 2c), (gq+8, 2c+1)
+        float sv[4];
+#pragma unroll
+        for (int i = 0; i < 4; ++i) sv[i] = sa[i] + (sb[i] + sc[i]);
+        if (nv < TT) {
+            if (gq >= nv) sv[0] = sv[1] = -INFINITY;
+            if (gq + 8 >= nv) sv[2] = sv[3] = -INFINITY;
+        }
+
+        // lazy rescale: only when a score exceeds its head's reference by 2^8
+        const bool need = sv[0] > mr0 + kRescaleLog2 || sv[2] > mr0 + kRescaleLog2 || sv[1] > mr1 + kRescaleLog2 ||
+                          sv[3] > mr1 + kRescaleLog2;
+        if (__any_sync(FULL, need)) {
+            float t0 = fmaxf(sv[0], sv[2]), t1 = fmaxf(sv[1], sv[3]);
+#pragma unroll
+            for (int m = 4; m < 32; m <<= 1) {
+                t0 = fmaxf(t0, __shfl_xor_sync(FULL, t0, m));
+                t1 = fmaxf(t1, __shfl_xor_sync(FULL, t1, m));
+            }
+            if (hv0) {
+                const float mn = fmaxf(mr0, t0);
+                const float al = fast_exp2(mr0 - mn);
+                l0 *= al;
+#pragma unroll
+                for (int mt = 0; mt < 8; ++mt) {
+                    o[mt][0] *= al;
+                    o[mt][2] *= al;
+                }
+                mr0 = mn;
+            }
+            if (hv1) {
+                const float mn = fmaxf(mr1, t1);
+                const float al = fast_exp2(mr1 - mn);
+                l1 *= al;
+#pragma unroll
+                for (int mt = 0; mt < 8; ++mt) {
+                    o[mt][1] *= al;
+                    o[mt][3] *= al;
+                }
+                mr1 = mn;
+            }
+        }
+        float pv[4];
+        pv[0] = fast_exp2(sv[0] - mr0);
+        pv[1] = fast_exp2(sv[1] - mr1);
+        pv[2] = fast_exp2(sv[2] - mr0);
+        pv[3] = fast_exp2(sv[3] - mr1);
+        l0 += pv[0] + pv[2];
+        l1 += pv[1] + pv[3];
+
+        // P^T as a B fragment: this thread needs P[head gq][tokens 2c, 2c+1,
+        // 2c+8, 2c+9]; P[h][t] sits in lane (t & 7)*4 + (h >> 1), value
+        // (t >> 3)*2 + (h & 1) of the score fragment
+        const int srcA = 8 * cq + (gq >> 1), srcB = srcA + 4;
+        const bool odd = gq & 1;
+        const float xa0 = __shfl_sync(FULL, pv[0], srcA), xa1 = __shfl_sync(FULL, pv[1], srcA);
+        const float xb0 = __shfl_sync(FULL, pv[0], srcB), xb1 = __shfl_sync(FULL, pv[1], srcB);
+        const float xa2 = __shfl_sync(FULL, pv[2], srcA), xa3 = __shfl_sync(FULL, pv[3], srcA);
+        const float xb2 = __shfl_sync(FULL, pv[2], srcB), xb3 = __shfl_sync(FULL, pv[3], srcB);
+        uint32_t pbh[2], pbl[2];
+        split_bf16x2(odd ? xa1 : xa0, odd ? xb1 : xb0, pbh[0], pbl[0]);
+        split_bf16x2(odd ? xa3 : xa2, odd ? xb3 : xb2, pbh[1], pbl[1]);
+
+        // O^T (128 dims x 8 heads) += V^T . P^T, one m-tile of 16 dims at a time
+        const bool t0ok = 2 * cq < nv, t1ok = 2 * cq + 1 < nv, t8ok = 2 * cq + 8 < nv, t9ok = 2 * cq + 9 < nv;
+#pragma unroll
+        for (int mt = 0; mt < 8; ++mt) {
+            const uint32_t mb = (uint32_t)(mt >> 1) * 2048u;
+            const uint32_t x0 = (uint32_t)(4 * (mt & 1)) << 4, x8 = (uint32_t)(4 * (mt & 1) + 2) << 4;
+            // (token, dim): a0 (2c, d) (2c+1, d), a1 (2c, d+8) (2c+1, d+8), a2 (2c+8, d) (2c+9, d), a3 (2c+8, d+8) (2c+9, d+8)
+            float v00 = *reinterpret_cast<const float *>(Vt + mb + (vofs[0] ^ x0));
+            float v01 = *reinterpret_cast<const float *>(Vt + mb + (vofs[1] ^ x0));
+            float v10 = *reinterpret_cast<const float *>(Vt + mb + (vofs[0] ^ x8));
+            float v11 = *reinterpret_cast<const float *>(Vt + mb + (vofs[1] ^ x8));
+            float v20 = *reinterpret_cast<const float *>(Vt + mb + 1024 + (vofs[0] ^ x0));
+            float v21 = *reinterpret_cast<const float *>(Vt + mb + 1024 + (vofs[1] ^ x0));
+            float v30 = *reinterpret_cast<const float *>(Vt + mb + 1024 + (vofs[0] ^ x8));
+            float v31 = *reinterpret_cast<const float *>(Vt + mb + 1024 + (vofs[1] ^ x8));
+            if (nv < TT) {   // rows past the split's end hold other positions: never multiplied in
+                v00 = t0ok ? v00 : 0.f;
+                v10 = t0ok ? v10 : 0.f;
+                v01 = t1ok ? v01 : 0.f;
+                v11 = t1ok ? v11 : 0.f;
+                v20 = t8ok ? v20 : 0.f;
+                v30 = t8ok ? v30 : 0.f;
+                v21 = t9ok ? v21 : 0.f;
+                v31 = t9ok ? v31 : 0.f;
+            }
+            uint32_t vh[4], vl[4];
+            split_bf16x2(v00, v01, vh[0], vl[0]);
+            split_bf16x2(v10, v11, vh[1], vl[1]);
+            split_bf16x2(v20, v21, vh[2], vl[2]);
+            split_bf16x2(v30, v31, vh[3], vl[3]);
+            mma_16816(o[mt], vh[0], vh[1], vh[2], vh[3], pbh[0], pbh[1]);
+            mma_16816(o[mt], vl[0], vl[1], vl[2], vl[3], pbh[0], pbh[1]);
+            mma_16816(o[mt], vh[0], vh[1], vh[2], vh[3], pbl[0], pbl[1]);
+        }
+        __syncwarp();   // every lane is done with the stage
+        if (lane == 0 && j + SPW < my_tiles) issue(j + SPW);
+    }
+
+    // sums of heads 2c, 2c+1 over the warp's tokens (lanes of equal c)
+#pragma unroll
+    for (int m = 4; m < 32; m <<= 1) {
+        l0 += __shfl_xor_sync(FULL, l0, m);
+        l1 += __shfl_xor_sync(FULL, l1, m);
+    }
+    __syncthreads();   // every tile consumed: the stage memory is free
+    KTRACE(3);
+
+    // CTA merge, position-wise: thread (gq, c) of every warp holds the same
+    // (dim, head) positions, so warp w finalises m-tiles w, w + NW, ... from
+    // the NW warps' fragments, weighted by 2^(m_w - M) per head.
+    float4 *xo = reinterpret_cast<float4 *>(base);                    // [NW][8 m-tiles][32 lanes]
+    float *xm = reinterpret_cast<float *>(base + (size_t)NW * 8 * 32 * 16);   // [NW][8]
+    float *xl = xm + NW * 8;                                          // [NW][8]
+#pragma unroll
+    for (int mt = 0; mt < 8; ++mt) xo[(warp * 8 + mt) * 32 + lane] = make_float4(o[mt][0], o[mt][1], o[mt][2], o[mt][3]);
+    if (gq == 0) {
+        xm[warp * 8 + 2 * cq] = hv0 ? mr0 : -INFINITY;
+        xm[warp * 8 + 2 * cq + 1] = hv1 ? mr1 : -INFINITY;
+        xl[warp * 8 + 2 * cq] = l0;
+        xl[warp * 8 + 2 * cq + 1] = l1;
+    }
+    __syncthreads();
+    float M0 = -INFINITY, M1 = -INFINITY;
+#pragma unroll
+    for (int w = 0; w < NW; ++w) {
+        M0 = fmaxf(M0, xm[w * 8 + 2 * cq]);
+        M1 = fmaxf(M1, xm[w * 8 + 2 * cq + 1]);
+    }
+    float e0[NW], e1[NW], L0 = 0.f, L1 = 0.f;
+#pragma unroll
+    for (int w = 0; w < NW; ++w) {
+        e0[w] = M0 == -INFINITY ? 0.f : fast_exp2(xm[w * 8 + 2 * cq] - M0);
+        e1[w] = M1 == -INFINITY ? 0.f : fast_exp2(xm[w * 8 + 2 * cq + 1] - M1);
+        L0 = fmaf(xl[w * 8 + 2 * cq], e0[w], L0);
+        L1 = fmaf(xl[w * 8 + 2 * cq + 1], e1[w], L1);
+    }
+    const size_t qh0 = (size_t)g * R;   // first query head of the group
+    const size_t part_base = (size_t)g * p.max_splits;
+    for (int mt = warp; mt < 8; mt += NW) {
+        float a[4] = {0.f, 0.f, 0.f, 0.f};
+#pragma unroll
+        for (int w = 0; w < NW; ++w) {
+            const float4 x = xo[(w * 8 + mt) * 32 + lane];
+            a[0] = fmaf(x.x, e0[w], a[0]);
+            a[1] = fmaf(x.y, e1[w], a[1]);
+            a[2] = fmaf(x.z, e0[w], a[2]);
+            a[3] = fmaf(x.w, e1[w], a[3]);
+        }
+        const int d0 = 16 * mt + gq;
         if (n_splits == 1) {
-            p.out[qh0 * D + idx] = L > 0.f ? O / L : 0.f;
-            if (p.lse && idx - h * D == 0) p.lse[qh0 + h] = L > 0.f ? M + __log2f(L) : -INFINITY;
+            if (hv0) {
+                p.out[(qh0 + 2 * cq) * D + d0] = L0 > 0.f ? a[0] / L0 : 0.f;
+                p.out[(qh0 + 2 * cq) * D + d0 + 8] = L0 > 0.f ? a[2] / L0 : 0.f;
+            }
+            if (hv1) {
+                p.out[(qh0 + 2 * cq + 1) * D + d0] = L1 > 0.f ? a[1] / L1 : 0.f;
+                p.out[(qh0 + 2 * cq + 1) * D + d0 + 8] = L1 > 0.f ? a[3] / L1 : 0.f;
+            }
         } else {
-            p.part_o[(part_base + split) * R * D + idx] = O;
-            if (idx - h * D == 0) p.part_ml[(part_base + split) * R + h] = make_float2(M, L);
+            float *po = p.part_o + (part_base + split) * R * D;
+            if (hv0) {
+                po[(2 * cq) * D + d0] = a[0];
+                po[(2 * cq) * D + d0 + 8] = a[2];
+            }
+            if (hv1) {
+                po[(2 * cq + 1) * D + d0] = a[1];
+                po[(2 * cq + 1) * D + d0 + 8] = a[3];
+            }
+        }
+    }
+    if (warp == 0 && gq == 0) {
+        if (n_splits == 1) {
+            if (p.lse && hv0) p.lse[qh0 + 2 * cq] = L0 > 0.f ? M0 + __log2f(L0) : -INFINITY;
+            if (p.lse && hv1) p.lse[qh0 + 2 * cq + 1] = L1 > 0.f ? M1 + __log2f(L1) : -INFINITY;
+        } else {
+            if (hv0) p.part_ml[(part_base + split) * R + 2 * cq] = make_float2(M0, L0);
+            if (hv1) p.part_ml[(part_base + split) * R + 2 * cq + 1] = make_float2(M1, L1);
         }
     }
     if (p.fused_exchange) {
-        // this split's partial is written: release it to the heads' merge CTAs
-        __threadfence();
+        // this split's partial is written (the barrier orders the CTA's stores
+        // before thread 0's release fence): count its arrival per query head
         __syncthreads();
-        if (tid == 0)
+        if (tid == 0) {
+            __threadfence();
+#pragma unroll
             for (int h = 0; h < R; ++h) atomicAdd(p.x_arrivals + g * R + h, 1);
+        }
     }
 #ifdef KORE_TRACE
     __syncthreads();
@@ -674,8 +1191,46 @@ cudaError_t launch_shape(const DecodeParams &p, int grid_x, cudaStream_t s, bool
     return cudaLaunchKernelEx(&mcfg, split_merge_kernel<D, R>, p);
 }
 
+// Tensor-core decode shape: NW warps of 16-token tiles, SPW stages each
+// (192 KB of K/V in flight per SM at 4 x 3, as the CUDA-core kernel's 8 x 8-token x 3).
+#ifndef KORE_DECODE_TC_NW
+#define KORE_DECODE_TC_NW 4
+#endif
+#ifndef KORE_DECODE_TC_SPW
+#define KORE_DECODE_TC_SPW 3
+#endif
+constexpr int kNWt = KORE_DECODE_TC_NW, kSPWt = KORE_DECODE_TC_SPW;
+static_assert(TcSmem<8, kNWt, kSPWt>::bytes <= 227 * 1024, "tensor-core decode stages exceed shared memory");
+static_assert(kNWt * 32 >= 128, "a merge CTA of a fused launch needs one thread per dim");
+
+template <int R>
+cudaError_t launch_tc(const DecodeParams &p, int grid_x, cudaStream_t s, bool merge) {
+    using SM = TcSmem<R, kNWt, kSPWt>;
+    auto kern = attn_decode_tc_kernel<R, kNWt, kSPWt>;
+    if (cudaError_t e = ensure_smem_limit(reinterpret_cast<const void *>(kern), (int)SM::bytes)) return e;
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = p.fused_exchange ? dim3(grid_x * p.kv.G + p.H) : dim3(grid_x, p.kv.G, 1);
+    cfg.blockDim = dim3(kNWt * 32);
+    cfg.dynamicSmemBytes = SM::bytes;
+    cfg.stream = s;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    cudaError_t e = cudaLaunchKernelEx(&cfg, kern, p);
+    if (e != cudaSuccess || grid_x == 1 || !merge || p.fused_exchange) return e;
+    cudaLaunchConfig_t mcfg = cfg;
+    mcfg.gridDim = dim3(p.kv.G * R, 1);
+    mcfg.blockDim = dim3(128);
+    mcfg.dynamicSmemBytes = 0;
+    return cudaLaunchKernelEx(&mcfg, split_merge_kernel<128, R>, p);
+}
+
 template <int D, int R>
 cudaError_t launch_dr(const DecodeParams &p, int grid_x, cudaStream_t s, bool merge) {
+    if constexpr (D == 128)
+        if (p.tc) return launch_tc<R>(p, grid_x, s, merge);
     if (p.n_q > 1 && !p.contiguous) return launch_shape<D, R, kNWb, kSPWb>(p, grid_x, s, merge);
     return launch_shape<D, R, kNW, kSPW>(p, grid_x, s, merge);
 }
@@ -709,6 +1264,8 @@ int decode_ctas_per_sm(int head_dim, int) {
 }
 
 int decode_tile_tokens() { return kTT; }
+
+int decode_tc_tile_tokens() { return kTcTT; }
 
 int decode_split_pages_max() { return kSplitPagesMax; }
 

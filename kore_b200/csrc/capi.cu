@@ -11,6 +11,8 @@
 #include "attn.cuh"
 #include "common.cuh"
 
+#include <cuda.h>   // CUtensorMap and its enums (the encoder is resolved at run time)
+
 #include <algorithm>
 #include <cmath>
 #include <cstdarg>
@@ -40,6 +42,15 @@ struct kore_cuda_ctx {
     float *kv = nullptr;        // [n_layer][2][n_pages][G][P][D]
     size_t layer_floats = 0;
     long long v_off = 0;
+    // the pool as rows of D = 128 floats for the tensor-core decode's TMA
+    // boxes (32 floats x 16 rows, 128-byte swizzle). KORE_CUDA_TC_DECODE=1
+    // runs single queries on the tensor-core kernel: measured no faster
+    // (both kernels stream at the HBM limit) and its split-bf16 products
+    // round more (~1e-6 relative), which flipped a near-tie greedy token of
+    // the 3B parity model, so the CUDA-core kernel is the default
+    kore::TmaDesc kv_map{};
+    bool kv_map_ok = false;
+    bool tc_decode = false;
     int *pt_d = nullptr;
     std::vector<int> pt_h;      // [max_seqs][pages_per_seq]
     std::vector<int> free_pages;
@@ -171,6 +182,39 @@ uintptr_t current_cuda_context() {
     void *c = nullptr;
     if (!fn || fn(&c) != 0) return 0;
     return reinterpret_cast<uintptr_t>(c);
+}
+
+// Encodes `rows` rows of 128 floats at `base` as a 2-D TMA tensor map with
+// boxes of 32 floats x 16 rows and the 128-byte swizzle (the tensor-core
+// decode's K/V tiles). The driver's encoder is resolved at run time; false
+// when it or the encoding is unavailable (the CUDA-core decode is used then).
+bool encode_kv_map(const float *base, size_t rows, TmaDesc *out) {
+    using encode_fn = CUresult (*)(CUtensorMap *, CUtensorMapDataType, cuuint32_t, void *, const cuuint64_t *,
+                                   const cuuint64_t *, const cuuint32_t *, const cuuint32_t *, CUtensorMapInterleave,
+                                   CUtensorMapSwizzle, CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
+    static encode_fn fn = []() -> encode_fn {
+        void *f = nullptr;
+        cudaDriverEntryPointQueryResult q;
+        if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &f, cudaEnableDefault, &q) != cudaSuccess ||
+            q != cudaDriverEntryPointSuccess) {
+            cudaGetLastError();
+            return nullptr;
+        }
+        return reinterpret_cast<encode_fn>(f);
+    }();
+    static_assert(sizeof(CUtensorMap) == sizeof(TmaDesc), "tensor map size");
+    if (!fn || !base || rows == 0 || rows >= (1ull << 31) || (reinterpret_cast<uintptr_t>(base) & 15)) return false;
+    const cuuint64_t dims[2] = {128, (cuuint64_t)rows};
+    const cuuint64_t strides[1] = {128 * sizeof(float)};
+    const cuuint32_t box[2] = {32, 16};
+    const cuuint32_t estr[2] = {1, 1};
+    CUtensorMap m;
+    if (fn(&m, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 2, const_cast<float *>(base), dims, strides, box, estr,
+           CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+           CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) != CUDA_SUCCESS)
+        return false;
+    memcpy(out, &m, sizeof m);
+    return true;
 }
 
 cudaError_t ensure_smem_limit(const void *kernel, int bytes) {
@@ -446,13 +490,15 @@ int run_decode(kore_cuda_ctx *c, int layer, int n_q, bool contiguous, int seq0, 
         total += cnt;
         max_count = std::max(max_count, cnt);
     }
-    const int TT = decode_tile_tokens();
+    // one query at D = 128 runs the tensor-core kernel (16-token tiles, one CTA per SM)
+    const bool use_tc = c->tc_decode && c->kv_map_ok && c->D == 128 && n_q == 1 && contiguous;
+    const int TT = use_tc ? decode_tc_tile_tokens() : decode_tile_tokens();
     // CTAs to aim for: two per SM, unless set otherwise (KORE_CUDA_DECODE_CTAS;
     // KORE_CUDA_SHARD_CTAS on a KV-split context), trading CTA count for
     // longer splits
     const long long target = c->NS > 1 && c->shard_ctas > 0 ? c->shard_ctas
                              : c->decode_ctas > 0           ? c->decode_ctas
-                                                            : (long long)c->num_sms * decode_ctas_per_sm(c->D, c->R);
+                                                            : (long long)c->num_sms * (use_tc ? 1 : decode_ctas_per_sm(c->D, c->R));
     long long st = (total * c->G + target - 1) / target;
     st = std::max<long long>(st, 4 * TT);
     st = std::max<long long>(st, (max_count + kMaxSplits - 1) / kMaxSplits);
@@ -531,6 +577,13 @@ int run_decode(kore_cuda_ctx *c, int layer, int n_q, bool contiguous, int seq0, 
     if (grid_x > kMaxSplits) return fail(c, KORE_CUDA_EINVAL, "too many splits for one decode launch");
     p.split_tokens = (int)st;
     p.max_splits = grid_x;
+    if (use_tc) {
+        p.tc = 1;
+        p.tm_k = c->kv_map;
+        p.tm_v = c->kv_map;
+        p.k_row0 = (long long)((size_t)layer * c->layer_floats / 128);
+        p.v_row0 = p.k_row0 + c->v_off / 128;
+    }
     if (fused_out) {   // the exchange CTAs join this launch (peer_exchange.cu's protocol)
         p.fused_exchange = 1;
         p.x_ranks = c->NS;
@@ -688,6 +741,7 @@ int kore_cuda_create(kore_cuda_ctx **out, const kore_cuda_cfg *cfg) {
     if (const char *dc = getenv("KORE_CUDA_DECODE_CTAS")) c->decode_ctas = std::max(0, atoi(dc));
     if (const char *fx = getenv("KORE_CUDA_FUSED_EXCHANGE")) c->fused_exchange = atoi(fx) != 0;
     if (const char *fm = getenv("KORE_CUDA_FUSED_MERGE")) c->fused_merge = atoi(fm) != 0;
+    if (const char *tc = getenv("KORE_CUDA_TC_DECODE")) c->tc_decode = atoi(tc) != 0;
     CKB(cudaStreamCreateWithFlags(&c->stream, cudaStreamNonBlocking));
     c->own_stream = true;
 
@@ -695,6 +749,7 @@ int kore_cuda_create(kore_cuda_ctx **out, const kore_cuda_cfg *cfg) {
     c->v_off = (long long)c->n_pages * c->G * P * c->D;
     CKB(cudaMalloc(&c->kv, c->layer_floats * f.n_layer * sizeof(float)));
     CKB(cudaMemsetAsync(c->kv, 0, c->layer_floats * f.n_layer * sizeof(float), c->stream));
+    if (c->D == 128) c->kv_map_ok = encode_kv_map(c->kv, c->layer_floats * f.n_layer / 128, &c->kv_map);
     CKB(cudaMalloc(&c->pt_d, c->pt_h.size() * sizeof(int)));
     CKB(cudaMemsetAsync(c->pt_d, 0xff, c->pt_h.size() * sizeof(int), c->stream));
 

@@ -103,6 +103,7 @@ def main() -> None:
     ap.add_argument("--steps", type=int, default=3)
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--per-launch", action="store_true", help="print every launch's row")
+    ap.add_argument("--dump", default="", help="also save the raw records (numpy .npy) to this path")
     args = ap.parse_args()
 
     import torch
@@ -157,6 +158,8 @@ def main() -> None:
             graph.replay()
     torch.cuda.synchronize()
     recs = read_trace(lib)
+    if args.dump:
+        np.save(args.dump, recs)
     del graph
     ctx.close()
     table = phase_table(launches(recs))

@@ -125,6 +125,34 @@ def test_fused_split_merge_equals_separate_merge_kernel(H, G, d, pos, monkeypatc
     assert_attn_close(outs[0][0], o.decode(pos, q, kn, vn), f"fused merge pos {pos}")
 
 
+@pytest.mark.parametrize("H,G,pos", [(28, 4, 0), (28, 4, 1), (28, 4, 15), (28, 4, 16), (28, 4, 17), (28, 4, 255),
+                                     (28, 4, 257), (28, 4, 1000), (28, 4, 9001), (16, 2, 777), (16, 4, 4099),
+                                     (4, 4, 3000), (8, 8, 65), (24, 4, 2048)])
+def test_tensor_core_decode_matches_oracle_and_cuda_core_path(H, G, pos, monkeypatch):
+    """Single-query decode at head_dim 128 runs the tensor-core kernel
+    (16-token tiles, split-bf16 products); KORE_CUDA_TC_DECODE=0 runs the
+    CUDA-core kernel. Both within tolerance of the oracle at tile and page
+    edges, for 1, 4, 6, 7 and 8 query heads per KV head; the cached rows are
+    kore's bit for bit on both."""
+    d = 128
+    o = O.OracleLayer(H, G, d, pos + 2)
+    k, v = normal(80 + pos, (pos, G * d), (pos, G * d))
+    if pos:
+        o.fill(0, k, v)
+    q, kn, vn = normal(81 + pos, (H * d,), (G * d,), (G * d,))
+    ref = o.decode(pos, q, kn, vn)
+    for tc in ("1", "0"):
+        monkeypatch.setenv("KORE_CUDA_TC_DECODE", tc)
+        g = make_ctx(H, G, d, pos + 2)
+        for p0 in range(0, pos, 4096):
+            g.append(0, 0, p0, k[p0:p0 + 4096], v[p0:p0 + 4096])
+        assert_attn_close(g.decode(0, 0, pos, q, kn, vn), ref, f"decode tc={tc} H={H} G={G} pos={pos}")
+        kr, vr = g.kv_read(0, 0, pos, 1)
+        np.testing.assert_array_equal(kr, o.kc[pos:pos + 1])
+        np.testing.assert_array_equal(vr, o.vc[pos:pos + 1])
+        g.close()
+
+
 def test_decode_dev_matches_host_path():
     import torch
     H, G, d = 28, 4, 128
