@@ -324,43 +324,76 @@ __device__ __forceinline__ void fused_exchange_cta(const DecodeParams &p, int h)
 // the query's normalised output (one split; plus its log2-domain LSE when
 // asked) or the split's partial (max, sum, o) in the split scratch; in a
 // fused launch the split's arrival is then counted for the heads' merge CTAs.
+// The weights 2^(m_w - M) and the sums are formed once per (warp, head) in
+// shared memory (wsm: [NW][8] weights, then [8] maxima and [8] sums), then
+// each thread combines float4 runs of dims, every product in warp order.
 template <int D, int R, int NW>
-__device__ __forceinline__ void cta_merge_write(const DecodeParams &p, const float *cm, int qi, int g, int split,
-                                                int n_splits) {
+__device__ __forceinline__ void cta_merge_write(const DecodeParams &p, const float *cm, float *wsm, int qi, int g,
+                                                int split, int n_splits) {
     constexpr int NT = NW * 32;
     const int tid = threadIdx.x;
     const float *cl = cm + NW * 8;
     const float *co = cl + NW * 8;
+    float *sM = wsm + NW * 8, *sL = sM + 8;
     const size_t qh0 = (size_t)qi * p.H + (size_t)g * R;     // first query head of the group
     const size_t part_base = ((size_t)qi * p.kv.G + g) * p.max_splits;
-    for (int idx = tid; idx < R * D; idx += NT) {
-        const int h = idx / D;
+    if (tid < R) {
+        const int h = tid;
         float M = -INFINITY;
 #pragma unroll
         for (int w = 0; w < NW; ++w) M = fmaxf(M, cm[w * 8 + h]);
-        float L = 0.f, O = 0.f;
-        if (M != -INFINITY) {
+        float L = 0.f;
 #pragma unroll
-            for (int w = 0; w < NW; ++w) {
-                const float e = fast_exp2(cm[w * 8 + h] - M);
-                L = fmaf(cl[w * 8 + h], e, L);
-                O = fmaf(co[(w * R + h) * D + (idx - h * D)], e, O);
-            }
+        for (int w = 0; w < NW; ++w) {
+            const float e = M == -INFINITY ? 0.f : fast_exp2(cm[w * 8 + h] - M);
+            wsm[w * 8 + h] = e;
+            L = fmaf(cl[w * 8 + h], e, L);
+        }
+        sM[h] = M;
+        sL[h] = L;
+        if (n_splits == 1) {
+            if (p.lse) p.lse[qh0 + h] = L > 0.f ? M + __log2f(L) : -INFINITY;
+        } else {
+            p.part_ml[(part_base + split) * R + h] = make_float2(M, L);
+        }
+    }
+    __syncthreads();
+    float *dst = n_splits == 1 ? p.out + qh0 * D : p.part_o + (part_base + split) * R * D;
+    const bool vec = (reinterpret_cast<uintptr_t>(dst) & 15) == 0;
+    for (int i4 = tid; i4 < R * D / 4; i4 += NT) {
+        const int h = i4 / (D / 4);
+        float4 a = make_float4(0.f, 0.f, 0.f, 0.f);
+#pragma unroll
+        for (int w = 0; w < NW; ++w) {
+            const float e = wsm[w * 8 + h];
+            const float4 x = reinterpret_cast<const float4 *>(co + (size_t)w * R * D)[i4];
+            a.x = fmaf(x.x, e, a.x);
+            a.y = fmaf(x.y, e, a.y);
+            a.z = fmaf(x.z, e, a.z);
+            a.w = fmaf(x.w, e, a.w);
         }
         if (n_splits == 1) {
-            p.out[qh0 * D + idx] = L > 0.f ? O / L : 0.f;
-            if (p.lse && idx - h * D == 0) p.lse[qh0 + h] = L > 0.f ? M + __log2f(L) : -INFINITY;
+            const float L = sL[h];
+            a = L > 0.f ? make_float4(a.x / L, a.y / L, a.z / L, a.w / L) : make_float4(0.f, 0.f, 0.f, 0.f);
+        }
+        if (vec) {
+            reinterpret_cast<float4 *>(dst)[i4] = a;
         } else {
-            p.part_o[(part_base + split) * R * D + idx] = O;
-            if (idx - h * D == 0) p.part_ml[(part_base + split) * R + h] = make_float2(M, L);
+            dst[4 * i4] = a.x;
+            dst[4 * i4 + 1] = a.y;
+            dst[4 * i4 + 2] = a.z;
+            dst[4 * i4 + 3] = a.w;
         }
     }
     if (p.fused_exchange) {
-        // this split's partial is written: release it to the heads' merge CTAs
-        __threadfence();
+        // this split's partial is written (the barrier orders the CTA's stores
+        // before thread 0's release fence): count its arrival per query head
         __syncthreads();
-        if (tid == 0)
+        if (tid == 0) {
+            __threadfence();
+#pragma unroll
             for (int h = 0; h < R; ++h) atomicAdd(p.x_arrivals + g * R + h, 1);
+        }
     }
 }
 
@@ -594,7 +627,7 @@ __global__ void __launch_bounds__(NW * 32, 1) attn_decode_kernel(const __grid_co
     __syncthreads();
 
     // ---------------------------------------------------------------- CTA merge
-    cta_merge_write<D, R, NW>(p, stages, qi, g, split, n_splits);
+    cta_merge_write<D, R, NW>(p, stages, pbuf_all, qi, g, split, n_splits);
 #ifdef KORE_TRACE
     __syncthreads();
     KTRACE(4);
