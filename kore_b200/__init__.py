@@ -115,10 +115,13 @@ def declared_symbols() -> list[str]:
     return sorted(set(names))
 
 
-def load_library(path: str = LIB):
+def load_library(path: str | None = None):
+    """Loads the C-ABI library once: `path`, else $KORE_CUDA_LIB (a build of
+    the same sources with other compile-time shapes), else the in-tree build."""
     global _lib
     if _lib is not None:
         return _lib
+    path = path or os.environ.get("KORE_CUDA_LIB") or LIB
     if not os.path.exists(path):
         raise ImportError(f"{path} is missing: build it with `python -m kore_b200.build`")
     L = ctypes.CDLL(path)

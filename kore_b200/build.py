@@ -45,17 +45,22 @@ def _stale(lib: str = LIB) -> bool:
     return any(os.path.getmtime(d) > t for d in deps)
 
 
-def build(force: bool = False, verbose: bool = False, trace: bool = False) -> str:
-    """Compiles every .cu under csrc/ into one shared library; returns its path."""
-    lib = TRACE_LIB if trace else LIB
-    if not force and not _stale(lib):
+def build(force: bool = False, verbose: bool = False, trace: bool = False, out: str | None = None,
+          defines: tuple[str, ...] = ()) -> str:
+    """Compiles every .cu under csrc/ into one shared library; returns its path.
+    `out` and `defines` (NAME=VALUE, e.g. KORE_ROWS_WARPS=12) build a variant
+    with other compile-time shapes elsewhere (loaded through $KORE_CUDA_LIB)."""
+    lib = out or (TRACE_LIB if trace else LIB)
+    if not force and not out and not _stale(lib):
         return lib
-    objdir = os.path.join(PKG, "_build_trace" if trace else "_build")
+    objdir = os.path.join(os.path.dirname(lib), "_build_" + os.path.basename(lib)) if out else \
+        os.path.join(PKG, "_build_trace" if trace else "_build")
     os.makedirs(objdir, exist_ok=True)
     objs = []
     for src in sources():
         obj = os.path.join(objdir, os.path.basename(src)[:-3] + ".o")
-        cmd = [nvcc(), *ARCH, *NVCC_FLAGS, *(["-DKORE_TRACE"] if trace else []), "-I", INCLUDE, "-c", src, "-o", obj]
+        cmd = [nvcc(), *ARCH, *NVCC_FLAGS, *(["-DKORE_TRACE"] if trace else []), *("-D" + d for d in defines),
+               "-I", INCLUDE, "-c", src, "-o", obj]
         if verbose:
             cmd += ["-Xptxas", "-v"]
             print(" ".join(cmd), flush=True)
@@ -69,4 +74,12 @@ def build(force: bool = False, verbose: bool = False, trace: bool = False) -> st
 
 
 if __name__ == "__main__":
-    print(build(force="--force" in sys.argv, verbose="--verbose" in sys.argv, trace="--trace" in sys.argv))
+    import argparse
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--force", action="store_true")
+    ap.add_argument("--verbose", action="store_true")
+    ap.add_argument("--trace", action="store_true")
+    ap.add_argument("--out", default=None, help="build a variant library at this path")
+    ap.add_argument("-D", dest="defines", action="append", default=[], help="NAME=VALUE for a variant build")
+    a = ap.parse_args()
+    print(build(force=a.force, verbose=a.verbose, trace=a.trace, out=a.out, defines=tuple(a.defines)))

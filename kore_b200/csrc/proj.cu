@@ -542,6 +542,450 @@ __global__ void __launch_bounds__(32 * kWarps, 1) qmatvec_kernel(const __grid_co
     }
 }
 
+// ---------------------------------------------------------------- row-task products
+//
+// qmatvec_rows_kernel: the same products with 16 rows per warp task, for
+// launches with many rows (the feed-forward gate/up pair and the output
+// matrix). Lane (slot, kh) = (lane & 15, lane >> 4) owns row slot `slot` of
+// the task and kore's AVX2 lanes k = 4 kh .. 4 kh + 3 of every block of that
+// row: it forms those lanes' exact integers for each block and advances their
+// fused multiply-add chains in block order itself, so no chain is handed
+// between lanes and the block header and scales are unpacked by 2 lanes of a
+// row instead of 16. The row's kore sums then take one shuffle (the other
+// half's lanes); the epilogue runs on all 16 row lanes at once. A warp's
+// items (task, chunk of kRCB blocks) stream through a private ring of
+// stages, 16 rows per stage, one bulk copy per row issued by that row's lane.
+// The Q8_K input is staged per CTA in natural order (word w = values 4w ..
+// 4w+3), which every lane reads as 16-byte runs.
+
+#ifndef KORE_ROWS_WARPS
+#define KORE_ROWS_WARPS 8
+#endif
+constexpr int kRW = KORE_ROWS_WARPS;   // warps per CTA
+constexpr int kRSlots = 16;     // row slots per task (pair mode: 8 gate rows, then the same 8 up rows)
+constexpr int kRCB = 2;         // blocks per row per ring stage
+constexpr int kQ8N = 320;       // staged Q8_K block: qs [256], bsums [16] int16, pairs [8] int16, d, pad
+
+// One warp quantises one 256-value block (lane l holds values 8l..8l+7) into
+// a natural-order staged Q8_K block (the same arithmetic as q8k_block).
+__device__ __forceinline__ void q8k_block_nat(const float (&v)[8], int lane, uint8_t *blk) {
+    float amax = 0.f, maxv = 0.f;
+    int idx = 1 << 30;
+#pragma unroll
+    for (int i = 0; i < 8; ++i) {
+        const float ax = fabsf(v[i]);
+        if (ax > amax) {
+            amax = ax;
+            maxv = v[i];
+            idx = 8 * lane + i;
+        }
+    }
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) {
+        const float am = __shfl_xor_sync(FULLW, amax, o);
+        const float mv = __shfl_xor_sync(FULLW, maxv, o);
+        const int ix = __shfl_xor_sync(FULLW, idx, o);
+        if (am > amax || (am == amax && ix < idx)) {
+            amax = am;
+            maxv = mv;
+            idx = ix;
+        }
+    }
+    int q[8];
+    float d = 0.f;
+    if (amax == 0.f) {
+#pragma unroll
+        for (int i = 0; i < 8; ++i) q[i] = 0;
+    } else {
+        const float iscale = __fdiv_rn(-127.0f, maxv);
+#pragma unroll
+        for (int i = 0; i < 8; ++i) {
+            const int t = __float2int_rn(__fmul_rn(iscale, v[i]));   // round half to even
+            q[i] = t > 127 ? 127 : t;
+        }
+        d = __fdiv_rn(1.0f, iscale);
+    }
+    int s = 0;
+#pragma unroll
+    for (int i = 0; i < 8; ++i) s += q[i];
+    s += __shfl_xor_sync(FULLW, s, 1);
+    uint2 w;
+    w.x = (uint32_t)(q[0] & 0xFF) | (uint32_t)(q[1] & 0xFF) << 8 | (uint32_t)(q[2] & 0xFF) << 16 |
+          (uint32_t)(q[3] & 0xFF) << 24;
+    w.y = (uint32_t)(q[4] & 0xFF) | (uint32_t)(q[5] & 0xFF) << 8 | (uint32_t)(q[6] & 0xFF) << 16 |
+          (uint32_t)(q[7] & 0xFF) << 24;
+    reinterpret_cast<uint2 *>(blk)[lane] = w;
+    int16_t *bsums = reinterpret_cast<int16_t *>(blk + 256);
+    int16_t *pairs = reinterpret_cast<int16_t *>(blk + 288);
+    if ((lane & 1) == 0) bsums[lane >> 1] = (int16_t)s;
+    const int s2 = (int)(int16_t)s + (int)(int16_t)__shfl_xor_sync(FULLW, s, 2);
+    if ((lane & 3) == 0) pairs[lane >> 2] = (int16_t)s2;
+    if (lane == 0) *reinterpret_cast<float *>(blk + 304) = d;
+}
+
+// Shared memory of a row-task launch: the Q8_K input, then per warp S stages
+// of kRSlots row slots; a slot's byte stride is 16 x an odd number, so that
+// the 16-byte loads of 8 consecutive row slots fall on distinct banks.
+__host__ __device__ constexpr int rows_slot_bytes(int type) {
+    return type == 12 ? (kRCB * kQ4Stride + 15) / 16 % 2 ? (kRCB * kQ4Stride + 15) / 16 * 16
+                                                          : ((kRCB * kQ4Stride + 15) / 16 + 1) * 16
+                      : ((kRCB * kQ6Stride + 15 + 15) / 16) % 2 ? ((kRCB * kQ6Stride + 15 + 15) / 16) * 16
+                                                                  : ((kRCB * kQ6Stride + 15 + 15) / 16 + 1) * 16;
+}
+static_assert(rows_slot_bytes(12) == 304 && rows_slot_bytes(14) == 464, "row slot strides");
+constexpr size_t rows_fixed_smem(int nb, int S) {
+    return (size_t)8 * kRW * S + 8 * kRW + 8 * kRW + 16 + (size_t)nb * kQ8N;
+}
+
+// One Q4_K block of a row for this lane's AVX2 lanes k = 4 kh + kl
+// (kore.cpp:553-586, as block_terms<12>): the exact integers of each lane,
+// then each lane's chains acc += d * s, accm += dm * e in block order.
+__device__ __forceinline__ void rows_block_q4(const uint8_t *blk, const uint8_t *q8, int kh, float (&acc)[4],
+                                              float (&accm)[4]) {
+    const uint4 h = *reinterpret_cast<const uint4 *>(blk);
+    const uint32_t u0 = h.y, u1 = h.z, u2 = h.w;
+    const uint32_t sc_lo = u0 & 0x3F3F3F3Fu, sc_hi = (u2 & 0x0F0F0F0Fu) | ((u0 >> 2) & 0x30303030u);
+    const uint32_t mn_lo = u1 & 0x3F3F3F3Fu, mn_hi = ((u2 >> 4) & 0x0F0F0F0Fu) | ((u1 >> 2) & 0x30303030u);
+    const float xd = *reinterpret_cast<const float *>(q8 + 304);
+    const float d = __fmul_rn(half_bits(h.x & 0xFFFFu), xd);
+    const float dm = -__fmul_rn(half_bits(h.x >> 16), xd);
+    const uint4 pr = *reinterpret_cast<const uint4 *>(q8 + 288);   // bsum pairs (2m, 2m+1) in word m
+    const uint32_t pm[4] = {pr.x, pr.y, pr.z, pr.w};
+    int s[4] = {0, 0, 0, 0};
+#pragma unroll
+    for (int c = 0; c < 4; ++c) {
+        const uint4 W = *reinterpret_cast<const uint4 *>(blk + 16 + 32 * c + 16 * kh);
+        const uint4 L = *reinterpret_cast<const uint4 *>(q8 + 4 * (16 * c + 4 * kh));
+        const uint4 H = *reinterpret_cast<const uint4 *>(q8 + 4 * (16 * c + 8 + 4 * kh));
+        const uint32_t w[4] = {W.x, W.y, W.z, W.w}, lo8[4] = {L.x, L.y, L.z, L.w}, hi8[4] = {H.x, H.y, H.z, H.w};
+        const uint32_t scw = c < 2 ? sc_lo : sc_hi;
+#pragma unroll
+        for (int kl = 0; kl < 4; ++kl) {
+            const int lo = __dp4a((int)(w[kl] & 0x0F0F0F0Fu), (int)lo8[kl], 0);
+            const int hi = __dp4a((int)((w[kl] >> 4) & 0x0F0F0F0Fu), (int)hi8[kl], 0);
+            const int pk = (int)__byte_perm((uint32_t)lo, (uint32_t)hi, 0x5410);
+            s[kl] = (c & 1) ? __dp2a_hi(pk, (int)scw, s[kl]) : __dp2a_lo(pk, (int)scw, s[kl]);
+        }
+    }
+#pragma unroll
+    for (int kl = 0; kl < 4; ++kl) {
+        // minimum lane m = k & 3 = kl: mn[2m] * pairs[2m] + mn[2m+1] * pairs[2m+1]
+        const uint32_t mnw = kl < 2 ? mn_lo : mn_hi;
+        const int e = __dp2a_lo((int)pm[kl], (int)(mnw >> (16 * (kl & 1))), 0);
+        acc[kl] = __fmaf_rn(d, __int2float_rn(s[kl]), acc[kl]);
+        accm[kl] = __fmaf_rn(dm, __int2float_rn(e), accm[kl]);
+    }
+}
+
+// Two consecutive Q4_K blocks of a row, their integer work interleaved (two
+// independent sets of lane sums), then the chains in block order: the same
+// values as rows_block_q4 twice.
+__device__ __forceinline__ void rows_block2_q4(const uint8_t *blk, const uint8_t *q8, int kh, float (&acc)[4],
+                                               float (&accm)[4]) {
+    uint32_t sc[2][2], mn[2][2];
+    float d[2], dm[2];
+    uint32_t pm[2][4];
+#pragma unroll
+    for (int b = 0; b < 2; ++b) {
+        const uint4 h = *reinterpret_cast<const uint4 *>(blk + b * kQ4Stride);
+        const uint32_t u0 = h.y, u1 = h.z, u2 = h.w;
+        sc[b][0] = u0 & 0x3F3F3F3Fu;
+        sc[b][1] = (u2 & 0x0F0F0F0Fu) | ((u0 >> 2) & 0x30303030u);
+        mn[b][0] = u1 & 0x3F3F3F3Fu;
+        mn[b][1] = ((u2 >> 4) & 0x0F0F0F0Fu) | ((u1 >> 2) & 0x30303030u);
+        const float xd = *reinterpret_cast<const float *>(q8 + b * kQ8N + 304);
+        d[b] = __fmul_rn(half_bits(h.x & 0xFFFFu), xd);
+        dm[b] = -__fmul_rn(half_bits(h.x >> 16), xd);
+        const uint4 pr = *reinterpret_cast<const uint4 *>(q8 + b * kQ8N + 288);
+        pm[b][0] = pr.x;
+        pm[b][1] = pr.y;
+        pm[b][2] = pr.z;
+        pm[b][3] = pr.w;
+    }
+    int s[2][4] = {{0, 0, 0, 0}, {0, 0, 0, 0}};
+#pragma unroll
+    for (int c = 0; c < 4; ++c) {
+#pragma unroll
+        for (int b = 0; b < 2; ++b) {
+            const uint4 W = *reinterpret_cast<const uint4 *>(blk + b * kQ4Stride + 16 + 32 * c + 16 * kh);
+            const uint4 L = *reinterpret_cast<const uint4 *>(q8 + b * kQ8N + 4 * (16 * c + 4 * kh));
+            const uint4 H = *reinterpret_cast<const uint4 *>(q8 + b * kQ8N + 4 * (16 * c + 8 + 4 * kh));
+            const uint32_t w[4] = {W.x, W.y, W.z, W.w}, lo8[4] = {L.x, L.y, L.z, L.w}, hi8[4] = {H.x, H.y, H.z, H.w};
+            const uint32_t scw = sc[b][c >> 1];
+#pragma unroll
+            for (int kl = 0; kl < 4; ++kl) {
+                const int lo = __dp4a((int)(w[kl] & 0x0F0F0F0Fu), (int)lo8[kl], 0);
+                const int hi = __dp4a((int)((w[kl] >> 4) & 0x0F0F0F0Fu), (int)hi8[kl], 0);
+                const int pk = (int)__byte_perm((uint32_t)lo, (uint32_t)hi, 0x5410);
+                s[b][kl] = (c & 1) ? __dp2a_hi(pk, (int)scw, s[b][kl]) : __dp2a_lo(pk, (int)scw, s[b][kl]);
+            }
+        }
+    }
+#pragma unroll
+    for (int b = 0; b < 2; ++b)
+#pragma unroll
+        for (int kl = 0; kl < 4; ++kl) {
+            const int e = __dp2a_lo((int)pm[b][kl], (int)(mn[b][kl >> 1] >> (16 * (kl & 1))), 0);
+            acc[kl] = __fmaf_rn(d[b], __int2float_rn(s[b][kl]), acc[kl]);
+            accm[kl] = __fmaf_rn(dm[b], __int2float_rn(e), accm[kl]);
+        }
+}
+
+// One Q6_K block (kore.cpp:603-636, as block_terms<14>); the block is 4-byte
+// aligned (212-byte stride), so its words are read one by one.
+__device__ __forceinline__ void rows_block_q6(const uint8_t *blk, const uint8_t *q8, int kh, float (&acc)[4],
+                                              float &accm) {
+    uint32_t sw[4];
+#pragma unroll
+    for (int i = 0; i < 4; ++i) sw[i] = lds_u32(blk + 192 + 4 * i);
+    const float xd = *reinterpret_cast<const float *>(q8 + 304);
+    const float d = __fmul_rn(half_bits(lds_u32(blk + 208) & 0xFFFFu), xd);
+    const float dm = -__fmul_rn(d, 32.0f);
+    const uint32_t o = kh ? 0x31u : 0x20u;   // this lane group's scale of each 32-value group: bytes o, o+2
+    int s[4] = {0, 0, 0, 0};
+#pragma unroll
+    for (int h = 0; h < 2; ++h) {
+        uint32_t Q[4][4];
+#pragma unroll
+        for (int kk = 0; kk < 4; ++kk) {
+            const uint4 q = *reinterpret_cast<const uint4 *>(q8 + 4 * (8 * (4 * h + kk) + 4 * kh));
+            Q[kk][0] = q.x;
+            Q[kk][1] = q.y;
+            Q[kk][2] = q.z;
+            Q[kk][3] = q.w;
+        }
+        const int scA = (int)__byte_perm(sw[2 * h], 0u, o), scB = (int)__byte_perm(sw[2 * h + 1], 0u, o);
+#pragma unroll
+        for (int kl = 0; kl < 4; ++kl) {
+            const int k4 = 16 * kh + 4 * kl;
+            const uint32_t qla = lds_u32(blk + 64 * h + k4), qlb = lds_u32(blk + 64 * h + 32 + k4);
+            const uint32_t qh = lds_u32(blk + 128 + 32 * h + k4);
+            int part[4];
+#pragma unroll
+            for (int kk = 0; kk < 4; ++kk) {
+                const uint32_t ql = (kk & 1) ? qlb : qla;
+                const uint32_t v = ((ql >> (4 * (kk >> 1))) & 0x0F0F0F0Fu) | (((qh >> (2 * kk)) & 0x03030303u) << 4);
+                part[kk] = __dp4a((int)v, (int)Q[kk][kl], 0);
+            }
+            s[kl] = __dp2a_lo((int)__byte_perm((uint32_t)part[0], (uint32_t)part[1], 0x5410), scA, s[kl]);
+            s[kl] = __dp2a_lo((int)__byte_perm((uint32_t)part[2], (uint32_t)part[3], 0x5410), scB, s[kl]);
+        }
+    }
+    const uint4 ba = *reinterpret_cast<const uint4 *>(q8 + 256);
+    const uint4 bb = *reinterpret_cast<const uint4 *>(q8 + 272);
+    const uint32_t bw[8] = {ba.x, ba.y, ba.z, ba.w, bb.x, bb.y, bb.z, bb.w};
+    int ib = 0;
+#pragma unroll
+    for (int i = 0; i < 8; ++i)
+        ib = (i & 1) ? __dp2a_hi((int)bw[i], (int)sw[i >> 1], ib) : __dp2a_lo((int)bw[i], (int)sw[i >> 1], ib);
+#pragma unroll
+    for (int kl = 0; kl < 4; ++kl) acc[kl] = __fmaf_rn(d, __int2float_rn(s[kl]), acc[kl]);
+    accm = __fmaf_rn(dm, __int2float_rn(ib), accm);
+}
+
+template <int TYPE>
+__global__ void __launch_bounds__(32 * kRW, 1) qmatvec_rows_kernel(const __grid_constant__ QMatvecParams p) {
+    extern __shared__ __align__(16) uint8_t smem[];
+    constexpr int BB = block_stride(TYPE);
+    constexpr int SLOT = rows_slot_bytes(TYPE);
+    constexpr size_t STAGE = (size_t)kRSlots * SLOT;
+    const int nb = p.cols / 256, S = p.stages;
+    const int n_chunks = (nb + kRCB - 1) / kRCB;
+    uint64_t *bars = reinterpret_cast<uint64_t *>(smem);                                 // [kRW][S]
+    unsigned long long *wkeys = reinterpret_cast<unsigned long long *>(bars + kRW * S);   // [kRW]
+    double *red = reinterpret_cast<double *>(wkeys + kRW);                              // [kRW]
+    float *s_scale = reinterpret_cast<float *>(red + kRW);                               // [4]
+    uint8_t *q8n = reinterpret_cast<uint8_t *>(s_scale + 4);                             // [nb][kQ8N]
+    uint8_t *stages = q8n + (size_t)nb * kQ8N;                                           // [kRW][S][slots]
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int slot = lane & 15, kh = lane >> 4;
+    uint64_t *mybar = bars + warp * S;
+    uint8_t *mystages = stages + (size_t)warp * S * STAGE;
+
+    // tasks: 16 rows of one segment, or (pair mode) the same 8 rows of both
+    int n_tasks = 0;
+    if (p.pair_segments) n_tasks = (p.seg[0].rows + 7) / 8;
+    else
+        for (int s = 0; s < p.n_seg; ++s) n_tasks += (p.seg[s].rows + kRSlots - 1) / kRSlots;
+    const int TW = (int)gridDim.x * kRW;
+    const int t0 = warp * (int)gridDim.x + (int)blockIdx.x;   // tasks warp-major over the grid
+    const int my_tasks = t0 < n_tasks ? (n_tasks - t0 + TW - 1) / TW : 0;
+    const int n_items = my_tasks * n_chunks;
+    // this lane's row (within its segment) in task t; false: the slot has no row
+    auto task_row = [&](int t, int &seg, int &row) -> bool {
+        if (p.pair_segments) {
+            seg = slot < 8 ? 0 : 1;
+            row = t * 8 + (slot & 7);
+            return row < p.seg[0].rows;
+        }
+        int s = 0;
+        while (s + 1 < p.n_seg && t >= (p.seg[s].rows + kRSlots - 1) / kRSlots) {
+            t -= (p.seg[s].rows + kRSlots - 1) / kRSlots;
+            ++s;
+        }
+        seg = s;
+        row = t * kRSlots + slot;
+        return row < p.seg[s].rows;
+    };
+    if (lane == 0) {
+        for (int s = 0; s < S; ++s) mbar_init(mybar + s, 1);
+        mbar_fence_init();
+    }
+    __syncwarp();
+
+    // item (task, chunk) into stage s: each row lane copies its row's chunk;
+    // lane 0 arms the stage's barrier with the warp's total
+    auto issue = [&](int ti, int c, int s) {
+        int seg = 0, row = 0;
+        uint32_t bytes = 0;
+        uintptr_t a0 = 0;
+        if (kh == 0 && task_row(t0 + ti * TW, seg, row)) {
+            const int c0 = c * kRCB, cb = min(kRCB, nb - c0);
+            const uintptr_t a = reinterpret_cast<uintptr_t>(p.seg[seg].w) + ((size_t)row * nb + c0) * BB;
+            a0 = a & ~uintptr_t(15);
+            bytes = (uint32_t)(((a - a0) + cb * BB + 15) & ~uintptr_t(15));
+        }
+        const uint32_t total = __reduce_add_sync(FULLW, bytes);
+        if (lane == 0) {
+            fence_proxy_async_smem();
+            mbar_arrive_expect_tx(mybar + s, total);
+        }
+        if (bytes) {
+            if (lane) fence_proxy_async_smem();
+            bulk_g2s_plain(mystages + (size_t)s * STAGE + (size_t)slot * SLOT, reinterpret_cast<const void *>(a0),
+                           bytes, mybar + s);
+        }
+    };
+    int iss_t = 0, iss_c = 0;
+    auto advance = [&](int &t, int &c) {
+        if (++c == n_chunks) {
+            c = 0;
+            ++t;
+        }
+    };
+    for (int it = 0; it < S && it < n_items; ++it) {
+        issue(iss_t, iss_c, it);
+        advance(iss_t, iss_c);
+    }
+    grid_dep_wait();
+
+    // ------------------------------------------------------------ the Q8_K input
+    float scale = 1.f;
+    if (p.in_mode == QIN_RMSNORM) scale = block_rms_scale(p.x, p.cols, p.eps, red, s_scale);   // kore.cpp:1367-1372
+    for (int b = warp; b < nb; b += kRW) {
+        const float4 *src = reinterpret_cast<const float4 *>(p.x + (size_t)b * 256 + 8 * lane);
+        const float4 a = src[0], c = src[1];
+        float v[8] = {a.x, a.y, a.z, a.w, c.x, c.y, c.z, c.w};
+        if (p.in_mode == QIN_RMSNORM) {
+            const float4 *ws = reinterpret_cast<const float4 *>(p.norm_w + (size_t)b * 256 + 8 * lane);
+            const float4 wa = ws[0], wc = ws[1];
+            const float w[8] = {wa.x, wa.y, wa.z, wa.w, wc.x, wc.y, wc.z, wc.w};
+#pragma unroll
+            for (int i = 0; i < 8; ++i) v[i] = __fmul_rn(__fmul_rn(v[i], scale), w[i]);
+        }
+        q8k_block_nat(v, lane, q8n + (size_t)b * kQ8N);
+    }
+    __syncthreads();
+    grid_dep_launch();
+
+    // ------------------------------------------------------------ the rows
+    unsigned long long best = 0;   // argmax key of this lane's rows (QOUT_ARGMAX)
+    int it = 0, s = 0;
+    uint32_t ph = 0;
+    bool gave_up = false;
+    for (int ti = 0; ti < my_tasks && !gave_up; ++ti) {
+        int seg = 0, row = 0;
+        const bool valid = task_row(t0 + ti * TW, seg, row);
+        const uintptr_t rbase = valid ? reinterpret_cast<uintptr_t>(p.seg[seg].w) + (size_t)row * nb * BB : 0;
+        float acc[4] = {0.f, 0.f, 0.f, 0.f}, accm[4] = {0.f, 0.f, 0.f, 0.f};
+        for (int c = 0; c < n_chunks; ++c) {
+            if (!__all_sync(FULLW, mbar_wait(mybar + s, ph, p.err, DEV_WAIT_FULL_TIMEOUT))) {
+                // gave up (recorded): let the copies still in flight land first
+                for (int u = it; u < n_items && u < it + S; ++u) mbar_drain(mybar + u % S, (u / S) & 1);
+                gave_up = true;
+                break;
+            }
+            const int c0 = c * kRCB, cb = min(kRCB, nb - c0);
+            if (valid) {
+                const uint8_t *blk0 = mystages + (size_t)s * STAGE + (size_t)slot * SLOT +
+                                      ((rbase + (size_t)c0 * BB) & 15);
+                if (TYPE == 12 && cb == 2) {
+                    rows_block2_q4(blk0, q8n + (size_t)c0 * kQ8N, kh, acc, accm);
+                } else {
+#pragma unroll
+                    for (int j = 0; j < kRCB; ++j) {
+                        if (j < cb) {
+                            if (TYPE == 12) rows_block_q4(blk0 + j * BB, q8n + (size_t)(c0 + j) * kQ8N, kh, acc, accm);
+                            else rows_block_q6(blk0 + j * BB, q8n + (size_t)(c0 + j) * kQ8N, kh, acc, accm[0]);
+                        }
+                    }
+                }
+            }
+            __syncwarp();   // every lane is done with the stage
+            if (it + S < n_items) {
+                issue(iss_t, iss_c, s);   // item it + S reuses this stage
+                advance(iss_t, iss_c);
+            }
+            ++it;
+            if (++s == S) {
+                s = 0;
+                ph ^= 1u;
+            }
+        }
+        if (gave_up) break;
+
+        // kore's horizontal sums: ((a0+a4)+(a2+a6)) + ((a1+a5)+(a3+a7)), plus
+        // for Q4_K ((m0+m2)+(m1+m3)), for Q6_K the offset chain
+        float other[4];
+#pragma unroll
+        for (int kl = 0; kl < 4; ++kl) other[kl] = __shfl_xor_sync(FULLW, acc[kl], 16);
+        const float t0s = __fadd_rn(acc[0], other[0]), t1s = __fadd_rn(acc[1], other[1]);
+        const float t2s = __fadd_rn(acc[2], other[2]), t3s = __fadd_rn(acc[3], other[3]);
+        const float a = __fadd_rn(__fadd_rn(t0s, t2s), __fadd_rn(t1s, t3s));
+        const float m = TYPE == 12 ? __fadd_rn(__fadd_rn(accm[0], accm[2]), __fadd_rn(accm[1], accm[3])) : accm[0];
+        const float r = __fadd_rn(a, m);   // valid on kh == 0 lanes
+        const float up = __shfl_sync(FULLW, r, (lane & 7) + 8);   // pair mode: the up row of this gate row
+        if (kh == 0 && valid) {
+            const QSeg &q = p.seg[seg];
+            switch (p.out_mode) {
+                case QOUT_STORE:
+                    q.out[row] = q.bias ? __fadd_rn(r, q.bias[row]) : r;
+                    break;
+                case QOUT_RESIDUAL:
+                    q.out[row] = __fadd_rn(p.resid[row], r);
+                    break;
+                case QOUT_SWIGLU:
+                    if (slot < 8) q.out[row] = kore_swiglu(r, up, p.exp_tab);
+                    break;
+                case QOUT_ARGMAX: {
+                    q.out[row] = r;
+                    int g = row;
+                    for (int s2 = 0; s2 < seg; ++s2) g += p.seg[s2].rows;
+                    const unsigned long long key = argmax_key(r, g);
+                    best = key > best ? key : best;
+                    break;
+                }
+                default:
+                    break;
+            }
+        }
+    }
+    if (p.out_mode == QOUT_ARGMAX) {
+#pragma unroll
+        for (int o = 16; o > 0; o >>= 1) {
+            const unsigned long long x = __shfl_xor_sync(FULLW, best, o);
+            best = x > best ? x : best;
+        }
+        if (lane == 0) wkeys[warp] = best;
+        __syncthreads();
+        if (threadIdx.x == 0) {
+            unsigned long long mx = 0;
+            for (int w = 0; w < kRW; ++w) mx = wkeys[w] > mx ? wkeys[w] : mx;
+            if (mx) atomicMax(p.argmax, mx);
+        }
+    }
+}
+
 cudaLaunchAttribute pdl_attr() {
     cudaLaunchAttribute a;
     a.id = cudaLaunchAttributeProgrammaticStreamSerialization;
@@ -578,6 +1022,17 @@ size_t qmatvec_config(int cols, int max_block_bytes, int *stages, int *row_slot)
     return fixed_smem(nb, S) + (size_t)kWarps * S * 2 * slot;
 }
 
+// Ring stages of the row-task kernel over cols in one block format; returns
+// the dynamic shared memory it needs.
+static size_t rows_config(int cols, int type, int *stages) {
+    const int nb = cols / 256;
+    const size_t per = (size_t)kRW * kRSlots * rows_slot_bytes(type);
+    int S = 6;
+    while (S > 2 && rows_fixed_smem(nb, S) + per * S > kQmatvecMaxSmem) --S;
+    if (stages) *stages = S;
+    return rows_fixed_smem(nb, S) + per * S;
+}
+
 cudaError_t launch_qmatvec(const QMatvecParams &p, int grid, cudaStream_t s) {
     if (p.n_seg <= 0 || p.n_seg > 3 || p.cols <= 0 || p.cols % 256 || !p.x || grid <= 0) return cudaErrorInvalidValue;
     if ((reinterpret_cast<uintptr_t>(p.x) & 15) || (p.in_mode == QIN_RMSNORM && (!p.norm_w ||
@@ -600,6 +1055,37 @@ cudaError_t launch_qmatvec(const QMatvecParams &p, int grid, cudaStream_t s) {
     for (int i = 0; i < p.n_seg; ++i) {
         all4 = all4 && p.seg[i].type == 12;
         all6 = all6 && p.seg[i].type == 14;
+    }
+    // Many Q4_K rows: the row-task kernel (every warp gets at least two
+    // 16-row tasks; measured 29.4 against 32.2 us on the 7B gate/up pair, and
+    // 2 % slower than the group kernel on the Q6_K output matrix, whose
+    // blocks it reads word by word). KORE_CUDA_ROW_PRODUCTS=0 keeps the group
+    // kernel for every launch, 2 takes the row-task kernel for every launch
+    // of one block format (the tests run both kernels on every shape).
+    static const int rows_mode = [] {
+        const char *e = getenv("KORE_CUDA_ROW_PRODUCTS");
+        return e ? atoi(e) : 1;
+    }();
+    if (rows_mode == 2 ? (all4 || all6) : (rows_mode == 1 && all4)) {
+        int n_tasks = 0;
+        if (p.pair_segments) n_tasks = (p.seg[0].rows + 7) / 8;
+        else
+            for (int i = 0; i < p.n_seg; ++i) n_tasks += (p.seg[i].rows + kRSlots - 1) / kRSlots;
+        QMatvecParams q = p;
+        const size_t rsmem = rows_config(p.cols, all4 ? 12 : 14, &q.stages);
+        if ((rows_mode == 2 || n_tasks >= 2 * grid * kRW) && rsmem <= kQmatvecMaxSmem) {
+            void (*rk)(QMatvecParams) = all4 ? qmatvec_rows_kernel<12> : qmatvec_rows_kernel<14>;
+            if (cudaError_t e = ensure_smem_limit(reinterpret_cast<const void *>(rk), (int)kQmatvecMaxSmem)) return e;
+            cudaLaunchConfig_t rcfg = {};
+            rcfg.gridDim = dim3(grid);
+            rcfg.blockDim = dim3(32 * kRW);
+            rcfg.dynamicSmemBytes = rsmem;
+            rcfg.stream = s;
+            cudaLaunchAttribute rattr = pdl_attr();
+            rcfg.attrs = &rattr;
+            rcfg.numAttrs = 1;
+            return cudaLaunchKernelEx(&rcfg, rk, q);
+        }
     }
     const bool wide = chunk_blocks(p.cols / 256, bb) == 16;
     void (*kern)(QMatvecParams) = all4 ? (wide ? qmatvec_kernel<12, 16> : qmatvec_kernel<12, 8>)
