@@ -562,6 +562,19 @@ __global__ void __launch_bounds__(32 * kWarps, 1) qmatvec_kernel(const __grid_co
 #define KORE_ROWS_WARPS 8
 #endif
 constexpr int kRW = KORE_ROWS_WARPS;   // warps per CTA
+
+// Shared-memory loads by 32-bit shared address (no generic addressing).
+__device__ __forceinline__ uint4 ld_sh128(uint32_t a) {
+    uint4 v;
+    asm volatile("ld.shared.v4.u32 {%0, %1, %2, %3}, [%4];" : "=r"(v.x), "=r"(v.y), "=r"(v.z), "=r"(v.w) : "r"(a));
+    return v;
+}
+__device__ __forceinline__ uint32_t ld_sh32(uint32_t a) {
+    uint32_t v;
+    asm volatile("ld.shared.u32 %0, [%1];" : "=r"(v) : "r"(a));
+    return v;
+}
+__device__ __forceinline__ float ld_shf(uint32_t a) { return __uint_as_float(ld_sh32(a)); }
 constexpr int kRSlots = 16;     // row slots per task (pair mode: 8 gate rows, then the same 8 up rows)
 constexpr int kRCB = 2;         // blocks per row per ring stage
 constexpr int kQ8N = 320;       // staged Q8_K block: qs [256], bsums [16] int16, pairs [8] int16, d, pad
@@ -640,23 +653,22 @@ constexpr size_t rows_fixed_smem(int nb, int S) {
 // One Q4_K block of a row for this lane's AVX2 lanes k = 4 kh + kl
 // (kore.cpp:553-586, as block_terms<12>): the exact integers of each lane,
 // then each lane's chains acc += d * s, accm += dm * e in block order.
-__device__ __forceinline__ void rows_block_q4(const uint8_t *blk, const uint8_t *q8, int kh, float (&acc)[4],
-                                              float (&accm)[4]) {
-    const uint4 h = *reinterpret_cast<const uint4 *>(blk);
+__device__ __forceinline__ void rows_block_q4(uint32_t blk, uint32_t q8, int kh, float (&acc)[4], float (&accm)[4]) {
+    const uint4 h = ld_sh128(blk);
     const uint32_t u0 = h.y, u1 = h.z, u2 = h.w;
     const uint32_t sc_lo = u0 & 0x3F3F3F3Fu, sc_hi = (u2 & 0x0F0F0F0Fu) | ((u0 >> 2) & 0x30303030u);
     const uint32_t mn_lo = u1 & 0x3F3F3F3Fu, mn_hi = ((u2 >> 4) & 0x0F0F0F0Fu) | ((u1 >> 2) & 0x30303030u);
-    const float xd = *reinterpret_cast<const float *>(q8 + 304);
+    const float xd = ld_shf(q8 + 304);
     const float d = __fmul_rn(half_bits(h.x & 0xFFFFu), xd);
     const float dm = -__fmul_rn(half_bits(h.x >> 16), xd);
-    const uint4 pr = *reinterpret_cast<const uint4 *>(q8 + 288);   // bsum pairs (2m, 2m+1) in word m
+    const uint4 pr = ld_sh128(q8 + 288);   // bsum pairs (2m, 2m+1) in word m
     const uint32_t pm[4] = {pr.x, pr.y, pr.z, pr.w};
     int s[4] = {0, 0, 0, 0};
 #pragma unroll
     for (int c = 0; c < 4; ++c) {
-        const uint4 W = *reinterpret_cast<const uint4 *>(blk + 16 + 32 * c + 16 * kh);
-        const uint4 L = *reinterpret_cast<const uint4 *>(q8 + 4 * (16 * c + 4 * kh));
-        const uint4 H = *reinterpret_cast<const uint4 *>(q8 + 4 * (16 * c + 8 + 4 * kh));
+        const uint4 W = ld_sh128(blk + 16 + 32 * c + 16 * kh);
+        const uint4 L = ld_sh128(q8 + 4 * (16 * c + 4 * kh));
+        const uint4 H = ld_sh128(q8 + 4 * (16 * c + 8 + 4 * kh));
         const uint32_t w[4] = {W.x, W.y, W.z, W.w}, lo8[4] = {L.x, L.y, L.z, L.w}, hi8[4] = {H.x, H.y, H.z, H.w};
         const uint32_t scw = c < 2 ? sc_lo : sc_hi;
 #pragma unroll
@@ -680,23 +692,22 @@ __device__ __forceinline__ void rows_block_q4(const uint8_t *blk, const uint8_t 
 // Two consecutive Q4_K blocks of a row, their integer work interleaved (two
 // independent sets of lane sums), then the chains in block order: the same
 // values as rows_block_q4 twice.
-__device__ __forceinline__ void rows_block2_q4(const uint8_t *blk, const uint8_t *q8, int kh, float (&acc)[4],
-                                               float (&accm)[4]) {
+__device__ __forceinline__ void rows_block2_q4(uint32_t blk, uint32_t q8, int kh, float (&acc)[4], float (&accm)[4]) {
     uint32_t sc[2][2], mn[2][2];
     float d[2], dm[2];
     uint32_t pm[2][4];
 #pragma unroll
     for (int b = 0; b < 2; ++b) {
-        const uint4 h = *reinterpret_cast<const uint4 *>(blk + b * kQ4Stride);
+        const uint4 h = ld_sh128(blk + b * kQ4Stride);
         const uint32_t u0 = h.y, u1 = h.z, u2 = h.w;
         sc[b][0] = u0 & 0x3F3F3F3Fu;
         sc[b][1] = (u2 & 0x0F0F0F0Fu) | ((u0 >> 2) & 0x30303030u);
         mn[b][0] = u1 & 0x3F3F3F3Fu;
         mn[b][1] = ((u2 >> 4) & 0x0F0F0F0Fu) | ((u1 >> 2) & 0x30303030u);
-        const float xd = *reinterpret_cast<const float *>(q8 + b * kQ8N + 304);
+        const float xd = ld_shf(q8 + b * kQ8N + 304);
         d[b] = __fmul_rn(half_bits(h.x & 0xFFFFu), xd);
         dm[b] = -__fmul_rn(half_bits(h.x >> 16), xd);
-        const uint4 pr = *reinterpret_cast<const uint4 *>(q8 + b * kQ8N + 288);
+        const uint4 pr = ld_sh128(q8 + b * kQ8N + 288);
         pm[b][0] = pr.x;
         pm[b][1] = pr.y;
         pm[b][2] = pr.z;
@@ -707,9 +718,9 @@ __device__ __forceinline__ void rows_block2_q4(const uint8_t *blk, const uint8_t
     for (int c = 0; c < 4; ++c) {
 #pragma unroll
         for (int b = 0; b < 2; ++b) {
-            const uint4 W = *reinterpret_cast<const uint4 *>(blk + b * kQ4Stride + 16 + 32 * c + 16 * kh);
-            const uint4 L = *reinterpret_cast<const uint4 *>(q8 + b * kQ8N + 4 * (16 * c + 4 * kh));
-            const uint4 H = *reinterpret_cast<const uint4 *>(q8 + b * kQ8N + 4 * (16 * c + 8 + 4 * kh));
+            const uint4 W = ld_sh128(blk + b * kQ4Stride + 16 + 32 * c + 16 * kh);
+            const uint4 L = ld_sh128(q8 + b * kQ8N + 4 * (16 * c + 4 * kh));
+            const uint4 H = ld_sh128(q8 + b * kQ8N + 4 * (16 * c + 8 + 4 * kh));
             const uint32_t w[4] = {W.x, W.y, W.z, W.w}, lo8[4] = {L.x, L.y, L.z, L.w}, hi8[4] = {H.x, H.y, H.z, H.w};
             const uint32_t scw = sc[b][c >> 1];
 #pragma unroll
@@ -733,13 +744,12 @@ __device__ __forceinline__ void rows_block2_q4(const uint8_t *blk, const uint8_t
 
 // One Q6_K block (kore.cpp:603-636, as block_terms<14>); the block is 4-byte
 // aligned (212-byte stride), so its words are read one by one.
-__device__ __forceinline__ void rows_block_q6(const uint8_t *blk, const uint8_t *q8, int kh, float (&acc)[4],
-                                              float &accm) {
+__device__ __forceinline__ void rows_block_q6(uint32_t blk, uint32_t q8, int kh, float (&acc)[4], float &accm) {
     uint32_t sw[4];
 #pragma unroll
-    for (int i = 0; i < 4; ++i) sw[i] = lds_u32(blk + 192 + 4 * i);
-    const float xd = *reinterpret_cast<const float *>(q8 + 304);
-    const float d = __fmul_rn(half_bits(lds_u32(blk + 208) & 0xFFFFu), xd);
+    for (int i = 0; i < 4; ++i) sw[i] = ld_sh32(blk + 192 + 4 * i);
+    const float xd = ld_shf(q8 + 304);
+    const float d = __fmul_rn(half_bits(ld_sh32(blk + 208) & 0xFFFFu), xd);
     const float dm = -__fmul_rn(d, 32.0f);
     const uint32_t o = kh ? 0x31u : 0x20u;   // this lane group's scale of each 32-value group: bytes o, o+2
     int s[4] = {0, 0, 0, 0};
@@ -748,7 +758,7 @@ __device__ __forceinline__ void rows_block_q6(const uint8_t *blk, const uint8_t 
         uint32_t Q[4][4];
 #pragma unroll
         for (int kk = 0; kk < 4; ++kk) {
-            const uint4 q = *reinterpret_cast<const uint4 *>(q8 + 4 * (8 * (4 * h + kk) + 4 * kh));
+            const uint4 q = ld_sh128(q8 + 4 * (8 * (4 * h + kk) + 4 * kh));
             Q[kk][0] = q.x;
             Q[kk][1] = q.y;
             Q[kk][2] = q.z;
@@ -758,8 +768,8 @@ __device__ __forceinline__ void rows_block_q6(const uint8_t *blk, const uint8_t 
 #pragma unroll
         for (int kl = 0; kl < 4; ++kl) {
             const int k4 = 16 * kh + 4 * kl;
-            const uint32_t qla = lds_u32(blk + 64 * h + k4), qlb = lds_u32(blk + 64 * h + 32 + k4);
-            const uint32_t qh = lds_u32(blk + 128 + 32 * h + k4);
+            const uint32_t qla = ld_sh32(blk + 64 * h + k4), qlb = ld_sh32(blk + 64 * h + 32 + k4);
+            const uint32_t qh = ld_sh32(blk + 128 + 32 * h + k4);
             int part[4];
 #pragma unroll
             for (int kk = 0; kk < 4; ++kk) {
@@ -771,8 +781,8 @@ __device__ __forceinline__ void rows_block_q6(const uint8_t *blk, const uint8_t 
             s[kl] = __dp2a_lo((int)__byte_perm((uint32_t)part[2], (uint32_t)part[3], 0x5410), scB, s[kl]);
         }
     }
-    const uint4 ba = *reinterpret_cast<const uint4 *>(q8 + 256);
-    const uint4 bb = *reinterpret_cast<const uint4 *>(q8 + 272);
+    const uint4 ba = ld_sh128(q8 + 256);
+    const uint4 bb = ld_sh128(q8 + 272);
     const uint32_t bw[8] = {ba.x, ba.y, ba.z, ba.w, bb.x, bb.y, bb.z, bb.w};
     int ib = 0;
 #pragma unroll
@@ -801,6 +811,8 @@ __global__ void __launch_bounds__(32 * kRW, 1) qmatvec_rows_kernel(const __grid_
     const int slot = lane & 15, kh = lane >> 4;
     uint64_t *mybar = bars + warp * S;
     uint8_t *mystages = stages + (size_t)warp * S * STAGE;
+    const uint32_t stage_sa = smem_u32(mystages) + (uint32_t)slot * SLOT;   // this lane's row slot in stage 0
+    const uint32_t q8_sa = smem_u32(q8n);
 
     // tasks: 16 rows of one segment, or (pair mode) the same 8 rows of both
     int n_tasks = 0;
@@ -907,16 +919,16 @@ __global__ void __launch_bounds__(32 * kRW, 1) qmatvec_rows_kernel(const __grid_
             }
             const int c0 = c * kRCB, cb = min(kRCB, nb - c0);
             if (valid) {
-                const uint8_t *blk0 = mystages + (size_t)s * STAGE + (size_t)slot * SLOT +
-                                      ((rbase + (size_t)c0 * BB) & 15);
+                const uint32_t blk0 = stage_sa + (uint32_t)s * (uint32_t)STAGE + (uint32_t)((rbase + (size_t)c0 * BB) & 15);
+                const uint32_t q8c = q8_sa + (uint32_t)c0 * kQ8N;
                 if (TYPE == 12 && cb == 2) {
-                    rows_block2_q4(blk0, q8n + (size_t)c0 * kQ8N, kh, acc, accm);
+                    rows_block2_q4(blk0, q8c, kh, acc, accm);
                 } else {
 #pragma unroll
                     for (int j = 0; j < kRCB; ++j) {
                         if (j < cb) {
-                            if (TYPE == 12) rows_block_q4(blk0 + j * BB, q8n + (size_t)(c0 + j) * kQ8N, kh, acc, accm);
-                            else rows_block_q6(blk0 + j * BB, q8n + (size_t)(c0 + j) * kQ8N, kh, acc, accm[0]);
+                            if (TYPE == 12) rows_block_q4(blk0 + j * BB, q8c + j * kQ8N, kh, acc, accm);
+                            else rows_block_q6(blk0 + j * BB, q8c + j * kQ8N, kh, acc, accm[0]);
                         }
                     }
                 }
