@@ -14,6 +14,7 @@
 #include <cuda.h>   // CUtensorMap and its enums (the encoder is resolved at run time)
 
 #include <algorithm>
+#include <atomic>
 #include <cmath>
 #include <cstdarg>
 #include <cstdio>
@@ -51,6 +52,9 @@ struct kore_cuda_ctx {
     kore::TmaDesc kv_map{};
     bool kv_map_ok = false;
     bool tc_decode = false;
+    // single-query host-buffer decode returns through mapped memory and a
+    // polled flag (KORE_CUDA_RET_MAPPED=0: copy back and synchronise)
+    bool ret_mapped = true;
     int *pt_d = nullptr;
     std::vector<int> pt_h;      // [max_seqs][pages_per_seq]
     std::vector<int> free_pages;
@@ -65,6 +69,13 @@ struct kore_cuda_ctx {
     size_t dev_stage_floats = 0;
     float *host_stage = nullptr;        // pinned, mapped into the device's address space
     const float *host_stage_dev = nullptr;   // its device address (null: copies go through the copy engine)
+    // Return buffer of the single-query host-buffer decode (pinned, mapped):
+    // word 0 the sequence number of the last finished call, word 1 its device
+    // error word, from byte kRetPad the output, written in place by the kernels
+    unsigned *host_ret = nullptr;
+    void *host_ret_dev = nullptr;
+    size_t host_ret_floats = 0;
+    unsigned ret_seq = 0;
     size_t host_stage_floats = 0;
     int *host_err = nullptr;
     int last_kv_layer = -1;     // layer whose KV the most recent kernel of this context wrote
@@ -336,6 +347,45 @@ void note_len(kore_cuda_ctx *c, int seq, int layer, int end) {
     len = std::max(len, end);
 }
 
+constexpr size_t kRetPad = 256;
+
+// The return buffer for `floats` outputs; false when the host memory cannot
+// be mapped (the call then copies its output back instead).
+bool grow_ret(kore_cuda_ctx *c, size_t floats) {
+    if (c->host_ret_dev && floats <= c->host_ret_floats) return true;
+    if (c->host_ret) cudaFreeHost(c->host_ret);
+    c->host_ret = nullptr;
+    c->host_ret_dev = nullptr;
+    c->host_ret_floats = 0;
+    void *h = nullptr, *d = nullptr;
+    if (cudaHostAlloc(&h, kRetPad + floats * sizeof(float), cudaHostAllocMapped) != cudaSuccess) {
+        cudaGetLastError();
+        return false;
+    }
+    memset(h, 0, kRetPad);
+    if (cudaHostGetDevicePointer(&d, h, 0) != cudaSuccess) {
+        cudaGetLastError();
+        cudaFreeHost(h);
+        return false;
+    }
+    c->host_ret = static_cast<unsigned *>(h);
+    c->host_ret_dev = d;
+    c->host_ret_floats = floats;
+    return true;
+}
+
+// Last kernel of a host-buffer call (after every other kernel of the call, in
+// stream order): the call's device error word, then its sequence number, into
+// the mapped return buffer the host polls.
+__global__ void ret_done_kernel(const int *err, unsigned *ret, unsigned seq) {
+    if (threadIdx.x == 0) {
+        const int e = *reinterpret_cast<const volatile int *>(err);
+        reinterpret_cast<volatile unsigned *>(ret)[1] = (unsigned)e;
+        __threadfence_system();
+        reinterpret_cast<volatile unsigned *>(ret)[0] = seq;
+    }
+}
+
 int grow_stage(kore_cuda_ctx *c, size_t floats) {
     if (floats > c->dev_stage_floats) {
         if (c->dev_stage) cudaFree(c->dev_stage);
@@ -425,6 +475,34 @@ int finish(kore_cuda_ctx *c, size_t extra = 0) {
         CK(cudaStreamSynchronize(c->stream));
         return fail(c, KORE_CUDA_EDEVICE, "device error %d (%s)", e, device_error_text(e));
     }
+    return KORE_CUDA_OK;
+}
+
+// Waits for the host-buffer call with sequence number `seq` by polling the
+// mapped return buffer (no copy back, no stream synchronisation); the stream
+// is queried now and then, so a failed launch or a lost flag ends in finish(),
+// which reports the CUDA or device error. A device error word read back with
+// the flag also goes through finish(), which clears it.
+int wait_ret(kore_cuda_ctx *c, unsigned seq) {
+    volatile unsigned *f = c->host_ret;
+    uint64_t idle_polls = 0;
+    for (uint64_t it = 1;; ++it) {
+        if (f[0] == seq) break;
+        if ((it & 4095) == 0 || idle_polls) {
+            if (!idle_polls) {
+                const cudaError_t q = cudaStreamQuery(c->stream);
+                if (q != cudaErrorNotReady && q != cudaSuccess) return finish(c);
+                if (q == cudaSuccess) idle_polls = 1;   // the flag's write is on its way
+            } else if (++idle_polls > ((uint64_t)1 << 24)) {
+                return finish(c);
+            }
+        }
+#if defined(__x86_64__)
+        __builtin_ia32_pause();
+#endif
+    }
+    std::atomic_thread_fence(std::memory_order_acquire);
+    if (f[1] != 0) return finish(c);
     return KORE_CUDA_OK;
 }
 
@@ -677,6 +755,7 @@ void kore_cuda_destroy(kore_cuda_ctx *c) {
         cudaFree(c->dev_stage);
         if (c->host_stage) cudaFreeHost(c->host_stage);
         if (c->host_err) cudaFreeHost(c->host_err);
+        if (c->host_ret) cudaFreeHost(c->host_ret);
         if (c->own_stream && c->stream) cudaStreamDestroy(c->stream);
     }
     delete c;
@@ -742,6 +821,7 @@ int kore_cuda_create(kore_cuda_ctx **out, const kore_cuda_cfg *cfg) {
     if (const char *fx = getenv("KORE_CUDA_FUSED_EXCHANGE")) c->fused_exchange = atoi(fx) != 0;
     if (const char *fm = getenv("KORE_CUDA_FUSED_MERGE")) c->fused_merge = atoi(fm) != 0;
     if (const char *tc = getenv("KORE_CUDA_TC_DECODE")) c->tc_decode = atoi(tc) != 0;
+    if (const char *rm = getenv("KORE_CUDA_RET_MAPPED")) c->ret_mapped = atoi(rm) != 0;
     CKB(cudaStreamCreateWithFlags(&c->stream, cudaStreamNonBlocking));
     c->own_stream = true;
 
@@ -1163,6 +1243,21 @@ static int decode_host(kore_cuda_ctx *c, int n_seq, const float *q, const float 
     memcpy(hs + nq, k, nk * sizeof(float));
     memcpy(hs + nq + nk, v, nk * sizeof(float));
     if (int rc = stage_in(c, nq + 2 * nk)) return rc;
+    if (!batch && c->ret_mapped && grow_ret(c, nq)) {
+        // one sequence: the kernels write the output into the mapped return
+        // buffer, a last one-thread kernel the error word and the call's
+        // sequence number, which the host polls
+        float *hout = reinterpret_cast<float *>(reinterpret_cast<char *>(c->host_ret_dev) + kRetPad);
+        if (int rc = sharded ? kore_cuda_attn_decode_sharded_dev(c, seq_ids[0], layer, pos[0], ds, ds + nq, ds + nq + nk, hout)
+                             : kore_cuda_attn_decode_dev(c, seq_ids[0], layer, pos[0], ds, ds + nq, ds + nq + nk, hout))
+            return rc;
+        if (++c->ret_seq == 0) ++c->ret_seq;
+        ret_done_kernel<<<1, 32, 0, c->stream>>>(c->err_d, static_cast<unsigned *>(c->host_ret_dev), c->ret_seq);
+        CK(cudaGetLastError());
+        if (int rc = wait_ret(c, c->ret_seq)) return rc;
+        memcpy(out, reinterpret_cast<const char *>(c->host_ret) + kRetPad, nq * sizeof(float));
+        return KORE_CUDA_OK;
+    }
     if (!batch) {
         // one sequence: the output lands right behind the error word and both
         // come back in one copy
