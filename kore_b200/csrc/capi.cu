@@ -1496,6 +1496,18 @@ int kore_cuda_attn_block_decode(kore_cuda_ctx *c, int seq, int layer, int pos, c
     if (int rc = grow_stage(c, (size_t)E)) return rc;
     memcpy(c->host_stage, xb, (size_t)E * sizeof(float));
     if (int rc = stage_in(c, (size_t)E)) return rc;
+    if (c->ret_mapped && grow_ret(c, (size_t)E)) {
+        // the Wo product writes into the mapped return buffer; the host polls
+        // the call's sequence number (as the host-buffer decode)
+        float *hout = reinterpret_cast<float *>(reinterpret_cast<char *>(c->host_ret_dev) + kRetPad);
+        if (int rc = kore_cuda_attn_block_decode_dev(c, seq, layer, pos, c->dev_stage, hout)) return rc;
+        if (++c->ret_seq == 0) ++c->ret_seq;
+        ret_done_kernel<<<1, 32, 0, c->stream>>>(c->err_d, static_cast<unsigned *>(c->host_ret_dev), c->ret_seq);
+        CK(cudaGetLastError());
+        if (int rc = wait_ret(c, c->ret_seq)) return rc;
+        memcpy(o, reinterpret_cast<const char *>(c->host_ret) + kRetPad, (size_t)E * sizeof(float));
+        return KORE_CUDA_OK;
+    }
     // the output lands right behind the error word and both come back in one copy
     float *dout = reinterpret_cast<float *>(reinterpret_cast<char *>(c->err_d) + kErrPad);
     if (int rc = kore_cuda_attn_block_decode_dev(c, seq, layer, pos, c->dev_stage, dout)) return rc;

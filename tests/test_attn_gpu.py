@@ -153,6 +153,30 @@ def test_tensor_core_decode_matches_oracle_and_cuda_core_path(H, G, pos, monkeyp
         g.close()
 
 
+@pytest.mark.parametrize("pos", [0, 700, 5000])
+def test_host_call_mapped_return_equals_copy_back(pos, monkeypatch):
+    """The host-buffer decode returns through mapped memory and a polled
+    completion word by default; KORE_CUDA_RET_MAPPED=0 copies the output back
+    and synchronises. Same bits, over repeated calls, and an error code still
+    comes back as an error with the context usable after it."""
+    H, G, d = 28, 4, 128
+    k, v = normal(90 + pos, (pos, G * d), (pos, G * d))
+    q, kn, vn = normal(91 + pos, (H * d,), (G * d,), (G * d,))
+    outs = []
+    for m in ("1", "0"):
+        monkeypatch.setenv("KORE_CUDA_RET_MAPPED", m)
+        g = make_ctx(H, G, d, pos + 2)
+        if pos:
+            g.append(0, 0, 0, k, v)
+        outs.append([g.decode(0, 0, pos, q, kn, vn) for _ in range(3)])
+        with pytest.raises(K.KoreCudaError):
+            g.decode(0, 0, pos + 5, q, kn, vn)   # a position beyond the context: refused
+        np.testing.assert_array_equal(g.decode(0, 0, pos, q, kn, vn), outs[-1][0])
+        g.close()
+    for a in outs[0] + outs[1]:
+        np.testing.assert_array_equal(a, outs[1][0])
+
+
 def test_decode_dev_matches_host_path():
     import torch
     H, G, d = 28, 4, 128
