@@ -576,7 +576,10 @@ __device__ __forceinline__ uint32_t ld_sh32(uint32_t a) {
 }
 __device__ __forceinline__ float ld_shf(uint32_t a) { return __uint_as_float(ld_sh32(a)); }
 constexpr int kRSlots = 16;     // row slots per task (pair mode: 8 gate rows, then the same 8 up rows)
-constexpr int kRCB = 2;         // blocks per row per ring stage
+#ifndef KORE_ROWS_CB
+#define KORE_ROWS_CB 2
+#endif
+constexpr int kRCB = KORE_ROWS_CB;   // blocks per row per ring stage
 constexpr int kQ8N = 320;       // staged Q8_K block: qs [256], bsums [16] int16, pairs [8] int16, d, pad
 
 // One warp quantises one 256-value block (lane l holds values 8l..8l+7) into
@@ -645,7 +648,7 @@ __host__ __device__ constexpr int rows_slot_bytes(int type) {
                       : ((kRCB * kQ6Stride + 15 + 15) / 16) % 2 ? ((kRCB * kQ6Stride + 15 + 15) / 16) * 16
                                                                   : ((kRCB * kQ6Stride + 15 + 15) / 16 + 1) * 16;
 }
-static_assert(rows_slot_bytes(12) == 304 && rows_slot_bytes(14) == 464, "row slot strides");
+static_assert(rows_slot_bytes(12) / 16 % 2 == 1 && rows_slot_bytes(14) / 16 % 2 == 1, "row slot strides");
 constexpr size_t rows_fixed_smem(int nb, int S) {
     return (size_t)8 * kRW * S + 8 * kRW + 8 * kRW + 16 + (size_t)nb * kQ8N;
 }
