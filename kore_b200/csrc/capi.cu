@@ -568,8 +568,9 @@ int run_decode(kore_cuda_ctx *c, int layer, int n_q, bool contiguous, int seq0, 
         total += cnt;
         max_count = std::max(max_count, cnt);
     }
-    // one query at D = 128 runs the tensor-core kernel (16-token tiles, one CTA per SM)
-    const bool use_tc = c->tc_decode && c->kv_map_ok && c->D == 128 && n_q == 1 && contiguous;
+    // one query at D = 128 on one GPU runs the tensor-core kernel when asked
+    // (16-token tiles, one CTA per SM)
+    const bool use_tc = c->tc_decode && c->kv_map_ok && c->D == 128 && n_q == 1 && contiguous && c->NS == 1;
     const int TT = use_tc ? decode_tc_tile_tokens() : decode_tile_tokens();
     // CTAs to aim for: two per SM, unless set otherwise (KORE_CUDA_DECODE_CTAS;
     // KORE_CUDA_SHARD_CTAS on a KV-split context), trading CTA count for
