@@ -380,8 +380,9 @@ def run_decode(args, rank: int, world: int, dist, pos: int, layers: int, steps: 
                 "call": "kore_cuda_attn_decode" if world == 1 else "kore_cuda_attn_decode_sharded",
                 "breakdown": breakdown},
         "roofline": {"bound": "hbm",
-                     "kernel": "attn_decode_kernel<128,7,8,8,3> + " + ("split_merge_kernel<128,7>" if world == 1
-                                                                       else "peer_exchange_kernel<128>"),
+                     "kernel": "attn_decode_kernel<128,7,8,8,3> with " + (
+                         "its split merge in the same launch" if world == 1
+                         else "its split merge and the peer exchange in the same launch"),
                      "achieved": round(achieved, 1), "peak": peaks["hbm_gbs"], "peak_source": peaks["source"],
                      "unit": "GB/s", "frac": round(achieved / peaks["hbm_gbs"], 4),
                      "traffic": load_traffic() if pos == 32768 and world == 1 else None,
@@ -389,7 +390,7 @@ def run_decode(args, rank: int, world: int, dist, pos: int, layers: int, steps: 
                      "algorithmic_bytes_per_launch": int(launch_bytes),
                      "timing": "launch_ms = timed region / (steps x layers), CUDA events on the context stream; "
                                "launch_ms_isolated = events around each layer's call (no inter-layer overlap)"},
-        "gpu_launches": steps * layers * 2,
+        "gpu_launches": steps * layers * (1 + merge_launch(world)),
         "clocks": clk,
     }
     if world == 1:
@@ -533,8 +534,8 @@ def run_block(args, ctx, stream, dev) -> dict:
                 "h2d_bytes_per_step": L * E * 4, "d2h_bytes_per_step": L * E * 4},
         "roofline": {"bound": "hbm", "achieved": round(achieved, 1), "peak": peaks["hbm_gbs"],
                      "peak_source": peaks["source"], "unit": "GB/s", "frac": round(achieved / peaks["hbm_gbs"], 4),
-                     "kernels": "qmatvec_kernel (QKV) + attn_decode_kernel + split_merge_kernel + qmatvec_kernel (Wo)"},
-        "gpu_launches": steps * L * 4,
+                     "kernels": "qmatvec_kernel (QKV) + attn_decode_kernel (split merge in the launch) + qmatvec_kernel (Wo)"},
+        "gpu_launches": steps * L * (3 + merge_launch()),
         "clocks": clk,
         "_cpu_proj_ms": cpu_proj_ms,
     }
@@ -648,8 +649,8 @@ def run_cfg1(args) -> dict:
         "roofline": {"bound": "latency", "note": "29.6 MFLOP of prefill and <= 0.2 MB per decode: launch and "
                                                  "dependency latency bound, far from HBM or tensor limits"},
         # prefill: append, operand split, tensor-core kernel; each decode: the
-        # decode kernel and its split merge (positions 128..191 take 4-6 splits)
-        "gpu_launches": steps * (3 + C1_DEC * 2),
+        # decode kernel with its split merge (positions 128..191 take 4-6 splits)
+        "gpu_launches": steps * (3 + C1_DEC * (1 + merge_launch())),
         "clocks": clk,
     }
     if not args.no_cpu_baseline:
@@ -809,9 +810,9 @@ def run_step_line(args) -> dict:
         "roofline": {"bound": "hbm", "achieved": round(gbs, 1), "peak": peaks["hbm_gbs"], "peak_source": peaks["source"],
                      "unit": "GB/s", "frac": round(gbs / peaks["hbm_gbs"], 4),
                      "algorithmic_bytes_per_step": int(step_bytes),
-                     "kernels": "embed + 28 x (qmatvec QKV, attn_decode, split_merge, qmatvec Wo, qmatvec gate/up, "
-                                "qmatvec down) + qmatvec logits + token"},
-        "gpu_launches": steps * (2 + L * 6 + 1),
+                     "kernels": "embed + 28 x (qmatvec QKV, attn_decode with its split merge, qmatvec Wo, "
+                                "qmatvec gate/up, qmatvec down) + qmatvec logits + token"},
+        "gpu_launches": steps * (2 + L * (5 + merge_launch()) + 1),
         "clocks": clk,
     }
     if not args.no_cpu_baseline:
@@ -1143,6 +1144,14 @@ def load_peaks() -> dict:
         return {"hbm_gbs": float(j["hbm_gbs"]), "bf16_tflops": float(j["bf16_tflops"]), "source": "measured"}
     except (OSError, KeyError, ValueError):
         return {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "source": "fallback"}
+
+
+def merge_launch(world: int = 1) -> int:
+    """Launches a single-query decode adds for its split merge (world == 1) or
+    its peer exchange (world > 1): 0 when they run in the decode's own launch
+    (the default), 1 when KORE_CUDA_FUSED_MERGE / KORE_CUDA_FUSED_EXCHANGE=0."""
+    var = "KORE_CUDA_FUSED_MERGE" if world == 1 else "KORE_CUDA_FUSED_EXCHANGE"
+    return 0 if os.environ.get(var, "1") != "0" else 1
 
 
 def load_traffic():
