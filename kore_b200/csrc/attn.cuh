@@ -59,6 +59,7 @@ struct DecodeParams {
     int prefetch_ok;           // 1: the preceding kernel in the stream wrote no KV of this layer,
                                //    so KV tiles may be fetched before waiting for it
     int prefetch_stages;       // with prefetch_ok: ring stages per warp fetched before the wait
+    int l2_inputs;             // with prefetch_ok: the CTA's q, new k/v and RoPE row asked into L2 first
                                //    (the rest right after it)
     int l2_prefetch_tokens;    // with prefetch_ok: positions of each split (from its start) that
                                //    are asked into L2 before the wait, so that HBM keeps streaming

@@ -493,6 +493,19 @@ __global__ void __launch_bounds__(NW * 32, 1) attn_decode_kernel(const __grid_co
     // this layer: a decode kernel lets its successor (a split-merge or
     // exchange kernel, or the next decode) start only after its own wait
     // returned, and a split-merge or exchange kernel lets the next decode start
+    // The CTA's inputs from the preceding kernel (q of the group, the new
+    // token) and its RoPE row are asked into L2 before the K/V copies below,
+    // so that the loads after the wait find them there instead of queueing
+    // behind the streamed K/V. L2 is where every SM's accesses meet, so a line
+    // fetched early still holds the preceding kernel's stores when it is read.
+    if (p.prefetch_ok && p.l2_inputs && tid == 0) {
+        bulk_prefetch_l2(p.q + (size_t)qi * p.H * D + (size_t)g * R * D, (uint32_t)(R * D * 4));
+        bulk_prefetch_l2(p.rope + (size_t)pos * HALF, (uint32_t)(HALF * 8));
+        if (do_new) {
+            bulk_prefetch_l2(p.k_new + (size_t)qi * kv.G * D + (size_t)g * D, (uint32_t)(D * 4));
+            bulk_prefetch_l2(p.v_new + (size_t)qi * kv.G * D + (size_t)g * D, (uint32_t)(D * 4));
+        }
+    }
     // at once, so at most the previous decode and its merge can still run
     const int pre = p.prefetch_ok ? min(SPW, p.prefetch_stages) : 0;
     if (lane == 0)
@@ -787,6 +800,14 @@ __global__ void __launch_bounds__(NW * 32, 1) attn_decode_tc_kernel(const __grid
             tma_load_2d(dst + SM::tile_bytes + q * 2048, &p.tm_v, 32 * q, (int)(p.v_row0 + row), bar, pol);
         }
     };
+    if (p.prefetch_ok && p.l2_inputs && tid == 0) {   // as in attn_decode_kernel
+        bulk_prefetch_l2(p.q + (size_t)g * R * D, (uint32_t)(R * D * 4));
+        bulk_prefetch_l2(p.rope + (size_t)pos * HALF, (uint32_t)(HALF * 8));
+        if (do_new) {
+            bulk_prefetch_l2(p.k_new + (size_t)g * D, (uint32_t)(D * 4));
+            bulk_prefetch_l2(p.v_new + (size_t)g * D, (uint32_t)(D * 4));
+        }
+    }
     const int pre = p.prefetch_ok ? min(SPW, p.prefetch_stages) : 0;
     if (lane == 0)
         for (int j = 0; j < pre && j < my_tiles; ++j) issue(j);

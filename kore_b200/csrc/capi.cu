@@ -93,6 +93,7 @@ struct kore_cuda_ctx {
     bool fused_merge = true;
     int *x_arrivals = nullptr;    // [H] arrivals per query head of a fused launch
     int prefetch_stages = 3;      // ring stages fetched early (KORE_CUDA_PREFETCH_STAGES)
+    bool l2_inputs = true;        // the decode's q / new token / RoPE row asked into L2 first (KORE_CUDA_L2_INPUTS)
     int shard_ctas = 0;           // decode CTAs aimed at on a KV-split context (KORE_CUDA_SHARD_CTAS; 0: 2 per SM)
     int decode_ctas = 0;          // decode CTAs aimed at otherwise (KORE_CUDA_DECODE_CTAS; 0: 2 per SM)
     // batched decode: split-length factor chosen for the last batch shape
@@ -679,6 +680,7 @@ int run_decode(kore_cuda_ctx *c, int layer, int n_q, bool contiguous, int seq0, 
     }
     p.prefetch_ok = !c->hold_prefetch && c->last_kv_layer != layer;
     p.prefetch_stages = c->prefetch_stages;
+    p.l2_inputs = c->l2_inputs ? 1 : 0;
     c->hold_prefetch = false;
     if (p.prefetch_ok && c->l2_prefetch_bytes > 0) {
         // L2 budget of the early fetch over all CTAs of the launch (a part of
@@ -817,6 +819,7 @@ int kore_cuda_create(kore_cuda_ctx **out, const kore_cuda_cfg *cfg) {
     if (const char *mb = getenv("KORE_CUDA_L2_PREFETCH_MB")) c->l2_prefetch_bytes = std::max(0ll, atoll(mb)) << 20;
     if (const char *sp = getenv("KORE_CUDA_SHARD_PREFETCH")) c->shard_prefetch = atoi(sp) != 0;
     if (const char *ps = getenv("KORE_CUDA_PREFETCH_STAGES")) c->prefetch_stages = std::max(0, atoi(ps));
+    if (const char *li = getenv("KORE_CUDA_L2_INPUTS")) c->l2_inputs = atoi(li) != 0;
     if (const char *sc = getenv("KORE_CUDA_SHARD_CTAS")) c->shard_ctas = std::max(0, atoi(sc));
     if (const char *dc = getenv("KORE_CUDA_DECODE_CTAS")) c->decode_ctas = std::max(0, atoi(dc));
     if (const char *fx = getenv("KORE_CUDA_FUSED_EXCHANGE")) c->fused_exchange = atoi(fx) != 0;
