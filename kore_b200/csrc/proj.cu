@@ -545,8 +545,9 @@ __global__ void __launch_bounds__(32 * kWarps, 1) qmatvec_kernel(const __grid_co
 // ---------------------------------------------------------------- row-task products
 //
 // qmatvec_rows_kernel: the same products with 16 rows per warp task, for
-// launches with many rows (the feed-forward gate/up pair and the output
-// matrix). Lane (slot, kh) = (lane & 15, lane >> 4) owns row slot `slot` of
+// Q4_K launches with many rows (the 7B feed-forward gate/up pair; launch_qmatvec
+// keeps the Q6_K launches, whose blocks this kernel reads word by word, on the
+// group kernel). Lane (slot, kh) = (lane & 15, lane >> 4) owns row slot `slot` of
 // the task and kore's AVX2 lanes k = 4 kh .. 4 kh + 3 of every block of that
 // row: it forms those lanes' exact integers for each block and advances their
 // fused multiply-add chains in block order itself, so no chain is handed
