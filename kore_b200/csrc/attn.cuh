@@ -221,6 +221,10 @@ constexpr size_t kQmatvecMaxSmem = 227 * 1024;
 // the given largest block size; returns the dynamic shared memory it needs.
 size_t qmatvec_config(int cols, int max_block_bytes, int *stages, int *row_slot);
 cudaError_t launch_qmatvec(const QMatvecParams &p, int grid, cudaStream_t s);
+#ifdef KORE_TRACE
+int proj_trace_read(void *host, unsigned max_recs, unsigned *n_recs);   // trace build only
+int proj_trace_reset();
+#endif
 
 // The embedding rows of n_tokens tokens (step.cu): row z of x =
 // get_row(table, token z) (kore.cpp:384-407) for table type 0 (F32), 1 (F16),

@@ -215,38 +215,10 @@ __device__ __forceinline__ void process_tile(WarpState<D, R> &st, const float *_
 }
 
 #ifdef KORE_TRACE
-// Trace build only (kore_b200/build.py --trace): %globaltimer stamps of every
-// decode, split-merge and merge CTA, read back with kore_trace_read. Thread 0
-// of a CTA claims a record and stamps it at fixed points (TraceRec::t).
-struct TraceRec {
-    unsigned long long t[5];   // entry, dependency wait returned, inputs staged / arrivals seen, tiles done, end
-    unsigned blk, sm, kind, pad;   // kind: 0 decode, 1 split_merge_kernel, 2 merge CTA of a fused launch
-    unsigned long long pad2;
-};
-constexpr unsigned kTraceRecs = 1u << 16;
-__device__ TraceRec g_trace[kTraceRecs];
-__device__ unsigned g_trace_n;
-__device__ __forceinline__ unsigned trace_open(unsigned kind) {
-    if (threadIdx.x != 0) return kTraceRecs;
-    const unsigned slot = atomicAdd(&g_trace_n, 1u);
-    if (slot < kTraceRecs) {
-        unsigned sm;
-        asm volatile("mov.u32 %0, %%smid;" : "=r"(sm));
-        g_trace[slot].t[0] = global_ns();
-        g_trace[slot].blk = blockIdx.x | (blockIdx.y << 16);
-        g_trace[slot].sm = sm;
-        g_trace[slot].kind = kind;
-    }
-    return slot;
-}
-__device__ __forceinline__ void trace_stamp(unsigned slot, int i) {
-    if (slot < kTraceRecs) g_trace[slot].t[i] = global_ns();
-}
-#define KTRACE_OPEN(kind) const unsigned tr_slot_ = trace_open(kind)
-#define KTRACE(i) trace_stamp(tr_slot_, i)
-#else
-#define KTRACE_OPEN(kind)
-#define KTRACE(i)
+// Trace build: every decode, split-merge and merge CTA stamps (TraceRec::t)
+// entry, dependency wait returned, inputs staged / arrivals seen, tiles done,
+// end. Kinds: 0 decode, 1 split_merge_kernel, 2 merge CTA of a fused launch.
+KORE_TRACE_BUFFER();
 #endif
 
 // The merge CTA of query head h at the end of a fused decode launch (the
@@ -1470,8 +1442,9 @@ extern "C" int kore_cuda_attn_decode_noalloc(const kore_cuda_kv_view *kv, int po
 
 #ifdef KORE_TRACE
 // Trace build only: the stamps of the CTAs run since the last reset, as
-// kore::TraceRec records of 64 bytes (see above), in the order the CTAs
-// claimed them. Not part of the ABI.
+// kore::TraceRec records of 64 bytes: the decode and merge CTAs in the order
+// they claimed them, then the product CTAs (proj.cu) in theirs. Not part of
+// the ABI.
 extern "C" int kore_trace_read(void *host, int max_recs, int *n_recs) {
     using namespace kore;
     static_assert(sizeof(TraceRec) == 64, "trace record layout");
@@ -1481,14 +1454,18 @@ extern "C" int kore_trace_read(void *host, int max_recs, int *n_recs) {
     n = n < kTraceRecs ? n : kTraceRecs;
     const unsigned m = max_recs < 0 ? 0u : ((unsigned)max_recs < n ? (unsigned)max_recs : n);
     if (m && cudaMemcpyFromSymbol(host, g_trace, (size_t)m * sizeof(TraceRec)) != cudaSuccess) return KORE_CUDA_ECUDA;
-    if (n_recs) *n_recs = (int)m;
+    unsigned m2 = 0;
+    if (max_recs > (int)m && proj_trace_read(static_cast<TraceRec *>(host) + m, (unsigned)max_recs - m, &m2))
+        return KORE_CUDA_ECUDA;
+    if (n_recs) *n_recs = (int)(m + m2);
     return KORE_CUDA_OK;
 }
 
 extern "C" int kore_trace_reset(void) {
     using namespace kore;
     const unsigned z = 0;
-    if (cudaDeviceSynchronize() != cudaSuccess || cudaMemcpyToSymbol(g_trace_n, &z, sizeof z) != cudaSuccess)
+    if (cudaDeviceSynchronize() != cudaSuccess || cudaMemcpyToSymbol(g_trace_n, &z, sizeof z) != cudaSuccess ||
+        proj_trace_reset())
         return KORE_CUDA_ECUDA;
     return KORE_CUDA_OK;
 }

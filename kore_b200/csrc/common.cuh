@@ -63,6 +63,48 @@ __device__ __forceinline__ uint64_t global_ns() {
     return t;
 }
 
+#ifdef KORE_TRACE
+// Trace build only (kore_b200/build.py --trace): thread 0 of a CTA claims a
+// record and stamps %globaltimer at fixed points of its kernel (TraceRec::t).
+// Each translation unit that stamps holds its own buffer (KORE_TRACE_BUFFER,
+// inside its anonymous namespace); kore_trace_read returns them all.
+struct TraceRec {
+    unsigned long long t[5];   // five stamps, entry first; their meaning is the kind's
+    unsigned blk, sm, kind, tag;   // tag, pad2: the launch's shape (products), else 0
+    unsigned long long pad2;
+};
+constexpr unsigned kTraceRecs = 1u << 16;
+__device__ __forceinline__ unsigned trace_open_in(TraceRec *buf, unsigned *n, unsigned kind, unsigned tag,
+                                                  unsigned long long tag2) {
+    if (threadIdx.x != 0) return kTraceRecs;
+    const unsigned slot = atomicAdd(n, 1u);
+    if (slot < kTraceRecs) {
+        unsigned sm;
+        asm volatile("mov.u32 %0, %%smid;" : "=r"(sm));
+        buf[slot].t[0] = global_ns();
+        buf[slot].blk = blockIdx.x | (blockIdx.y << 16);
+        buf[slot].sm = sm;
+        buf[slot].kind = kind;
+        buf[slot].tag = tag;
+        buf[slot].pad2 = tag2;
+    }
+    return slot;
+}
+__device__ __forceinline__ void trace_stamp_in(TraceRec *buf, unsigned slot, int i) {
+    if (slot < kTraceRecs) buf[slot].t[i] = global_ns();
+}
+#define KORE_TRACE_BUFFER() \
+    __device__ TraceRec g_trace[kTraceRecs]; \
+    __device__ unsigned g_trace_n
+#define KTRACE_OPEN(kind) const unsigned tr_slot_ = trace_open_in(g_trace, &g_trace_n, kind, 0u, 0ull)
+#define KTRACE_OPEN_TAGGED(kind, tag, tag2) const unsigned tr_slot_ = trace_open_in(g_trace, &g_trace_n, kind, tag, tag2)
+#define KTRACE(i) trace_stamp_in(g_trace, tr_slot_, i)
+#else
+#define KTRACE_OPEN(kind)
+#define KTRACE_OPEN_TAGGED(kind, tag, tag2)
+#define KTRACE(i)
+#endif
+
 // Bounded wait on a phase of an mbarrier: gives up after `limit_ns` of wall
 // time (checked every 8 polls) or kWaitPolls polls, whichever comes first,
 // records `code` in the error word and returns false. A healthy pipeline waits

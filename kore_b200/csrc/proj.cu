@@ -78,6 +78,26 @@ namespace {
 constexpr int kWarps = 16;   // warps per CTA (one CTA per SM)
 constexpr unsigned FULLW = 0xffffffffu;
 
+#ifdef KORE_TRACE
+// Trace build: every product CTA stamps (TraceRec::t) entry, dependency wait
+// returned, Q8_K input built, warp 0's first weights landed, end (after a
+// barrier over the CTA). Kinds: 3 qmatvec_kernel, 4 qmatvec_rows_kernel;
+// tag = the first segment's rows, pad2 = cols | out_mode << 32 | n_seg << 40.
+KORE_TRACE_BUFFER();
+#define KTRACE_PRODUCT(kind) \
+    KTRACE_OPEN_TAGGED(kind, (unsigned)p.seg[0].rows, \
+                       (unsigned long long)p.cols | (unsigned long long)p.out_mode << 32 | (unsigned long long)p.n_seg << 40)
+#define KTRACE_FIRST_LANDED(it) \
+    if ((it) == 0) KTRACE(3)
+#define KTRACE_END() \
+    __syncthreads(); \
+    KTRACE(4)
+#else
+#define KTRACE_PRODUCT(kind)
+#define KTRACE_FIRST_LANDED(it)
+#define KTRACE_END()
+#endif
+
 __device__ __forceinline__ float half_bits(uint32_t h) { return __half2float(__ushort_as_half((unsigned short)h)); }
 
 // ---------------------------------------------------------------- Q8_K
@@ -318,6 +338,7 @@ __device__ __forceinline__ int group_row(const QMatvecParams &p, int gg, int rr,
 template <int TYPES, int CB>
 __global__ void __launch_bounds__(32 * kWarps, 1) qmatvec_kernel(const __grid_constant__ QMatvecParams p) {
     extern __shared__ __align__(16) uint8_t smem[];
+    KTRACE_PRODUCT(3);
     const int nb = p.cols / 256, S = p.stages;
     const int n_chunks = (nb + CB - 1) / CB;
     uint64_t *bars = reinterpret_cast<uint64_t *>(smem);                                  // [kWarps][S]
@@ -402,6 +423,7 @@ __global__ void __launch_bounds__(32 * kWarps, 1) qmatvec_kernel(const __grid_co
         advance(iss_t, iss_c);
     }
     grid_dep_wait();
+    KTRACE(1);
 
     // ------------------------------------------------------------ the Q8_K input
     float scale = 1.f;
@@ -421,6 +443,7 @@ __global__ void __launch_bounds__(32 * kWarps, 1) qmatvec_kernel(const __grid_co
     }
     __syncthreads();
     grid_dep_launch();
+    KTRACE(2);
 
     // ------------------------------------------------------------ the rows
     unsigned long long best = 0;   // argmax key of this lane's rows (QOUT_ARGMAX)
@@ -444,6 +467,7 @@ __global__ void __launch_bounds__(32 * kWarps, 1) qmatvec_kernel(const __grid_co
                 gave_up = true;
                 break;
             }
+            KTRACE_FIRST_LANDED(it);
             const int c0 = c * CB, cb = min(CB, nb - c0), half0 = (cb + 1) >> 1;
             const uintptr_t a = reinterpret_cast<uintptr_t>(wrow) + (size_t)c0 * (q4 ? kQ4Stride : kQ6Stride);
             const uint8_t *blk0 = myslots + s * stage_bytes + (size_t)rr * p.row_slot + (a & 15);
@@ -540,6 +564,7 @@ __global__ void __launch_bounds__(32 * kWarps, 1) qmatvec_kernel(const __grid_co
             if (m) atomicMax(p.argmax, m);
         }
     }
+    KTRACE_END();
 }
 
 // ---------------------------------------------------------------- row-task products
@@ -800,6 +825,7 @@ __device__ __forceinline__ void rows_block_q6(uint32_t blk, uint32_t q8, int kh,
 template <int TYPE>
 __global__ void __launch_bounds__(32 * kRW, 1) qmatvec_rows_kernel(const __grid_constant__ QMatvecParams p) {
     extern __shared__ __align__(16) uint8_t smem[];
+    KTRACE_PRODUCT(4);
     constexpr int BB = block_stride(TYPE);
     constexpr int SLOT = rows_slot_bytes(TYPE);
     constexpr size_t STAGE = (size_t)kRSlots * SLOT;
@@ -884,6 +910,7 @@ __global__ void __launch_bounds__(32 * kRW, 1) qmatvec_rows_kernel(const __grid_
         advance(iss_t, iss_c);
     }
     grid_dep_wait();
+    KTRACE(1);
 
     // ------------------------------------------------------------ the Q8_K input
     float scale = 1.f;
@@ -903,6 +930,7 @@ __global__ void __launch_bounds__(32 * kRW, 1) qmatvec_rows_kernel(const __grid_
     }
     __syncthreads();
     grid_dep_launch();
+    KTRACE(2);
 
     // ------------------------------------------------------------ the rows
     unsigned long long best = 0;   // argmax key of this lane's rows (QOUT_ARGMAX)
@@ -921,6 +949,7 @@ __global__ void __launch_bounds__(32 * kRW, 1) qmatvec_rows_kernel(const __grid_
                 gave_up = true;
                 break;
             }
+            KTRACE_FIRST_LANDED(it);
             const int c0 = c * kRCB, cb = min(kRCB, nb - c0);
             if (valid) {
                 const uint32_t blk0 = stage_sa + (uint32_t)s * (uint32_t)STAGE + (uint32_t)((rbase + (size_t)c0 * BB) & 15);
@@ -1000,6 +1029,7 @@ __global__ void __launch_bounds__(32 * kRW, 1) qmatvec_rows_kernel(const __grid_
             if (mx) atomicMax(p.argmax, mx);
         }
     }
+    KTRACE_END();
 }
 
 cudaLaunchAttribute pdl_attr() {
@@ -1118,5 +1148,24 @@ cudaError_t launch_qmatvec(const QMatvecParams &p, int grid, cudaStream_t s) {
     cfg.numAttrs = 1;
     return cudaLaunchKernelEx(&cfg, kern, p);
 }
+
+#ifdef KORE_TRACE
+// Trace build only: the product CTAs' records since the last reset (read
+// after the decode's by kore_trace_read).
+int proj_trace_read(void *host, unsigned max_recs, unsigned *n_recs) {
+    unsigned n = 0;
+    if (cudaMemcpyFromSymbol(&n, g_trace_n, sizeof n) != cudaSuccess) return -1;
+    n = n < kTraceRecs ? n : kTraceRecs;
+    const unsigned m = max_recs < n ? max_recs : n;
+    if (m && cudaMemcpyFromSymbol(host, g_trace, (size_t)m * sizeof(TraceRec)) != cudaSuccess) return -1;
+    *n_recs = m;
+    return 0;
+}
+
+int proj_trace_reset() {
+    const unsigned z = 0;
+    return cudaMemcpyToSymbol(g_trace_n, &z, sizeof z) == cudaSuccess ? 0 : -1;
+}
+#endif
 
 }  // namespace kore
