@@ -211,6 +211,7 @@ struct QMatvecParams {
     const float *x;
     const float *norm_w;          // QIN_RMSNORM weight [cols], 16-byte aligned
     float eps;                    // QIN_RMSNORM epsilon
+    int rms_sequential;           // QIN_RMSNORM: always sum the squares in kore's order (launch_qmatvec sets it)
     const float *resid;           // QOUT_RESIDUAL
     unsigned long long *argmax;   // QOUT_ARGMAX: orderable (value << 32 | ~row) key, zeroed beforehand
     int *err;

@@ -331,6 +331,114 @@ __device__ __forceinline__ int group_row(const QMatvecParams &p, int gg, int rr,
     return s;
 }
 
+// ---------------------------------------------------------------- the Q8_K input
+
+__device__ __forceinline__ void ld8(const float *base, int b, int lane, float (&o)[8]) {
+    const float4 *s = reinterpret_cast<const float4 *>(base + (size_t)b * 256 + 8 * lane);
+    const float4 a = s[0], c = s[1];
+    o[0] = a.x;
+    o[1] = a.y;
+    o[2] = a.z;
+    o[3] = a.w;
+    o[4] = c.x;
+    o[5] = c.y;
+    o[6] = c.z;
+    o[7] = c.w;
+}
+
+// The RMSNorm weights of a warp's first KW blocks (w, w + NW, ...): loaded
+// before the kernel waits for its predecessor (weights do not depend on it).
+template <int NW, int KW>
+__device__ __forceinline__ void load_norm_first(const QMatvecParams &p, int nb, float (&nw)[KW][8]) {
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+#pragma unroll
+    for (int k = 0; k < KW; ++k)
+        if (warp + k * NW < nb) ld8(p.norm_w, warp + k * NW, lane, nw[k]);
+}
+
+// The product's Q8_K input: x, or RMSNorm(x) * norm_w (kore.cpp:1367-1372),
+// handed block by block to quant(b, v) (v: this lane's values 8 lane ..
+// 8 lane + 7 of block b). Warp w takes blocks w, w + NW, ...; KB of them at a
+// time are loaded before any is used, so their latencies overlap (one or two
+// rounds for the inputs of kore's products). The RMSNorm scale: each warp sums
+// the squares of its blocks in double, and after one barrier every warp adds
+// the warps' partial sums in the same butterfly order, so all form the same
+// float; mean_square_float then proves it equal to kore's (sequential sum,
+// rounded mean), else (about one vector in 10^5, or always under
+// rms_sequential) each warp sums in kore's order. Then (float) mean + eps,
+// sqrtf, 1/x, (x * scale) * w, as kore. nw: load_norm_first's registers.
+template <int NW, int KB, int KW, class Quant>
+__device__ __forceinline__ void build_q8_input(const QMatvecParams &p, int nb, double *red, const float (&nw)[KW][8],
+                                               Quant &&quant) {
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const bool norm = p.in_mode == QIN_RMSNORM;
+    float v[KB][8];
+    auto load_x = [&](int b0) {
+#pragma unroll
+        for (int k = 0; k < KB; ++k)
+            if (b0 + k * NW < nb) ld8(p.x, b0 + k * NW, lane, v[k]);
+    };
+    load_x(warp);
+    float scale = 1.f;
+    if (norm) {
+        double ss = 0.0;
+        for (int b0 = warp; b0 < nb; b0 += NW * KB) {
+            if (b0 != warp) load_x(b0);
+#pragma unroll
+            for (int k = 0; k < KB; ++k)
+                if (b0 + k * NW < nb)
+#pragma unroll
+                    for (int i = 0; i < 8; ++i) {
+                        const double xi = (double)v[k][i];
+                        ss = __dadd_rn(ss, __dmul_rn(xi, xi));
+                    }
+        }
+#pragma unroll
+        for (int o = 16; o > 0; o >>= 1) ss = __dadd_rn(ss, __shfl_xor_sync(FULLW, ss, o));
+        if (lane == 0) red[warp] = ss;
+        __syncthreads();
+        double S = lane < NW ? red[lane] : 0.0;
+#pragma unroll
+        for (int o = 16; o > 0; o >>= 1) S = __dadd_rn(S, __shfl_xor_sync(FULLW, S, o));
+        float f = p.rms_sequential ? __int_as_float(0x7fffffff) : mean_square_float(S, p.cols);
+        if (f != f) {   // too close to a rounding boundary (or not finite): kore's order
+            float fs = 0.f;
+            if (lane == 0) {
+                double seq = 0.0;
+                for (int i = 0; i < p.cols; ++i) {
+                    const double xi = (double)p.x[i];
+                    seq = __dadd_rn(seq, __dmul_rn(xi, xi));
+                }
+                fs = __double2float_rn(__ddiv_rn(seq, (double)p.cols));
+            }
+            f = __shfl_sync(FULLW, fs, 0);
+        }
+        scale = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(f, p.eps)));
+        if (nb > NW * KB) load_x(warp);   // later rounds overwrote the first blocks
+    }
+    for (int b0 = warp; b0 < nb; b0 += NW * KB) {
+        if (b0 != warp) load_x(b0);
+#pragma unroll
+        for (int k = 0; k < KB; ++k) {
+            const int b = b0 + k * NW;
+            if (b < nb) {
+                if (norm) {
+                    float w[8];
+                    if (b0 == warp && k < KW) {
+#pragma unroll
+                        for (int i = 0; i < 8; ++i) w[i] = nw[k < KW ? k : 0][i];
+                    } else {
+                        ld8(p.norm_w, b, lane, w);
+                    }
+#pragma unroll
+                    for (int i = 0; i < 8; ++i) v[k][i] = __fmul_rn(__fmul_rn(v[k][i], scale), w[i]);
+                }
+                quant(b, v[k]);
+            }
+        }
+    }
+}
+
 // One product launch. TYPES: 12 or 14 when every segment is Q4_K or Q6_K
 // (the kernel then carries one format's code only), 0 for a mix (each group
 // lies in one segment, so the branch is uniform over a warp). CB: blocks of
@@ -422,25 +530,15 @@ __global__ void __launch_bounds__(32 * kWarps, 1) qmatvec_kernel(const __grid_co
         issue(iss_t, iss_c, it);
         advance(iss_t, iss_c);
     }
+    float nw[1][8];
+    if (p.in_mode == QIN_RMSNORM) load_norm_first<kWarps, 1>(p, nb, nw);
     grid_dep_wait();
     KTRACE(1);
 
     // ------------------------------------------------------------ the Q8_K input
-    float scale = 1.f;
-    if (p.in_mode == QIN_RMSNORM) scale = block_rms_scale(p.x, p.cols, p.eps, red, s_scale);   // kore.cpp:1367-1372
-    for (int b = warp; b < nb; b += kWarps) {
-        const float4 *src = reinterpret_cast<const float4 *>(p.x + (size_t)b * 256 + 8 * lane);
-        const float4 a = src[0], c = src[1];
-        float v[8] = {a.x, a.y, a.z, a.w, c.x, c.y, c.z, c.w};
-        if (p.in_mode == QIN_RMSNORM) {
-            const float4 *ws = reinterpret_cast<const float4 *>(p.norm_w + (size_t)b * 256 + 8 * lane);
-            const float4 wa = ws[0], wc = ws[1];
-            const float w[8] = {wa.x, wa.y, wa.z, wa.w, wc.x, wc.y, wc.z, wc.w};
-#pragma unroll
-            for (int i = 0; i < 8; ++i) v[i] = __fmul_rn(__fmul_rn(v[i], scale), w[i]);
-        }
+    build_q8_input<kWarps, 3, 1>(p, nb, red, nw, [&](int b, const float (&v)[8]) {
         q8k_block(v, lane, q8t + (size_t)b * kQ8Block, xds + b, bss + (size_t)b * 16, prs + (size_t)b * 8);
-    }
+    });
     __syncthreads();
     grid_dep_launch();
     KTRACE(2);
@@ -909,25 +1007,14 @@ __global__ void __launch_bounds__(32 * kRW, 1) qmatvec_rows_kernel(const __grid_
         issue(iss_t, iss_c, it);
         advance(iss_t, iss_c);
     }
+    float nw[2][8];
+    if (p.in_mode == QIN_RMSNORM) load_norm_first<kRW, 2>(p, nb, nw);
     grid_dep_wait();
     KTRACE(1);
 
     // ------------------------------------------------------------ the Q8_K input
-    float scale = 1.f;
-    if (p.in_mode == QIN_RMSNORM) scale = block_rms_scale(p.x, p.cols, p.eps, red, s_scale);   // kore.cpp:1367-1372
-    for (int b = warp; b < nb; b += kRW) {
-        const float4 *src = reinterpret_cast<const float4 *>(p.x + (size_t)b * 256 + 8 * lane);
-        const float4 a = src[0], c = src[1];
-        float v[8] = {a.x, a.y, a.z, a.w, c.x, c.y, c.z, c.w};
-        if (p.in_mode == QIN_RMSNORM) {
-            const float4 *ws = reinterpret_cast<const float4 *>(p.norm_w + (size_t)b * 256 + 8 * lane);
-            const float4 wa = ws[0], wc = ws[1];
-            const float w[8] = {wa.x, wa.y, wa.z, wa.w, wc.x, wc.y, wc.z, wc.w};
-#pragma unroll
-            for (int i = 0; i < 8; ++i) v[i] = __fmul_rn(__fmul_rn(v[i], scale), w[i]);
-        }
-        q8k_block_nat(v, lane, q8n + (size_t)b * kQ8N);
-    }
+    build_q8_input<kRW, 4, 2>(p, nb, red, nw,
+                              [&](int b, const float (&v)[8]) { q8k_block_nat(v, lane, q8n + (size_t)b * kQ8N); });
     __syncthreads();
     grid_dep_launch();
     KTRACE(2);
@@ -1079,7 +1166,15 @@ static size_t rows_config(int cols, int type, int *stages) {
     return rows_fixed_smem(nb, S) + per * S;
 }
 
-cudaError_t launch_qmatvec(const QMatvecParams &p, int grid, cudaStream_t s) {
+cudaError_t launch_qmatvec(const QMatvecParams &p_in, int grid, cudaStream_t s) {
+    // KORE_CUDA_RMS_SEQUENTIAL=1: every RMSNorm input sums its squares in
+    // kore's order (the path a mean next to a rounding boundary takes; tests)
+    static const int rms_seq = [] {
+        const char *e = getenv("KORE_CUDA_RMS_SEQUENTIAL");
+        return e && atoi(e) != 0 ? 1 : 0;
+    }();
+    QMatvecParams p = p_in;
+    p.rms_sequential = rms_seq;
     if (p.n_seg <= 0 || p.n_seg > 3 || p.cols <= 0 || p.cols % 256 || !p.x || grid <= 0) return cudaErrorInvalidValue;
     if ((reinterpret_cast<uintptr_t>(p.x) & 15) || (p.in_mode == QIN_RMSNORM && (!p.norm_w ||
         (reinterpret_cast<uintptr_t>(p.norm_w) & 15))))
@@ -1107,7 +1202,8 @@ cudaError_t launch_qmatvec(const QMatvecParams &p, int grid, cudaStream_t s) {
     // 2 % slower than the group kernel on the Q6_K output matrix, whose
     // blocks it reads word by word). KORE_CUDA_ROW_PRODUCTS=0 keeps the group
     // kernel for every launch, 2 takes the row-task kernel for every launch
-    // of one block format (the tests run both kernels on every shape).
+    // of one block format (tests/test_product_switches_gpu.py runs the
+    // product and step tests under both).
     static const int rows_mode = [] {
         const char *e = getenv("KORE_CUDA_ROW_PRODUCTS");
         return e ? atoi(e) : 1;
