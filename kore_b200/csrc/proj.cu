@@ -52,7 +52,10 @@
 // each way per chunk), so the float order stays kore's. Rows are streamed in
 // chunks (a whole row of up to 16 blocks, else 8 blocks) through a ring of
 // stages per warp (one bulk copy per row and chunk, issued by the row's first
-// lane, mbarrier completion), refilled as soon as a chunk has been consumed
+// lane, mbarrier completion; marked first to evict from L2, as every weight
+// byte is read once: weights kept at normal priority filled L2 with lines
+// nobody reads again and slowed the decode that follows the products by
+// ~5 us per layer), refilled as soon as a chunk has been consumed
 // and running on into the warp's next group, so long rows (the 18944-wide
 // down projection) fit and every warp keeps several copies in flight. A
 // launch whose matrices share one block format runs a kernel compiled for
@@ -514,8 +517,8 @@ __global__ void __launch_bounds__(32 * kWarps, 1) qmatvec_kernel(const __grid_co
         __syncwarp();
         if ((lane & 15) == 0 && by) {
             if (lane == 16) fence_proxy_async_smem();
-            bulk_g2s_plain(myslots + s * stage_bytes + (size_t)rr * p.row_slot, reinterpret_cast<const void *>(a0), by,
-                           mybar + s);
+            bulk_g2s(myslots + s * stage_bytes + (size_t)rr * p.row_slot, reinterpret_cast<const void *>(a0), by,
+                     mybar + s, l2_evict_first_policy());
         }
     };
     // the next item to issue, as (group, chunk), advanced incrementally
@@ -992,8 +995,8 @@ __global__ void __launch_bounds__(32 * kRW, 1) qmatvec_rows_kernel(const __grid_
         }
         if (bytes) {
             if (lane) fence_proxy_async_smem();
-            bulk_g2s_plain(mystages + (size_t)s * STAGE + (size_t)slot * SLOT, reinterpret_cast<const void *>(a0),
-                           bytes, mybar + s);
+            bulk_g2s(mystages + (size_t)s * STAGE + (size_t)slot * SLOT, reinterpret_cast<const void *>(a0), bytes,
+                     mybar + s, l2_evict_first_policy());
         }
     };
     int iss_t = 0, iss_c = 0;
