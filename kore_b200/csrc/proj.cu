@@ -52,20 +52,20 @@
 // each way per chunk), so the float order stays kore's. Rows are streamed in
 // chunks (a whole row of up to 16 blocks, else 8 blocks) through a ring of
 // stages per warp (one bulk copy per row and chunk, issued by the row's first
-// lane, mbarrier completion; marked first to evict from L2, as every weight
-// byte is read once: weights kept at normal priority filled L2 with lines
-// nobody reads again and slowed the decode that follows the products by
-// ~5 us per layer), refilled as soon as a chunk has been consumed
+// lane, mbarrier completion), refilled as soon as a chunk has been consumed
 // and running on into the warp's next group, so long rows (the 18944-wide
-// down projection) fit and every warp keeps several copies in flight. A
-// launch whose matrices share one block format runs a kernel compiled for
-// that format alone. The first stages are issued before the kernel waits for its
-// predecessor (programmatic dependent launch): weights do not depend on it.
-// Meanwhile every CTA builds the Q8_K input in shared memory itself (14 KB
-// at 7B, 28 KB for the feed-forward width: cheaper than a kernel boundary),
-// transposed so that each lane reads its 8 words of a block with two 16-byte
-// loads on distinct banks. Memory-bound: algorithmic bytes = the weight
-// bytes (+ the small vectors), read once.
+// down projection) fit and every warp keeps several copies in flight. The
+// copies are marked first to evict from L2: every weight byte is read once,
+// and weights left in L2 at normal priority slowed the decode that follows
+// the products by ~5 us per layer. A launch whose matrices share one block
+// format runs a kernel compiled for that format alone. The first stages are
+// issued before the kernel waits for its predecessor (programmatic dependent
+// launch): weights do not depend on it. Meanwhile every CTA builds the Q8_K
+// input in shared memory itself (build_q8_input; 14 KB at 7B, 28 KB for the
+// feed-forward width: cheaper than a kernel boundary), transposed so that
+// each lane reads its 8 words of a block with two 16-byte loads on distinct
+// banks. Memory-bound: algorithmic bytes = the weight bytes (+ the small
+// vectors), read once.
 
 #include "attn.cuh"
 #include "common.cuh"
