@@ -287,18 +287,32 @@ def run_decode(args, rank: int, world: int, dist, pos: int, layers: int, steps: 
     iso_ms = sum(a.elapsed_time(b) for a, b in evs) / len(evs)
 
     # end to end through the host-buffer entry point (kore's own call shape):
-    # q/k/v in from host memory, the merged output back, one call per layer
+    # q/k/v in from host memory, the merged output back into host memory, one
+    # C-ABI call per layer with kore's raw pointers (the library copies in and
+    # out inside each call); the numpy wrapper's cost is reported beside it
     hq, hk, hv = q.cpu().numpy(), kn.cpu().numpy(), vn.cpu().numpy()
     ho = np.empty((layers, H * D), np.float32)
-    call = ctx.decode if world == 1 else ctx.decode_sharded
-    for layer in range(layers):
-        ho[layer] = call(0, layer, pos, hq[layer], hk[layer], hv[layer]).reshape(-1)
+    c_dec = ctx.c_call("kore_cuda_attn_decode" if world == 1 else "kore_cuda_attn_decode_sharded")
+    ptrs = [(hq[l].ctypes.data, hk[l].ctypes.data, hv[l].ctypes.data, ho[l].ctypes.data) for l in range(layers)]
+
+    def host_step():
+        for layer in range(layers):
+            qa, ka, va, oa = ptrs[layer]
+            c_dec(0, layer, pos, qa, ka, va, oa)
+    host_step()
     barrier()
     t0 = time.perf_counter()
     for _ in range(e2e_steps):
-        for layer in range(layers):
-            ho[layer] = call(0, layer, pos, hq[layer], hk[layer], hv[layer]).reshape(-1)
+        host_step()
     e2e_ms = (time.perf_counter() - t0) * 1e3 / e2e_steps
+    barrier()
+    wrap = ctx.decode if world == 1 else ctx.decode_sharded
+    n_w = max(3, e2e_steps // 10)
+    t0 = time.perf_counter()
+    for _ in range(n_w):
+        for layer in range(layers):
+            ho[layer] = wrap(0, layer, pos, hq[layer], hk[layer], hv[layer]).reshape(-1)
+    wrapped_us = (time.perf_counter() - t0) * 1e6 / (n_w * layers)
     barrier()
 
     # where a host-buffer call's time goes (one GPU): the same layer calls with
@@ -320,10 +334,13 @@ def run_decode(args, rank: int, world: int, dist, pos: int, layers: int, steps: 
                 ctx.sync()
             sync_us = (time.perf_counter() - t0) * 1e6 / (n_b * layers)
         breakdown = {"host_call_us": round(e2e_ms * 1e3 / layers, 2),
+                     "python_wrapper_call_us": round(wrapped_us, 2),
                      "device_inputs_call_plus_sync_us": round(dev_sync_us, 2),
                      "sync_alone_us": round(sync_us, 2),
                      "staging_us": round(e2e_ms * 1e3 / layers - dev_sync_us, 2),
-                     "note": "per layer: host_call = kore_cuda_attn_decode with host q/k/v/out; the second figure is "
+                     "note": "per layer: host_call = kore_cuda_attn_decode with host q/k/v/out (raw pointers, as "
+                             "kore calls it); python_wrapper_call = the same through KoreCuda.decode (numpy "
+                             "conversions and a new output array per call); the next figure is "
                              "kore_cuda_attn_decode_dev (inputs in HBM) + kore_cuda_sync after each call; sync_alone "
                              "is kore_cuda_sync with nothing queued (error-word copy + stream wait); staging = "
                              "host_call - the second figure (host copies, the input kernel, the output copy)"}
@@ -502,14 +519,18 @@ def run_block(args, ctx, stream, dev) -> dict:
     ms = e0.elapsed_time(e1) / steps
     del graph
     # end to end through the host-buffer entry point (xb in, Wo*att out per layer)
+    # (raw host pointers, as kore passes them)
     hx = xb.cpu().numpy()
+    hob = np.empty_like(hx)
+    c_blk = ctx.c_call("kore_cuda_attn_block_decode")
+    bptr = [(hx[l].ctypes.data, hob[l].ctypes.data) for l in range(L)]
     for layer in range(L):
-        ctx.attn_block_decode(0, layer, POS, hx[layer])
+        c_blk(0, layer, POS, *bptr[layer])
     n_e2e = max(1, args.e2e_steps // 4)
     t0 = time.perf_counter()
     for _ in range(n_e2e):
         for layer in range(L):
-            ctx.attn_block_decode(0, layer, POS, hx[layer])
+            c_blk(0, layer, POS, *bptr[layer])
     e2e_ms = (time.perf_counter() - t0) * 1e3 / n_e2e
     # CPU leg: kore's own quantize + matvec_mt of one layer's four matrices on
     # one core (the compiled reference), added to its one-core attention time
@@ -619,12 +640,17 @@ def run_cfg1(args) -> dict:
     torch.cuda.synchronize(dev)
     pre_us = ev[0].elapsed_time(ev[1]) * 1e3
     dec_us = ev[1].elapsed_time(ev[-1]) * 1e3 / C1_DEC
-    # end to end: kore's host-buffer calls
+    # end to end: kore's host-buffer calls, with raw host pointers as kore
+    # passes them (outputs into one host array)
+    ho = np.empty((C1_PRE + C1_DEC, hd), np.float32)
+    c_pre, c_dec = ctx.c_call("kore_cuda_attn_prefill"), ctx.c_call("kore_cuda_attn_decode")
+    row = lambda a, i: a.ctypes.data + i * a.strides[0]  # noqa: E731
+
     def e2e_once():
-        ctx.prefill(0, 0, 0, hq[:C1_PRE], hk[:C1_PRE], hv[:C1_PRE])
+        c_pre(0, 0, 0, C1_PRE, row(hq, 0), row(hk, 0), row(hv, 0), row(ho, 0))
         for i in range(C1_DEC):
             p = C1_PRE + i
-            ctx.decode(0, 0, p, hq[p], hk[p], hv[p])
+            c_dec(0, 0, p, row(hq, p), row(hk, p), row(hv, p), row(ho, p))
     for _ in range(3):
         e2e_once()
     n_e2e = 20

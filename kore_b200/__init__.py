@@ -242,6 +242,20 @@ class KoreCuda:
         if rc:
             raise KoreCudaError(rc, self._L.kore_cuda_last_error(self._h).decode())
 
+    def c_call(self, name: str):
+        """The C-ABI entry point `name` bound to this context: f(*args) calls
+        name(ctx, *args) with the arguments as given (raw host or device
+        addresses as ints, as kore passes its own buffers) and raises
+        KoreCudaError on a non-zero return. No numpy conversion or allocation
+        per call: the caller owns every buffer."""
+        fn, h, ck = getattr(self._L, name), self._h, self._ck
+
+        def call(*args):
+            rc = fn(h, *args)
+            if rc:
+                ck(rc)
+        return call
+
     @property
     def handle(self) -> int:
         return self._h.value

@@ -62,3 +62,27 @@ def test_create_without_gpu_reports_error_instead_of_aborting():
     with pytest.raises(K.KoreCudaError) as e:
         K.KoreCuda(2, 28, 4, 128, 64)
     assert e.value.code == -4 and "device" in str(e.value).lower()
+
+
+def test_c_call_binds_the_context_and_raises_on_error():
+    """KoreCuda.c_call (the raw-pointer form kore's own calls take, used by the
+    bench's host-buffer timings) passes the context handle first, the
+    arguments unchanged, and turns a non-zero return into KoreCudaError."""
+    calls = []
+
+    class FakeLib:
+        def kore_cuda_x(self, h, *a):
+            calls.append((h,) + a)
+            return 0 if a[0] >= 0 else 22
+
+        def kore_cuda_last_error(self, h):
+            return b"bad argument"
+
+    c = object.__new__(K.KoreCuda)
+    c._L, c._h = FakeLib(), "ctx"
+    f = c.c_call("kore_cuda_x")
+    f(1, 2, 0x1000)
+    assert calls == [("ctx", 1, 2, 0x1000)]
+    with pytest.raises(K.KoreCudaError, match="bad argument"):
+        f(-1)
+    c._h = None   # nothing to close
